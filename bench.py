@@ -1,0 +1,398 @@
+#!/usr/bin/env python3
+"""Benchmark: batch-1 greedy decode of the Llama-3.1-8B architecture with a
+Q4_K_M-style weight mix, plus the per-kernel HBM rooflines
+of configs 0-2 (Q4_K / Q6_K matvec, decode attention).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One process per GPU; for N > 1 launch with torch.distributed.run (RANK,
+WORLD_SIZE, LOCAL_RANK from the environment).  Rank 0 prints one JSON line.
+
+Workload (synthetic, seeded; no dataset is involved): random-init weights of
+the Llama-3.1-8B shape (32 layers, hidden 4096, 32 q / 8 kv heads, FFN 14336,
+vocab 128256) as Q4_K with Q6_K for attn_v, ffn_down and the output head;
+the KV context is pre-filled to 4096 positions with seeded ~N(0,1) values,
+then K greedy decode steps run from position 4096 + W.  A step is one token
+through all 32 layers, the final norm, the output head and the argmax.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+LLAMA8B = dict(hidden_dim=4096, n_heads=32, n_kv_heads=8, n_layers=32, ff_dim=14336, vocab_size=128256)
+CTX = 4096
+SEED = 1234
+METRIC = "decode tokens/s (Llama-3.1-8B arch, Q4_K_M, ctx 4096, batch 1)"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def ncu_traffic():
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu
+    summary (profiles/q4k_matvec_14336x4096.md), or None."""
+    p = os.path.join(ROOT, "profiles", "q4k_matvec_14336x4096.md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class Clocks:
+    """nvidia-smi samples of SM clock and throttle reasons during a region."""
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "100"],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.p = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        self.rows = []
+        if self.p is None:
+            return
+        time.sleep(0.15)
+        self.p.terminate()
+        out, _ = self.p.communicate(timeout=10)
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) == 7:
+                self.rows.append(f)
+
+    def summary(self):
+        if not getattr(self, "rows", None):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[3 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# ---------------------------------------------------------------- our arm
+def kernel_benchmarks(gb, torch, dm, peak):
+    """Isolated kernel timings with CUDA events on the launching stream.
+    Every timed launch reads a buffer that is not in L2 (copies rotate over
+    more than 4x the 126 MB L2)."""
+    st = torch.cuda.Stream()
+    sp = st.cuda_stream
+    res = {}
+
+    def timed(launch, n_iter, warm=3):
+        for i in range(warm):
+            launch(i)
+        st.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for i in range(n_iter):
+            launch(i)
+        e1.record(st)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / n_iter * 1e-3   # seconds per launch
+
+    def matvec_case(tag, dt, rows, cols, copies, n_iter):
+        wbytes = gb.matrix_bytes(dt, rows, cols)
+        bufs = [torch.empty(wbytes + 16, dtype=torch.uint8, device="cuda") for _ in range(copies)]
+        nblk = wbytes // gb.BLOCK_BYTES[dt]
+        for j, b in enumerate(bufs):
+            gb.synth_blocks(dt, b, nblk, SEED, 77 + j, stream=sp)
+        x = torch.empty(cols, dtype=torch.float32, device="cuda")
+        gb.synth_normal(x, cols, SEED, 5, stream=sp)
+        y = torch.empty(rows, dtype=torch.float32, device="cuda")
+        st.synchronize()
+        t = timed(lambda i: gb.matvec(dt, bufs[i % copies], rows, cols, x, y, stream=sp), n_iter)
+        alg = wbytes + 4 * cols + 4 * rows
+        gbs = alg / t / 1e9
+        res[tag] = {"us": round(t * 1e6, 2), "alg_bytes": alg, "GB/s": round(gbs, 1), "frac": round(gbs / peak, 3)}
+        del bufs
+        torch.cuda.empty_cache()
+        return gbs, alg, t
+
+    main = matvec_case("q4k_matvec_14336x4096", 4, 14336, 4096, 12, 200)
+    matvec_case("q4k_matvec_4096x4096 (config 0)", 4, 4096, 4096, 40, 400)
+    matvec_case("q6k_matvec_4096x14336 (config 1)", 5, 4096, 14336, 10, 200)
+    matvec_case("q6k_matvec_128256x4096 (config 1, output head)", 5, 128256, 4096, 2, 40)
+
+    # config 2: RoPE + append + GQA attention over 8193 positions (fp32 KV)
+    nh, nkv, hd, ms, pos = 32, 8, 128, 8448, 8192
+    copies = 5
+    kv_elems = nkv * ms * hd
+    kcs = [torch.empty(kv_elems, dtype=torch.float32, device="cuda") for _ in range(copies)]
+    vcs = [torch.empty(kv_elems, dtype=torch.float32, device="cuda") for _ in range(copies)]
+    for j in range(copies):
+        gb.synth_normal(kcs[j], kv_elems, SEED, 900 + j, stream=sp)
+        gb.synth_normal(vcs[j], kv_elems, SEED, 950 + j, stream=sp)
+    q = torch.empty(nh * hd, dtype=torch.float32, device="cuda")
+    k = torch.empty(nkv * hd, dtype=torch.float32, device="cuda")
+    v = torch.empty(nkv * hd, dtype=torch.float32, device="cuda")
+    for t_, n_, s_ in ((q, nh * hd, 1), (k, nkv * hd, 2), (v, nkv * hd, 3)):
+        gb.synth_normal(t_, n_, SEED, s_, stream=sp)
+    cs = torch.empty(ms * hd, dtype=torch.float32, device="cuda")
+    gb.rope_table(cs, ms, hd, stream=sp)
+    ws = torch.zeros(gb.attn_workspace_bytes(nh, nkv, hd, ms), dtype=torch.uint8, device="cuda")
+    d_pos = torch.tensor([pos], dtype=torch.int32, device="cuda")
+    out = torch.empty(nh * hd, dtype=torch.float32, device="cuda")
+    st.synchronize()
+    t = timed(lambda i: gb.attention_decode(q, k, v, kcs[i % copies], vcs[i % copies], cs, d_pos, nh, nkv, hd, ms,
+                                            out, ws, stream=sp), 200)
+    alg = 2 * nkv * (pos + 1) * hd * 4 + 2 * nkv * hd * 4 + 2 * nh * hd * 4
+    gbs = alg / t / 1e9
+    res["attention_decode_8193 (config 2)"] = {"us": round(t * 1e6, 2), "alg_bytes": alg, "GB/s": round(gbs, 1),
+                                               "frac": round(gbs / peak, 3)}
+    del kcs, vcs
+    torch.cuda.empty_cache()
+    return res, main
+
+
+def cpu_reference_token_time(threads: int, n_layers_sample: int = 1, reps: int = 2):
+    """Seconds per Llama-8B decode token on the host cores through the
+    reference's own forward() (oracle/_ref, compiled unchanged), measured on a
+    bounded sample: forward() of a model with n_layers_sample layers plus the
+    full output head, and the output-head matvec alone; the token time is
+    head + 32 * (sample - head) / n_layers_sample."""
+    import numpy as np
+    from oracle import oracle as O
+    if not O.ref_available():
+        return None
+    R = O.ref()
+    R.ref_set_threads(threads)
+
+    class M:
+        pass
+    m = M()
+    c = LLAMA8B
+    m.H, m.n_heads, m.n_kv, m.hd, m.ff = c["hidden_dim"], c["n_heads"], c["n_kv_heads"], 128, c["ff_dim"]
+    m.vocab, m.n_layers, m.max_seq = c["vocab_size"], n_layers_sample, CTX + 8
+    m.layers = []
+    kv = m.n_kv * m.hd
+    shapes = [(m.H, m.H), (kv, m.H), (kv, m.H), (m.H, m.H), (m.ff, m.H), (m.ff, m.H), (m.H, m.ff)]
+    dts = [4, 4, 5, 4, 4, 4, 5]
+    for li in range(n_layers_sample):
+        L = M()
+        L.w = [O.synth_blocks(dt, r, cc, SEED, li * 7 + i + 1) for i, (dt, (r, cc)) in enumerate(zip(dts, shapes))]
+        L.dtypes = dts
+        L.rms_att = np.ones(m.H, np.float32)
+        L.rms_ffn = np.ones(m.H, np.float32)
+        m.layers.append(L)
+    m.emb_dtype, m.lm_dtype = 4, 5
+    m.embedding = O.synth_blocks(4, m.vocab, m.H, SEED, 1000001)
+    m.lm_head = O.synth_blocks(5, m.vocab, m.H, SEED, 1000002)
+    m.rms_final = np.ones(m.H, np.float32)
+    ref = O.RefModel(m)
+    for li in range(n_layers_sample):
+        for which in (0, 1):
+            buf = ref.kv(li, which, m.n_kv * m.max_seq * m.hd).reshape(m.n_kv, m.max_seq, m.hd)
+            buf[:, :CTX] = O.synth_normal(m.n_kv * CTX * m.hd, SEED, 77 + which).reshape(m.n_kv, CTX, m.hd)
+    x = O.synth_normal(m.H, SEED, 3)
+    t_fw, t_head = [], []
+    for r in range(reps):
+        t0 = time.perf_counter()
+        ref.forward(1, CTX + r)
+        t_fw.append(time.perf_counter() - t0)
+        t0 = time.perf_counter()
+        O.ref_matvec(5, m.lm_head, m.vocab, m.H, x)
+        t_head.append(time.perf_counter() - t0)
+    ref.close()
+    R.ref_set_threads(1)
+    fw, head = min(t_fw), min(t_head)
+    return head + LLAMA8B["n_layers"] * max(fw - head, 0.0) / n_layers_sample
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import guanaco_b200 as gb
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    peak, peak_kind = peaks()
+    K, W = args.steps, args.warmup
+    c = LLAMA8B
+    max_seq = CTX + 2 * (W + K) + 64
+    dm = gb.DecodeModel(c["hidden_dim"], c["n_heads"], c["n_kv_heads"], c["n_layers"], c["ff_dim"],
+                        c["vocab_size"], max_seq)
+    dm.synthesize(SEED)
+    dm.fill_kv(CTX, SEED)
+    st = torch.cuda.Stream()
+    d_tok = torch.tensor([1], dtype=torch.int32, device="cuda")
+    d_pos = torch.tensor([CTX], dtype=torch.int32, device="cuda")
+    toks = torch.zeros(max(W, K) + 1, dtype=torch.int32, device="cuda")
+    dm.generate(d_tok, d_pos, W, toks, stream=st.cuda_stream)
+    st.synchronize()
+    if dm.error() != 0:
+        raise RuntimeError(f"decode error {dm.error()}")
+    pos_timed0 = CTX + W
+
+    with Clocks(local_rank) as clk:
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        dm.generate(d_tok, d_pos, K, toks, stream=st.cuda_stream)
+        e1.record(st)
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+    t_ms = e0.elapsed_time(e1)
+    if dist:
+        tt = torch.tensor([t_ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_ms = float(tt.item())
+    if dm.error() != 0:
+        raise RuntimeError(f"decode error {dm.error()}")
+    tokens = world * K
+    value = tokens / (t_ms / 1e3)
+    ms_per_step = t_ms / K
+
+    # e2e: the host-buffer C-ABI call, token in / next token out per step
+    pos = CTX + W + K
+    tok = 1
+    for _ in range(3):
+        tok = dm.decode_host(tok, pos)
+        pos += 1
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(K):
+        tok = dm.decode_host(tok, pos)
+        pos += 1
+    t_e2e = time.perf_counter() - t0
+    if dist:
+        tt = torch.tensor([t_e2e], dtype=torch.float64, device="cuda")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        t_e2e = float(tt.item())
+    e2e = world * K / t_e2e
+
+    step_bytes = dm.step_bytes(pos_timed0 + K // 2)
+    kernels, main = (None, None)
+    if rank == 0:
+        kernels, main = kernel_benchmarks(gb, torch, dm, peak)
+    launches = dm.launches_per_step() * K + K   # + the feedback kernel per step
+    dm.close()
+
+    line = None
+    if rank == 0:
+        gbs, alg, t_launch = main
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cores = os.cpu_count() or 1
+            tt = cpu_reference_token_time(cores)
+            if tt:
+                cpu = {"value": round(1.0 / tt, 4), "unit": "tokens/s", "cores": cores, "kind": "reference",
+                       "sample": "reference forward() (oracle/_ref) on the Llama-8B config at pos 4096: one "
+                                 "layer + output head timed, head timed alone, token = head + 32 x layer; "
+                                 "Q4_K matvec uses all cores, Q6_K is single-threaded in the reference"}
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init weights, ~N(0,1) KV fill)",
+            "config": {"workload": "llama3.1-8b-q4km-decode (BASELINE config 4)", "global_batch": world,
+                       "seq_len": CTX, "parallelism": f"replicas{world}" if world > 1 else "single",
+                       "weights": "Q4_K + Q6_K(attn_v, ffn_down, output)", "kv": "fp32 head-major",
+                       "l2": "weights 4.9 GB stream every step (> 126 MB L2); no flush needed",
+                       "positions": [pos_timed0, pos_timed0 + K - 1],
+                       "step_alg_bytes": round(step_bytes), "step_hbm_frac": round(step_bytes / (t_ms / K * 1e-3) / 1e9 / peak, 3)},
+            "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4,
+                    "api": "gb_model_decode_host (token, pos in; next token out)"},
+            "gpu_launches": launches,
+            "roofline": {"bound": "hbm", "kernel": "q4k_matvec 14336x4096 (gate/up)", "achieved": round(gbs, 1),
+                         "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 3), "traffic": ncu_traffic(),
+                         "alg_bytes_per_launch": alg, "peak_kind": peak_kind},
+            "kernels": kernels,
+            "cpu_baseline": cpu,
+            "clocks": clk.summary(),
+        }
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return line
+
+
+# ---------------------------------------------------------------- reference arm
+def run_reference(args, rank, world):
+    """The reference's own CPU implementation of the path (oracle/_ref: the
+    reference C sources compiled unchanged) on the host cores, same metric.
+    Each step is a bounded sample (see cpu_reference_token_time)."""
+    if rank != 0:
+        return None
+    from oracle import oracle as O
+    if not O.ref_available():
+        return {"impl": "reference", "unavailable": "oracle/_ref/libref.so was not built"}
+    cores = os.cpu_count() or 1
+    for _ in range(max(0, min(args.warmup, 1))):
+        cpu_reference_token_time(cores, reps=1)
+    times = [cpu_reference_token_time(cores, reps=1) for _ in range(args.steps_ref)]
+    tt = statistics.median(times)
+    v = 1.0 / tt
+    return {"metric": METRIC, "value": round(v, 4), "unit": "tokens/s", "n_gpus": world, "steps": len(times),
+            "warmup": args.warmup, "ms_per_step": round(tt * 1e3, 1), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": "llama3.1-8b-q4km-decode (BASELINE config 4)", "global_batch": 1,
+                       "seq_len": CTX, "parallelism": "host threads"},
+            "cpu_baseline": {"value": round(v, 4), "unit": "tokens/s", "cores": cores, "kind": "reference",
+                             "sample": "per step: reference forward() with one Llama-8B layer + output head at "
+                                       "pos 4096, output head timed alone; token = head + 32 x layer"},
+            "e2e": {"value": round(v, 4), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--steps-ref", type=int, default=None, help="reference arm samples (default min(steps, 5))")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    args.steps_ref = args.steps_ref or max(1, min(args.steps, 5))
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+    else:
+        line = run_ours(args, rank, world, local_rank)
+    if rank == 0 and line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,289 @@
+// gb_attn.cu -- single-query GQA decode attention fused with RoPE and the KV
+// append, split across CTAs over the context and merged with an online-softmax
+// reduction.
+//
+// Reference semantics (T = 1): src/engine/engine.c:372-509 --
+//   rope(q, k, pos)                       kernels_cpu.c:391-431
+//   kv_cache_append(k, v, pos)            kv_cache.c:95-128 (slot pos % max_seq)
+//   for each q head h, kv head h / (n_heads / n_kv):
+//     s = (q . K[t]) * (1/sqrt(hd)),  p = softmax(s over t = 0..pos),
+//     out_h = sum_t p_t V[t]
+// Replaces cuda_update_kv_cache_kernel, cuda_attn_scores_kernel_gqa,
+// cuda_softmax_kernel and cuda_attn_context_kernel_gqa
+// (src/kernels/cuda/cuda_layer_kernels.cu:425-504).
+//
+// Layout: the KV cache keeps the reference's fp32 head-major layout
+// [n_kv][max_seq][head_dim] per layer (kv_cache.c:90-93).
+//
+// Shape: grid = n_kv * grid_splits CTAs of 256 threads.  A CTA owns one KV
+// head and P consecutive positions (P from pos, so the active splits fill the
+// grid); it serves all GROUP = n_heads / n_kv query heads of that KV head, so
+// each K and V row is read from HBM exactly once.
+//   pass 1: LPP lanes share one K row (DPL dims each, 128-bit loads), dot
+//           products for all GROUP heads, shuffle-reduced -> scores in smem;
+//   pass 2: per-head max / exp / sum over the split;
+//   pass 3: V rows (one per VL lanes) accumulate p * V for all heads; the
+//           8 warps reduce through shared memory;
+//   merge:  each CTA publishes (m, l, o[hd]) per head; the last CTA of the KV
+//           head (atomic ticket) combines the splits and resets the ticket.
+// pos comes from device memory so the launch can live inside a CUDA graph;
+// a pos outside [0, max_seq) sets the error word and touches nothing.
+#include "gb_common.cuh"
+#include "gb_internal.h"
+
+namespace gb {
+
+constexpr int ATTN_THREADS = 256;
+constexpr int ATTN_MAX_P = 1024;
+
+int attn_grid_splits(int n_kv, int max_seq) {
+    const int a = (2 * GB_NUM_SMS + n_kv - 1) / n_kv;
+    const int b = (max_seq + ATTN_MAX_P - 1) / ATTN_MAX_P;
+    return a > b ? a : b;
+}
+
+template <int HD, int GROUP>
+struct AttnCfg {
+    static constexpr int DPL = GROUP <= 4 ? 16 : 8;   // K dims per lane
+    static constexpr int LPP = HD / DPL;              // lanes per K row
+    static constexpr int PPW = 32 / LPP;              // K rows per warp step
+    static constexpr int VL = HD / 4;                 // lanes per V row
+    static constexpr int RPW = 32 / VL;               // V rows per warp step
+    static constexpr int RED = 8 * RPW * GROUP * HD;  // pass-3 reduction floats
+    static constexpr int SF = ATTN_MAX_P * 8;         // score buffer floats
+    static_assert(RED <= SF, "reduction buffer aliases the score buffer");
+    static constexpr size_t SMEM = (size_t)(GROUP * HD + 2 * HD + SF + 16) * sizeof(float);
+};
+
+template <int HD, int GROUP>
+__global__ void __launch_bounds__(ATTN_THREADS)
+k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const float* __restrict__ vnew,
+              float* __restrict__ kc, float* __restrict__ vc, const float* __restrict__ rope_cs,
+              const int* __restrict__ d_pos, int n_kv, int max_seq, int grid_splits,
+              float* __restrict__ out, float* __restrict__ part, unsigned* __restrict__ tickets) {
+    using C = AttnCfg<HD, GROUP>;
+    extern __shared__ __align__(16) float sm[];
+    float* qs = sm;                       // [GROUP][HD] rotated q
+    float* kn = qs + GROUP * HD;          // [HD] rotated new k
+    float* vn = kn + HD;                  // [HD] new v
+    float* S = vn + HD;                   // [P][8] scores, then probabilities
+    float* st = S + C::SF;                // [GROUP] max, [GROUP] sum (8 + 8)
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int kvh = blockIdx.x / grid_splits, split = blockIdx.x % grid_splits;
+    const int pos = *d_pos;
+    unsigned* err = tickets + n_kv;
+    if (pos < 0 || pos >= max_seq) {
+        if (blockIdx.x == 0 && tid == 0) atomicExch(err, (unsigned)(-GB_EPOS));
+        return;
+    }
+    const int seq = pos + 1;
+    int P = (seq + grid_splits - 1) / grid_splits;
+    P = (P + 31) & ~31;
+    const int nsplit = (seq + P - 1) / P;
+    if (split >= nsplit) return;
+    const int s0 = split * P, n = min(seq, s0 + P) - s0;
+    const bool owner = pos >= s0 && pos < s0 + n;   // this split holds the new row
+
+    // ---- RoPE (reference rounding: a*c - b*s, a*s + b*c, no contraction)
+    const float* cs = rope_cs + (size_t)pos * HD;
+    for (int e = tid; e < (GROUP + 1) * (HD / 2); e += ATTN_THREADS) {
+        const int h = e / (HD / 2), i = e % (HD / 2);
+        const float* src = h < GROUP ? q + (size_t)(kvh * GROUP + h) * HD : knew + (size_t)kvh * HD;
+        float* dst = h < GROUP ? qs + h * HD : kn;
+        const float a = src[2 * i], b = src[2 * i + 1], c = cs[2 * i], s = cs[2 * i + 1];
+        dst[2 * i] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+        dst[2 * i + 1] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+    }
+    for (int i = tid; i < HD; i += ATTN_THREADS) vn[i] = vnew[(size_t)kvh * HD + i];
+    __syncthreads();
+
+    const size_t head_base = (size_t)kvh * max_seq * HD;
+    if (owner) {   // KV append at slot pos (the ring index pos % max_seq == pos here)
+        for (int i = tid; i < HD; i += ATTN_THREADS) {
+            kc[head_base + (size_t)pos * HD + i] = kn[i];
+            vc[head_base + (size_t)pos * HD + i] = vn[i];
+        }
+    }
+
+    // ---- pass 1: scores
+    const float scale = 1.0f / sqrtf((float)HD);
+    {
+        const int lp = lane % C::LPP, pw = lane / C::LPP;
+        float qr[GROUP][C::DPL];
+#pragma unroll
+        for (int h = 0; h < GROUP; h++)
+#pragma unroll
+            for (int j = 0; j < C::DPL / 4; j++) {
+                const float4 v = *reinterpret_cast<const float4*>(qs + h * HD + j * C::LPP * 4 + lp * 4);
+                qr[h][4 * j] = v.x; qr[h][4 * j + 1] = v.y; qr[h][4 * j + 2] = v.z; qr[h][4 * j + 3] = v.w;
+            }
+        for (int base = warp * C::PPW; base < n; base += 8 * C::PPW) {
+            const int s = base + pw;
+            const int gs = s0 + (s < n ? s : 0);
+            float4 kr[C::DPL / 4];
+            const float* krow = (gs == pos) ? kn : kc + head_base + (size_t)gs * HD;
+#pragma unroll
+            for (int j = 0; j < C::DPL / 4; j++) {
+                const float* p = krow + j * C::LPP * 4 + lp * 4;
+                kr[j] = (gs == pos) ? *reinterpret_cast<const float4*>(p) : __ldg(reinterpret_cast<const float4*>(p));
+            }
+            float dots[GROUP];
+#pragma unroll
+            for (int h = 0; h < GROUP; h++) {
+                float2 a = make_float2(0.f, 0.f);
+#pragma unroll
+                for (int j = 0; j < C::DPL / 4; j++) {
+                    a = ffma2(make_float2(qr[h][4 * j], qr[h][4 * j + 1]), make_float2(kr[j].x, kr[j].y), a);
+                    a = ffma2(make_float2(qr[h][4 * j + 2], qr[h][4 * j + 3]), make_float2(kr[j].z, kr[j].w), a);
+                }
+                float d = a.x + a.y;
+#pragma unroll
+                for (int o = C::LPP / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+                dots[h] = d;
+            }
+            if (s < n && lp < GROUP) {
+                float v = dots[0];
+#pragma unroll
+                for (int h = 1; h < GROUP; h++) if (lp == h) v = dots[h];
+                S[s * 8 + lp] = __fmul_rn(v, scale);
+            }
+        }
+    }
+    __syncthreads();
+
+    // ---- pass 2: per-head max, exp, sum over this split
+    if (warp < GROUP) {
+        const int h = warp;
+        float m = -INFINITY;
+        for (int s = lane; s < n; s += 32) m = fmaxf(m, S[s * 8 + h]);
+        m = warp_max(m);
+        float l = 0.f;
+        for (int s = lane; s < n; s += 32) {
+            const float p = expf(S[s * 8 + h] - m);
+            S[s * 8 + h] = p;
+            l += p;
+        }
+        l = warp_sum(l);
+        if (lane == 0) { st[h] = m; st[8 + h] = l; }
+    }
+    __syncthreads();
+
+    // ---- pass 3: o_h = sum_s p_h[s] V[s]
+    float4 acc[GROUP];
+#pragma unroll
+    for (int h = 0; h < GROUP; h++) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int vl = lane % C::VL, vr = lane / C::VL;
+    for (int s = warp * C::RPW + vr; s < n; s += 8 * C::RPW) {
+        const int gs = s0 + s;
+        const float4 vv = (gs == pos) ? *reinterpret_cast<const float4*>(vn + vl * 4)
+                                      : __ldg(reinterpret_cast<const float4*>(vc + head_base + (size_t)gs * HD + vl * 4));
+        float p[8];
+        const float4 p0 = *reinterpret_cast<const float4*>(S + s * 8);
+        p[0] = p0.x; p[1] = p0.y; p[2] = p0.z; p[3] = p0.w;
+        if (GROUP > 4) {
+            const float4 p1 = *reinterpret_cast<const float4*>(S + s * 8 + 4);
+            p[4] = p1.x; p[5] = p1.y; p[6] = p1.z; p[7] = p1.w;
+        }
+#pragma unroll
+        for (int h = 0; h < GROUP; h++) {
+            float2 lo = ffma2(make_float2(p[h], p[h]), make_float2(vv.x, vv.y), make_float2(acc[h].x, acc[h].y));
+            float2 hi = ffma2(make_float2(p[h], p[h]), make_float2(vv.z, vv.w), make_float2(acc[h].z, acc[h].w));
+            acc[h] = make_float4(lo.x, lo.y, hi.x, hi.y);
+        }
+    }
+    __syncthreads();   // S is dead from here on; reuse it as the reduction buffer
+    float* red = S;
+#pragma unroll
+    for (int h = 0; h < GROUP; h++)
+        *reinterpret_cast<float4*>(red + ((warp * C::RPW + vr) * GROUP + h) * HD + vl * 4) = acc[h];
+    __syncthreads();
+
+    const bool single = nsplit == 1;
+    float* my = part + ((size_t)kvh * grid_splits + split) * GROUP * (HD + 2);
+    for (int e = tid; e < GROUP * HD; e += ATTN_THREADS) {
+        float o = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8 * C::RPW; w++) o += red[w * GROUP * HD + e];
+        const int h = e / HD, d = e % HD;
+        if (single) out[(size_t)(kvh * GROUP + h) * HD + d] = o / st[8 + h];
+        else my[h * (HD + 2) + 2 + d] = o;
+    }
+    if (single) return;
+    if (tid < GROUP) { my[tid * (HD + 2)] = st[tid]; my[tid * (HD + 2) + 1] = st[8 + tid]; }
+
+    // ---- merge in the last CTA of this KV head
+    __shared__ unsigned last;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last = (atomicAdd(&tickets[kvh], 1u) == (unsigned)(nsplit - 1));
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    const float* base = part + (size_t)kvh * grid_splits * GROUP * (HD + 2);
+    for (int e = tid; e < GROUP * HD; e += ATTN_THREADS) {
+        const int h = e / HD, d = e % HD;
+        float M = -INFINITY;
+        for (int j = 0; j < nsplit; j++) M = fmaxf(M, __ldcg(base + ((size_t)j * GROUP + h) * (HD + 2)));
+        float L = 0.f, O = 0.f;
+        for (int j = 0; j < nsplit; j++) {
+            const float* pj = base + ((size_t)j * GROUP + h) * (HD + 2);
+            const float w = expf(__ldcg(pj) - M);
+            L = fmaf(__ldcg(pj + 1), w, L);
+            O = fmaf(__ldcg(pj + 2 + d), w, O);
+        }
+        out[(size_t)(kvh * GROUP + h) * HD + d] = O / L;
+    }
+    if (tid == 0) tickets[kvh] = 0u;   // every split has arrived: safe to rearm
+}
+
+template <int HD, int GROUP>
+static cudaError_t launch_attn(const float* q, const float* k, const float* v, float* kc, float* vc,
+                               const float* cs, const int* d_pos, int n_kv, int max_seq, float* out,
+                               void* ws, cudaStream_t st) {
+    using C = AttnCfg<HD, GROUP>;
+    static unsigned configured = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(configured & (1u << (dev & 31)))) {
+        cudaError_t e = cudaFuncSetAttribute(k_attn_decode<HD, GROUP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)C::SMEM);
+        if (e != cudaSuccess) return e;
+        configured |= 1u << (dev & 31);
+    }
+    const int G = attn_grid_splits(n_kv, max_seq);
+    float* part = static_cast<float*>(ws);
+    unsigned* tickets = reinterpret_cast<unsigned*>(part + (size_t)n_kv * G * GROUP * (HD + 2));
+    k_attn_decode<HD, GROUP><<<n_kv * G, ATTN_THREADS, C::SMEM, st>>>(q, k, v, kc, vc, cs, d_pos, n_kv, max_seq, G,
+                                                                      out, part, tickets);
+    return cudaGetLastError();
+}
+
+}  // namespace gb
+
+using namespace gb;
+
+extern "C" size_t gb_attn_workspace_bytes(int n_heads, int n_kv, int head_dim, int max_seq) {
+    if (n_kv <= 0 || n_heads % n_kv) return 0;
+    const int group = n_heads / n_kv;
+    const int G = attn_grid_splits(n_kv, max_seq);
+    const size_t part = (size_t)n_kv * G * group * (head_dim + 2) * sizeof(float);
+    return part + (size_t)(n_kv + 1) * sizeof(unsigned);
+}
+
+extern "C" int gb_attention_decode(const float* q, const float* k, const float* v, float* k_cache, float* v_cache,
+                                   const float* rope_cs, const int* d_pos, int n_heads, int n_kv, int head_dim,
+                                   int max_seq, float* out, void* ws, void* stream) {
+    if (!q || !k || !v || !k_cache || !v_cache || !rope_cs || !d_pos || !out || !ws) return GB_EINVAL;
+    if (n_kv <= 0 || n_heads <= 0 || n_heads % n_kv || max_seq <= 0) return GB_EINVAL;
+    const int group = n_heads / n_kv;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaErrorInvalidValue;
+#define GB_ATTN_CASE(HDV, GV) \
+    if (head_dim == HDV && group == GV) e = launch_attn<HDV, GV>(q, k, v, k_cache, v_cache, rope_cs, d_pos, n_kv, max_seq, out, ws, st);
+    GB_ATTN_CASE(128, 1) GB_ATTN_CASE(128, 2) GB_ATTN_CASE(128, 4) GB_ATTN_CASE(128, 8)
+    GB_ATTN_CASE(64, 1) GB_ATTN_CASE(64, 2) GB_ATTN_CASE(64, 4) GB_ATTN_CASE(64, 8)
+#undef GB_ATTN_CASE
+    if (e == cudaErrorInvalidValue) return GB_EINVAL;
+    return e == cudaSuccess ? GB_OK : GB_ECUDA;
+}

@@ -1,0 +1,551 @@
+// gb_layer.cu -- layer glue kernels and the device-resident decode model.
+//
+// The model runs forward() of src/engine/engine.c:559-594 for one token
+// (T = 1) entirely on the device:
+//   embedding row dequant                        engine.c:214-283
+//   per layer (engine.c:353-554):
+//     rmsnorm -> Wq, Wk, Wv -> RoPE + KV append + attention -> Wo (+residual)
+//     -> rmsnorm -> gate, up -> silu(gate)*up -> down (+residual)
+//   final rmsnorm -> lm_head -> greedy argmax (tokenizer.c:175-185)
+// The whole step is captured once into a CUDA graph (token and position are
+// read from device memory) and replayed per token.
+#include "gb_common.cuh"
+#include "gb_internal.h"
+
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <vector>
+
+namespace gb {
+
+// ---------------------------------------------------------------- glue kernels
+__device__ __forceinline__ float block_sum_1024(float v, float* sh) {
+    v = warp_sum(v);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) sh[warp] = v;
+    __syncthreads();
+    v = (threadIdx.x < (blockDim.x >> 5)) ? sh[threadIdx.x] : 0.f;
+    if (warp == 0) v = warp_sum(v);
+    if (threadIdx.x == 0) sh[32] = v;
+    __syncthreads();
+    const float r = sh[32];
+    __syncthreads();
+    return r;
+}
+
+// out = w * (x * r), r = 1/sqrt(sum(x^2)/n + eps)  (kernels_cpu.c:242-263)
+__global__ void __launch_bounds__(1024) k_rmsnorm(const float* __restrict__ x, const float* __restrict__ w,
+                                                  float* __restrict__ out, int n, float eps) {
+    __shared__ float sh[33];
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
+    ss = block_sum_1024(ss, sh);
+    const float r = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)n), eps)));
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+        out[i] = __fmul_rn(w ? w[i] : 1.0f, __fmul_rn(x[i], r));
+}
+
+// gate = (gate * (1/(1+exp(-gate)))) * up  (kernels_cpu.c:323-336, 381-384)
+__global__ void k_silu_mul(float* __restrict__ g, const float* __restrict__ u, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float x = g[i];
+    const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));
+    g[i] = __fmul_rn(__fmul_rn(x, sig), u[i]);
+}
+
+// First index of the maximum, strict > (ties keep the lower index).
+__global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ x, int n, int* __restrict__ out) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = x[i];
+        if (v > bv) { bv = v; bi = i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) { sv[warp] = bv; si[warp] = bi; }
+    __syncthreads();
+    if (warp == 0) {
+        const int nw = blockDim.x >> 5;
+        bv = lane < nw ? sv[lane] : -INFINITY;
+        bi = lane < nw ? si[lane] : 0x7fffffff;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+        if (lane == 0) *out = bi == 0x7fffffff ? 0 : bi;
+    }
+}
+
+// Embedding row of *d_token (engine.c:214-283): F32 copy, Q8_0 q*scale,
+// Q4_K d1*q - m1 -- bit-exact with the reference dequantiser.
+__global__ void k_embed(const void* __restrict__ emb, int dtype, const int* __restrict__ d_token, int vocab, int H,
+                        float* __restrict__ out, unsigned* __restrict__ err) {
+    const int tok = *d_token;
+    if (tok < 0 || tok >= vocab) {
+        if (threadIdx.x == 0 && blockIdx.x == 0 && err) atomicExch(err, (unsigned)(-GB_EINVAL));
+        return;
+    }
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < H; i += gridDim.x * blockDim.x) {
+        if (dtype == GB_DT_F32) {
+            out[i] = static_cast<const float*>(emb)[(size_t)tok * H + i];
+        } else if (dtype == GB_DT_Q8_0) {
+            const uint8_t* blk = static_cast<const uint8_t*>(emb) + ((size_t)tok * (H / 32) + i / 32) * GB_Q80_BYTES;
+            out[i] = __fmul_rn((float)(int8_t)blk[2 + (i & 31)], f16_bits_to_f32(blk[0] | (blk[1] << 8)));
+        } else {   // Q4_K
+            const uint8_t* blk = static_cast<const uint8_t*>(emb) + ((size_t)tok * (H / 256) + i / 256) * GB_Q4K_BYTES;
+            const int w = i & 255, g = w >> 6, hi = (w >> 5) & 1, l = w & 31, j = 2 * g + hi;
+            const uint8_t* s = blk + 4;
+            uint32_t sc, mn;
+            if (j < 4) { sc = s[j] & 63; mn = s[j + 4] & 63; }
+            else { sc = (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4); mn = (s[j + 4] >> 4) | ((s[j] >> 6) << 4); }
+            const float d_all = f16_bits_to_f32(blk[0] | (blk[1] << 8));
+            const float min_all = f16_bits_to_f32(blk[2] | (blk[3] << 8));
+            const uint8_t qb = blk[16 + 32 * g + l];
+            const uint32_t q = hi ? (qb >> 4) : (qb & 0xF);
+            out[i] = __fsub_rn(__fmul_rn(__fmul_rn(d_all, (float)sc), (float)q), __fmul_rn(min_all, (float)mn));
+        }
+    }
+}
+
+__global__ void k_set_int(int* p, int v) { *p = v; }
+// Feed the greedy token back and move to the next position; record it.
+__global__ void k_advance(int* tok, const int* next, int* pos, int* out, int* count) {
+    *tok = *next;
+    *pos += 1;
+    if (out) out[*count] = *next;
+    *count += 1;
+}
+
+}  // namespace gb
+
+using namespace gb;
+
+// ---------------------------------------------------------------- glue C ABI
+extern "C" int gb_rmsnorm(const float* x, const float* w, float* out, int n, float eps, void* stream) {
+    if (!x || !out || n <= 0) return GB_EINVAL;
+    k_rmsnorm<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(x, w, out, n, eps);
+    return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
+}
+extern "C" int gb_silu_mul(float* gate, const float* up, int n, void* stream) {
+    if (!gate || !up || n <= 0) return GB_EINVAL;
+    k_silu_mul<<<(n + 255) / 256, 256, 0, static_cast<cudaStream_t>(stream)>>>(gate, up, n);
+    return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
+}
+extern "C" int gb_argmax(const float* x, int n, int* d_out, void* stream) {
+    if (!x || !d_out || n <= 0) return GB_EINVAL;
+    k_argmax<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(x, n, d_out);
+    return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
+}
+
+extern "C" void gb_host_rope_table(float* h_cs, int max_seq, int head_dim, float theta);  // gb_host.c
+
+extern "C" int gb_rope_table(float* cs, int max_seq, int head_dim, float theta, void* stream) {
+    if (!cs || max_seq <= 0 || head_dim <= 0 || (head_dim & 1)) return GB_EINVAL;
+    const size_t n = (size_t)max_seq * head_dim;
+    float* h = nullptr;
+    if (cudaMallocHost(&h, n * sizeof(float)) != cudaSuccess) return GB_ENOMEM;
+    gb_host_rope_table(h, max_seq, head_dim, theta);
+    cudaError_t e = cudaMemcpyAsync(cs, h, n * sizeof(float), cudaMemcpyHostToDevice, static_cast<cudaStream_t>(stream));
+    if (e == cudaSuccess) e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    cudaFreeHost(h);
+    return e == cudaSuccess ? GB_OK : GB_ECUDA;
+}
+
+extern "C" const char* gb_version(void) { return "guanaco_b200 0.1 (sm_100a)"; }
+extern "C" int gb_device_sm_count(void) {
+    int dev = 0, n = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    return n;
+}
+
+// ---------------------------------------------------------------- model
+struct gb_model {
+    gb_model_config c;
+    int kv_dim = 0;
+    std::vector<const void*> w;       // [n_layers * 7]
+    std::vector<int> dt;              // [n_layers * 7]
+    std::vector<const float*> ra, rf; // [n_layers]
+    const void* emb = nullptr;
+    int emb_dt = GB_DT_Q4_K;
+    const float* rms_final = nullptr;
+    const void* lm = nullptr;
+    int lm_dt = GB_DT_Q6_K;
+    std::vector<void*> owned;         // allocations freed with the model
+
+    float *kc = nullptr, *vc = nullptr, *rope = nullptr;
+    void* attn_ws = nullptr;
+    float *hidden = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr;
+    float *gate = nullptr, *up = nullptr, *logits = nullptr;
+    unsigned* err = nullptr;
+    int *d_tok = nullptr, *d_pos = nullptr, *d_next = nullptr;
+    int* h_io = nullptr;              // pinned {token, pos, next}
+    cudaStream_t stream = nullptr;
+
+    cudaGraphExec_t exec = nullptr;
+    const void* key[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+    cudaGraphExec_t gen_exec = nullptr;   // step + advance, for gb_model_generate
+    const void* gen_key[4] = {nullptr, nullptr, nullptr, nullptr};
+    int* d_count = nullptr;
+};
+
+static void* dalloc(gb_model* m, size_t bytes) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) return nullptr;
+    m->owned.push_back(p);
+    return p;
+}
+
+extern "C" gb_model* gb_model_create(const gb_model_config* cfg) {
+    if (!cfg) return nullptr;
+    const gb_model_config& c = *cfg;
+    if (c.hidden_dim <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.n_heads % c.n_kv_heads ||
+        c.head_dim * c.n_heads != c.hidden_dim || c.n_layers <= 0 || c.ff_dim <= 0 || c.vocab_size <= 0 ||
+        c.max_seq <= 0)
+        return nullptr;
+    gb_model* m = new gb_model();
+    m->c = c;
+    m->kv_dim = c.n_kv_heads * c.head_dim;
+    m->w.assign((size_t)c.n_layers * GB_NMAT, nullptr);
+    m->dt.assign((size_t)c.n_layers * GB_NMAT, GB_DT_Q4_K);
+    m->ra.assign(c.n_layers, nullptr);
+    m->rf.assign(c.n_layers, nullptr);
+    const size_t kv_elems = (size_t)c.n_layers * m->kv_dim * c.max_seq;
+    bool ok = true;
+    ok &= (m->kc = (float*)dalloc(m, kv_elems * 4)) != nullptr;
+    ok &= (m->vc = (float*)dalloc(m, kv_elems * 4)) != nullptr;
+    ok &= (m->rope = (float*)dalloc(m, (size_t)c.max_seq * c.head_dim * 4)) != nullptr;
+    const size_t ws = gb_attn_workspace_bytes(c.n_heads, c.n_kv_heads, c.head_dim, c.max_seq);
+    ok &= ws > 0 && (m->attn_ws = dalloc(m, ws)) != nullptr;
+    const int H = c.hidden_dim, F = c.ff_dim;
+    ok &= (m->hidden = (float*)dalloc(m, (size_t)H * 4)) != nullptr;
+    ok &= (m->xn = (float*)dalloc(m, (size_t)(H > F ? H : F) * 4)) != nullptr;
+    ok &= (m->q = (float*)dalloc(m, (size_t)H * 4)) != nullptr;
+    ok &= (m->k = (float*)dalloc(m, (size_t)m->kv_dim * 4)) != nullptr;
+    ok &= (m->v = (float*)dalloc(m, (size_t)m->kv_dim * 4)) != nullptr;
+    ok &= (m->attn = (float*)dalloc(m, (size_t)H * 4)) != nullptr;
+    ok &= (m->gate = (float*)dalloc(m, (size_t)F * 4)) != nullptr;
+    ok &= (m->up = (float*)dalloc(m, (size_t)F * 4)) != nullptr;
+    ok &= (m->logits = (float*)dalloc(m, (size_t)c.vocab_size * 4)) != nullptr;
+    ok &= (m->err = (unsigned*)dalloc(m, 16)) != nullptr;
+    ok &= (m->d_tok = (int*)dalloc(m, 16)) != nullptr;
+    ok &= (m->d_pos = (int*)dalloc(m, 16)) != nullptr;
+    ok &= (m->d_next = (int*)dalloc(m, 16)) != nullptr;
+    ok &= (m->d_count = (int*)dalloc(m, 16)) != nullptr;
+    ok &= cudaMallocHost(&m->h_io, 4 * sizeof(int)) == cudaSuccess;
+    ok &= cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) == cudaSuccess;
+    if (ok) ok &= cudaMemset(m->kc, 0, kv_elems * 4) == cudaSuccess && cudaMemset(m->vc, 0, kv_elems * 4) == cudaSuccess;
+    if (ok) ok &= cudaMemset(m->attn_ws, 0, ws) == cudaSuccess && cudaMemset(m->err, 0, 16) == cudaSuccess;
+    if (ok) ok &= gb_rope_table(m->rope, c.max_seq, c.head_dim, c.rope_theta, m->stream) == GB_OK;
+    if (!ok) {
+        gb_model_destroy(m);
+        return nullptr;
+    }
+    return m;
+}
+
+extern "C" void gb_model_destroy(gb_model* m) {
+    if (!m) return;
+    if (m->exec) cudaGraphExecDestroy(m->exec);
+    if (m->gen_exec) cudaGraphExecDestroy(m->gen_exec);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    for (void* p : m->owned) cudaFree(p);
+    if (m->h_io) cudaFreeHost(m->h_io);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+}
+
+static void invalidate_graph(gb_model* m) {
+    if (m->exec) { cudaGraphExecDestroy(m->exec); m->exec = nullptr; }
+    if (m->gen_exec) { cudaGraphExecDestroy(m->gen_exec); m->gen_exec = nullptr; }
+}
+
+extern "C" int gb_model_set_matrix(gb_model* m, int layer, int which, int dtype, const void* d_w) {
+    if (!m || layer < 0 || layer >= m->c.n_layers || which < 0 || which >= GB_NMAT || !d_w) return GB_EINVAL;
+    if (dtype != GB_DT_Q4_K && dtype != GB_DT_Q6_K && dtype != GB_DT_Q8_0) return GB_EINVAL;
+    m->w[(size_t)layer * GB_NMAT + which] = d_w;
+    m->dt[(size_t)layer * GB_NMAT + which] = dtype;
+    invalidate_graph(m);
+    return GB_OK;
+}
+extern "C" int gb_model_set_norms(gb_model* m, int layer, const float* a, const float* f) {
+    if (!m || layer < 0 || layer >= m->c.n_layers || !a || !f) return GB_EINVAL;
+    m->ra[layer] = a;
+    m->rf[layer] = f;
+    invalidate_graph(m);
+    return GB_OK;
+}
+extern "C" int gb_model_set_head(gb_model* m, int emb_dtype, const void* emb, const float* rms_final, int lm_dtype,
+                                 const void* lm) {
+    if (!m || !emb || !rms_final || !lm) return GB_EINVAL;
+    if (emb_dtype != GB_DT_Q4_K && emb_dtype != GB_DT_Q8_0 && emb_dtype != GB_DT_F32) return GB_EINVAL;
+    m->emb = emb; m->emb_dt = emb_dtype; m->rms_final = rms_final; m->lm = lm; m->lm_dt = lm_dtype;
+    invalidate_graph(m);
+    return GB_OK;
+}
+
+extern "C" float* gb_model_k_cache(gb_model* m, int layer) {
+    return (m && layer >= 0 && layer < m->c.n_layers) ? m->kc + (size_t)layer * m->kv_dim * m->c.max_seq : nullptr;
+}
+extern "C" float* gb_model_v_cache(gb_model* m, int layer) {
+    return (m && layer >= 0 && layer < m->c.n_layers) ? m->vc + (size_t)layer * m->kv_dim * m->c.max_seq : nullptr;
+}
+
+// Matrix shapes per slot: (rows, cols).
+static void mat_shape(const gb_model* m, int which, int* rows, int* cols) {
+    const int H = m->c.hidden_dim, F = m->c.ff_dim, KV = m->kv_dim;
+    static const int R[GB_NMAT] = {0, 1, 1, 0, 2, 2, 0}, Cc[GB_NMAT] = {0, 0, 0, 0, 0, 0, 2};
+    const int dims[3] = {H, KV, F};
+    *rows = dims[R[which]];
+    *cols = which == GB_WDOWN ? F : H;
+    (void)Cc;
+}
+
+extern "C" int gb_model_synthesize(gb_model* m, uint64_t seed) {
+    if (!m) return GB_EINVAL;
+    const gb_model_config& c = m->c;
+    const int H = c.hidden_dim;
+    float* ones = (float*)dalloc(m, (size_t)H * 4);
+    if (!ones) return GB_ENOMEM;
+    int rc = gb_fill_f32(ones, H, 1.0f, m->stream);
+    if (rc) return rc;
+    for (int l = 0; l < c.n_layers; l++) {
+        for (int wi = 0; wi < GB_NMAT; wi++) {
+            const int dtype = (wi == GB_WV || wi == GB_WDOWN) ? GB_DT_Q6_K : GB_DT_Q4_K;
+            int rows, cols;
+            mat_shape(m, wi, &rows, &cols);
+            if (cols % 256) return GB_ESHAPE;
+            const size_t nblk = (size_t)rows * (cols / 256);
+            void* p = dalloc(m, nblk * gb_block_bytes(dtype) + 16);
+            if (!p) return GB_ENOMEM;
+            rc = gb_synth_blocks(dtype, p, nblk, seed, (uint64_t)(l * GB_NMAT + wi + 1), m->stream);
+            if (rc) return rc;
+            gb_model_set_matrix(m, l, wi, dtype, p);
+        }
+        gb_model_set_norms(m, l, ones, ones);
+    }
+    const size_t eblk = (size_t)c.vocab_size * (H / 256);
+    void* e = dalloc(m, eblk * GB_Q4K_BYTES);
+    void* lmp = dalloc(m, eblk * GB_Q6K_BYTES + 16);
+    if (!e || !lmp) return GB_ENOMEM;
+    if ((rc = gb_synth_blocks(GB_DT_Q4_K, e, eblk, seed, 1000001ull, m->stream))) return rc;
+    if ((rc = gb_synth_blocks(GB_DT_Q6_K, lmp, eblk, seed, 1000002ull, m->stream))) return rc;
+    gb_model_set_head(m, GB_DT_Q4_K, e, ones, GB_DT_Q6_K, lmp);
+    return cudaStreamSynchronize(m->stream) == cudaSuccess ? GB_OK : GB_ECUDA;
+}
+
+namespace gb {
+// One decode layer (engine.c:353-554) on stream st; shared by the model and
+// the drop-in cuda_transformer_layer_gpu.
+int enqueue_layer(const LayerArgs& a, cudaStream_t st) {
+    const int H = a.H, F = a.ff, KV = a.n_kv * a.hd;
+    int rc;
+    if ((rc = gb_rmsnorm(a.hidden, a.ra, a.xn, H, a.eps, st))) return rc;
+    if ((rc = gb_matvec(a.dt[GB_WQ], a.w[GB_WQ], a.n_heads * a.hd, H, a.xn, a.q, nullptr, st))) return rc;
+    if ((rc = gb_matvec(a.dt[GB_WK], a.w[GB_WK], KV, H, a.xn, a.k, nullptr, st))) return rc;
+    if ((rc = gb_matvec(a.dt[GB_WV], a.w[GB_WV], KV, H, a.xn, a.v, nullptr, st))) return rc;
+    if ((rc = gb_attention_decode(a.q, a.k, a.v, a.kc, a.vc, a.rope, a.d_pos, a.n_heads, a.n_kv, a.hd, a.max_seq,
+                                  a.attn, a.attn_ws, st)))
+        return rc;
+    if ((rc = gb_matvec(a.dt[GB_WO], a.w[GB_WO], H, a.n_heads * a.hd, a.attn, a.hidden, a.hidden, st))) return rc;
+    if ((rc = gb_rmsnorm(a.hidden, a.rf, a.xn, H, a.eps, st))) return rc;
+    if ((rc = gb_matvec(a.dt[GB_WGATE], a.w[GB_WGATE], F, H, a.xn, a.gate, nullptr, st))) return rc;
+    if ((rc = gb_matvec(a.dt[GB_WUP], a.w[GB_WUP], F, H, a.xn, a.up, nullptr, st))) return rc;
+    if ((rc = gb_silu_mul(a.gate, a.up, F, st))) return rc;
+    return gb_matvec(a.dt[GB_WDOWN], a.w[GB_WDOWN], H, F, a.gate, a.hidden, a.hidden, st);
+}
+
+int embed(const void* emb, int dtype, const int* d_token, int vocab, int H, float* out, unsigned* err, cudaStream_t st) {
+    k_embed<<<(H + 255) / 256, 256, 0, st>>>(emb, dtype, d_token, vocab, H, out, err);
+    return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
+}
+int set_device_int(int* p, int v, cudaStream_t st) {
+    k_set_int<<<1, 1, 0, st>>>(p, v);
+    return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
+}
+}  // namespace gb
+
+// Enqueue one decode step on stream st.
+static int enqueue_step(gb_model* m, const int* d_token, const int* d_pos, float* d_logits, int* d_next,
+                        cudaStream_t st) {
+    const gb_model_config& c = m->c;
+    const int H = c.hidden_dim;
+    int rc;
+    if ((rc = embed(m->emb, m->emb_dt, d_token, c.vocab_size, H, m->hidden, m->err, st))) return rc;
+    for (int l = 0; l < c.n_layers; l++) {
+        LayerArgs a;
+        for (int i = 0; i < GB_NMAT; i++) {
+            a.w[i] = m->w[(size_t)l * GB_NMAT + i];
+            a.dt[i] = m->dt[(size_t)l * GB_NMAT + i];
+        }
+        a.ra = m->ra[l]; a.rf = m->rf[l];
+        a.kc = gb_model_k_cache(m, l); a.vc = gb_model_v_cache(m, l);
+        a.rope = m->rope; a.d_pos = d_pos; a.attn_ws = m->attn_ws;
+        a.hidden = m->hidden; a.xn = m->xn; a.q = m->q; a.k = m->k; a.v = m->v; a.attn = m->attn;
+        a.gate = m->gate; a.up = m->up;
+        a.H = H; a.n_heads = c.n_heads; a.n_kv = c.n_kv_heads; a.hd = c.head_dim; a.ff = c.ff_dim;
+        a.max_seq = c.max_seq; a.eps = c.rms_eps;
+        if ((rc = enqueue_layer(a, st))) return rc;
+    }
+    if ((rc = gb_rmsnorm(m->hidden, m->rms_final, m->xn, H, c.rms_eps, st))) return rc;
+    float* lg = d_logits ? d_logits : m->logits;
+    if ((rc = gb_matvec(m->lm_dt, m->lm, c.vocab_size, H, m->xn, lg, nullptr, st))) return rc;
+    return gb_argmax(lg, c.vocab_size, d_next, st);
+}
+
+static bool model_ready(const gb_model* m) {
+    for (size_t i = 0; i < m->w.size(); i++) if (!m->w[i]) return false;
+    for (int l = 0; l < m->c.n_layers; l++) if (!m->ra[l] || !m->rf[l]) return false;
+    return m->emb && m->lm && m->rms_final;
+}
+
+extern "C" int gb_model_decode(gb_model* m, const int* d_token, const int* d_pos, float* d_logits, int* d_next,
+                               void* stream) {
+    if (!m || !d_token || !d_pos || !d_next) return GB_EINVAL;
+    if (!model_ready(m)) return GB_EINVAL;
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : m->stream;
+    const void* key[5] = {d_token, d_pos, d_logits, d_next, st};
+    if (!m->exec || memcmp(key, m->key, sizeof(key)) != 0) {
+        invalidate_graph(m);
+        cudaStream_t cap = m->stream;   // capture on the model's own stream, replay on st
+        if (cudaStreamBeginCapture(cap, cudaStreamCaptureModeRelaxed) != cudaSuccess) return GB_ECUDA;
+        const int rc = enqueue_step(m, d_token, d_pos, d_logits, d_next, cap);
+        cudaGraph_t g = nullptr;
+        const cudaError_t ec = cudaStreamEndCapture(cap, &g);
+        if (rc != GB_OK || ec != cudaSuccess) {
+            if (g) cudaGraphDestroy(g);
+            return rc != GB_OK ? rc : GB_ECUDA;
+        }
+        const cudaError_t ei = cudaGraphInstantiate(&m->exec, g, 0);
+        cudaGraphDestroy(g);
+        if (ei != cudaSuccess) { m->exec = nullptr; return GB_ECUDA; }
+        memcpy(m->key, key, sizeof(key));
+    }
+    return cudaGraphLaunch(m->exec, st) == cudaSuccess ? GB_OK : GB_ECUDA;
+}
+
+// Capture the sequence [enqueue] on the model stream into a graph.
+template <class Fn>
+static int capture(gb_model* m, cudaGraphExec_t* exec, Fn&& enqueue) {
+    cudaStream_t cap = m->stream;
+    if (cudaStreamBeginCapture(cap, cudaStreamCaptureModeRelaxed) != cudaSuccess) return GB_ECUDA;
+    const int rc = enqueue(cap);
+    cudaGraph_t g = nullptr;
+    const cudaError_t ec = cudaStreamEndCapture(cap, &g);
+    if (rc != GB_OK || ec != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        return rc != GB_OK ? rc : GB_ECUDA;
+    }
+    const cudaError_t ei = cudaGraphInstantiate(exec, g, 0);
+    cudaGraphDestroy(g);
+    if (ei != cudaSuccess) { *exec = nullptr; return GB_ECUDA; }
+    return GB_OK;
+}
+
+extern "C" int gb_model_generate(gb_model* m, int* d_token, int* d_pos, int n_steps, int* d_tokens_out,
+                                 void* stream) {
+    if (!m || !d_token || !d_pos || n_steps < 0) return GB_EINVAL;
+    if (!model_ready(m)) return GB_EINVAL;
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : m->stream;
+    const void* key[4] = {d_token, d_pos, d_tokens_out, st};
+    if (!m->gen_exec || memcmp(key, m->gen_key, sizeof(key)) != 0) {
+        if (m->gen_exec) { cudaGraphExecDestroy(m->gen_exec); m->gen_exec = nullptr; }
+        int* cnt = m->d_count;
+        int* nxt = m->d_next;
+        const int rc = capture(m, &m->gen_exec, [&](cudaStream_t cap) {
+            int r = enqueue_step(m, d_token, d_pos, m->logits, nxt, cap);
+            if (r) return r;
+            k_advance<<<1, 1, 0, cap>>>(d_token, nxt, d_pos, d_tokens_out, cnt);
+            return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
+        });
+        if (rc) return rc;
+        memcpy(m->gen_key, key, sizeof(key));
+    }
+    GB_CUDA_TRY(cudaMemsetAsync(m->d_count, 0, sizeof(int), st));
+    for (int i = 0; i < n_steps; i++) GB_CUDA_TRY(cudaGraphLaunch(m->gen_exec, st));
+    return GB_OK;
+}
+
+extern "C" int gb_model_error(gb_model* m) {
+    if (!m) return GB_EINVAL;
+    unsigned herr = 0;
+    GB_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    GB_CUDA_TRY(cudaMemcpy(&herr, m->err, sizeof(unsigned), cudaMemcpyDeviceToHost));
+    return -(int)herr;
+}
+
+extern "C" int gb_model_fill_kv(gb_model* m, int n_pos, uint64_t seed) {
+    if (!m || n_pos < 0 || n_pos > m->c.max_seq) return GB_EINVAL;
+    const gb_model_config& c = m->c;
+    for (int l = 0; l < c.n_layers; l++)
+        for (int which = 0; which < 2; which++) {
+            float* base = which ? gb_model_v_cache(m, l) : gb_model_k_cache(m, l);
+            for (int h = 0; h < c.n_kv_heads; h++) {
+                float* p = base + (size_t)h * c.max_seq * c.head_dim;
+                const int rc = gb_synth_normal(p, (size_t)n_pos * c.head_dim, seed,
+                                               (uint64_t)((l * 2 + which) * 256 + h) + 5000000ull, m->stream);
+                if (rc) return rc;
+            }
+        }
+    return cudaStreamSynchronize(m->stream) == cudaSuccess ? GB_OK : GB_ECUDA;
+}
+
+extern "C" int gb_model_launches_per_step(const gb_model* m) {
+    // embed + per layer (2 rmsnorm, 7 matvec, attention, silu_mul) + rmsnorm, lm_head, argmax
+    return m ? 1 + m->c.n_layers * 11 + 3 : 0;
+}
+
+extern "C" int gb_model_decode_host(gb_model* m, int token, int pos, int* h_next, float* h_logits) {
+    if (!m || !h_next) return GB_EINVAL;
+    if (pos < 0 || pos >= m->c.max_seq) return GB_EPOS;
+    if (token < 0 || token >= m->c.vocab_size) return GB_EINVAL;
+    cudaStream_t st = m->stream;
+    m->h_io[0] = token;
+    m->h_io[1] = pos;
+    GB_CUDA_TRY(cudaMemcpyAsync(m->d_tok, &m->h_io[0], sizeof(int), cudaMemcpyHostToDevice, st));
+    GB_CUDA_TRY(cudaMemcpyAsync(m->d_pos, &m->h_io[1], sizeof(int), cudaMemcpyHostToDevice, st));
+    int rc = gb_model_decode(m, m->d_tok, m->d_pos, m->logits, m->d_next, st);
+    if (rc) return rc;
+    GB_CUDA_TRY(cudaMemcpyAsync(&m->h_io[2], m->d_next, sizeof(int), cudaMemcpyDeviceToHost, st));
+    if (h_logits)
+        GB_CUDA_TRY(cudaMemcpyAsync(h_logits, m->logits, (size_t)m->c.vocab_size * 4, cudaMemcpyDeviceToHost, st));
+    GB_CUDA_TRY(cudaStreamSynchronize(st));
+    unsigned herr = 0;
+    GB_CUDA_TRY(cudaMemcpy(&herr, m->err, sizeof(unsigned), cudaMemcpyDeviceToHost));
+    if (herr) return -(int)herr;
+    *h_next = m->h_io[2];
+    return GB_OK;
+}
+
+extern "C" double gb_model_step_bytes(const gb_model* m, int pos) {
+    if (!m) return 0.0;
+    const gb_model_config& c = m->c;
+    double b = 0.0;
+    for (int l = 0; l < c.n_layers; l++)
+        for (int wi = 0; wi < GB_NMAT; wi++) {
+            int rows, cols;
+            mat_shape(m, wi, &rows, &cols);
+            b += (double)gb_matrix_bytes(m->dt[(size_t)l * GB_NMAT + wi], rows, cols);
+        }
+    b += (double)gb_matrix_bytes(m->lm_dt, c.vocab_size, c.hidden_dim);
+    b += (double)(2 * c.n_layers + 1) * c.hidden_dim * 4;                   // norm weights
+    b += 2.0 * c.n_layers * m->kv_dim * (double)(pos + 1) * 4;              // K and V read
+    b += 2.0 * c.n_layers * m->kv_dim * 4;                                  // append
+    b += (double)gb_matrix_bytes(m->emb_dt == GB_DT_F32 ? GB_DT_Q4_K : m->emb_dt, 1, c.hidden_dim);
+    return b;
+}
+

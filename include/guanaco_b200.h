@@ -1,0 +1,218 @@
+/*
+ * guanaco_b200.h -- C ABI of libguanaco_b200.so, the sm_100a (B200) decode
+ * hot path for the Guanaco GGUF inference engine.
+ *
+ * Two layers of entry points:
+ *
+ *  1. DROP-IN SYMBOLS.  Exactly the extern "C" functions the unchanged Guanaco
+ *     engine, loader and KV cache bind when built with USE_CUDA=1; linking this
+ *     library in place of the reference CUDA sources (src/kernels/cuda) and src/backend/cuda_backend.c
+ *     replaces the reference CUDA path.  Each declaration cites the reference
+ *     interface it replaces (paths relative to the Guanaco repo root).  The
+ *     vtable factory (backend_cuda_create / backend_cuda_destroy) is declared in
+ *     guanaco_backend_abi.h because it needs the reference's struct types.
+ *
+ *  2. NATIVE API (gb_*).  Device-pointer kernels and a device-resident decode
+ *     model used by the drop-in symbols, the tests and the benchmark.  All
+ *     pointers are device pointers unless the parameter name starts with h_;
+ *     `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *
+ * Return codes: 0 success; -1 NULL/bad dtype/ndim; -2 cols not a multiple of
+ * the block width; -3 byte_size too small (these three follow
+ * src/kernels/cpu/quant_matvec_q4_k.c:143-158); -4 position outside
+ * [0, max_seq); -5 CUDA runtime error; -6 out of device memory; -7 a bounded
+ * device wait ran out; -8 size above a documented maximum.
+ *
+ * dtype codes follow the reference DataType enum (src/include/types.h:16-24):
+ * F32 = 0, Q8_0 = 2, Q4_K = 4, Q6_K = 5.
+ */
+#ifndef GUANACO_B200_H
+#define GUANACO_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ========================================================================
+ * 1. Drop-in symbols
+ * ===================================================================== */
+
+/* Replaces cuda_upload_weight (src/kernels/cuda/matvec_q4k_cuda.cu:115-133,
+ * called by src/engine/loader.c:713): copy `size` bytes of GGUF blocks to the
+ * device; returns the device pointer or NULL (the loader then keeps the tensor
+ * on the CPU).  Safe to call on mmap'd MAP_PRIVATE pages. */
+void* cuda_upload_weight(const void* host_ptr, size_t size);
+
+/* Replaces cuda_matvec_q4k_f32_impl (src/kernels/cuda/matvec_q4k_cuda.cu:85-113,
+ * used by src/backend/cuda_backend.c:35-40 and tests/test_quant.c:245-281):
+ * y = W x for a device-resident Q4_K matrix, host x and y, synchronous. */
+int cuda_matvec_q4k_f32_impl(const void* W_data, const float* x, float* y, int num_rows, int num_cols);
+
+/* Replaces cuda_transformer_layer_gpu (src/kernels/cuda/cuda_layer_kernels.cu:605-713,
+ * declared src/include/kernels.h:46-58, called src/engine/engine.c:334-346):
+ * one full decode layer (T = 1) with device-resident Q4_K / Q6_K / Q8_0
+ * weights.  h_hidden is host in/out; h_k_cache / h_v_cache are the layer's
+ * host KV bases ([n_kv][max_seq][head_dim] fp32, head_stride = max_seq*hd);
+ * the appended K/V row is also written back into them.  Asynchronous: the
+ * caller syncs with cuda_finish_layer() before reading h_hidden.  Non-zero
+ * return makes the engine run the CPU layer instead (engine.c:347-349). */
+int cuda_transformer_layer_gpu(
+    const void* wq, int wq_rows, int wq_cols, int wq_dtype,
+    const void* wk, int wk_rows, int wk_cols, int wk_dtype,
+    const void* wv, int wv_rows, int wv_cols, int wv_dtype,
+    const void* wo, int wo_rows, int wo_cols, int wo_dtype,
+    const void* w_gate, int gate_rows, int gate_cols, int gate_dtype,
+    const void* w_up, int up_rows, int up_cols, int up_dtype,
+    const void* w_down, int down_rows, int down_cols, int down_dtype,
+    const float* h_rms_att, const float* h_rms_ffn,
+    float* h_hidden,
+    float* h_k_cache, float* h_v_cache, int head_stride,
+    int H, int n_heads, int n_kv_heads, int head_dim,
+    int pos, int layer, int max_seq_len);
+
+/* Replaces cuda_finish_layer (src/kernels/cuda/cuda_layer_kernels.cu:715-717,
+ * called src/engine/engine.c:321): wait for all queued layer work. */
+void cuda_finish_layer(void);
+
+/* Replaces cuda_sync_kv_cache (src/kernels/cuda/cuda_layer_kernels.cu:585-603,
+ * called src/engine/engine.c:398-403): upload positions [pos, pos+T) of one
+ * layer's host KV into the device cache after a CPU prefill. */
+void cuda_sync_kv_cache(int layer, int n_kv_heads, int head_dim, int pos, int T,
+                        const float* h_k_cache, const float* h_v_cache, int stride0, int max_seq);
+
+/* Replaces cuda_get_temperature (src/backend/cuda_backend.c:26-33, called
+ * src/engine/generate.c:284): GPU temperature in C, 0 when unknown. */
+int cuda_get_temperature(void);
+
+/* ========================================================================
+ * 2. Native API
+ * ===================================================================== */
+
+/* Library / device information. */
+const char* gb_version(void);
+int gb_device_sm_count(void);
+
+/* y[rows] = W[rows, cols] . x[cols] (+ residual[rows] when residual != NULL).
+ * W: GGUF blocks (Q4_K: 16-byte aligned; Q6_K / Q8_0: 2-byte aligned);
+ * x: 16-byte aligned.  y may alias residual. */
+int gb_matvec(int dtype, const void* W, int rows, int cols, const float* x, float* y,
+              const float* residual, void* stream);
+
+/* The same product with host x[cols] / y[rows] (copies in, sync out): the path
+ * behind the backend vtable's matvec slots. */
+int gb_matvec_host(int dtype, const void* W, int rows, int cols, const float* h_x, float* h_y);
+
+/* Bit-exact dequantisation of nblocks GGUF blocks into fp32 (256 values per
+ * Q4_K / Q6_K block, 32 per Q8_0 block). */
+int gb_dequant(int dtype, const void* blocks, size_t nblocks, float* out, void* stream);
+
+/* Seeded synthetic inputs, byte-identical to the CPU generators in the test
+ * oracle: blocks with the value distributions of the benchmark configs and
+ * approximately N(0,1) floats (sum of twelve uniforms). */
+int gb_synth_blocks(int dtype, void* blocks, size_t nblocks, uint64_t seed, uint64_t stream_id, void* stream);
+int gb_synth_normal(float* out, size_t n, uint64_t seed, uint64_t stream_id, void* stream);
+int gb_fill_f32(float* out, size_t n, float value, void* stream);
+
+/* RoPE table for positions [0, max_seq): cs[(pos*head_dim/2 + i)*2 + {0,1}] =
+ * {cos, sin}(pos * freq_i), freq_i = 1/theta^(2i/head_dim), computed on the
+ * host with the reference's float formula (src/kernels/cpu/kernels_cpu.c:408-413)
+ * and uploaded.  cs holds max_seq * head_dim floats. */
+int gb_rope_table(float* cs, int max_seq, int head_dim, float theta, void* stream);
+
+/* Decode attention for one layer at one position, fused with RoPE and the KV
+ * append (engine.c:372-509 semantics):
+ *   q[n_heads*hd] and k[n_kv*hd] are rotated (RoPE row pos of rope_cs),
+ *   k_rot and v are written to slot pos of k_cache / v_cache
+ *   ([n_kv][max_seq][hd] fp32), then out[n_heads*hd] = softmax(q k^T / sqrt(hd)) V
+ *   over positions [0, pos].
+ * pos is read from device memory (d_pos) so the call can be captured in a
+ * CUDA graph.  The context is split across CTAs (split-K) and merged with an
+ * online-softmax reduction in the last CTA of each KV head.
+ * ws: workspace of gb_attn_workspace_bytes(...) bytes, zeroed once before the
+ * first call (the kernel leaves its counters at zero on return).
+ * head_dim must be 64 or 128 and n_heads/n_kv in {1, 2, 4, 8}. */
+size_t gb_attn_workspace_bytes(int n_heads, int n_kv, int head_dim, int max_seq);
+int gb_attention_decode(const float* q, const float* k, const float* v,
+                        float* k_cache, float* v_cache, const float* rope_cs,
+                        const int* d_pos, int n_heads, int n_kv, int head_dim, int max_seq,
+                        float* out, void* ws, void* stream);
+
+/* out = w * (x * rsqrt(mean(x^2) + eps))  (kernels_cpu.c:199-265), one row of n. */
+int gb_rmsnorm(const float* x, const float* w, float* out, int n, float eps, void* stream);
+/* gate = silu(gate) * up  (kernels_cpu.c:312-341 + 367-389). */
+int gb_silu_mul(float* gate, const float* up, int n, void* stream);
+/* first index of the maximum (strict >, src/tokenizer/tokenizer.c:175-185). */
+int gb_argmax(const float* x, int n, int* d_out, void* stream);
+
+/* ---- Device-resident decode model (the fast path behind forward()) ---- */
+typedef struct gb_model gb_model;
+
+typedef struct {
+    int hidden_dim, n_heads, n_kv_heads, head_dim, n_layers, ff_dim, vocab_size, max_seq;
+    float rms_eps;      /* the reference hard-codes 1e-6 (engine.c:359,524,582) */
+    float rope_theta;   /* the reference hard-codes 500000 (kernels_cpu.c:408) */
+} gb_model_config;
+
+/* Matrix slots per layer, in this order. */
+enum { GB_WQ = 0, GB_WK, GB_WV, GB_WO, GB_WGATE, GB_WUP, GB_WDOWN, GB_NMAT };
+
+/* Allocate activations, KV cache, RoPE table and workspaces on the current
+ * device.  Weights are attached separately. */
+gb_model* gb_model_create(const gb_model_config* cfg);
+void gb_model_destroy(gb_model* m);
+
+/* Attach weights by device pointer (the model does not own them).
+ * which = GB_WQ..GB_WDOWN; norms are fp32 [hidden_dim]. */
+int gb_model_set_matrix(gb_model* m, int layer, int which, int dtype, const void* d_w);
+int gb_model_set_norms(gb_model* m, int layer, const float* d_rms_att, const float* d_rms_ffn);
+int gb_model_set_head(gb_model* m, int emb_dtype, const void* d_embedding, const float* d_rms_final,
+                      int lm_dtype, const void* d_lm_head);
+
+/* Allocate and fill every weight with seeded synthetic blocks (Q4_K_M-style
+ * mix: Q4_K everywhere except Q6_K for wv, w_down and lm_head; norms 1.0;
+ * Q4_K embedding).  The model owns these buffers. */
+int gb_model_synthesize(gb_model* m, uint64_t seed);
+
+/* Device KV cache of one layer ([n_kv][max_seq][hd] fp32 each). */
+float* gb_model_k_cache(gb_model* m, int layer);
+float* gb_model_v_cache(gb_model* m, int layer);
+
+/* One decode step for token at position pos (forward() of engine.c:559-594
+ * at T = 1, then greedy argmax).  Everything stays on the device:
+ * d_logits (may be NULL) receives vocab_size logits, d_next the argmax.
+ * The step is captured once into a CUDA graph and replayed. */
+int gb_model_decode(gb_model* m, const int* d_token, const int* d_pos, float* d_logits, int* d_next,
+                    void* stream);
+
+/* Same step with host token/position in and host next token (and optionally
+ * host logits) out: the end-to-end entry point. */
+int gb_model_decode_host(gb_model* m, int token, int pos, int* h_next, float* h_logits);
+
+/* Greedy generation entirely on the device: n_steps replays of a graph that
+ * runs one decode step and then feeds the argmax back (*d_token = next,
+ * *d_pos += 1).  Step i's token goes to d_tokens_out[i] when not NULL.
+ * Asynchronous on `stream`. */
+int gb_model_generate(gb_model* m, int* d_token, int* d_pos, int n_steps, int* d_tokens_out, void* stream);
+
+/* Fill positions [0, n_pos) of every layer's K and V cache with seeded
+ * synthetic values (approximately N(0,1)): a stand-in for a prefilled context. */
+int gb_model_fill_kv(gb_model* m, int n_pos, uint64_t seed);
+
+/* Device error word of the model (0 = none; e.g. -4 for a position outside
+ * [0, max_seq) or -1 for a token outside the vocabulary).  Synchronises. */
+int gb_model_error(gb_model* m);
+
+/* Kernel launches one decode step issues. */
+int gb_model_launches_per_step(const gb_model* m);
+
+/* Byte count of one decode step's algorithmic HBM traffic at position pos
+ * (weights + KV read + KV append + activations), for rooflines. */
+double gb_model_step_bytes(const gb_model* m, int pos);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GUANACO_B200_H */

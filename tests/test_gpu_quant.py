@@ -1,0 +1,222 @@
+"""GPU parity: Q4_K / Q6_K / Q8_0 dequantisation (bit-exact) and fused
+dequant+matvec (relative L2 <= 1e-3 against the oracle, which is bit-exact
+with the reference CPU kernels)."""
+import numpy as np
+import pytest
+
+from tests.helpers import REL_L2_TOL, from_dev, rel_l2, to_dev
+
+pytestmark = pytest.mark.gpu
+
+DTS = {"q4k": 4, "q6k": 5, "q8_0": 2}
+
+
+def dev_blocks(cuda, host_bytes, pad=16):
+    t = cuda.zeros(host_bytes.size + pad, dtype=cuda.uint8, device="cuda")
+    t[: host_bytes.size] = to_dev(cuda, host_bytes)
+    return t
+
+
+@pytest.mark.parametrize("name", list(DTS))
+def test_synth_bytes_match_cpu_generator(gb, oracle, cuda, name):
+    dt = DTS[name]
+    rows, cols = 37, 512 if dt != 2 else 224
+    host = oracle.synth_blocks(dt, rows, cols, 1234, 9)
+    nblk = host.size // oracle.block_bytes(dt)
+    d = cuda.zeros(host.size + 16, dtype=cuda.uint8, device="cuda")
+    gb.synth_blocks(dt, d, nblk, 1234, 9)
+    cuda.cuda.synchronize()
+    assert np.array_equal(from_dev(d)[: host.size], host)
+    x = cuda.empty(1001, dtype=cuda.float32, device="cuda")
+    gb.synth_normal(x, 1001, 77, 5)
+    cuda.cuda.synchronize()
+    assert np.array_equal(from_dev(x), oracle.synth_normal(1001, 77, 5))
+
+
+def special_blocks(oracle, dt, n):
+    """Seeded blocks whose fp16 scales are overwritten with edge values:
+    subnormals, zero, negative, large, Inf and NaN."""
+    B = oracle.synth_blocks(dt, n, 256 if dt != 2 else 32, 3, 3).reshape(n, -1).copy()
+    specials = np.array([0x0001, 0x03FF, 0x0000, 0x8000, 0xBC00, 0x7BFF, 0x7C00, 0xFE01, 0x0400, 0x3555],
+                        dtype=np.uint16)
+    off = {4: [0, 2], 5: [208], 2: [0]}[dt]
+    for i in range(n):
+        for o in off:
+            B[i, o:o + 2] = np.frombuffer(specials[(i + o) % specials.size].tobytes(), np.uint8)
+    return B.ravel()
+
+
+@pytest.mark.parametrize("name", list(DTS))
+def test_dequant_bit_exact(gb, oracle, cuda, name):
+    dt = DTS[name]
+    for host in (oracle.synth_blocks(dt, 64, 1024, 11, 1), special_blocks(oracle, dt, 20)):
+        nblk = host.size // oracle.block_bytes(dt)
+        d = dev_blocks(cuda, host)
+        out = cuda.empty(nblk * (256 if dt != 2 else 32), dtype=cuda.float32, device="cuda")
+        gb.dequant(dt, d, nblk, out)
+        cuda.cuda.synchronize()
+        got = from_dev(out).view(np.uint32)
+        want = oracle.dequant(dt, host).view(np.uint32)
+        assert np.array_equal(got, want)
+
+
+def test_dequant_matches_golden(gb, cuda, golden):
+    for dt in (4, 2):
+        host = golden[f"dq_{dt}_blocks"]
+        nblk = host.size // (144 if dt == 4 else 34)
+        out = cuda.empty(nblk * (256 if dt == 4 else 32), dtype=cuda.float32, device="cuda")
+        gb.dequant(dt, dev_blocks(cuda, host), nblk, out)
+        cuda.cuda.synchronize()
+        assert np.array_equal(from_dev(out).view(np.uint32), golden[f"dq_{dt}_out"].view(np.uint32))
+
+
+def run_matvec(gb, cuda, dt, W_host, rows, cols, x_host, residual=None):
+    W = dev_blocks(cuda, W_host)
+    x = to_dev(cuda, x_host)
+    y = cuda.full((rows,), float("nan"), dtype=cuda.float32, device="cuda")
+    r = to_dev(cuda, residual) if residual is not None else None
+    gb.matvec(dt, W, rows, cols, x, y, residual=r)
+    cuda.cuda.synchronize()
+    return from_dev(y)
+
+
+SHAPES = [(1, 256), (3, 512), (5, 768), (17, 1024), (33, 2048), (100, 4096), (129, 1280), (7, 5632), (64, 14336)]
+
+
+@pytest.mark.parametrize("name", list(DTS))
+@pytest.mark.parametrize("rows,cols", SHAPES)
+def test_matvec_parity(gb, oracle, cuda, name, rows, cols):
+    dt = DTS[name]
+    W = oracle.synth_blocks(dt, rows, cols, 1234, rows * 7 + cols)
+    x = oracle.synth_normal(cols, 1234, cols)
+    rc, y_ref = oracle.matvec(dt, W, rows, cols, x)
+    assert rc == 0
+    y = run_matvec(gb, cuda, dt, W, rows, cols, x)
+    assert np.all(np.isfinite(y))
+    assert rel_l2(y, y_ref) <= REL_L2_TOL
+    assert rel_l2(y, y_ref) <= 1e-5   # fp32 accumulation: far inside the tolerance
+
+
+@pytest.mark.parametrize("rows,cols", [(3, 32), (9, 96), (31, 160), (300, 4128)])
+def test_matvec_q8_0_ragged_columns(gb, oracle, cuda, rows, cols):
+    W = oracle.synth_blocks(2, rows, cols, 5, cols)
+    x = oracle.synth_normal(cols, 5, 1)
+    _, y_ref = oracle.matvec(2, W, rows, cols, x)
+    assert rel_l2(run_matvec(gb, cuda, 2, W, rows, cols, x), y_ref) <= 1e-5
+
+
+def test_matvec_golden_vectors(gb, cuda, golden):
+    keys = sorted({k.rsplit("_", 1)[0] for k in golden.files if k.startswith("mv_")})
+    for key in keys:
+        _, dt, shape = key.split("_")
+        rows, cols = map(int, shape.split("x"))
+        y = run_matvec(gb, cuda, int(dt), golden[key + "_W"], rows, cols, golden[key + "_x"])
+        assert rel_l2(y, golden[key + "_y"]) <= REL_L2_TOL, key
+
+
+def test_matvec_residual_epilogue(gb, oracle, cuda):
+    rows, cols = 513, 2048
+    W = oracle.synth_blocks(4, rows, cols, 2, 2)
+    x = oracle.synth_normal(cols, 2, 3)
+    r = oracle.synth_normal(rows, 2, 4)
+    _, y_ref = oracle.matvec(4, W, rows, cols, x)
+    y = run_matvec(gb, cuda, 4, W, rows, cols, x, residual=r)
+    assert rel_l2(y, y_ref + r) <= 1e-5
+
+
+@pytest.mark.parametrize("name", list(DTS))
+def test_matvec_kat_values(gb, cuda, golden, name):
+    dt = DTS[name]
+    if dt == 2:
+        y = run_matvec(gb, cuda, 2, golden["kat_q8_0_blocks"], 1, 64, golden["kat_q8_0_x"])
+        assert abs(y[0] - (-528.0)) <= 1e-4
+    elif dt == 4:
+        y = run_matvec(gb, cuda, 4, golden["kat_q4k_uniform_blocks"], 1, 256, golden["kat_q4k_uniform_x"])
+        assert abs(y[0] - 384.0) <= 1e-4
+        y = run_matvec(gb, cuda, 4, golden["kat_q4k_mapping_blocks"], 1, 256, golden["kat_q4k_mapping_x"])
+        assert abs(y[0] - golden["kat_q4k_mapping_expected"][0]) <= 1e-4
+    else:
+        # Q6_K has no reference KAT; use an all-scales-one block: w = d*(q-32)
+        B = np.zeros(210, np.uint8)
+        B[192:208] = 1
+        B[208:210] = np.frombuffer(np.uint16(0x3C00).tobytes(), np.uint8)   # d = 1
+        B[0:128] = 0x21   # low nibbles 1, high nibbles 2; qh = 0 -> q in {1, 2}
+        y = run_matvec(gb, cuda, 5, B, 1, 256, np.ones(256, np.float32))
+        assert y[0] == 128 * (1 - 32) + 128 * (2 - 32)
+
+
+def test_matvec_error_codes(gb, cuda):
+    L = gb.lib()
+    W = cuda.zeros(4096, dtype=cuda.uint8, device="cuda")
+    x = cuda.zeros(1024, dtype=cuda.float32, device="cuda")
+    y = cuda.zeros(16, dtype=cuda.float32, device="cuda")
+    s = cuda.cuda.current_stream().cuda_stream
+    assert L.gb_matvec(4, W.data_ptr(), 1, 300, x.data_ptr(), y.data_ptr(), None, s) == gb.GB_ESHAPE
+    assert L.gb_matvec(2, W.data_ptr(), 1, 33, x.data_ptr(), y.data_ptr(), None, s) == gb.GB_ESHAPE
+    assert L.gb_matvec(4, None, 1, 256, x.data_ptr(), y.data_ptr(), None, s) == gb.GB_EINVAL
+    assert L.gb_matvec(7, W.data_ptr(), 1, 256, x.data_ptr(), y.data_ptr(), None, s) == gb.GB_EINVAL
+    assert L.gb_matvec(4, W.data_ptr() + 8, 1, 256, x.data_ptr(), y.data_ptr(), None, s) == gb.GB_EINVAL
+    assert L.gb_matvec(4, W.data_ptr(), 1, 256, x.data_ptr() + 4, y.data_ptr(), None, s) == gb.GB_EINVAL
+
+
+@pytest.mark.parametrize("dt,rows,cols", [(4, 4096, 4096), (5, 4096, 14336), (5, 128256, 4096), (4, 14336, 4096)])
+def test_matvec_benchmark_shapes(gb, oracle, cuda, dt, rows, cols):
+    """The BASELINE configs at full size, checked against the oracle on every row."""
+    W = oracle.synth_blocks(dt, rows, cols, 1234, 1)
+    x = oracle.synth_normal(cols, 1234, 2)
+    _, y_ref = oracle.matvec(dt, W, rows, cols, x)
+    y = run_matvec(gb, cuda, dt, W, rows, cols, x)
+    assert rel_l2(y, y_ref) <= REL_L2_TOL
+    assert np.max(np.abs(y - y_ref)) <= 1e-4 * max(1.0, np.max(np.abs(y_ref)))
+
+
+def test_vtable_slots(gb, oracle, cuda, golden):
+    """backend_cuda_create's quantised slots, called like the engine does,
+    for device-resident and host-only (lazily uploaded) tensors."""
+    be = gb.CudaBackend()
+    try:
+        for dt, rows, cols in [(4, 64, 1024), (5, 48, 2048), (2, 33, 512)]:
+            W = oracle.synth_blocks(dt, rows, cols, 3, dt)
+            x = oracle.synth_normal(cols, 3, 9)
+            _, y_ref = oracle.matvec(dt, W, rows, cols, x)
+            # host-only tensor: uploaded on first use
+            t = gb.make_tensor(dt, W, rows, cols)
+            y = np.zeros(rows, np.float32)
+            assert be.matvec(t, x, y) == 0
+            assert rel_l2(y, y_ref) <= REL_L2_TOL
+            # resident tensor through cuda_upload_weight (the loader's path)
+            d = gb.lib().cuda_upload_weight(W.ctypes.data, W.nbytes)
+            assert d
+            t2 = gb.make_tensor(dt, W, rows, cols, d_data=d)
+            y2 = np.zeros(rows, np.float32)
+            assert be.matvec(t2, x, y2) == 0
+            assert rel_l2(y2, y_ref) <= REL_L2_TOL
+            # reference error convention
+            t3 = gb.make_tensor(dt, W, rows, cols, byte_size=W.nbytes - 1)
+            assert be.matvec(t3, x, y2) == -3
+        t4 = gb.make_tensor(4, golden["kat_q4k_uniform_blocks"], 1, 256)
+        t4.dtype = 5   # wrong dtype for the Q4_K slot
+        assert be.kernels.matvec_q4k_f32(gb.C.byref(t4), golden["kat_q4k_uniform_x"].ctypes.data,
+                                         np.zeros(1, np.float32).ctypes.data) == -1
+        t5 = gb.make_tensor(4, golden["kat_q4k_uniform_blocks"], 1, 256)
+        out = np.zeros(1, np.float32)
+        assert be.matvec(t5, golden["kat_q4k_uniform_x"], out) == 0 and out[0] == 384.0
+    finally:
+        be.close()
+
+
+def test_cuda_matvec_q4k_impl_parity(gb, oracle):
+    """tests/test_quant.c:249-303: 32x1024 Q4_K, CPU vs GPU, abs tol 1e-4."""
+    rows, cols = 32, 1024
+    B = np.zeros((rows * 4, 144), np.uint8)
+    B[:, 0:2] = np.frombuffer(np.uint16(0x3C00).tobytes(), np.uint8)
+    B[:, 2:4] = np.frombuffer(np.uint16(0x3C00).tobytes(), np.uint8)
+    B[:, 4:16] = np.arange(12, dtype=np.uint8) % 8
+    B[:, 16:144] = np.arange(128, dtype=np.uint8)
+    B = B.ravel()
+    x = (np.arange(cols, dtype=np.float32) / 1024.0).astype(np.float32)
+    _, y_cpu = oracle.matvec(4, B, rows, cols, x)
+    d = gb.lib().cuda_upload_weight(B.ctypes.data, B.nbytes)
+    y = np.zeros(rows, np.float32)
+    assert gb.lib().cuda_matvec_q4k_f32_impl(d, x.ctypes.data, y.ctypes.data, rows, cols) == 0
+    assert np.max(np.abs(y - y_cpu)) <= 1e-4 * max(1.0, np.abs(y_cpu).max())
