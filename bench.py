@@ -343,6 +343,57 @@ def run_ours(args, rank, world, local_rank):
     return line
 
 
+def profile_kernel(name: str) -> None:
+    """A few launches of one kernel on a case that fits an ncu capture
+    (inputs larger than L2, a few hundred MB on the device): 3 warm-up
+    launches, then 2 more.  Prints the per-launch time of the last two."""
+    import torch
+    import guanaco_b200 as gb
+    torch.cuda.set_device(0)
+    st = torch.cuda.Stream()
+    sp = st.cuda_stream
+    if name == "attn":
+        nh, nkv, hd, ms, pos = 32, 8, 128, 8448, 8192
+        copies = 3
+        n = nkv * ms * hd
+        kc = [torch.empty(n, dtype=torch.float32, device="cuda") for _ in range(copies)]
+        vc = [torch.empty(n, dtype=torch.float32, device="cuda") for _ in range(copies)]
+        for j in range(copies):
+            gb.synth_normal(kc[j], n, SEED, 10 + j, stream=sp)
+            gb.synth_normal(vc[j], n, SEED, 20 + j, stream=sp)
+        q = torch.ones(nh * hd, dtype=torch.float32, device="cuda")
+        k = torch.ones(nkv * hd, dtype=torch.float32, device="cuda")
+        v = torch.ones(nkv * hd, dtype=torch.float32, device="cuda")
+        cs = torch.empty(ms * hd, dtype=torch.float32, device="cuda")
+        gb.rope_table(cs, ms, hd, stream=sp)
+        ws = torch.zeros(gb.attn_workspace_bytes(nh, nkv, hd, ms), dtype=torch.uint8, device="cuda")
+        d_pos = torch.tensor([pos], dtype=torch.int32, device="cuda")
+        out = torch.empty(nh * hd, dtype=torch.float32, device="cuda")
+        launch = lambda i: gb.attention_decode(q, k, v, kc[i % copies], vc[i % copies], cs, d_pos, nh, nkv, hd,  # noqa
+                                               ms, out, ws, stream=sp)
+    else:
+        dt, rows, cols, copies = {"q4k": (4, 14336, 4096, 6), "q6k": (5, 4096, 14336, 4),
+                                  "q6k_head": (5, 128256, 4096, 1), "q8_0": (2, 14336, 4096, 4)}[name]
+        wb = gb.matrix_bytes(dt, rows, cols)
+        bufs = [torch.empty(wb + 16, dtype=torch.uint8, device="cuda") for _ in range(copies)]
+        for j, b in enumerate(bufs):
+            gb.synth_blocks(dt, b, wb // gb.BLOCK_BYTES[dt], SEED, 40 + j, stream=sp)
+        x = torch.empty(cols, dtype=torch.float32, device="cuda")
+        gb.synth_normal(x, cols, SEED, 5, stream=sp)
+        y = torch.empty(rows, dtype=torch.float32, device="cuda")
+        launch = lambda i: gb.matvec(dt, bufs[i % copies], rows, cols, x, y, stream=sp)  # noqa: E731
+    for i in range(3):
+        launch(i)
+    st.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for i in range(3, 5):
+        launch(i)
+    e1.record(st)
+    e1.synchronize()
+    print(json.dumps({"kernel": name, "us_per_launch": round(e0.elapsed_time(e1) / 2 * 1e3, 2)}))
+
+
 # ---------------------------------------------------------------- reference arm
 def run_reference(args, rank, world):
     """The reference's own CPU implementation of the path (oracle/_ref: the
@@ -379,6 +430,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--steps-ref", type=int, default=None, help="reference arm samples (default min(steps, 5))")
+    ap.add_argument("--kernel", choices=["q4k", "q6k", "q6k_head", "q8_0", "attn"], default=None,
+                    help="run only a few launches of one kernel (for ncu captures) and exit")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
@@ -386,6 +439,8 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.kernel:
+        return profile_kernel(args.kernel)
     if args.impl == "reference":
         line = run_reference(args, rank, world)
     else:

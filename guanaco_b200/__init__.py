@@ -96,6 +96,7 @@ SIGNATURES = {
     "gb_device_sm_count": (_i, []),
     "gb_matvec": (_i, [_i, _vp, _i, _i, _vp, _vp, _vp, _vp]),
     "gb_matvec_host": (_i, [_i, _vp, _i, _i, _vp, _vp]),
+    "gb_device_error": (_i, [_i]),
     "gb_dequant": (_i, [_i, _vp, _sz, _vp, _vp]),
     "gb_synth_blocks": (_i, [_i, _vp, _sz, _u64, _u64, _vp]),
     "gb_synth_normal": (_i, [_vp, _sz, _u64, _u64, _vp]),

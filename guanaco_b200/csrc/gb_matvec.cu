@@ -1,0 +1,698 @@
+// gb_matvec.cu -- fused dequantise + matvec y = W x over GGUF Q4_K / Q6_K /
+// Q8_0 blocks for batch-1 decode on sm_100a.
+//
+// Reference semantics: y[r] = sum_c dequant(W[r, c]) * x[c]
+//   Q4_K  src/kernels/cpu/quant_matvec_q4_k.c:65-173 (w = d*sc*q - dmin*m)
+//   Q6_K  src/kernels/cpu/quant_matvec_q6_k.c:43-98  (w = d*sc*(q - 32))
+//   Q8_0  src/kernels/cpu/quant_matvec_q8_0.c:41-78  (w = d*q)
+// The reference CUDA kernels these replace are matvec_q4k_kernel
+// (src/kernels/cuda/matvec_q4k_cuda.cu:29-77) and matvec_q6k_kernel
+// (src/kernels/cuda/cuda_layer_kernels.cu:26-75); there was no Q8_0 kernel.
+//
+// Design (B200):
+//  * Memory: one producer warp per CTA streams row tiles from HBM into a
+//    3-8 stage shared-memory ring with cp.async.bulk (one copy per row, one
+//    row per producer lane, rows placed at a padded stride so 128-bit shared
+//    reads are bank-conflict free), completion counted on mbarriers.  Bytes in flight per SM are set
+//    by the ring depth (100-200 KB), not by registers.
+//  * Math: on B200 the integer ALU, not HBM, limits a CUDA-core GEMV over
+//    4-bit blocks (one mask per weight plus the fp32 FMA).  Q4_K and Q6_K
+//    therefore run their multiply-accumulates on the int8 tensor cores:
+//    mma.sync m16n8k32 u8 x s8 -> s32 with 16 weight rows per warp.  Weights
+//    enter as exact u8 codes (one LOP3 per 4 Q4_K weights); x enters as two
+//    int8 limbs x ~ s * (x0 + x1 / 256) with one scale s per sub-block, which
+//    keeps ~16 significant bits of every element; the 8 output columns are 4
+//    sub-blocks x 2 limbs, so each thread owns whole sub-blocks and applies
+//    their 6-bit / int8 block scales in fp32.  The result carries ~1e-5
+//    relative error, inside the 1e-3 relative-L2 parity bound.
+//  * Q8_0 keeps a CUDA-core fp32 consumer (field extraction into exact
+//    subnormal floats, FFMA2) on the same ring.
+//  * Every mbarrier wait is bounded (2 s of %globaltimer); a timeout records
+//    GB_ETIMEOUT in the device error word and the CTA winds down without
+//    touching global memory it does not own.
+#include "gb_common.cuh"
+#include "gb_internal.h"
+
+namespace gb {
+
+constexpr int MV_CONSUMERS = 16;                      // consumer warps per CTA
+constexpr int MV_THREADS = (MV_CONSUMERS + 1) * 32;   // + one producer warp
+constexpr int MV_SMEM_MAX = 227 * 1024;
+constexpr unsigned long long MV_WAIT_NS = 2000000000ull;
+
+__device__ unsigned g_gb_device_err;
+
+// ------------------------------------------------------------------ primitives
+__device__ __forceinline__ uint32_t sptr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ uint64_t gtimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t n) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(sptr(b)), "r"(n) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint64_t* b, uint32_t tx) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sptr(b)), "r"(tx) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sptr(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(sptr(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Wait for the phase of parity `parity`; false on timeout or when the CTA is
+// already aborting (the caller then proceeds without the data).
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag) {
+    if (mbar_test(b, parity)) return true;
+    const uint64_t t0 = gtimer();
+    for (;;) {
+        if (*abort_flag) return false;
+        for (int i = 0; i < 32; i++)
+            if (mbar_test(b, parity)) return true;
+        if (gtimer() - t0 > MV_WAIT_NS) {
+            *abort_flag = 1;
+            atomicExch(&g_gb_device_err, (unsigned)(-GB_ETIMEOUT));
+            return false;
+        }
+    }
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* b) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(sptr(dst)), "l"(src), "r"(bytes), "r"(sptr(b))
+                 : "memory");
+}
+__device__ __forceinline__ void consumer_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(MV_CONSUMERS * 32) : "memory");
+}
+// D += A(16x32 u8, row) * B(32x8 s8, col), s32 accumulate.
+__device__ __forceinline__ void mma_u8s8(int4& d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d.x), "+r"(d.y), "+r"(d.z), "+r"(d.w)
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// 8 bytes at a 2-byte-aligned shared address: two aligned words, one aligned
+// half word, two funnel shifts (shift 0 or 16, so the read ends at p + 8).
+struct Pair32 { uint32_t lo, hi; };
+__device__ __forceinline__ Pair32 lds8_unaligned(const uint8_t* p) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+    const uint32_t sh = (uint32_t)(a & 3u) * 8u;
+    const uint32_t w0 = w[0], w1 = w[1], w2 = *reinterpret_cast<const uint16_t*>(w + 2);
+    return {__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh)};
+}
+
+// Two int8 limbs of x: x ~ s * (x0 + x1/256), |x0| <= 127, s = max|x| / 127
+// over the sub-block; v is x / s.
+__device__ __forceinline__ void limbs(float v, int& x0, int& x1) {
+    const float r0 = rintf(v);
+    x0 = (int)r0;
+    const int r1 = (int)rintf((v - r0) * 256.f);
+    x1 = r1 > 127 ? 127 : (r1 < -128 ? -128 : r1);
+}
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+    return (uint32_t)(a & 255) | ((uint32_t)(b & 255) << 8) | ((uint32_t)(c & 255) << 16) | ((uint32_t)(d & 255) << 24);
+}
+
+// ------------------------------------------------------------------ geometry
+// Work is cut into row groups of T rows (16 = one tensor-core tile); each
+// group streams through the ring as nk sub-tiles of KC blocks.  Row r of a
+// sub-tile sits at stage + r * RS + (segment_start & 15), RS = 16 (mod 128)
+// for conflict-free 128-bit reads across the row groups of a warp.  CTA i
+// processes groups i, i + grid, ...; accumulators live in registers across a
+// group's sub-tiles.
+struct MvGeom {
+    int T;         // rows per group
+    int KC;        // blocks per sub-tile
+    int nk;        // sub-tiles per group
+    int S;         // ring stages
+    int RS;        // row stride inside a stage (bytes)
+    int SB;        // bytes per stage
+    int ngroups;
+    int red_off, ring_off, bar_off;   // offsets inside dynamic shared memory
+};
+
+// Producer warp: per sub-tile, lane r issues the bulk copy of row r,
+// [floor16(start), ceil16(end)) clamped to the matrix (the last < 16 bytes of
+// a matrix whose size is not a multiple of 16 are copied by hand); lane 0
+// first posts the stage's total transaction bytes on the full barrier.
+__device__ void ring_producer(const uint8_t* __restrict__ W, int rows, int nb, size_t bbytes, const MvGeom& g,
+                              uint8_t* ring, uint64_t* full, uint64_t* empty, volatile int* abort_flag) {
+    const int lane = threadIdx.x & 31;
+    const size_t rb = (size_t)nb * bbytes;
+    const size_t total = rb * (size_t)rows, tot16 = total & ~size_t(15);
+    int it = 0;
+    bool stop = false;
+    for (int grp = blockIdx.x; grp < g.ngroups && !stop; grp += gridDim.x) {
+        const int row0 = grp * g.T;
+        const int nr = rows - row0 < g.T ? rows - row0 : g.T;
+        for (int kc = 0; kc < g.nk; kc++, it++) {
+            const int s = it % g.S, n = it / g.S;
+            int ok = 1;
+            if (n > 0 && lane == 0) ok = mbar_wait(&empty[s], (n - 1) & 1, abort_flag);
+            if (!__shfl_sync(0xffffffffu, ok, 0)) { stop = true; break; }
+            const int b0 = kc * g.KC, nblk = nb - b0 < g.KC ? nb - b0 : g.KC;
+            uint8_t* stage = ring + (size_t)s * g.SB;
+            size_t a = 0, e = 0;
+            if (lane < nr) {
+                const size_t start = (size_t)(row0 + lane) * rb + (size_t)b0 * bbytes, end = start + nblk * bbytes;
+                a = start & ~size_t(15);
+                e = (end + 15) & ~size_t(15);
+                if (e > tot16) e = tot16;
+                uint8_t* dst = stage + (size_t)lane * g.RS;
+                for (size_t i = e > start ? e : start; i < end; i++) dst[i - a] = W[i];
+                if (e < a) e = a;
+            }
+            uint32_t tx = (uint32_t)(e - a);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) tx += __shfl_xor_sync(0xffffffffu, tx, o);
+            if (lane == 0) mbar_arrive_tx(&full[s], tx);
+            __syncwarp();
+            if (e > a) bulk_g2s(stage + (size_t)lane * g.RS, W + a, (uint32_t)(e - a), &full[s]);
+        }
+    }
+    // every issued copy has landed before the producer warp leaves
+    if (lane == 0)
+        for (int j = it - g.S > 0 ? it - g.S : 0; j < it; j++) mbar_wait(&full[j % g.S], (j / g.S) & 1, abort_flag);
+    __syncwarp();
+}
+
+// Offset of row r's data inside a sub-tile stage.
+__device__ __forceinline__ size_t seg_lead(int row, int b0, size_t rb, size_t bbytes) {
+    return ((size_t)row * rb + (size_t)b0 * bbytes) & 15;
+}
+
+// Per-CTA shared state layout, set up by kernel_prologue.
+struct MvShared {
+    uint8_t* ring;
+    uint64_t* full;
+    uint64_t* empty;
+    int* cnt;
+    volatile int* abort_flag;
+    float* red;
+};
+
+__device__ __forceinline__ MvShared kernel_prologue(uint8_t* smem, const MvGeom& g) {
+    MvShared sh;
+    sh.red = reinterpret_cast<float*>(smem + g.red_off);
+    sh.ring = smem + g.ring_off;
+    sh.full = reinterpret_cast<uint64_t*>(smem + g.bar_off);
+    sh.empty = sh.full + g.S;
+    sh.cnt = reinterpret_cast<int*>(sh.empty + g.S);
+    sh.abort_flag = sh.cnt + g.S + 2;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < g.S; s++) {
+            mbar_init(&sh.full[s], 1);
+            mbar_init(&sh.empty[s], MV_CONSUMERS);
+        }
+        for (int s = 0; s < g.S + 2; s++) sh.cnt[s] = 0;
+        *sh.abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    __syncthreads();
+    return sh;
+}
+
+// Group epilogue, run after the group's last stage was already released:
+// red[slot][w][row] holds each consumer warp's row partials; the last warp to
+// arrive sums the warps in order and writes y.  Slots rotate over S + 2
+// groups: a warp cannot run more than S sub-tiles ahead of the slowest one
+// (stage reuse waits for every warp), so a slot is never refilled while its
+// finisher may still be reading it.
+__device__ __forceinline__ void group_epilogue(const MvShared& sh, const MvGeom& g, int slot, int row0, int nrows,
+                                               float* __restrict__ y, const float* __restrict__ residual) {
+    const int lane = threadIdx.x & 31, WK = MV_CONSUMERS;
+    float* rs = sh.red + (size_t)slot * WK * g.T;
+    __syncwarp();            // every lane's partial-sum store precedes lane 0's ticket
+    __threadfence_block();
+    int last = 0;
+    if (lane == 0) last = atomicAdd(&sh.cnt[slot], 1) == MV_CONSUMERS - 1;
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (last) {
+        __threadfence_block();
+        for (int r = lane; r < nrows; r += 32) {
+            float v = 0.f;
+#pragma unroll 4
+            for (int k = 0; k < WK; k++) v += rs[k * g.T + r];
+            y[row0 + r] = v + (residual ? residual[row0 + r] : 0.f);
+        }
+        __syncwarp();
+        if (lane == 0) sh.cnt[slot] = 0;
+    }
+}
+
+// ================================================================== Q4_K (MMA)
+// Staged x per block b (256 columns), for mma u (0..3) x lohi (0..1):
+//   xb[(b*8 + 2u + lohi)*8 + 2c + limb] = {limb of columns 64c + 32 lohi + 8u
+//   + 0..3, + 4..7} -- the B-fragment pair of the lanes of column group c;
+//   xs[b*8 + j]: x scale of sub-block j = 2c + lohi (the hi one divided by 16
+//   because hi nibbles are masked in place as 16 q); xsum[b*8 + j]: sum of x
+//   over sub-block j (for the dmin * m term).
+// Lane (gq = lane >> 2, c = lane & 3) holds A rows gq and gq + 8 of its
+// warp's 16-row group: k-slots 4c..4c+3 / 16+4c..16+4c+3 = the low (or high)
+// nibbles of qs bytes 32c + 8u + 0..3 / 4..7, i.e. sub-block 2c (or 2c+1).
+// The consumer warps split each sub-tile's blocks (warp w: blocks w, w+8, ..).
+__global__ void __launch_bounds__(MV_THREADS)
+k_mv_q4k(const uint8_t* __restrict__ W, int rows, int nb, const float* __restrict__ x, float* __restrict__ y,
+         const float* __restrict__ residual, MvGeom g) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint2* xb = reinterpret_cast<uint2*>(smem);
+    float* xs = reinterpret_cast<float*>(xb + (size_t)nb * 64);
+    float* xsum = xs + (size_t)nb * 8;
+    const MvShared sh = kernel_prologue(smem, g);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (warp == MV_CONSUMERS) {
+        ring_producer(W, rows, nb, GB_Q4K_BYTES, g, sh.ring, sh.full, sh.empty, sh.abort_flag);
+        return;
+    }
+    // ---- stage x: one warp per 32-column sub-block, one lane per column
+    for (int e = warp; e < nb * 8; e += MV_CONSUMERS) {
+        const int b = e >> 3, j = e & 7, cg = j >> 1, lohi = j & 1;
+        const float v = x[b * 256 + 64 * cg + 32 * lohi + lane];
+        const float mx = warp_max(fabsf(v));
+        const float sum = warp_sum(v);
+        int a0, a1;
+        limbs(v * (mx > 0.f ? 127.f / mx : 0.f), a0, a1);
+        uint8_t* dst = reinterpret_cast<uint8_t*>(xb + (size_t)((b * 8 + 2 * (lane >> 3) + lohi) * 8 + 2 * cg));
+        dst[lane & 7] = (uint8_t)a0;
+        dst[8 + (lane & 7)] = (uint8_t)a1;
+        if (lane == 0) {
+            xs[e] = (mx / 127.f) * (lohi ? 0.0625f : 1.f);
+            xsum[e] = sum;
+        }
+    }
+    consumer_sync();
+
+    const int gq = lane >> 2, c = lane & 3;
+    const bool bact = c == (gq >> 1);   // this lane carries a nonzero B fragment
+    const int bsel = 2 * c + (gq & 1);
+    const int sh8 = (c & 1) << 4;
+    int it = 0, gi = 0;
+    for (int grp = blockIdx.x; grp < g.ngroups; grp += gridDim.x) {
+        const int row0 = grp * g.T;
+        const int nrows = rows - row0 < g.T ? rows - row0 : g.T;
+        const bool va = gq < nrows, vb = gq + 8 < nrows;
+        float acc_a = 0.f, acc_b = 0.f;
+        for (int kc = 0; kc < g.nk; kc++, it++) {
+            const int s = it % g.S;
+            mbar_wait(&sh.full[s], (it / g.S) & 1, sh.abort_flag);
+            const int b0 = kc * g.KC, nblk = nb - b0 < g.KC ? nb - b0 : g.KC;
+            const uint8_t* stage = sh.ring + (size_t)s * g.SB;
+            const uint8_t* pa = stage + (size_t)(va ? gq : 0) * g.RS;        // Q4_K segments are 16-byte aligned
+            const uint8_t* pb = stage + (size_t)(vb ? gq + 8 : 0) * g.RS;
+            for (int bl = warp; bl < nblk; bl += MV_CONSUMERS) {
+                const int b = b0 + bl;
+                const uint8_t* ba = pa + (size_t)bl * GB_Q4K_BYTES;
+                const uint8_t* bb = pb + (size_t)bl * GB_Q4K_BYTES;
+                const uint4 ha = *reinterpret_cast<const uint4*>(ba);
+                const uint4 hb = *reinterpret_cast<const uint4*>(bb);
+                uint4 qa[2], qb[2];
+#pragma unroll
+                for (int v = 0; v < 2; v++) {
+                    qa[v] = va ? *reinterpret_cast<const uint4*>(ba + 16 + 32 * c + 16 * v) : make_uint4(0, 0, 0, 0);
+                    qb[v] = vb ? *reinterpret_cast<const uint4*>(bb + 16 + 32 * c + 16 * v) : make_uint4(0, 0, 0, 0);
+                }
+                int4 cl[2] = {make_int4(0, 0, 0, 0), make_int4(0, 0, 0, 0)};
+                int4 ch[2] = {make_int4(0, 0, 0, 0), make_int4(0, 0, 0, 0)};
+                const uint2* xbb = xb + (size_t)b * 64;
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const uint32_t wa0 = (u & 1) ? qa[u >> 1].z : qa[u >> 1].x;
+                    const uint32_t wa1 = (u & 1) ? qa[u >> 1].w : qa[u >> 1].y;
+                    const uint32_t wb0 = (u & 1) ? qb[u >> 1].z : qb[u >> 1].x;
+                    const uint32_t wb1 = (u & 1) ? qb[u >> 1].w : qb[u >> 1].y;
+                    uint2 blo = make_uint2(0, 0), bhi = make_uint2(0, 0);
+                    if (bact) {
+                        blo = xbb[(2 * u) * 8 + bsel];
+                        bhi = xbb[(2 * u + 1) * 8 + bsel];
+                    }
+                    mma_u8s8(cl[u & 1], wa0 & 0x0F0F0F0Fu, wb0 & 0x0F0F0F0Fu, wa1 & 0x0F0F0F0Fu, wb1 & 0x0F0F0F0Fu,
+                             blo.x, blo.y);
+                    mma_u8s8(ch[u & 1], wa0 & 0xF0F0F0F0u, wb0 & 0xF0F0F0F0u, wa1 & 0xF0F0F0F0u, wb1 & 0xF0F0F0F0u,
+                             bhi.x, bhi.y);
+                }
+                const int4 clo = make_int4(cl[0].x + cl[1].x, cl[0].y + cl[1].y, cl[0].z + cl[1].z, cl[0].w + cl[1].w);
+                const int4 chi = make_int4(ch[0].x + ch[1].x, ch[0].y + ch[1].y, ch[0].z + ch[1].z, ch[0].w + ch[1].w);
+                // sub-blocks 2c (lo) and 2c+1 (hi): scales and mins of rows a and b
+                const float2 sxs = *reinterpret_cast<const float2*>(xs + b * 8 + 2 * c);
+                const float2 sxm = *reinterpret_cast<const float2*>(xsum + b * 8 + 2 * c);
+#pragma unroll
+                for (int w = 0; w < 2; w++) {
+                    const uint4 h = w ? hb : ha;
+                    const uint32_t scw = c < 2 ? (h.y & 0x3F3F3F3Fu) : ((h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u));
+                    const uint32_t mw = c < 2 ? (h.z & 0x3F3F3F3Fu)
+                                              : (((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u));
+                    const float sc_lo = (float)((scw >> sh8) & 0xFFu), sc_hi = (float)((scw >> (sh8 + 8)) & 0xFFu);
+                    const float m_lo = (float)((mw >> sh8) & 0xFFu), m_hi = (float)((mw >> (sh8 + 8)) & 0xFFu);
+                    const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+                    const int c0 = w ? clo.z : clo.x, c1 = w ? clo.w : clo.y;
+                    const int e0 = w ? chi.z : chi.x, e1 = w ? chi.w : chi.y;
+                    const float dlo = fmaf((float)c1, 0.00390625f, (float)c0);
+                    const float dhi = fmaf((float)e1, 0.00390625f, (float)e0);
+                    const float part = dm.x * (sc_lo * sxs.x * dlo + sc_hi * sxs.y * dhi) -
+                                       dm.y * (m_lo * sxm.x + m_hi * sxm.y);
+                    if (w) acc_b += part; else acc_a += part;
+                }
+            }
+            __syncwarp();   // release the stage as soon as this warp is done with it
+            if (lane == 0) mbar_arrive(&sh.empty[s]);
+        }
+        // reduce over the 4 column-group lanes of each row, then across warps
+        acc_a += __shfl_xor_sync(0xffffffffu, acc_a, 1);
+        acc_a += __shfl_xor_sync(0xffffffffu, acc_a, 2);
+        acc_b += __shfl_xor_sync(0xffffffffu, acc_b, 1);
+        acc_b += __shfl_xor_sync(0xffffffffu, acc_b, 2);
+        const int slot = gi++ % (g.S + 2);
+        float* rs = sh.red + (size_t)slot * MV_CONSUMERS * g.T + warp * g.T;
+        if (c == 0) {
+            if (va) rs[gq] = acc_a;
+            if (vb) rs[gq + 8] = acc_b;
+        }
+        group_epilogue(sh, g, slot, row0, nrows, y, residual);
+    }
+}
+
+// ================================================================== Q6_K (MMA)
+// mma (n, G) of a block: half n (0..1), group G (0..3); the lanes of column
+// group c hold weights l in [8c, 8c+8) of group G (columns 128n + 32G + l),
+// q = (ql nibble | qh bits << 4), a u8 code 0..63; their sub-block is
+// 8n + 2G + (c >> 1) (16 weights, int8 scale).
+// Staged x per block: xb[(b*8 + 4n + G)*8 + 2c + limb] (B-fragment pair of
+// columns 128n + 32G + 8c + 0..3, 4..7), xs[b*16 + 8n + 2G + (c>>1)] = x
+// scale of the 16-column sub-block, xs32[b*32 + (4n + G)*4 + c] = 32 * sum of
+// x over the lanes' 8 columns (the -32 offset of the codes).
+__global__ void __launch_bounds__(MV_THREADS)
+k_mv_q6k(const uint8_t* __restrict__ W, int rows, int nb, const float* __restrict__ x, float* __restrict__ y,
+         const float* __restrict__ residual, MvGeom g) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint2* xb = reinterpret_cast<uint2*>(smem);
+    float* xs = reinterpret_cast<float*>(xb + (size_t)nb * 64);
+    float* xs32 = xs + (size_t)nb * 16;
+    const MvShared sh = kernel_prologue(smem, g);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const size_t rb = (size_t)nb * GB_Q6K_BYTES;
+    if (warp == MV_CONSUMERS) {
+        ring_producer(W, rows, nb, GB_Q6K_BYTES, g, sh.ring, sh.full, sh.empty, sh.abort_flag);
+        return;
+    }
+    // ---- stage x: one warp per 32 columns (b, n, G) = two 16-column
+    // sub-blocks, one lane per column; column group c = lane >> 3
+    for (int e = warp; e < nb * 8; e += MV_CONSUMERS) {
+        const int b = e >> 3, n = (e >> 2) & 1, G = e & 3;
+        const float v = x[b * 256 + 128 * n + 32 * G + lane];
+        float mx = fabsf(v);
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float s8 = v;
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) s8 += __shfl_xor_sync(0xffffffffu, s8, o);
+        int a0, a1;
+        limbs(v * (mx > 0.f ? 127.f / mx : 0.f), a0, a1);
+        const int c = lane >> 3;
+        uint8_t* dst = reinterpret_cast<uint8_t*>(xb + (size_t)((b * 8 + 4 * n + G) * 8 + 2 * c));
+        dst[lane & 7] = (uint8_t)a0;
+        dst[8 + (lane & 7)] = (uint8_t)a1;
+        if ((lane & 15) == 0) xs[b * 16 + 8 * n + 2 * G + (lane >> 4)] = mx / 127.f;
+        if ((lane & 7) == 0) xs32[b * 32 + (4 * n + G) * 4 + c] = 32.f * s8;
+    }
+    consumer_sync();
+
+    const int gq = lane >> 2, c = lane & 3;
+    const bool bact = c == (gq >> 1);
+    const int bsel = 2 * c + (gq & 1);
+    int it = 0, gi = 0;
+    for (int grp = blockIdx.x; grp < g.ngroups; grp += gridDim.x) {
+        const int row0 = grp * g.T;
+        const int nrows = rows - row0 < g.T ? rows - row0 : g.T;
+        const bool va = gq < nrows, vb = gq + 8 < nrows;
+        const int ia = va ? gq : 0, ib = vb ? gq + 8 : 0;
+        float acc_a = 0.f, acc_b = 0.f;
+        for (int kc = 0; kc < g.nk; kc++, it++) {
+            const int s = it % g.S;
+            mbar_wait(&sh.full[s], (it / g.S) & 1, sh.abort_flag);
+            const int b0 = kc * g.KC, nblk = nb - b0 < g.KC ? nb - b0 : g.KC;
+            const uint8_t* stage = sh.ring + (size_t)s * g.SB;
+            const uint8_t* pa = stage + (size_t)ia * g.RS + seg_lead(row0 + ia, b0, rb, GB_Q6K_BYTES);
+            const uint8_t* pb = stage + (size_t)ib * g.RS + seg_lead(row0 + ib, b0, rb, GB_Q6K_BYTES);
+            for (int bl = warp; bl < nblk; bl += MV_CONSUMERS) {
+                const int b = b0 + bl;
+                const uint8_t* ba = pa + (size_t)bl * GB_Q6K_BYTES;
+                const uint8_t* bb = pb + (size_t)bl * GB_Q6K_BYTES;
+                const float da = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(ba + 208)));
+                const float db = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(bb + 208)));
+                const uint2* xbb = xb + (size_t)b * 64;
+#pragma unroll
+                for (int n = 0; n < 2; n++) {
+                    Pair32 qa0 = {0, 0}, qa1 = {0, 0}, ha = {0, 0}, qb0 = {0, 0}, qb1 = {0, 0}, hb = {0, 0};
+                    if (va) {
+                        qa0 = lds8_unaligned(ba + 64 * n + 8 * c);
+                        qa1 = lds8_unaligned(ba + 64 * n + 32 + 8 * c);
+                        ha = lds8_unaligned(ba + 128 + 32 * n + 8 * c);
+                    }
+                    if (vb) {
+                        qb0 = lds8_unaligned(bb + 64 * n + 8 * c);
+                        qb1 = lds8_unaligned(bb + 64 * n + 32 + 8 * c);
+                        hb = lds8_unaligned(bb + 128 + 32 * n + 8 * c);
+                    }
+#pragma unroll
+                    for (int G = 0; G < 4; G++) {
+                        // a0: row a word 0, a1: row b word 0, a2: row a word 1, a3: row b word 1
+                        uint32_t A[4];
+#pragma unroll
+                        for (int t = 0; t < 4; t++) {
+                            const Pair32& ql = (t & 1) ? ((G & 1) ? qb1 : qb0) : ((G & 1) ? qa1 : qa0);
+                            const Pair32& qh = (t & 1) ? hb : ha;
+                            const uint32_t lw = (t >> 1) ? ql.hi : ql.lo;
+                            const uint32_t hw = (t >> 1) ? qh.hi : qh.lo;
+                            const uint32_t nib = (G >> 1) ? ((lw >> 4) & 0x0F0F0F0Fu) : (lw & 0x0F0F0F0Fu);
+                            const uint32_t hi2 = G == 0 ? (hw << 4) : G == 1 ? (hw << 2) : G == 2 ? hw : (hw >> 2);
+                            A[t] = nib | (hi2 & 0x30303030u);
+                        }
+                        uint2 bf = make_uint2(0, 0);
+                        if (bact) bf = xbb[(4 * n + G) * 8 + bsel];
+                        int4 cc = make_int4(0, 0, 0, 0);
+                        mma_u8s8(cc, A[0], A[1], A[2], A[3], bf.x, bf.y);
+                        const int sb = 8 * n + 2 * G + (c >> 1);
+                        const float xsc = xs[b * 16 + sb];
+                        const float x32 = xs32[b * 32 + (4 * n + G) * 4 + c];
+                        const float sca = (float)(int)(int8_t)ba[192 + sb];
+                        const float scb = (float)(int)(int8_t)bb[192 + sb];
+                        const float dla = fmaf((float)cc.y, 0.00390625f, (float)cc.x);
+                        const float dlb = fmaf((float)cc.w, 0.00390625f, (float)cc.z);
+                        acc_a = fmaf(da * sca, fmaf(xsc, dla, -x32), acc_a);
+                        acc_b = fmaf(db * scb, fmaf(xsc, dlb, -x32), acc_b);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh.empty[s]);
+        }
+        acc_a += __shfl_xor_sync(0xffffffffu, acc_a, 1);
+        acc_a += __shfl_xor_sync(0xffffffffu, acc_a, 2);
+        acc_b += __shfl_xor_sync(0xffffffffu, acc_b, 1);
+        acc_b += __shfl_xor_sync(0xffffffffu, acc_b, 2);
+        const int slot = gi++ % (g.S + 2);
+        float* rs = sh.red + (size_t)slot * MV_CONSUMERS * g.T + warp * g.T;
+        if (c == 0) {
+            if (va) rs[gq] = acc_a;
+            if (vb) rs[gq + 8] = acc_b;
+        }
+        group_epilogue(sh, g, slot, row0, nrows, y, residual);
+    }
+}
+
+// ================================================================== Q8_0 (CUDA cores)
+// Lane map per warp chunk of 8 blocks: block = lane>>2, s = lane&3 -> quants
+// [8s, 8s+8).  Quants are read as unsigned bytes u = q + 128 (XOR 0x80) and
+// masked in place into exact subnormal floats u * 2^(p-149); x carries the
+// compensating power of two so products land at u * x * 2^-49.  Each warp
+// owns whole rows of the 16-row group (row w, w + 16/..), so the cross-warp
+// reduction only moves finished sums.
+constexpr float P100 = 0x1p100f, P92 = 0x1p92f, P84 = 0x1p84f, P49 = 0x1p49f;
+
+__global__ void __launch_bounds__(MV_THREADS)
+k_mv_q8_0(const uint8_t* __restrict__ W, int rows, int nb, const float* __restrict__ x, float* __restrict__ y,
+          const float* __restrict__ residual, MvGeom g) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int nchunks = (nb + 7) / 8;
+    float4* xs = reinterpret_cast<float4*>(smem);      // [chunk][lane][2] prescaled x
+    float* sx = reinterpret_cast<float*>(xs + (size_t)nchunks * 64);   // [chunk][lane] 128 * sum x
+    const MvShared sh = kernel_prologue(smem, g);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const size_t rb = (size_t)nb * GB_Q80_BYTES;
+    if (warp == MV_CONSUMERS) {
+        ring_producer(W, rows, nb, GB_Q80_BYTES, g, sh.ring, sh.full, sh.empty, sh.abort_flag);
+        return;
+    }
+    for (int e = tid; e < nchunks * 32; e += MV_CONSUMERS * 32) {
+        const int c = e >> 5, L = e & 31, b = c * 8 + (L >> 2);
+        float4 u = make_float4(0.f, 0.f, 0.f, 0.f), v = u;
+        if (b < nb) {
+            const float4* p = reinterpret_cast<const float4*>(x + b * 32 + 8 * (L & 3));
+            u = p[0];
+            v = p[1];
+        }
+        const int sw = (L >> 2) & 1;
+        xs[(size_t)e * 2 + (0 ^ sw)] = make_float4(u.x * P100, u.y * P92, u.z * P84, u.w * P84);
+        xs[(size_t)e * 2 + (1 ^ sw)] = make_float4(v.x * P100, v.y * P92, v.z * P84, v.w * P84);
+        sx[e] = 128.f * (((u.x + u.y) + (u.z + u.w)) + ((v.x + v.y) + (v.z + v.w)));
+    }
+    consumer_sync();
+
+    const int sw = (lane >> 2) & 1;
+    int it = 0, gi = 0;
+    for (int grp = blockIdx.x; grp < g.ngroups; grp += gridDim.x) {
+        const int row0 = grp * g.T;
+        const int nrows = rows - row0 < g.T ? rows - row0 : g.T;
+        float acc[2] = {0.f, 0.f};
+        for (int kc = 0; kc < g.nk; kc++, it++) {
+            const int s = it % g.S;
+            mbar_wait(&sh.full[s], (it / g.S) & 1, sh.abort_flag);
+            const int b0 = kc * g.KC, nblk = nb - b0 < g.KC ? nb - b0 : g.KC;
+            const uint8_t* stage = sh.ring + (size_t)s * g.SB;
+#pragma unroll
+            for (int rr = 0; rr < 16 / MV_CONSUMERS; rr++) {
+                const int lr = warp + MV_CONSUMERS * rr;
+                if (lr >= nrows) continue;
+                const uint8_t* prow = stage + (size_t)lr * g.RS + seg_lead(row0 + lr, b0, rb, GB_Q80_BYTES);
+                for (int cl = 0; cl * 8 < nblk; cl++) {
+                    const int bl = cl * 8 + (lane >> 2);
+                    if (bl >= nblk) continue;
+                    const int c = (b0 + bl) >> 3;   // global chunk (KC is a multiple of 8)
+                    const uint8_t* blk = prow + (size_t)bl * GB_Q80_BYTES;
+                    const Pair32 q = lds8_unaligned(blk + 2 + 8 * (lane & 3));
+                    const float d = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(blk)));
+                    const float4 x0 = xs[((size_t)c * 32 + lane) * 2 + (0 ^ sw)];
+                    const float4 x1 = xs[((size_t)c * 32 + lane) * 2 + (1 ^ sw)];
+                    float2 a = make_float2(0.f, 0.f);
+                    const uint32_t u0 = q.lo ^ 0x80808080u, u1 = q.hi ^ 0x80808080u;
+                    a = __ffma2_rn(make_float2(__uint_as_float(u0 & 0xFFu), __uint_as_float(u0 & 0xFF00u)), make_float2(x0.x, x0.y), a);
+                    a = __ffma2_rn(make_float2(__uint_as_float(u0 & 0xFF0000u), __uint_as_float(__byte_perm(u0, 0u, 0x4344u))), make_float2(x0.z, x0.w), a);
+                    a = __ffma2_rn(make_float2(__uint_as_float(u1 & 0xFFu), __uint_as_float(u1 & 0xFF00u)), make_float2(x1.x, x1.y), a);
+                    a = __ffma2_rn(make_float2(__uint_as_float(u1 & 0xFF0000u), __uint_as_float(__byte_perm(u1, 0u, 0x4344u))), make_float2(x1.z, x1.w), a);
+                    acc[rr] += d * fmaf(a.x + a.y, P49, -sx[c * 32 + lane]);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh.empty[s]);
+        }
+        const int slot = gi++ % (g.S + 2);
+        // whole rows per warp: the owner fills every warp slot of its rows
+        // (its sum in slot 0, zeros elsewhere) so the shared epilogue applies
+#pragma unroll
+        for (int rr = 0; rr < 16 / MV_CONSUMERS; rr++) {
+            const float v = warp_sum(acc[rr]);
+            const int lr = warp + MV_CONSUMERS * rr;
+            if (lane == 0) {
+                for (int k = 0; k < MV_CONSUMERS; k++)
+                    if (lr < nrows) sh.red[(size_t)slot * MV_CONSUMERS * g.T + k * g.T + lr] = k == 0 ? v : 0.f;
+            }
+        }
+        group_epilogue(sh, g, slot, row0, nrows, y, residual);
+    }
+}
+
+// ================================================================== launch
+__host__ __device__ constexpr int round_up(int v, int a) { return (v + a - 1) / a * a; }
+
+static int staged_bytes(int dtype, int nb) {
+    switch (dtype) {
+        case GB_DT_Q4_K: return nb * (64 * 8 + 16 * 4);
+        case GB_DT_Q6_K: return nb * (64 * 8 + 48 * 4);
+        default: return ((nb + 7) / 8) * 32 * (2 * 16 + 4);
+    }
+}
+
+// Geometry: 16-row groups; the sub-tile width KC (a multiple of 8 blocks, or
+// the whole row when shorter) is the largest that leaves >= 4 ring stages
+// (>= 3 for very long rows).
+static bool choose_geom(int dtype, int rows, int nb, MvGeom* g) {
+    const int bytes = (int)gb_block_bytes(dtype);
+    const int xb = round_up(staged_bytes(dtype, nb), 128);
+    g->T = 16;
+    const int red = round_up(10 * MV_CONSUMERS * g->T * 4, 128);   // S + 2 <= 10 slots
+    const long avail = MV_SMEM_MAX - xb - red - 256;
+    int kc_best = 0;
+    for (int min_stages = 4; min_stages >= 2 && !kc_best; min_stages--) {
+        for (int KC = nb; KC >= 1; KC = KC > 8 ? ((KC - 1) & ~7) : KC - 1) {
+            if (KC < nb && (KC & 7)) continue;
+            const int RS = round_up(KC * bytes + 32, 128) + 16;
+            const long SB = (long)g->T * RS + 128;
+            if (SB * min_stages <= avail) { kc_best = KC; break; }
+        }
+    }
+    if (!kc_best) return false;
+    g->KC = kc_best;
+    g->nk = (nb + g->KC - 1) / g->KC;
+    g->RS = round_up(g->KC * bytes + 32, 128) + 16;
+    g->SB = g->T * g->RS + 128;
+    g->ngroups = (rows + g->T - 1) / g->T;
+    g->red_off = xb;
+    g->ring_off = xb + red;
+    const int S = (int)((MV_SMEM_MAX - g->ring_off - 256) / g->SB);
+    g->S = S > 8 ? 8 : S;
+    g->bar_off = g->ring_off + g->S * g->SB;
+    return g->S >= 2;
+}
+
+template <typename K>
+static cudaError_t launch_kernel(K kernel, const void* W, int rows, int nb, const float* x, float* y,
+                                 const float* residual, const MvGeom& g, cudaStream_t st, unsigned* configured) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(*configured & (1u << (dev & 31)))) {
+        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, MV_SMEM_MAX);
+        if (e != cudaSuccess) return e;
+        *configured |= 1u << (dev & 31);
+    }
+    const size_t smem = (size_t)g.bar_off + 2 * g.S * sizeof(uint64_t) + (g.S + 3) * sizeof(int);
+    const int grid = g.ngroups < GB_NUM_SMS ? g.ngroups : GB_NUM_SMS;
+    kernel<<<grid, MV_THREADS, smem, st>>>(static_cast<const uint8_t*>(W), rows, nb, x, y, residual, g);
+    return cudaGetLastError();
+}
+
+}  // namespace gb
+
+using namespace gb;
+
+extern "C" int gb_matvec(int dtype, const void* W, int rows, int cols, const float* x, float* y,
+                         const float* residual, void* stream) {
+    if (!W || !x || !y || rows <= 0 || cols <= 0) return GB_EINVAL;
+    // Row tiles are fetched with cp.async.bulk (16-byte aligned source) and x
+    // is staged with 128-bit loads.
+    if ((reinterpret_cast<uintptr_t>(W) & 15) || (reinterpret_cast<uintptr_t>(x) & 15)) return GB_EINVAL;
+    if (dtype != GB_DT_Q4_K && dtype != GB_DT_Q6_K && dtype != GB_DT_Q8_0) return GB_EINVAL;
+    const int width = dtype == GB_DT_Q8_0 ? 32 : 256;
+    if (cols % width) return GB_ESHAPE;
+    const int nb = cols / width;
+    MvGeom g;
+    if (!choose_geom(dtype, rows, nb, &g)) return GB_ELIMIT;
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    static unsigned conf[3] = {0, 0, 0};
+    cudaError_t e;
+    switch (dtype) {
+        case GB_DT_Q4_K: e = launch_kernel(k_mv_q4k, W, rows, nb, x, y, residual, g, st, &conf[0]); break;
+        case GB_DT_Q6_K: e = launch_kernel(k_mv_q6k, W, rows, nb, x, y, residual, g, st, &conf[1]); break;
+        default: e = launch_kernel(k_mv_q8_0, W, rows, nb, x, y, residual, g, st, &conf[2]); break;
+    }
+    return e == cudaSuccess ? GB_OK : GB_ECUDA;
+}
+
+extern "C" int gb_device_error(int clear) {
+    unsigned v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_gb_device_err, sizeof(v)) != cudaSuccess) return GB_ECUDA;
+    if (clear && v) {
+        const unsigned z = 0;
+        if (cudaMemcpyToSymbol(g_gb_device_err, &z, sizeof(z)) != cudaSuccess) return GB_ECUDA;
+    }
+    return -(int)v;
+}

@@ -96,10 +96,15 @@ const char* gb_version(void);
 int gb_device_sm_count(void);
 
 /* y[rows] = W[rows, cols] . x[cols] (+ residual[rows] when residual != NULL).
- * W: GGUF blocks (Q4_K: 16-byte aligned; Q6_K / Q8_0: 2-byte aligned);
- * x: 16-byte aligned.  y may alias residual. */
+ * W: GGUF blocks, 16-byte aligned (row tiles are fetched with bulk copies);
+ * x: 16-byte aligned.  y may alias residual.  The kernel's bounded waits
+ * report through gb_device_error(). */
 int gb_matvec(int dtype, const void* W, int rows, int cols, const float* x, float* y,
               const float* residual, void* stream);
+
+/* Sticky device error word set by the library's kernels (0 = none, -7 for a
+ * bounded wait that ran out).  Synchronous; clear != 0 resets it. */
+int gb_device_error(int clear);
 
 /* The same product with host x[cols] / y[rows] (copies in, sync out): the path
  * behind the backend vtable's matvec slots. */

@@ -55,9 +55,14 @@ def test_dequant_bit_exact(gb, oracle, cuda, name):
         out = cuda.empty(nblk * (256 if dt != 2 else 32), dtype=cuda.float32, device="cuda")
         gb.dequant(dt, d, nblk, out)
         cuda.cuda.synchronize()
-        got = from_dev(out).view(np.uint32)
-        want = oracle.dequant(dt, host).view(np.uint32)
-        assert np.array_equal(got, want)
+        got = from_dev(out)
+        want = oracle.dequant(dt, host)
+        # bit-exact wherever the result is a number; NaN wherever the
+        # reference produces NaN (the NaN bit pattern an invalid operation
+        # creates is platform-defined: 0xFFC00000 on x86, 0x7FFFFFFF here)
+        nan = np.isnan(want)
+        assert np.array_equal(np.isnan(got), nan)
+        assert np.array_equal(got[~nan].view(np.uint32), want[~nan].view(np.uint32))
 
 
 def test_dequant_matches_golden(gb, cuda, golden):
@@ -94,7 +99,10 @@ def test_matvec_parity(gb, oracle, cuda, name, rows, cols):
     y = run_matvec(gb, cuda, dt, W, rows, cols, x)
     assert np.all(np.isfinite(y))
     assert rel_l2(y, y_ref) <= REL_L2_TOL
-    assert rel_l2(y, y_ref) <= 1e-5   # fp32 accumulation: far inside the tolerance
+    # far inside the tolerance: Q8_0 accumulates in fp32; Q4_K / Q6_K carry x
+    # as two int8 limbs per sub-block (~16 significant bits) into the tensor cores
+    assert rel_l2(y, y_ref) <= (1e-5 if dt == 2 else 1e-4)
+    assert gb.lib().gb_device_error(1) == 0
 
 
 @pytest.mark.parametrize("rows,cols", [(3, 32), (9, 96), (31, 160), (300, 4128)])
@@ -121,7 +129,7 @@ def test_matvec_residual_epilogue(gb, oracle, cuda):
     r = oracle.synth_normal(rows, 2, 4)
     _, y_ref = oracle.matvec(4, W, rows, cols, x)
     y = run_matvec(gb, cuda, 4, W, rows, cols, x, residual=r)
-    assert rel_l2(y, y_ref + r) <= 1e-5
+    assert rel_l2(y, y_ref + r) <= 1e-4
 
 
 @pytest.mark.parametrize("name", list(DTS))
@@ -156,6 +164,7 @@ def test_matvec_error_codes(gb, cuda):
     assert L.gb_matvec(4, None, 1, 256, x.data_ptr(), y.data_ptr(), None, s) == gb.GB_EINVAL
     assert L.gb_matvec(7, W.data_ptr(), 1, 256, x.data_ptr(), y.data_ptr(), None, s) == gb.GB_EINVAL
     assert L.gb_matvec(4, W.data_ptr() + 8, 1, 256, x.data_ptr(), y.data_ptr(), None, s) == gb.GB_EINVAL
+    assert L.gb_matvec(5, W.data_ptr() + 2, 1, 256, x.data_ptr(), y.data_ptr(), None, s) == gb.GB_EINVAL
     assert L.gb_matvec(4, W.data_ptr(), 1, 256, x.data_ptr() + 4, y.data_ptr(), None, s) == gb.GB_EINVAL
 
 
