@@ -48,6 +48,10 @@ struct Ctx {
     std::vector<LayerKV> kv;
     std::unordered_map<const void*, void*> norm_cache;
     std::unordered_map<const void*, void*> weight_cache;
+    // prepared matvecs keyed by device weight pointer, and their workspace
+    std::unordered_map<const void*, MvPlan> plans;
+    void* mv_ws = nullptr;
+    size_t mv_ws_size = 0;
 };
 
 static std::mutex g_mu;
@@ -188,6 +192,34 @@ static int matvec_hostio(Ctx* c, int dtype, const void* dW, int rows, int cols, 
     return GB_OK;
 }
 
+// The prepared matvec for device weights dW (re-planned if the shape changed),
+// with the context's shared workspace grown to cover it.
+static const MvPlan* plan_for(Ctx* c, int dtype, const void* dW, int rows, int cols, int* rc) {
+    MvPlan& p = c->plans[dW];
+    if (p.W != dW || p.dtype != dtype || p.rows != rows || p.cols != cols) {
+        if ((*rc = mv_plan(&p, dtype, dW, rows, cols))) {
+            c->plans.erase(dW);
+            return nullptr;
+        }
+    }
+    const size_t need = mv_ws_bytes(p);
+    if (need > c->mv_ws_size) {
+        if (c->mv_ws) {
+            cudaStreamSynchronize(c->st);
+            cudaFree(c->mv_ws);
+            c->mv_ws = nullptr;
+            c->mv_ws_size = 0;
+        }
+        if (cudaMalloc(&c->mv_ws, need) != cudaSuccess || cudaMemset(c->mv_ws, 0, need) != cudaSuccess) {
+            *rc = GB_ENOMEM;
+            return nullptr;
+        }
+        c->mv_ws_size = need;
+    }
+    *rc = GB_OK;
+    return &p;
+}
+
 static int check_dtype_shape(int dtype, int rows, int cols) {
     if (rows <= 0 || cols <= 0) return GB_EINVAL;
     if (dtype != GB_DT_Q4_K && dtype != GB_DT_Q6_K && dtype != GB_DT_Q8_0) return GB_EINVAL;
@@ -305,7 +337,9 @@ extern "C" int cuda_transformer_layer_gpu(
     GB_CUDA_TRY(cudaMemcpyAsync(c->hidden, h_hidden, (size_t)H * sizeof(float), cudaMemcpyHostToDevice, c->st));
     if ((rc = set_device_int(c->d_pos, pos, c->st))) return rc;
     LayerArgs a;
-    for (int i = 0; i < GB_NMAT; i++) { a.w[i] = W[i]; a.dt[i] = D[i]; }
+    for (int i = 0; i < GB_NMAT; i++)
+        if (!(a.mv[i] = plan_for(c, D[i], W[i], R[i], Cc[i], &rc))) return rc;
+    a.mv_ws = c->mv_ws;
     a.ra = ra; a.rf = rf; a.kc = L->k; a.vc = L->v; a.rope = c->rope; a.d_pos = c->d_pos; a.attn_ws = c->ws;
     a.hidden = c->hidden; a.xn = c->xn; a.q = c->q; a.k = c->k; a.v = c->v; a.attn = c->attn;
     a.gate = c->gate; a.up = c->up;

@@ -12,10 +12,32 @@ namespace gb {
 // P chosen in-kernel from pos so that the active splits fit the grid.
 int attn_grid_splits(int n_kv, int max_seq);
 
+// A prepared matvec: kernel choice, launch geometry and, for the TMA path,
+// the encoded tensor map of W.  Built once per weight matrix on the host
+// (the map holds W's address, so a plan is tied to one device buffer).
+struct MvPlan {
+    alignas(64) unsigned char tmap[128];   // CUtensorMap for the TMA kernels
+    const void* W = nullptr;
+    int dtype = 0, rows = 0, cols = 0, nb = 0;
+    int kind = 0;                          // MV_RING or MV_TMA
+    int nch = 0, T = 0, ncta = 0, S = 0, ngroups = 0;
+    size_t smem = 0;
+};
+enum { MV_RING = 0, MV_TMA = 1 };
+int mv_plan(MvPlan* p, int dtype, const void* W, int rows, int cols);
+// Device workspace the plan's launches need (stream-K partials + per-group
+// tickets).  Zero it once; every launch leaves the tickets at zero again.
+// Launches that share a workspace must not overlap in time.
+size_t mv_ws_bytes(const MvPlan& p);
+// pdl: launch with programmatic stream serialization, so the kernel's weight
+// prefetch overlaps the tail of the previous kernel on the stream.
+int mv_launch(const MvPlan& p, const float* x, float* y, const float* residual, void* ws, cudaStream_t st,
+              bool pdl);
+
 // Everything one decode layer needs; all pointers are device pointers.
 struct LayerArgs {
-    const void* w[GB_NMAT];
-    int dt[GB_NMAT];
+    const MvPlan* mv[GB_NMAT];
+    void* mv_ws;
     const float* ra;          // pre-attention RMSNorm weight
     const float* rf;          // pre-MLP RMSNorm weight
     float* kc;                // this layer's K cache [n_kv][max_seq][hd]

@@ -185,6 +185,10 @@ struct gb_model {
     const float* rms_final = nullptr;
     const void* lm = nullptr;
     int lm_dt = GB_DT_Q6_K;
+    std::vector<MvPlan> plan;         // [n_layers * 7] prepared matvecs
+    MvPlan lm_plan;
+    void* mv_ws = nullptr;            // shared matvec workspace (zeroed)
+    size_t mv_ws_size = 0;
     std::vector<void*> owned;         // allocations freed with the model
 
     float *kc = nullptr, *vc = nullptr, *rope = nullptr;
@@ -222,6 +226,7 @@ extern "C" gb_model* gb_model_create(const gb_model_config* cfg) {
     m->kv_dim = c.n_kv_heads * c.head_dim;
     m->w.assign((size_t)c.n_layers * GB_NMAT, nullptr);
     m->dt.assign((size_t)c.n_layers * GB_NMAT, GB_DT_Q4_K);
+    m->plan.assign((size_t)c.n_layers * GB_NMAT, MvPlan{});
     m->ra.assign(c.n_layers, nullptr);
     m->rf.assign(c.n_layers, nullptr);
     const size_t kv_elems = (size_t)c.n_layers * m->kv_dim * c.max_seq;
@@ -274,11 +279,19 @@ static void invalidate_graph(gb_model* m) {
     if (m->gen_exec) { cudaGraphExecDestroy(m->gen_exec); m->gen_exec = nullptr; }
 }
 
+static void mat_shape(const gb_model* m, int which, int* rows, int* cols);
+
 extern "C" int gb_model_set_matrix(gb_model* m, int layer, int which, int dtype, const void* d_w) {
     if (!m || layer < 0 || layer >= m->c.n_layers || which < 0 || which >= GB_NMAT || !d_w) return GB_EINVAL;
     if (dtype != GB_DT_Q4_K && dtype != GB_DT_Q6_K && dtype != GB_DT_Q8_0) return GB_EINVAL;
+    int rows, cols;
+    mat_shape(m, which, &rows, &cols);
+    MvPlan p;
+    const int rc = mv_plan(&p, dtype, d_w, rows, cols);
+    if (rc) return rc;
     m->w[(size_t)layer * GB_NMAT + which] = d_w;
     m->dt[(size_t)layer * GB_NMAT + which] = dtype;
+    m->plan[(size_t)layer * GB_NMAT + which] = p;
     invalidate_graph(m);
     return GB_OK;
 }
@@ -293,7 +306,11 @@ extern "C" int gb_model_set_head(gb_model* m, int emb_dtype, const void* emb, co
                                  const void* lm) {
     if (!m || !emb || !rms_final || !lm) return GB_EINVAL;
     if (emb_dtype != GB_DT_Q4_K && emb_dtype != GB_DT_Q8_0 && emb_dtype != GB_DT_F32) return GB_EINVAL;
+    MvPlan p;
+    const int rc = mv_plan(&p, lm_dtype, lm, m->c.vocab_size, m->c.hidden_dim);
+    if (rc) return rc;
     m->emb = emb; m->emb_dt = emb_dtype; m->rms_final = rms_final; m->lm = lm; m->lm_dt = lm_dtype;
+    m->lm_plan = p;
     invalidate_graph(m);
     return GB_OK;
 }
@@ -352,21 +369,24 @@ namespace gb {
 // One decode layer (engine.c:353-554) on stream st; shared by the model and
 // the drop-in cuda_transformer_layer_gpu.
 int enqueue_layer(const LayerArgs& a, cudaStream_t st) {
-    const int H = a.H, F = a.ff, KV = a.n_kv * a.hd;
+    const int H = a.H, F = a.ff;
     int rc;
+    auto mv = [&](int which, const float* x, float* y, const float* res) {
+        return mv_launch(*a.mv[which], x, y, res, a.mv_ws, st, true);
+    };
     if ((rc = gb_rmsnorm(a.hidden, a.ra, a.xn, H, a.eps, st))) return rc;
-    if ((rc = gb_matvec(a.dt[GB_WQ], a.w[GB_WQ], a.n_heads * a.hd, H, a.xn, a.q, nullptr, st))) return rc;
-    if ((rc = gb_matvec(a.dt[GB_WK], a.w[GB_WK], KV, H, a.xn, a.k, nullptr, st))) return rc;
-    if ((rc = gb_matvec(a.dt[GB_WV], a.w[GB_WV], KV, H, a.xn, a.v, nullptr, st))) return rc;
+    if ((rc = mv(GB_WQ, a.xn, a.q, nullptr))) return rc;
+    if ((rc = mv(GB_WK, a.xn, a.k, nullptr))) return rc;
+    if ((rc = mv(GB_WV, a.xn, a.v, nullptr))) return rc;
     if ((rc = gb_attention_decode(a.q, a.k, a.v, a.kc, a.vc, a.rope, a.d_pos, a.n_heads, a.n_kv, a.hd, a.max_seq,
                                   a.attn, a.attn_ws, st)))
         return rc;
-    if ((rc = gb_matvec(a.dt[GB_WO], a.w[GB_WO], H, a.n_heads * a.hd, a.attn, a.hidden, a.hidden, st))) return rc;
+    if ((rc = mv(GB_WO, a.attn, a.hidden, a.hidden))) return rc;
     if ((rc = gb_rmsnorm(a.hidden, a.rf, a.xn, H, a.eps, st))) return rc;
-    if ((rc = gb_matvec(a.dt[GB_WGATE], a.w[GB_WGATE], F, H, a.xn, a.gate, nullptr, st))) return rc;
-    if ((rc = gb_matvec(a.dt[GB_WUP], a.w[GB_WUP], F, H, a.xn, a.up, nullptr, st))) return rc;
+    if ((rc = mv(GB_WGATE, a.xn, a.gate, nullptr))) return rc;
+    if ((rc = mv(GB_WUP, a.xn, a.up, nullptr))) return rc;
     if ((rc = gb_silu_mul(a.gate, a.up, F, st))) return rc;
-    return gb_matvec(a.dt[GB_WDOWN], a.w[GB_WDOWN], H, F, a.gate, a.hidden, a.hidden, st);
+    return mv(GB_WDOWN, a.gate, a.hidden, a.hidden);
 }
 
 int embed(const void* emb, int dtype, const int* d_token, int vocab, int H, float* out, unsigned* err, cudaStream_t st) {
@@ -388,10 +408,8 @@ static int enqueue_step(gb_model* m, const int* d_token, const int* d_pos, float
     if ((rc = embed(m->emb, m->emb_dt, d_token, c.vocab_size, H, m->hidden, m->err, st))) return rc;
     for (int l = 0; l < c.n_layers; l++) {
         LayerArgs a;
-        for (int i = 0; i < GB_NMAT; i++) {
-            a.w[i] = m->w[(size_t)l * GB_NMAT + i];
-            a.dt[i] = m->dt[(size_t)l * GB_NMAT + i];
-        }
+        for (int i = 0; i < GB_NMAT; i++) a.mv[i] = &m->plan[(size_t)l * GB_NMAT + i];
+        a.mv_ws = m->mv_ws;
         a.ra = m->ra[l]; a.rf = m->rf[l];
         a.kc = gb_model_k_cache(m, l); a.vc = gb_model_v_cache(m, l);
         a.rope = m->rope; a.d_pos = d_pos; a.attn_ws = m->attn_ws;
@@ -403,14 +421,25 @@ static int enqueue_step(gb_model* m, const int* d_token, const int* d_pos, float
     }
     if ((rc = gb_rmsnorm(m->hidden, m->rms_final, m->xn, H, c.rms_eps, st))) return rc;
     float* lg = d_logits ? d_logits : m->logits;
-    if ((rc = gb_matvec(m->lm_dt, m->lm, c.vocab_size, H, m->xn, lg, nullptr, st))) return rc;
+    if ((rc = mv_launch(m->lm_plan, m->xn, lg, nullptr, m->mv_ws, st, true))) return rc;
     return gb_argmax(lg, c.vocab_size, d_next, st);
 }
 
-static bool model_ready(const gb_model* m) {
+// All weights set, and the shared matvec workspace sized for every plan.
+static bool model_ready(gb_model* m) {
     for (size_t i = 0; i < m->w.size(); i++) if (!m->w[i]) return false;
     for (int l = 0; l < m->c.n_layers; l++) if (!m->ra[l] || !m->rf[l]) return false;
-    return m->emb && m->lm && m->rms_final;
+    if (!(m->emb && m->lm && m->rms_final)) return false;
+    size_t need = mv_ws_bytes(m->lm_plan);
+    for (const MvPlan& p : m->plan) need = mv_ws_bytes(p) > need ? mv_ws_bytes(p) : need;
+    if (need > m->mv_ws_size) {
+        void* p = dalloc(m, need);
+        if (!p || cudaMemset(p, 0, need) != cudaSuccess) return false;
+        m->mv_ws = p;
+        m->mv_ws_size = need;
+        invalidate_graph(m);
+    }
+    return true;
 }
 
 extern "C" int gb_model_decode(gb_model* m, const int* d_token, const int* d_pos, float* d_logits, int* d_next,

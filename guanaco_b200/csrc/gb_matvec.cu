@@ -33,6 +33,12 @@
 #include "gb_common.cuh"
 #include "gb_internal.h"
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <map>
+#include <mutex>
+
 namespace gb {
 
 constexpr int MV_CONSUMERS = 16;                      // consumer warps per CTA
@@ -264,7 +270,7 @@ __device__ __forceinline__ void group_epilogue(const MvShared& sh, const MvGeom&
 __global__ void __launch_bounds__(MV_THREADS)
 k_mv_q4k(const uint8_t* __restrict__ W, int rows, int nb, const float* __restrict__ x, float* __restrict__ y,
          const float* __restrict__ residual, MvGeom g) {
-    extern __shared__ __align__(128) uint8_t smem[];
+    extern __shared__ __align__(1024) uint8_t smem[];
     uint2* xb = reinterpret_cast<uint2*>(smem);
     float* xs = reinterpret_cast<float*>(xb + (size_t)nb * 64);
     float* xsum = xs + (size_t)nb * 8;
@@ -393,7 +399,7 @@ k_mv_q4k(const uint8_t* __restrict__ W, int rows, int nb, const float* __restric
 __global__ void __launch_bounds__(MV_THREADS)
 k_mv_q6k(const uint8_t* __restrict__ W, int rows, int nb, const float* __restrict__ x, float* __restrict__ y,
          const float* __restrict__ residual, MvGeom g) {
-    extern __shared__ __align__(128) uint8_t smem[];
+    extern __shared__ __align__(1024) uint8_t smem[];
     uint2* xb = reinterpret_cast<uint2*>(smem);
     float* xs = reinterpret_cast<float*>(xb + (size_t)nb * 64);
     float* xs32 = xs + (size_t)nb * 16;
@@ -522,7 +528,7 @@ constexpr float P100 = 0x1p100f, P92 = 0x1p92f, P84 = 0x1p84f, P49 = 0x1p49f;
 __global__ void __launch_bounds__(MV_THREADS)
 k_mv_q8_0(const uint8_t* __restrict__ W, int rows, int nb, const float* __restrict__ x, float* __restrict__ y,
           const float* __restrict__ residual, MvGeom g) {
-    extern __shared__ __align__(128) uint8_t smem[];
+    extern __shared__ __align__(1024) uint8_t smem[];
     const int nchunks = (nb + 7) / 8;
     float4* xs = reinterpret_cast<float4*>(smem);      // [chunk][lane][2] prescaled x
     float* sx = reinterpret_cast<float*>(xs + (size_t)nchunks * 64);   // [chunk][lane] 128 * sum x
@@ -601,6 +607,316 @@ k_mv_q8_0(const uint8_t* __restrict__ W, int rows, int nb, const float* __restri
     }
 }
 
+// ================================================================== TMA path
+// Q4_K with one TMA tensor copy per ring stage.  The matrix is viewed as a
+// 3-D tensor {144-byte block (18 x u64), row, block index} with strides
+// {row_bytes, 144}; one box {18, 32 rows, 16 blocks} lands in shared memory
+// as [block][row][144 B], so every 16-row tile of a block is a dense 2304-byte
+// slab (conflict-free 128-bit reads) and the copy start is always x = 0
+// (16-byte aligned).  Out-of-range rows and blocks are zero-filled by the TMA
+// unit and skipped by the consumers.
+//
+// Work split (stream-K): the (32-row group, 16-block chunk) stage items are
+// cut into one contiguous range per CTA, so every CTA streams the same number
+// of bytes.  Groups that straddle two CTAs finish through a per-group ticket:
+// each owner writes its partial rows to the workspace and the last one sums
+// the partials in CTA order (deterministic) and writes y.
+//
+// x is quantised inside every CTA (int8 limb planes + per-32-column scale and
+// sum in shared memory) while the first weight boxes are in flight.  With
+// programmatic dependent launch the producer issues those boxes before
+// griddepcontrol.wait; consumers read x and write y only after it.
+constexpr int MT_NC = 8;                  // consumer warps
+constexpr int MT_KC = 16;                 // blocks per stage
+constexpr int MT_GR = 32;                 // rows per group (two 16-row tiles)
+constexpr int MT_STG = MT_KC * MT_GR * GB_Q4K_BYTES;
+constexpr int MT_THREADS = (MT_NC + 1) * 32;
+
+__device__ __forceinline__ void mbs_init(uint32_t b, uint32_t n) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(b), "r"(n) : "memory");
+}
+__device__ __forceinline__ void mbs_expect(uint32_t b, uint32_t tx) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(b), "r"(tx) : "memory");
+}
+__device__ __forceinline__ void mbs_arrive(uint32_t b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(b) : "memory");
+}
+__device__ __forceinline__ bool mbs_test(uint32_t b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(b), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait (2 s of %globaltimer); false on timeout, recorded as GB_ETIMEOUT.
+__device__ __noinline__ bool mbs_wait_slow(uint32_t b, uint32_t parity) {
+    const uint64_t t0 = gtimer();
+    while (!mbs_test(b, parity)) {
+        if (gtimer() - t0 > MV_WAIT_NS) {
+            atomicExch(&g_gb_device_err, (unsigned)(-GB_ETIMEOUT));
+            return false;
+        }
+    }
+    return true;
+}
+__device__ __forceinline__ bool mbs_wait(uint32_t b, uint32_t parity) {
+    return mbs_test(b, parity) || mbs_wait_slow(b, parity);
+}
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* map, int x, int y, int z, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+        ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(z), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+__device__ __forceinline__ void mt_consumer_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(MT_NC * 32) : "memory");
+}
+// Stage item t of a matrix with nch chunks per group: CTA c owns
+// [t_start(c), t_start(c + 1)); owner(t) is the CTA whose range holds t.
+__device__ __forceinline__ int mt_start(int c, int T, int n) { return (int)((long long)c * T / n); }
+__device__ __forceinline__ int mt_owner(int t, int T, int n) { return (int)(((long long)(t + 1) * n - 1) / T); }
+
+struct MtArgs {
+    const float* x;
+    float* y;
+    const float* residual;
+    float* part;        // [ncta][2][MT_GR] stream-K partial rows
+    unsigned* tickets;  // [ngroups], zero between launches
+    int rows, nb, nch, T, ncta, S;
+};
+
+// Quantise x (K = 256 nb columns) into the shared limb planes: x0[K], x1[K]
+// (int8) then, per 64-column chunk, float4 {scale lo, scale hi, sum lo, sum hi}
+// of its two 32-column sub-blocks.  Threads of the consumer warps, one float4
+// each per step; 8 lanes share a sub-block.
+__device__ __forceinline__ void mt_quantise_x(const float* __restrict__ x, int K, uint8_t* xq, int tid, int nthr) {
+    uint32_t* p0 = reinterpret_cast<uint32_t*>(xq);
+    uint32_t* p1 = reinterpret_cast<uint32_t*>(xq + K);
+    float* f = reinterpret_cast<float*>(xq + 2 * K);
+    for (int t = tid; t < K / 4; t += nthr) {
+        const float4 v = reinterpret_cast<const float4*>(x)[t];
+        float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+        float sm = (v.x + v.y) + (v.z + v.w);
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) {
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            sm += __shfl_xor_sync(0xffffffffu, sm, o);
+        }
+        const float inv = mx > 0.f ? 127.f / mx : 0.f;
+        int a0, a1, b0, b1, c0, c1, d0, d1;
+        limbs(v.x * inv, a0, a1);
+        limbs(v.y * inv, b0, b1);
+        limbs(v.z * inv, c0, c1);
+        limbs(v.w * inv, d0, d1);
+        p0[t] = pack4(a0, b0, c0, d0);
+        p1[t] = pack4(a1, b1, c1, d1);
+        const int sb = t >> 3;
+        if ((t & 7) == 0) {
+            f[(sb >> 1) * 4 + (sb & 1)] = mx / 127.f;
+            f[(sb >> 1) * 4 + 2 + (sb & 1)] = sm;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(MT_THREADS, 1) k_mvt_q4k(const __grid_constant__ CUtensorMap tmap, const MtArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nb = a.nb, K = nb * 256, S = a.S, nch = a.nch;
+    const int NSLOT = S + 2;
+    // shared layout: ring [S][MT_STG] | x planes | zero[64] | red [NSLOT][MT_NC][MT_GR] | cnt | barriers
+    const uint32_t sbase = sptr(smem);
+    const uint32_t xq_off = (uint32_t)S * MT_STG;
+    const uint32_t xq_bytes = (uint32_t)K * 2 + (uint32_t)K / 2;
+    const uint32_t zero_off = xq_off + ((xq_bytes + 15) & ~15u);
+    float* red = reinterpret_cast<float*>(smem + zero_off + 64);
+    unsigned* cnt = reinterpret_cast<unsigned*>(red + NSLOT * MT_NC * MT_GR);
+    const uint32_t bar_full = (sptr(cnt + NSLOT) + 15) & ~7u;
+    const uint32_t bar_empty = bar_full + 8 * S;
+    const int c0 = blockIdx.x;
+    const int t0 = mt_start(c0, a.T, a.ncta), t1 = mt_start(c0 + 1, a.T, a.ncta);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; s++) {
+            mbs_init(bar_full + 8 * s, 1);
+            mbs_init(bar_empty + 8 * s, MT_NC);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    for (int i = threadIdx.x; i < NSLOT; i += blockDim.x) cnt[i] = 0;
+    if (threadIdx.x < 16) reinterpret_cast<uint32_t*>(smem + zero_off)[threadIdx.x] = 0;
+    __syncthreads();
+    griddep_launch();
+
+    if (warp == MT_NC) {   // ---- producer: one elected lane streams the stage boxes
+        if (lane == 0) {
+            int grp = t0 / nch, ch = t0 - grp * nch;
+            const int n_it = t1 - t0;
+            bool ok = true;
+            for (int i = 0; i < n_it; i++) {
+                const int s = i % S;
+                if (i >= S && !(ok = mbs_wait(bar_empty + 8 * s, ((i / S) - 1) & 1))) break;
+                mbs_expect(bar_full + 8 * s, MT_STG);
+                tma_load_3d(sbase + s * MT_STG, &tmap, 0, grp * MT_GR, ch * MT_KC, bar_full + 8 * s);
+                if (++ch == nch) { ch = 0; grp++; }
+            }
+            // do not retire while a box is still landing in this CTA's ring
+            for (int i = n_it > S ? n_it - S : 0; ok && i < n_it; i++)
+                ok = mbs_wait(bar_empty + 8 * (i % S), (i / S) & 1);
+        }
+        return;
+    }
+
+    // ---- consumers
+    griddep_wait();
+    uint8_t* xq = smem + xq_off;
+    mt_quantise_x(a.x, K, xq, threadIdx.x, MT_NC * 32);
+    mt_consumer_sync();
+    const int gq = lane >> 2, c = lane & 3;
+    const bool bact = c == (gq >> 1);   // this lane carries a nonzero B fragment
+    const uint8_t* xlb = bact ? xq + (gq & 1) * K + 64 * c : smem + zero_off;
+    const int xstr = bact ? 256 : 0;
+    const float4* xfb = reinterpret_cast<const float4*>(xq + 2 * K) + c;
+    const int sh8 = (c & 1) << 4;
+    const uint32_t MW = c >= 2 ? 0x0F0Fu : 0u, MY = c >= 2 ? 0x3030u : 0x3F3Fu, SY = c >= 2 ? 2u : 0u;
+    int grp = t0 / nch, ch = t0 - grp * nch, gi = 0;
+    const int first_grp = grp;
+    bool ok = true;
+    float acc_a[2] = {0.f, 0.f}, acc_b[2] = {0.f, 0.f};
+    for (int t = t0, i = 0; t < t1; t++, i++) {
+        const int s = i % S;
+        if (ok) ok = mbs_wait(bar_full + 8 * s, (i / S) & 1);
+        const uint8_t* stg = smem + s * MT_STG;
+        float pa[2][2], pb[2][2];
+#pragma unroll
+        for (int j = 0; j < 2; j++) {   // blocks warp and warp + 8 of the stage
+            const int bl = warp + j * MT_NC;
+            const int b = ch * MT_KC + bl;
+            pa[j][0] = pa[j][1] = pb[j][0] = pb[j][1] = 0.f;
+            if (!ok || b >= nb) continue;
+            const uint4* xb = reinterpret_cast<const uint4*>(xlb + b * xstr);
+            const uint4 bl0 = xb[0], bl1 = xb[1], bh0 = xb[2], bh1 = xb[3];
+            const float4 xf = xfb[b * 4];
+            const float xlo = xf.x * 0.00390625f, xhi = xf.y * (0.00390625f * 0.0625f);
+#pragma unroll
+            for (int m = 0; m < 2; m++) {   // two 16-row tiles
+                const uint8_t* ra = stg + bl * (MT_GR * GB_Q4K_BYTES) + (m * 16 + gq) * GB_Q4K_BYTES;
+                const uint8_t* rb = ra + 8 * GB_Q4K_BYTES;
+                const uint4 ha = *reinterpret_cast<const uint4*>(ra);
+                const uint4 hb = *reinterpret_cast<const uint4*>(rb);
+                const uint4 qa0 = *reinterpret_cast<const uint4*>(ra + 16 + 32 * c);
+                const uint4 qa1 = *reinterpret_cast<const uint4*>(ra + 32 + 32 * c);
+                const uint4 qb0 = *reinterpret_cast<const uint4*>(rb + 16 + 32 * c);
+                const uint4 qb1 = *reinterpret_cast<const uint4*>(rb + 32 + 32 * c);
+                int4 cl = make_int4(0, 0, 0, 0), chh = make_int4(0, 0, 0, 0);
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const uint4& qa = (u >> 1) ? qa1 : qa0;
+                    const uint4& qb = (u >> 1) ? qb1 : qb0;
+                    const uint32_t wa0 = (u & 1) ? qa.z : qa.x, wa1 = (u & 1) ? qa.w : qa.y;
+                    const uint32_t wb0 = (u & 1) ? qb.z : qb.x, wb1 = (u & 1) ? qb.w : qb.y;
+                    const uint4& blx = (u >> 1) ? bl1 : bl0;
+                    const uint4& bhx = (u >> 1) ? bh1 : bh0;
+                    const uint32_t l0 = (u & 1) ? blx.z : blx.x, l1 = (u & 1) ? blx.w : blx.y;
+                    const uint32_t h0 = (u & 1) ? bhx.z : bhx.x, h1 = (u & 1) ? bhx.w : bhx.y;
+                    mma_u8s8(cl, wa0 & 0x0F0F0F0Fu, wb0 & 0x0F0F0F0Fu, wa1 & 0x0F0F0F0Fu, wb1 & 0x0F0F0F0Fu, l0, l1);
+                    mma_u8s8(chh, wa0 & 0xF0F0F0F0u, wb0 & 0xF0F0F0F0u, wa1 & 0xF0F0F0F0u, wb1 & 0xF0F0F0F0u, h0, h1);
+                }
+                // sub-blocks 2c (low nibbles) and 2c + 1 (high nibbles) of rows a, b
+#pragma unroll
+                for (int w = 0; w < 2; w++) {
+                    const uint4 h = w ? hb : ha;
+                    const uint32_t y = h.y >> sh8, z = h.z >> sh8, ww = h.w >> sh8;
+                    const uint32_t sc = (ww & MW) | ((y >> SY) & MY);
+                    const uint32_t mn = ((ww >> 4) & MW) | ((z >> SY) & MY);
+                    const float sc_lo = (float)(sc & 0xFFu), sc_hi = (float)((sc >> 8) & 0xFFu);
+                    const float m_lo = (float)(mn & 0xFFu), m_hi = (float)((mn >> 8) & 0xFFu);
+                    const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+                    const int dl = (w ? cl.z : cl.x) * 256 + (w ? cl.w : cl.y);
+                    const int dh = (w ? chh.z : chh.x) * 256 + (w ? chh.w : chh.y);
+                    const float tt = (sc_lo * xlo) * (float)dl + (sc_hi * xhi) * (float)dh;
+                    const float mm = m_lo * xf.z + m_hi * xf.w;
+                    (w ? pb : pa)[j][m] = fmaf(dm.x, tt, -dm.y * mm);
+                }
+            }
+        }
+#pragma unroll
+        for (int m = 0; m < 2; m++) {
+            acc_a[m] += pa[0][m] + pa[1][m];
+            acc_b[m] += pb[0][m] + pb[1][m];
+        }
+        __syncwarp();
+        if (lane == 0) mbs_arrive(bar_empty + 8 * s);
+
+        if (ch == nch - 1 || t == t1 - 1) {   // ---- this CTA's part of group grp is done
+#pragma unroll
+            for (int m = 0; m < 2; m++) {
+                acc_a[m] += __shfl_xor_sync(0xffffffffu, acc_a[m], 1);
+                acc_a[m] += __shfl_xor_sync(0xffffffffu, acc_a[m], 2);
+                acc_b[m] += __shfl_xor_sync(0xffffffffu, acc_b[m], 1);
+                acc_b[m] += __shfl_xor_sync(0xffffffffu, acc_b[m], 2);
+            }
+            const int slot = gi % NSLOT;
+            float* rs = red + (slot * MT_NC + warp) * MT_GR;
+            if (c == 0) {
+                rs[gq] = acc_a[0];
+                rs[gq + 8] = acc_b[0];
+                rs[16 + gq] = acc_a[1];
+                rs[24 + gq] = acc_b[1];
+            }
+            __syncwarp();
+            unsigned tk = 0;
+            if (lane == 0) {
+                __threadfence_block();
+                tk = atomicAdd(&cnt[slot], 1u);
+            }
+            tk = __shfl_sync(0xffffffffu, tk, 0);
+            if (tk == MT_NC - 1) {   // last consumer warp: sum the CTA's partials in warp order
+                __threadfence_block();
+                float v = 0.f;
+                const float* r0 = red + slot * MT_NC * MT_GR + lane;
+#pragma unroll
+                for (int w2 = 0; w2 < MT_NC; w2++) v += r0[w2 * MT_GR];
+                __syncwarp();
+                if (lane == 0) cnt[slot] = 0;
+                const int gs = grp * nch;
+                const int row = grp * MT_GR + lane;
+                if (gs >= t0 && gs + nch <= t1) {
+                    if (row < a.rows) a.y[row] = v + (a.residual ? a.residual[row] : 0.f);
+                } else {
+                    const int half = grp == first_grp ? 0 : 1;
+                    a.part[(c0 * 2 + half) * MT_GR + lane] = v;
+                    __syncwarp();
+                    const int cf = mt_owner(gs, a.T, a.ncta), cl2 = mt_owner(gs + nch - 1, a.T, a.ncta);
+                    unsigned g = 0;
+                    if (lane == 0) g = atom_add_acq_rel(&a.tickets[grp], 1u);
+                    g = __shfl_sync(0xffffffffu, g, 0);
+                    __syncwarp();
+                    if (g == (unsigned)(cl2 - cf)) {   // last owner: sum the owners' partials in CTA order
+                        float u = 0.f;
+                        for (int c2 = cf; c2 <= cl2; c2++) {
+                            const int h2 = grp == mt_start(c2, a.T, a.ncta) / nch ? 0 : 1;
+                            u += __ldcg(a.part + (c2 * 2 + h2) * MT_GR + lane);
+                        }
+                        if (row < a.rows) a.y[row] = u + (a.residual ? a.residual[row] : 0.f);
+                        if (lane == 0) a.tickets[grp] = 0u;
+                    }
+                }
+            }
+            acc_a[0] = acc_a[1] = acc_b[0] = acc_b[1] = 0.f;
+            gi++;
+        }
+        if (++ch == nch) { ch = 0; grp++; }
+    }
+}
+
 // ================================================================== launch
 __host__ __device__ constexpr int round_up(int v, int a) { return (v + a - 1) / a * a; }
 
@@ -664,27 +980,170 @@ static cudaError_t launch_kernel(K kernel, const void* W, int rows, int nb, cons
 
 using namespace gb;
 
+namespace gb {
+
+// ------------------------------------------------------------------ plans
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q;
+        void* p = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+static size_t mt_smem_bytes(int S, int K) {
+    const size_t xq = ((size_t)K * 2 + (size_t)K / 2 + 15) & ~(size_t)15;
+    const int nslot = S + 2;
+    return (size_t)S * MT_STG + xq + 64 + (size_t)nslot * MT_NC * MT_GR * 4 + (size_t)nslot * 4 + 16 + 16 * (size_t)S;
+}
+
+int mv_plan(MvPlan* p, int dtype, const void* W, int rows, int cols) {
+    if (!p || !W || rows <= 0 || cols <= 0) return GB_EINVAL;
+    if (reinterpret_cast<uintptr_t>(W) & 15) return GB_EINVAL;
+    if (dtype != GB_DT_Q4_K && dtype != GB_DT_Q6_K && dtype != GB_DT_Q8_0) return GB_EINVAL;
+    const int width = gb_block_width(dtype);
+    if (cols % width) return GB_ESHAPE;
+    *p = MvPlan{};
+    p->W = W;
+    p->dtype = dtype;
+    p->rows = rows;
+    p->cols = cols;
+    p->nb = cols / width;
+    p->kind = MV_RING;
+    if (dtype == GB_DT_Q4_K) {
+        auto enc = tensor_map_encoder();
+        int S = 4;
+        while (S > 2 && mt_smem_bytes(S, cols) > (size_t)MV_SMEM_MAX) S--;
+        if (enc && mt_smem_bytes(S, cols) <= (size_t)MV_SMEM_MAX) {
+            const cuuint64_t rb = (cuuint64_t)p->nb * GB_Q4K_BYTES;
+            cuuint64_t dims[3] = {GB_Q4K_BYTES / 8, (cuuint64_t)rows, (cuuint64_t)p->nb};
+            cuuint64_t strides[2] = {rb, GB_Q4K_BYTES};
+            cuuint32_t box[3] = {GB_Q4K_BYTES / 8, MT_GR, MT_KC};
+            cuuint32_t es[3] = {1, 1, 1};
+            CUtensorMap* m = reinterpret_cast<CUtensorMap*>(p->tmap);
+            if (enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<void*>(W), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
+                p->kind = MV_TMA;
+                p->S = S;
+                p->smem = mt_smem_bytes(S, cols);
+                p->nch = (p->nb + MT_KC - 1) / MT_KC;
+                p->ngroups = (rows + MT_GR - 1) / MT_GR;
+                p->T = p->ngroups * p->nch;
+                p->ncta = p->T < GB_NUM_SMS ? p->T : GB_NUM_SMS;
+            }
+        }
+    }
+    if (p->kind == MV_RING) {
+        MvGeom g;
+        if (!choose_geom(dtype, rows, p->nb, &g)) return GB_ELIMIT;
+        if ((reinterpret_cast<uintptr_t>(W) & 15)) return GB_EINVAL;
+    }
+    return GB_OK;
+}
+
+size_t mv_ws_bytes(const MvPlan& p) {
+    if (p.kind != MV_TMA) return 0;
+    return (size_t)GB_NUM_SMS * 2 * MT_GR * sizeof(float) + ((size_t)p.ngroups * sizeof(unsigned) + 255) / 256 * 256;
+}
+
+int mv_launch(const MvPlan& p, const float* x, float* y, const float* residual, void* ws, cudaStream_t st, bool pdl) {
+    if (!x || !y) return GB_EINVAL;
+    if (reinterpret_cast<uintptr_t>(x) & 15) return GB_EINVAL;
+    if (p.kind == MV_RING) {
+        MvGeom g;
+        if (!choose_geom(p.dtype, p.rows, p.nb, &g)) return GB_ELIMIT;
+        static unsigned conf[3] = {0, 0, 0};
+        cudaError_t e;
+        switch (p.dtype) {
+            case GB_DT_Q4_K: e = launch_kernel(k_mv_q4k, p.W, p.rows, p.nb, x, y, residual, g, st, &conf[0]); break;
+            case GB_DT_Q6_K: e = launch_kernel(k_mv_q6k, p.W, p.rows, p.nb, x, y, residual, g, st, &conf[1]); break;
+            default: e = launch_kernel(k_mv_q8_0, p.W, p.rows, p.nb, x, y, residual, g, st, &conf[2]); break;
+        }
+        return e == cudaSuccess ? GB_OK : GB_ECUDA;
+    }
+    if (!ws) return GB_EINVAL;
+    static unsigned configured = 0;
+    int dev = 0;
+    GB_CUDA_TRY(cudaGetDevice(&dev));
+    if (!(configured & (1u << (dev & 31)))) {
+        GB_CUDA_TRY(cudaFuncSetAttribute(k_mvt_q4k, cudaFuncAttributeMaxDynamicSharedMemorySize, MV_SMEM_MAX));
+        configured |= 1u << (dev & 31);
+    }
+    MtArgs a;
+    a.x = x;
+    a.y = y;
+    a.residual = residual;
+    a.part = static_cast<float*>(ws);
+    a.tickets = reinterpret_cast<unsigned*>(static_cast<char*>(ws) + (size_t)GB_NUM_SMS * 2 * MT_GR * sizeof(float));
+    a.rows = p.rows;
+    a.nb = p.nb;
+    a.nch = p.nch;
+    a.T = p.T;
+    a.ncta = p.ncta;
+    a.S = p.S;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.ncta);
+    cfg.blockDim = dim3(MT_THREADS);
+    cfg.dynamicSmemBytes = p.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    const CUtensorMap* m = reinterpret_cast<const CUtensorMap*>(p.tmap);
+    GB_CUDA_TRY(cudaLaunchKernelEx(&cfg, k_mvt_q4k, *m, a));
+    return GB_OK;
+}
+
+// Workspace for the plain C entry point: one zeroed buffer per (device,
+// stream), grown on demand.  Calls on one stream are ordered, so they can
+// share it; different streams get different buffers.
+static std::mutex g_ws_mu;
+static std::map<std::pair<int, cudaStream_t>, std::pair<void*, size_t>> g_ws;
+
+static void* stream_workspace(cudaStream_t st, size_t bytes) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+    std::lock_guard<std::mutex> lk(g_ws_mu);
+    auto& e = g_ws[{dev, st}];
+    if (e.second >= bytes) return e.first;
+    if (e.first) {
+        cudaStreamSynchronize(st);
+        cudaFree(e.first);
+        e = {nullptr, 0};
+    }
+    void* ptr = nullptr;
+    if (cudaMalloc(&ptr, bytes) != cudaSuccess) return nullptr;
+    if (cudaMemset(ptr, 0, bytes) != cudaSuccess) {
+        cudaFree(ptr);
+        return nullptr;
+    }
+    e = {ptr, bytes};
+    return ptr;
+}
+
+}  // namespace gb
+
 extern "C" int gb_matvec(int dtype, const void* W, int rows, int cols, const float* x, float* y,
                          const float* residual, void* stream) {
     if (!W || !x || !y || rows <= 0 || cols <= 0) return GB_EINVAL;
-    // Row tiles are fetched with cp.async.bulk (16-byte aligned source) and x
-    // is staged with 128-bit loads.
+    // Weights are fetched by bulk / tensor copies (16-byte aligned source) and
+    // x is read with 128-bit loads.
     if ((reinterpret_cast<uintptr_t>(W) & 15) || (reinterpret_cast<uintptr_t>(x) & 15)) return GB_EINVAL;
-    if (dtype != GB_DT_Q4_K && dtype != GB_DT_Q6_K && dtype != GB_DT_Q8_0) return GB_EINVAL;
-    const int width = dtype == GB_DT_Q8_0 ? 32 : 256;
-    if (cols % width) return GB_ESHAPE;
-    const int nb = cols / width;
-    MvGeom g;
-    if (!choose_geom(dtype, rows, nb, &g)) return GB_ELIMIT;
+    MvPlan p;
+    int rc = mv_plan(&p, dtype, W, rows, cols);
+    if (rc) return rc;
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    static unsigned conf[3] = {0, 0, 0};
-    cudaError_t e;
-    switch (dtype) {
-        case GB_DT_Q4_K: e = launch_kernel(k_mv_q4k, W, rows, nb, x, y, residual, g, st, &conf[0]); break;
-        case GB_DT_Q6_K: e = launch_kernel(k_mv_q6k, W, rows, nb, x, y, residual, g, st, &conf[1]); break;
-        default: e = launch_kernel(k_mv_q8_0, W, rows, nb, x, y, residual, g, st, &conf[2]); break;
-    }
-    return e == cudaSuccess ? GB_OK : GB_ECUDA;
+    void* ws = nullptr;
+    if (p.kind == MV_TMA && !(ws = stream_workspace(st, mv_ws_bytes(p)))) return GB_ENOMEM;
+    return mv_launch(p, x, y, residual, ws, st, false);
 }
 
 extern "C" int gb_device_error(int clear) {
