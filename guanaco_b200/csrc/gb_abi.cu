@@ -12,6 +12,8 @@
 #include "gb_common.cuh"
 #include "gb_internal.h"
 
+#include <cstring>
+
 #include <dlfcn.h>
 #include <stdlib.h>
 #include <string.h>
@@ -47,7 +49,12 @@ struct Ctx {
     size_t ws_bytes = 0;
     std::vector<LayerKV> kv;
     std::unordered_map<const void*, void*> norm_cache;
-    std::unordered_map<const void*, void*> weight_cache;
+    struct CachedWeight {
+        void* d = nullptr;
+        size_t bytes = 0;
+        uint64_t sig = 0;   // checksum of sampled bytes (detects a reused host address)
+    };
+    std::unordered_map<const void*, CachedWeight> weight_cache;
     // prepared matvecs keyed by device weight pointer, and their workspace
     std::unordered_map<const void*, MvPlan> plans;
     void* mv_ws = nullptr;
@@ -110,7 +117,8 @@ static bool ensure_ws(Ctx* c, int n_heads, int n_kv, int hd, int max_seq) {
     if (c->ws) { cudaStreamSynchronize(c->st); cudaFree(c->ws); }
     c->ws = nullptr;
     if (cudaMalloc(&c->ws, need) != cudaSuccess) { c->ws = nullptr; return false; }
-    if (cudaMemset(c->ws, 0, need) != cudaSuccess) return false;
+    // zeroed in stream order: the split-K tickets must read 0 on first use
+    if (cudaMemsetAsync(c->ws, 0, need, c->st) != cudaSuccess) return false;
     c->ws_bytes = need;
     return true;
 }
@@ -210,7 +218,7 @@ static const MvPlan* plan_for(Ctx* c, int dtype, const void* dW, int rows, int c
             c->mv_ws = nullptr;
             c->mv_ws_size = 0;
         }
-        if (cudaMalloc(&c->mv_ws, need) != cudaSuccess || cudaMemset(c->mv_ws, 0, need) != cudaSuccess) {
+        if (cudaMalloc(&c->mv_ws, need) != cudaSuccess || cudaMemsetAsync(c->mv_ws, 0, need, c->st) != cudaSuccess) {
             *rc = GB_ENOMEM;
             return nullptr;
         }
@@ -218,6 +226,24 @@ static const MvPlan* plan_for(Ctx* c, int dtype, const void* dW, int rows, int c
     }
     *rc = GB_OK;
     return &p;
+}
+
+// FNV-1a over 64 words spread evenly through the buffer (and its last word).
+static uint64_t sample_signature(const void* p, size_t n) {
+    const unsigned char* b = static_cast<const unsigned char*>(p);
+    uint64_t h = 1469598103934665603ull ^ n;
+    const size_t step = n / 64 > 8 ? n / 64 : 8;
+    for (size_t off = 0; off + 8 <= n; off += step) {
+        uint64_t w;
+        memcpy(&w, b + off, 8);
+        h = (h ^ w) * 1099511628211ull;
+    }
+    if (n >= 8) {
+        uint64_t w;
+        memcpy(&w, b + n - 8, 8);
+        h = (h ^ w) * 1099511628211ull;
+    }
+    return h;
 }
 
 static int check_dtype_shape(int dtype, int rows, int cols) {
@@ -264,15 +290,27 @@ extern "C" __attribute__((visibility("hidden"))) int gb_vtable_matvec(int dtype,
     if (!c) return GB_ECUDA;
     const void* dW = (resident && d_data) ? d_data : nullptr;
     if (!dW) {
-        auto it = c->weight_cache.find(host_data);
-        if (it != c->weight_cache.end()) {
-            dW = it->second;
-        } else {
+        // A cached copy is reused only for the same size and sampled content:
+        // a host buffer freed and reallocated at the same address must not
+        // pick up (or over-read) the old device copy.
+        const uint64_t sig = sample_signature(host_data, need);
+        Ctx::CachedWeight& e = c->weight_cache[host_data];
+        if (!e.d || e.bytes != need || e.sig != sig) {
+            if (e.d) {
+                cudaStreamSynchronize(c->st);
+                cudaFree(e.d);
+                e = Ctx::CachedWeight{};
+            }
             void* d = upload_bytes(host_data, need, c->st);
-            if (!d) return GB_ENOMEM;
-            c->weight_cache[host_data] = d;
-            dW = d;
+            if (!d) {
+                c->weight_cache.erase(host_data);
+                return GB_ENOMEM;
+            }
+            e.d = d;
+            e.bytes = need;
+            e.sig = sig;
         }
+        dW = e.d;
     }
     return matvec_hostio(c, dtype, dW, rows, cols, x, y);
 }

@@ -29,8 +29,10 @@ int mv_plan(MvPlan* p, int dtype, const void* W, int rows, int cols);
 // tickets).  Zero it once; every launch leaves the tickets at zero again.
 // Launches that share a workspace must not overlap in time.
 size_t mv_ws_bytes(const MvPlan& p);
-// pdl: launch with programmatic stream serialization, so the kernel's weight
-// prefetch overlaps the tail of the previous kernel on the stream.
+// ws may be null: the TMA path then splits the rows by whole groups (no
+// cross-CTA partials, less even for short matrices).  pdl: launch with
+// programmatic stream serialization, so the kernel's weight prefetch overlaps
+// the tail of the previous kernel on the stream.
 int mv_launch(const MvPlan& p, const float* x, float* y, const float* residual, void* ws, cudaStream_t st,
               bool pdl);
 

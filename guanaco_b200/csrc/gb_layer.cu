@@ -253,9 +253,13 @@ extern "C" gb_model* gb_model_create(const gb_model_config* cfg) {
     ok &= (m->d_count = (int*)dalloc(m, 16)) != nullptr;
     ok &= cudaMallocHost(&m->h_io, 4 * sizeof(int)) == cudaSuccess;
     ok &= cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) == cudaSuccess;
-    if (ok) ok &= cudaMemset(m->kc, 0, kv_elems * 4) == cudaSuccess && cudaMemset(m->vc, 0, kv_elems * 4) == cudaSuccess;
-    if (ok) ok &= cudaMemset(m->attn_ws, 0, ws) == cudaSuccess && cudaMemset(m->err, 0, 16) == cudaSuccess;
+    // zero in stream order, then wait: decode may run on any stream
+    if (ok) ok &= cudaMemsetAsync(m->kc, 0, kv_elems * 4, m->stream) == cudaSuccess &&
+                  cudaMemsetAsync(m->vc, 0, kv_elems * 4, m->stream) == cudaSuccess;
+    if (ok) ok &= cudaMemsetAsync(m->attn_ws, 0, ws, m->stream) == cudaSuccess &&
+                  cudaMemsetAsync(m->err, 0, 16, m->stream) == cudaSuccess;
     if (ok) ok &= gb_rope_table(m->rope, c.max_seq, c.head_dim, c.rope_theta, m->stream) == GB_OK;
+    if (ok) ok &= cudaStreamSynchronize(m->stream) == cudaSuccess;
     if (!ok) {
         gb_model_destroy(m);
         return nullptr;
@@ -434,7 +438,9 @@ static bool model_ready(gb_model* m) {
     for (const MvPlan& p : m->plan) need = mv_ws_bytes(p) > need ? mv_ws_bytes(p) : need;
     if (need > m->mv_ws_size) {
         void* p = dalloc(m, need);
-        if (!p || cudaMemset(p, 0, need) != cudaSuccess) return false;
+        if (!p || cudaMemsetAsync(p, 0, need, m->stream) != cudaSuccess ||
+            cudaStreamSynchronize(m->stream) != cudaSuccess)
+            return false;
         m->mv_ws = p;
         m->mv_ws_size = need;
         invalidate_graph(m);

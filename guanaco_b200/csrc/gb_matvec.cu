@@ -626,11 +626,8 @@ k_mv_q8_0(const uint8_t* __restrict__ W, int rows, int nb, const float* __restri
 // sum in shared memory) while the first weight boxes are in flight.  With
 // programmatic dependent launch the producer issues those boxes before
 // griddepcontrol.wait; consumers read x and write y only after it.
-constexpr int MT_NC = 8;                  // consumer warps
-constexpr int MT_KC = 16;                 // blocks per stage
 constexpr int MT_GR = 32;                 // rows per group (two 16-row tiles)
-constexpr int MT_STG = MT_KC * MT_GR * GB_Q4K_BYTES;
-constexpr int MT_THREADS = (MT_NC + 1) * 32;
+constexpr int MT_MAX_THREADS = 17 * 32;   // up to 16 consumer warps + the producer
 
 __device__ __forceinline__ void mbs_init(uint32_t b, uint32_t n) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(b), "r"(n) : "memory");
@@ -677,8 +674,9 @@ __device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
     asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
     return old;
 }
+template <int NC>
 __device__ __forceinline__ void mt_consumer_sync() {
-    asm volatile("bar.sync 1, %0;" ::"n"(MT_NC * 32) : "memory");
+    asm volatile("bar.sync 1, %0;" ::"n"(NC * 32) : "memory");
 }
 // Stage item t of a matrix with nch chunks per group: CTA c owns
 // [t_start(c), t_start(c + 1)); owner(t) is the CTA whose range holds t.
@@ -692,25 +690,38 @@ struct MtArgs {
     float* part;        // [ncta][2][MT_GR] stream-K partial rows
     unsigned* tickets;  // [ngroups], zero between launches
     int rows, nb, nch, T, ncta, S;
+    int unit;           // split granularity in stage items: 1, or nch (whole groups, no workspace)
 };
 
-// Quantise x (K = 256 nb columns) into the shared limb planes: x0[K], x1[K]
-// (int8) then, per 64-column chunk, float4 {scale lo, scale hi, sum lo, sum hi}
-// of its two 32-column sub-blocks.  Threads of the consumer warps, one float4
-// each per step; 8 lanes share a sub-block.
+// x in shared memory (K = 256 nb columns):
+//   x0[K], x1[K]                int8 limbs, x ~ s * (x0 + x1 / 256)
+//   f[K/64][4]                  per 64 columns {s lo, s hi, sum lo, sum hi} of
+//                               its two 32-column sub-blocks (s = max|x| / 127)
+//   s16[K/256][2][8]  (Q6_K)    sums of the 16-column sub-blocks 8n + 2G + h,
+//                               stored at [b][h][4n + G]
+__host__ __device__ constexpr int mt_xq_bytes(int K, bool s16) { return 2 * K + K / 4 + (s16 ? K / 4 : 0); }
+constexpr int MT_ZERO = 256;   // zero line read by lanes without a B fragment
+
+template <bool S16>
 __device__ __forceinline__ void mt_quantise_x(const float* __restrict__ x, int K, uint8_t* xq, int tid, int nthr) {
     uint32_t* p0 = reinterpret_cast<uint32_t*>(xq);
     uint32_t* p1 = reinterpret_cast<uint32_t*>(xq + K);
     float* f = reinterpret_cast<float*>(xq + 2 * K);
-    for (int t = tid; t < K / 4; t += nthr) {
+    float* f16 = f + K / 16;
+    for (int t = tid; t < K / 4; t += nthr) {   // 8 lanes (32 columns) per sub-block
         const float4 v = reinterpret_cast<const float4*>(x)[t];
         float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
         float sm = (v.x + v.y) + (v.z + v.w);
-#pragma unroll
-        for (int o = 1; o < 8; o <<= 1) {
-            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            sm += __shfl_xor_sync(0xffffffffu, sm, o);
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+        if (S16 && (t & 3) == 0) {   // 16-column sum: column c0 = 4t = 256 b + 128 n + 32 G + 16 h
+            const int c0 = 4 * t, b = c0 >> 8, n = (c0 >> 7) & 1, G = (c0 >> 5) & 3, h = (c0 >> 4) & 1;
+            f16[b * 16 + h * 8 + 4 * n + G] = sm;
         }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        sm += __shfl_xor_sync(0xffffffffu, sm, 4);
         const float inv = mx > 0.f ? 127.f / mx : 0.f;
         int a0, a1, b0, b1, c0, c1, d0, d1;
         limbs(v.x * inv, a0, a1);
@@ -727,81 +738,40 @@ __device__ __forceinline__ void mt_quantise_x(const float* __restrict__ x, int K
     }
 }
 
-__global__ void __launch_bounds__(MT_THREADS, 1) k_mvt_q4k(const __grid_constant__ CUtensorMap tmap, const MtArgs a) {
-    extern __shared__ __align__(1024) uint8_t smem[];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nb = a.nb, K = nb * 256, S = a.S, nch = a.nch;
-    const int NSLOT = S + 2;
-    // shared layout: ring [S][MT_STG] | x planes | zero[64] | red [NSLOT][MT_NC][MT_GR] | cnt | barriers
-    const uint32_t sbase = sptr(smem);
-    const uint32_t xq_off = (uint32_t)S * MT_STG;
-    const uint32_t xq_bytes = (uint32_t)K * 2 + (uint32_t)K / 2;
-    const uint32_t zero_off = xq_off + ((xq_bytes + 15) & ~15u);
-    float* red = reinterpret_cast<float*>(smem + zero_off + 64);
-    unsigned* cnt = reinterpret_cast<unsigned*>(red + NSLOT * MT_NC * MT_GR);
-    const uint32_t bar_full = (sptr(cnt + NSLOT) + 15) & ~7u;
-    const uint32_t bar_empty = bar_full + 8 * S;
-    const int c0 = blockIdx.x;
-    const int t0 = mt_start(c0, a.T, a.ncta), t1 = mt_start(c0 + 1, a.T, a.ncta);
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < S; s++) {
-            mbs_init(bar_full + 8 * s, 1);
-            mbs_init(bar_empty + 8 * s, MT_NC);
-        }
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    for (int i = threadIdx.x; i < NSLOT; i += blockDim.x) cnt[i] = 0;
-    if (threadIdx.x < 16) reinterpret_cast<uint32_t*>(smem + zero_off)[threadIdx.x] = 0;
-    __syncthreads();
-    griddep_launch();
+// Per-lane constants of the tensor-core fragment map (g = lane / 4 is the
+// row within an 8-row half tile and the B column; c = lane % 4 the column
+// group).  Only lanes with c == g / 2 carry nonzero B fragments; the others
+// read a zero line, with a zero stride, so no lane branches.
+struct MtLane {
+    int gq, c;
+    const uint8_t* xlb;   // B fragment base
+    int xstr;             // bytes per 256-column block (0 for zero lanes)
+};
 
-    if (warp == MT_NC) {   // ---- producer: one elected lane streams the stage boxes
-        if (lane == 0) {
-            int grp = t0 / nch, ch = t0 - grp * nch;
-            const int n_it = t1 - t0;
-            bool ok = true;
-            for (int i = 0; i < n_it; i++) {
-                const int s = i % S;
-                if (i >= S && !(ok = mbs_wait(bar_empty + 8 * s, ((i / S) - 1) & 1))) break;
-                mbs_expect(bar_full + 8 * s, MT_STG);
-                tma_load_3d(sbase + s * MT_STG, &tmap, 0, grp * MT_GR, ch * MT_KC, bar_full + 8 * s);
-                if (++ch == nch) { ch = 0; grp++; }
-            }
-            // do not retire while a box is still landing in this CTA's ring
-            for (int i = n_it > S ? n_it - S : 0; ok && i < n_it; i++)
-                ok = mbs_wait(bar_empty + 8 * (i % S), (i / S) & 1);
-        }
-        return;
-    }
-
-    // ---- consumers
-    griddep_wait();
-    uint8_t* xq = smem + xq_off;
-    mt_quantise_x(a.x, K, xq, threadIdx.x, MT_NC * 32);
-    mt_consumer_sync();
-    const int gq = lane >> 2, c = lane & 3;
-    const bool bact = c == (gq >> 1);   // this lane carries a nonzero B fragment
-    const uint8_t* xlb = bact ? xq + (gq & 1) * K + 64 * c : smem + zero_off;
-    const int xstr = bact ? 256 : 0;
-    const float4* xfb = reinterpret_cast<const float4*>(xq + 2 * K) + c;
-    const int sh8 = (c & 1) << 4;
-    const uint32_t MW = c >= 2 ? 0x0F0Fu : 0u, MY = c >= 2 ? 0x3030u : 0x3F3Fu, SY = c >= 2 ? 2u : 0u;
-    int grp = t0 / nch, ch = t0 - grp * nch, gi = 0;
-    const int first_grp = grp;
-    bool ok = true;
-    float acc_a[2] = {0.f, 0.f}, acc_b[2] = {0.f, 0.f};
-    for (int t = t0, i = 0; t < t1; t++, i++) {
-        const int s = i % S;
-        if (ok) ok = mbs_wait(bar_full + 8 * s, (i / S) & 1);
-        const uint8_t* stg = smem + s * MT_STG;
+// ---------------------------------------------------------------- Q4_K stage
+// Box {18 x u64, 32 rows, 16 blocks}: shared layout [block][row][144 B].  Warp
+// w takes blocks w and w + 8 of the stage, both 16-row tiles of each.
+struct MtQ4K {
+    static constexpr int NC = 8;         // consumer warps: blocks w and w + 8, both tiles
+    static constexpr int KC = 16;
+    static constexpr int STG = KC * MT_GR * GB_Q4K_BYTES;
+    static constexpr bool S16 = false;
+    static constexpr int XB_LANE = 64;   // B fragment offset per column group
+    static constexpr int ZSTEP = KC;     // tensor-map z units (blocks) per stage
+    __device__ static __forceinline__ void consume(const uint8_t* stg, int ch, int nb, int warp, const MtLane& L,
+                                                   const uint8_t* xq, int K, float acc_a[2], float acc_b[2]) {
+        const int gq = L.gq, c = L.c;
+        const float4* xfb = reinterpret_cast<const float4*>(xq + 2 * K) + c;
+        const int sh8 = (c & 1) << 4;
+        const uint32_t MW = c >= 2 ? 0x0F0Fu : 0u, MY = c >= 2 ? 0x3030u : 0x3F3Fu, SY = c >= 2 ? 2u : 0u;
         float pa[2][2], pb[2][2];
 #pragma unroll
         for (int j = 0; j < 2; j++) {   // blocks warp and warp + 8 of the stage
-            const int bl = warp + j * MT_NC;
-            const int b = ch * MT_KC + bl;
+            const int bl = warp + j * NC;
+            const int b = ch * KC + bl;
             pa[j][0] = pa[j][1] = pb[j][0] = pb[j][1] = 0.f;
-            if (!ok || b >= nb) continue;
-            const uint4* xb = reinterpret_cast<const uint4*>(xlb + b * xstr);
+            if (b >= nb) continue;
+            const uint4* xb = reinterpret_cast<const uint4*>(L.xlb + b * L.xstr);
             const uint4 bl0 = xb[0], bl1 = xb[1], bh0 = xb[2], bh1 = xb[3];
             const float4 xf = xfb[b * 4];
             const float xlo = xf.x * 0.00390625f, xhi = xf.y * (0.00390625f * 0.0625f);
@@ -852,10 +822,215 @@ __global__ void __launch_bounds__(MT_THREADS, 1) k_mvt_q4k(const __grid_constant
             acc_a[m] += pa[0][m] + pa[1][m];
             acc_b[m] += pb[0][m] + pb[1][m];
         }
+    }
+};
+
+// ---------------------------------------------------------------- Q6_K stage
+// Box {210 x u64 = 8 blocks, 32 rows, 1 chunk}: shared layout [row][1680 B];
+// warp w takes block w of every row, so its blocks start at 210 w within a
+// row and every field of the block sits at the same offset mod 8, MIS =
+// (2 w) mod 8.  Loads are specialised on MIS: 64-bit when aligned, two words
+// at 4, three words and two byte permutes at 2 or 6.
+template <int MIS>
+__device__ __forceinline__ uint2 lds8_mis(const uint8_t* p) {
+    if constexpr (MIS == 0) {
+        return *reinterpret_cast<const uint2*>(p);
+    } else if constexpr (MIS == 4) {
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(p);
+        return make_uint2(w[0], w[1]);
+    } else {
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(p - 2);
+        const uint32_t w0 = w[0], w1 = w[1], w2 = w[2];
+        return make_uint2(__byte_perm(w0, w1, 0x5432), __byte_perm(w1, w2, 0x5432));
+    }
+}
+// 6-bit codes of weights 128 n + 32 G + [8c, 8c + 8) from the ql / qh words
+// (low / high word of the lane's 8 bytes): low nibble for G < 2, high for
+// G >= 2; ql from byte 8c (G even) or 32 + 8c (G odd); qh bits 2G..2G+1.
+// Byte of w chosen by the prmt selector sel, sign-extended (prmt selector
+// nibbles with bit 3 set replicate the sign of the chosen byte).
+__device__ __forceinline__ int prmt_sext(uint32_t w, int sel) {
+    int r;
+    asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(w), "r"(sel));
+    return r;
+}
+template <int G>
+__device__ __forceinline__ uint32_t q6_code(uint32_t lw, uint32_t hw) {
+    const uint32_t nib = (G >> 1) ? ((lw >> 4) & 0x0F0F0F0Fu) : (lw & 0x0F0F0F0Fu);
+    const uint32_t hi = G == 0 ? (hw << 4) : G == 1 ? (hw << 2) : G == 2 ? hw : (hw >> 2);
+    return nib | (hi & 0x30303030u);
+}
+struct MtQ6K {
+    static constexpr int NC = 16;        // consumer warps: block w % 8, 16-row tile w / 8
+    static constexpr int KC = 8;
+    static constexpr int RB = 8 * GB_Q6K_BYTES;   // 1680 bytes per row per stage
+    static constexpr int STG = MT_GR * RB;
+    static constexpr bool S16 = true;
+    static constexpr int XB_LANE = 8;
+    static constexpr int ZSTEP = 1;      // tensor-map z units (8-block chunks) per stage
+    template <int MIS>
+    __device__ static __forceinline__ void tile(const uint8_t* blk_a, int c, const uint8_t* xb, const float* xf,
+                                                const float4 s16lo, const float4 s16hi, float fc, int selsc0,
+                                                int selsc1, float& acc_a, float& acc_b) {
+        const uint8_t* blk_b = blk_a + 8 * RB;
+        const uint8_t* ra = blk_a + 8 * c;   // the lane's 8 bytes of each 32-byte ql / qh run
+        const uint8_t* rb = blk_b + 8 * c;
+        float ba = 0.f, bb = 0.f;   // block sums before the super-scale d
+        // int8 scales of rows a and b, 16 bytes at 192
+        uint32_t sa[4], sb[4];
+        {
+            const uint2 a0 = lds8_mis<MIS>(blk_a + 192), a1 = lds8_mis<MIS>(blk_a + 200);
+            const uint2 b0 = lds8_mis<MIS>(blk_b + 192), b1 = lds8_mis<MIS>(blk_b + 200);
+            sa[0] = a0.x; sa[1] = a0.y; sa[2] = a1.x; sa[3] = a1.y;
+            sb[0] = b0.x; sb[1] = b0.y; sb[2] = b1.x; sb[3] = b1.y;
+        }
+#pragma unroll
+        for (int n = 0; n < 2; n++) {
+            const uint2 qa0 = lds8_mis<MIS>(ra + 64 * n), qa1 = lds8_mis<MIS>(ra + 64 * n + 32);
+            const uint2 qb0 = lds8_mis<MIS>(rb + 64 * n), qb1 = lds8_mis<MIS>(rb + 64 * n + 32);
+            const uint2 ha = lds8_mis<MIS>(ra + 128 + 32 * n), hb = lds8_mis<MIS>(rb + 128 + 32 * n);
+            const float4 xs = *reinterpret_cast<const float4*>(xf + 8 * n);       // sub-blocks 4n, 4n+1
+            const float4 xs2 = *reinterpret_cast<const float4*>(xf + 8 * n + 4);  // sub-blocks 4n+2, 4n+3
+#pragma unroll
+            for (int G = 0; G < 4; G++) {
+                const uint2& la = (G & 1) ? qa1 : qa0;
+                const uint2& lb = (G & 1) ? qb1 : qb0;
+                uint32_t A0, A1, A2, A3;
+                switch (G) {
+                    case 0: A0 = q6_code<0>(la.x, ha.x); A1 = q6_code<0>(lb.x, hb.x); A2 = q6_code<0>(la.y, ha.y); A3 = q6_code<0>(lb.y, hb.y); break;
+                    case 1: A0 = q6_code<1>(la.x, ha.x); A1 = q6_code<1>(lb.x, hb.x); A2 = q6_code<1>(la.y, ha.y); A3 = q6_code<1>(lb.y, hb.y); break;
+                    case 2: A0 = q6_code<2>(la.x, ha.x); A1 = q6_code<2>(lb.x, hb.x); A2 = q6_code<2>(la.y, ha.y); A3 = q6_code<2>(lb.y, hb.y); break;
+                    default: A0 = q6_code<3>(la.x, ha.x); A1 = q6_code<3>(lb.x, hb.x); A2 = q6_code<3>(la.y, ha.y); A3 = q6_code<3>(lb.y, hb.y); break;
+                }
+                const uint2 bf = *reinterpret_cast<const uint2*>(xb + 128 * n + 32 * G);
+                int4 cc = make_int4(0, 0, 0, 0);
+                mma_u8s8(cc, A0, A1, A2, A3, bf.x, bf.y);
+                const float xsg = ((G >> 1) ? ((G & 1) ? xs2.y : xs2.x) : ((G & 1) ? xs.y : xs.x)) * 0.00390625f;
+                const float s16 = n ? ((G == 0) ? s16hi.x : (G == 1) ? s16hi.y : (G == 2) ? s16hi.z : s16hi.w)
+                                    : ((G == 0) ? s16lo.x : (G == 1) ? s16lo.y : (G == 2) ? s16lo.z : s16lo.w);
+                // scale byte 8n + 2G + (c >> 1): word 2n + (G >> 1), byte 2 (G & 1) + (c >> 1)
+                const int sel = (G & 1) ? selsc1 : selsc0;
+                const float sca = (float)prmt_sext(sa[2 * n + (G >> 1)], sel);
+                const float scb = (float)prmt_sext(sb[2 * n + (G >> 1)], sel);
+                const float ta = fmaf(xsg, (float)(cc.x * 256 + cc.y), fc * s16);
+                const float tb = fmaf(xsg, (float)(cc.z * 256 + cc.w), fc * s16);
+                ba = fmaf(sca, ta, ba);
+                bb = fmaf(scb, tb, bb);
+            }
+        }
+        const float da = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(blk_a + 208)));
+        const float db = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(blk_b + 208)));
+        acc_a = fmaf(da, ba, acc_a);
+        acc_b = fmaf(db, bb, acc_b);
+    }
+    template <int MIS>
+    __device__ static __forceinline__ void run(const uint8_t* stg, int b, int warp, const MtLane& L, const uint8_t* xq,
+                                               int K, float acc_a[2], float acc_b[2]) {
+        const int c = L.c;
+        const uint8_t* xb = L.xlb + b * L.xstr;
+        const float* xf = reinterpret_cast<const float*>(xq + 2 * K) + b * 16;   // {s, s, sum, sum} x 4
+        // xf holds per 64-column chunk {s lo, s hi, sum lo, sum hi}: the scale
+        // of 32-column sub-block 4n + G is xf[8n + 4 (G >> 1) + (G & 1)]
+        const float* f16 = reinterpret_cast<const float*>(xq + 2 * K + K / 4) + b * 16 + (c >> 1) * 8;
+        const float4 s16lo = *reinterpret_cast<const float4*>(f16);
+        const float4 s16hi = *reinterpret_cast<const float4*>(f16 + 4);
+        const float fc = (c & 1) ? 0.f : -32.f;   // the -32 offset of the codes, once per 16 columns
+        const int h = c >> 1;
+        // prmt selectors extracting byte 2 (G & 1) + h sign-extended
+        const int b0 = h, b1 = 2 + h;
+        const int selsc0 = b0 | ((b0 | 8) << 4) | ((b0 | 8) << 8) | ((b0 | 8) << 12);
+        const int selsc1 = b1 | ((b1 | 8) << 4) | ((b1 | 8) << 8) | ((b1 | 8) << 12);
+        const int m = warp >> 3;
+        const uint8_t* blk = stg + (m * 16 + L.gq) * RB + (warp & 7) * GB_Q6K_BYTES;
+        tile<MIS>(blk, c, xb, xf, s16lo, s16hi, fc, selsc0, selsc1, acc_a[m], acc_b[m]);
+    }
+    __device__ static __forceinline__ void consume(const uint8_t* stg, int ch, int nb, int warp, const MtLane& L,
+                                                   const uint8_t* xq, int K, float acc_a[2], float acc_b[2]) {
+        const int b = ch * KC + (warp & 7);
+        if (b >= nb) return;
+        switch ((2 * warp) & 7) {
+            case 0: run<0>(stg, b, warp, L, xq, K, acc_a, acc_b); break;
+            case 2: run<2>(stg, b, warp, L, xq, K, acc_a, acc_b); break;
+            case 4: run<4>(stg, b, warp, L, xq, K, acc_a, acc_b); break;
+            default: run<6>(stg, b, warp, L, xq, K, acc_a, acc_b); break;
+        }
+    }
+};
+
+template <class F>
+__global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_constant__ CUtensorMap tmap, const MtArgs a) {
+    constexpr int MT_NC = F::NC;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nb = a.nb, K = nb * 256, S = a.S, nch = a.nch;
+    const int NSLOT = S + 2;
+    // shared layout: ring [S][F::STG] | x | zero[64] | red [NSLOT][MT_NC][MT_GR] | cnt | barriers
+    const uint32_t sbase = sptr(smem);
+    const uint32_t xq_off = (uint32_t)S * F::STG;
+    const uint32_t xq_bytes = (uint32_t)mt_xq_bytes(K, F::S16);
+    const uint32_t zero_off = xq_off + ((xq_bytes + 15) & ~15u);
+    float* red = reinterpret_cast<float*>(smem + zero_off + MT_ZERO);
+    unsigned* cnt = reinterpret_cast<unsigned*>(red + NSLOT * MT_NC * MT_GR);
+    const uint32_t bar_full = (sptr(cnt + NSLOT) + 15) & ~7u;
+    const uint32_t bar_empty = bar_full + 8 * S;
+    const int c0 = blockIdx.x;
+    const int TU = a.T / a.unit;
+    const int t0 = mt_start(c0, TU, a.ncta) * a.unit, t1 = mt_start(c0 + 1, TU, a.ncta) * a.unit;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; s++) {
+            mbs_init(bar_full + 8 * s, 1);
+            mbs_init(bar_empty + 8 * s, MT_NC);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    for (int i = threadIdx.x; i < NSLOT; i += blockDim.x) cnt[i] = 0;
+    if (threadIdx.x < MT_ZERO / 4) reinterpret_cast<uint32_t*>(smem + zero_off)[threadIdx.x] = 0;
+    __syncthreads();
+    griddep_launch();
+
+    if (warp == MT_NC) {   // ---- producer: one elected lane streams the stage boxes
+        if (lane == 0) {
+            int grp = t0 / nch, ch = t0 - grp * nch;
+            const int n_it = t1 - t0;
+            bool ok = true;
+            for (int i = 0; i < n_it; i++) {
+                const int s = i % S;
+                if (i >= S && !(ok = mbs_wait(bar_empty + 8 * s, ((i / S) - 1) & 1))) break;
+                mbs_expect(bar_full + 8 * s, F::STG);
+                tma_load_3d(sbase + s * F::STG, &tmap, 0, grp * MT_GR, ch * F::ZSTEP, bar_full + 8 * s);
+                if (++ch == nch) { ch = 0; grp++; }
+            }
+            // do not retire while a box is still landing in this CTA's ring
+            for (int i = n_it > S ? n_it - S : 0; ok && i < n_it; i++)
+                ok = mbs_wait(bar_empty + 8 * (i % S), (i / S) & 1);
+        }
+        return;
+    }
+
+    // ---- consumers
+    griddep_wait();
+    uint8_t* xq = smem + xq_off;
+    mt_quantise_x<F::S16>(a.x, K, xq, threadIdx.x, MT_NC * 32);
+    mt_consumer_sync<MT_NC>();
+    MtLane L;
+    L.gq = lane >> 2;
+    L.c = lane & 3;
+    const bool bact = L.c == (L.gq >> 1);   // this lane carries a nonzero B fragment
+    L.xlb = bact ? xq + (L.gq & 1) * K + F::XB_LANE * L.c : smem + zero_off;
+    L.xstr = bact ? 256 : 0;
+    int grp = t0 / nch, ch = t0 - grp * nch, gi = 0;
+    const int first_grp = grp;
+    bool ok = true;
+    float acc_a[2] = {0.f, 0.f}, acc_b[2] = {0.f, 0.f};
+    for (int t = t0, i = 0; t < t1; t++, i++) {
+        const int s = i % S;
+        if (ok) ok = mbs_wait(bar_full + 8 * s, (i / S) & 1);
+        if (ok) F::consume(smem + s * F::STG, ch, nb, warp, L, xq, K, acc_a, acc_b);
         __syncwarp();
         if (lane == 0) mbs_arrive(bar_empty + 8 * s);
 
         if (ch == nch - 1 || t == t1 - 1) {   // ---- this CTA's part of group grp is done
+            const int gq = L.gq, c = L.c;
 #pragma unroll
             for (int m = 0; m < 2; m++) {
                 acc_a[m] += __shfl_xor_sync(0xffffffffu, acc_a[m], 1);
@@ -894,7 +1069,7 @@ __global__ void __launch_bounds__(MT_THREADS, 1) k_mvt_q4k(const __grid_constant
                     const int half = grp == first_grp ? 0 : 1;
                     a.part[(c0 * 2 + half) * MT_GR + lane] = v;
                     __syncwarp();
-                    const int cf = mt_owner(gs, a.T, a.ncta), cl2 = mt_owner(gs + nch - 1, a.T, a.ncta);
+                    const int cf = mt_owner(gs, a.T, a.ncta), cl2 = mt_owner(gs + nch - 1, a.T, a.ncta);   // unit == 1 here
                     unsigned g = 0;
                     if (lane == 0) g = atom_add_acq_rel(&a.tickets[grp], 1u);
                     g = __shfl_sync(0xffffffffu, g, 0);
@@ -996,10 +1171,41 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return fn;
 }
 
+template <class F>
 static size_t mt_smem_bytes(int S, int K) {
-    const size_t xq = ((size_t)K * 2 + (size_t)K / 2 + 15) & ~(size_t)15;
+    const size_t xq = ((size_t)mt_xq_bytes(K, F::S16) + 15) & ~(size_t)15;
     const int nslot = S + 2;
-    return (size_t)S * MT_STG + xq + 64 + (size_t)nslot * MT_NC * MT_GR * 4 + (size_t)nslot * 4 + 16 + 16 * (size_t)S;
+    return (size_t)S * F::STG + xq + MT_ZERO + (size_t)nslot * F::NC * MT_GR * 4 + (size_t)nslot * 4 + 16 +
+           16 * (size_t)S;
+}
+
+// Encode the 3-D view {one box row of bytes as u64, rows, z} of W for format F.
+template <class F>
+static bool mt_encode(MvPlan* p, const void* W, int rows, int nb) {
+    auto enc = tensor_map_encoder();
+    if (!enc) return false;
+    int S = 4;
+    while (S > 2 && mt_smem_bytes<F>(S, nb * 256) > (size_t)MV_SMEM_MAX) S--;
+    if (mt_smem_bytes<F>(S, nb * 256) > (size_t)MV_SMEM_MAX) return false;
+    const int blk = F::STG / (MT_GR * F::KC);   // bytes per block
+    const cuuint64_t rb = (cuuint64_t)nb * blk;
+    const int inner = F::ZSTEP == 1 ? F::KC * blk : blk;   // bytes per box row
+    cuuint64_t dims[3] = {(cuuint64_t)inner / 8, (cuuint64_t)rows, (cuuint64_t)(nb * blk / inner)};
+    cuuint64_t strides[2] = {rb, (cuuint64_t)inner};
+    cuuint32_t box[3] = {(cuuint32_t)inner / 8, MT_GR, (cuuint32_t)(F::ZSTEP == 1 ? 1 : F::KC)};
+    cuuint32_t es[3] = {1, 1, 1};
+    if (enc(reinterpret_cast<CUtensorMap*>(p->tmap), CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<void*>(W), dims,
+            strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    p->kind = MV_TMA;
+    p->S = S;
+    p->smem = mt_smem_bytes<F>(S, nb * 256);
+    p->nch = (nb + F::KC - 1) / F::KC;
+    p->ngroups = (rows + MT_GR - 1) / MT_GR;
+    p->T = p->ngroups * p->nch;
+    p->ncta = p->T < GB_NUM_SMS ? p->T : GB_NUM_SMS;
+    return true;
 }
 
 int mv_plan(MvPlan* p, int dtype, const void* W, int rows, int cols) {
@@ -1015,34 +1221,13 @@ int mv_plan(MvPlan* p, int dtype, const void* W, int rows, int cols) {
     p->cols = cols;
     p->nb = cols / width;
     p->kind = MV_RING;
-    if (dtype == GB_DT_Q4_K) {
-        auto enc = tensor_map_encoder();
-        int S = 4;
-        while (S > 2 && mt_smem_bytes(S, cols) > (size_t)MV_SMEM_MAX) S--;
-        if (enc && mt_smem_bytes(S, cols) <= (size_t)MV_SMEM_MAX) {
-            const cuuint64_t rb = (cuuint64_t)p->nb * GB_Q4K_BYTES;
-            cuuint64_t dims[3] = {GB_Q4K_BYTES / 8, (cuuint64_t)rows, (cuuint64_t)p->nb};
-            cuuint64_t strides[2] = {rb, GB_Q4K_BYTES};
-            cuuint32_t box[3] = {GB_Q4K_BYTES / 8, MT_GR, MT_KC};
-            cuuint32_t es[3] = {1, 1, 1};
-            CUtensorMap* m = reinterpret_cast<CUtensorMap*>(p->tmap);
-            if (enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<void*>(W), dims, strides, box, es,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
-                p->kind = MV_TMA;
-                p->S = S;
-                p->smem = mt_smem_bytes(S, cols);
-                p->nch = (p->nb + MT_KC - 1) / MT_KC;
-                p->ngroups = (rows + MT_GR - 1) / MT_GR;
-                p->T = p->ngroups * p->nch;
-                p->ncta = p->T < GB_NUM_SMS ? p->T : GB_NUM_SMS;
-            }
-        }
-    }
+    // TMA path: Q4_K rows (144 nb bytes) are always 16-byte multiples; Q6_K
+    // rows (210 nb bytes) are when nb is a multiple of 8.
+    if (dtype == GB_DT_Q4_K) mt_encode<MtQ4K>(p, W, rows, p->nb);
+    if (dtype == GB_DT_Q6_K && p->nb % 8 == 0) mt_encode<MtQ6K>(p, W, rows, p->nb);
     if (p->kind == MV_RING) {
         MvGeom g;
         if (!choose_geom(dtype, rows, p->nb, &g)) return GB_ELIMIT;
-        if ((reinterpret_cast<uintptr_t>(W) & 15)) return GB_EINVAL;
     }
     return GB_OK;
 }
@@ -1067,13 +1252,14 @@ int mv_launch(const MvPlan& p, const float* x, float* y, const float* residual, 
         }
         return e == cudaSuccess ? GB_OK : GB_ECUDA;
     }
-    if (!ws) return GB_EINVAL;
-    static unsigned configured = 0;
+    static unsigned configured[2] = {0, 0};
+    const bool q6 = p.dtype == GB_DT_Q6_K;
     int dev = 0;
     GB_CUDA_TRY(cudaGetDevice(&dev));
-    if (!(configured & (1u << (dev & 31)))) {
-        GB_CUDA_TRY(cudaFuncSetAttribute(k_mvt_q4k, cudaFuncAttributeMaxDynamicSharedMemorySize, MV_SMEM_MAX));
-        configured |= 1u << (dev & 31);
+    if (!(configured[q6] & (1u << (dev & 31)))) {
+        GB_CUDA_TRY(cudaFuncSetAttribute(q6 ? k_mvt<MtQ6K> : k_mvt<MtQ4K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         MV_SMEM_MAX));
+        configured[q6] |= 1u << (dev & 31);
     }
     MtArgs a;
     a.x = x;
@@ -1085,11 +1271,13 @@ int mv_launch(const MvPlan& p, const float* x, float* y, const float* residual, 
     a.nb = p.nb;
     a.nch = p.nch;
     a.T = p.T;
-    a.ncta = p.ncta;
+    // with a workspace: stream-K over stage items; without: whole groups per CTA
+    a.unit = ws ? 1 : p.nch;
+    a.ncta = ws ? p.ncta : (p.ngroups < GB_NUM_SMS ? p.ngroups : GB_NUM_SMS);
     a.S = p.S;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(p.ncta);
-    cfg.blockDim = dim3(MT_THREADS);
+    cfg.gridDim = dim3(a.ncta);
+    cfg.blockDim = dim3(((q6 ? MtQ6K::NC : MtQ4K::NC) + 1) * 32);
     cfg.dynamicSmemBytes = p.smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -1098,7 +1286,10 @@ int mv_launch(const MvPlan& p, const float* x, float* y, const float* residual, 
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
     const CUtensorMap* m = reinterpret_cast<const CUtensorMap*>(p.tmap);
-    GB_CUDA_TRY(cudaLaunchKernelEx(&cfg, k_mvt_q4k, *m, a));
+    if (q6)
+        GB_CUDA_TRY(cudaLaunchKernelEx(&cfg, k_mvt<MtQ6K>, *m, a));
+    else
+        GB_CUDA_TRY(cudaLaunchKernelEx(&cfg, k_mvt<MtQ4K>, *m, a));
     return GB_OK;
 }
 
@@ -1108,12 +1299,16 @@ int mv_launch(const MvPlan& p, const float* x, float* y, const float* residual, 
 static std::mutex g_ws_mu;
 static std::map<std::pair<int, cudaStream_t>, std::pair<void*, size_t>> g_ws;
 
+// Returns nullptr when no buffer can be made now (the stream is being
+// captured); the launch then splits by whole groups and needs none.
 static void* stream_workspace(cudaStream_t st, size_t bytes) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
     std::lock_guard<std::mutex> lk(g_ws_mu);
     auto& e = g_ws[{dev, st}];
     if (e.second >= bytes) return e.first;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return nullptr;
     if (e.first) {
         cudaStreamSynchronize(st);
         cudaFree(e.first);
@@ -1121,7 +1316,7 @@ static void* stream_workspace(cudaStream_t st, size_t bytes) {
     }
     void* ptr = nullptr;
     if (cudaMalloc(&ptr, bytes) != cudaSuccess) return nullptr;
-    if (cudaMemset(ptr, 0, bytes) != cudaSuccess) {
+    if (cudaMemsetAsync(ptr, 0, bytes, st) != cudaSuccess) {
         cudaFree(ptr);
         return nullptr;
     }
@@ -1141,8 +1336,7 @@ extern "C" int gb_matvec(int dtype, const void* W, int rows, int cols, const flo
     int rc = mv_plan(&p, dtype, W, rows, cols);
     if (rc) return rc;
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    void* ws = nullptr;
-    if (p.kind == MV_TMA && !(ws = stream_workspace(st, mv_ws_bytes(p)))) return GB_ENOMEM;
+    void* ws = p.kind == MV_TMA ? stream_workspace(st, mv_ws_bytes(p)) : nullptr;
     return mv_launch(p, x, y, residual, ws, st, false);
 }
 

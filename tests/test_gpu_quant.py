@@ -229,3 +229,97 @@ def test_cuda_matvec_q4k_impl_parity(gb, oracle):
     y = np.zeros(rows, np.float32)
     assert gb.lib().cuda_matvec_q4k_f32_impl(d, x.ctypes.data, y.ctypes.data, rows, cols) == 0
     assert np.max(np.abs(y - y_cpu)) <= 1e-4 * max(1.0, np.abs(y_cpu).max())
+
+
+@pytest.mark.parametrize("dt,rows,cols", [(4, 1000, 16384), (5, 1000, 16384), (4, 4099, 4096), (5, 77, 2048)])
+def test_matvec_split_groups_deterministic(gb, oracle, cuda, dt, rows, cols):
+    """Groups split across CTAs finish through the ticketed partials: two calls
+    in a row agree bit for bit (fixed summation order) and with the oracle."""
+    W = oracle.synth_blocks(dt, rows, cols, 99, rows + cols)
+    x = oracle.synth_normal(cols, 99, 1)
+    _, y_ref = oracle.matvec(dt, W, rows, cols, x)
+    y1 = run_matvec(gb, cuda, dt, W, rows, cols, x)
+    y2 = run_matvec(gb, cuda, dt, W, rows, cols, x)
+    assert np.array_equal(y1, y2)
+    assert rel_l2(y1, y_ref) <= 1e-4
+    assert gb.lib().gb_device_error(1) == 0
+
+
+@pytest.mark.parametrize("dt,rows,cols", [(4, 4096, 4096), (5, 4096, 14336), (4, 50, 256)])
+def test_matvec_in_place_residual(gb, oracle, cuda, dt, rows, cols):
+    """y = residual + W x with y and residual the same buffer (the decode
+    layer's hidden += W x)."""
+    W = oracle.synth_blocks(dt, rows, cols, 7, 8)
+    x = oracle.synth_normal(cols, 7, 9)
+    r = oracle.synth_normal(rows, 7, 10)
+    _, y_ref = oracle.matvec(dt, W, rows, cols, x)
+    dW = cuda.zeros(W.size + 16, dtype=cuda.uint8, device="cuda")
+    dW[: W.size] = cuda.from_numpy(W).cuda()
+    dx = cuda.from_numpy(x).cuda()
+    h = cuda.from_numpy(r.copy()).cuda()
+    gb.matvec(dt, dW, rows, cols, dx, h, residual=h)
+    cuda.cuda.synchronize()
+    assert rel_l2(h.cpu().numpy(), y_ref + r) <= 1e-4
+
+
+def test_matvec_two_streams(gb, oracle, cuda):
+    """Calls on different streams use different workspaces."""
+    rows, cols = 3000, 4096
+    Ws = [oracle.synth_blocks(4, rows, cols, 3, s) for s in (1, 2)]
+    x = oracle.synth_normal(cols, 3, 3)
+    refs = [oracle.matvec(4, W, rows, cols, x)[1] for W in Ws]
+    dWs = []
+    for W in Ws:
+        d = cuda.zeros(W.size + 16, dtype=cuda.uint8, device="cuda")
+        d[: W.size] = cuda.from_numpy(W).cuda()
+        dWs.append(d)
+    dx = cuda.from_numpy(x).cuda()
+    streams = [cuda.cuda.Stream() for _ in range(2)]
+    ys = [cuda.empty(rows, dtype=cuda.float32, device="cuda") for _ in range(2)]
+    cuda.cuda.synchronize()
+    for it in range(20):
+        for i in range(2):
+            gb.matvec(4, dWs[i], rows, cols, dx, ys[i], stream=streams[i].cuda_stream)
+    cuda.cuda.synchronize()
+    for i in range(2):
+        assert rel_l2(ys[i].cpu().numpy(), refs[i]) <= 1e-4
+
+
+@pytest.mark.parametrize("dt,rows,cols", [(4, 14336, 4096), (5, 4096, 14336), (4, 33, 512)])
+def test_matvec_captured_without_workspace(gb, oracle, cuda, dt, rows, cols):
+    """First use on a stream that is being captured: no workspace can be made,
+    so the launch splits by whole row groups; the graph replays correctly."""
+    W = oracle.synth_blocks(dt, rows, cols, 11, 12)
+    x = oracle.synth_normal(cols, 11, 13)
+    _, y_ref = oracle.matvec(dt, W, rows, cols, x)
+    dW = cuda.zeros(W.size + 16, dtype=cuda.uint8, device="cuda")
+    dW[: W.size] = cuda.from_numpy(W).cuda()
+    dx = cuda.from_numpy(x).cuda()
+    y = cuda.zeros(rows, dtype=cuda.float32, device="cuda")
+    cuda.cuda.synchronize()
+    g = cuda.cuda.CUDAGraph()
+    with cuda.cuda.graph(g, capture_error_mode="relaxed"):
+        gb.matvec(dt, dW, rows, cols, dx, y)
+    g.replay()
+    cuda.cuda.synchronize()
+    assert rel_l2(y.cpu().numpy(), y_ref) <= 1e-4
+    del g
+
+
+def test_vtable_host_cache_detects_reuse(gb, oracle, cuda):
+    """A host weight buffer rewritten at the same address (as a freed and
+    reallocated numpy array can be) is uploaded again, not served stale."""
+    be = gb.CudaBackend()
+    try:
+        rows, cols = 40, 2048
+        W = oracle.synth_blocks(5, rows, cols, 21, 1)
+        x = oracle.synth_normal(cols, 21, 2)
+        t = gb.make_tensor(5, W, rows, cols)
+        y = np.zeros(rows, np.float32)
+        assert be.matvec(t, x, y) == 0
+        assert rel_l2(y, oracle.matvec(5, W, rows, cols, x)[1]) <= 1e-4
+        W[:] = oracle.synth_blocks(5, rows, cols, 21, 2)   # same address, new content
+        assert be.matvec(t, x, y) == 0
+        assert rel_l2(y, oracle.matvec(5, W, rows, cols, x)[1]) <= 1e-4
+    finally:
+        be.close()
