@@ -104,6 +104,8 @@ SIGNATURES = {
     "gb_rope_table": (_i, [_vp, _i, _i, _f, _vp]),
     "gb_attn_workspace_bytes": (_sz, [_i, _i, _i, _i]),
     "gb_attention_decode": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp, _vp]),
+    "gb_attention_decode_static": (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp, _vp]),
+    "gb_attention_static_error": (_i, [_i]),
     "gb_rmsnorm": (_i, [_vp, _vp, _vp, _i, _f, _vp]),
     "gb_silu_mul": (_i, [_vp, _vp, _i, _vp]),
     "gb_argmax": (_i, [_vp, _i, _vp, _vp]),
@@ -191,6 +193,15 @@ def attention_decode(q, k, v, k_cache, v_cache, rope_cs, d_pos, n_heads, n_kv, h
     check("gb_attention_decode", lib().gb_attention_decode(
         _ptr(q), _ptr(k), _ptr(v), _ptr(k_cache), _ptr(v_cache), _ptr(rope_cs), _ptr(d_pos),
         n_heads, n_kv, head_dim, max_seq, _ptr(out), _ptr(ws), _stream(stream)))
+
+
+def attention_decode_static(q, k, v, k_cache, v_cache, rope_cs, d_pos, n_heads, n_kv, head_dim, max_seq, out,
+                            stream=None) -> None:
+    """gb_attention_decode with the library's static scratch (no workspace,
+    no allocation); calls on one device must not overlap."""
+    check("gb_attention_decode_static", lib().gb_attention_decode_static(
+        _ptr(q), _ptr(k), _ptr(v), _ptr(k_cache), _ptr(v_cache), _ptr(rope_cs), _ptr(d_pos),
+        n_heads, n_kv, head_dim, max_seq, _ptr(out), _stream(stream)))
 
 
 def rmsnorm(x, w, out, n, eps, stream=None) -> None:

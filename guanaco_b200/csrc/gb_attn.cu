@@ -31,6 +31,8 @@
 #include "gb_common.cuh"
 #include "gb_internal.h"
 
+#include <mutex>
+
 namespace gb {
 
 constexpr int ATTN_THREADS = 256;
@@ -60,7 +62,8 @@ __global__ void __launch_bounds__(ATTN_THREADS)
 k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const float* __restrict__ vnew,
               float* __restrict__ kc, float* __restrict__ vc, const float* __restrict__ rope_cs,
               const int* __restrict__ d_pos, int n_kv, int max_seq, int grid_splits,
-              float* __restrict__ out, float* __restrict__ part, unsigned* __restrict__ tickets) {
+              float* __restrict__ out, float* __restrict__ part, unsigned* __restrict__ tickets,
+              unsigned* __restrict__ err) {
     using C = AttnCfg<HD, GROUP>;
     extern __shared__ __align__(16) float sm[];
     float* qs = sm;                       // [GROUP][HD] rotated q
@@ -72,7 +75,6 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int kvh = blockIdx.x / grid_splits, split = blockIdx.x % grid_splits;
     const int pos = *d_pos;
-    unsigned* err = tickets + n_kv;
     if (pos < 0 || pos >= max_seq) {
         if (blockIdx.x == 0 && tid == 0) atomicExch(err, (unsigned)(-GB_EPOS));
         return;
@@ -237,10 +239,12 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
     if (tid == 0) tickets[kvh] = 0u;   // every split has arrived: safe to rearm
 }
 
+// part: split partials; tickets: n_kv per-KV-head counters (zero between
+// calls); err: the error word (GB_EPOS when pos is outside [0, max_seq)).
 template <int HD, int GROUP>
 static cudaError_t launch_attn(const float* q, const float* k, const float* v, float* kc, float* vc,
                                const float* cs, const int* d_pos, int n_kv, int max_seq, float* out,
-                               void* ws, cudaStream_t st) {
+                               float* part, unsigned* tickets, unsigned* err, cudaStream_t st) {
     using C = AttnCfg<HD, GROUP>;
     static unsigned configured = 0;
     int dev = 0;
@@ -252,11 +256,50 @@ static cudaError_t launch_attn(const float* q, const float* k, const float* v, f
         configured |= 1u << (dev & 31);
     }
     const int G = attn_grid_splits(n_kv, max_seq);
-    float* part = static_cast<float*>(ws);
-    unsigned* tickets = reinterpret_cast<unsigned*>(part + (size_t)n_kv * G * GROUP * (HD + 2));
     k_attn_decode<HD, GROUP><<<n_kv * G, ATTN_THREADS, C::SMEM, st>>>(q, k, v, kc, vc, cs, d_pos, n_kv, max_seq, G,
-                                                                      out, part, tickets);
+                                                                      out, part, tickets, err);
     return cudaGetLastError();
+}
+
+// Both entry points: pick the instantiation for (head_dim, group).
+static int attn_dispatch(const float* q, const float* k, const float* v, float* kc, float* vc, const float* cs,
+                         const int* d_pos, int n_heads, int n_kv, int head_dim, int max_seq, float* out,
+                         float* part, unsigned* tickets, unsigned* err, cudaStream_t st) {
+    const int group = n_heads / n_kv;
+    cudaError_t e = cudaErrorInvalidValue;
+#define GB_ATTN_CASE(HDV, GV)                                                                                       \
+    if (head_dim == HDV && group == GV)                                                                             \
+        e = launch_attn<HDV, GV>(q, k, v, kc, vc, cs, d_pos, n_kv, max_seq, out, part, tickets, err, st);
+    GB_ATTN_CASE(128, 1) GB_ATTN_CASE(128, 2) GB_ATTN_CASE(128, 4) GB_ATTN_CASE(128, 8)
+    GB_ATTN_CASE(64, 1) GB_ATTN_CASE(64, 2) GB_ATTN_CASE(64, 4) GB_ATTN_CASE(64, 8)
+#undef GB_ATTN_CASE
+    if (e == cudaErrorInvalidValue) return GB_EINVAL;
+    return e == cudaSuccess ? GB_OK : GB_ECUDA;
+}
+
+// ---------------------------------------------------------------- static scratch
+// Scratch of gb_attention_decode_static: a file-scope device array, zero at
+// module load.  Layout: words [0, n_kv) split-K tickets (only ever tickets,
+// back to zero after every call), word GB_ATTN_STATIC_ERR_WORD the error word,
+// partials from byte GB_ATTN_STATIC_PART_OFFSET.
+constexpr int GB_ATTN_STATIC_ERR_WORD = 1023;
+constexpr size_t GB_ATTN_STATIC_PART_OFFSET = 4096;
+static __device__ __align__(256) unsigned char g_attn_static[GB_ATTN_STATIC_BYTES];
+static std::mutex g_attn_static_mu;
+static void* g_attn_static_addr[64];   // per device, resolved once
+
+static unsigned char* attn_static_scratch(int* rc) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) { *rc = GB_ECUDA; return nullptr; }
+    if (dev < 0 || dev >= 64) { *rc = GB_ELIMIT; return nullptr; }
+    std::lock_guard<std::mutex> lk(g_attn_static_mu);
+    if (!g_attn_static_addr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_attn_static) != cudaSuccess || !p) { *rc = GB_ECUDA; return nullptr; }
+        g_attn_static_addr[dev] = p;
+    }
+    *rc = GB_OK;
+    return static_cast<unsigned char*>(g_attn_static_addr[dev]);
 }
 
 }  // namespace gb
@@ -277,13 +320,40 @@ extern "C" int gb_attention_decode(const float* q, const float* k, const float* 
     if (!q || !k || !v || !k_cache || !v_cache || !rope_cs || !d_pos || !out || !ws) return GB_EINVAL;
     if (n_kv <= 0 || n_heads <= 0 || n_heads % n_kv || max_seq <= 0) return GB_EINVAL;
     const int group = n_heads / n_kv;
-    const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    cudaError_t e = cudaErrorInvalidValue;
-#define GB_ATTN_CASE(HDV, GV) \
-    if (head_dim == HDV && group == GV) e = launch_attn<HDV, GV>(q, k, v, k_cache, v_cache, rope_cs, d_pos, n_kv, max_seq, out, ws, st);
-    GB_ATTN_CASE(128, 1) GB_ATTN_CASE(128, 2) GB_ATTN_CASE(128, 4) GB_ATTN_CASE(128, 8)
-    GB_ATTN_CASE(64, 1) GB_ATTN_CASE(64, 2) GB_ATTN_CASE(64, 4) GB_ATTN_CASE(64, 8)
-#undef GB_ATTN_CASE
-    if (e == cudaErrorInvalidValue) return GB_EINVAL;
-    return e == cudaSuccess ? GB_OK : GB_ECUDA;
+    const int G = attn_grid_splits(n_kv, max_seq);
+    float* part = static_cast<float*>(ws);
+    unsigned* tickets = reinterpret_cast<unsigned*>(part + (size_t)n_kv * G * group * (head_dim + 2));
+    return attn_dispatch(q, k, v, k_cache, v_cache, rope_cs, d_pos, n_heads, n_kv, head_dim, max_seq, out, part,
+                         tickets, tickets + n_kv, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int gb_attention_decode_static(const float* q, const float* k, const float* v, float* k_cache,
+                                          float* v_cache, const float* rope_cs, const int* d_pos, int n_heads,
+                                          int n_kv, int head_dim, int max_seq, float* out, void* stream) {
+    if (!q || !k || !v || !k_cache || !v_cache || !rope_cs || !d_pos || !out) return GB_EINVAL;
+    if (n_kv <= 0 || n_heads <= 0 || n_heads % n_kv || max_seq <= 0) return GB_EINVAL;
+    if (n_kv >= GB_ATTN_STATIC_ERR_WORD) return GB_ELIMIT;
+    const int group = n_heads / n_kv;
+    const int G = attn_grid_splits(n_kv, max_seq);
+    const size_t part_bytes = (size_t)n_kv * G * group * (head_dim + 2) * sizeof(float);
+    if (part_bytes > GB_ATTN_STATIC_BYTES - GB_ATTN_STATIC_PART_OFFSET) return GB_ELIMIT;
+    int rc;
+    unsigned char* base = attn_static_scratch(&rc);
+    if (!base) return rc;
+    unsigned* words = reinterpret_cast<unsigned*>(base);
+    return attn_dispatch(q, k, v, k_cache, v_cache, rope_cs, d_pos, n_heads, n_kv, head_dim, max_seq, out,
+                         reinterpret_cast<float*>(base + GB_ATTN_STATIC_PART_OFFSET), words,
+                         words + GB_ATTN_STATIC_ERR_WORD, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int gb_attention_static_error(int clear) {
+    int rc;
+    unsigned char* base = attn_static_scratch(&rc);
+    if (!base) return rc;
+    unsigned* e = reinterpret_cast<unsigned*>(base) + GB_ATTN_STATIC_ERR_WORD;
+    unsigned v = 0;
+    if (cudaMemcpy(&v, e, sizeof(v), cudaMemcpyDeviceToHost) != cudaSuccess) return GB_ECUDA;
+    const unsigned z = 0;
+    if (clear && v && cudaMemcpy(e, &z, sizeof(z), cudaMemcpyHostToDevice) != cudaSuccess) return GB_ECUDA;
+    return -(int)v;
 }

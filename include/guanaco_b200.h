@@ -145,6 +145,25 @@ int gb_attention_decode(const float* q, const float* k, const float* v,
                         const int* d_pos, int n_heads, int n_kv, int head_dim, int max_seq,
                         float* out, void* ws, void* stream);
 
+/* gb_attention_decode without a caller workspace and without allocating:
+ * the split-K scratch is a file-scope device array of GB_ATTN_STATIC_BYTES
+ * (4 MiB), resolved with cudaGetSymbolAddress once per device.  Returns
+ * GB_ELIMIT when the configuration needs more (partials of n_kv * splits *
+ * (n_heads / n_kv) * (head_dim + 2) floats above 4 MiB - 4 KiB, or n_kv >= 1023).
+ * The scratch is shared by every call on the device: calls that overlap in
+ * time (other streams, other threads) race and must not be issued.  The first
+ * call on a device does the symbol lookup, so make it before any stream
+ * capture.  A position outside [0, max_seq) is reported through
+ * gb_attention_static_error (after synchronising the stream). */
+#define GB_ATTN_STATIC_BYTES (4u << 20)
+int gb_attention_decode_static(const float* q, const float* k, const float* v,
+                               float* k_cache, float* v_cache, const float* rope_cs,
+                               const int* d_pos, int n_heads, int n_kv, int head_dim, int max_seq,
+                               float* out, void* stream);
+/* The static variant's error word as a GB_E* code (0 if none); clear != 0
+ * resets it. */
+int gb_attention_static_error(int clear);
+
 /* out = w * (x * rsqrt(mean(x^2) + eps))  (kernels_cpu.c:199-265), one row of n. */
 int gb_rmsnorm(const float* x, const float* w, float* out, int n, float eps, void* stream);
 /* gate = silu(gate) * up  (kernels_cpu.c:312-341 + 367-389). */
