@@ -109,17 +109,28 @@ def kernel_benchmarks(gb, torch, dm, peak):
     sp = st.cuda_stream
     res = {}
 
-    def timed(launch, n_iter, warm=3):
+    def timed(launch, n_iter, warm=3, reps=3):
+        """Seconds per launch: n_iter launches captured in one CUDA graph on
+        the launching stream (as the decode step issues them, without host
+        overhead), replayed reps times between CUDA events on that stream."""
         for i in range(warm):
             launch(i)
         st.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st, capture_error_mode="relaxed"):
+            for i in range(n_iter):
+                launch(i)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(st)
-        for i in range(n_iter):
-            launch(i)
-        e1.record(st)
+        with torch.cuda.stream(st):   # replay() launches on the current stream
+            g.replay()
+            st.synchronize()
+            e0.record(st)
+            for _ in range(reps):
+                g.replay()
+            e1.record(st)
         e1.synchronize()
-        return e0.elapsed_time(e1) / n_iter * 1e-3   # seconds per launch
+        del g
+        return e0.elapsed_time(e1) / (n_iter * reps) * 1e-3
 
     def matvec_case(tag, dt, rows, cols, copies, n_iter):
         wbytes = gb.matrix_bytes(dt, rows, cols)
@@ -275,6 +286,11 @@ def run_ours(args, rank, world, local_rank):
         t_ms = float(tt.item())
     if dm.error() != 0:
         raise RuntimeError(f"decode error {dm.error()}")
+    if args.decode_only:   # profiling runs: the timed decode steps only
+        dm.close()
+        if rank == 0:
+            print(json.dumps({"decode_only": True, "ms_per_step": round(t_ms / K, 4)}), flush=True)
+        return None
     tokens = world * K
     value = tokens / (t_ms / 1e3)
     ms_per_step = t_ms / K
@@ -429,6 +445,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode-only", action="store_true",
+                    help="run the warm-up and timed decode steps only (for ncu launch lists) and exit")
     ap.add_argument("--steps-ref", type=int, default=None, help="reference arm samples (default min(steps, 5))")
     ap.add_argument("--kernel", choices=["q4k", "q6k", "q6k_head", "q8_0", "attn"], default=None,
                     help="run only a few launches of one kernel (for ncu captures) and exit")
