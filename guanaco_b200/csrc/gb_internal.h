@@ -33,8 +33,18 @@ size_t mv_ws_bytes(const MvPlan& p);
 // cross-CTA partials, less even for short matrices).  pdl: launch with
 // programmatic stream serialization, so the kernel's weight prefetch overlaps
 // the tail of the previous kernel on the stream.
+// Optional transform of x inside the matvec (TMA path only): RMSNorm
+// x * r * w (r = 1 / sqrt(mean(x^2) + eps), the reference's rounding), or
+// silu(x) * x2 (the SwiGLU product).
+enum { MV_X_NONE = 0, MV_X_RMSNORM = 1, MV_X_SILU_MUL = 2 };
+struct MvXform {
+    int mode = MV_X_NONE;
+    const float* w = nullptr;    // RMSNorm weight
+    const float* x2 = nullptr;   // the up projection for MV_X_SILU_MUL
+    float eps = 0.f;
+};
 int mv_launch(const MvPlan& p, const float* x, float* y, const float* residual, void* ws, cudaStream_t st,
-              bool pdl);
+              bool pdl, const MvXform* xf = nullptr);
 
 // Everything one decode layer needs; all pointers are device pointers.
 struct LayerArgs {

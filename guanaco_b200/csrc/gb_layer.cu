@@ -12,6 +12,8 @@
 #include "gb_common.cuh"
 #include "gb_internal.h"
 
+#include <algorithm>
+
 #include <math.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -55,6 +57,57 @@ __global__ void k_silu_mul(float* __restrict__ g, const float* __restrict__ u, i
     const float x = g[i];
     const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));
     g[i] = __fmul_rn(__fmul_rn(x, sig), u[i]);
+}
+
+// Multi-CTA argmax for long vectors (the output head): CTA c scans the
+// contiguous chunk [c n / G, (c + 1) n / G) and writes its (max, first index);
+// the last CTA to finish (ticket) merges the chunks in index order, so the
+// first maximum wins as in sample_greedy (tokenizer.c:175-185).
+struct ArgPart { float v; int i; };
+constexpr int AM_MAX_CTAS = GB_NUM_SMS;
+constexpr size_t AM_WS_BYTES = AM_MAX_CTAS * sizeof(ArgPart) + 16;
+__global__ void __launch_bounds__(1024) k_argmax_split(const float* __restrict__ x, int n, int* __restrict__ out,
+                                                       ArgPart* __restrict__ part, unsigned* __restrict__ ticket) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    __shared__ bool last;
+    const int G = gridDim.x, c = blockIdx.x;
+    const int lo = (int)((long long)c * n / G), hi = (int)((long long)(c + 1) * n / G);
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        const float v = x[i];
+        if (v > bv) { bv = v; bi = i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) { sv[warp] = bv; si[warp] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++)
+            if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) { bv = sv[w]; bi = si[w]; }
+        part[c].v = bv;
+        part[c].i = bi;
+        __threadfence();
+        last = atomicAdd(ticket, 1u) == (unsigned)(G - 1);
+    }
+    __syncthreads();
+    if (!last || threadIdx.x != 0) return;
+    __threadfence();
+    float mv = -INFINITY;
+    int mi = 0x7fffffff;
+    for (int k = 0; k < G; k++) {   // chunk order = index order: strict > keeps the first maximum
+        const float v = __ldcg(&part[k].v);
+        const int i = __ldcg(&part[k].i);
+        if (v > mv || (v == mv && i < mi)) { mv = v; mi = i; }
+    }
+    *out = mi == 0x7fffffff ? 0 : mi;
+    *ticket = 0u;
 }
 
 // First index of the maximum, strict > (ties keep the lower index).
@@ -205,6 +258,7 @@ struct gb_model {
     cudaGraphExec_t gen_exec = nullptr;   // step + advance, for gb_model_generate
     const void* gen_key[4] = {nullptr, nullptr, nullptr, nullptr};
     int* d_count = nullptr;
+    void* am_ws = nullptr;            // argmax partials + ticket (zeroed)
 };
 
 static void* dalloc(gb_model* m, size_t bytes) {
@@ -251,13 +305,15 @@ extern "C" gb_model* gb_model_create(const gb_model_config* cfg) {
     ok &= (m->d_pos = (int*)dalloc(m, 16)) != nullptr;
     ok &= (m->d_next = (int*)dalloc(m, 16)) != nullptr;
     ok &= (m->d_count = (int*)dalloc(m, 16)) != nullptr;
+    ok &= (m->am_ws = dalloc(m, AM_WS_BYTES)) != nullptr;
     ok &= cudaMallocHost(&m->h_io, 4 * sizeof(int)) == cudaSuccess;
     ok &= cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) == cudaSuccess;
     // zero in stream order, then wait: decode may run on any stream
     if (ok) ok &= cudaMemsetAsync(m->kc, 0, kv_elems * 4, m->stream) == cudaSuccess &&
                   cudaMemsetAsync(m->vc, 0, kv_elems * 4, m->stream) == cudaSuccess;
     if (ok) ok &= cudaMemsetAsync(m->attn_ws, 0, ws, m->stream) == cudaSuccess &&
-                  cudaMemsetAsync(m->err, 0, 16, m->stream) == cudaSuccess;
+                  cudaMemsetAsync(m->err, 0, 16, m->stream) == cudaSuccess &&
+                  cudaMemsetAsync(m->am_ws, 0, AM_WS_BYTES, m->stream) == cudaSuccess;
     if (ok) ok &= gb_rope_table(m->rope, c.max_seq, c.head_dim, c.rope_theta, m->stream) == GB_OK;
     if (ok) ok &= cudaStreamSynchronize(m->stream) == cudaSuccess;
     if (!ok) {
@@ -375,22 +431,44 @@ namespace gb {
 int enqueue_layer(const LayerArgs& a, cudaStream_t st) {
     const int H = a.H, F = a.ff;
     int rc;
-    auto mv = [&](int which, const float* x, float* y, const float* res) {
-        return mv_launch(*a.mv[which], x, y, res, a.mv_ws, st, true);
+    auto mv = [&](int which, const float* x, float* y, const float* res, const MvXform* xf) {
+        return mv_launch(*a.mv[which], x, y, res, a.mv_ws, st, true, xf);
     };
-    if ((rc = gb_rmsnorm(a.hidden, a.ra, a.xn, H, a.eps, st))) return rc;
-    if ((rc = mv(GB_WQ, a.xn, a.q, nullptr))) return rc;
-    if ((rc = mv(GB_WK, a.xn, a.k, nullptr))) return rc;
-    if ((rc = mv(GB_WV, a.xn, a.v, nullptr))) return rc;
+    auto tma = [&](int which) { return a.mv[which]->kind == MV_TMA; };
+    // RMSNorm and the SwiGLU product run inside the consuming matvecs' x
+    // quantiser when those are on the TMA path (no separate launches)
+    MvXform att, ffn, swi;
+    att.mode = ffn.mode = MV_X_RMSNORM;
+    att.w = a.ra;
+    ffn.w = a.rf;
+    att.eps = ffn.eps = a.eps;
+    swi.mode = MV_X_SILU_MUL;
+    swi.x2 = a.up;
+    if (tma(GB_WQ) && tma(GB_WK) && tma(GB_WV)) {
+        if ((rc = mv(GB_WQ, a.hidden, a.q, nullptr, &att))) return rc;
+        if ((rc = mv(GB_WK, a.hidden, a.k, nullptr, &att))) return rc;
+        if ((rc = mv(GB_WV, a.hidden, a.v, nullptr, &att))) return rc;
+    } else {
+        if ((rc = gb_rmsnorm(a.hidden, a.ra, a.xn, H, a.eps, st))) return rc;
+        if ((rc = mv(GB_WQ, a.xn, a.q, nullptr, nullptr))) return rc;
+        if ((rc = mv(GB_WK, a.xn, a.k, nullptr, nullptr))) return rc;
+        if ((rc = mv(GB_WV, a.xn, a.v, nullptr, nullptr))) return rc;
+    }
     if ((rc = gb_attention_decode(a.q, a.k, a.v, a.kc, a.vc, a.rope, a.d_pos, a.n_heads, a.n_kv, a.hd, a.max_seq,
                                   a.attn, a.attn_ws, st)))
         return rc;
-    if ((rc = mv(GB_WO, a.attn, a.hidden, a.hidden))) return rc;
-    if ((rc = gb_rmsnorm(a.hidden, a.rf, a.xn, H, a.eps, st))) return rc;
-    if ((rc = mv(GB_WGATE, a.xn, a.gate, nullptr))) return rc;
-    if ((rc = mv(GB_WUP, a.xn, a.up, nullptr))) return rc;
+    if ((rc = mv(GB_WO, a.attn, a.hidden, a.hidden, nullptr))) return rc;
+    if (tma(GB_WGATE) && tma(GB_WUP)) {
+        if ((rc = mv(GB_WGATE, a.hidden, a.gate, nullptr, &ffn))) return rc;
+        if ((rc = mv(GB_WUP, a.hidden, a.up, nullptr, &ffn))) return rc;
+    } else {
+        if ((rc = gb_rmsnorm(a.hidden, a.rf, a.xn, H, a.eps, st))) return rc;
+        if ((rc = mv(GB_WGATE, a.xn, a.gate, nullptr, nullptr))) return rc;
+        if ((rc = mv(GB_WUP, a.xn, a.up, nullptr, nullptr))) return rc;
+    }
+    if (tma(GB_WDOWN)) return mv(GB_WDOWN, a.gate, a.hidden, a.hidden, &swi);
     if ((rc = gb_silu_mul(a.gate, a.up, F, st))) return rc;
-    return mv(GB_WDOWN, a.gate, a.hidden, a.hidden);
+    return mv(GB_WDOWN, a.gate, a.hidden, a.hidden, nullptr);
 }
 
 int embed(const void* emb, int dtype, const int* d_token, int vocab, int H, float* out, unsigned* err, cudaStream_t st) {
@@ -423,10 +501,22 @@ static int enqueue_step(gb_model* m, const int* d_token, const int* d_pos, float
         a.max_seq = c.max_seq; a.eps = c.rms_eps;
         if ((rc = enqueue_layer(a, st))) return rc;
     }
-    if ((rc = gb_rmsnorm(m->hidden, m->rms_final, m->xn, H, c.rms_eps, st))) return rc;
     float* lg = d_logits ? d_logits : m->logits;
-    if ((rc = mv_launch(m->lm_plan, m->xn, lg, nullptr, m->mv_ws, st, true))) return rc;
-    return gb_argmax(lg, c.vocab_size, d_next, st);
+    if (m->lm_plan.kind == MV_TMA) {   // final RMSNorm inside the output-head matvec
+        MvXform fin;
+        fin.mode = MV_X_RMSNORM;
+        fin.w = m->rms_final;
+        fin.eps = c.rms_eps;
+        if ((rc = mv_launch(m->lm_plan, m->hidden, lg, nullptr, m->mv_ws, st, true, &fin))) return rc;
+    } else {
+        if ((rc = gb_rmsnorm(m->hidden, m->rms_final, m->xn, H, c.rms_eps, st))) return rc;
+        if ((rc = mv_launch(m->lm_plan, m->xn, lg, nullptr, m->mv_ws, st, true))) return rc;
+    }
+    const int G = std::min(AM_MAX_CTAS, (c.vocab_size + 4095) / 4096);
+    ArgPart* part = static_cast<ArgPart*>(m->am_ws);
+    k_argmax_split<<<G, 1024, 0, st>>>(lg, c.vocab_size, d_next, part,
+                                       reinterpret_cast<unsigned*>(part + AM_MAX_CTAS));
+    return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
 }
 
 // All weights set, and the shared matvec workspace sized for every plan.
@@ -540,8 +630,20 @@ extern "C" int gb_model_fill_kv(gb_model* m, int n_pos, uint64_t seed) {
 }
 
 extern "C" int gb_model_launches_per_step(const gb_model* m) {
-    // embed + per layer (2 rmsnorm, 7 matvec, attention, silu_mul) + rmsnorm, lm_head, argmax
-    return m ? 1 + m->c.n_layers * 11 + 3 : 0;
+    // embed + per layer (7 matvecs, attention, and the RMSNorm / SwiGLU
+    // kernels that are not fused into a TMA matvec) + output head (+ final
+    // norm when not fused) + argmax
+    if (!m) return 0;
+    int n = 1;
+    for (int l = 0; l < m->c.n_layers; l++) {
+        auto tma = [&](int w) { return m->plan[(size_t)l * GB_NMAT + w].kind == MV_TMA; };
+        n += 8;
+        n += (tma(GB_WQ) && tma(GB_WK) && tma(GB_WV)) ? 0 : 1;
+        n += (tma(GB_WGATE) && tma(GB_WUP)) ? 0 : 1;
+        n += tma(GB_WDOWN) ? 0 : 1;
+    }
+    n += m->lm_plan.kind == MV_TMA ? 1 : 2;
+    return n + 1;
 }
 
 extern "C" int gb_model_decode_host(gb_model* m, int token, int pos, int* h_next, float* h_logits) {

@@ -691,6 +691,12 @@ struct MtArgs {
     unsigned* tickets;  // [ngroups], zero between launches
     int rows, nb, nch, T, ncta, S;
     int unit;           // split granularity in stage items: 1, or nch (whole groups, no workspace)
+    // x transform applied while quantising (MV_X_*): RMSNorm with weight nw
+    // and eps, or silu(x) * x2
+    int xmode;
+    const float* nw;
+    const float* x2;
+    float eps;
 };
 
 // x in shared memory (K = 256 nb columns):
@@ -702,14 +708,48 @@ struct MtArgs {
 __host__ __device__ constexpr int mt_xq_bytes(int K, bool s16) { return 2 * K + K / 4 + (s16 ? K / 4 : 0); }
 constexpr int MT_ZERO = 256;   // zero line read by lanes without a B fragment
 
+// RMSNorm scale 1 / sqrt(mean(x^2) + eps) over the K columns, summed by the
+// consumer threads and combined in fixed warp order (every CTA gets the
+// same value).  scratch: NC floats of shared memory.
+template <int NC>
+__device__ __forceinline__ float mt_rms_scale(const float* __restrict__ x, int K, float eps, float* scratch, int tid) {
+    float ss = 0.f;
+    for (int t = tid; t < K / 4; t += NC * 32) {
+        const float4 v = reinterpret_cast<const float4*>(x)[t];
+        ss = fmaf(v.x, v.x, ss);
+        ss = fmaf(v.y, v.y, ss);
+        ss = fmaf(v.z, v.z, ss);
+        ss = fmaf(v.w, v.w, ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((tid & 31) == 0) scratch[tid >> 5] = ss;
+    mt_consumer_sync<NC>();
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < NC; w++) tot += scratch[w];
+    return __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)K), eps)));
+}
+__device__ __forceinline__ float mt_silu_mul(float g, float u) {
+    return __fmul_rn(__fmul_rn(g, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)))), u);
+}
+
 template <bool S16>
-__device__ __forceinline__ void mt_quantise_x(const float* __restrict__ x, int K, uint8_t* xq, int tid, int nthr) {
+__device__ __forceinline__ void mt_quantise_x(const MtArgs& a, int K, uint8_t* xq, int tid, int nthr, float rs) {
     uint32_t* p0 = reinterpret_cast<uint32_t*>(xq);
     uint32_t* p1 = reinterpret_cast<uint32_t*>(xq + K);
     float* f = reinterpret_cast<float*>(xq + 2 * K);
     float* f16 = f + K / 16;
     for (int t = tid; t < K / 4; t += nthr) {   // 8 lanes (32 columns) per sub-block
-        const float4 v = reinterpret_cast<const float4*>(x)[t];
+        float4 v = reinterpret_cast<const float4*>(a.x)[t];
+        if (a.xmode == MV_X_RMSNORM) {   // w * (x * r), the reference's rounding
+            const float4 w = reinterpret_cast<const float4*>(a.nw)[t];
+            v = make_float4(__fmul_rn(w.x, __fmul_rn(v.x, rs)), __fmul_rn(w.y, __fmul_rn(v.y, rs)),
+                            __fmul_rn(w.z, __fmul_rn(v.z, rs)), __fmul_rn(w.w, __fmul_rn(v.w, rs)));
+        } else if (a.xmode == MV_X_SILU_MUL) {
+            const float4 u = reinterpret_cast<const float4*>(a.x2)[t];
+            v = make_float4(mt_silu_mul(v.x, u.x), mt_silu_mul(v.y, u.y), mt_silu_mul(v.z, u.z), mt_silu_mul(v.w, u.w));
+        }
         float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
         float sm = (v.x + v.y) + (v.z + v.w);
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
@@ -1010,7 +1050,8 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
     // ---- consumers
     griddep_wait();
     uint8_t* xq = smem + xq_off;
-    mt_quantise_x<F::S16>(a.x, K, xq, threadIdx.x, MT_NC * 32);
+    const float rs = a.xmode == MV_X_RMSNORM ? mt_rms_scale<MT_NC>(a.x, K, a.eps, red, threadIdx.x) : 1.f;
+    mt_quantise_x<F::S16>(a, K, xq, threadIdx.x, MT_NC * 32, rs);
     mt_consumer_sync<MT_NC>();
     MtLane L;
     L.gq = lane >> 2;
@@ -1237,9 +1278,16 @@ size_t mv_ws_bytes(const MvPlan& p) {
     return (size_t)GB_NUM_SMS * 2 * MT_GR * sizeof(float) + ((size_t)p.ngroups * sizeof(unsigned) + 255) / 256 * 256;
 }
 
-int mv_launch(const MvPlan& p, const float* x, float* y, const float* residual, void* ws, cudaStream_t st, bool pdl) {
+int mv_launch(const MvPlan& p, const float* x, float* y, const float* residual, void* ws, cudaStream_t st, bool pdl,
+              const MvXform* xf) {
     if (!x || !y) return GB_EINVAL;
     if (reinterpret_cast<uintptr_t>(x) & 15) return GB_EINVAL;
+    const int xmode = xf ? xf->mode : MV_X_NONE;
+    if (xmode != MV_X_NONE) {   // transforms run in the TMA kernels' x quantiser only
+        if (p.kind != MV_TMA) return GB_EINVAL;
+        const float* other = xmode == MV_X_RMSNORM ? xf->w : xf->x2;
+        if (!other || (reinterpret_cast<uintptr_t>(other) & 15)) return GB_EINVAL;
+    }
     if (p.kind == MV_RING) {
         MvGeom g;
         if (!choose_geom(p.dtype, p.rows, p.nb, &g)) return GB_ELIMIT;
@@ -1271,6 +1319,10 @@ int mv_launch(const MvPlan& p, const float* x, float* y, const float* residual, 
     a.nb = p.nb;
     a.nch = p.nch;
     a.T = p.T;
+    a.xmode = xmode;
+    a.nw = xmode == MV_X_RMSNORM ? xf->w : nullptr;
+    a.x2 = xmode == MV_X_SILU_MUL ? xf->x2 : nullptr;
+    a.eps = xf ? xf->eps : 0.f;
     // with a workspace: stream-K over stage items; without: whole groups per CTA
     a.unit = ws ? 1 : p.nch;
     a.ncta = ws ? p.ncta : (p.ngroups < GB_NUM_SMS ? p.ngroups : GB_NUM_SMS);
@@ -1337,7 +1389,7 @@ extern "C" int gb_matvec(int dtype, const void* W, int rows, int cols, const flo
     if (rc) return rc;
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     void* ws = p.kind == MV_TMA ? stream_workspace(st, mv_ws_bytes(p)) : nullptr;
-    return mv_launch(p, x, y, residual, ws, st, false);
+    return mv_launch(p, x, y, residual, ws, st, false, nullptr);
 }
 
 extern "C" int gb_device_error(int clear) {

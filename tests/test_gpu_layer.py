@@ -23,6 +23,9 @@ def layer_weights(oracle, H, nh, nkv, hd, ff, seed, dtypes=(4, 4, 5, 4, 4, 4, 5)
     (512, 4, 2, 1024, (4, 4, 5, 4, 4, 4, 5)),
     (512, 8, 2, 1536, (4, 4, 4, 4, 4, 4, 4)),
     (1024, 8, 8, 768, (2, 2, 2, 2, 2, 2, 2)),
+    # every matrix on the TMA path (Q6_K rows of 8-block multiples): RMSNorm and
+    # the SwiGLU product run inside the matvecs
+    (2048, 16, 4, 4096, (4, 4, 5, 4, 4, 4, 5)),
 ])
 def test_dropin_layer_sequence(gb, oracle, cuda, H, nh, nkv, ff, dtypes):
     hd = H // nh
@@ -152,5 +155,20 @@ def test_model_synthesized_decode_runs(gb, cuda):
         dm2.close()
         with pytest.raises(gb.GBError):
             dm.decode_host(1, 128)
+    finally:
+        dm.close()
+
+
+@pytest.mark.parametrize("vocab", [20000, 4096 * 3 + 5])
+def test_model_argmax_split_first_maximum(gb, cuda, vocab):
+    """The output head's argmax runs split over several CTAs for long
+    vocabularies; the next token is the first index of the maximum logit."""
+    dm = gb.DecodeModel(256, 4, 2, 1, 512, vocab, 32)
+    try:
+        dm.synthesize(77)
+        for pos in range(3):
+            logits = np.zeros(vocab, np.float32)
+            nxt = dm.decode_host(5 + pos, pos, logits=logits)
+            assert nxt == int(np.argmax(logits))
     finally:
         dm.close()
