@@ -48,7 +48,11 @@ struct Ctx {
     void* ws = nullptr;
     size_t ws_bytes = 0;
     std::vector<LayerKV> kv;
-    std::unordered_map<const void*, void*> norm_cache;
+    struct CachedNorm {
+        float* d = nullptr;
+        std::vector<float> host;   // the uploaded values (a reused host address must match them)
+    };
+    std::unordered_map<const void*, CachedNorm> norm_cache;
     struct CachedWeight {
         void* d = nullptr;
         size_t bytes = 0;
@@ -152,14 +156,29 @@ static int upload_kv(Ctx* c, LayerKV* L, const float* hk, const float* hv, int s
     return GB_OK;
 }
 
+// Norm weights are small (H floats): a cached device copy is reused only when
+// the host values are identical, so a host buffer freed and reallocated at
+// the same address (or resized) is uploaded again.
 static const float* cached_norm(Ctx* c, const float* h, int n) {
-    auto it = c->norm_cache.find(h);
-    if (it != c->norm_cache.end()) return static_cast<const float*>(it->second);
+    const size_t bytes = (size_t)n * sizeof(float);
+    Ctx::CachedNorm& e = c->norm_cache[h];
+    if (e.d && e.host.size() == (size_t)n && memcmp(e.host.data(), h, bytes) == 0) return e.d;
+    if (e.d) {   // kernels still queued may read the old copy
+        cudaStreamSynchronize(c->st);
+        cudaFree(e.d);
+        e.d = nullptr;
+    }
+    e.host.assign(h, h + n);
     void* d = nullptr;
-    if (cudaMalloc(&d, (size_t)n * sizeof(float)) != cudaSuccess) return nullptr;
-    if (cudaMemcpy(d, h, (size_t)n * sizeof(float), cudaMemcpyHostToDevice) != cudaSuccess) { cudaFree(d); return nullptr; }
-    c->norm_cache[h] = d;
-    return static_cast<const float*>(d);
+    if (cudaMalloc(&d, bytes) != cudaSuccess ||
+        cudaMemcpyAsync(d, e.host.data(), bytes, cudaMemcpyHostToDevice, c->st) != cudaSuccess ||
+        cudaStreamSynchronize(c->st) != cudaSuccess) {
+        if (d) cudaFree(d);
+        c->norm_cache.erase(h);
+        return nullptr;
+    }
+    e.d = static_cast<float*>(d);
+    return e.d;
 }
 
 // Upload `size` bytes through a pinned bounce buffer: the CPU reads the

@@ -54,8 +54,51 @@ struct AttnCfg {
     static constexpr int RED = 8 * RPW * GROUP * HD;  // pass-3 reduction floats
     static constexpr int SF = ATTN_MAX_P * 8;         // score buffer floats
     static_assert(RED <= SF, "reduction buffer aliases the score buffer");
-    static constexpr size_t SMEM = (size_t)(GROUP * HD + 2 * HD + SF + 16) * sizeof(float);
+    static constexpr int TP = 32;                     // positions per K / V tile
+    static constexpr int R = 4;                       // tiles in flight per CTA
+    static constexpr int TILE = TP * HD;              // floats per tile
+    static constexpr size_t RING_OFF = ((size_t)(GROUP * HD + 2 * HD + SF + 16) * sizeof(float) + 127) / 128 * 128;
+    static constexpr size_t BAR_OFF = RING_OFF + (size_t)R * TILE * sizeof(float);
+    static constexpr size_t SMEM = BAR_OFF + R * sizeof(unsigned long long);
 };
+
+// ---- bulk-copy ring primitives (shared-memory addresses)
+__device__ __forceinline__ uint32_t a_sptr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void a_bar_init(uint32_t b, uint32_t n) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(b), "r"(n) : "memory");
+}
+__device__ __forceinline__ void a_bar_expect(uint32_t b, uint32_t tx) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(b), "r"(tx) : "memory");
+}
+__device__ __forceinline__ bool a_bar_test(uint32_t b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(b), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t a_gtimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait (2 s); false on timeout (the caller records GB_ETIMEOUT).
+__device__ __noinline__ bool a_bar_wait_slow(uint32_t b, uint32_t parity) {
+    const uint64_t t0 = a_gtimer();
+    while (!a_bar_test(b, parity))
+        if (a_gtimer() - t0 > 2000000000ull) return false;
+    return true;
+}
+__device__ __forceinline__ bool a_bar_wait(uint32_t b, uint32_t parity) {
+    return a_bar_test(b, parity) || a_bar_wait_slow(b, parity);
+}
+__device__ __forceinline__ void a_bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
 
 template <int HD, int GROUP>
 __global__ void __launch_bounds__(ATTN_THREADS)
@@ -108,6 +151,40 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
         }
     }
 
+    // ---- K / V tiles stream through a ring of R bulk copies: item i < T is K
+    // tile i, item T + i is V tile i; item i lands in stage i % R.  Thread 0
+    // issues item i + R once every thread is done with item i (the
+    // __syncthreads after each tile).  The row of the new position is read
+    // from kn / vn, never from the tile (the copy may precede the append).
+    unsigned char* smb = reinterpret_cast<unsigned char*>(sm);
+    float* ring = reinterpret_cast<float*>(smb + C::RING_OFF);
+    const uint32_t bars = a_sptr(smb + C::BAR_OFF);
+    const int T = (n + C::TP - 1) / C::TP;
+    auto issue = [&](int it) {
+        const bool isv = it >= T;
+        const int t = isv ? it - T : it;
+        const int rows = min(C::TP, n - t * C::TP);
+        const float* src = (isv ? vc : kc) + head_base + (size_t)(s0 + t * C::TP) * HD;
+        const uint32_t bar = bars + 8 * (it % C::R);
+        a_bar_expect(bar, rows * HD * 4);
+        a_bulk_g2s(a_sptr(ring + (it % C::R) * C::TILE), src, rows * HD * 4, bar);
+    };
+    if (tid == 0) {
+        for (int r = 0; r < C::R; r++) a_bar_init(bars + 8 * r, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int it = 0; it < C::R && it < 2 * T; it++) issue(it);
+    }
+    __syncthreads();
+    bool ok = true;
+    // every issued copy is waited on (bounded), so no copy is still landing
+    // in this CTA's shared memory when it exits, even after a timeout
+    auto wait_item = [&](int it) {
+        if (!a_bar_wait(bars + 8 * (it % C::R), (it / C::R) & 1) && ok) {
+            ok = false;
+            atomicExch(err, (unsigned)(-GB_ETIMEOUT));
+        }
+    };
+
     // ---- pass 1: scores
     const float scale = 1.0f / sqrtf((float)HD);
     {
@@ -120,36 +197,41 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
                 const float4 v = *reinterpret_cast<const float4*>(qs + h * HD + j * C::LPP * 4 + lp * 4);
                 qr[h][4 * j] = v.x; qr[h][4 * j + 1] = v.y; qr[h][4 * j + 2] = v.z; qr[h][4 * j + 3] = v.w;
             }
-        for (int base = warp * C::PPW; base < n; base += 8 * C::PPW) {
-            const int s = base + pw;
-            const int gs = s0 + (s < n ? s : 0);
-            float4 kr[C::DPL / 4];
-            const float* krow = (gs == pos) ? kn : kc + head_base + (size_t)gs * HD;
+        for (int t = 0; t < T; t++) {
+            wait_item(t);
+            const float* tile = ring + (t % C::R) * C::TILE;
+            const int nt = min(C::TP, n - t * C::TP);
+            for (int base = warp * C::PPW; base < nt; base += 8 * C::PPW) {
+                const int r = base + pw;
+                const int rr = r < nt ? r : 0;
+                const int s = t * C::TP + rr;
+                const float* krow = (s0 + s == pos) ? kn : tile + rr * HD;
+                float4 kr[C::DPL / 4];
 #pragma unroll
-            for (int j = 0; j < C::DPL / 4; j++) {
-                const float* p = krow + j * C::LPP * 4 + lp * 4;
-                kr[j] = (gs == pos) ? *reinterpret_cast<const float4*>(p) : __ldg(reinterpret_cast<const float4*>(p));
-            }
-            float dots[GROUP];
+                for (int j = 0; j < C::DPL / 4; j++) kr[j] = *reinterpret_cast<const float4*>(krow + j * C::LPP * 4 + lp * 4);
+                float dots[GROUP];
 #pragma unroll
-            for (int h = 0; h < GROUP; h++) {
-                float2 a = make_float2(0.f, 0.f);
+                for (int h = 0; h < GROUP; h++) {
+                    float2 acc2 = make_float2(0.f, 0.f);
 #pragma unroll
-                for (int j = 0; j < C::DPL / 4; j++) {
-                    a = ffma2(make_float2(qr[h][4 * j], qr[h][4 * j + 1]), make_float2(kr[j].x, kr[j].y), a);
-                    a = ffma2(make_float2(qr[h][4 * j + 2], qr[h][4 * j + 3]), make_float2(kr[j].z, kr[j].w), a);
+                    for (int j = 0; j < C::DPL / 4; j++) {
+                        acc2 = ffma2(make_float2(qr[h][4 * j], qr[h][4 * j + 1]), make_float2(kr[j].x, kr[j].y), acc2);
+                        acc2 = ffma2(make_float2(qr[h][4 * j + 2], qr[h][4 * j + 3]), make_float2(kr[j].z, kr[j].w), acc2);
+                    }
+                    float d = acc2.x + acc2.y;
+#pragma unroll
+                    for (int o = C::LPP / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+                    dots[h] = d;
                 }
-                float d = a.x + a.y;
+                if (r < nt && lp < GROUP) {
+                    float v = dots[0];
 #pragma unroll
-                for (int o = C::LPP / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-                dots[h] = d;
+                    for (int h = 1; h < GROUP; h++) if (lp == h) v = dots[h];
+                    S[s * 8 + lp] = __fmul_rn(v, scale);
+                }
             }
-            if (s < n && lp < GROUP) {
-                float v = dots[0];
-#pragma unroll
-                for (int h = 1; h < GROUP; h++) if (lp == h) v = dots[h];
-                S[s * 8 + lp] = __fmul_rn(v, scale);
-            }
+            __syncthreads();
+            if (tid == 0 && t + C::R < 2 * T) issue(t + C::R);
         }
     }
     __syncthreads();
@@ -176,23 +258,31 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
 #pragma unroll
     for (int h = 0; h < GROUP; h++) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
     const int vl = lane % C::VL, vr = lane / C::VL;
-    for (int s = warp * C::RPW + vr; s < n; s += 8 * C::RPW) {
-        const int gs = s0 + s;
-        const float4 vv = (gs == pos) ? *reinterpret_cast<const float4*>(vn + vl * 4)
-                                      : __ldg(reinterpret_cast<const float4*>(vc + head_base + (size_t)gs * HD + vl * 4));
-        float p[8];
-        const float4 p0 = *reinterpret_cast<const float4*>(S + s * 8);
-        p[0] = p0.x; p[1] = p0.y; p[2] = p0.z; p[3] = p0.w;
-        if (GROUP > 4) {
-            const float4 p1 = *reinterpret_cast<const float4*>(S + s * 8 + 4);
-            p[4] = p1.x; p[5] = p1.y; p[6] = p1.z; p[7] = p1.w;
-        }
+    for (int t = 0; t < T; t++) {
+        const int it = T + t;
+        wait_item(it);
+        const float* tile = ring + (it % C::R) * C::TILE;
+        const int nt = min(C::TP, n - t * C::TP);
+        for (int r = warp * C::RPW + vr; r < nt; r += 8 * C::RPW) {
+            const int s = t * C::TP + r;
+            const float4 vv = (s0 + s == pos) ? *reinterpret_cast<const float4*>(vn + vl * 4)
+                                              : *reinterpret_cast<const float4*>(tile + r * HD + vl * 4);
+            float p[8];
+            const float4 p0 = *reinterpret_cast<const float4*>(S + s * 8);
+            p[0] = p0.x; p[1] = p0.y; p[2] = p0.z; p[3] = p0.w;
+            if (GROUP > 4) {
+                const float4 p1 = *reinterpret_cast<const float4*>(S + s * 8 + 4);
+                p[4] = p1.x; p[5] = p1.y; p[6] = p1.z; p[7] = p1.w;
+            }
 #pragma unroll
-        for (int h = 0; h < GROUP; h++) {
-            float2 lo = ffma2(make_float2(p[h], p[h]), make_float2(vv.x, vv.y), make_float2(acc[h].x, acc[h].y));
-            float2 hi = ffma2(make_float2(p[h], p[h]), make_float2(vv.z, vv.w), make_float2(acc[h].z, acc[h].w));
-            acc[h] = make_float4(lo.x, lo.y, hi.x, hi.y);
+            for (int h = 0; h < GROUP; h++) {
+                float2 lo = ffma2(make_float2(p[h], p[h]), make_float2(vv.x, vv.y), make_float2(acc[h].x, acc[h].y));
+                float2 hi = ffma2(make_float2(p[h], p[h]), make_float2(vv.z, vv.w), make_float2(acc[h].z, acc[h].w));
+                acc[h] = make_float4(lo.x, lo.y, hi.x, hi.y);
+            }
         }
+        __syncthreads();
+        if (tid == 0 && it + C::R < 2 * T) issue(it + C::R);
     }
     __syncthreads();   // S is dead from here on; reuse it as the reduction buffer
     float* red = S;

@@ -36,6 +36,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
 #include <map>
 #include <mutex>
 
@@ -1278,6 +1279,16 @@ size_t mv_ws_bytes(const MvPlan& p) {
     return (size_t)GB_NUM_SMS * 2 * MT_GR * sizeof(float) + ((size_t)p.ngroups * sizeof(unsigned) + 255) / 256 * 256;
 }
 
+// GB_DISABLE_PDL=1 in the environment turns programmatic dependent launch off
+// (every matvec then waits for the previous kernel to finish before starting).
+static bool pdl_allowed() {
+    static const bool ok = [] {
+        const char* e = getenv("GB_DISABLE_PDL");
+        return !(e && e[0] && e[0] != '0');
+    }();
+    return ok;
+}
+
 int mv_launch(const MvPlan& p, const float* x, float* y, const float* residual, void* ws, cudaStream_t st, bool pdl,
               const MvXform* xf) {
     if (!x || !y) return GB_EINVAL;
@@ -1336,7 +1347,7 @@ int mv_launch(const MvPlan& p, const float* x, float* y, const float* residual, 
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
+    cfg.numAttrs = (pdl && pdl_allowed()) ? 1 : 0;
     const CUtensorMap* m = reinterpret_cast<const CUtensorMap*>(p.tmap);
     if (q6)
         GB_CUDA_TRY(cudaLaunchKernelEx(&cfg, k_mvt<MtQ6K>, *m, a));

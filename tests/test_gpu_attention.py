@@ -28,6 +28,7 @@ CASES = [
     (8, 2, 128, 80, 0), (8, 2, 128, 80, 1), (8, 2, 128, 80, 31), (8, 2, 128, 80, 32), (8, 2, 128, 80, 79),
     (8, 8, 128, 64, 40), (16, 2, 128, 300, 257), (32, 4, 64, 300, 200), (8, 1, 64, 40, 0),
     (16, 2, 64, 130, 129), (4, 4, 64, 700, 650), (32, 8, 128, 2100, 2049),
+    (8, 2, 64, 40, 9), (8, 2, 64, 40, 13), (16, 4, 64, 600, 333), (4, 2, 128, 100, 70),
 ]
 
 

@@ -172,3 +172,29 @@ def test_model_argmax_split_first_maximum(gb, cuda, vocab):
             assert nxt == int(np.argmax(logits))
     finally:
         dm.close()
+
+
+def test_dropin_norm_cache_follows_host_values(gb, oracle, cuda):
+    """Norm weights are cached by host pointer: new values at the same address
+    (a freed and reallocated host buffer) must be used, not the old copy."""
+    H, nh, nkv, ff, ms, layer = 512, 8, 2, 1536, 40, 11
+    hd = H // nh
+    ws, dts, shapes, ra, rf = layer_weights(oracle, H, nh, nkv, hd, ff, 5, (4, 4, 4, 4, 4, 4, 4))
+    L = gb.lib()
+    dptr = [L.cuda_upload_weight(w.ctypes.data, w.nbytes) for w in ws]
+    kc = np.zeros(nkv * ms * hd, np.float32)
+    vc = np.zeros(nkv * ms * hd, np.float32)
+    args = []
+    for d, (r, c), dt in zip(dptr, shapes, dts):
+        args += [d, r, c, dt]
+    for trial in range(2):
+        if trial == 1:   # same arrays, new values
+            ra[:] = (1.0 + 0.05 * oracle.synth_normal(H, 6, 30)).astype(np.float32)
+            rf[:] = (1.0 + 0.05 * oracle.synth_normal(H, 6, 31)).astype(np.float32)
+        h = oracle.synth_normal(H, 5, 3)
+        kc_ref, vc_ref = kc.copy(), vc.copy()
+        h_ref, _, _ = oracle.layer_decode(ws, dts, shapes, ra, rf, h.copy(), kc_ref, vc_ref, H, nh, nkv, hd, ff, ms, 0)
+        assert L.cuda_transformer_layer_gpu(*args, ra.ctypes.data, rf.ctypes.data, h.ctypes.data, kc.ctypes.data,
+                                            vc.ctypes.data, ms * hd, H, nh, nkv, hd, 0, layer, ms) == 0
+        L.cuda_finish_layer()
+        assert rel_l2(h, h_ref) <= REL_L2_TOL, trial
