@@ -110,6 +110,10 @@ SIGNATURES = {
     "gb_silu_mul": (_i, [_vp, _vp, _i, _vp]),
     "gb_argmax": (_i, [_vp, _i, _vp, _vp]),
     "gb_model_create": (_vp, [C.POINTER(ModelConfig)]),
+    "gb_model_create_tp": (_vp, [C.POINTER(ModelConfig), _i, _i]),
+    "gb_model_comm_handle": (_i, [_vp, _vp]),
+    "gb_model_comm_open": (_i, [_vp, _vp]),
+    "gb_model_tp_info": (_i, [_vp, _vp, _vp, _vp, _vp]),
     "gb_model_destroy": (None, [_vp]),
     "gb_model_set_matrix": (_i, [_vp, _i, _i, _i, _vp]),
     "gb_model_set_norms": (_i, [_vp, _i, _vp, _vp]),
@@ -220,16 +224,48 @@ def matrix_bytes(dtype, rows, cols) -> int:
     return rows * (cols // BLOCK_WIDTH[dtype]) * BLOCK_BYTES[dtype]
 
 
+IPC_HANDLE_BYTES = 64
+
+
 class DecodeModel:
-    """Device-resident decode model (forward() at T = 1, greedy)."""
+    """Device-resident decode model (forward() at T = 1, greedy).  With
+    tp_world > 1 this is rank tp_rank's tensor-parallel slice; call
+    exchange_handles() (or comm_handle / comm_open) on every rank before
+    decoding, and drive every rank through the same decode calls."""
 
     def __init__(self, hidden_dim, n_heads, n_kv_heads, n_layers, ff_dim, vocab_size, max_seq,
-                 rms_eps=1e-6, rope_theta=500000.0):
+                 rms_eps=1e-6, rope_theta=500000.0, tp_rank=0, tp_world=1):
         self.cfg = ModelConfig(hidden_dim, n_heads, n_kv_heads, hidden_dim // n_heads, n_layers, ff_dim,
                                vocab_size, max_seq, rms_eps, rope_theta)
-        self.h = lib().gb_model_create(C.byref(self.cfg))
+        self.tp_rank, self.tp_world = tp_rank, tp_world
+        self.h = lib().gb_model_create_tp(C.byref(self.cfg), tp_rank, tp_world)
         if not self.h:
-            raise GBError("gb_model_create", GB_ENOMEM)
+            raise GBError("gb_model_create_tp", GB_EINVAL)
+
+    def comm_handle(self) -> bytes:
+        buf = C.create_string_buffer(IPC_HANDLE_BYTES)
+        check("gb_model_comm_handle", lib().gb_model_comm_handle(self.h, buf))
+        return buf.raw
+
+    def comm_open(self, handles) -> None:
+        """handles: the world ranks' comm_handle() bytes, in rank order."""
+        blob = b"".join(handles)
+        if len(blob) != IPC_HANDLE_BYTES * self.tp_world:
+            raise GBError("gb_model_comm_open", GB_EINVAL)
+        buf = C.create_string_buffer(blob, len(blob))
+        check("gb_model_comm_open", lib().gb_model_comm_open(self.h, buf))
+
+    def exchange_handles(self, dist, group=None) -> None:
+        """All-gather the ranks' handles with torch.distributed (any backend)
+        and open the peers' exchange buffers."""
+        out = [None] * self.tp_world
+        dist.all_gather_object(out, self.comm_handle(), group=group)
+        self.comm_open(out)
+
+    def tp_info(self):
+        r, w, off, n = C.c_int(), C.c_int(), C.c_int(), C.c_int()
+        check("gb_model_tp_info", lib().gb_model_tp_info(self.h, C.byref(r), C.byref(w), C.byref(off), C.byref(n)))
+        return r.value, w.value, off.value, n.value
 
     def synthesize(self, seed: int) -> None:
         check("gb_model_synthesize", lib().gb_model_synthesize(self.h, seed))

@@ -46,8 +46,23 @@ struct MvXform {
 int mv_launch(const MvPlan& p, const float* x, float* y, const float* residual, void* ws, cudaStream_t st,
               bool pdl, const MvXform* xf = nullptr);
 
+// Tensor-parallel context of a layer (world > 1): the wo and ffn_down
+// matvecs write this rank's partial to `part`, then an all-reduce over peer
+// memory adds every rank's partial to the hidden state.
+struct TpCtx {
+    int rank = 0, world = 1;
+    void* const* d_peers = nullptr;          // device array: every rank's exchange buffer
+    const unsigned long long* d_step = nullptr;
+    int calls = 0;                            // exchanges per step
+    unsigned* err = nullptr;
+    float* part = nullptr;                    // [H] local partial
+};
+int tp_allreduce(const TpCtx& tp, float* hidden, int H, int call, cudaStream_t st);
+
 // Everything one decode layer needs; all pointers are device pointers.
 struct LayerArgs {
+    const TpCtx* tp = nullptr;   // null: one GPU
+    int layer = 0;
     const MvPlan* mv[GB_NMAT];
     void* mv_ws;
     const float* ra;          // pre-attention RMSNorm weight
@@ -63,7 +78,13 @@ struct LayerArgs {
 };
 int enqueue_layer(const LayerArgs& a, cudaStream_t st);
 int embed(const void* emb, int dtype, const int* d_token, int vocab, int H, float* out, unsigned* err,
-          cudaStream_t st);
+          cudaStream_t st, unsigned long long* step = nullptr);
 int set_device_int(int* p, int v, cudaStream_t st);
+// Synthetic blocks of a slice of a larger matrix: local block r * sn + j
+// (r < rows, j < sn) is global block (row0 + r) * nbg + c0 + j of stream
+// stream_id, written at out block r * ldo + j (ldo >= sn; blocks j >= sn of a
+// row are left untouched).
+int synth_blocks_shard(int dtype, void* out, size_t rows, size_t sn, size_t ldo, uint64_t row0, uint64_t nbg,
+                       uint64_t c0, uint64_t seed, uint64_t stream_id, cudaStream_t st);
 
 }  // namespace gb

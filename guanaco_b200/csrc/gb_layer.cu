@@ -67,7 +67,8 @@ struct ArgPart { float v; int i; };
 constexpr int AM_MAX_CTAS = GB_NUM_SMS;
 constexpr size_t AM_WS_BYTES = AM_MAX_CTAS * sizeof(ArgPart) + 16;
 __global__ void __launch_bounds__(1024) k_argmax_split(const float* __restrict__ x, int n, int* __restrict__ out,
-                                                       ArgPart* __restrict__ part, unsigned* __restrict__ ticket) {
+                                                       ArgPart* __restrict__ part, unsigned* __restrict__ ticket,
+                                                       ArgPart* __restrict__ result, int off) {
     __shared__ float sv[32];
     __shared__ int si[32];
     __shared__ bool last;
@@ -106,7 +107,12 @@ __global__ void __launch_bounds__(1024) k_argmax_split(const float* __restrict__
         const int i = __ldcg(&part[k].i);
         if (v > mv || (v == mv && i < mi)) { mv = v; mi = i; }
     }
-    *out = mi == 0x7fffffff ? 0 : mi;
+    mi = mi == 0x7fffffff ? 0 : mi;
+    *out = mi + off;
+    if (result) {   // (max, global index) for the tensor-parallel merge
+        result->v = mv;
+        result->i = mi + off;
+    }
     *ticket = 0u;
 }
 
@@ -146,7 +152,8 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ x, in
 // Embedding row of *d_token (engine.c:214-283): F32 copy, Q8_0 q*scale,
 // Q4_K d1*q - m1 -- bit-exact with the reference dequantiser.
 __global__ void k_embed(const void* __restrict__ emb, int dtype, const int* __restrict__ d_token, int vocab, int H,
-                        float* __restrict__ out, unsigned* __restrict__ err) {
+                        float* __restrict__ out, unsigned* __restrict__ err, unsigned long long* __restrict__ step) {
+    if (step && blockIdx.x == 0 && threadIdx.x == 0) *step += 1;   // epochs of this step's exchanges
     const int tok = *d_token;
     if (tok < 0 || tok >= vocab) {
         if (threadIdx.x == 0 && blockIdx.x == 0 && err) atomicExch(err, (unsigned)(-GB_EINVAL));
@@ -181,6 +188,105 @@ __global__ void k_advance(int* tok, const int* next, int* pos, int* out, int* co
     *pos += 1;
     if (out) out[*count] = *next;
     *count += 1;
+}
+
+// ---------------------------------------------------------------- tensor parallel exchanges
+// Every rank owns a receive buffer in its own HBM; the others write into it
+// over NVLink through CUDA IPC mappings.  Layout (world <= 8, H floats):
+//   slots [2][world][H] fp32 | results [2][world] ArgPart | flags [2][world] u32
+// Exchange e of a step gets epoch = step * calls + e + 1 (unique, the same on
+// every rank); it uses parity e & 1 of the slots and flags, so a rank one
+// exchange ahead never overwrites data a peer is still reading.  A sender
+// stores its data, fences at system scope and releases flag[parity][sender]
+// = epoch; a receiver acquires until every flag reached the epoch (bounded:
+// 2 s, then GB_ETIMEOUT in the error word).
+__device__ __forceinline__ size_t tp_slots_bytes(int world, int H) { return (size_t)2 * world * H * sizeof(float); }
+__device__ __forceinline__ unsigned* tp_flags(void* base, int world, int H) {
+    return reinterpret_cast<unsigned*>(static_cast<char*>(base) + tp_slots_bytes(world, H) + 2 * world * sizeof(ArgPart));
+}
+__device__ __forceinline__ ArgPart* tp_results(void* base, int world, int H) {
+    return reinterpret_cast<ArgPart*>(static_cast<char*>(base) + tp_slots_bytes(world, H));
+}
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint64_t tp_gtimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// wait until flags[i] has reached ep (wrap-safe); false after 2 s
+__device__ bool tp_wait_flag(const unsigned* flag, unsigned ep) {
+    if ((int)(ld_acquire_sys(flag) - ep) >= 0) return true;
+    const uint64_t t0 = tp_gtimer();
+    while ((int)(ld_acquire_sys(flag) - ep) < 0)
+        if (tp_gtimer() - t0 > 2000000000ull) return false;
+    return true;
+}
+
+// hidden += sum over ranks (in rank order) of every rank's partial.  Grid =
+// world CTAs: CTA p pushes this rank's partial to peer p, then reduces slice
+// p of hidden from this rank's own buffer.
+__global__ void __launch_bounds__(512) k_tp_allreduce(const float* __restrict__ part, float* __restrict__ hidden,
+                                                      int H, int rank, int world, void* const* __restrict__ peers,
+                                                      const unsigned long long* __restrict__ step, int calls,
+                                                      int call, unsigned* __restrict__ err) {
+    const unsigned ep = (unsigned)(*step * (unsigned long long)calls + call + 1);
+    const int par = ep & 1, p = blockIdx.x, tid = threadIdx.x;
+    float* dst = static_cast<float*>(peers[p]) + ((size_t)par * world + rank) * H;
+    for (int i = 4 * tid; i < H; i += 4 * blockDim.x)
+        *reinterpret_cast<float4*>(dst + i) = *reinterpret_cast<const float4*>(part + i);
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence_system();
+        st_release_sys(tp_flags(peers[p], world, H) + par * world + rank, ep);
+    }
+    void* mine = peers[rank];
+    if (tid < world && !tp_wait_flag(tp_flags(mine, world, H) + par * world + tid, ep))
+        atomicExch(err, (unsigned)(-GB_ETIMEOUT));
+    __syncthreads();
+    const float* slots = static_cast<const float*>(mine) + (size_t)par * world * H;
+    const int lo = (int)((long long)p * H / world), hi = (int)((long long)(p + 1) * H / world);
+    for (int i = lo + tid; i < hi; i += blockDim.x) {
+        float sum = 0.f;
+        for (int q = 0; q < world; q++) sum += __ldcg(slots + (size_t)q * H + i);
+        hidden[i] = hidden[i] + sum;
+    }
+}
+
+// Greedy token over the vocabulary shards: every rank publishes its shard's
+// (max, global index) and takes the best in rank order (shards are in index
+// order, so ties keep the lowest index, as sample_greedy).
+__global__ void k_tp_argmax(const ArgPart* __restrict__ mine_res, int* __restrict__ out, int H, int rank, int world,
+                            void* const* __restrict__ peers, const unsigned long long* __restrict__ step, int calls,
+                            int call, unsigned* __restrict__ err) {
+    const unsigned ep = (unsigned)(*step * (unsigned long long)calls + call + 1);
+    const int par = ep & 1, t = threadIdx.x;
+    if (t < world) {
+        tp_results(peers[t], world, H)[par * world + rank] = *mine_res;
+        __threadfence_system();
+        st_release_sys(tp_flags(peers[t], world, H) + par * world + rank, ep);
+    }
+    __syncwarp();
+    void* mine = peers[rank];
+    if (t < world && !tp_wait_flag(tp_flags(mine, world, H) + par * world + t, ep))
+        atomicExch(err, (unsigned)(-GB_ETIMEOUT));
+    __syncwarp();
+    if (t != 0) return;
+    const ArgPart* r = tp_results(mine, world, H) + par * world;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int q = 0; q < world; q++) {
+        const float v = __ldcg(&r[q].v);
+        const int i = __ldcg(&r[q].i);
+        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+    }
+    *out = bi == 0x7fffffff ? 0 : bi;
 }
 
 }  // namespace gb
@@ -229,7 +335,21 @@ extern "C" int gb_device_sm_count(void) {
 // ---------------------------------------------------------------- model
 struct gb_model {
     gb_model_config c;
-    int kv_dim = 0;
+    int kv_dim = 0;                   // local KV width (nkv * head_dim)
+    // tensor parallelism: this rank's slice of the model (rank, world)
+    int rank = 0, world = 1;
+    int nh = 0, nkv = 0;              // local q / kv heads
+    int ff = 0, ff_pad = 0;           // local FFN rows; padded width of the gate / up buffers
+    int vocab_l = 0, vocab_off = 0;   // output-head rows of this rank
+    void* comm = nullptr;             // exchange buffer (world > 1)
+    size_t comm_bytes = 0;
+    void** d_peers = nullptr;         // device array of the world exchange buffers
+    void* peer_open[8] = {};          // IPC mappings opened by this rank
+    bool comm_ready = false;
+    unsigned long long* d_step = nullptr;
+    float* part = nullptr;            // local partial of wo / ffn_down
+    ArgPart* am_res = nullptr;        // local (max, index) of the output head
+    TpCtx tp;
     std::vector<const void*> w;       // [n_layers * 7]
     std::vector<int> dt;              // [n_layers * 7]
     std::vector<const float*> ra, rf; // [n_layers]
@@ -268,44 +388,79 @@ static void* dalloc(gb_model* m, size_t bytes) {
     return p;
 }
 
-extern "C" gb_model* gb_model_create(const gb_model_config* cfg) {
+static void invalidate_graph(gb_model* m);
+
+// Exchange buffer of one rank: slots [2][world][H] fp32, results [2][world],
+// flags [2][world] u32 (see k_tp_allreduce).
+static size_t tp_comm_bytes(int world, int H) {
+    return (size_t)2 * world * H * sizeof(float) + 2 * world * sizeof(ArgPart) + 2 * world * sizeof(unsigned);
+}
+
+extern "C" gb_model* gb_model_create_tp(const gb_model_config* cfg, int rank, int world) {
     if (!cfg) return nullptr;
     const gb_model_config& c = *cfg;
     if (c.hidden_dim <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.n_heads % c.n_kv_heads ||
         c.head_dim * c.n_heads != c.hidden_dim || c.n_layers <= 0 || c.ff_dim <= 0 || c.vocab_size <= 0 ||
         c.max_seq <= 0)
         return nullptr;
+    // shards: heads by rank (KV heads too), FFN rows in 256-column blocks,
+    // wo columns in whole blocks, vocabulary rows by rank
+    if (world < 1 || world > 8 || rank < 0 || rank >= world) return nullptr;
+    if (world > 1 && (c.n_kv_heads % world || c.ff_dim % (256 * world) ||
+                      (c.n_heads / world * c.head_dim) % 256 || c.hidden_dim % 4))
+        return nullptr;
     gb_model* m = new gb_model();
     m->c = c;
-    m->kv_dim = c.n_kv_heads * c.head_dim;
+    m->rank = rank;
+    m->world = world;
+    m->nh = c.n_heads / world;
+    m->nkv = c.n_kv_heads / world;
+    m->ff = c.ff_dim / world;
+    // a Q6_K ffn_down shard keeps its rows at 8-block multiples (zero blocks
+    // after the shard's columns) so its tensor map has a 16-byte stride; the
+    // gate / up buffers carry the matching zero tail
+    m->ff_pad = world > 1 ? (m->ff + 2047) / 2048 * 2048 : m->ff;
+    m->vocab_off = (int)((long long)rank * c.vocab_size / world);
+    m->vocab_l = (int)((long long)(rank + 1) * c.vocab_size / world) - m->vocab_off;
+    m->kv_dim = m->nkv * c.head_dim;
     m->w.assign((size_t)c.n_layers * GB_NMAT, nullptr);
     m->dt.assign((size_t)c.n_layers * GB_NMAT, GB_DT_Q4_K);
     m->plan.assign((size_t)c.n_layers * GB_NMAT, MvPlan{});
     m->ra.assign(c.n_layers, nullptr);
     m->rf.assign(c.n_layers, nullptr);
     const size_t kv_elems = (size_t)c.n_layers * m->kv_dim * c.max_seq;
+    const int H = c.hidden_dim, QD = m->nh * c.head_dim, FP = m->ff_pad;
     bool ok = true;
     ok &= (m->kc = (float*)dalloc(m, kv_elems * 4)) != nullptr;
     ok &= (m->vc = (float*)dalloc(m, kv_elems * 4)) != nullptr;
     ok &= (m->rope = (float*)dalloc(m, (size_t)c.max_seq * c.head_dim * 4)) != nullptr;
-    const size_t ws = gb_attn_workspace_bytes(c.n_heads, c.n_kv_heads, c.head_dim, c.max_seq);
+    const size_t ws = gb_attn_workspace_bytes(m->nh, m->nkv, c.head_dim, c.max_seq);
     ok &= ws > 0 && (m->attn_ws = dalloc(m, ws)) != nullptr;
-    const int H = c.hidden_dim, F = c.ff_dim;
     ok &= (m->hidden = (float*)dalloc(m, (size_t)H * 4)) != nullptr;
-    ok &= (m->xn = (float*)dalloc(m, (size_t)(H > F ? H : F) * 4)) != nullptr;
-    ok &= (m->q = (float*)dalloc(m, (size_t)H * 4)) != nullptr;
+    ok &= (m->xn = (float*)dalloc(m, (size_t)(H > FP ? H : FP) * 4)) != nullptr;
+    ok &= (m->q = (float*)dalloc(m, (size_t)QD * 4)) != nullptr;
     ok &= (m->k = (float*)dalloc(m, (size_t)m->kv_dim * 4)) != nullptr;
     ok &= (m->v = (float*)dalloc(m, (size_t)m->kv_dim * 4)) != nullptr;
-    ok &= (m->attn = (float*)dalloc(m, (size_t)H * 4)) != nullptr;
-    ok &= (m->gate = (float*)dalloc(m, (size_t)F * 4)) != nullptr;
-    ok &= (m->up = (float*)dalloc(m, (size_t)F * 4)) != nullptr;
-    ok &= (m->logits = (float*)dalloc(m, (size_t)c.vocab_size * 4)) != nullptr;
+    ok &= (m->attn = (float*)dalloc(m, (size_t)QD * 4)) != nullptr;
+    ok &= (m->gate = (float*)dalloc(m, (size_t)FP * 4)) != nullptr;
+    ok &= (m->up = (float*)dalloc(m, (size_t)FP * 4)) != nullptr;
+    ok &= (m->logits = (float*)dalloc(m, (size_t)m->vocab_l * 4)) != nullptr;
     ok &= (m->err = (unsigned*)dalloc(m, 16)) != nullptr;
     ok &= (m->d_tok = (int*)dalloc(m, 16)) != nullptr;
     ok &= (m->d_pos = (int*)dalloc(m, 16)) != nullptr;
     ok &= (m->d_next = (int*)dalloc(m, 16)) != nullptr;
     ok &= (m->d_count = (int*)dalloc(m, 16)) != nullptr;
     ok &= (m->am_ws = dalloc(m, AM_WS_BYTES)) != nullptr;
+    ok &= (m->d_step = (unsigned long long*)dalloc(m, 16)) != nullptr;
+    ok &= (m->am_res = (ArgPart*)dalloc(m, 16)) != nullptr;
+    if (world > 1) {
+        m->comm_bytes = tp_comm_bytes(world, H);
+        ok &= (m->part = (float*)dalloc(m, (size_t)H * 4)) != nullptr;
+        ok &= (m->d_peers = (void**)dalloc(m, 8 * sizeof(void*))) != nullptr;
+        // the exchange buffer gets its own allocation: it is shared with the
+        // peers through cudaIpcGetMemHandle
+        if (ok && cudaMalloc(&m->comm, m->comm_bytes) != cudaSuccess) { m->comm = nullptr; ok = false; }
+    }
     ok &= cudaMallocHost(&m->h_io, 4 * sizeof(int)) == cudaSuccess;
     ok &= cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) == cudaSuccess;
     // zero in stream order, then wait: decode may run on any stream
@@ -313,14 +468,67 @@ extern "C" gb_model* gb_model_create(const gb_model_config* cfg) {
                   cudaMemsetAsync(m->vc, 0, kv_elems * 4, m->stream) == cudaSuccess;
     if (ok) ok &= cudaMemsetAsync(m->attn_ws, 0, ws, m->stream) == cudaSuccess &&
                   cudaMemsetAsync(m->err, 0, 16, m->stream) == cudaSuccess &&
-                  cudaMemsetAsync(m->am_ws, 0, AM_WS_BYTES, m->stream) == cudaSuccess;
+                  cudaMemsetAsync(m->am_ws, 0, AM_WS_BYTES, m->stream) == cudaSuccess &&
+                  cudaMemsetAsync(m->d_step, 0, 16, m->stream) == cudaSuccess &&
+                  cudaMemsetAsync(m->gate, 0, (size_t)FP * 4, m->stream) == cudaSuccess &&
+                  cudaMemsetAsync(m->up, 0, (size_t)FP * 4, m->stream) == cudaSuccess;
+    if (ok && m->comm) ok &= cudaMemsetAsync(m->comm, 0, m->comm_bytes, m->stream) == cudaSuccess;
     if (ok) ok &= gb_rope_table(m->rope, c.max_seq, c.head_dim, c.rope_theta, m->stream) == GB_OK;
     if (ok) ok &= cudaStreamSynchronize(m->stream) == cudaSuccess;
     if (!ok) {
         gb_model_destroy(m);
         return nullptr;
     }
+    m->tp.rank = rank;
+    m->tp.world = world;
+    m->tp.d_peers = m->d_peers;
+    m->tp.d_step = m->d_step;
+    m->tp.calls = 2 * c.n_layers + 1;
+    m->tp.err = m->err;
+    m->tp.part = m->part;
     return m;
+}
+
+extern "C" gb_model* gb_model_create(const gb_model_config* cfg) { return gb_model_create_tp(cfg, 0, 1); }
+
+extern "C" int gb_model_comm_handle(gb_model* m, void* handle) {
+    if (!m || !handle || m->world < 2 || !m->comm) return GB_EINVAL;
+    cudaIpcMemHandle_t h;
+    GB_CUDA_TRY(cudaIpcGetMemHandle(&h, m->comm));
+    memcpy(handle, &h, sizeof(h));
+    return GB_OK;
+}
+
+extern "C" int gb_model_comm_open(gb_model* m, const void* handles) {
+    if (!m || !handles || m->world < 2 || !m->comm || m->comm_ready) return GB_EINVAL;
+    void* peers[8] = {};
+    for (int q = 0; q < m->world; q++) {
+        if (q == m->rank) {
+            peers[q] = m->comm;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const char*>(handles) + (size_t)q * GB_IPC_HANDLE_BYTES, sizeof(h));
+        if (cudaIpcOpenMemHandle(&peers[q], h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            for (int j = 0; j < q; j++)
+                if (j != m->rank && peers[j]) cudaIpcCloseMemHandle(peers[j]);
+            return GB_ECUDA;
+        }
+    }
+    for (int q = 0; q < m->world; q++) m->peer_open[q] = q == m->rank ? nullptr : peers[q];
+    GB_CUDA_TRY(cudaMemcpy(m->d_peers, peers, sizeof(peers), cudaMemcpyHostToDevice));
+    m->comm_ready = true;
+    invalidate_graph(m);
+    return GB_OK;
+}
+
+extern "C" int gb_model_tp_info(const gb_model* m, int* rank, int* world, int* vocab_off, int* vocab_rows) {
+    if (!m) return GB_EINVAL;
+    if (rank) *rank = m->rank;
+    if (world) *world = m->world;
+    if (vocab_off) *vocab_off = m->vocab_off;
+    if (vocab_rows) *vocab_rows = m->vocab_l;
+    return GB_OK;
 }
 
 extern "C" void gb_model_destroy(gb_model* m) {
@@ -328,6 +536,9 @@ extern "C" void gb_model_destroy(gb_model* m) {
     if (m->exec) cudaGraphExecDestroy(m->exec);
     if (m->gen_exec) cudaGraphExecDestroy(m->gen_exec);
     if (m->stream) cudaStreamSynchronize(m->stream);
+    for (void* p : m->peer_open)
+        if (p) cudaIpcCloseMemHandle(p);
+    if (m->comm) cudaFree(m->comm);
     for (void* p : m->owned) cudaFree(p);
     if (m->h_io) cudaFreeHost(m->h_io);
     if (m->stream) cudaStreamDestroy(m->stream);
@@ -339,13 +550,14 @@ static void invalidate_graph(gb_model* m) {
     if (m->gen_exec) { cudaGraphExecDestroy(m->gen_exec); m->gen_exec = nullptr; }
 }
 
-static void mat_shape(const gb_model* m, int which, int* rows, int* cols);
+static void mat_shape(const gb_model* m, int which, int dtype, int* rows, int* cols);
+static void invalidate_graph(gb_model* m);
 
 extern "C" int gb_model_set_matrix(gb_model* m, int layer, int which, int dtype, const void* d_w) {
     if (!m || layer < 0 || layer >= m->c.n_layers || which < 0 || which >= GB_NMAT || !d_w) return GB_EINVAL;
     if (dtype != GB_DT_Q4_K && dtype != GB_DT_Q6_K && dtype != GB_DT_Q8_0) return GB_EINVAL;
     int rows, cols;
-    mat_shape(m, which, &rows, &cols);
+    mat_shape(m, which, dtype, &rows, &cols);
     MvPlan p;
     const int rc = mv_plan(&p, dtype, d_w, rows, cols);
     if (rc) return rc;
@@ -367,7 +579,7 @@ extern "C" int gb_model_set_head(gb_model* m, int emb_dtype, const void* emb, co
     if (!m || !emb || !rms_final || !lm) return GB_EINVAL;
     if (emb_dtype != GB_DT_Q4_K && emb_dtype != GB_DT_Q8_0 && emb_dtype != GB_DT_F32) return GB_EINVAL;
     MvPlan p;
-    const int rc = mv_plan(&p, lm_dtype, lm, m->c.vocab_size, m->c.hidden_dim);
+    const int rc = mv_plan(&p, lm_dtype, lm, m->vocab_l, m->c.hidden_dim);   // this rank's vocabulary rows
     if (rc) return rc;
     m->emb = emb; m->emb_dt = emb_dtype; m->rms_final = rms_final; m->lm = lm; m->lm_dt = lm_dtype;
     m->lm_plan = p;
@@ -382,14 +594,49 @@ extern "C" float* gb_model_v_cache(gb_model* m, int layer) {
     return (m && layer >= 0 && layer < m->c.n_layers) ? m->vc + (size_t)layer * m->kv_dim * m->c.max_seq : nullptr;
 }
 
-// Matrix shapes per slot: (rows, cols).
-static void mat_shape(const gb_model* m, int which, int* rows, int* cols) {
-    const int H = m->c.hidden_dim, F = m->c.ff_dim, KV = m->kv_dim;
-    static const int R[GB_NMAT] = {0, 1, 1, 0, 2, 2, 0}, Cc[GB_NMAT] = {0, 0, 0, 0, 0, 0, 2};
-    const int dims[3] = {H, KV, F};
-    *rows = dims[R[which]];
-    *cols = which == GB_WDOWN ? F : H;
-    (void)Cc;
+// This rank's matrix shape per slot (rows, cols): q / k / v rows of its
+// heads, wo columns of its heads, gate / up rows and ffn_down columns of its
+// FFN slice (a Q6_K ffn_down shard is stored with rows padded to 8 blocks).
+static void mat_shape(const gb_model* m, int which, int dtype, int* rows, int* cols) {
+    const int H = m->c.hidden_dim, QD = m->nh * m->c.head_dim;
+    switch (which) {
+        case GB_WQ: *rows = QD; *cols = H; break;
+        case GB_WK: case GB_WV: *rows = m->kv_dim; *cols = H; break;
+        case GB_WO: *rows = H; *cols = QD; break;
+        case GB_WGATE: case GB_WUP: *rows = m->ff; *cols = H; break;
+        default: *rows = H; *cols = (dtype == GB_DT_Q6_K && m->world > 1) ? m->ff_pad : m->ff; break;
+    }
+}
+
+// The slice of the full synthetic matrix `which` (stream stream_id) this rank
+// holds, with the bytes the one-GPU model would have at those positions.
+static int synth_slice(gb_model* m, int which, int dtype, void* p, uint64_t seed, uint64_t stream_id) {
+    const gb_model_config& c = m->c;
+    const int H = c.hidden_dim, hd = c.head_dim;
+    const uint64_t nbH = H / 256;
+    int rows, cols;
+    mat_shape(m, which, dtype, &rows, &cols);
+    switch (which) {
+        case GB_WQ:
+            return synth_blocks_shard(dtype, p, rows, nbH, nbH, (uint64_t)m->rank * rows, nbH, 0, seed, stream_id, m->stream);
+        case GB_WK: case GB_WV:
+            return synth_blocks_shard(dtype, p, rows, nbH, nbH, (uint64_t)m->rank * rows, nbH, 0, seed, stream_id, m->stream);
+        case GB_WGATE: case GB_WUP:
+            return synth_blocks_shard(dtype, p, rows, nbH, nbH, (uint64_t)m->rank * rows, nbH, 0, seed, stream_id, m->stream);
+        case GB_WO: {
+            const uint64_t sn = (uint64_t)m->nh * hd / 256;
+            return synth_blocks_shard(dtype, p, rows, sn, sn, 0, (uint64_t)c.n_heads * hd / 256, m->rank * sn, seed,
+                                      stream_id, m->stream);
+        }
+        default: {   // ffn_down: this rank's FFN columns, zero padding after them
+            const uint64_t sn = (uint64_t)m->ff / 256, ldo = (uint64_t)cols / 256;
+            if (ldo > sn &&
+                cudaMemsetAsync(p, 0, (size_t)rows * ldo * gb_block_bytes(dtype), m->stream) != cudaSuccess)
+                return GB_ECUDA;
+            return synth_blocks_shard(dtype, p, rows, sn, ldo, 0, (uint64_t)c.ff_dim / 256, m->rank * sn, seed,
+                                      stream_id, m->stream);
+        }
+    }
 }
 
 extern "C" int gb_model_synthesize(gb_model* m, uint64_t seed) {
@@ -404,24 +651,26 @@ extern "C" int gb_model_synthesize(gb_model* m, uint64_t seed) {
         for (int wi = 0; wi < GB_NMAT; wi++) {
             const int dtype = (wi == GB_WV || wi == GB_WDOWN) ? GB_DT_Q6_K : GB_DT_Q4_K;
             int rows, cols;
-            mat_shape(m, wi, &rows, &cols);
+            mat_shape(m, wi, dtype, &rows, &cols);
             if (cols % 256) return GB_ESHAPE;
             const size_t nblk = (size_t)rows * (cols / 256);
             void* p = dalloc(m, nblk * gb_block_bytes(dtype) + 16);
             if (!p) return GB_ENOMEM;
-            rc = gb_synth_blocks(dtype, p, nblk, seed, (uint64_t)(l * GB_NMAT + wi + 1), m->stream);
-            if (rc) return rc;
-            gb_model_set_matrix(m, l, wi, dtype, p);
+            if ((rc = synth_slice(m, wi, dtype, p, seed, (uint64_t)(l * GB_NMAT + wi + 1)))) return rc;
+            if ((rc = gb_model_set_matrix(m, l, wi, dtype, p))) return rc;
         }
         gb_model_set_norms(m, l, ones, ones);
     }
     const size_t eblk = (size_t)c.vocab_size * (H / 256);
+    const size_t lblk = (size_t)m->vocab_l * (H / 256);
     void* e = dalloc(m, eblk * GB_Q4K_BYTES);
-    void* lmp = dalloc(m, eblk * GB_Q6K_BYTES + 16);
+    void* lmp = dalloc(m, lblk * GB_Q6K_BYTES + 16);
     if (!e || !lmp) return GB_ENOMEM;
-    if ((rc = gb_synth_blocks(GB_DT_Q4_K, e, eblk, seed, 1000001ull, m->stream))) return rc;
-    if ((rc = gb_synth_blocks(GB_DT_Q6_K, lmp, eblk, seed, 1000002ull, m->stream))) return rc;
-    gb_model_set_head(m, GB_DT_Q4_K, e, ones, GB_DT_Q6_K, lmp);
+    if ((rc = gb_synth_blocks(GB_DT_Q4_K, e, eblk, seed, 1000001ull, m->stream))) return rc;   // every rank: full table
+    if ((rc = synth_blocks_shard(GB_DT_Q6_K, lmp, m->vocab_l, H / 256, H / 256, (uint64_t)m->vocab_off, H / 256, 0,
+                                 seed, 1000002ull, m->stream)))
+        return rc;
+    if ((rc = gb_model_set_head(m, GB_DT_Q4_K, e, ones, GB_DT_Q6_K, lmp))) return rc;
     return cudaStreamSynchronize(m->stream) == cudaSuccess ? GB_OK : GB_ECUDA;
 }
 
@@ -457,7 +706,13 @@ int enqueue_layer(const LayerArgs& a, cudaStream_t st) {
     if ((rc = gb_attention_decode(a.q, a.k, a.v, a.kc, a.vc, a.rope, a.d_pos, a.n_heads, a.n_kv, a.hd, a.max_seq,
                                   a.attn, a.attn_ws, st)))
         return rc;
-    if ((rc = mv(GB_WO, a.attn, a.hidden, a.hidden, nullptr))) return rc;
+    const bool tp = a.tp && a.tp->world > 1;
+    if (tp) {   // this rank's columns of wo, then hidden += sum of the ranks' partials
+        if ((rc = mv(GB_WO, a.attn, a.tp->part, nullptr, nullptr))) return rc;
+        if ((rc = tp_allreduce(*a.tp, a.hidden, H, 2 * a.layer, st))) return rc;
+    } else if ((rc = mv(GB_WO, a.attn, a.hidden, a.hidden, nullptr))) {
+        return rc;
+    }
     if (tma(GB_WGATE) && tma(GB_WUP)) {
         if ((rc = mv(GB_WGATE, a.hidden, a.gate, nullptr, &ffn))) return rc;
         if ((rc = mv(GB_WUP, a.hidden, a.up, nullptr, &ffn))) return rc;
@@ -466,13 +721,26 @@ int enqueue_layer(const LayerArgs& a, cudaStream_t st) {
         if ((rc = mv(GB_WGATE, a.xn, a.gate, nullptr, nullptr))) return rc;
         if ((rc = mv(GB_WUP, a.xn, a.up, nullptr, nullptr))) return rc;
     }
-    if (tma(GB_WDOWN)) return mv(GB_WDOWN, a.gate, a.hidden, a.hidden, &swi);
-    if ((rc = gb_silu_mul(a.gate, a.up, F, st))) return rc;
-    return mv(GB_WDOWN, a.gate, a.hidden, a.hidden, nullptr);
+    float* dy = tp ? a.tp->part : a.hidden;
+    const float* dres = tp ? nullptr : a.hidden;
+    if (tma(GB_WDOWN)) {
+        rc = mv(GB_WDOWN, a.gate, dy, dres, &swi);
+    } else {
+        if ((rc = gb_silu_mul(a.gate, a.up, F, st))) return rc;
+        rc = mv(GB_WDOWN, a.gate, dy, dres, nullptr);
+    }
+    if (rc || !tp) return rc;
+    return tp_allreduce(*a.tp, a.hidden, H, 2 * a.layer + 1, st);
 }
 
-int embed(const void* emb, int dtype, const int* d_token, int vocab, int H, float* out, unsigned* err, cudaStream_t st) {
-    k_embed<<<(H + 255) / 256, 256, 0, st>>>(emb, dtype, d_token, vocab, H, out, err);
+int embed(const void* emb, int dtype, const int* d_token, int vocab, int H, float* out, unsigned* err, cudaStream_t st,
+          unsigned long long* step) {
+    k_embed<<<(H + 255) / 256, 256, 0, st>>>(emb, dtype, d_token, vocab, H, out, err, step);
+    return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
+}
+int tp_allreduce(const TpCtx& tp, float* hidden, int H, int call, cudaStream_t st) {
+    k_tp_allreduce<<<tp.world, 512, 0, st>>>(tp.part, hidden, H, tp.rank, tp.world, tp.d_peers, tp.d_step, tp.calls,
+                                             call, tp.err);
     return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
 }
 int set_device_int(int* p, int v, cudaStream_t st) {
@@ -487,9 +755,11 @@ static int enqueue_step(gb_model* m, const int* d_token, const int* d_pos, float
     const gb_model_config& c = m->c;
     const int H = c.hidden_dim;
     int rc;
-    if ((rc = embed(m->emb, m->emb_dt, d_token, c.vocab_size, H, m->hidden, m->err, st))) return rc;
+    if ((rc = embed(m->emb, m->emb_dt, d_token, c.vocab_size, H, m->hidden, m->err, st, m->d_step))) return rc;
     for (int l = 0; l < c.n_layers; l++) {
         LayerArgs a;
+        a.tp = m->world > 1 ? &m->tp : nullptr;
+        a.layer = l;
         for (int i = 0; i < GB_NMAT; i++) a.mv[i] = &m->plan[(size_t)l * GB_NMAT + i];
         a.mv_ws = m->mv_ws;
         a.ra = m->ra[l]; a.rf = m->rf[l];
@@ -497,7 +767,7 @@ static int enqueue_step(gb_model* m, const int* d_token, const int* d_pos, float
         a.rope = m->rope; a.d_pos = d_pos; a.attn_ws = m->attn_ws;
         a.hidden = m->hidden; a.xn = m->xn; a.q = m->q; a.k = m->k; a.v = m->v; a.attn = m->attn;
         a.gate = m->gate; a.up = m->up;
-        a.H = H; a.n_heads = c.n_heads; a.n_kv = c.n_kv_heads; a.hd = c.head_dim; a.ff = c.ff_dim;
+        a.H = H; a.n_heads = m->nh; a.n_kv = m->nkv; a.hd = c.head_dim; a.ff = m->ff;
         a.max_seq = c.max_seq; a.eps = c.rms_eps;
         if ((rc = enqueue_layer(a, st))) return rc;
     }
@@ -512,15 +782,22 @@ static int enqueue_step(gb_model* m, const int* d_token, const int* d_pos, float
         if ((rc = gb_rmsnorm(m->hidden, m->rms_final, m->xn, H, c.rms_eps, st))) return rc;
         if ((rc = mv_launch(m->lm_plan, m->xn, lg, nullptr, m->mv_ws, st, true))) return rc;
     }
-    const int G = std::min(AM_MAX_CTAS, (c.vocab_size + 4095) / 4096);
+    const int G = std::min(AM_MAX_CTAS, (m->vocab_l + 4095) / 4096);
     ArgPart* part = static_cast<ArgPart*>(m->am_ws);
-    k_argmax_split<<<G, 1024, 0, st>>>(lg, c.vocab_size, d_next, part,
-                                       reinterpret_cast<unsigned*>(part + AM_MAX_CTAS));
-    return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
+    k_argmax_split<<<G, 1024, 0, st>>>(lg, m->vocab_l, d_next, part, reinterpret_cast<unsigned*>(part + AM_MAX_CTAS),
+                                       m->world > 1 ? m->am_res : nullptr, m->vocab_off);
+    if (cudaGetLastError() != cudaSuccess) return GB_ECUDA;
+    if (m->world > 1) {   // the best (value, index) over the ranks' vocabulary slices
+        k_tp_argmax<<<1, 32, 0, st>>>(m->am_res, d_next, H, m->rank, m->world, m->d_peers, m->d_step, m->tp.calls,
+                                      2 * c.n_layers, m->err);
+        if (cudaGetLastError() != cudaSuccess) return GB_ECUDA;
+    }
+    return GB_OK;
 }
 
 // All weights set, and the shared matvec workspace sized for every plan.
 static bool model_ready(gb_model* m) {
+    if (m->world > 1 && !m->comm_ready) return false;   // gb_model_comm_open first
     for (size_t i = 0; i < m->w.size(); i++) if (!m->w[i]) return false;
     for (int l = 0; l < m->c.n_layers; l++) if (!m->ra[l] || !m->rf[l]) return false;
     if (!(m->emb && m->lm && m->rms_final)) return false;
@@ -619,10 +896,11 @@ extern "C" int gb_model_fill_kv(gb_model* m, int n_pos, uint64_t seed) {
     for (int l = 0; l < c.n_layers; l++)
         for (int which = 0; which < 2; which++) {
             float* base = which ? gb_model_v_cache(m, l) : gb_model_k_cache(m, l);
-            for (int h = 0; h < c.n_kv_heads; h++) {
+            for (int h = 0; h < m->nkv; h++) {   // this rank's KV heads, numbered globally
                 float* p = base + (size_t)h * c.max_seq * c.head_dim;
+                const int hg = m->rank * m->nkv + h;
                 const int rc = gb_synth_normal(p, (size_t)n_pos * c.head_dim, seed,
-                                               (uint64_t)((l * 2 + which) * 256 + h) + 5000000ull, m->stream);
+                                               (uint64_t)((l * 2 + which) * 256 + hg) + 5000000ull, m->stream);
                 if (rc) return rc;
             }
         }
@@ -643,6 +921,7 @@ extern "C" int gb_model_launches_per_step(const gb_model* m) {
         n += tma(GB_WDOWN) ? 0 : 1;
     }
     n += m->lm_plan.kind == MV_TMA ? 1 : 2;
+    if (m->world > 1) n += 2 * m->c.n_layers + 1;   // all-reduces after wo / ffn_down, argmax merge
     return n + 1;
 }
 
@@ -659,7 +938,7 @@ extern "C" int gb_model_decode_host(gb_model* m, int token, int pos, int* h_next
     if (rc) return rc;
     GB_CUDA_TRY(cudaMemcpyAsync(&m->h_io[2], m->d_next, sizeof(int), cudaMemcpyDeviceToHost, st));
     if (h_logits)
-        GB_CUDA_TRY(cudaMemcpyAsync(h_logits, m->logits, (size_t)m->c.vocab_size * 4, cudaMemcpyDeviceToHost, st));
+        GB_CUDA_TRY(cudaMemcpyAsync(h_logits, m->logits, (size_t)m->vocab_l * 4, cudaMemcpyDeviceToHost, st));
     GB_CUDA_TRY(cudaStreamSynchronize(st));
     unsigned herr = 0;
     GB_CUDA_TRY(cudaMemcpy(&herr, m->err, sizeof(unsigned), cudaMemcpyDeviceToHost));
@@ -675,10 +954,11 @@ extern "C" double gb_model_step_bytes(const gb_model* m, int pos) {
     for (int l = 0; l < c.n_layers; l++)
         for (int wi = 0; wi < GB_NMAT; wi++) {
             int rows, cols;
-            mat_shape(m, wi, &rows, &cols);
-            b += (double)gb_matrix_bytes(m->dt[(size_t)l * GB_NMAT + wi], rows, cols);
+            const int dt = m->dt[(size_t)l * GB_NMAT + wi];
+            mat_shape(m, wi, dt, &rows, &cols);
+            b += (double)gb_matrix_bytes(dt, rows, cols);
         }
-    b += (double)gb_matrix_bytes(m->lm_dt, c.vocab_size, c.hidden_dim);
+    b += (double)gb_matrix_bytes(m->lm_dt, m->vocab_l, c.hidden_dim);
     b += (double)(2 * c.n_layers + 1) * c.hidden_dim * 4;                   // norm weights
     b += 2.0 * c.n_layers * m->kv_dim * (double)(pos + 1) * 4;              // K and V read
     b += 2.0 * c.n_layers * m->kv_dim * 4;                                  // append

@@ -628,7 +628,6 @@ k_mv_q8_0(const uint8_t* __restrict__ W, int rows, int nb, const float* __restri
 // programmatic dependent launch the producer issues those boxes before
 // griddepcontrol.wait; consumers read x and write y only after it.
 constexpr int MT_GR = 32;                 // rows per group (two 16-row tiles)
-constexpr int MT_MAX_THREADS = 17 * 32;   // up to 16 consumer warps + the producer
 
 __device__ __forceinline__ void mbs_init(uint32_t b, uint32_t n) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(b), "r"(n) : "memory");

@@ -86,11 +86,9 @@ __device__ __forceinline__ uint16_t synth_scale(uint64_t bits) {
     return __half_as_ushort(__float2half_rn(v));
 }
 
-__global__ void k_synth_q4k(uint8_t* B, size_t nblocks, uint64_t seed, uint64_t stream) {
-    const size_t b = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (b >= nblocks) return;
-    uint8_t* blk = B + b * GB_Q4K_BYTES;
-    const uint64_t i0 = (uint64_t)b * 32;
+// Block g of the synthetic matrix (stream `stream`) written to blk.
+__device__ void synth_q4k_block(uint8_t* blk, uint64_t g, uint64_t seed, uint64_t stream) {
+    const uint64_t i0 = g * 32;
     const uint64_t r0 = rand64(seed, stream, i0);
     const uint16_t d = synth_scale(r0), dm = synth_scale(r0 >> 24);
     const uint64_t r1 = rand64(seed, stream, i0 + 1), r2 = rand64(seed, stream, i0 + 2);
@@ -114,12 +112,9 @@ __global__ void k_synth_q4k(uint8_t* B, size_t nblocks, uint64_t seed, uint64_t 
     }
 }
 
-__global__ void k_synth_q6k(uint8_t* B, size_t nblocks, uint64_t seed, uint64_t stream) {
-    const size_t b = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (b >= nblocks) return;
-    uint8_t* blk = B + b * GB_Q6K_BYTES;    // 2-byte aligned: write 16-bit halves
-    uint16_t* d16 = reinterpret_cast<uint16_t*>(blk);
-    const uint64_t i0 = (uint64_t)b * 32;
+__device__ void synth_q6k_block(uint8_t* blk, uint64_t g, uint64_t seed, uint64_t stream) {
+    uint16_t* d16 = reinterpret_cast<uint16_t*>(blk);   // 2-byte aligned: write 16-bit halves
+    const uint64_t i0 = g * 32;
     for (int w = 0; w < 24; w++) {
         const uint64_t r = rand64(seed, stream, i0 + w);
         for (int k = 0; k < 4; k++) d16[4 * w + k] = (uint16_t)(r >> (16 * k));
@@ -134,16 +129,35 @@ __global__ void k_synth_q6k(uint8_t* B, size_t nblocks, uint64_t seed, uint64_t 
     d16[104] = synth_scale(rand64(seed, stream, i0 + 26));
 }
 
-__global__ void k_synth_q8_0(uint8_t* B, size_t nblocks, uint64_t seed, uint64_t stream) {
-    const size_t b = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (b >= nblocks) return;
-    uint16_t* d16 = reinterpret_cast<uint16_t*>(B + b * GB_Q80_BYTES);
-    const uint64_t i0 = (uint64_t)b * 8;
+__device__ void synth_q8_0_block(uint8_t* blk, uint64_t g, uint64_t seed, uint64_t stream) {
+    uint16_t* d16 = reinterpret_cast<uint16_t*>(blk);
+    const uint64_t i0 = g * 8;
     d16[0] = synth_scale(rand64(seed, stream, i0));
     for (int w = 0; w < 4; w++) {
         const uint64_t r = rand64(seed, stream, i0 + 1 + w);
         for (int k = 0; k < 4; k++) d16[1 + 4 * w + k] = (uint16_t)(r >> (16 * k));
     }
+}
+
+// Local block b = r * sn + j (r < rows, j < sn) is global block
+// (row0 + r) * nbg + c0 + j, written at output block r * ldo + j: a row or
+// column slice of a larger synthetic matrix (tensor-parallel shards) gets
+// exactly the bytes of the full matrix.  The identity map is rows = 1,
+// sn = ldo = nbg = n, row0 = c0 = 0.
+struct SynthMap {
+    uint64_t row0, nbg, c0, sn, ldo;
+};
+template <int DT>
+__global__ void k_synth_map(uint8_t* B, uint64_t n_local, uint64_t seed, uint64_t stream, SynthMap m) {
+    const uint64_t b = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= n_local) return;
+    const uint64_t r = b / m.sn, j = b - r * m.sn;
+    const uint64_t g = (m.row0 + r) * m.nbg + m.c0 + j;
+    constexpr int BYTES = DT == GB_DT_Q4_K ? GB_Q4K_BYTES : DT == GB_DT_Q6_K ? GB_Q6K_BYTES : GB_Q80_BYTES;
+    uint8_t* blk = B + (r * m.ldo + j) * BYTES;
+    if (DT == GB_DT_Q4_K) synth_q4k_block(blk, g, seed, stream);
+    else if (DT == GB_DT_Q6_K) synth_q6k_block(blk, g, seed, stream);
+    else synth_q8_0_block(blk, g, seed, stream);
 }
 
 __global__ void k_synth_normal(float* out, size_t n, uint64_t seed, uint64_t stream) {
@@ -182,26 +196,36 @@ extern "C" int gb_dequant(int dtype, const void* blocks, size_t nblocks, float* 
     return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
 }
 
-extern "C" int gb_synth_blocks(int dtype, void* blocks, size_t nblocks, uint64_t seed, uint64_t stream_id,
-                               void* stream) {
-    if (!blocks) return GB_EINVAL;
-    if (nblocks == 0) return GB_OK;
-    const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const unsigned grid = (unsigned)((nblocks + 255) / 256);
-    uint8_t* B = static_cast<uint8_t*>(blocks);
+namespace gb {
+int synth_blocks_shard(int dtype, void* out, size_t rows, size_t sn, size_t ldo, uint64_t row0, uint64_t nbg,
+                       uint64_t c0, uint64_t seed, uint64_t stream_id, cudaStream_t st) {
+    if (!out || sn > ldo) return GB_EINVAL;
+    const uint64_t n = (uint64_t)rows * sn;
+    if (n == 0) return GB_OK;
+    const unsigned grid = (unsigned)((n + 255) / 256);
+    uint8_t* B = static_cast<uint8_t*>(out);
+    const SynthMap m{row0, nbg, c0, sn, ldo};
     switch (dtype) {
         case GB_DT_Q4_K:
-            if (reinterpret_cast<uintptr_t>(blocks) & 15) return GB_EINVAL;
-            k_synth_q4k<<<grid, 256, 0, st>>>(B, nblocks, seed, stream_id); break;
+            if (reinterpret_cast<uintptr_t>(out) & 15) return GB_EINVAL;
+            k_synth_map<GB_DT_Q4_K><<<grid, 256, 0, st>>>(B, n, seed, stream_id, m); break;
         case GB_DT_Q6_K:
-            if (reinterpret_cast<uintptr_t>(blocks) & 1) return GB_EINVAL;
-            k_synth_q6k<<<grid, 256, 0, st>>>(B, nblocks, seed, stream_id); break;
+            if (reinterpret_cast<uintptr_t>(out) & 1) return GB_EINVAL;
+            k_synth_map<GB_DT_Q6_K><<<grid, 256, 0, st>>>(B, n, seed, stream_id, m); break;
         case GB_DT_Q8_0:
-            if (reinterpret_cast<uintptr_t>(blocks) & 1) return GB_EINVAL;
-            k_synth_q8_0<<<grid, 256, 0, st>>>(B, nblocks, seed, stream_id); break;
+            if (reinterpret_cast<uintptr_t>(out) & 1) return GB_EINVAL;
+            k_synth_map<GB_DT_Q8_0><<<grid, 256, 0, st>>>(B, n, seed, stream_id, m); break;
         default: return GB_EINVAL;
     }
     return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
+}
+}  // namespace gb
+
+extern "C" int gb_synth_blocks(int dtype, void* blocks, size_t nblocks, uint64_t seed, uint64_t stream_id,
+                               void* stream) {
+    if (!blocks) return GB_EINVAL;
+    return gb::synth_blocks_shard(dtype, blocks, 1, nblocks, nblocks, 0, nblocks, 0, seed, stream_id,
+                                  static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int gb_synth_normal(float* out, size_t n, uint64_t seed, uint64_t stream_id, void* stream) {

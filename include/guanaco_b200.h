@@ -185,6 +185,25 @@ enum { GB_WQ = 0, GB_WK, GB_WV, GB_WO, GB_WGATE, GB_WUP, GB_WDOWN, GB_NMAT };
 
 /* Allocate activations, KV cache, RoPE table and workspaces on the current
  * device.  Weights are attached separately. */
+/* Tensor-parallel slice `rank` of `world` (1..8) GPUs, one process per GPU:
+ * q / k / v rows and wo columns of this rank's n_heads / world query heads and
+ * n_kv_heads / world KV heads (attention and its KV cache stay local), gate /
+ * up rows and ffn_down columns of its ff_dim / world FFN slice, output-head
+ * rows [vocab_off, vocab_off + vocab_rows).  After wo and ffn_down the ranks'
+ * partial hidden vectors are summed over NVLink peer memory (in rank order:
+ * every rank holds the same hidden state); the greedy token is the best of the
+ * ranks' slices.  A Q6_K ffn_down shard is stored with its rows padded to a
+ * multiple of 8 blocks (zero blocks after the shard's columns).  Requires
+ * n_kv_heads % world == 0, ff_dim % (256 * world) == 0 and
+ * (n_heads / world * head_dim) % 256 == 0.  Before decoding, exchange the
+ * ranks' handles: gb_model_comm_handle on every rank, then gb_model_comm_open
+ * with all world handles (GB_IPC_HANDLE_BYTES each, in rank order).  Every
+ * rank must run the same sequence of decode calls (the exchanges pair them). */
+gb_model* gb_model_create_tp(const gb_model_config* cfg, int rank, int world);
+#define GB_IPC_HANDLE_BYTES 64
+int gb_model_comm_handle(gb_model* m, void* handle);
+int gb_model_comm_open(gb_model* m, const void* handles);
+int gb_model_tp_info(const gb_model* m, int* rank, int* world, int* vocab_off, int* vocab_rows);
 gb_model* gb_model_create(const gb_model_config* cfg);
 void gb_model_destroy(gb_model* m);
 
@@ -214,6 +233,7 @@ int gb_model_decode(gb_model* m, const int* d_token, const int* d_pos, float* d_
 /* Same step with host token/position in and host next token (and optionally
  * host logits) out: the end-to-end entry point. */
 int gb_model_decode_host(gb_model* m, int token, int pos, int* h_next, float* h_logits);
+/* (h_logits / d_logits receive this rank's vocabulary rows; all of them on one GPU.) */
 
 /* Greedy generation entirely on the device: n_steps replays of a graph that
  * runs one decode step and then feeds the argmax back (*d_token = next,

@@ -1,0 +1,91 @@
+"""Tensor-parallel decode on two GPUs: each rank holds its slice of the same
+synthetic model (heads, FFN rows / columns, vocabulary rows), the ranks add
+their partial hidden vectors over NVLink peer memory, and the greedy tokens
+must match the one-GPU model; each rank's logits must match its slice of the
+one-GPU logits.  Skipped with fewer than two GPUs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+# H 2048 keeps every matrix on the tensor-map path; ff 5120 gives each of two
+# ranks 2560 FFN columns, so the Q6_K ffn_down shard needs zero padding
+CFG = dict(hidden_dim=2048, n_heads=16, n_kv_heads=4, n_layers=2, ff_dim=5120, vocab_size=5000, max_seq=64)
+SEED, CTX, STEPS = 4321, 20, 6
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _decode(dm, vocab_rows):
+    toks, logits = [], []
+    tok, pos = 7, CTX
+    for _ in range(STEPS):
+        lg = np.zeros(vocab_rows, np.float32)
+        tok = dm.decode_host(tok, pos, logits=lg)
+        toks.append(tok)
+        logits.append(lg)
+        pos += 1
+    return toks, logits
+
+
+def _worker(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+    import guanaco_b200 as gb
+    torch.cuda.set_device(rank)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        c = CFG
+        dm = gb.DecodeModel(c["hidden_dim"], c["n_heads"], c["n_kv_heads"], c["n_layers"], c["ff_dim"],
+                            c["vocab_size"], c["max_seq"], tp_rank=rank, tp_world=world)
+        dm.exchange_handles(dist)
+        dm.synthesize(SEED)
+        dm.fill_kv(CTX, SEED)
+        _, _, off, n = dm.tp_info()
+        toks, logits = _decode(dm, n)
+        assert dm.error() == 0
+        q.put((rank, off, toks, logits))
+        dist.barrier()
+        dm.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2])
+def test_tp_decode_matches_one_gpu(gb, cuda, world):
+    if cuda.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    c = CFG
+    ref = gb.DecodeModel(c["hidden_dim"], c["n_heads"], c["n_kv_heads"], c["n_layers"], c["ff_dim"],
+                         c["vocab_size"], c["max_seq"])
+    try:
+        ref.synthesize(SEED)
+        ref.fill_kv(CTX, SEED)
+        toks_ref, logits_ref = _decode(ref, c["vocab_size"])
+    finally:
+        ref.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, off, toks, logits in got:
+        assert toks == toks_ref, (rank, toks, toks_ref)
+        for step, (lg, lr) in enumerate(zip(logits, logits_ref)):
+            sl = lr[off:off + len(lg)]
+            assert np.linalg.norm(lg - sl) / np.linalg.norm(sl) <= 1e-3, (rank, step)
