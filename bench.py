@@ -254,8 +254,12 @@ def run_ours(args, rank, world, local_rank):
     K, W = args.steps, args.warmup
     c = LLAMA8B
     max_seq = CTX + 2 * (W + K) + 64
+    # N > 1: tensor parallelism (one token stream, each GPU holds 1/N of the
+    # weights and KV); the ranks add partial hidden vectors over NVLink
     dm = gb.DecodeModel(c["hidden_dim"], c["n_heads"], c["n_kv_heads"], c["n_layers"], c["ff_dim"],
-                        c["vocab_size"], max_seq)
+                        c["vocab_size"], max_seq, tp_rank=rank, tp_world=world)
+    if world > 1:
+        dm.exchange_handles(dist)
     dm.synthesize(SEED)
     dm.fill_kv(CTX, SEED)
     st = torch.cuda.Stream()
@@ -287,11 +291,15 @@ def run_ours(args, rank, world, local_rank):
     if dm.error() != 0:
         raise RuntimeError(f"decode error {dm.error()}")
     if args.decode_only:   # profiling runs: the timed decode steps only
+        if dist:
+            dist.barrier()
         dm.close()
+        if dist:
+            dist.destroy_process_group()
         if rank == 0:
             print(json.dumps({"decode_only": True, "ms_per_step": round(t_ms / K, 4)}), flush=True)
         return None
-    tokens = world * K
+    tokens = K   # one token stream, whatever the number of GPUs
     value = tokens / (t_ms / 1e3)
     ms_per_step = t_ms / K
 
@@ -312,13 +320,19 @@ def run_ours(args, rank, world, local_rank):
         tt = torch.tensor([t_e2e], dtype=torch.float64, device="cuda")
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         t_e2e = float(tt.item())
-    e2e = world * K / t_e2e
+    e2e = K / t_e2e
 
-    step_bytes = dm.step_bytes(pos_timed0 + K // 2)
+    step_bytes = dm.step_bytes(pos_timed0 + K // 2)   # this rank's share
+    if dist:
+        sb = torch.tensor([step_bytes], dtype=torch.float64, device="cuda")
+        dist.all_reduce(sb)
+        step_bytes = float(sb.item())
     kernels, main = (None, None)
     if rank == 0:
         kernels, main = kernel_benchmarks(gb, torch, dm, peak)
     launches = dm.launches_per_step() * K + K   # + the feedback kernel per step
+    if dist:
+        dist.barrier()   # every rank is done with the peers' exchange buffers
     dm.close()
 
     line = None
@@ -335,14 +349,16 @@ def run_ours(args, rank, world, local_rank):
                                  "Q4_K matvec uses all cores, Q6_K is single-threaded in the reference"}
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": K,
-            "warmup": W, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak",
+            "warmup": W, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+            "scaling": "strong" if world > 1 else "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init weights, ~N(0,1) KV fill)",
-            "config": {"workload": "llama3.1-8b-q4km-decode (BASELINE config 4)", "global_batch": world,
-                       "seq_len": CTX, "parallelism": f"replicas{world}" if world > 1 else "single",
+            "config": {"workload": "llama3.1-8b-q4km-decode (BASELINE config 4)", "global_batch": 1,
+                       "seq_len": CTX, "parallelism": f"tp{world}" if world > 1 else "single",
                        "weights": "Q4_K + Q6_K(attn_v, ffn_down, output)", "kv": "fp32 head-major",
                        "l2": "weights 4.9 GB stream every step (> 126 MB L2); no flush needed",
                        "positions": [pos_timed0, pos_timed0 + K - 1],
-                       "step_alg_bytes": round(step_bytes), "step_hbm_frac": round(step_bytes / (t_ms / K * 1e-3) / 1e9 / peak, 3)},
+                       "step_alg_bytes": round(step_bytes),
+                       "step_hbm_frac": round(step_bytes / world / (t_ms / K * 1e-3) / 1e9 / peak, 3)},
             "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4,
                     "api": "gb_model_decode_host (token, pos in; next token out)"},
             "gpu_launches": launches,

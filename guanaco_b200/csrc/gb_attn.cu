@@ -313,18 +313,34 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
     if (!last) return;
     __threadfence();
     const float* base = part + (size_t)kvh * grid_splits * GROUP * (HD + 2);
-    for (int e = tid; e < GROUP * HD; e += ATTN_THREADS) {
-        const int h = e / HD, d = e % HD;
+    // split weights w_j = exp(m_j - M) and L = sum l_j w_j once per head (one
+    // warp per head), then every output is a weighted sum over the splits in
+    // split order; S (dead) holds the weights [GROUP][nsplit]
+    float* wbuf = S;
+    if (warp < GROUP) {
+        const int h = warp;
         float M = -INFINITY;
-        for (int j = 0; j < nsplit; j++) M = fmaxf(M, __ldcg(base + ((size_t)j * GROUP + h) * (HD + 2)));
-        float L = 0.f, O = 0.f;
-        for (int j = 0; j < nsplit; j++) {
+        for (int j = lane; j < nsplit; j += 32) M = fmaxf(M, __ldcg(base + ((size_t)j * GROUP + h) * (HD + 2)));
+        M = warp_max(M);
+        float L = 0.f;
+        for (int j = lane; j < nsplit; j += 32) {
             const float* pj = base + ((size_t)j * GROUP + h) * (HD + 2);
             const float w = expf(__ldcg(pj) - M);
+            wbuf[h * nsplit + j] = w;
             L = fmaf(__ldcg(pj + 1), w, L);
-            O = fmaf(__ldcg(pj + 2 + d), w, O);
         }
-        out[(size_t)(kvh * GROUP + h) * HD + d] = O / L;
+        L = warp_sum(L);
+        if (lane == 0) st[8 + h] = L;
+    }
+    __syncthreads();
+    for (int e = tid; e < GROUP * HD; e += ATTN_THREADS) {
+        const int h = e / HD, d = e % HD;
+        const float* wj = wbuf + h * nsplit;
+        const float* pj = base + (size_t)h * (HD + 2) + 2 + d;
+        float O = 0.f;
+#pragma unroll 8
+        for (int j = 0; j < nsplit; j++) O = fmaf(__ldcg(pj + (size_t)j * GROUP * (HD + 2)), wj[j], O);
+        out[(size_t)(kvh * GROUP + h) * HD + d] = O / st[8 + h];
     }
     if (tid == 0) tickets[kvh] = 0u;   // every split has arrived: safe to rearm
 }
@@ -356,6 +372,8 @@ static int attn_dispatch(const float* q, const float* k, const float* v, float* 
                          const int* d_pos, int n_heads, int n_kv, int head_dim, int max_seq, float* out,
                          float* part, unsigned* tickets, unsigned* err, cudaStream_t st) {
     const int group = n_heads / n_kv;
+    // the merge keeps one weight per (head, split) in the score buffer
+    if ((size_t)group * attn_grid_splits(n_kv, max_seq) > (size_t)ATTN_MAX_P * 8) return GB_ELIMIT;
     cudaError_t e = cudaErrorInvalidValue;
 #define GB_ATTN_CASE(HDV, GV)                                                                                       \
     if (head_dim == HDV && group == GV)                                                                             \
