@@ -229,22 +229,26 @@ static const MvPlan* plan_for(Ctx* c, int dtype, const void* dW, int rows, int c
             return nullptr;
         }
     }
-    const size_t need = mv_ws_bytes(p);
-    if (need > c->mv_ws_size) {
-        if (c->mv_ws) {
-            cudaStreamSynchronize(c->st);
-            cudaFree(c->mv_ws);
-            c->mv_ws = nullptr;
-            c->mv_ws_size = 0;
-        }
-        if (cudaMalloc(&c->mv_ws, need) != cudaSuccess || cudaMemsetAsync(c->mv_ws, 0, need, c->st) != cudaSuccess) {
-            *rc = GB_ENOMEM;
-            return nullptr;
-        }
-        c->mv_ws_size = need;
-    }
     *rc = GB_OK;
     return &p;
+}
+
+// Grow the context's matvec workspace (zeroed in stream order) to `need`.
+static int ensure_mv_ws(Ctx* c, size_t need) {
+    if (need <= c->mv_ws_size) return GB_OK;
+    if (c->mv_ws) {
+        cudaStreamSynchronize(c->st);
+        cudaFree(c->mv_ws);
+        c->mv_ws = nullptr;
+        c->mv_ws_size = 0;
+    }
+    if (cudaMalloc(&c->mv_ws, need) != cudaSuccess) {
+        c->mv_ws = nullptr;
+        return GB_ENOMEM;
+    }
+    if (cudaMemsetAsync(c->mv_ws, 0, need, c->st) != cudaSuccess) return GB_ECUDA;
+    c->mv_ws_size = need;
+    return GB_OK;
 }
 
 // FNV-1a over 64 words spread evenly through the buffer (and its last word).
@@ -396,6 +400,7 @@ extern "C" int cuda_transformer_layer_gpu(
     LayerArgs a;
     for (int i = 0; i < GB_NMAT; i++)
         if (!(a.mv[i] = plan_for(c, D[i], W[i], R[i], Cc[i], &rc))) return rc;
+    if ((rc = ensure_mv_ws(c, layer_ws_bytes(a.mv)))) return rc;
     a.mv_ws = c->mv_ws;
     a.ra = ra; a.rf = rf; a.kc = L->k; a.vc = L->v; a.rope = c->rope; a.d_pos = c->d_pos; a.attn_ws = c->ws;
     a.hidden = c->hidden; a.xn = c->xn; a.q = c->q; a.k = c->k; a.v = c->v; a.attn = c->attn;

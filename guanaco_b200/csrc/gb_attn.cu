@@ -108,6 +108,7 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
               float* __restrict__ out, float* __restrict__ part, unsigned* __restrict__ tickets,
               unsigned* __restrict__ err) {
     using C = AttnCfg<HD, GROUP>;
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // wo may start its weight prefetch
     extern __shared__ __align__(16) float sm[];
     float* qs = sm;                       // [GROUP][HD] rotated q
     float* kn = qs + GROUP * HD;          // [HD] rotated new k

@@ -45,6 +45,12 @@ struct MvXform {
 };
 int mv_launch(const MvPlan& p, const float* x, float* y, const float* residual, void* ws, cudaStream_t st,
               bool pdl, const MvXform* xf = nullptr);
+// Several matrices that share x as one launch (TMA plans of one format, one
+// column count and ring depth; at most 3): ys[i] = W_i x (+ res[i]).
+bool mv_groupable(const MvPlan* const* ps, int n);
+size_t mv_ws_bytes_group(const MvPlan* const* ps, int n);
+int mv_launch_group(const MvPlan* const* ps, int n, const float* x, float* const* ys, const float* const* res,
+                    void* ws, cudaStream_t st, bool pdl, const MvXform* xf = nullptr);
 
 // Tensor-parallel context of a layer (world > 1): the wo and ffn_down
 // matvecs write this rank's partial to `part`, then an all-reduce over peer
@@ -77,6 +83,8 @@ struct LayerArgs {
     float eps;
 };
 int enqueue_layer(const LayerArgs& a, cudaStream_t st);
+// Matvec workspace one layer's launches need (grouped launches included).
+size_t layer_ws_bytes(const MvPlan* const* mv);
 int embed(const void* emb, int dtype, const int* d_token, int vocab, int H, float* out, unsigned* err,
           cudaStream_t st, unsigned long long* step = nullptr);
 int set_device_int(int* p, int v, cudaStream_t st);

@@ -41,6 +41,7 @@ __device__ __forceinline__ float block_sum_1024(float v, float* sh) {
 // out = w * (x * r), r = 1/sqrt(sum(x^2)/n + eps)  (kernels_cpu.c:242-263)
 __global__ void __launch_bounds__(1024) k_rmsnorm(const float* __restrict__ x, const float* __restrict__ w,
                                                   float* __restrict__ out, int n, float eps) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // successors may start their weight prefetch
     __shared__ float sh[33];
     float ss = 0.f;
     for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
@@ -52,6 +53,7 @@ __global__ void __launch_bounds__(1024) k_rmsnorm(const float* __restrict__ x, c
 
 // gate = (gate * (1/(1+exp(-gate)))) * up  (kernels_cpu.c:323-336, 381-384)
 __global__ void k_silu_mul(float* __restrict__ g, const float* __restrict__ u, int n) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // successors may start their weight prefetch
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const float x = g[i];
@@ -69,6 +71,7 @@ constexpr size_t AM_WS_BYTES = AM_MAX_CTAS * sizeof(ArgPart) + 16;
 __global__ void __launch_bounds__(1024) k_argmax_split(const float* __restrict__ x, int n, int* __restrict__ out,
                                                        ArgPart* __restrict__ part, unsigned* __restrict__ ticket,
                                                        ArgPart* __restrict__ result, int off) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // successors may start their weight prefetch
     __shared__ float sv[32];
     __shared__ int si[32];
     __shared__ bool last;
@@ -153,6 +156,7 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ x, in
 // Q4_K d1*q - m1 -- bit-exact with the reference dequantiser.
 __global__ void k_embed(const void* __restrict__ emb, int dtype, const int* __restrict__ d_token, int vocab, int H,
                         float* __restrict__ out, unsigned* __restrict__ err, unsigned long long* __restrict__ step) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // successors may start their weight prefetch
     if (step && blockIdx.x == 0 && threadIdx.x == 0) *step += 1;   // epochs of this step's exchanges
     const int tok = *d_token;
     if (tok < 0 || tok >= vocab) {
@@ -236,6 +240,8 @@ __global__ void __launch_bounds__(512) k_tp_allreduce(const float* __restrict__ 
                                                       int H, int rank, int world, void* const* __restrict__ peers,
                                                       const unsigned long long* __restrict__ step, int calls,
                                                       int call, unsigned* __restrict__ err) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // successors may start their weight prefetch
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // successors may start their weight prefetch
     const unsigned ep = (unsigned)(*step * (unsigned long long)calls + call + 1);
     const int par = ep & 1, p = blockIdx.x, tid = threadIdx.x;
     float* dst = static_cast<float*>(peers[p]) + ((size_t)par * world + rank) * H;
@@ -693,10 +699,26 @@ int enqueue_layer(const LayerArgs& a, cudaStream_t st) {
     att.eps = ffn.eps = a.eps;
     swi.mode = MV_X_SILU_MUL;
     swi.x2 = a.up;
+    // matrices that share x and a format run as one launch
+    auto group = [&](const int* which, int n, const float* x, float* const* ys, const MvXform* xf) {
+        const MvPlan* ps[3];
+        for (int i = 0; i < n; i++) ps[i] = a.mv[which[i]];
+        return mv_launch_group(ps, n, x, ys, nullptr, a.mv_ws, st, true, xf);
+    };
     if (tma(GB_WQ) && tma(GB_WK) && tma(GB_WV)) {
-        if ((rc = mv(GB_WQ, a.hidden, a.q, nullptr, &att))) return rc;
-        if ((rc = mv(GB_WK, a.hidden, a.k, nullptr, &att))) return rc;
-        if ((rc = mv(GB_WV, a.hidden, a.v, nullptr, &att))) return rc;
+        const int qkv[3] = {GB_WQ, GB_WK, GB_WV};
+        float* ys[3] = {a.q, a.k, a.v};
+        const MvPlan* ps[3] = {a.mv[GB_WQ], a.mv[GB_WK], a.mv[GB_WV]};
+        if (mv_groupable(ps, 3)) {
+            if ((rc = group(qkv, 3, a.hidden, ys, &att))) return rc;
+        } else if (mv_groupable(ps, 2)) {
+            if ((rc = group(qkv, 2, a.hidden, ys, &att))) return rc;
+            if ((rc = mv(GB_WV, a.hidden, a.v, nullptr, &att))) return rc;
+        } else {
+            if ((rc = mv(GB_WQ, a.hidden, a.q, nullptr, &att))) return rc;
+            if ((rc = mv(GB_WK, a.hidden, a.k, nullptr, &att))) return rc;
+            if ((rc = mv(GB_WV, a.hidden, a.v, nullptr, &att))) return rc;
+        }
     } else {
         if ((rc = gb_rmsnorm(a.hidden, a.ra, a.xn, H, a.eps, st))) return rc;
         if ((rc = mv(GB_WQ, a.xn, a.q, nullptr, nullptr))) return rc;
@@ -714,8 +736,15 @@ int enqueue_layer(const LayerArgs& a, cudaStream_t st) {
         return rc;
     }
     if (tma(GB_WGATE) && tma(GB_WUP)) {
-        if ((rc = mv(GB_WGATE, a.hidden, a.gate, nullptr, &ffn))) return rc;
-        if ((rc = mv(GB_WUP, a.hidden, a.up, nullptr, &ffn))) return rc;
+        const int gu[2] = {GB_WGATE, GB_WUP};
+        float* ys[2] = {a.gate, a.up};
+        const MvPlan* ps[2] = {a.mv[GB_WGATE], a.mv[GB_WUP]};
+        if (mv_groupable(ps, 2)) {
+            if ((rc = group(gu, 2, a.hidden, ys, &ffn))) return rc;
+        } else {
+            if ((rc = mv(GB_WGATE, a.hidden, a.gate, nullptr, &ffn))) return rc;
+            if ((rc = mv(GB_WUP, a.hidden, a.up, nullptr, &ffn))) return rc;
+        }
     } else {
         if ((rc = gb_rmsnorm(a.hidden, a.rf, a.xn, H, a.eps, st))) return rc;
         if ((rc = mv(GB_WGATE, a.xn, a.gate, nullptr, nullptr))) return rc;
@@ -731,6 +760,17 @@ int enqueue_layer(const LayerArgs& a, cudaStream_t st) {
     }
     if (rc || !tp) return rc;
     return tp_allreduce(*a.tp, a.hidden, H, 2 * a.layer + 1, st);
+}
+
+size_t layer_ws_bytes(const MvPlan* const* mv) {
+    size_t need = 0;
+    for (int i = 0; i < GB_NMAT; i++) need = std::max(need, mv_ws_bytes(*mv[i]));
+    const MvPlan* qkv[3] = {mv[GB_WQ], mv[GB_WK], mv[GB_WV]};
+    const MvPlan* gu[2] = {mv[GB_WGATE], mv[GB_WUP]};
+    need = std::max(need, mv_ws_bytes_group(qkv, 3));
+    need = std::max(need, mv_ws_bytes_group(qkv, 2));
+    need = std::max(need, mv_ws_bytes_group(gu, 2));
+    return need;
 }
 
 int embed(const void* emb, int dtype, const int* d_token, int vocab, int H, float* out, unsigned* err, cudaStream_t st,
@@ -802,7 +842,11 @@ static bool model_ready(gb_model* m) {
     for (int l = 0; l < m->c.n_layers; l++) if (!m->ra[l] || !m->rf[l]) return false;
     if (!(m->emb && m->lm && m->rms_final)) return false;
     size_t need = mv_ws_bytes(m->lm_plan);
-    for (const MvPlan& p : m->plan) need = mv_ws_bytes(p) > need ? mv_ws_bytes(p) : need;
+    for (int l = 0; l < m->c.n_layers; l++) {
+        const MvPlan* mv[GB_NMAT];
+        for (int i = 0; i < GB_NMAT; i++) mv[i] = &m->plan[(size_t)l * GB_NMAT + i];
+        need = std::max(need, layer_ws_bytes(mv));
+    }
     if (need > m->mv_ws_size) {
         void* p = dalloc(m, need);
         if (!p || cudaMemsetAsync(p, 0, need, m->stream) != cudaSuccess ||
@@ -914,10 +958,19 @@ extern "C" int gb_model_launches_per_step(const gb_model* m) {
     if (!m) return 0;
     int n = 1;
     for (int l = 0; l < m->c.n_layers; l++) {
-        auto tma = [&](int w) { return m->plan[(size_t)l * GB_NMAT + w].kind == MV_TMA; };
-        n += 8;
-        n += (tma(GB_WQ) && tma(GB_WK) && tma(GB_WV)) ? 0 : 1;
-        n += (tma(GB_WGATE) && tma(GB_WUP)) ? 0 : 1;
+        auto P = [&](int w) { return &m->plan[(size_t)l * GB_NMAT + w]; };
+        auto tma = [&](int w) { return P(w)->kind == MV_TMA; };
+        const MvPlan* qkv[3] = {P(GB_WQ), P(GB_WK), P(GB_WV)};
+        const MvPlan* gu[2] = {P(GB_WGATE), P(GB_WUP)};
+        n += 1 + 1 + 1;   // attention, wo, ffn_down
+        if (tma(GB_WQ) && tma(GB_WK) && tma(GB_WV))
+            n += mv_groupable(qkv, 3) ? 1 : (mv_groupable(qkv, 2) ? 2 : 3);
+        else
+            n += 4;   // RMSNorm + three matvecs
+        if (tma(GB_WGATE) && tma(GB_WUP))
+            n += mv_groupable(gu, 2) ? 1 : 2;
+        else
+            n += 3;
         n += tma(GB_WDOWN) ? 0 : 1;
     }
     n += m->lm_plan.kind == MV_TMA ? 1 : 2;

@@ -683,13 +683,20 @@ __device__ __forceinline__ void mt_consumer_sync() {
 __device__ __forceinline__ int mt_start(int c, int T, int n) { return (int)((long long)c * T / n); }
 __device__ __forceinline__ int mt_owner(int t, int T, int n) { return (int)(((long long)(t + 1) * n - 1) / T); }
 
+// Up to MT_MAXM matrices of one format and one column count that share x run
+// as one launch: their (group, chunk) stage items are concatenated, matrix m
+// owning the global 32-row groups [gbase[m], gbase[m + 1]).
+constexpr int MT_MAXM = 3;
 struct MtArgs {
     const float* x;
-    float* y;
-    const float* residual;
+    float* y[MT_MAXM];
+    const float* residual[MT_MAXM];
+    int rows[MT_MAXM];
+    int gbase[MT_MAXM + 1];
+    int nm;
     float* part;        // [ncta][2][MT_GR] stream-K partial rows
-    unsigned* tickets;  // [ngroups], zero between launches
-    int rows, nb, nch, T, ncta, S;
+    unsigned* tickets;  // [total groups], zero between launches
+    int nb, nch, T, ncta, S;
     int unit;           // split granularity in stage items: 1, or nch (whole groups, no workspace)
     // x transform applied while quantising (MV_X_*): RMSNorm with weight nw
     // and eps, or silu(x) * x2
@@ -997,8 +1004,13 @@ struct MtQ6K {
     }
 };
 
+// matrix of global group g
+__device__ __forceinline__ int mt_matrix(const MtArgs& a, int g) { return g >= a.gbase[1] ? (g >= a.gbase[2] ? 2 : 1) : 0; }
+
 template <class F>
-__global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_constant__ CUtensorMap tmap, const MtArgs a) {
+__global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_constant__ CUtensorMap tm0,
+                                                            const __grid_constant__ CUtensorMap tm1,
+                                                            const __grid_constant__ CUtensorMap tm2, const MtArgs a) {
     constexpr int MT_NC = F::NC;
     extern __shared__ __align__(1024) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1036,8 +1048,10 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
             for (int i = 0; i < n_it; i++) {
                 const int s = i % S;
                 if (i >= S && !(ok = mbs_wait(bar_empty + 8 * s, ((i / S) - 1) & 1))) break;
+                const int m = mt_matrix(a, grp);
+                const CUtensorMap* tm = m == 0 ? &tm0 : (m == 1 ? &tm1 : &tm2);
                 mbs_expect(bar_full + 8 * s, F::STG);
-                tma_load_3d(sbase + s * F::STG, &tmap, 0, grp * MT_GR, ch * F::ZSTEP, bar_full + 8 * s);
+                tma_load_3d(sbase + s * F::STG, tm, 0, (grp - a.gbase[m]) * MT_GR, ch * F::ZSTEP, bar_full + 8 * s);
                 if (++ch == nch) { ch = 0; grp++; }
             }
             // do not retire while a box is still landing in this CTA's ring
@@ -1103,9 +1117,12 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
                 __syncwarp();
                 if (lane == 0) cnt[slot] = 0;
                 const int gs = grp * nch;
-                const int row = grp * MT_GR + lane;
+                const int m = mt_matrix(a, grp);
+                const int row = (grp - a.gbase[m]) * MT_GR + lane;
+                float* const ym = a.y[m];
+                const float* const rm = a.residual[m];
                 if (gs >= t0 && gs + nch <= t1) {
-                    if (row < a.rows) a.y[row] = v + (a.residual ? a.residual[row] : 0.f);
+                    if (row < a.rows[m]) ym[row] = v + (rm ? rm[row] : 0.f);
                 } else {
                     const int half = grp == first_grp ? 0 : 1;
                     a.part[(c0 * 2 + half) * MT_GR + lane] = v;
@@ -1121,7 +1138,7 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
                             const int h2 = grp == mt_start(c2, a.T, a.ncta) / nch ? 0 : 1;
                             u += __ldcg(a.part + (c2 * 2 + h2) * MT_GR + lane);
                         }
-                        if (row < a.rows) a.y[row] = u + (a.residual ? a.residual[row] : 0.f);
+                        if (row < a.rows[m]) ym[row] = u + (rm ? rm[row] : 0.f);
                         if (lane == 0) a.tickets[grp] = 0u;
                     }
                 }
@@ -1288,28 +1305,61 @@ static bool pdl_allowed() {
     return ok;
 }
 
+static int mv_check_xform(const MvXform* xf, bool tma) {
+    const int xmode = xf ? xf->mode : MV_X_NONE;
+    if (xmode == MV_X_NONE) return GB_OK;
+    if (!tma) return GB_EINVAL;   // transforms run in the TMA kernels' x quantiser only
+    const float* other = xmode == MV_X_RMSNORM ? xf->w : xf->x2;
+    if (!other || (reinterpret_cast<uintptr_t>(other) & 15)) return GB_EINVAL;
+    return GB_OK;
+}
+
 int mv_launch(const MvPlan& p, const float* x, float* y, const float* residual, void* ws, cudaStream_t st, bool pdl,
               const MvXform* xf) {
     if (!x || !y) return GB_EINVAL;
     if (reinterpret_cast<uintptr_t>(x) & 15) return GB_EINVAL;
-    const int xmode = xf ? xf->mode : MV_X_NONE;
-    if (xmode != MV_X_NONE) {   // transforms run in the TMA kernels' x quantiser only
-        if (p.kind != MV_TMA) return GB_EINVAL;
-        const float* other = xmode == MV_X_RMSNORM ? xf->w : xf->x2;
-        if (!other || (reinterpret_cast<uintptr_t>(other) & 15)) return GB_EINVAL;
+    if (p.kind == MV_TMA) {
+        const MvPlan* ps[1] = {&p};
+        float* ys[1] = {y};
+        const float* rs[1] = {residual};
+        return mv_launch_group(ps, 1, x, ys, rs, ws, st, pdl, xf);
     }
-    if (p.kind == MV_RING) {
-        MvGeom g;
-        if (!choose_geom(p.dtype, p.rows, p.nb, &g)) return GB_ELIMIT;
-        static unsigned conf[3] = {0, 0, 0};
-        cudaError_t e;
-        switch (p.dtype) {
-            case GB_DT_Q4_K: e = launch_kernel(k_mv_q4k, p.W, p.rows, p.nb, x, y, residual, g, st, &conf[0]); break;
-            case GB_DT_Q6_K: e = launch_kernel(k_mv_q6k, p.W, p.rows, p.nb, x, y, residual, g, st, &conf[1]); break;
-            default: e = launch_kernel(k_mv_q8_0, p.W, p.rows, p.nb, x, y, residual, g, st, &conf[2]); break;
-        }
-        return e == cudaSuccess ? GB_OK : GB_ECUDA;
+    int rc = mv_check_xform(xf, false);
+    if (rc) return rc;
+    MvGeom g;
+    if (!choose_geom(p.dtype, p.rows, p.nb, &g)) return GB_ELIMIT;
+    static unsigned conf[3] = {0, 0, 0};
+    cudaError_t e;
+    switch (p.dtype) {
+        case GB_DT_Q4_K: e = launch_kernel(k_mv_q4k, p.W, p.rows, p.nb, x, y, residual, g, st, &conf[0]); break;
+        case GB_DT_Q6_K: e = launch_kernel(k_mv_q6k, p.W, p.rows, p.nb, x, y, residual, g, st, &conf[1]); break;
+        default: e = launch_kernel(k_mv_q8_0, p.W, p.rows, p.nb, x, y, residual, g, st, &conf[2]); break;
     }
+    return e == cudaSuccess ? GB_OK : GB_ECUDA;
+}
+
+bool mv_groupable(const MvPlan* const* ps, int n) {
+    if (n < 1 || n > MT_MAXM) return false;
+    for (int i = 0; i < n; i++)
+        if (ps[i]->kind != MV_TMA || ps[i]->dtype != ps[0]->dtype || ps[i]->nb != ps[0]->nb || ps[i]->S != ps[0]->S)
+            return false;
+    return true;
+}
+
+size_t mv_ws_bytes_group(const MvPlan* const* ps, int n) {
+    if (!mv_groupable(ps, n)) return 0;
+    size_t groups = 0;
+    for (int i = 0; i < n; i++) groups += (size_t)ps[i]->ngroups;
+    return (size_t)GB_NUM_SMS * 2 * MT_GR * sizeof(float) + (groups * sizeof(unsigned) + 255) / 256 * 256;
+}
+
+int mv_launch_group(const MvPlan* const* ps, int n, const float* x, float* const* ys, const float* const* res,
+                    void* ws, cudaStream_t st, bool pdl, const MvXform* xf) {
+    if (!x || !ys || !mv_groupable(ps, n)) return GB_EINVAL;
+    if (reinterpret_cast<uintptr_t>(x) & 15) return GB_EINVAL;
+    int rc = mv_check_xform(xf, true);
+    if (rc) return rc;
+    const MvPlan& p = *ps[0];
     static unsigned configured[2] = {0, 0};
     const bool q6 = p.dtype == GB_DT_Q6_K;
     int dev = 0;
@@ -1319,23 +1369,33 @@ int mv_launch(const MvPlan& p, const float* x, float* y, const float* residual, 
                                          MV_SMEM_MAX));
         configured[q6] |= 1u << (dev & 31);
     }
-    MtArgs a;
+    MtArgs a = {};
     a.x = x;
-    a.y = y;
-    a.residual = residual;
+    a.nm = n;
+    a.gbase[0] = 0;
+    for (int i = 0; i < MT_MAXM; i++) {
+        const bool on = i < n;
+        if (on && !ys[i]) return GB_EINVAL;
+        a.y[i] = on ? ys[i] : nullptr;
+        a.residual[i] = on && res ? res[i] : nullptr;
+        a.rows[i] = on ? ps[i]->rows : 0;
+        a.gbase[i + 1] = a.gbase[i] + (on ? ps[i]->ngroups : 0);
+    }
+    const int groups = a.gbase[MT_MAXM];
     a.part = static_cast<float*>(ws);
-    a.tickets = reinterpret_cast<unsigned*>(static_cast<char*>(ws) + (size_t)GB_NUM_SMS * 2 * MT_GR * sizeof(float));
-    a.rows = p.rows;
+    a.tickets = ws ? reinterpret_cast<unsigned*>(static_cast<char*>(ws) + (size_t)GB_NUM_SMS * 2 * MT_GR * sizeof(float))
+                   : nullptr;
     a.nb = p.nb;
     a.nch = p.nch;
-    a.T = p.T;
-    a.xmode = xmode;
-    a.nw = xmode == MV_X_RMSNORM ? xf->w : nullptr;
-    a.x2 = xmode == MV_X_SILU_MUL ? xf->x2 : nullptr;
+    a.T = groups * p.nch;
+    a.xmode = xf ? xf->mode : MV_X_NONE;
+    a.nw = a.xmode == MV_X_RMSNORM ? xf->w : nullptr;
+    a.x2 = a.xmode == MV_X_SILU_MUL ? xf->x2 : nullptr;
     a.eps = xf ? xf->eps : 0.f;
     // with a workspace: stream-K over stage items; without: whole groups per CTA
     a.unit = ws ? 1 : p.nch;
-    a.ncta = ws ? p.ncta : (p.ngroups < GB_NUM_SMS ? p.ngroups : GB_NUM_SMS);
+    const int units = ws ? a.T : groups;
+    a.ncta = units < GB_NUM_SMS ? units : GB_NUM_SMS;
     a.S = p.S;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.ncta);
@@ -1347,11 +1407,13 @@ int mv_launch(const MvPlan& p, const float* x, float* y, const float* residual, 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = (pdl && pdl_allowed()) ? 1 : 0;
-    const CUtensorMap* m = reinterpret_cast<const CUtensorMap*>(p.tmap);
+    const CUtensorMap* m0 = reinterpret_cast<const CUtensorMap*>(ps[0]->tmap);
+    const CUtensorMap* m1 = reinterpret_cast<const CUtensorMap*>(ps[n > 1 ? 1 : 0]->tmap);
+    const CUtensorMap* m2 = reinterpret_cast<const CUtensorMap*>(ps[n > 2 ? 2 : 0]->tmap);
     if (q6)
-        GB_CUDA_TRY(cudaLaunchKernelEx(&cfg, k_mvt<MtQ6K>, *m, a));
+        GB_CUDA_TRY(cudaLaunchKernelEx(&cfg, k_mvt<MtQ6K>, *m0, *m1, *m2, a));
     else
-        GB_CUDA_TRY(cudaLaunchKernelEx(&cfg, k_mvt<MtQ4K>, *m, a));
+        GB_CUDA_TRY(cudaLaunchKernelEx(&cfg, k_mvt<MtQ4K>, *m0, *m1, *m2, a));
     return GB_OK;
 }
 
