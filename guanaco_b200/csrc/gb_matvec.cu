@@ -609,19 +609,21 @@ k_mv_q8_0(const uint8_t* __restrict__ W, int rows, int nb, const float* __restri
 }
 
 // ================================================================== TMA path
-// Q4_K with one TMA tensor copy per ring stage.  The matrix is viewed as a
-// 3-D tensor {144-byte block (18 x u64), row, block index} with strides
-// {row_bytes, 144}; one box {18, 32 rows, 16 blocks} lands in shared memory
-// as [block][row][144 B], so every 16-row tile of a block is a dense 2304-byte
-// slab (conflict-free 128-bit reads) and the copy start is always x = 0
-// (16-byte aligned).  Out-of-range rows and blocks are zero-filled by the TMA
-// unit and skipped by the consumers.
+// Weights stream through a ring of shared-memory stages filled by TMA tensor
+// copies.  Q4_K: the matrix is viewed as a 3-D tensor {144-byte block
+// (18 x u64), row, block index} with strides {row_bytes, 144}; one box
+// {18, 32 rows, 1 block} is one split item, and up to 16 of them (consecutive
+// blocks of one 32-row group) fill a stage laid out [block][row][144 B], so
+// every 16-row tile of a block is a dense 2304-byte slab (conflict-free
+// 128-bit reads).  Q6_K: the item is a run of 8 blocks (1680 bytes, the
+// shortest 16-byte multiple) of 32 rows.  Every copy starts at x = 0 (16-byte
+// aligned).  Out-of-range rows are zero-filled by the TMA unit and skipped.
 //
-// Work split (stream-K): the (32-row group, 16-block chunk) stage items are
-// cut into one contiguous range per CTA, so every CTA streams the same number
-// of bytes.  Groups that straddle two CTAs finish through a per-group ticket:
-// each owner writes its partial rows to the workspace and the last one sums
-// the partials in CTA order (deterministic) and writes y.
+// Work split (stream-K): the (32-row group, item) sequence is cut into one
+// contiguous range per CTA, so every CTA streams the same number of bytes
+// to within one item.  Groups that straddle CTAs finish through a per-group
+// ticket: each owner writes its partial rows to the workspace and the last
+// one sums the partials in CTA order (deterministic) and writes y.
 //
 // x is quantised inside every CTA (int8 limb planes + per-32-column scale and
 // sum in shared memory) while the first weight boxes are in flight.  With
@@ -674,17 +676,25 @@ __device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
     asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
     return old;
 }
+__device__ __forceinline__ void red_add_release(unsigned* p, unsigned v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
 template <int NC>
 __device__ __forceinline__ void mt_consumer_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(NC * 32) : "memory");
 }
-// Stage item t of a matrix with nch chunks per group: CTA c owns
+// Split item t of a matrix with nch items per group: CTA c owns
 // [t_start(c), t_start(c + 1)); owner(t) is the CTA whose range holds t.
 __device__ __forceinline__ int mt_start(int c, int T, int n) { return (int)((long long)c * T / n); }
 __device__ __forceinline__ int mt_owner(int t, int T, int n) { return (int)(((long long)(t + 1) * n - 1) / T); }
 
 // Up to MT_MAXM matrices of one format and one column count that share x run
-// as one launch: their (group, chunk) stage items are concatenated, matrix m
+// as one launch: their (group, item) sequences are concatenated, matrix m
 // owning the global 32-row groups [gbase[m], gbase[m + 1]).
 constexpr int MT_MAXM = 3;
 struct MtArgs {
@@ -697,7 +707,7 @@ struct MtArgs {
     float* part;        // [ncta][2][MT_GR] stream-K partial rows
     unsigned* tickets;  // [total groups], zero between launches
     int nb, nch, T, ncta, S;
-    int unit;           // split granularity in stage items: 1, or nch (whole groups, no workspace)
+    int unit;           // split granularity in items: 1, or nch (whole groups, no workspace)
     // x transform applied while quantising (MV_X_*): RMSNorm with weight nw
     // and eps, or silu(x) * x2
     int xmode;
@@ -718,15 +728,25 @@ constexpr int MT_ZERO = 256;   // zero line read by lanes without a B fragment
 // RMSNorm scale 1 / sqrt(mean(x^2) + eps) over the K columns, summed by the
 // consumer threads and combined in fixed warp order (every CTA gets the
 // same value).  scratch: NC floats of shared memory.
+constexpr int MT_XU = 4;   // float4 loads of x in flight per thread
 template <int NC>
 __device__ __forceinline__ float mt_rms_scale(const float* __restrict__ x, int K, float eps, float* scratch, int tid) {
     float ss = 0.f;
-    for (int t = tid; t < K / 4; t += NC * 32) {
-        const float4 v = reinterpret_cast<const float4*>(x)[t];
-        ss = fmaf(v.x, v.x, ss);
-        ss = fmaf(v.y, v.y, ss);
-        ss = fmaf(v.z, v.z, ss);
-        ss = fmaf(v.w, v.w, ss);
+    const int n4 = K / 4;
+    for (int base = tid; base < n4; base += MT_XU * NC * 32) {
+        float4 v[MT_XU];
+#pragma unroll
+        for (int j = 0; j < MT_XU; j++) {
+            const int t = base + j * NC * 32;
+            v[j] = t < n4 ? reinterpret_cast<const float4*>(x)[t] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int j = 0; j < MT_XU; j++) {
+            ss = fmaf(v[j].x, v[j].x, ss);
+            ss = fmaf(v[j].y, v[j].y, ss);
+            ss = fmaf(v[j].z, v[j].z, ss);
+            ss = fmaf(v[j].w, v[j].w, ss);
+        }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
@@ -741,46 +761,74 @@ __device__ __forceinline__ float mt_silu_mul(float g, float u) {
     return __fmul_rn(__fmul_rn(g, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)))), u);
 }
 
+// One float4 of x (columns 4t .. 4t + 3): transform, quantise to two int8
+// limbs per value against the 32-column sub-block's max |x|, and record the
+// sub-block scale and sum.  Lanes 8k .. 8k + 7 of a warp hold one sub-block.
 template <bool S16>
-__device__ __forceinline__ void mt_quantise_x(const MtArgs& a, int K, uint8_t* xq, int tid, int nthr, float rs) {
+__device__ __forceinline__ void mt_quantise4(const MtArgs& a, int K, uint8_t* xq, int t, float4 v, float4 w, float rs) {
     uint32_t* p0 = reinterpret_cast<uint32_t*>(xq);
     uint32_t* p1 = reinterpret_cast<uint32_t*>(xq + K);
     float* f = reinterpret_cast<float*>(xq + 2 * K);
     float* f16 = f + K / 16;
-    for (int t = tid; t < K / 4; t += nthr) {   // 8 lanes (32 columns) per sub-block
-        float4 v = reinterpret_cast<const float4*>(a.x)[t];
-        if (a.xmode == MV_X_RMSNORM) {   // w * (x * r), the reference's rounding
-            const float4 w = reinterpret_cast<const float4*>(a.nw)[t];
-            v = make_float4(__fmul_rn(w.x, __fmul_rn(v.x, rs)), __fmul_rn(w.y, __fmul_rn(v.y, rs)),
-                            __fmul_rn(w.z, __fmul_rn(v.z, rs)), __fmul_rn(w.w, __fmul_rn(v.w, rs)));
-        } else if (a.xmode == MV_X_SILU_MUL) {
-            const float4 u = reinterpret_cast<const float4*>(a.x2)[t];
-            v = make_float4(mt_silu_mul(v.x, u.x), mt_silu_mul(v.y, u.y), mt_silu_mul(v.z, u.z), mt_silu_mul(v.w, u.w));
+    if (a.xmode == MV_X_RMSNORM) {   // w * (x * r), the reference's rounding
+        v = make_float4(__fmul_rn(w.x, __fmul_rn(v.x, rs)), __fmul_rn(w.y, __fmul_rn(v.y, rs)),
+                        __fmul_rn(w.z, __fmul_rn(v.z, rs)), __fmul_rn(w.w, __fmul_rn(v.w, rs)));
+    } else if (a.xmode == MV_X_SILU_MUL) {
+        v = make_float4(mt_silu_mul(v.x, w.x), mt_silu_mul(v.y, w.y), mt_silu_mul(v.z, w.z), mt_silu_mul(v.w, w.w));
+    }
+    float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    float sm = (v.x + v.y) + (v.z + v.w);
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    sm += __shfl_xor_sync(0xffffffffu, sm, 1);
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    sm += __shfl_xor_sync(0xffffffffu, sm, 2);
+    if (S16 && (t & 3) == 0) {   // 16-column sum: column c0 = 4t = 256 b + 128 n + 32 G + 16 h
+        const int c0 = 4 * t, b = c0 >> 8, n = (c0 >> 7) & 1, G = (c0 >> 5) & 3, h = (c0 >> 4) & 1;
+        f16[b * 16 + h * 8 + 4 * n + G] = sm;
+    }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    sm += __shfl_xor_sync(0xffffffffu, sm, 4);
+    const float inv = mx > 0.f ? 127.f / mx : 0.f;
+    int a0, a1, b0, b1, c0, c1, d0, d1;
+    limbs(v.x * inv, a0, a1);
+    limbs(v.y * inv, b0, b1);
+    limbs(v.z * inv, c0, c1);
+    limbs(v.w * inv, d0, d1);
+    p0[t] = pack4(a0, b0, c0, d0);
+    p1[t] = pack4(a1, b1, c1, d1);
+    const int sb = t >> 3;
+    if ((t & 7) == 0) {
+        f[(sb >> 1) * 4 + (sb & 1)] = mx / 127.f;
+        f[(sb >> 1) * 4 + 2 + (sb & 1)] = sm;
+    }
+}
+
+// Quantise x into shared memory.  The loads of MT_XU float4 per thread (and
+// of the transform's second operand) are issued before any is used, so the
+// L2 latency is paid once per MT_XU float4 rather than once per float4.
+// nthr is a multiple of 32 and K / 4 of 64, so the bounds test is
+// warp-uniform and the shuffles see full warps.
+template <bool S16>
+__device__ __forceinline__ void mt_quantise_x(const MtArgs& a, int K, uint8_t* xq, int tid, int nthr, float rs) {
+    const int n4 = K / 4;
+    const float4* x4 = reinterpret_cast<const float4*>(a.x);
+    const float4* w4 = reinterpret_cast<const float4*>(a.xmode == MV_X_RMSNORM ? a.nw : a.x2);
+    const bool aux = a.xmode != MV_X_NONE;
+    for (int base = tid; base < n4; base += MT_XU * nthr) {
+        float4 v[MT_XU], w[MT_XU];
+#pragma unroll
+        for (int j = 0; j < MT_XU; j++) {
+            const int t = base + j * nthr;
+            v[j] = w[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (t < n4) {
+                v[j] = x4[t];
+                if (aux) w[j] = w4[t];
+            }
         }
-        float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-        float sm = (v.x + v.y) + (v.z + v.w);
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        sm += __shfl_xor_sync(0xffffffffu, sm, 1);
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        sm += __shfl_xor_sync(0xffffffffu, sm, 2);
-        if (S16 && (t & 3) == 0) {   // 16-column sum: column c0 = 4t = 256 b + 128 n + 32 G + 16 h
-            const int c0 = 4 * t, b = c0 >> 8, n = (c0 >> 7) & 1, G = (c0 >> 5) & 3, h = (c0 >> 4) & 1;
-            f16[b * 16 + h * 8 + 4 * n + G] = sm;
-        }
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-        sm += __shfl_xor_sync(0xffffffffu, sm, 4);
-        const float inv = mx > 0.f ? 127.f / mx : 0.f;
-        int a0, a1, b0, b1, c0, c1, d0, d1;
-        limbs(v.x * inv, a0, a1);
-        limbs(v.y * inv, b0, b1);
-        limbs(v.z * inv, c0, c1);
-        limbs(v.w * inv, d0, d1);
-        p0[t] = pack4(a0, b0, c0, d0);
-        p1[t] = pack4(a1, b1, c1, d1);
-        const int sb = t >> 3;
-        if ((t & 7) == 0) {
-            f[(sb >> 1) * 4 + (sb & 1)] = mx / 127.f;
-            f[(sb >> 1) * 4 + 2 + (sb & 1)] = sm;
+#pragma unroll
+        for (int j = 0; j < MT_XU; j++) {
+            const int t = base + j * nthr;
+            if (t < n4) mt_quantise4<S16>(a, K, xq, t, v[j], w[j], rs);
         }
     }
 }
@@ -797,27 +845,34 @@ struct MtLane {
 
 // ---------------------------------------------------------------- Q4_K stage
 // Box {18 x u64, 32 rows, 16 blocks}: shared layout [block][row][144 B].  Warp
-// w takes blocks w and w + 8 of the stage, both 16-row tiles of each.
-struct MtQ4K {
-    static constexpr int NC = 8;         // consumer warps: blocks w and w + 8, both tiles
+// w takes block w of the stage, both 16-row tiles.
+template <int IGV>
+struct MtQ4KT {
+    static constexpr int NC = 16;        // consumer warps: warp w takes block w of the stage, both tiles
     static constexpr int KC = 16;
+    static constexpr int ILP = KC / NC;
     static constexpr int STG = KC * MT_GR * GB_Q4K_BYTES;
     static constexpr bool S16 = false;
     static constexpr int XB_LANE = 64;   // B fragment offset per column group
-    static constexpr int ZSTEP = KC;     // tensor-map z units (blocks) per stage
-    __device__ static __forceinline__ void consume(const uint8_t* stg, int ch, int nb, int warp, const MtLane& L,
+    static constexpr int IG = IGV;       // blocks per split item
+    static constexpr int SI = KC / IG;   // items per full stage
+    static constexpr int ITEM = STG / SI;
+    static constexpr int ZUNIT = 1;      // blocks per tensor-map z unit
+    static constexpr int BOXZ = IG;      // box depth: one box per item
+    // blocks [b0, bend) of the group land at stage blocks 0 .. bend - b0 - 1
+    __device__ static __forceinline__ void consume(const uint8_t* stg, int b0, int bend, int warp, const MtLane& L,
                                                    const uint8_t* xq, int K, float acc_a[2], float acc_b[2]) {
         const int gq = L.gq, c = L.c;
         const float4* xfb = reinterpret_cast<const float4*>(xq + 2 * K) + c;
         const int sh8 = (c & 1) << 4;
         const uint32_t MW = c >= 2 ? 0x0F0Fu : 0u, MY = c >= 2 ? 0x3030u : 0x3F3Fu, SY = c >= 2 ? 2u : 0u;
-        float pa[2][2], pb[2][2];
+        float pa[2][2] = {}, pb[2][2] = {};
 #pragma unroll
-        for (int j = 0; j < 2; j++) {   // blocks warp and warp + 8 of the stage
+        for (int j = 0; j < ILP; j++) {   // block warp (+ NC) of the stage
             const int bl = warp + j * NC;
-            const int b = ch * KC + bl;
+            const int b = b0 + bl;
             pa[j][0] = pa[j][1] = pb[j][0] = pb[j][1] = 0.f;
-            if (b >= nb) continue;
+            if (b >= bend) continue;
             const uint4* xb = reinterpret_cast<const uint4*>(L.xlb + b * L.xstr);
             const uint4 bl0 = xb[0], bl1 = xb[1], bh0 = xb[2], bh1 = xb[3];
             const float4 xf = xfb[b * 4];
@@ -871,6 +926,9 @@ struct MtQ4K {
         }
     }
 };
+// 16-block items: a stage is one box and a 32-row group of a 4096-column
+// matrix is one item, so such launches split by whole groups
+using MtQ4K = MtQ4KT<16>;
 
 // ---------------------------------------------------------------- Q6_K stage
 // Box {210 x u64 = 8 blocks, 32 rows, 1 chunk}: shared layout [row][1680 B];
@@ -914,7 +972,11 @@ struct MtQ6K {
     static constexpr int STG = MT_GR * RB;
     static constexpr bool S16 = true;
     static constexpr int XB_LANE = 8;
-    static constexpr int ZSTEP = 1;      // tensor-map z units (8-block chunks) per stage
+    static constexpr int IG = 8;         // blocks per split item: one 16-byte aligned 1680-byte row run
+    static constexpr int SI = 1;         // items per stage
+    static constexpr int ITEM = STG;
+    static constexpr int ZUNIT = 8;      // blocks per tensor-map z unit
+    static constexpr int BOXZ = 1;
     template <int MIS>
     __device__ static __forceinline__ void tile(const uint8_t* blk_a, int c, const uint8_t* xb, const float* xf,
                                                 const float4 s16lo, const float4 s16hi, float fc, int selsc0,
@@ -991,10 +1053,10 @@ struct MtQ6K {
         const uint8_t* blk = stg + (m * 16 + L.gq) * RB + (warp & 7) * GB_Q6K_BYTES;
         tile<MIS>(blk, c, xb, xf, s16lo, s16hi, fc, selsc0, selsc1, acc_a[m], acc_b[m]);
     }
-    __device__ static __forceinline__ void consume(const uint8_t* stg, int ch, int nb, int warp, const MtLane& L,
+    __device__ static __forceinline__ void consume(const uint8_t* stg, int b0, int bend, int warp, const MtLane& L,
                                                    const uint8_t* xq, int K, float acc_a[2], float acc_b[2]) {
-        const int b = ch * KC + (warp & 7);
-        if (b >= nb) return;
+        const int b = b0 + (warp & 7);
+        if (b >= bend) return;
         switch ((2 * warp) & 7) {
             case 0: run<0>(stg, b, warp, L, xq, K, acc_a, acc_b); break;
             case 2: run<2>(stg, b, warp, L, xq, K, acc_a, acc_b); break;
@@ -1042,21 +1104,23 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
 
     if (warp == MT_NC) {   // ---- producer: one elected lane streams the stage boxes
         if (lane == 0) {
-            int grp = t0 / nch, ch = t0 - grp * nch;
-            const int n_it = t1 - t0;
             bool ok = true;
-            for (int i = 0; i < n_it; i++) {
+            int i = 0;
+            for (int t = t0; t < t1; i++) {
+                const int grp = t / nch, it = t - grp * nch;
+                const int n = min(min(F::SI, nch - it), t1 - t);
                 const int s = i % S;
                 if (i >= S && !(ok = mbs_wait(bar_empty + 8 * s, ((i / S) - 1) & 1))) break;
                 const int m = mt_matrix(a, grp);
                 const CUtensorMap* tm = m == 0 ? &tm0 : (m == 1 ? &tm1 : &tm2);
-                mbs_expect(bar_full + 8 * s, F::STG);
-                tma_load_3d(sbase + s * F::STG, tm, 0, (grp - a.gbase[m]) * MT_GR, ch * F::ZSTEP, bar_full + 8 * s);
-                if (++ch == nch) { ch = 0; grp++; }
+                mbs_expect(bar_full + 8 * s, n * F::ITEM);
+                for (int j = 0; j < n; j++)
+                    tma_load_3d(sbase + s * F::STG + j * F::ITEM, tm, 0, (grp - a.gbase[m]) * MT_GR,
+                                (it + j) * F::IG / F::ZUNIT, bar_full + 8 * s);
+                t += n;
             }
             // do not retire while a box is still landing in this CTA's ring
-            for (int i = n_it > S ? n_it - S : 0; ok && i < n_it; i++)
-                ok = mbs_wait(bar_empty + 8 * (i % S), (i / S) & 1);
+            for (int k = i > S ? i - S : 0; ok && k < i; k++) ok = mbs_wait(bar_empty + 8 * (k % S), (k / S) & 1);
         }
         return;
     }
@@ -1073,18 +1137,21 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
     const bool bact = L.c == (L.gq >> 1);   // this lane carries a nonzero B fragment
     L.xlb = bact ? xq + (L.gq & 1) * K + F::XB_LANE * L.c : smem + zero_off;
     L.xstr = bact ? 256 : 0;
-    int grp = t0 / nch, ch = t0 - grp * nch, gi = 0;
-    const int first_grp = grp;
+    int gi = 0;
     bool ok = true;
     float acc_a[2] = {0.f, 0.f}, acc_b[2] = {0.f, 0.f};
-    for (int t = t0, i = 0; t < t1; t++, i++) {
+    for (int t = t0, i = 0; t < t1; i++) {
+        // stage i: items [it, it + n) of group grp, the same walk as the producer's
+        const int grp = t / nch, it = t - grp * nch;
+        const int n = min(min(F::SI, nch - it), t1 - t);
         const int s = i % S;
         if (ok) ok = mbs_wait(bar_full + 8 * s, (i / S) & 1);
-        if (ok) F::consume(smem + s * F::STG, ch, nb, warp, L, xq, K, acc_a, acc_b);
+        if (ok) F::consume(smem + s * F::STG, it * F::IG, min(nb, (it + n) * F::IG), warp, L, xq, K, acc_a, acc_b);
         __syncwarp();
         if (lane == 0) mbs_arrive(bar_empty + 8 * s);
+        t += n;
 
-        if (ch == nch - 1 || t == t1 - 1) {   // ---- this CTA's part of group grp is done
+        if (it + n == nch || t == t1) {   // ---- this CTA's part of group grp is done
             const int gq = L.gq, c = L.c;
 #pragma unroll
             for (int m = 0; m < 2; m++) {
@@ -1124,7 +1191,12 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
                 if (gs >= t0 && gs + nch <= t1) {
                     if (row < a.rows[m]) ym[row] = v + (rm ? rm[row] : 0.f);
                 } else {
-                    const int half = grp == first_grp ? 0 : 1;
+                    // split group: every owner publishes its partial rows and
+                    // takes a ticket; the last one sums the partials in CTA
+                    // order (deterministic).  Wait-free: no CTA waits on
+                    // another, so launches on concurrent streams cannot block
+                    // each other.
+                    const int half = grp == t0 / nch ? 0 : 1;
                     a.part[(c0 * 2 + half) * MT_GR + lane] = v;
                     __syncwarp();
                     const int cf = mt_owner(gs, a.T, a.ncta), cl2 = mt_owner(gs + nch - 1, a.T, a.ncta);   // unit == 1 here
@@ -1132,7 +1204,7 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
                     if (lane == 0) g = atom_add_acq_rel(&a.tickets[grp], 1u);
                     g = __shfl_sync(0xffffffffu, g, 0);
                     __syncwarp();
-                    if (g == (unsigned)(cl2 - cf)) {   // last owner: sum the owners' partials in CTA order
+                    if (g == (unsigned)(cl2 - cf)) {
                         float u = 0.f;
                         for (int c2 = cf; c2 <= cl2; c2++) {
                             const int h2 = grp == mt_start(c2, a.T, a.ncta) / nch ? 0 : 1;
@@ -1146,7 +1218,6 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
             acc_a[0] = acc_a[1] = acc_b[0] = acc_b[1] = 0.f;
             gi++;
         }
-        if (++ch == nch) { ch = 0; grp++; }
     }
 }
 
@@ -1247,10 +1318,10 @@ static bool mt_encode(MvPlan* p, const void* W, int rows, int nb) {
     if (mt_smem_bytes<F>(S, nb * 256) > (size_t)MV_SMEM_MAX) return false;
     const int blk = F::STG / (MT_GR * F::KC);   // bytes per block
     const cuuint64_t rb = (cuuint64_t)nb * blk;
-    const int inner = F::ZSTEP == 1 ? F::KC * blk : blk;   // bytes per box row
-    cuuint64_t dims[3] = {(cuuint64_t)inner / 8, (cuuint64_t)rows, (cuuint64_t)(nb * blk / inner)};
+    const int inner = F::ZUNIT * blk;   // bytes per box row
+    cuuint64_t dims[3] = {(cuuint64_t)inner / 8, (cuuint64_t)rows, (cuuint64_t)(nb / F::ZUNIT)};
     cuuint64_t strides[2] = {rb, (cuuint64_t)inner};
-    cuuint32_t box[3] = {(cuuint32_t)inner / 8, MT_GR, (cuuint32_t)(F::ZSTEP == 1 ? 1 : F::KC)};
+    cuuint32_t box[3] = {(cuuint32_t)inner / 8, MT_GR, (cuuint32_t)F::BOXZ};
     cuuint32_t es[3] = {1, 1, 1};
     if (enc(reinterpret_cast<CUtensorMap*>(p->tmap), CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<void*>(W), dims,
             strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -1259,7 +1330,7 @@ static bool mt_encode(MvPlan* p, const void* W, int rows, int nb) {
     p->kind = MV_TMA;
     p->S = S;
     p->smem = mt_smem_bytes<F>(S, nb * 256);
-    p->nch = (nb + F::KC - 1) / F::KC;
+    p->nch = (nb + F::IG - 1) / F::IG;   // split items per 32-row group
     p->ngroups = (rows + MT_GR - 1) / MT_GR;
     p->T = p->ngroups * p->nch;
     p->ncta = p->T < GB_NUM_SMS ? p->T : GB_NUM_SMS;
