@@ -32,6 +32,7 @@
 //    touching global memory it does not own.
 #include "gb_common.cuh"
 #include "gb_internal.h"
+#include "gb_mt.cuh"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -50,12 +51,6 @@ constexpr unsigned long long MV_WAIT_NS = 2000000000ull;
 __device__ unsigned g_gb_device_err;
 
 // ------------------------------------------------------------------ primitives
-__device__ __forceinline__ uint32_t sptr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-__device__ __forceinline__ uint64_t gtimer() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
 __device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t n) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(sptr(b)), "r"(n) : "memory");
 }
@@ -98,14 +93,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 __device__ __forceinline__ void consumer_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(MV_CONSUMERS * 32) : "memory");
 }
-// D += A(16x32 u8, row) * B(32x8 s8, col), s32 accumulate.
-__device__ __forceinline__ void mma_u8s8(int4& d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                         uint32_t b1) {
-    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-        : "+r"(d.x), "+r"(d.y), "+r"(d.z), "+r"(d.w)
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
 // 8 bytes at a 2-byte-aligned shared address: two aligned words, one aligned
 // half word, two funnel shifts (shift 0 or 16, so the read ends at p + 8).
 struct Pair32 { uint32_t lo, hi; };
@@ -115,18 +102,6 @@ __device__ __forceinline__ Pair32 lds8_unaligned(const uint8_t* p) {
     const uint32_t sh = (uint32_t)(a & 3u) * 8u;
     const uint32_t w0 = w[0], w1 = w[1], w2 = *reinterpret_cast<const uint16_t*>(w + 2);
     return {__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh)};
-}
-
-// Two int8 limbs of x: x ~ s * (x0 + x1/256), |x0| <= 127, s = max|x| / 127
-// over the sub-block; v is x / s.
-__device__ __forceinline__ void limbs(float v, int& x0, int& x1) {
-    const float r0 = rintf(v);
-    x0 = (int)r0;
-    const int r1 = (int)rintf((v - r0) * 256.f);
-    x1 = r1 > 127 ? 127 : (r1 < -128 ? -128 : r1);
-}
-__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
-    return (uint32_t)(a & 255) | ((uint32_t)(b & 255) << 8) | ((uint32_t)(c & 255) << 16) | ((uint32_t)(d & 255) << 24);
 }
 
 // ------------------------------------------------------------------ geometry
@@ -608,91 +583,6 @@ k_mv_q8_0(const uint8_t* __restrict__ W, int rows, int nb, const float* __restri
     }
 }
 
-// ================================================================== TMA path
-// Weights stream through a ring of shared-memory stages filled by TMA tensor
-// copies.  Q4_K: the matrix is viewed as a 3-D tensor {144-byte block
-// (18 x u64), row, block index} with strides {row_bytes, 144}; one box
-// {18, 32 rows, 1 block} is one split item, and up to 16 of them (consecutive
-// blocks of one 32-row group) fill a stage laid out [block][row][144 B], so
-// every 16-row tile of a block is a dense 2304-byte slab (conflict-free
-// 128-bit reads).  Q6_K: the item is a run of 8 blocks (1680 bytes, the
-// shortest 16-byte multiple) of 32 rows.  Every copy starts at x = 0 (16-byte
-// aligned).  Out-of-range rows are zero-filled by the TMA unit and skipped.
-//
-// Work split (stream-K): the (32-row group, item) sequence is cut into one
-// contiguous range per CTA, so every CTA streams the same number of bytes
-// to within one item.  Groups that straddle CTAs finish through a per-group
-// ticket: each owner writes its partial rows to the workspace and the last
-// one sums the partials in CTA order (deterministic) and writes y.
-//
-// x is quantised inside every CTA (int8 limb planes + per-32-column scale and
-// sum in shared memory) while the first weight boxes are in flight.  With
-// programmatic dependent launch the producer issues those boxes before
-// griddepcontrol.wait; consumers read x and write y only after it.
-constexpr int MT_GR = 32;                 // rows per group (two 16-row tiles)
-
-__device__ __forceinline__ void mbs_init(uint32_t b, uint32_t n) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(b), "r"(n) : "memory");
-}
-__device__ __forceinline__ void mbs_expect(uint32_t b, uint32_t tx) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(b), "r"(tx) : "memory");
-}
-__device__ __forceinline__ void mbs_arrive(uint32_t b) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(b) : "memory");
-}
-__device__ __forceinline__ bool mbs_test(uint32_t b, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n}"
-        : "=r"(ok)
-        : "r"(b), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Bounded wait (2 s of %globaltimer); false on timeout, recorded as GB_ETIMEOUT.
-__device__ __noinline__ bool mbs_wait_slow(uint32_t b, uint32_t parity) {
-    const uint64_t t0 = gtimer();
-    while (!mbs_test(b, parity)) {
-        if (gtimer() - t0 > MV_WAIT_NS) {
-            atomicExch(&g_gb_device_err, (unsigned)(-GB_ETIMEOUT));
-            return false;
-        }
-    }
-    return true;
-}
-__device__ __forceinline__ bool mbs_wait(uint32_t b, uint32_t parity) {
-    return mbs_test(b, parity) || mbs_wait_slow(b, parity);
-}
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* map, int x, int y, int z, uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
-        ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(z), "r"(bar)
-        : "memory");
-}
-__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
-    unsigned old;
-    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-    return old;
-}
-__device__ __forceinline__ void red_add_release(unsigned* p, unsigned v) {
-    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-template <int NC>
-__device__ __forceinline__ void mt_consumer_sync() {
-    asm volatile("bar.sync 1, %0;" ::"n"(NC * 32) : "memory");
-}
-// Split item t of a matrix with nch items per group: CTA c owns
-// [t_start(c), t_start(c + 1)); owner(t) is the CTA whose range holds t.
-__device__ __forceinline__ int mt_start(int c, int T, int n) { return (int)((long long)c * T / n); }
-__device__ __forceinline__ int mt_owner(int t, int T, int n) { return (int)(((long long)(t + 1) * n - 1) / T); }
-
 // Up to MT_MAXM matrices of one format and one column count that share x run
 // as one launch: their (group, item) sequences are concatenated, matrix m
 // owning the global 32-row groups [gbase[m], gbase[m + 1]).
@@ -714,356 +604,6 @@ struct MtArgs {
     const float* nw;
     const float* x2;
     float eps;
-};
-
-// x in shared memory (K = 256 nb columns):
-//   x0[K], x1[K]                int8 limbs, x ~ s * (x0 + x1 / 256)
-//   f[K/64][4]                  per 64 columns {s lo, s hi, sum lo, sum hi} of
-//                               its two 32-column sub-blocks (s = max|x| / 127)
-//   s16[K/256][2][8]  (Q6_K)    sums of the 16-column sub-blocks 8n + 2G + h,
-//                               stored at [b][h][4n + G]
-__host__ __device__ constexpr int mt_xq_bytes(int K, bool s16) { return 2 * K + K / 4 + (s16 ? K / 4 : 0); }
-constexpr int MT_ZERO = 256;   // zero line read by lanes without a B fragment
-
-// RMSNorm scale 1 / sqrt(mean(x^2) + eps) over the K columns, summed by the
-// consumer threads and combined in fixed warp order (every CTA gets the
-// same value).  scratch: NC floats of shared memory.
-constexpr int MT_XU = 4;   // float4 loads of x in flight per thread
-template <int NC>
-__device__ __forceinline__ float mt_rms_scale(const float* __restrict__ x, int K, float eps, float* scratch, int tid) {
-    float ss = 0.f;
-    const int n4 = K / 4;
-    for (int base = tid; base < n4; base += MT_XU * NC * 32) {
-        float4 v[MT_XU];
-#pragma unroll
-        for (int j = 0; j < MT_XU; j++) {
-            const int t = base + j * NC * 32;
-            v[j] = t < n4 ? reinterpret_cast<const float4*>(x)[t] : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int j = 0; j < MT_XU; j++) {
-            ss = fmaf(v[j].x, v[j].x, ss);
-            ss = fmaf(v[j].y, v[j].y, ss);
-            ss = fmaf(v[j].z, v[j].z, ss);
-            ss = fmaf(v[j].w, v[j].w, ss);
-        }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if ((tid & 31) == 0) scratch[tid >> 5] = ss;
-    mt_consumer_sync<NC>();
-    float tot = 0.f;
-#pragma unroll
-    for (int w = 0; w < NC; w++) tot += scratch[w];
-    return __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)K), eps)));
-}
-__device__ __forceinline__ float mt_silu_mul(float g, float u) {
-    return __fmul_rn(__fmul_rn(g, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-g)))), u);
-}
-
-// One float4 of x (columns 4t .. 4t + 3): transform, quantise to two int8
-// limbs per value against the 32-column sub-block's max |x|, and record the
-// sub-block scale and sum.  Lanes 8k .. 8k + 7 of a warp hold one sub-block.
-template <bool S16>
-__device__ __forceinline__ void mt_quantise4(const MtArgs& a, int K, uint8_t* xq, int t, float4 v, float4 w, float rs) {
-    uint32_t* p0 = reinterpret_cast<uint32_t*>(xq);
-    uint32_t* p1 = reinterpret_cast<uint32_t*>(xq + K);
-    float* f = reinterpret_cast<float*>(xq + 2 * K);
-    float* f16 = f + K / 16;
-    if (a.xmode == MV_X_RMSNORM) {   // w * (x * r), the reference's rounding
-        v = make_float4(__fmul_rn(w.x, __fmul_rn(v.x, rs)), __fmul_rn(w.y, __fmul_rn(v.y, rs)),
-                        __fmul_rn(w.z, __fmul_rn(v.z, rs)), __fmul_rn(w.w, __fmul_rn(v.w, rs)));
-    } else if (a.xmode == MV_X_SILU_MUL) {
-        v = make_float4(mt_silu_mul(v.x, w.x), mt_silu_mul(v.y, w.y), mt_silu_mul(v.z, w.z), mt_silu_mul(v.w, w.w));
-    }
-    float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-    float sm = (v.x + v.y) + (v.z + v.w);
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    sm += __shfl_xor_sync(0xffffffffu, sm, 1);
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    sm += __shfl_xor_sync(0xffffffffu, sm, 2);
-    if (S16 && (t & 3) == 0) {   // 16-column sum: column c0 = 4t = 256 b + 128 n + 32 G + 16 h
-        const int c0 = 4 * t, b = c0 >> 8, n = (c0 >> 7) & 1, G = (c0 >> 5) & 3, h = (c0 >> 4) & 1;
-        f16[b * 16 + h * 8 + 4 * n + G] = sm;
-    }
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-    sm += __shfl_xor_sync(0xffffffffu, sm, 4);
-    const float inv = mx > 0.f ? 127.f / mx : 0.f;
-    int a0, a1, b0, b1, c0, c1, d0, d1;
-    limbs(v.x * inv, a0, a1);
-    limbs(v.y * inv, b0, b1);
-    limbs(v.z * inv, c0, c1);
-    limbs(v.w * inv, d0, d1);
-    p0[t] = pack4(a0, b0, c0, d0);
-    p1[t] = pack4(a1, b1, c1, d1);
-    const int sb = t >> 3;
-    if ((t & 7) == 0) {
-        f[(sb >> 1) * 4 + (sb & 1)] = mx / 127.f;
-        f[(sb >> 1) * 4 + 2 + (sb & 1)] = sm;
-    }
-}
-
-// Quantise x into shared memory.  The loads of MT_XU float4 per thread (and
-// of the transform's second operand) are issued before any is used, so the
-// L2 latency is paid once per MT_XU float4 rather than once per float4.
-// nthr is a multiple of 32 and K / 4 of 64, so the bounds test is
-// warp-uniform and the shuffles see full warps.
-template <bool S16>
-__device__ __forceinline__ void mt_quantise_x(const MtArgs& a, int K, uint8_t* xq, int tid, int nthr, float rs) {
-    const int n4 = K / 4;
-    const float4* x4 = reinterpret_cast<const float4*>(a.x);
-    const float4* w4 = reinterpret_cast<const float4*>(a.xmode == MV_X_RMSNORM ? a.nw : a.x2);
-    const bool aux = a.xmode != MV_X_NONE;
-    for (int base = tid; base < n4; base += MT_XU * nthr) {
-        float4 v[MT_XU], w[MT_XU];
-#pragma unroll
-        for (int j = 0; j < MT_XU; j++) {
-            const int t = base + j * nthr;
-            v[j] = w[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (t < n4) {
-                v[j] = x4[t];
-                if (aux) w[j] = w4[t];
-            }
-        }
-#pragma unroll
-        for (int j = 0; j < MT_XU; j++) {
-            const int t = base + j * nthr;
-            if (t < n4) mt_quantise4<S16>(a, K, xq, t, v[j], w[j], rs);
-        }
-    }
-}
-
-// Per-lane constants of the tensor-core fragment map (g = lane / 4 is the
-// row within an 8-row half tile and the B column; c = lane % 4 the column
-// group).  Only lanes with c == g / 2 carry nonzero B fragments; the others
-// read a zero line, with a zero stride, so no lane branches.
-struct MtLane {
-    int gq, c;
-    const uint8_t* xlb;   // B fragment base
-    int xstr;             // bytes per 256-column block (0 for zero lanes)
-};
-
-// ---------------------------------------------------------------- Q4_K stage
-// Box {18 x u64, 32 rows, 16 blocks}: shared layout [block][row][144 B].  Warp
-// w takes block w of the stage, both 16-row tiles.
-template <int IGV>
-struct MtQ4KT {
-    static constexpr int NC = 16;        // consumer warps: warp w takes block w of the stage, both tiles
-    static constexpr int KC = 16;
-    static constexpr int ILP = KC / NC;
-    static constexpr int STG = KC * MT_GR * GB_Q4K_BYTES;
-    static constexpr bool S16 = false;
-    static constexpr int XB_LANE = 64;   // B fragment offset per column group
-    static constexpr int IG = IGV;       // blocks per split item
-    static constexpr int SI = KC / IG;   // items per full stage
-    static constexpr int ITEM = STG / SI;
-    static constexpr int ZUNIT = 1;      // blocks per tensor-map z unit
-    static constexpr int BOXZ = IG;      // box depth: one box per item
-    // blocks [b0, bend) of the group land at stage blocks 0 .. bend - b0 - 1
-    __device__ static __forceinline__ void consume(const uint8_t* stg, int b0, int bend, int warp, const MtLane& L,
-                                                   const uint8_t* xq, int K, float acc_a[2], float acc_b[2]) {
-        const int gq = L.gq, c = L.c;
-        const float4* xfb = reinterpret_cast<const float4*>(xq + 2 * K) + c;
-        const int sh8 = (c & 1) << 4;
-        const uint32_t MW = c >= 2 ? 0x0F0Fu : 0u, MY = c >= 2 ? 0x3030u : 0x3F3Fu, SY = c >= 2 ? 2u : 0u;
-        float pa[2][2] = {}, pb[2][2] = {};
-#pragma unroll
-        for (int j = 0; j < ILP; j++) {   // block warp (+ NC) of the stage
-            const int bl = warp + j * NC;
-            const int b = b0 + bl;
-            pa[j][0] = pa[j][1] = pb[j][0] = pb[j][1] = 0.f;
-            if (b >= bend) continue;
-            const uint4* xb = reinterpret_cast<const uint4*>(L.xlb + b * L.xstr);
-            const uint4 bl0 = xb[0], bl1 = xb[1], bh0 = xb[2], bh1 = xb[3];
-            const float4 xf = xfb[b * 4];
-            const float xlo = xf.x * 0.00390625f, xhi = xf.y * (0.00390625f * 0.0625f);
-#pragma unroll
-            for (int m = 0; m < 2; m++) {   // two 16-row tiles
-                const uint8_t* ra = stg + bl * (MT_GR * GB_Q4K_BYTES) + (m * 16 + gq) * GB_Q4K_BYTES;
-                const uint8_t* rb = ra + 8 * GB_Q4K_BYTES;
-                const uint4 ha = *reinterpret_cast<const uint4*>(ra);
-                const uint4 hb = *reinterpret_cast<const uint4*>(rb);
-                const uint4 qa0 = *reinterpret_cast<const uint4*>(ra + 16 + 32 * c);
-                const uint4 qa1 = *reinterpret_cast<const uint4*>(ra + 32 + 32 * c);
-                const uint4 qb0 = *reinterpret_cast<const uint4*>(rb + 16 + 32 * c);
-                const uint4 qb1 = *reinterpret_cast<const uint4*>(rb + 32 + 32 * c);
-                int4 cl = make_int4(0, 0, 0, 0), chh = make_int4(0, 0, 0, 0);
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const uint4& qa = (u >> 1) ? qa1 : qa0;
-                    const uint4& qb = (u >> 1) ? qb1 : qb0;
-                    const uint32_t wa0 = (u & 1) ? qa.z : qa.x, wa1 = (u & 1) ? qa.w : qa.y;
-                    const uint32_t wb0 = (u & 1) ? qb.z : qb.x, wb1 = (u & 1) ? qb.w : qb.y;
-                    const uint4& blx = (u >> 1) ? bl1 : bl0;
-                    const uint4& bhx = (u >> 1) ? bh1 : bh0;
-                    const uint32_t l0 = (u & 1) ? blx.z : blx.x, l1 = (u & 1) ? blx.w : blx.y;
-                    const uint32_t h0 = (u & 1) ? bhx.z : bhx.x, h1 = (u & 1) ? bhx.w : bhx.y;
-                    mma_u8s8(cl, wa0 & 0x0F0F0F0Fu, wb0 & 0x0F0F0F0Fu, wa1 & 0x0F0F0F0Fu, wb1 & 0x0F0F0F0Fu, l0, l1);
-                    mma_u8s8(chh, wa0 & 0xF0F0F0F0u, wb0 & 0xF0F0F0F0u, wa1 & 0xF0F0F0F0u, wb1 & 0xF0F0F0F0u, h0, h1);
-                }
-                // sub-blocks 2c (low nibbles) and 2c + 1 (high nibbles) of rows a, b
-#pragma unroll
-                for (int w = 0; w < 2; w++) {
-                    const uint4 h = w ? hb : ha;
-                    const uint32_t y = h.y >> sh8, z = h.z >> sh8, ww = h.w >> sh8;
-                    const uint32_t sc = (ww & MW) | ((y >> SY) & MY);
-                    const uint32_t mn = ((ww >> 4) & MW) | ((z >> SY) & MY);
-                    const float sc_lo = (float)(sc & 0xFFu), sc_hi = (float)((sc >> 8) & 0xFFu);
-                    const float m_lo = (float)(mn & 0xFFu), m_hi = (float)((mn >> 8) & 0xFFu);
-                    const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
-                    const int dl = (w ? cl.z : cl.x) * 256 + (w ? cl.w : cl.y);
-                    const int dh = (w ? chh.z : chh.x) * 256 + (w ? chh.w : chh.y);
-                    const float tt = (sc_lo * xlo) * (float)dl + (sc_hi * xhi) * (float)dh;
-                    const float mm = m_lo * xf.z + m_hi * xf.w;
-                    (w ? pb : pa)[j][m] = fmaf(dm.x, tt, -dm.y * mm);
-                }
-            }
-        }
-#pragma unroll
-        for (int m = 0; m < 2; m++) {
-            acc_a[m] += pa[0][m] + pa[1][m];
-            acc_b[m] += pb[0][m] + pb[1][m];
-        }
-    }
-};
-// 16-block items: a stage is one box and a 32-row group of a 4096-column
-// matrix is one item, so such launches split by whole groups
-using MtQ4K = MtQ4KT<16>;
-
-// ---------------------------------------------------------------- Q6_K stage
-// Box {210 x u64 = 8 blocks, 32 rows, 1 chunk}: shared layout [row][1680 B];
-// warp w takes block w of every row, so its blocks start at 210 w within a
-// row and every field of the block sits at the same offset mod 8, MIS =
-// (2 w) mod 8.  Loads are specialised on MIS: 64-bit when aligned, two words
-// at 4, three words and two byte permutes at 2 or 6.
-template <int MIS>
-__device__ __forceinline__ uint2 lds8_mis(const uint8_t* p) {
-    if constexpr (MIS == 0) {
-        return *reinterpret_cast<const uint2*>(p);
-    } else if constexpr (MIS == 4) {
-        const uint32_t* w = reinterpret_cast<const uint32_t*>(p);
-        return make_uint2(w[0], w[1]);
-    } else {
-        const uint32_t* w = reinterpret_cast<const uint32_t*>(p - 2);
-        const uint32_t w0 = w[0], w1 = w[1], w2 = w[2];
-        return make_uint2(__byte_perm(w0, w1, 0x5432), __byte_perm(w1, w2, 0x5432));
-    }
-}
-// 6-bit codes of weights 128 n + 32 G + [8c, 8c + 8) from the ql / qh words
-// (low / high word of the lane's 8 bytes): low nibble for G < 2, high for
-// G >= 2; ql from byte 8c (G even) or 32 + 8c (G odd); qh bits 2G..2G+1.
-// Byte of w chosen by the prmt selector sel, sign-extended (prmt selector
-// nibbles with bit 3 set replicate the sign of the chosen byte).
-__device__ __forceinline__ int prmt_sext(uint32_t w, int sel) {
-    int r;
-    asm("prmt.b32 %0, %1, 0, %2;" : "=r"(r) : "r"(w), "r"(sel));
-    return r;
-}
-template <int G>
-__device__ __forceinline__ uint32_t q6_code(uint32_t lw, uint32_t hw) {
-    const uint32_t nib = (G >> 1) ? ((lw >> 4) & 0x0F0F0F0Fu) : (lw & 0x0F0F0F0Fu);
-    const uint32_t hi = G == 0 ? (hw << 4) : G == 1 ? (hw << 2) : G == 2 ? hw : (hw >> 2);
-    return nib | (hi & 0x30303030u);
-}
-struct MtQ6K {
-    static constexpr int NC = 16;        // consumer warps: block w % 8, 16-row tile w / 8
-    static constexpr int KC = 8;
-    static constexpr int RB = 8 * GB_Q6K_BYTES;   // 1680 bytes per row per stage
-    static constexpr int STG = MT_GR * RB;
-    static constexpr bool S16 = true;
-    static constexpr int XB_LANE = 8;
-    static constexpr int IG = 8;         // blocks per split item: one 16-byte aligned 1680-byte row run
-    static constexpr int SI = 1;         // items per stage
-    static constexpr int ITEM = STG;
-    static constexpr int ZUNIT = 8;      // blocks per tensor-map z unit
-    static constexpr int BOXZ = 1;
-    template <int MIS>
-    __device__ static __forceinline__ void tile(const uint8_t* blk_a, int c, const uint8_t* xb, const float* xf,
-                                                const float4 s16lo, const float4 s16hi, float fc, int selsc0,
-                                                int selsc1, float& acc_a, float& acc_b) {
-        const uint8_t* blk_b = blk_a + 8 * RB;
-        const uint8_t* ra = blk_a + 8 * c;   // the lane's 8 bytes of each 32-byte ql / qh run
-        const uint8_t* rb = blk_b + 8 * c;
-        float ba = 0.f, bb = 0.f;   // block sums before the super-scale d
-        // int8 scales of rows a and b, 16 bytes at 192
-        uint32_t sa[4], sb[4];
-        {
-            const uint2 a0 = lds8_mis<MIS>(blk_a + 192), a1 = lds8_mis<MIS>(blk_a + 200);
-            const uint2 b0 = lds8_mis<MIS>(blk_b + 192), b1 = lds8_mis<MIS>(blk_b + 200);
-            sa[0] = a0.x; sa[1] = a0.y; sa[2] = a1.x; sa[3] = a1.y;
-            sb[0] = b0.x; sb[1] = b0.y; sb[2] = b1.x; sb[3] = b1.y;
-        }
-#pragma unroll
-        for (int n = 0; n < 2; n++) {
-            const uint2 qa0 = lds8_mis<MIS>(ra + 64 * n), qa1 = lds8_mis<MIS>(ra + 64 * n + 32);
-            const uint2 qb0 = lds8_mis<MIS>(rb + 64 * n), qb1 = lds8_mis<MIS>(rb + 64 * n + 32);
-            const uint2 ha = lds8_mis<MIS>(ra + 128 + 32 * n), hb = lds8_mis<MIS>(rb + 128 + 32 * n);
-            const float4 xs = *reinterpret_cast<const float4*>(xf + 8 * n);       // sub-blocks 4n, 4n+1
-            const float4 xs2 = *reinterpret_cast<const float4*>(xf + 8 * n + 4);  // sub-blocks 4n+2, 4n+3
-#pragma unroll
-            for (int G = 0; G < 4; G++) {
-                const uint2& la = (G & 1) ? qa1 : qa0;
-                const uint2& lb = (G & 1) ? qb1 : qb0;
-                uint32_t A0, A1, A2, A3;
-                switch (G) {
-                    case 0: A0 = q6_code<0>(la.x, ha.x); A1 = q6_code<0>(lb.x, hb.x); A2 = q6_code<0>(la.y, ha.y); A3 = q6_code<0>(lb.y, hb.y); break;
-                    case 1: A0 = q6_code<1>(la.x, ha.x); A1 = q6_code<1>(lb.x, hb.x); A2 = q6_code<1>(la.y, ha.y); A3 = q6_code<1>(lb.y, hb.y); break;
-                    case 2: A0 = q6_code<2>(la.x, ha.x); A1 = q6_code<2>(lb.x, hb.x); A2 = q6_code<2>(la.y, ha.y); A3 = q6_code<2>(lb.y, hb.y); break;
-                    default: A0 = q6_code<3>(la.x, ha.x); A1 = q6_code<3>(lb.x, hb.x); A2 = q6_code<3>(la.y, ha.y); A3 = q6_code<3>(lb.y, hb.y); break;
-                }
-                const uint2 bf = *reinterpret_cast<const uint2*>(xb + 128 * n + 32 * G);
-                int4 cc = make_int4(0, 0, 0, 0);
-                mma_u8s8(cc, A0, A1, A2, A3, bf.x, bf.y);
-                const float xsg = ((G >> 1) ? ((G & 1) ? xs2.y : xs2.x) : ((G & 1) ? xs.y : xs.x)) * 0.00390625f;
-                const float s16 = n ? ((G == 0) ? s16hi.x : (G == 1) ? s16hi.y : (G == 2) ? s16hi.z : s16hi.w)
-                                    : ((G == 0) ? s16lo.x : (G == 1) ? s16lo.y : (G == 2) ? s16lo.z : s16lo.w);
-                // scale byte 8n + 2G + (c >> 1): word 2n + (G >> 1), byte 2 (G & 1) + (c >> 1)
-                const int sel = (G & 1) ? selsc1 : selsc0;
-                const float sca = (float)prmt_sext(sa[2 * n + (G >> 1)], sel);
-                const float scb = (float)prmt_sext(sb[2 * n + (G >> 1)], sel);
-                const float ta = fmaf(xsg, (float)(cc.x * 256 + cc.y), fc * s16);
-                const float tb = fmaf(xsg, (float)(cc.z * 256 + cc.w), fc * s16);
-                ba = fmaf(sca, ta, ba);
-                bb = fmaf(scb, tb, bb);
-            }
-        }
-        const float da = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(blk_a + 208)));
-        const float db = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(blk_b + 208)));
-        acc_a = fmaf(da, ba, acc_a);
-        acc_b = fmaf(db, bb, acc_b);
-    }
-    template <int MIS>
-    __device__ static __forceinline__ void run(const uint8_t* stg, int b, int warp, const MtLane& L, const uint8_t* xq,
-                                               int K, float acc_a[2], float acc_b[2]) {
-        const int c = L.c;
-        const uint8_t* xb = L.xlb + b * L.xstr;
-        const float* xf = reinterpret_cast<const float*>(xq + 2 * K) + b * 16;   // {s, s, sum, sum} x 4
-        // xf holds per 64-column chunk {s lo, s hi, sum lo, sum hi}: the scale
-        // of 32-column sub-block 4n + G is xf[8n + 4 (G >> 1) + (G & 1)]
-        const float* f16 = reinterpret_cast<const float*>(xq + 2 * K + K / 4) + b * 16 + (c >> 1) * 8;
-        const float4 s16lo = *reinterpret_cast<const float4*>(f16);
-        const float4 s16hi = *reinterpret_cast<const float4*>(f16 + 4);
-        const float fc = (c & 1) ? 0.f : -32.f;   // the -32 offset of the codes, once per 16 columns
-        const int h = c >> 1;
-        // prmt selectors extracting byte 2 (G & 1) + h sign-extended
-        const int b0 = h, b1 = 2 + h;
-        const int selsc0 = b0 | ((b0 | 8) << 4) | ((b0 | 8) << 8) | ((b0 | 8) << 12);
-        const int selsc1 = b1 | ((b1 | 8) << 4) | ((b1 | 8) << 8) | ((b1 | 8) << 12);
-        const int m = warp >> 3;
-        const uint8_t* blk = stg + (m * 16 + L.gq) * RB + (warp & 7) * GB_Q6K_BYTES;
-        tile<MIS>(blk, c, xb, xf, s16lo, s16hi, fc, selsc0, selsc1, acc_a[m], acc_b[m]);
-    }
-    __device__ static __forceinline__ void consume(const uint8_t* stg, int b0, int bend, int warp, const MtLane& L,
-                                                   const uint8_t* xq, int K, float acc_a[2], float acc_b[2]) {
-        const int b = b0 + (warp & 7);
-        if (b >= bend) return;
-        switch ((2 * warp) & 7) {
-            case 0: run<0>(stg, b, warp, L, xq, K, acc_a, acc_b); break;
-            case 2: run<2>(stg, b, warp, L, xq, K, acc_a, acc_b); break;
-            case 4: run<4>(stg, b, warp, L, xq, K, acc_a, acc_b); break;
-            default: run<6>(stg, b, warp, L, xq, K, acc_a, acc_b); break;
-        }
-    }
 };
 
 // matrix of global group g
@@ -1110,7 +650,7 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
                 const int grp = t / nch, it = t - grp * nch;
                 const int n = min(min(F::SI, nch - it), t1 - t);
                 const int s = i % S;
-                if (i >= S && !(ok = mbs_wait(bar_empty + 8 * s, ((i / S) - 1) & 1))) break;
+                if (i >= S && !(ok = mbs_wait(bar_empty + 8 * s, ((i / S) - 1) & 1, &g_gb_device_err))) break;
                 const int m = mt_matrix(a, grp);
                 const CUtensorMap* tm = m == 0 ? &tm0 : (m == 1 ? &tm1 : &tm2);
                 mbs_expect(bar_full + 8 * s, n * F::ITEM);
@@ -1120,7 +660,7 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
                 t += n;
             }
             // do not retire while a box is still landing in this CTA's ring
-            for (int k = i > S ? i - S : 0; ok && k < i; k++) ok = mbs_wait(bar_empty + 8 * (k % S), (k / S) & 1);
+            for (int k = i > S ? i - S : 0; ok && k < i; k++) ok = mbs_wait(bar_empty + 8 * (k % S), (k / S) & 1, &g_gb_device_err);
         }
         return;
     }
@@ -1145,7 +685,7 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
         const int grp = t / nch, it = t - grp * nch;
         const int n = min(min(F::SI, nch - it), t1 - t);
         const int s = i % S;
-        if (ok) ok = mbs_wait(bar_full + 8 * s, (i / S) & 1);
+        if (ok) ok = mbs_wait(bar_full + 8 * s, (i / S) & 1, &g_gb_device_err);
         if (ok) F::consume(smem + s * F::STG, it * F::IG, min(nb, (it + n) * F::IG), warp, L, xq, K, acc_a, acc_b);
         __syncwarp();
         if (lane == 0) mbs_arrive(bar_empty + 8 * s);
@@ -1298,6 +838,43 @@ static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
             fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
     });
     return fn;
+}
+
+// Tensor map of the 3-D view {box row as u64, rows, z} of a Q4_K (z = block,
+// box depth boxz blocks) or Q6_K (z = 8-block run, depth 1) matrix with nb
+// blocks per row.  W and the row pitch must be 16-byte aligned.
+bool mt_encode_view(void* map128, int dtype, const void* W, int rows, int nb, int boxz) {
+    auto enc = tensor_map_encoder();
+    if (!enc || (reinterpret_cast<uintptr_t>(W) & 15)) return false;
+    const bool q6 = dtype == GB_DT_Q6_K;
+    if (!q6 && dtype != GB_DT_Q4_K) return false;
+    if (q6 && (nb % 8 || boxz != 1)) return false;
+    const int blk = q6 ? GB_Q6K_BYTES : GB_Q4K_BYTES;
+    const int inner = (q6 ? 8 : 1) * blk;
+    cuuint64_t dims[3] = {(cuuint64_t)inner / 8, (cuuint64_t)rows, (cuuint64_t)(nb / (q6 ? 8 : 1))};
+    cuuint64_t strides[2] = {(cuuint64_t)nb * blk, (cuuint64_t)inner};
+    cuuint32_t box[3] = {(cuuint32_t)inner / 8, MT_GR, (cuuint32_t)boxz};
+    cuuint32_t es[3] = {1, 1, 1};
+    return enc(reinterpret_cast<CUtensorMap*>(map128), CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<void*>(W), dims,
+               strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Tensor map of a Q4_K matrix as rows of bytes {18 nb u64, rows, 1}: a box
+// {box_u64, 32 rows} copies box_u64 * 8 consecutive bytes of 32 rows (x
+// coordinates are multiples of 18 u64 = one block, 16-byte aligned; bytes past
+// the row end are zero-filled).
+bool mt_encode_rows(void* map128, const void* W, int rows, int nb, int box_u64) {
+    auto enc = tensor_map_encoder();
+    if (!enc || (reinterpret_cast<uintptr_t>(W) & 15) || box_u64 <= 0 || box_u64 > 256 || box_u64 % 2) return false;
+    const cuuint64_t rb = (cuuint64_t)nb * GB_Q4K_BYTES;
+    cuuint64_t dims[3] = {rb / 8, (cuuint64_t)rows, 1};
+    cuuint64_t strides[2] = {rb, rb * (cuuint64_t)rows};
+    cuuint32_t box[3] = {(cuuint32_t)box_u64, MT_GR, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    return enc(reinterpret_cast<CUtensorMap*>(map128), CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<void*>(W), dims,
+               strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 template <class F>
