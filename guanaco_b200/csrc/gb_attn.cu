@@ -15,17 +15,22 @@
 // Layout: the KV cache keeps the reference's fp32 head-major layout
 // [n_kv][max_seq][head_dim] per layer (kv_cache.c:90-93).
 //
-// Shape: grid = n_kv * grid_splits CTAs of 256 threads.  A CTA owns one KV
-// head and P consecutive positions (P from pos, so the active splits fill the
-// grid); it serves all GROUP = n_heads / n_kv query heads of that KV head, so
-// each K and V row is read from HBM exactly once.
-//   pass 1: LPP lanes share one K row (DPL dims each, 128-bit loads), dot
-//           products for all GROUP heads, shuffle-reduced -> scores in smem;
-//   pass 2: per-head max / exp / sum over the split;
-//   pass 3: V rows (one per VL lanes) accumulate p * V for all heads; the
-//           8 warps reduce through shared memory;
-//   merge:  each CTA publishes (m, l, o[hd]) per head; the last CTA of the KV
-//           head (atomic ticket) combines the splits and resets the ticket.
+// Shape: grid = n_kv * grid_splits CTAs, one CTA per SM over all KV heads.
+// A CTA owns one KV head and P consecutive positions (P from pos, so the
+// active splits fill the grid); it serves all GROUP = n_heads / n_kv query
+// heads of that KV head, so each K and V row is read from HBM exactly once.
+// One producer lane streams K and V tiles of 32 positions through a ring of
+// bulk copies (about 200 KB per SM in flight); each of 8 consumer warps owns
+// every 8th tile and runs its own online softmax, with no CTA-wide barrier
+// per tile:
+//   scores:  LPP lanes share one K row (DPL dims each, 128-bit loads), dot
+//            products for all GROUP heads, shuffle-reduced;
+//   softmax: per head, the tile's max updates the warp's running max m, and
+//            the running sum l and the output are rescaled by exp(m_old - m);
+//   P.V:     each lane accumulates one float4 column of every head;
+//   merge:   the warps' (m, l, o) combine in shared memory, each CTA
+//            publishes its (m, l, o[hd]) per head, and the last CTA of the KV
+//            head (atomic ticket) combines the splits and resets the ticket.
 // pos comes from device memory so the launch can live inside a CUDA graph;
 // a pos outside [0, max_seq) sets the error word and touches nothing.
 #include "gb_common.cuh"
@@ -35,31 +40,39 @@
 
 namespace gb {
 
-constexpr int ATTN_THREADS = 256;
-constexpr int ATTN_MAX_P = 1024;
+constexpr int ATTN_CWARPS = 8;                        // consumer warps
+constexpr int ATTN_THREADS = (ATTN_CWARPS + 1) * 32;   // + the producer warp
+constexpr int ATTN_SMEM_MAX = 227 * 1024;
 
+// Splits per KV head: one CTA per SM over all heads (every split then has
+// its whole share of K/V requested nearly at once), at least one 32-position
+// tile per split.
 int attn_grid_splits(int n_kv, int max_seq) {
-    const int a = (2 * GB_NUM_SMS + n_kv - 1) / n_kv;
-    const int b = (max_seq + ATTN_MAX_P - 1) / ATTN_MAX_P;
-    return a > b ? a : b;
+    int s = GB_NUM_SMS / n_kv;
+    if (s < 1) s = 1;
+    const int tiles = (max_seq + 31) / 32;
+    return s < tiles ? s : tiles;
 }
 
 template <int HD, int GROUP>
 struct AttnCfg {
-    static constexpr int DPL = GROUP <= 4 ? 16 : 8;   // K dims per lane
+    static constexpr int DPL = GROUP <= 4 ? 16 : 8;   // K dims per lane (scores)
     static constexpr int LPP = HD / DPL;              // lanes per K row
     static constexpr int PPW = 32 / LPP;              // K rows per warp step
-    static constexpr int VL = HD / 4;                 // lanes per V row
-    static constexpr int RPW = 32 / VL;               // V rows per warp step
-    static constexpr int RED = 8 * RPW * GROUP * HD;  // pass-3 reduction floats
-    static constexpr int SF = ATTN_MAX_P * 8;         // score buffer floats
-    static_assert(RED <= SF, "reduction buffer aliases the score buffer");
     static constexpr int TP = 32;                     // positions per K / V tile
-    static constexpr int R = 4;                       // tiles in flight per CTA
     static constexpr int TILE = TP * HD;              // floats per tile
-    static constexpr size_t RING_OFF = ((size_t)(GROUP * HD + 2 * HD + SF + 16) * sizeof(float) + 127) / 128 * 128;
+    static constexpr int CH = HD / 4;                 // float4 columns of a V row
+    static constexpr int RPL = 32 / CH;               // rows a warp's P.V step covers
+    // shared: q[GROUP][HD] | k_new[HD] | v_new[HD] | per-warp p[TP][8] |
+    // merge sums [8] | issued-item count [4] | ring[R][TILE] | full[R], empty[R]
+    static constexpr int HEAD_FLOATS = GROUP * HD + 2 * HD + ATTN_CWARPS * TP * 8 + 8 + 4;
+    static constexpr size_t RING_OFF = ((size_t)HEAD_FLOATS * sizeof(float) + 127) / 128 * 128;
+    static constexpr int R0 = (int)((ATTN_SMEM_MAX - RING_OFF - 512) / (TILE * sizeof(float)));
+    static constexpr int R = R0 < 24 ? R0 : 24;       // items (K or V tiles) in flight per CTA
     static constexpr size_t BAR_OFF = RING_OFF + (size_t)R * TILE * sizeof(float);
-    static constexpr size_t SMEM = BAR_OFF + R * sizeof(unsigned long long);
+    static constexpr size_t SMEM = BAR_OFF + 2 * R * sizeof(unsigned long long);
+    // the warps' (m, l, o) merge reuses the ring
+    static_assert(ATTN_CWARPS * GROUP * (HD + 4) + GROUP * GB_NUM_SMS <= R * TILE, "merge buffers");
 };
 
 // ---- bulk-copy ring primitives (shared-memory addresses)
@@ -100,8 +113,12 @@ __device__ __forceinline__ void a_bulk_g2s(uint32_t dst, const void* src, uint32
                  : "memory");
 }
 
+__device__ __forceinline__ void a_bar_arrive(uint32_t b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(b) : "memory");
+}
+
 template <int HD, int GROUP>
-__global__ void __launch_bounds__(ATTN_THREADS)
+__global__ void __launch_bounds__(ATTN_THREADS, 1)
 k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const float* __restrict__ vnew,
               float* __restrict__ kc, float* __restrict__ vc, const float* __restrict__ rope_cs,
               const int* __restrict__ d_pos, int n_kv, int max_seq, int grid_splits,
@@ -113,8 +130,12 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
     float* qs = sm;                       // [GROUP][HD] rotated q
     float* kn = qs + GROUP * HD;          // [HD] rotated new k
     float* vn = kn + HD;                  // [HD] new v
-    float* S = vn + HD;                   // [P][8] scores, then probabilities
-    float* st = S + C::SF;                // [GROUP] max, [GROUP] sum (8 + 8)
+    float* pw_all = vn + HD;              // [CWARPS][TP][8] each warp's scores, then probabilities
+    float* lm = pw_all + ATTN_CWARPS * C::TP * 8;   // [GROUP] merge: sum over the splits
+    // items the producer has issued: a consumer waits for its item to be
+    // issued before it waits on the slot's barrier (a slot's barrier only
+    // tells one generation from the next, and warps wait out of item order)
+    volatile int* issued = reinterpret_cast<volatile int*>(lm + 8);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int kvh = blockIdx.x / grid_splits, split = blockIdx.x % grid_splits;
@@ -125,12 +146,25 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
     }
     const int seq = pos + 1;
     int P = (seq + grid_splits - 1) / grid_splits;
-    P = (P + 31) & ~31;
+    P = (P + C::TP - 1) / C::TP * C::TP;
     const int nsplit = (seq + P - 1) / P;
     if (split >= nsplit) return;
     const int s0 = split * P, n = min(seq, s0 + P) - s0;
     const bool owner = pos >= s0 && pos < s0 + n;   // this split holds the new row
+    const size_t head_base = (size_t)kvh * max_seq * HD;
+    const int T = (n + C::TP - 1) / C::TP;
 
+    unsigned char* smb = reinterpret_cast<unsigned char*>(sm);
+    float* ring = reinterpret_cast<float*>(smb + C::RING_OFF);
+    const uint32_t full = a_sptr(smb + C::BAR_OFF), empty = full + 8 * C::R;
+    if (tid == 0) {
+        for (int r = 0; r < C::R; r++) {
+            a_bar_init(full + 8 * r, 1);
+            a_bar_init(empty + 8 * r, 1);   // the warp that owns the tile releases it
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        *issued = 0;
+    }
     // ---- RoPE (reference rounding: a*c - b*s, a*s + b*c, no contraction)
     const float* cs = rope_cs + (size_t)pos * HD;
     for (int e = tid; e < (GROUP + 1) * (HD / 2); e += ATTN_THREADS) {
@@ -143,8 +177,6 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
     }
     for (int i = tid; i < HD; i += ATTN_THREADS) vn[i] = vnew[(size_t)kvh * HD + i];
     __syncthreads();
-
-    const size_t head_base = (size_t)kvh * max_seq * HD;
     if (owner) {   // KV append at slot pos (the ring index pos % max_seq == pos here)
         for (int i = tid; i < HD; i += ATTN_THREADS) {
             kc[head_base + (size_t)pos * HD + i] = kn[i];
@@ -152,61 +184,85 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
         }
     }
 
-    // ---- K / V tiles stream through a ring of R bulk copies: item i < T is K
-    // tile i, item T + i is V tile i; item i lands in stage i % R.  Thread 0
-    // issues item i + R once every thread is done with item i (the
-    // __syncthreads after each tile).  The row of the new position is read
-    // from kn / vn, never from the tile (the copy may precede the append).
-    unsigned char* smb = reinterpret_cast<unsigned char*>(sm);
-    float* ring = reinterpret_cast<float*>(smb + C::RING_OFF);
-    const uint32_t bars = a_sptr(smb + C::BAR_OFF);
-    const int T = (n + C::TP - 1) / C::TP;
-    auto issue = [&](int it) {
-        const bool isv = it >= T;
-        const int t = isv ? it - T : it;
-        const int rows = min(C::TP, n - t * C::TP);
-        const float* src = (isv ? vc : kc) + head_base + (size_t)(s0 + t * C::TP) * HD;
-        const uint32_t bar = bars + 8 * (it % C::R);
-        a_bar_expect(bar, rows * HD * 4);
-        a_bulk_g2s(a_sptr(ring + (it % C::R) * C::TILE), src, rows * HD * 4, bar);
-    };
-    if (tid == 0) {
-        for (int r = 0; r < C::R; r++) a_bar_init(bars + 8 * r, 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        for (int it = 0; it < C::R && it < 2 * T; it++) issue(it);
+    // ---- items: 2t = K tile t, 2t + 1 = V tile t, in slot item % R.  Tile t
+    // belongs to consumer warp t % CWARPS, which releases both of its slots.
+    // The row of the new position is read from kn / vn, never from a tile
+    // (the copy may precede the append).
+    if (warp == ATTN_CWARPS) {   // ---- producer
+        if (lane == 0) {
+            bool ok = true;
+            int it = 0;
+            for (; it < 2 * T; it++) {
+                const int sl = it % C::R;
+                if (it >= C::R && !a_bar_wait(empty + 8 * sl, ((it / C::R) - 1) & 1)) {
+                    ok = false;
+                    atomicExch(err, (unsigned)(-GB_ETIMEOUT));
+                    break;
+                }
+                const int t = it >> 1;
+                const int rows = min(C::TP, n - t * C::TP);
+                const float* src = ((it & 1) ? vc : kc) + head_base + (size_t)(s0 + t * C::TP) * HD;
+                a_bar_expect(full + 8 * sl, rows * HD * 4);
+                a_bulk_g2s(a_sptr(ring + sl * C::TILE), src, rows * HD * 4, full + 8 * sl);
+                __threadfence_block();
+                *issued = it + 1;
+            }
+            // do not retire while a copy may still be landing in the ring
+            for (int j = it > C::R ? it - C::R : 0; ok && j < it; j++)
+                if (!a_bar_wait(empty + 8 * (j % C::R), (j / C::R) & 1)) {
+                    ok = false;
+                    atomicExch(err, (unsigned)(-GB_ETIMEOUT));
+                }
+        }
+        return;
     }
-    __syncthreads();
+
+    // ---- consumer warps: each runs its own online softmax over its tiles
+    const float scale = 1.0f / sqrtf((float)HD);
+    const int lp = lane % C::LPP, pw = lane / C::LPP;
+    float qr[GROUP][C::DPL];
+#pragma unroll
+    for (int h = 0; h < GROUP; h++)
+#pragma unroll
+        for (int j = 0; j < C::DPL / 4; j++) {
+            const float4 v = *reinterpret_cast<const float4*>(qs + h * HD + j * C::LPP * 4 + lp * 4);
+            qr[h][4 * j] = v.x; qr[h][4 * j + 1] = v.y; qr[h][4 * j + 2] = v.z; qr[h][4 * j + 3] = v.w;
+        }
+    float* pw8 = pw_all + warp * C::TP * 8;   // this warp's [TP][8]
+    const int ch = lane % C::CH, rl = lane / C::CH;
+    float m[GROUP], l[GROUP];
+    float4 acc[GROUP];
+#pragma unroll
+    for (int h = 0; h < GROUP; h++) {
+        m[h] = -INFINITY;
+        l[h] = 0.f;
+        acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     bool ok = true;
-    // every issued copy is waited on (bounded), so no copy is still landing
-    // in this CTA's shared memory when it exits, even after a timeout
     auto wait_item = [&](int it) {
-        if (!a_bar_wait(bars + 8 * (it % C::R), (it / C::R) & 1) && ok) {
+        bool got = true;
+        if (*issued <= it) {   // bounded (2 s), like every wait here
+            const uint64_t t0 = a_gtimer();
+            while (*issued <= it)
+                if (a_gtimer() - t0 > 2000000000ull) { got = false; break; }
+        }
+        if (got) got = a_bar_wait(full + 8 * (it % C::R), (it / C::R) & 1);
+        if (!got && ok) {
             ok = false;
             atomicExch(err, (unsigned)(-GB_ETIMEOUT));
         }
     };
-
-    // ---- pass 1: scores
-    const float scale = 1.0f / sqrtf((float)HD);
-    {
-        const int lp = lane % C::LPP, pw = lane / C::LPP;
-        float qr[GROUP][C::DPL];
-#pragma unroll
-        for (int h = 0; h < GROUP; h++)
-#pragma unroll
-            for (int j = 0; j < C::DPL / 4; j++) {
-                const float4 v = *reinterpret_cast<const float4*>(qs + h * HD + j * C::LPP * 4 + lp * 4);
-                qr[h][4 * j] = v.x; qr[h][4 * j + 1] = v.y; qr[h][4 * j + 2] = v.z; qr[h][4 * j + 3] = v.w;
-            }
-        for (int t = 0; t < T; t++) {
-            wait_item(t);
-            const float* tile = ring + (t % C::R) * C::TILE;
-            const int nt = min(C::TP, n - t * C::TP);
-            for (int base = warp * C::PPW; base < nt; base += 8 * C::PPW) {
-                const int r = base + pw;
+    for (int t = warp; t < T; t += ATTN_CWARPS) {
+        const int nt = min(C::TP, n - t * C::TP);
+        const int kit = 2 * t, vit = 2 * t + 1;
+        // ---- scores of K tile t: LPP lanes per row, dot products for all heads
+        wait_item(kit);
+        {
+            const float* tile = ring + (kit % C::R) * C::TILE;
+            for (int r0 = 0; r0 < nt; r0 += C::PPW) {
+                const int r = r0 + pw;
                 const int rr = r < nt ? r : 0;
-                const int s = t * C::TP + rr;
-                const float* krow = (s0 + s == pos) ? kn : tile + rr * HD;
+                const float* krow = (s0 + t * C::TP + rr == pos) ? kn : tile + rr * HD;
                 float4 kr[C::DPL / 4];
 #pragma unroll
                 for (int j = 0; j < C::DPL / 4; j++) kr[j] = *reinterpret_cast<const float4*>(krow + j * C::LPP * 4 + lp * 4);
@@ -228,96 +284,113 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
                     float v = dots[0];
 #pragma unroll
                     for (int h = 1; h < GROUP; h++) if (lp == h) v = dots[h];
-                    S[s * 8 + lp] = __fmul_rn(v, scale);
+                    pw8[r * 8 + lp] = __fmul_rn(v, scale);
                 }
             }
-            __syncthreads();
-            if (tid == 0 && t + C::R < 2 * T) issue(t + C::R);
         }
-    }
-    __syncthreads();
-
-    // ---- pass 2: per-head max, exp, sum over this split
-    if (warp < GROUP) {
-        const int h = warp;
-        float m = -INFINITY;
-        for (int s = lane; s < n; s += 32) m = fmaxf(m, S[s * 8 + h]);
-        m = warp_max(m);
-        float l = 0.f;
-        for (int s = lane; s < n; s += 32) {
-            const float p = expf(S[s * 8 + h] - m);
-            S[s * 8 + h] = p;
-            l += p;
+        __syncwarp();
+        if (lane == 0) a_bar_arrive(empty + 8 * (kit % C::R));   // the K slot is free
+        // ---- online softmax over the tile: lane r holds row r
+        float alpha[GROUP];
+#pragma unroll
+        for (int h = 0; h < GROUP; h++) {
+            const float v = lane < nt ? pw8[lane * 8 + h] : -INFINITY;
+            const float mn = fmaxf(m[h], warp_max(v));
+            const float p = lane < nt ? expf(v - mn) : 0.f;
+            alpha[h] = expf(m[h] - mn);   // 0 on the warp's first tile (m = -inf)
+            l[h] = fmaf(l[h], alpha[h], warp_sum(p));
+            m[h] = mn;
+            pw8[lane * 8 + h] = p;
         }
-        l = warp_sum(l);
-        if (lane == 0) { st[h] = m; st[8 + h] = l; }
-    }
-    __syncthreads();
-
-    // ---- pass 3: o_h = sum_s p_h[s] V[s]
-    float4 acc[GROUP];
+        __syncwarp();
+        // ---- o_h = o_h * alpha_h + sum_r p_h[r] V[r]
+        wait_item(vit);
+        {
+            const float* vt = ring + (vit % C::R) * C::TILE;
 #pragma unroll
-    for (int h = 0; h < GROUP; h++) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
-    const int vl = lane % C::VL, vr = lane / C::VL;
-    for (int t = 0; t < T; t++) {
-        const int it = T + t;
-        wait_item(it);
-        const float* tile = ring + (it % C::R) * C::TILE;
-        const int nt = min(C::TP, n - t * C::TP);
-        for (int r = warp * C::RPW + vr; r < nt; r += 8 * C::RPW) {
-            const int s = t * C::TP + r;
-            const float4 vv = (s0 + s == pos) ? *reinterpret_cast<const float4*>(vn + vl * 4)
-                                              : *reinterpret_cast<const float4*>(tile + r * HD + vl * 4);
-            float p[8];
-            const float4 p0 = *reinterpret_cast<const float4*>(S + s * 8);
-            p[0] = p0.x; p[1] = p0.y; p[2] = p0.z; p[3] = p0.w;
-            if (GROUP > 4) {
-                const float4 p1 = *reinterpret_cast<const float4*>(S + s * 8 + 4);
-                p[4] = p1.x; p[5] = p1.y; p[6] = p1.z; p[7] = p1.w;
-            }
+            for (int h = 0; h < GROUP; h++)
+                acc[h] = make_float4(acc[h].x * alpha[h], acc[h].y * alpha[h], acc[h].z * alpha[h], acc[h].w * alpha[h]);
+            for (int r = rl; r < nt; r += C::RPL) {
+                const float4 vv = (s0 + t * C::TP + r == pos) ? *reinterpret_cast<const float4*>(vn + ch * 4)
+                                                              : *reinterpret_cast<const float4*>(vt + r * HD + ch * 4);
+                float p[8];
+                const float4 p0 = *reinterpret_cast<const float4*>(pw8 + r * 8);
+                p[0] = p0.x; p[1] = p0.y; p[2] = p0.z; p[3] = p0.w;
+                if (GROUP > 4) {
+                    const float4 p1 = *reinterpret_cast<const float4*>(pw8 + r * 8 + 4);
+                    p[4] = p1.x; p[5] = p1.y; p[6] = p1.z; p[7] = p1.w;
+                }
 #pragma unroll
-            for (int h = 0; h < GROUP; h++) {
-                float2 lo = ffma2(make_float2(p[h], p[h]), make_float2(vv.x, vv.y), make_float2(acc[h].x, acc[h].y));
-                float2 hi = ffma2(make_float2(p[h], p[h]), make_float2(vv.z, vv.w), make_float2(acc[h].z, acc[h].w));
-                acc[h] = make_float4(lo.x, lo.y, hi.x, hi.y);
+                for (int h = 0; h < GROUP; h++) {
+                    float2 lo = ffma2(make_float2(p[h], p[h]), make_float2(vv.x, vv.y), make_float2(acc[h].x, acc[h].y));
+                    float2 hi = ffma2(make_float2(p[h], p[h]), make_float2(vv.z, vv.w), make_float2(acc[h].z, acc[h].w));
+                    acc[h] = make_float4(lo.x, lo.y, hi.x, hi.y);
+                }
             }
         }
-        __syncthreads();
-        if (tid == 0 && it + C::R < 2 * T) issue(it + C::R);
+        __syncwarp();
+        if (lane == 0) a_bar_arrive(empty + 8 * (vit % C::R));   // the V slot is free
     }
-    __syncthreads();   // S is dead from here on; reuse it as the reduction buffer
-    float* red = S;
+    // lanes that covered other rows of the same columns (head_dim < 128)
 #pragma unroll
-    for (int h = 0; h < GROUP; h++)
-        *reinterpret_cast<float4*>(red + ((warp * C::RPW + vr) * GROUP + h) * HD + vl * 4) = acc[h];
-    __syncthreads();
+    for (int o = C::CH; o < 32; o <<= 1)
+#pragma unroll
+        for (int h = 0; h < GROUP; h++) {
+            acc[h].x += __shfl_xor_sync(0xffffffffu, acc[h].x, o);
+            acc[h].y += __shfl_xor_sync(0xffffffffu, acc[h].y, o);
+            acc[h].z += __shfl_xor_sync(0xffffffffu, acc[h].z, o);
+            acc[h].w += __shfl_xor_sync(0xffffffffu, acc[h].w, o);
+        }
 
+    // ---- merge the warps' (m, l, o) in the ring (every tile is consumed)
+    asm volatile("bar.sync 1, %0;" ::"n"(ATTN_CWARPS * 32) : "memory");
+    constexpr int WS = HD + 4;   // m, l, 2 pad, o[HD]: o stays 16-byte aligned
+    float* wst = ring;           // [CWARPS][GROUP][WS]
+#pragma unroll
+    for (int h = 0; h < GROUP; h++) {
+        float* w = wst + (warp * GROUP + h) * WS;
+        if (lane == 0) { w[0] = m[h]; w[1] = l[h]; }
+        if (lane < C::CH) *reinterpret_cast<float4*>(w + 4 + ch * 4) = acc[h];
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(ATTN_CWARPS * 32) : "memory");
+    const int ctid = tid;   // 0 .. 255
     const bool single = nsplit == 1;
     float* my = part + ((size_t)kvh * grid_splits + split) * GROUP * (HD + 2);
-    for (int e = tid; e < GROUP * HD; e += ATTN_THREADS) {
-        float o = 0.f;
-#pragma unroll
-        for (int w = 0; w < 8 * C::RPW; w++) o += red[w * GROUP * HD + e];
+    for (int e = ctid; e < GROUP * HD; e += ATTN_CWARPS * 32) {
         const int h = e / HD, d = e % HD;
-        if (single) out[(size_t)(kvh * GROUP + h) * HD + d] = o / st[8 + h];
-        else my[h * (HD + 2) + 2 + d] = o;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < ATTN_CWARPS; w++) M = fmaxf(M, wst[(w * GROUP + h) * WS]);
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int w = 0; w < ATTN_CWARPS; w++) {
+            const float* ws = wst + (w * GROUP + h) * WS;
+            const float a = ws[0] == -INFINITY ? 0.f : expf(ws[0] - M);   // warps without tiles
+            L = fmaf(ws[1], a, L);
+            O = fmaf(ws[4 + d], a, O);
+        }
+        if (single) {
+            out[(size_t)(kvh * GROUP + h) * HD + d] = O / L;
+        } else {
+            my[h * (HD + 2) + 2 + d] = O;
+            if (d == 0) { my[h * (HD + 2)] = M; my[h * (HD + 2) + 1] = L; }
+        }
     }
     if (single) return;
-    if (tid < GROUP) { my[tid * (HD + 2)] = st[tid]; my[tid * (HD + 2) + 1] = st[8 + tid]; }
 
     // ---- merge in the last CTA of this KV head
     __shared__ unsigned last;
     __threadfence();
-    __syncthreads();
-    if (tid == 0) last = (atomicAdd(&tickets[kvh], 1u) == (unsigned)(nsplit - 1));
-    __syncthreads();
+    asm volatile("bar.sync 1, %0;" ::"n"(ATTN_CWARPS * 32) : "memory");
+    if (ctid == 0) last = (atomicAdd(&tickets[kvh], 1u) == (unsigned)(nsplit - 1));
+    asm volatile("bar.sync 1, %0;" ::"n"(ATTN_CWARPS * 32) : "memory");
     if (!last) return;
     __threadfence();
     const float* base = part + (size_t)kvh * grid_splits * GROUP * (HD + 2);
     // split weights w_j = exp(m_j - M) and L = sum l_j w_j once per head (one
     // warp per head), then every output is a weighted sum over the splits in
-    // split order; S (dead) holds the weights [GROUP][nsplit]
-    float* wbuf = S;
+    // split order; the ring (free) holds the weights [GROUP][nsplit]
+    float* wbuf = ring + ATTN_CWARPS * GROUP * WS;
     if (warp < GROUP) {
         const int h = warp;
         float M = -INFINITY;
@@ -331,19 +404,19 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
             L = fmaf(__ldcg(pj + 1), w, L);
         }
         L = warp_sum(L);
-        if (lane == 0) st[8 + h] = L;
+        if (lane == 0) lm[h] = L;
     }
-    __syncthreads();
-    for (int e = tid; e < GROUP * HD; e += ATTN_THREADS) {
+    asm volatile("bar.sync 1, %0;" ::"n"(ATTN_CWARPS * 32) : "memory");
+    for (int e = ctid; e < GROUP * HD; e += ATTN_CWARPS * 32) {
         const int h = e / HD, d = e % HD;
         const float* wj = wbuf + h * nsplit;
         const float* pj = base + (size_t)h * (HD + 2) + 2 + d;
         float O = 0.f;
 #pragma unroll 8
         for (int j = 0; j < nsplit; j++) O = fmaf(__ldcg(pj + (size_t)j * GROUP * (HD + 2)), wj[j], O);
-        out[(size_t)(kvh * GROUP + h) * HD + d] = O / st[8 + h];
+        out[(size_t)(kvh * GROUP + h) * HD + d] = O / lm[h];
     }
-    if (tid == 0) tickets[kvh] = 0u;   // every split has arrived: safe to rearm
+    if (ctid == 0) tickets[kvh] = 0u;   // every split has arrived: safe to rearm
 }
 
 // part: split partials; tickets: n_kv per-KV-head counters (zero between
@@ -373,8 +446,6 @@ static int attn_dispatch(const float* q, const float* k, const float* v, float* 
                          const int* d_pos, int n_heads, int n_kv, int head_dim, int max_seq, float* out,
                          float* part, unsigned* tickets, unsigned* err, cudaStream_t st) {
     const int group = n_heads / n_kv;
-    // the merge keeps one weight per (head, split) in the score buffer
-    if ((size_t)group * attn_grid_splits(n_kv, max_seq) > (size_t)ATTN_MAX_P * 8) return GB_ELIMIT;
     cudaError_t e = cudaErrorInvalidValue;
 #define GB_ATTN_CASE(HDV, GV)                                                                                       \
     if (head_dim == HDV && group == GV)                                                                             \
