@@ -40,7 +40,7 @@
 
 namespace gb {
 
-constexpr int ATTN_CWARPS = 8;                        // consumer warps
+constexpr int ATTN_CWARPS = 16;                       // consumer warps
 constexpr int ATTN_THREADS = (ATTN_CWARPS + 1) * 32;   // + the producer warp
 constexpr int ATTN_SMEM_MAX = 227 * 1024;
 
@@ -56,23 +56,28 @@ int attn_grid_splits(int n_kv, int max_seq) {
 
 template <int HD, int GROUP>
 struct AttnCfg {
-    static constexpr int DPL = GROUP <= 4 ? 16 : 8;   // K dims per lane (scores)
+    // a warp serves HPW query heads of one tile: NHG head groups, so TW warps
+    // (tile lanes) work on different tiles at the same time
+    static constexpr int HPW = GROUP < 2 ? GROUP : 2;
+    static constexpr int NHG = GROUP / HPW;
+    static constexpr int TW = ATTN_CWARPS / NHG;
+    static constexpr int DPL = 16;                    // K dims per lane (scores)
     static constexpr int LPP = HD / DPL;              // lanes per K row
     static constexpr int PPW = 32 / LPP;              // K rows per warp step
     static constexpr int TP = 32;                     // positions per K / V tile
     static constexpr int TILE = TP * HD;              // floats per tile
     static constexpr int CH = HD / 4;                 // float4 columns of a V row
     static constexpr int RPL = 32 / CH;               // rows a warp's P.V step covers
-    // shared: q[GROUP][HD] | k_new[HD] | v_new[HD] | per-warp p[TP][8] |
+    // shared: q[GROUP][HD] | k_new[HD] | v_new[HD] | per-warp p[TP][2] |
     // merge sums [8] | issued-item count [4] | ring[R][TILE] | full[R], empty[R]
-    static constexpr int HEAD_FLOATS = GROUP * HD + 2 * HD + ATTN_CWARPS * TP * 8 + 8 + 4;
+    static constexpr int HEAD_FLOATS = GROUP * HD + 2 * HD + ATTN_CWARPS * TP * 2 + 8 + 4;
     static constexpr size_t RING_OFF = ((size_t)HEAD_FLOATS * sizeof(float) + 127) / 128 * 128;
     static constexpr int R0 = (int)((ATTN_SMEM_MAX - RING_OFF - 512) / (TILE * sizeof(float)));
     static constexpr int R = R0 < 24 ? R0 : 24;       // items (K or V tiles) in flight per CTA
     static constexpr size_t BAR_OFF = RING_OFF + (size_t)R * TILE * sizeof(float);
     static constexpr size_t SMEM = BAR_OFF + 2 * R * sizeof(unsigned long long);
     // the warps' (m, l, o) merge reuses the ring
-    static_assert(ATTN_CWARPS * GROUP * (HD + 4) + GROUP * GB_NUM_SMS <= R * TILE, "merge buffers");
+    static_assert(TW * GROUP * (HD + 4) + GROUP * GB_NUM_SMS <= R * TILE, "merge buffers");
 };
 
 // ---- bulk-copy ring primitives (shared-memory addresses)
@@ -130,8 +135,8 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
     float* qs = sm;                       // [GROUP][HD] rotated q
     float* kn = qs + GROUP * HD;          // [HD] rotated new k
     float* vn = kn + HD;                  // [HD] new v
-    float* pw_all = vn + HD;              // [CWARPS][TP][8] each warp's scores, then probabilities
-    float* lm = pw_all + ATTN_CWARPS * C::TP * 8;   // [GROUP] merge: sum over the splits
+    float* pw_all = vn + HD;              // [CWARPS][TP][2] each warp's scores, then probabilities
+    float* lm = pw_all + ATTN_CWARPS * C::TP * 2;   // [GROUP] merge: sum over the splits
     // items the producer has issued: a consumer waits for its item to be
     // issued before it waits on the slot's barrier (a slot's barrier only
     // tells one generation from the next, and warps wait out of item order)
@@ -160,7 +165,7 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
     if (tid == 0) {
         for (int r = 0; r < C::R; r++) {
             a_bar_init(full + 8 * r, 1);
-            a_bar_init(empty + 8 * r, 1);   // the warp that owns the tile releases it
+            a_bar_init(empty + 8 * r, C::NHG);   // the warps that own the tile release it
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         *issued = 0;
@@ -185,7 +190,8 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
     }
 
     // ---- items: 2t = K tile t, 2t + 1 = V tile t, in slot item % R.  Tile t
-    // belongs to consumer warp t % CWARPS, which releases both of its slots.
+    // belongs to the NHG consumer warps of tile lane t % TW (one per group of
+    // HPW query heads), which release both of its slots.
     // The row of the new position is read from kn / vn, never from a tile
     // (the copy may precede the append).
     if (warp == ATTN_CWARPS) {   // ---- producer
@@ -218,25 +224,27 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
     }
 
     // ---- consumer warps: each runs its own online softmax over its tiles
+    // for its HPW query heads hg * HPW ..
+    const int hg = warp / C::TW, tl = warp % C::TW;
     const float scale = 1.0f / sqrtf((float)HD);
     const int lp = lane % C::LPP, pw = lane / C::LPP;
-    float qr[GROUP][C::DPL];
+    float qr[C::HPW][C::DPL];
 #pragma unroll
-    for (int h = 0; h < GROUP; h++)
+    for (int j = 0; j < C::HPW; j++)
 #pragma unroll
-        for (int j = 0; j < C::DPL / 4; j++) {
-            const float4 v = *reinterpret_cast<const float4*>(qs + h * HD + j * C::LPP * 4 + lp * 4);
-            qr[h][4 * j] = v.x; qr[h][4 * j + 1] = v.y; qr[h][4 * j + 2] = v.z; qr[h][4 * j + 3] = v.w;
+        for (int i = 0; i < C::DPL / 4; i++) {
+            const float4 v = *reinterpret_cast<const float4*>(qs + (hg * C::HPW + j) * HD + i * C::LPP * 4 + lp * 4);
+            qr[j][4 * i] = v.x; qr[j][4 * i + 1] = v.y; qr[j][4 * i + 2] = v.z; qr[j][4 * i + 3] = v.w;
         }
-    float* pw8 = pw_all + warp * C::TP * 8;   // this warp's [TP][8]
+    float* pw2 = pw_all + warp * C::TP * 2;   // this warp's [TP][2]
     const int ch = lane % C::CH, rl = lane / C::CH;
-    float m[GROUP], l[GROUP];
-    float4 acc[GROUP];
+    float m[C::HPW], l[C::HPW];
+    float4 acc[C::HPW];
 #pragma unroll
-    for (int h = 0; h < GROUP; h++) {
-        m[h] = -INFINITY;
-        l[h] = 0.f;
-        acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < C::HPW; j++) {
+        m[j] = -INFINITY;
+        l[j] = 0.f;
+        acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
     bool ok = true;
     auto wait_item = [&](int it) {
@@ -252,55 +260,51 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
             atomicExch(err, (unsigned)(-GB_ETIMEOUT));
         }
     };
-    for (int t = warp; t < T; t += ATTN_CWARPS) {
+    for (int t = tl; t < T; t += C::TW) {
         const int nt = min(C::TP, n - t * C::TP);
         const int kit = 2 * t, vit = 2 * t + 1;
-        // ---- scores of K tile t: LPP lanes per row, dot products for all heads
+        // ---- scores of K tile t: LPP lanes per row, dot products for HPW heads
         wait_item(kit);
         {
             const float* tile = ring + (kit % C::R) * C::TILE;
+#pragma unroll 2
             for (int r0 = 0; r0 < nt; r0 += C::PPW) {
                 const int r = r0 + pw;
                 const int rr = r < nt ? r : 0;
                 const float* krow = (s0 + t * C::TP + rr == pos) ? kn : tile + rr * HD;
                 float4 kr[C::DPL / 4];
 #pragma unroll
-                for (int j = 0; j < C::DPL / 4; j++) kr[j] = *reinterpret_cast<const float4*>(krow + j * C::LPP * 4 + lp * 4);
-                float dots[GROUP];
+                for (int i = 0; i < C::DPL / 4; i++) kr[i] = *reinterpret_cast<const float4*>(krow + i * C::LPP * 4 + lp * 4);
+                float dots[C::HPW];
 #pragma unroll
-                for (int h = 0; h < GROUP; h++) {
+                for (int j = 0; j < C::HPW; j++) {
                     float2 acc2 = make_float2(0.f, 0.f);
 #pragma unroll
-                    for (int j = 0; j < C::DPL / 4; j++) {
-                        acc2 = ffma2(make_float2(qr[h][4 * j], qr[h][4 * j + 1]), make_float2(kr[j].x, kr[j].y), acc2);
-                        acc2 = ffma2(make_float2(qr[h][4 * j + 2], qr[h][4 * j + 3]), make_float2(kr[j].z, kr[j].w), acc2);
+                    for (int i = 0; i < C::DPL / 4; i++) {
+                        acc2 = ffma2(make_float2(qr[j][4 * i], qr[j][4 * i + 1]), make_float2(kr[i].x, kr[i].y), acc2);
+                        acc2 = ffma2(make_float2(qr[j][4 * i + 2], qr[j][4 * i + 3]), make_float2(kr[i].z, kr[i].w), acc2);
                     }
                     float d = acc2.x + acc2.y;
 #pragma unroll
                     for (int o = C::LPP / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-                    dots[h] = d;
+                    dots[j] = d;
                 }
-                if (r < nt && lp < GROUP) {
-                    float v = dots[0];
-#pragma unroll
-                    for (int h = 1; h < GROUP; h++) if (lp == h) v = dots[h];
-                    pw8[r * 8 + lp] = __fmul_rn(v, scale);
-                }
+                if (r < nt && lp < C::HPW) pw2[r * 2 + lp] = __fmul_rn(lp ? dots[C::HPW - 1] : dots[0], scale);
             }
         }
         __syncwarp();
-        if (lane == 0) a_bar_arrive(empty + 8 * (kit % C::R));   // the K slot is free
+        if (lane == 0) a_bar_arrive(empty + 8 * (kit % C::R));   // this warp is done with the K slot
         // ---- online softmax over the tile: lane r holds row r
-        float alpha[GROUP];
+        float alpha[C::HPW];
 #pragma unroll
-        for (int h = 0; h < GROUP; h++) {
-            const float v = lane < nt ? pw8[lane * 8 + h] : -INFINITY;
-            const float mn = fmaxf(m[h], warp_max(v));
+        for (int j = 0; j < C::HPW; j++) {
+            const float v = lane < nt ? pw2[lane * 2 + j] : -INFINITY;
+            const float mn = fmaxf(m[j], warp_max(v));
             const float p = lane < nt ? expf(v - mn) : 0.f;
-            alpha[h] = expf(m[h] - mn);   // 0 on the warp's first tile (m = -inf)
-            l[h] = fmaf(l[h], alpha[h], warp_sum(p));
-            m[h] = mn;
-            pw8[lane * 8 + h] = p;
+            alpha[j] = expf(m[j] - mn);   // 0 on the warp's first tile (m = -inf)
+            l[j] = fmaf(l[j], alpha[j], warp_sum(p));
+            m[j] = mn;
+            pw2[lane * 2 + j] = p;
         }
         __syncwarp();
         // ---- o_h = o_h * alpha_h + sum_r p_h[r] V[r]
@@ -308,49 +312,45 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
         {
             const float* vt = ring + (vit % C::R) * C::TILE;
 #pragma unroll
-            for (int h = 0; h < GROUP; h++)
-                acc[h] = make_float4(acc[h].x * alpha[h], acc[h].y * alpha[h], acc[h].z * alpha[h], acc[h].w * alpha[h]);
+            for (int j = 0; j < C::HPW; j++)
+                acc[j] = make_float4(acc[j].x * alpha[j], acc[j].y * alpha[j], acc[j].z * alpha[j], acc[j].w * alpha[j]);
+#pragma unroll 4
             for (int r = rl; r < nt; r += C::RPL) {
                 const float4 vv = (s0 + t * C::TP + r == pos) ? *reinterpret_cast<const float4*>(vn + ch * 4)
                                                               : *reinterpret_cast<const float4*>(vt + r * HD + ch * 4);
-                float p[8];
-                const float4 p0 = *reinterpret_cast<const float4*>(pw8 + r * 8);
-                p[0] = p0.x; p[1] = p0.y; p[2] = p0.z; p[3] = p0.w;
-                if (GROUP > 4) {
-                    const float4 p1 = *reinterpret_cast<const float4*>(pw8 + r * 8 + 4);
-                    p[4] = p1.x; p[5] = p1.y; p[6] = p1.z; p[7] = p1.w;
-                }
+                const float2 pp = *reinterpret_cast<const float2*>(pw2 + r * 2);
 #pragma unroll
-                for (int h = 0; h < GROUP; h++) {
-                    float2 lo = ffma2(make_float2(p[h], p[h]), make_float2(vv.x, vv.y), make_float2(acc[h].x, acc[h].y));
-                    float2 hi = ffma2(make_float2(p[h], p[h]), make_float2(vv.z, vv.w), make_float2(acc[h].z, acc[h].w));
-                    acc[h] = make_float4(lo.x, lo.y, hi.x, hi.y);
+                for (int j = 0; j < C::HPW; j++) {
+                    const float pj = j ? pp.y : pp.x;
+                    float2 lo = ffma2(make_float2(pj, pj), make_float2(vv.x, vv.y), make_float2(acc[j].x, acc[j].y));
+                    float2 hi = ffma2(make_float2(pj, pj), make_float2(vv.z, vv.w), make_float2(acc[j].z, acc[j].w));
+                    acc[j] = make_float4(lo.x, lo.y, hi.x, hi.y);
                 }
             }
         }
         __syncwarp();
-        if (lane == 0) a_bar_arrive(empty + 8 * (vit % C::R));   // the V slot is free
+        if (lane == 0) a_bar_arrive(empty + 8 * (vit % C::R));   // this warp is done with the V slot
     }
     // lanes that covered other rows of the same columns (head_dim < 128)
 #pragma unroll
     for (int o = C::CH; o < 32; o <<= 1)
 #pragma unroll
-        for (int h = 0; h < GROUP; h++) {
-            acc[h].x += __shfl_xor_sync(0xffffffffu, acc[h].x, o);
-            acc[h].y += __shfl_xor_sync(0xffffffffu, acc[h].y, o);
-            acc[h].z += __shfl_xor_sync(0xffffffffu, acc[h].z, o);
-            acc[h].w += __shfl_xor_sync(0xffffffffu, acc[h].w, o);
+        for (int j = 0; j < C::HPW; j++) {
+            acc[j].x += __shfl_xor_sync(0xffffffffu, acc[j].x, o);
+            acc[j].y += __shfl_xor_sync(0xffffffffu, acc[j].y, o);
+            acc[j].z += __shfl_xor_sync(0xffffffffu, acc[j].z, o);
+            acc[j].w += __shfl_xor_sync(0xffffffffu, acc[j].w, o);
         }
 
     // ---- merge the warps' (m, l, o) in the ring (every tile is consumed)
     asm volatile("bar.sync 1, %0;" ::"n"(ATTN_CWARPS * 32) : "memory");
     constexpr int WS = HD + 4;   // m, l, 2 pad, o[HD]: o stays 16-byte aligned
-    float* wst = ring;           // [CWARPS][GROUP][WS]
+    float* wst = ring;           // [TW][GROUP][WS]
 #pragma unroll
-    for (int h = 0; h < GROUP; h++) {
-        float* w = wst + (warp * GROUP + h) * WS;
-        if (lane == 0) { w[0] = m[h]; w[1] = l[h]; }
-        if (lane < C::CH) *reinterpret_cast<float4*>(w + 4 + ch * 4) = acc[h];
+    for (int j = 0; j < C::HPW; j++) {
+        float* w = wst + (tl * GROUP + hg * C::HPW + j) * WS;
+        if (lane == 0) { w[0] = m[j]; w[1] = l[j]; }
+        if (lane < C::CH) *reinterpret_cast<float4*>(w + 4 + ch * 4) = acc[j];
     }
     asm volatile("bar.sync 1, %0;" ::"n"(ATTN_CWARPS * 32) : "memory");
     const int ctid = tid;   // 0 .. 255
@@ -360,10 +360,10 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
         const int h = e / HD, d = e % HD;
         float M = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < ATTN_CWARPS; w++) M = fmaxf(M, wst[(w * GROUP + h) * WS]);
+        for (int w = 0; w < C::TW; w++) M = fmaxf(M, wst[(w * GROUP + h) * WS]);
         float L = 0.f, O = 0.f;
 #pragma unroll
-        for (int w = 0; w < ATTN_CWARPS; w++) {
+        for (int w = 0; w < C::TW; w++) {
             const float* ws = wst + (w * GROUP + h) * WS;
             const float a = ws[0] == -INFINITY ? 0.f : expf(ws[0] - M);   // warps without tiles
             L = fmaf(ws[1], a, L);
@@ -390,7 +390,7 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
     // split weights w_j = exp(m_j - M) and L = sum l_j w_j once per head (one
     // warp per head), then every output is a weighted sum over the splits in
     // split order; the ring (free) holds the weights [GROUP][nsplit]
-    float* wbuf = ring + ATTN_CWARPS * GROUP * WS;
+    float* wbuf = ring + C::TW * GROUP * WS;
     if (warp < GROUP) {
         const int h = warp;
         float M = -INFINITY;
