@@ -390,6 +390,7 @@ struct gb_model {
     // layer l - 1 and q/k/v of layer l, launch L = the last layer's wo,
     // gate/up, down and the output head
     ChainSet* chain = nullptr;
+    std::vector<int> chain_seg;       // segment s (before attention s) = launches [seg[s], seg[s + 1])
     bool chain_built = false;         // tried since the last weight change
     int chain_mode = -1;              // 1 / 0: gb_model_use_persistent; -1: GB_CHAIN
 };
@@ -570,6 +571,7 @@ static void drop_chain(gb_model* m) {
         chain_destroy(m->chain);
     }
     m->chain = nullptr;
+    m->chain_seg.clear();
     m->chain_built = false;
 }
 
@@ -591,6 +593,7 @@ extern "C" int gb_model_set_matrix(gb_model* m, int layer, int which, int dtype,
     drop_chain(m);
     return GB_OK;
 }
+extern "C" int gb_model_persistent(const gb_model* m) { return m && m->chain ? 1 : 0; }
 extern "C" int gb_model_use_persistent(gb_model* m, int on) {
     if (!m) return GB_EINVAL;
     m->chain_mode = on ? 1 : 0;
@@ -825,12 +828,19 @@ static int enqueue_step(gb_model* m, const int* d_token, const int* d_pos, float
     int rc;
     if ((rc = embed(m->emb, m->emb_dt, d_token, c.vocab_size, H, m->hidden, m->err, st, m->d_step))) return rc;
     if (m->chain) {   // persistent launches between the attention kernels
-        if ((rc = chain_launch(m->chain, 0, m->err, st))) return rc;
+        auto segment = [&](int sgi) {
+            for (int i = m->chain_seg[sgi]; i < m->chain_seg[sgi + 1]; i++) {
+                const int r = chain_launch(m->chain, i, m->err, st);
+                if (r) return r;
+            }
+            return (int)GB_OK;
+        };
+        if ((rc = segment(0))) return rc;
         for (int l = 0; l < c.n_layers; l++) {
             if ((rc = gb_attention_decode(m->q, m->k, m->v, gb_model_k_cache(m, l), gb_model_v_cache(m, l), m->rope,
                                           d_pos, m->nh, m->nkv, c.head_dim, c.max_seq, m->attn, m->attn_ws, st)))
                 return rc;
-            if ((rc = chain_launch(m->chain, l + 1, m->err, st))) return rc;
+            if ((rc = segment(l + 1))) return rc;
         }
         if (d_logits && d_logits != m->logits)
             GB_CUDA_TRY(cudaMemcpyAsync(d_logits, m->logits, (size_t)m->vocab_l * sizeof(float),
@@ -895,6 +905,17 @@ static bool chain_enabled() {
     return v;
 }
 
+// Phases per persistent launch (GB_CHAIN_PHASES, 1 .. CH_MAXP; default 4,
+// one launch per layer boundary).
+static int chain_max_phases() {
+    static const int v = [] {
+        const char* e = getenv("GB_CHAIN_PHASES");
+        const int n = e ? atoi(e) : 4;
+        return n < 1 ? 1 : (n > CH_MAXP ? CH_MAXP : n);
+    }();
+    return v;
+}
+
 static void build_chain(gb_model* m) {
     const gb_model_config& c = m->c;
     const int L = c.n_layers;
@@ -952,14 +973,24 @@ static void build_chain(gb_model* m) {
         dn.xf.x2 = m->up;
         ph.push_back(dn);
     };
-    first.push_back(0);
+    // segment s holds the phases between attention s - 1 and attention s; a
+    // segment is cut into launches of at most maxp phases
+    const int maxp = chain_max_phases();
+    std::vector<int> seg;
+    auto close_segment = [&](size_t p0) {
+        seg.push_back((int)first.size());
+        for (size_t p = p0; p < ph.size(); p += maxp) first.push_back((int)p);
+    };
+    size_t p0 = ph.size();
     qkv(0);
+    close_segment(p0);
     for (int l = 1; l < L; l++) {
-        first.push_back((int)ph.size());
+        p0 = ph.size();
         tail(l - 1);
         qkv(l);
+        close_segment(p0);
     }
-    first.push_back((int)ph.size());
+    p0 = ph.size();
     tail(L - 1);
     ChPhaseSpec lm;
     lm.m[0].dtype = m->lm_dt;
@@ -973,9 +1004,14 @@ static void build_chain(gb_model* m) {
     lm.xf.w = m->rms_final;
     lm.xf.eps = c.rms_eps;
     ph.push_back(lm);
+    close_segment(p0);
+    seg.push_back((int)first.size());
     first.push_back((int)ph.size());
     ChainSet* cs = nullptr;
-    if (chain_create(ph.data(), first.data(), (int)first.size() - 1, &cs) == GB_OK) m->chain = cs;
+    if (chain_create(ph.data(), first.data(), (int)first.size() - 1, &cs) == GB_OK) {
+        m->chain = cs;
+        m->chain_seg = seg;
+    }
 }
 
 static bool model_ready(gb_model* m) {
@@ -1102,7 +1138,8 @@ extern "C" int gb_model_launches_per_step(const gb_model* m) {
     // kernels that are not fused into a TMA matvec) + output head (+ final
     // norm when not fused) + argmax
     if (!m) return 0;
-    if (m->chain) return 1 + 1 + 2 * m->c.n_layers + 1;   // embed, q/k/v, attention + persistent launch per layer, argmax
+    if (m->chain)   // embed, persistent launches, attention per layer, argmax
+        return 1 + m->chain_seg.back() + m->c.n_layers + 1;
     int n = 1;
     for (int l = 0; l < m->c.n_layers; l++) {
         auto P = [&](int w) { return &m->plan[(size_t)l * GB_NMAT + w]; };

@@ -38,6 +38,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdlib>
+#include <type_traits>
 #include <map>
 #include <mutex>
 
@@ -596,8 +597,11 @@ struct MtArgs {
     int nm;
     float* part;        // [ncta][2][MT_GR] stream-K partial rows
     unsigned* tickets;  // [total groups], zero between launches
-    int nb, nch, T, ncta, S;
-    int unit;           // split granularity in items: 1, or nch (whole groups, no workspace)
+    int nb, T, ncta, S;
+    int ibase[MT_MAXM + 1];   // first item of matrix m (T = ibase[nm])
+    int nchm[MT_MAXM];        // items per 32-row group of matrix m
+    int fmt[MT_MAXM];         // matrix m is Q6_K (mixed-format launches)
+    int unit;           // split granularity in items: 1, or the items per group (whole groups, no workspace)
     // x transform applied while quantising (MV_X_*): RMSNorm with weight nw
     // and eps, or silu(x) * x2
     int xmode;
@@ -606,17 +610,34 @@ struct MtArgs {
     float eps;
 };
 
-// matrix of global group g
-__device__ __forceinline__ int mt_matrix(const MtArgs& a, int g) { return g >= a.gbase[1] ? (g >= a.gbase[2] ? 2 : 1) : 0; }
+// A launch whose matrices mix Q4_K and Q6_K (e.g. q, k and v): stage slots
+// sized for the larger stage, each stage consumed by its matrix's format.
+struct MtMix {
+    static constexpr int NC = 16;
+    static_assert(MtQ4K::NC == NC && MtQ6K::NC == NC, "one consumer layout");
+    static constexpr int STG = MtQ4K::STG > MtQ6K::STG ? MtQ4K::STG : MtQ6K::STG;
+    static constexpr bool S16 = true;
+};
+static_assert(MtQ4K::SI == 1 && MtQ6K::SI == 1, "one split item per stage");
+
+// matrix, group within it and item within the group of item t
+__device__ __forceinline__ void mt_locate(const MtArgs& a, int t, int& m, int& g, int& it) {
+    m = t >= a.ibase[1] ? (t >= a.ibase[2] ? 2 : 1) : 0;
+    const int u = t - a.ibase[m];
+    g = u / a.nchm[m];
+    it = u - g * a.nchm[m];
+}
 
 template <class F>
 __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_constant__ CUtensorMap tm0,
                                                             const __grid_constant__ CUtensorMap tm1,
                                                             const __grid_constant__ CUtensorMap tm2, const MtArgs a) {
     constexpr int MT_NC = F::NC;
+    constexpr bool MIXED = std::is_same<F, MtMix>::value;
+    constexpr bool FQ6 = std::is_same<F, MtQ6K>::value;
     extern __shared__ __align__(1024) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nb = a.nb, K = nb * 256, S = a.S, nch = a.nch;
+    const int nb = a.nb, K = nb * 256, S = a.S;
     const int NSLOT = S + 2;
     // shared layout: ring [S][F::STG] | x | zero[64] | red [NSLOT][MT_NC][MT_GR] | cnt | barriers
     const uint32_t sbase = sptr(smem);
@@ -646,18 +667,16 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
         if (lane == 0) {
             bool ok = true;
             int i = 0;
-            for (int t = t0; t < t1; i++) {
-                const int grp = t / nch, it = t - grp * nch;
-                const int n = min(min(F::SI, nch - it), t1 - t);
+            for (int t = t0; t < t1; i++, t++) {   // one item (one box) per stage
+                int m, g, it;
+                mt_locate(a, t, m, g, it);
                 const int s = i % S;
                 if (i >= S && !(ok = mbs_wait(bar_empty + 8 * s, ((i / S) - 1) & 1, &g_gb_device_err))) break;
-                const int m = mt_matrix(a, grp);
                 const CUtensorMap* tm = m == 0 ? &tm0 : (m == 1 ? &tm1 : &tm2);
-                mbs_expect(bar_full + 8 * s, n * F::ITEM);
-                for (int j = 0; j < n; j++)
-                    tma_load_3d(sbase + s * F::STG + j * F::ITEM, tm, 0, (grp - a.gbase[m]) * MT_GR,
-                                (it + j) * F::IG / F::ZUNIT, bar_full + 8 * s);
-                t += n;
+                const bool q6 = MIXED ? a.fmt[m] != 0 : FQ6;
+                // z: 16-block units of blocks (Q4_K), 8-block runs (Q6_K)
+                mbs_expect(bar_full + 8 * s, q6 ? MtQ6K::ITEM : MtQ4K::ITEM);
+                tma_load_3d(sbase + s * F::STG, tm, 0, g * MT_GR, q6 ? it : it * MtQ4K::IG, bar_full + 8 * s);
             }
             // do not retire while a box is still landing in this CTA's ring
             for (int k = i > S ? i - S : 0; ok && k < i; k++) ok = mbs_wait(bar_empty + 8 * (k % S), (k / S) & 1, &g_gb_device_err);
@@ -671,34 +690,45 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
     const float rs = a.xmode == MV_X_RMSNORM ? mt_rms_scale<MT_NC>(a.x, K, a.eps, red, threadIdx.x) : 1.f;
     mt_quantise_x<F::S16>(a, K, xq, threadIdx.x, MT_NC * 32, rs);
     mt_consumer_sync<MT_NC>();
-    MtLane L;
-    L.gq = lane >> 2;
-    L.c = lane & 3;
-    const bool bact = L.c == (L.gq >> 1);   // this lane carries a nonzero B fragment
-    L.xlb = bact ? xq + (L.gq & 1) * K + F::XB_LANE * L.c : smem + zero_off;
-    L.xstr = bact ? 256 : 0;
+    MtLane L4, L6;   // fragment maps of the Q4_K and Q6_K stage consumers
+    L4.gq = L6.gq = lane >> 2;
+    L4.c = L6.c = lane & 3;
+    const bool bact = L4.c == (L4.gq >> 1);   // this lane carries a nonzero B fragment
+    L4.xlb = bact ? xq + (L4.gq & 1) * K + MtQ4K::XB_LANE * L4.c : smem + zero_off;
+    L6.xlb = bact ? xq + (L6.gq & 1) * K + MtQ6K::XB_LANE * L6.c : smem + zero_off;
+    L4.xstr = L6.xstr = bact ? 256 : 0;
     int gi = 0;
     bool ok = true;
     float acc_a[2] = {0.f, 0.f}, acc_b[2] = {0.f, 0.f};
     for (int t = t0, i = 0; t < t1; i++) {
-        // stage i: items [it, it + n) of group grp, the same walk as the producer's
-        const int grp = t / nch, it = t - grp * nch;
-        const int n = min(min(F::SI, nch - it), t1 - t);
+        // stage i: item t, the same walk as the producer's
+        int m, grp, it;
+        mt_locate(a, t, m, grp, it);
         const int s = i % S;
         if (ok) ok = mbs_wait(bar_full + 8 * s, (i / S) & 1, &g_gb_device_err);
-        if (ok) F::consume(smem + s * F::STG, it * F::IG, min(nb, (it + n) * F::IG), warp, L, xq, K, acc_a, acc_b);
+        if (ok) {
+            const bool q6 = MIXED ? a.fmt[m] != 0 : FQ6;
+            if (q6)
+                MtQ6K::consume(smem + s * F::STG, it * MtQ6K::IG, min(nb, (it + 1) * MtQ6K::IG), warp, L6, xq, K,
+                               acc_a, acc_b);
+            else
+                MtQ4K::consume(smem + s * F::STG, it * MtQ4K::IG, min(nb, (it + 1) * MtQ4K::IG), warp, L4, xq, K,
+                               acc_a, acc_b);
+        }
         __syncwarp();
         if (lane == 0) mbs_arrive(bar_empty + 8 * s);
-        t += n;
+        t++;
 
-        if (it + n == nch || t == t1) {   // ---- this CTA's part of group grp is done
-            const int gq = L.gq, c = L.c;
+        const int nch = a.nchm[m];
+        if (it + 1 == nch || t == t1) {   // ---- this CTA's part of group grp of matrix m is done
+            const int gl = a.gbase[m] + grp;   // the launch's group index (tickets)
+            const int gq = L4.gq, c = L4.c;
 #pragma unroll
-            for (int m = 0; m < 2; m++) {
-                acc_a[m] += __shfl_xor_sync(0xffffffffu, acc_a[m], 1);
-                acc_a[m] += __shfl_xor_sync(0xffffffffu, acc_a[m], 2);
-                acc_b[m] += __shfl_xor_sync(0xffffffffu, acc_b[m], 1);
-                acc_b[m] += __shfl_xor_sync(0xffffffffu, acc_b[m], 2);
+            for (int j = 0; j < 2; j++) {   // the two 16-row tiles
+                acc_a[j] += __shfl_xor_sync(0xffffffffu, acc_a[j], 1);
+                acc_a[j] += __shfl_xor_sync(0xffffffffu, acc_a[j], 2);
+                acc_b[j] += __shfl_xor_sync(0xffffffffu, acc_b[j], 1);
+                acc_b[j] += __shfl_xor_sync(0xffffffffu, acc_b[j], 2);
             }
             const int slot = gi % NSLOT;
             float* rs = red + (slot * MT_NC + warp) * MT_GR;
@@ -723,9 +753,8 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
                 for (int w2 = 0; w2 < MT_NC; w2++) v += r0[w2 * MT_GR];
                 __syncwarp();
                 if (lane == 0) cnt[slot] = 0;
-                const int gs = grp * nch;
-                const int m = mt_matrix(a, grp);
-                const int row = (grp - a.gbase[m]) * MT_GR + lane;
+                const int gs = a.ibase[m] + grp * nch;   // the group's first item
+                const int row = grp * MT_GR + lane;
                 float* const ym = a.y[m];
                 const float* const rm = a.residual[m];
                 if (gs >= t0 && gs + nch <= t1) {
@@ -736,22 +765,22 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
                     // order (deterministic).  Wait-free: no CTA waits on
                     // another, so launches on concurrent streams cannot block
                     // each other.
-                    const int half = grp == t0 / nch ? 0 : 1;
+                    const int half = t0 >= gs ? 0 : 1;   // the group is this CTA's first
                     a.part[(c0 * 2 + half) * MT_GR + lane] = v;
                     __syncwarp();
                     const int cf = mt_owner(gs, a.T, a.ncta), cl2 = mt_owner(gs + nch - 1, a.T, a.ncta);   // unit == 1 here
                     unsigned g = 0;
-                    if (lane == 0) g = atom_add_acq_rel(&a.tickets[grp], 1u);
+                    if (lane == 0) g = atom_add_acq_rel(&a.tickets[gl], 1u);
                     g = __shfl_sync(0xffffffffu, g, 0);
                     __syncwarp();
                     if (g == (unsigned)(cl2 - cf)) {
                         float u = 0.f;
                         for (int c2 = cf; c2 <= cl2; c2++) {
-                            const int h2 = grp == mt_start(c2, a.T, a.ncta) / nch ? 0 : 1;
+                            const int h2 = mt_start(c2, a.T, a.ncta) >= gs ? 0 : 1;
                             u += __ldcg(a.part + (c2 * 2 + h2) * MT_GR + lane);
                         }
                         if (row < a.rows[m]) ym[row] = u + (rm ? rm[row] : 0.f);
-                        if (lane == 0) a.tickets[grp] = 0u;
+                        if (lane == 0) a.tickets[gl] = 0u;
                     }
                 }
             }
@@ -986,19 +1015,34 @@ int mv_launch(const MvPlan& p, const float* x, float* y, const float* residual, 
     return e == cudaSuccess ? GB_OK : GB_ECUDA;
 }
 
-bool mv_groupable(const MvPlan* const* ps, int n) {
-    if (n < 1 || n > MT_MAXM) return false;
-    for (int i = 0; i < n; i++)
-        if (ps[i]->kind != MV_TMA || ps[i]->dtype != ps[0]->dtype || ps[i]->nb != ps[0]->nb || ps[i]->S != ps[0]->S)
-            return false;
-    return true;
-}
-
 size_t mv_ws_bytes_group(const MvPlan* const* ps, int n) {
     if (!mv_groupable(ps, n)) return 0;
     size_t groups = 0;
     for (int i = 0; i < n; i++) groups += (size_t)ps[i]->ngroups;
     return (size_t)GB_NUM_SMS * 2 * MT_GR * sizeof(float) + (groups * sizeof(unsigned) + 255) / 256 * 256;
+}
+
+// Ring depth of a mixed-format launch with K columns (0 if none fits).
+static int mix_stages(int K) {
+    for (int S = 4; S >= 2; S--)
+        if (mt_smem_bytes<MtMix>(S, K) <= (size_t)MV_SMEM_MAX) return S;
+    return 0;
+}
+
+template <class F>
+static cudaError_t mvt_configure() {
+    static unsigned configured = 0;
+    static std::mutex mu;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!(configured & (1u << (dev & 31)))) {
+        e = cudaFuncSetAttribute(k_mvt<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, MV_SMEM_MAX);
+        if (e != cudaSuccess) return e;
+        configured |= 1u << (dev & 31);
+    }
+    return cudaSuccess;
 }
 
 int mv_launch_group(const MvPlan* const* ps, int n, const float* x, float* const* ys, const float* const* res,
@@ -1008,47 +1052,52 @@ int mv_launch_group(const MvPlan* const* ps, int n, const float* x, float* const
     int rc = mv_check_xform(xf, true);
     if (rc) return rc;
     const MvPlan& p = *ps[0];
-    static unsigned configured[2] = {0, 0};
-    const bool q6 = p.dtype == GB_DT_Q6_K;
-    int dev = 0;
-    GB_CUDA_TRY(cudaGetDevice(&dev));
-    if (!(configured[q6] & (1u << (dev & 31)))) {
-        GB_CUDA_TRY(cudaFuncSetAttribute(q6 ? k_mvt<MtQ6K> : k_mvt<MtQ4K>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         MV_SMEM_MAX));
-        configured[q6] |= 1u << (dev & 31);
+    bool mixed = false;
+    for (int i = 1; i < n; i++) mixed |= ps[i]->dtype != p.dtype;
+    if (mixed && !ws) {   // mixed formats split by items, which needs the workspace: one launch per matrix
+        for (int i = 0; i < n; i++)
+            if ((rc = mv_launch_group(&ps[i], 1, x, &ys[i], res ? &res[i] : nullptr, ws, st, pdl, xf))) return rc;
+        return GB_OK;
     }
+    const bool q6 = p.dtype == GB_DT_Q6_K;
+    GB_CUDA_TRY(mixed ? mvt_configure<MtMix>() : (q6 ? mvt_configure<MtQ6K>() : mvt_configure<MtQ4K>()));
     MtArgs a = {};
     a.x = x;
     a.nm = n;
     a.gbase[0] = 0;
+    a.ibase[0] = 0;
     for (int i = 0; i < MT_MAXM; i++) {
         const bool on = i < n;
         if (on && !ys[i]) return GB_EINVAL;
         a.y[i] = on ? ys[i] : nullptr;
         a.residual[i] = on && res ? res[i] : nullptr;
         a.rows[i] = on ? ps[i]->rows : 0;
+        a.nchm[i] = on ? ps[i]->nch : 1;
+        a.fmt[i] = on && ps[i]->dtype == GB_DT_Q6_K ? 1 : 0;
         a.gbase[i + 1] = a.gbase[i] + (on ? ps[i]->ngroups : 0);
+        a.ibase[i + 1] = a.ibase[i] + (on ? ps[i]->ngroups * ps[i]->nch : 0);
     }
     const int groups = a.gbase[MT_MAXM];
     a.part = static_cast<float*>(ws);
     a.tickets = ws ? reinterpret_cast<unsigned*>(static_cast<char*>(ws) + (size_t)GB_NUM_SMS * 2 * MT_GR * sizeof(float))
                    : nullptr;
     a.nb = p.nb;
-    a.nch = p.nch;
-    a.T = groups * p.nch;
+    a.T = a.ibase[MT_MAXM];
     a.xmode = xf ? xf->mode : MV_X_NONE;
     a.nw = a.xmode == MV_X_RMSNORM ? xf->w : nullptr;
     a.x2 = a.xmode == MV_X_SILU_MUL ? xf->x2 : nullptr;
     a.eps = xf ? xf->eps : 0.f;
-    // with a workspace: stream-K over stage items; without: whole groups per CTA
+    // with a workspace: stream-K over items; without: whole groups per CTA
+    // (one format, so every group has the same item count)
     a.unit = ws ? 1 : p.nch;
     const int units = ws ? a.T : groups;
     a.ncta = units < GB_NUM_SMS ? units : GB_NUM_SMS;
-    a.S = p.S;
+    a.S = mixed ? mix_stages(p.nb * 256) : p.S;
+    if (a.S < 2) return GB_ELIMIT;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.ncta);
-    cfg.blockDim = dim3(((q6 ? MtQ6K::NC : MtQ4K::NC) + 1) * 32);
-    cfg.dynamicSmemBytes = p.smem;
+    cfg.blockDim = dim3((MtMix::NC + 1) * 32);
+    cfg.dynamicSmemBytes = mixed ? mt_smem_bytes<MtMix>(a.S, p.nb * 256) : p.smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1058,11 +1107,25 @@ int mv_launch_group(const MvPlan* const* ps, int n, const float* x, float* const
     const CUtensorMap* m0 = reinterpret_cast<const CUtensorMap*>(ps[0]->tmap);
     const CUtensorMap* m1 = reinterpret_cast<const CUtensorMap*>(ps[n > 1 ? 1 : 0]->tmap);
     const CUtensorMap* m2 = reinterpret_cast<const CUtensorMap*>(ps[n > 2 ? 2 : 0]->tmap);
-    if (q6)
+    if (mixed)
+        GB_CUDA_TRY(cudaLaunchKernelEx(&cfg, k_mvt<MtMix>, *m0, *m1, *m2, a));
+    else if (q6)
         GB_CUDA_TRY(cudaLaunchKernelEx(&cfg, k_mvt<MtQ6K>, *m0, *m1, *m2, a));
     else
         GB_CUDA_TRY(cudaLaunchKernelEx(&cfg, k_mvt<MtQ4K>, *m0, *m1, *m2, a));
     return GB_OK;
+}
+// TMA plans of one column count; one format, or Q4_K and Q6_K mixed when a
+// ring of at least two mixed stages fits.
+bool mv_groupable(const MvPlan* const* ps, int n) {
+    if (n < 1 || n > MT_MAXM) return false;
+    bool mixed = false;
+    for (int i = 0; i < n; i++) {
+        if (ps[i]->kind != MV_TMA || ps[i]->nb != ps[0]->nb) return false;
+        if (ps[i]->dtype != ps[0]->dtype) mixed = true;
+        else if (ps[i]->S != ps[0]->S) return false;
+    }
+    return !mixed || mix_stages(ps[0]->nb * 256) >= 2;
 }
 
 // Workspace for the plain C entry point: one zeroed buffer per (device,

@@ -259,6 +259,9 @@ int gb_model_launches_per_step(const gb_model* m);
  * Needs every matrix on the TMA path (Q6_K rows of a multiple of 2048
  * columns); otherwise the per-matrix schedule runs. */
 int gb_model_use_persistent(gb_model* m, int on);
+/* 1 when the last decode step ran the persistent schedule (set up lazily by
+ * the first decode after a weight change), else 0. */
+int gb_model_persistent(const gb_model* m);
 
 /* Byte count of one decode step's algorithmic HBM traffic at position pos
  * (weights + KV read + KV append + activations), for rooflines. */
