@@ -343,6 +343,7 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
         }
 
     // ---- merge the warps' (m, l, o) in the ring (every tile is consumed)
+    __syncwarp();   // bar.sync is warp-aligned: reconverge the warp first
     asm volatile("bar.sync 1, %0;" ::"n"(ATTN_CWARPS * 32) : "memory");
     constexpr int WS = HD + 4;   // m, l, 2 pad, o[HD]: o stays 16-byte aligned
     float* wst = ring;           // [TW][GROUP][WS]
@@ -352,6 +353,7 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
         if (lane == 0) { w[0] = m[j]; w[1] = l[j]; }
         if (lane < C::CH) *reinterpret_cast<float4*>(w + 4 + ch * 4) = acc[j];
     }
+    __syncwarp();   // bar.sync is warp-aligned: reconverge the warp first
     asm volatile("bar.sync 1, %0;" ::"n"(ATTN_CWARPS * 32) : "memory");
     const int ctid = tid;   // 0 .. 255
     const bool single = nsplit == 1;
@@ -381,8 +383,10 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
     // ---- merge in the last CTA of this KV head
     __shared__ unsigned last;
     __threadfence();
+    __syncwarp();   // bar.sync is warp-aligned: reconverge the warp first
     asm volatile("bar.sync 1, %0;" ::"n"(ATTN_CWARPS * 32) : "memory");
     if (ctid == 0) last = (atomicAdd(&tickets[kvh], 1u) == (unsigned)(nsplit - 1));
+    __syncwarp();   // bar.sync is warp-aligned: reconverge the warp first
     asm volatile("bar.sync 1, %0;" ::"n"(ATTN_CWARPS * 32) : "memory");
     if (!last) return;
     __threadfence();
@@ -406,6 +410,7 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
         L = warp_sum(L);
         if (lane == 0) lm[h] = L;
     }
+    __syncwarp();   // bar.sync is warp-aligned: reconverge the warp first
     asm volatile("bar.sync 1, %0;" ::"n"(ATTN_CWARPS * 32) : "memory");
     for (int e = ctid; e < GROUP * HD; e += ATTN_CWARPS * 32) {
         const int h = e / HD, d = e % HD;

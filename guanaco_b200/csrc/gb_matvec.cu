@@ -92,6 +92,7 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                  : "memory");
 }
 __device__ __forceinline__ void consumer_sync() {
+    __syncwarp();   // bar.sync is warp-aligned: reconverge the warp first
     asm volatile("bar.sync 1, %0;" ::"n"(MV_CONSUMERS * 32) : "memory");
 }
 // 8 bytes at a 2-byte-aligned shared address: two aligned words, one aligned
@@ -687,8 +688,14 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
     // ---- consumers
     griddep_wait();
     uint8_t* xq = smem + xq_off;
-    const float rs = a.xmode == MV_X_RMSNORM ? mt_rms_scale<MT_NC>(a.x, K, a.eps, red, threadIdx.x) : 1.f;
-    mt_quantise_x<F::S16>(a, K, xq, threadIdx.x, MT_NC * 32, rs);
+    // RMSNorm: one pass over x and the weight when every thread can hold its
+    // share in registers (K <= 8192), else a scale pass and a quantise pass
+    if (a.xmode == MV_X_RMSNORM && K / 4 <= MT_XU * MT_NC * 32) {
+        mt_quantise_x_rms<F::S16, MT_NC>(a, K, xq, threadIdx.x, red);
+    } else {
+        const float rs = a.xmode == MV_X_RMSNORM ? mt_rms_scale<MT_NC>(a.x, K, a.eps, red, threadIdx.x) : 1.f;
+        mt_quantise_x<F::S16>(a, K, xq, threadIdx.x, MT_NC * 32, rs);
+    }
     mt_consumer_sync<MT_NC>();
     MtLane L4, L6;   // fragment maps of the Q4_K and Q6_K stage consumers
     L4.gq = L6.gq = lane >> 2;

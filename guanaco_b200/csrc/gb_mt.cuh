@@ -117,6 +117,7 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
 }
 template <int NC>
 __device__ __forceinline__ void mt_consumer_sync() {
+    __syncwarp();   // bar.sync is warp-aligned: reconverge the warp first
     asm volatile("bar.sync 1, %0;" ::"n"(NC * 32) : "memory");
 }
 // Split item t of a matrix with nch items per group: CTA c owns
@@ -243,6 +244,48 @@ __device__ __forceinline__ void mt_quantise_x(const A& a, int K, uint8_t* xq, in
             const int t = base + j * nthr;
             if (t < n4) mt_quantise4<S16, A>(a, K, xq, t, v[j], w[j], rs);
         }
+    }
+}
+
+// RMSNorm and quantisation in one pass (K / 4 <= MT_XU * NC * 32): every
+// float4 of x and of the weight is loaded once, the sum of squares reduced
+// (same order as mt_rms_scale, so the same scale), then the registers are
+// quantised.  One round trip to L2 instead of two.  scratch: NC floats.
+template <bool S16, int NC, class A>
+__device__ __forceinline__ void mt_quantise_x_rms(const A& a, int K, uint8_t* xq, int tid, float* scratch) {
+    const int n4 = K / 4, nthr = NC * 32;
+    const float4* x4 = reinterpret_cast<const float4*>(a.x);
+    const float4* w4 = reinterpret_cast<const float4*>(a.nw);
+    float4 v[MT_XU], w[MT_XU];
+#pragma unroll
+    for (int j = 0; j < MT_XU; j++) {
+        const int t = tid + j * nthr;
+        v[j] = w[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (t < n4) {
+            v[j] = __ldcg(x4 + t);
+            w[j] = __ldcg(w4 + t);
+        }
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < MT_XU; j++) {
+        ss = fmaf(v[j].x, v[j].x, ss);
+        ss = fmaf(v[j].y, v[j].y, ss);
+        ss = fmaf(v[j].z, v[j].z, ss);
+        ss = fmaf(v[j].w, v[j].w, ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((tid & 31) == 0) scratch[tid >> 5] = ss;
+    mt_consumer_sync<NC>();
+    float tot = 0.f;
+#pragma unroll
+    for (int w2 = 0; w2 < NC; w2++) tot += scratch[w2];
+    const float rs = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(tot, (float)K), a.eps)));
+#pragma unroll
+    for (int j = 0; j < MT_XU; j++) {
+        const int t = tid + j * nthr;
+        if (t < n4) mt_quantise4<S16, A>(a, K, xq, t, v[j], w[j], rs);
     }
 }
 
