@@ -43,14 +43,34 @@ struct MvXform {
     const float* x2 = nullptr;   // the up projection for MV_X_SILU_MUL
     float eps = 0.f;
 };
+// Tensor-parallel exchange attached to a TMA matvec launch (world > 1).
+// Every rank owns a receive buffer whose first part is slots[2][world][H]
+// of {value bits, epoch} pairs (8-byte stores, so a value is valid once its
+// epoch tag matches: no flag, no fence); the peers write it over NVLink
+// through CUDA IPC mappings.  Exchange c of a step has epoch
+// step * calls + c + 1 and uses slot parity epoch & 1.
+//   push_call >= 0: the launch's y rows (one matrix, no residual) go to slot
+//                   [rank] of every rank's buffer instead of y.
+//   in_call >= 0:   x (RMSNorm input) = x + sum over ranks, in rank order,
+//                   of this rank's slots of exchange in_call (bounded wait
+//                   for the tags); each CTA writes its slice of that sum to
+//                   h_out, the hidden state after the exchange.
+struct MvTp {
+    void* const* peers = nullptr;               // device array of the ranks' receive buffers
+    const unsigned long long* step = nullptr;   // device step counter
+    unsigned* err = nullptr;                    // device error word (GB_ETIMEOUT)
+    int rank = 0, world = 1, calls = 0, H = 0;
+    int push_call = -1, in_call = -1;
+    float* h_out = nullptr;
+};
 int mv_launch(const MvPlan& p, const float* x, float* y, const float* residual, void* ws, cudaStream_t st,
-              bool pdl, const MvXform* xf = nullptr);
+              bool pdl, const MvXform* xf = nullptr, const MvTp* tp = nullptr);
 // Several matrices that share x as one launch (TMA plans of one format, one
 // column count and ring depth; at most 3): ys[i] = W_i x (+ res[i]).
 bool mv_groupable(const MvPlan* const* ps, int n);
 size_t mv_ws_bytes_group(const MvPlan* const* ps, int n);
 int mv_launch_group(const MvPlan* const* ps, int n, const float* x, float* const* ys, const float* const* res,
-                    void* ws, cudaStream_t st, bool pdl, const MvXform* xf = nullptr);
+                    void* ws, cudaStream_t st, bool pdl, const MvXform* xf = nullptr, const MvTp* tp = nullptr);
 // Tensor map of a Q4_K / Q6_K weight view (gb_matvec.cu).
 bool mt_encode_view(void* map128, int dtype, const void* W, int rows, int nb, int boxz);
 bool mt_encode_rows(void* map128, const void* W, int rows, int nb, int box_u64);
@@ -91,8 +111,22 @@ struct TpCtx {
     int calls = 0;                            // exchanges per step
     unsigned* err = nullptr;
     float* part = nullptr;                    // [H] local partial
+    float* h[2] = {nullptr, nullptr};         // hidden state: exchange c reads h[c & 1], writes h[(c + 1) & 1]
+    // an exchange attached to a matvec (push_call / in_call filled in by the caller)
+    MvTp mv() const {
+        MvTp t;
+        t.peers = d_peers;
+        t.step = d_step;
+        t.err = err;
+        t.rank = rank;
+        t.world = world;
+        t.calls = calls;
+        return t;
+    }
 };
-int tp_allreduce(const TpCtx& tp, float* hidden, int H, int call, cudaStream_t st);
+// Exchange `call` as its own launch: push part to every rank, then
+// h_out = h_in + sum of the ranks' partials (rank order).
+int tp_allreduce(const TpCtx& tp, const float* h_in, float* h_out, int H, int call, cudaStream_t st);
 
 // Everything one decode layer needs; all pointers are device pointers.
 struct LayerArgs {
@@ -110,8 +144,10 @@ struct LayerArgs {
     float *hidden, *xn, *q, *k, *v, *attn, *gate, *up;
     int H, n_heads, n_kv, hd, ff, max_seq;
     float eps;
+    bool tp_fused = false;    // tensor parallel: exchanges inside the matvecs (tp_fusable for every layer)
 };
 int enqueue_layer(const LayerArgs& a, cudaStream_t st);
+bool tp_fusable(const MvPlan* const* mv, int H);
 // Matvec workspace one layer's launches need (grouped launches included).
 size_t layer_ws_bytes(const MvPlan* const* mv);
 int embed(const void* emb, int dtype, const int* d_token, int vocab, int H, float* out, unsigned* err,

@@ -197,14 +197,19 @@ __global__ void k_advance(int* tok, const int* next, int* pos, int* out, int* co
 // ---------------------------------------------------------------- tensor parallel exchanges
 // Every rank owns a receive buffer in its own HBM; the others write into it
 // over NVLink through CUDA IPC mappings.  Layout (world <= 8, H floats):
-//   slots [2][world][H] fp32 | results [2][world] ArgPart | flags [2][world] u32
+//   slots [2][world][H] {value bits, epoch} | results [2][world] ArgPart |
+//   flags [2][world] u32
 // Exchange e of a step gets epoch = step * calls + e + 1 (unique, the same on
-// every rank); it uses parity e & 1 of the slots and flags, so a rank one
-// exchange ahead never overwrites data a peer is still reading.  A sender
-// stores its data, fences at system scope and releases flag[parity][sender]
-// = epoch; a receiver acquires until every flag reached the epoch (bounded:
-// 2 s, then GB_ETIMEOUT in the error word).
-__device__ __forceinline__ size_t tp_slots_bytes(int world, int H) { return (size_t)2 * world * H * sizeof(float); }
+// every rank); it uses parity e & 1, so a rank one exchange ahead never
+// overwrites data a peer is still reading.  Slots: a sender writes each
+// value together with its epoch in one 8-byte store; a reader waits until
+// the epoch tag matches (bounded: 2 s, then GB_ETIMEOUT in the error word).
+// The hidden-state exchanges normally run inside the matvecs (MvTp: wo /
+// ffn_down push their rows, the next RMSNorm matvec sums them);
+// k_tp_allreduce does both sides as its own launch for shapes those kernels
+// do not take.  The argmax exchange publishes one (max, index) per rank and
+// releases flag[parity][sender] = epoch after a system-scope fence.
+__device__ __forceinline__ size_t tp_slots_bytes(int world, int H) { return (size_t)2 * world * H * sizeof(uint2); }
 __device__ __forceinline__ unsigned* tp_flags(void* base, int world, int H) {
     return reinterpret_cast<unsigned*>(static_cast<char*>(base) + tp_slots_bytes(world, H) + 2 * world * sizeof(ArgPart));
 }
@@ -232,36 +237,51 @@ __device__ bool tp_wait_flag(const unsigned* flag, unsigned ep) {
         if (tp_gtimer() - t0 > 2000000000ull) return false;
     return true;
 }
+__device__ __forceinline__ void tp_ll_store(uint2* p, float v, unsigned tag) {
+    asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)), "r"(tag) : "memory");
+}
+// value of slot p once its tag is ep; false after 2 s
+__device__ __forceinline__ bool tp_ll_wait(const uint2* p, unsigned ep, float& v) {
+    uint32_t x, t;
+    asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(x), "=r"(t) : "l"(p) : "memory");
+    if (t != ep) {
+        const uint64_t t0 = tp_gtimer();
+        do {
+            if (tp_gtimer() - t0 > 2000000000ull) return false;
+            asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(x), "=r"(t) : "l"(p) : "memory");
+        } while (t != ep);
+    }
+    v = __uint_as_float(x);
+    return true;
+}
 
-// hidden += sum over ranks (in rank order) of every rank's partial.  Grid =
-// world CTAs: CTA p pushes this rank's partial to peer p, then reduces slice
-// p of hidden from this rank's own buffer.
-__global__ void __launch_bounds__(512) k_tp_allreduce(const float* __restrict__ part, float* __restrict__ hidden,
-                                                      int H, int rank, int world, void* const* __restrict__ peers,
+// h_out = h_in + sum over ranks (in rank order) of every rank's partial.
+// Grid = world CTAs: CTA p pushes this rank's partial to peer p, then
+// reduces slice p from this rank's own buffer.
+__global__ void __launch_bounds__(512) k_tp_allreduce(const float* __restrict__ part, const float* __restrict__ h_in,
+                                                      float* __restrict__ h_out, int H, int rank, int world,
+                                                      void* const* __restrict__ peers,
                                                       const unsigned long long* __restrict__ step, int calls,
                                                       int call, unsigned* __restrict__ err) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // successors may start their weight prefetch
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // successors may start their weight prefetch
     const unsigned ep = (unsigned)(*step * (unsigned long long)calls + call + 1);
     const int par = ep & 1, p = blockIdx.x, tid = threadIdx.x;
-    float* dst = static_cast<float*>(peers[p]) + ((size_t)par * world + rank) * H;
-    for (int i = 4 * tid; i < H; i += 4 * blockDim.x)
-        *reinterpret_cast<float4*>(dst + i) = *reinterpret_cast<const float4*>(part + i);
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence_system();
-        st_release_sys(tp_flags(peers[p], world, H) + par * world + rank, ep);
-    }
-    void* mine = peers[rank];
-    if (tid < world && !tp_wait_flag(tp_flags(mine, world, H) + par * world + tid, ep))
-        atomicExch(err, (unsigned)(-GB_ETIMEOUT));
-    __syncthreads();
-    const float* slots = static_cast<const float*>(mine) + (size_t)par * world * H;
+    uint2* dst = static_cast<uint2*>(peers[p]) + ((size_t)par * world + rank) * H;
+    for (int i = tid; i < H; i += blockDim.x) tp_ll_store(dst + i, part[i], ep);
+    const uint2* slots = static_cast<const uint2*>(peers[rank]) + (size_t)par * world * H;
     const int lo = (int)((long long)p * H / world), hi = (int)((long long)(p + 1) * H / world);
+    bool ok = true;
     for (int i = lo + tid; i < hi; i += blockDim.x) {
         float sum = 0.f;
-        for (int q = 0; q < world; q++) sum += __ldcg(slots + (size_t)q * H + i);
-        hidden[i] = hidden[i] + sum;
+        for (int q = 0; q < world; q++) {
+            float v = 0.f;
+            if (ok && !tp_ll_wait(slots + (size_t)q * H + i, ep, v)) {
+                ok = false;
+                atomicExch(err, (unsigned)(-GB_ETIMEOUT));
+            }
+            sum += v;
+        }
+        h_out[i] = h_in[i] + sum;
     }
 }
 
@@ -371,6 +391,7 @@ struct gb_model {
     std::vector<void*> owned;         // allocations freed with the model
 
     float *kc = nullptr, *vc = nullptr, *rope = nullptr;
+    float* hidden2 = nullptr;         // tensor parallel: second hidden-state buffer (exchanges ping-pong)
     void* attn_ws = nullptr;
     float *hidden = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr;
     float *gate = nullptr, *up = nullptr, *logits = nullptr;
@@ -404,10 +425,10 @@ static void* dalloc(gb_model* m, size_t bytes) {
 
 static void invalidate_graph(gb_model* m);
 
-// Exchange buffer of one rank: slots [2][world][H] fp32, results [2][world],
-// flags [2][world] u32 (see k_tp_allreduce).
+// Exchange buffer of one rank: slots [2][world][H] {value, epoch} pairs,
+// results [2][world], flags [2][world] u32 (see k_tp_allreduce).
 static size_t tp_comm_bytes(int world, int H) {
-    return (size_t)2 * world * H * sizeof(float) + 2 * world * sizeof(ArgPart) + 2 * world * sizeof(unsigned);
+    return (size_t)2 * world * H * sizeof(uint2) + 2 * world * sizeof(ArgPart) + 2 * world * sizeof(unsigned);
 }
 
 extern "C" gb_model* gb_model_create_tp(const gb_model_config* cfg, int rank, int world) {
@@ -470,6 +491,7 @@ extern "C" gb_model* gb_model_create_tp(const gb_model_config* cfg, int rank, in
     if (world > 1) {
         m->comm_bytes = tp_comm_bytes(world, H);
         ok &= (m->part = (float*)dalloc(m, (size_t)H * 4)) != nullptr;
+        ok &= (m->hidden2 = (float*)dalloc(m, (size_t)H * 4)) != nullptr;
         ok &= (m->d_peers = (void**)dalloc(m, 8 * sizeof(void*))) != nullptr;
         // the exchange buffer gets its own allocation: it is shared with the
         // peers through cudaIpcGetMemHandle
@@ -500,6 +522,8 @@ extern "C" gb_model* gb_model_create_tp(const gb_model_config* cfg, int rank, in
     m->tp.calls = 2 * c.n_layers + 1;
     m->tp.err = m->err;
     m->tp.part = m->part;
+    m->tp.h[0] = m->hidden;
+    m->tp.h[1] = m->hidden2;
     return m;
 }
 
@@ -713,11 +737,49 @@ extern "C" int gb_model_synthesize(gb_model* m, uint64_t seed) {
 namespace gb {
 // One decode layer (engine.c:353-554) on stream st; shared by the model and
 // the drop-in cuda_transformer_layer_gpu.
+// Tensor parallelism with the hidden-state exchanges inside the matvecs:
+// every matvec of the layer (and the output head) on the TMA path, and x
+// small enough for the one-pass RMSNorm quantiser.
+bool tp_fusable(const MvPlan* const* mv, int H) {
+    if (H % 4 || H > 8192) return false;
+    for (int i = 0; i < GB_NMAT; i++)
+        if (mv[i]->kind != MV_TMA) return false;
+    return true;
+}
+
 int enqueue_layer(const LayerArgs& a, cudaStream_t st) {
     const int H = a.H, F = a.ff;
     int rc;
-    auto mv = [&](int which, const float* x, float* y, const float* res, const MvXform* xf) {
-        return mv_launch(*a.mv[which], x, y, res, a.mv_ws, st, true, xf);
+    const bool tp = a.tp && a.tp->world > 1;
+    const bool fx = tp && a.tp_fused;   // exchanges inside the matvecs
+    const int c_wo = 2 * a.layer, c_dn = 2 * a.layer + 1;   // this layer's exchanges
+    // hidden state read by the q/k/v and the gate/up matvecs.  One GPU: one
+    // buffer updated in place by the residual adds.  Tensor parallel:
+    // exchange c reads h[c & 1] and writes h[(c + 1) & 1]; with the exchanges
+    // inside the matvecs the q/k/v matvec sums the previous layer's ffn_down
+    // exchange (none before layer 0) and the gate/up matvec the wo exchange.
+    float* hq = a.hidden;
+    float* hf = a.hidden;
+    if (tp) {
+        hq = fx && a.layer > 0 ? a.tp->h[1] : a.tp->h[0];
+        hf = fx ? a.tp->h[0] : a.tp->h[1];
+    }
+    MvTp tq, twp, tg, tdp;   // q/k/v input, wo push, gate/up input, ffn_down push
+    if (fx) {
+        tq = twp = tg = tdp = a.tp->mv();
+        tq.H = twp.H = tg.H = tdp.H = H;
+        if (a.layer > 0) {
+            tq.in_call = c_wo - 1;
+            tq.h_out = a.tp->h[0];
+        }
+        twp.push_call = c_wo;
+        tg.in_call = c_wo;
+        tg.h_out = a.tp->h[1];
+        tdp.push_call = c_dn;
+    }
+    auto mv = [&](int which, const float* x, float* y, const float* res, const MvXform* xf,
+                  const MvTp* tpx = nullptr) {
+        return mv_launch(*a.mv[which], x, y, res, a.mv_ws, st, true, xf, tpx);
     };
     auto tma = [&](int which) { return a.mv[which]->kind == MV_TMA; };
     // RMSNorm and the SwiGLU product run inside the consuming matvecs' x
@@ -730,27 +792,29 @@ int enqueue_layer(const LayerArgs& a, cudaStream_t st) {
     swi.mode = MV_X_SILU_MUL;
     swi.x2 = a.up;
     // matrices that share x and a format run as one launch
-    auto group = [&](const int* which, int n, const float* x, float* const* ys, const MvXform* xf) {
+    auto group = [&](const int* which, int n, const float* x, float* const* ys, const MvXform* xf,
+                     const MvTp* tpx) {
         const MvPlan* ps[3];
         for (int i = 0; i < n; i++) ps[i] = a.mv[which[i]];
-        return mv_launch_group(ps, n, x, ys, nullptr, a.mv_ws, st, true, xf);
+        return mv_launch_group(ps, n, x, ys, nullptr, a.mv_ws, st, true, xf, tpx);
     };
+    const MvTp* tqp = fx ? &tq : nullptr;
     if (tma(GB_WQ) && tma(GB_WK) && tma(GB_WV)) {
         const int qkv[3] = {GB_WQ, GB_WK, GB_WV};
         float* ys[3] = {a.q, a.k, a.v};
         const MvPlan* ps[3] = {a.mv[GB_WQ], a.mv[GB_WK], a.mv[GB_WV]};
         if (mv_groupable(ps, 3)) {
-            if ((rc = group(qkv, 3, a.hidden, ys, &att))) return rc;
+            if ((rc = group(qkv, 3, hq, ys, &att, tqp))) return rc;
         } else if (mv_groupable(ps, 2)) {
-            if ((rc = group(qkv, 2, a.hidden, ys, &att))) return rc;
-            if ((rc = mv(GB_WV, a.hidden, a.v, nullptr, &att))) return rc;
+            if ((rc = group(qkv, 2, hq, ys, &att, tqp))) return rc;
+            if ((rc = mv(GB_WV, hq, a.v, nullptr, &att, tqp))) return rc;
         } else {
-            if ((rc = mv(GB_WQ, a.hidden, a.q, nullptr, &att))) return rc;
-            if ((rc = mv(GB_WK, a.hidden, a.k, nullptr, &att))) return rc;
-            if ((rc = mv(GB_WV, a.hidden, a.v, nullptr, &att))) return rc;
+            if ((rc = mv(GB_WQ, hq, a.q, nullptr, &att, tqp))) return rc;
+            if ((rc = mv(GB_WK, hq, a.k, nullptr, &att, tqp))) return rc;
+            if ((rc = mv(GB_WV, hq, a.v, nullptr, &att, tqp))) return rc;
         }
     } else {
-        if ((rc = gb_rmsnorm(a.hidden, a.ra, a.xn, H, a.eps, st))) return rc;
+        if ((rc = gb_rmsnorm(hq, a.ra, a.xn, H, a.eps, st))) return rc;
         if ((rc = mv(GB_WQ, a.xn, a.q, nullptr, nullptr))) return rc;
         if ((rc = mv(GB_WK, a.xn, a.k, nullptr, nullptr))) return rc;
         if ((rc = mv(GB_WV, a.xn, a.v, nullptr, nullptr))) return rc;
@@ -758,38 +822,40 @@ int enqueue_layer(const LayerArgs& a, cudaStream_t st) {
     if ((rc = gb_attention_decode(a.q, a.k, a.v, a.kc, a.vc, a.rope, a.d_pos, a.n_heads, a.n_kv, a.hd, a.max_seq,
                                   a.attn, a.attn_ws, st)))
         return rc;
-    const bool tp = a.tp && a.tp->world > 1;
-    if (tp) {   // this rank's columns of wo, then hidden += sum of the ranks' partials
+    if (fx) {   // this rank's columns of wo, pushed to every rank
+        if ((rc = mv(GB_WO, a.attn, a.tp->part, nullptr, nullptr, &twp))) return rc;
+    } else if (tp) {   // this rank's columns of wo, then the exchange as its own launch
         if ((rc = mv(GB_WO, a.attn, a.tp->part, nullptr, nullptr))) return rc;
-        if ((rc = tp_allreduce(*a.tp, a.hidden, H, 2 * a.layer, st))) return rc;
+        if ((rc = tp_allreduce(*a.tp, a.tp->h[0], a.tp->h[1], H, c_wo, st))) return rc;
     } else if ((rc = mv(GB_WO, a.attn, a.hidden, a.hidden, nullptr))) {
         return rc;
     }
+    const MvTp* tgp = fx ? &tg : nullptr;
     if (tma(GB_WGATE) && tma(GB_WUP)) {
         const int gu[2] = {GB_WGATE, GB_WUP};
         float* ys[2] = {a.gate, a.up};
         const MvPlan* ps[2] = {a.mv[GB_WGATE], a.mv[GB_WUP]};
         if (mv_groupable(ps, 2)) {
-            if ((rc = group(gu, 2, a.hidden, ys, &ffn))) return rc;
+            if ((rc = group(gu, 2, hf, ys, &ffn, tgp))) return rc;
         } else {
-            if ((rc = mv(GB_WGATE, a.hidden, a.gate, nullptr, &ffn))) return rc;
-            if ((rc = mv(GB_WUP, a.hidden, a.up, nullptr, &ffn))) return rc;
+            if ((rc = mv(GB_WGATE, hf, a.gate, nullptr, &ffn, tgp))) return rc;
+            if ((rc = mv(GB_WUP, hf, a.up, nullptr, &ffn, tgp))) return rc;
         }
     } else {
-        if ((rc = gb_rmsnorm(a.hidden, a.rf, a.xn, H, a.eps, st))) return rc;
+        if ((rc = gb_rmsnorm(hf, a.rf, a.xn, H, a.eps, st))) return rc;
         if ((rc = mv(GB_WGATE, a.xn, a.gate, nullptr, nullptr))) return rc;
         if ((rc = mv(GB_WUP, a.xn, a.up, nullptr, nullptr))) return rc;
     }
     float* dy = tp ? a.tp->part : a.hidden;
     const float* dres = tp ? nullptr : a.hidden;
     if (tma(GB_WDOWN)) {
-        rc = mv(GB_WDOWN, a.gate, dy, dres, &swi);
+        rc = mv(GB_WDOWN, a.gate, dy, dres, &swi, fx ? &tdp : nullptr);
     } else {
         if ((rc = gb_silu_mul(a.gate, a.up, F, st))) return rc;
         rc = mv(GB_WDOWN, a.gate, dy, dres, nullptr);
     }
-    if (rc || !tp) return rc;
-    return tp_allreduce(*a.tp, a.hidden, H, 2 * a.layer + 1, st);
+    if (rc || !tp || fx) return rc;
+    return tp_allreduce(*a.tp, a.tp->h[1], a.tp->h[0], H, c_dn, st);
 }
 
 size_t layer_ws_bytes(const MvPlan* const* mv) {
@@ -808,9 +874,9 @@ int embed(const void* emb, int dtype, const int* d_token, int vocab, int H, floa
     k_embed<<<(H + 255) / 256, 256, 0, st>>>(emb, dtype, d_token, vocab, H, out, err, step);
     return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
 }
-int tp_allreduce(const TpCtx& tp, float* hidden, int H, int call, cudaStream_t st) {
-    k_tp_allreduce<<<tp.world, 512, 0, st>>>(tp.part, hidden, H, tp.rank, tp.world, tp.d_peers, tp.d_step, tp.calls,
-                                             call, tp.err);
+int tp_allreduce(const TpCtx& tp, const float* h_in, float* h_out, int H, int call, cudaStream_t st) {
+    k_tp_allreduce<<<tp.world, 512, 0, st>>>(tp.part, h_in, h_out, H, tp.rank, tp.world, tp.d_peers, tp.d_step,
+                                             tp.calls, call, tp.err);
     return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
 }
 int set_device_int(int* p, int v, cudaStream_t st) {
@@ -818,6 +884,20 @@ int set_device_int(int* p, int v, cudaStream_t st) {
     return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
 }
 }  // namespace gb
+
+// Tensor parallel with the exchanges inside the matvecs: every layer and the
+// output head on the TMA path (otherwise each exchange is its own launch).
+static bool tp_fused(const gb_model* m) {
+    const char* e = getenv("GB_TP_FUSED");   // 0: every exchange as its own launch
+    if (e && e[0] == '0') return false;
+    if (m->lm_plan.kind != MV_TMA) return false;
+    for (int l = 0; l < m->c.n_layers; l++) {
+        const MvPlan* mv[GB_NMAT];
+        for (int i = 0; i < GB_NMAT; i++) mv[i] = &m->plan[(size_t)l * GB_NMAT + i];
+        if (!tp_fusable(mv, m->c.hidden_dim)) return false;
+    }
+    return true;
+}
 
 // Enqueue one decode step on stream st.
 static int enqueue_argmax(gb_model* m, const float* lg, int* d_next, cudaStream_t st);
@@ -847,9 +927,11 @@ static int enqueue_step(gb_model* m, const int* d_token, const int* d_pos, float
                                         cudaMemcpyDeviceToDevice, st));
         return enqueue_argmax(m, m->logits, d_next, st);
     }
+    const bool fx = m->world > 1 && tp_fused(m);
     for (int l = 0; l < c.n_layers; l++) {
         LayerArgs a;
         a.tp = m->world > 1 ? &m->tp : nullptr;
+        a.tp_fused = fx;
         a.layer = l;
         for (int i = 0; i < GB_NMAT; i++) a.mv[i] = &m->plan[(size_t)l * GB_NMAT + i];
         a.mv_ws = m->mv_ws;
@@ -868,7 +950,15 @@ static int enqueue_step(gb_model* m, const int* d_token, const int* d_pos, float
         fin.mode = MV_X_RMSNORM;
         fin.w = m->rms_final;
         fin.eps = c.rms_eps;
-        if ((rc = mv_launch(m->lm_plan, m->hidden, lg, nullptr, m->mv_ws, st, true, &fin))) return rc;
+        MvTp th;   // tensor parallel: the head sums the last layer's ffn_down exchange
+        if (fx) {
+            th = m->tp.mv();
+            th.H = H;
+            th.in_call = 2 * c.n_layers - 1;
+            th.h_out = m->tp.h[0];
+        }
+        const float* hx = fx ? m->tp.h[1] : m->hidden;
+        if ((rc = mv_launch(m->lm_plan, hx, lg, nullptr, m->mv_ws, st, true, &fin, fx ? &th : nullptr))) return rc;
     } else {
         if ((rc = gb_rmsnorm(m->hidden, m->rms_final, m->xn, H, c.rms_eps, st))) return rc;
         if ((rc = mv_launch(m->lm_plan, m->xn, lg, nullptr, m->mv_ws, st, true))) return rc;
@@ -1158,7 +1248,8 @@ extern "C" int gb_model_launches_per_step(const gb_model* m) {
         n += tma(GB_WDOWN) ? 0 : 1;
     }
     n += m->lm_plan.kind == MV_TMA ? 1 : 2;
-    if (m->world > 1) n += 2 * m->c.n_layers + 1;   // all-reduces after wo / ffn_down, argmax merge
+    if (m->world > 1)   // all-reduces after wo / ffn_down (unless inside the matvecs), argmax merge
+        n += (tp_fused(m) ? 0 : 2 * m->c.n_layers) + 1;
     return n + 1;
 }
 

@@ -609,7 +609,19 @@ struct MtArgs {
     const float* nw;
     const float* x2;
     float eps;
+    MvTp tp;            // tensor-parallel exchange (push_call / in_call < 0: none)
 };
+
+// y row of matrix m: to y, or (tensor-parallel push) as {value, epoch} to
+// slot [rank] of every rank's receive buffer
+__device__ __forceinline__ void mt_put(const MtArgs& a, int m, int row, float v, unsigned ep) {
+    if (a.tp.push_call >= 0) {
+        const size_t off = ((size_t)(ep & 1) * a.tp.world + a.tp.rank) * a.tp.H + row;
+        for (int q = 0; q < a.tp.world; q++) ll_store(static_cast<uint2*>(a.tp.peers[q]) + off, v, ep);
+    } else {
+        a.y[m][row] = v;
+    }
+}
 
 // A launch whose matrices mix Q4_K and Q6_K (e.g. q, k and v): stage slots
 // sized for the larger stage, each stage consumed by its matrix's format.
@@ -688,10 +700,18 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
     // ---- consumers
     griddep_wait();
     uint8_t* xq = smem + xq_off;
+    // epochs of the tensor-parallel exchanges (the step counter is written
+    // by the step's first kernel, complete by now)
+    unsigned ep_push = 0, ep_in = 0;
+    if (a.tp.push_call >= 0 || a.tp.in_call >= 0) {
+        const unsigned long long sc = *a.tp.step * (unsigned long long)a.tp.calls;
+        ep_push = (unsigned)(sc + a.tp.push_call + 1);
+        ep_in = (unsigned)(sc + a.tp.in_call + 1);
+    }
     // RMSNorm: one pass over x and the weight when every thread can hold its
     // share in registers (K <= 8192), else a scale pass and a quantise pass
     if (a.xmode == MV_X_RMSNORM && K / 4 <= MT_XU * MT_NC * 32) {
-        mt_quantise_x_rms<F::S16, MT_NC>(a, K, xq, threadIdx.x, red);
+        mt_quantise_x_rms<F::S16, MT_NC>(a, K, xq, threadIdx.x, red, a.tp.in_call >= 0 ? &a.tp : nullptr, ep_in);
     } else {
         const float rs = a.xmode == MV_X_RMSNORM ? mt_rms_scale<MT_NC>(a.x, K, a.eps, red, threadIdx.x) : 1.f;
         mt_quantise_x<F::S16>(a, K, xq, threadIdx.x, MT_NC * 32, rs);
@@ -762,10 +782,9 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
                 if (lane == 0) cnt[slot] = 0;
                 const int gs = a.ibase[m] + grp * nch;   // the group's first item
                 const int row = grp * MT_GR + lane;
-                float* const ym = a.y[m];
                 const float* const rm = a.residual[m];
                 if (gs >= t0 && gs + nch <= t1) {
-                    if (row < a.rows[m]) ym[row] = v + (rm ? rm[row] : 0.f);
+                    if (row < a.rows[m]) mt_put(a, m, row, v + (rm ? rm[row] : 0.f), ep_push);
                 } else {
                     // split group: every owner publishes its partial rows and
                     // takes a ticket; the last one sums the partials in CTA
@@ -786,7 +805,7 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
                             const int h2 = mt_start(c2, a.T, a.ncta) >= gs ? 0 : 1;
                             u += __ldcg(a.part + (c2 * 2 + h2) * MT_GR + lane);
                         }
-                        if (row < a.rows[m]) ym[row] = u + (rm ? rm[row] : 0.f);
+                        if (row < a.rows[m]) mt_put(a, m, row, u + (rm ? rm[row] : 0.f), ep_push);
                         if (lane == 0) a.tickets[gl] = 0u;
                     }
                 }
@@ -999,15 +1018,16 @@ static int mv_check_xform(const MvXform* xf, bool tma) {
 }
 
 int mv_launch(const MvPlan& p, const float* x, float* y, const float* residual, void* ws, cudaStream_t st, bool pdl,
-              const MvXform* xf) {
+              const MvXform* xf, const MvTp* tp) {
     if (!x || !y) return GB_EINVAL;
     if (reinterpret_cast<uintptr_t>(x) & 15) return GB_EINVAL;
     if (p.kind == MV_TMA) {
         const MvPlan* ps[1] = {&p};
         float* ys[1] = {y};
         const float* rs[1] = {residual};
-        return mv_launch_group(ps, 1, x, ys, rs, ws, st, pdl, xf);
+        return mv_launch_group(ps, 1, x, ys, rs, ws, st, pdl, xf, tp);
     }
+    if (tp && (tp->push_call >= 0 || tp->in_call >= 0)) return GB_EINVAL;   // exchanges run in the TMA kernels only
     int rc = mv_check_xform(xf, false);
     if (rc) return rc;
     MvGeom g;
@@ -1053,7 +1073,7 @@ static cudaError_t mvt_configure() {
 }
 
 int mv_launch_group(const MvPlan* const* ps, int n, const float* x, float* const* ys, const float* const* res,
-                    void* ws, cudaStream_t st, bool pdl, const MvXform* xf) {
+                    void* ws, cudaStream_t st, bool pdl, const MvXform* xf, const MvTp* tp) {
     if (!x || !ys || !mv_groupable(ps, n)) return GB_EINVAL;
     if (reinterpret_cast<uintptr_t>(x) & 15) return GB_EINVAL;
     int rc = mv_check_xform(xf, true);
@@ -1063,8 +1083,16 @@ int mv_launch_group(const MvPlan* const* ps, int n, const float* x, float* const
     for (int i = 1; i < n; i++) mixed |= ps[i]->dtype != p.dtype;
     if (mixed && !ws) {   // mixed formats split by items, which needs the workspace: one launch per matrix
         for (int i = 0; i < n; i++)
-            if ((rc = mv_launch_group(&ps[i], 1, x, &ys[i], res ? &res[i] : nullptr, ws, st, pdl, xf))) return rc;
+            if ((rc = mv_launch_group(&ps[i], 1, x, &ys[i], res ? &res[i] : nullptr, ws, st, pdl, xf, tp))) return rc;
         return GB_OK;
+    }
+    if (tp && (tp->push_call >= 0 || tp->in_call >= 0)) {   // tensor-parallel exchange: check its shape
+        if (!tp->peers || !tp->step || !tp->err || tp->world < 2 || tp->H <= 0) return GB_EINVAL;
+        if (tp->push_call >= 0 && (n != 1 || (res && res[0]) || ps[0]->rows > tp->H)) return GB_EINVAL;
+        if (tp->in_call >= 0 && (!xf || xf->mode != MV_X_RMSNORM || p.nb * 256 != tp->H ||
+                                 p.nb * 64 > MT_XU * MtMix::NC * 32 || !tp->h_out ||
+                                 (reinterpret_cast<uintptr_t>(tp->h_out) & 15)))
+            return GB_EINVAL;
     }
     const bool q6 = p.dtype == GB_DT_Q6_K;
     GB_CUDA_TRY(mixed ? mvt_configure<MtMix>() : (q6 ? mvt_configure<MtQ6K>() : mvt_configure<MtQ4K>()));
@@ -1094,6 +1122,8 @@ int mv_launch_group(const MvPlan* const* ps, int n, const float* x, float* const
     a.nw = a.xmode == MV_X_RMSNORM ? xf->w : nullptr;
     a.x2 = a.xmode == MV_X_SILU_MUL ? xf->x2 : nullptr;
     a.eps = xf ? xf->eps : 0.f;
+    if (tp) a.tp = *tp;
+    if (!tp) a.tp.push_call = a.tp.in_call = -1;
     // with a workspace: stream-K over items; without: whole groups per CTA
     // (one format, so every group has the same item count)
     a.unit = ws ? 1 : p.nch;

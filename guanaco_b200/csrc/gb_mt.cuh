@@ -247,12 +247,45 @@ __device__ __forceinline__ void mt_quantise_x(const A& a, int K, uint8_t* xq, in
     }
 }
 
+// ---- tensor-parallel exchange slots: {value bits, epoch} pairs written
+// with one 8-byte store, so a reader that sees the epoch sees the value.
+__device__ __forceinline__ void ll_store(void* p, float v, unsigned tag) {
+    asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)), "r"(tag) : "memory");
+}
+__device__ __forceinline__ uint4 ll_load2(const void* p) {   // two consecutive pairs
+    uint4 r;
+    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p)
+                 : "memory");
+    return r;
+}
+// Four consecutive values (p 16-byte aligned) once all four carry epoch ep;
+// false after 2 s.
+__device__ __forceinline__ bool ll_wait4(const uint2* p, unsigned ep, float4& out) {
+    uint4 a = ll_load2(p), b = ll_load2(p + 2);
+    if (a.y != ep || a.w != ep || b.y != ep || b.w != ep) {
+        const uint64_t t0 = gtimer();
+        do {
+            if (gtimer() - t0 > MT_WAIT_NS) return false;
+            a = ll_load2(p);
+            b = ll_load2(p + 2);
+        } while (a.y != ep || a.w != ep || b.y != ep || b.w != ep);
+    }
+    out = make_float4(__uint_as_float(a.x), __uint_as_float(a.z), __uint_as_float(b.x), __uint_as_float(b.z));
+    return true;
+}
+
 // RMSNorm and quantisation in one pass (K / 4 <= MT_XU * NC * 32): every
 // float4 of x and of the weight is loaded once, the sum of squares reduced
 // (same order as mt_rms_scale, so the same scale), then the registers are
 // quantised.  One round trip to L2 instead of two.  scratch: NC floats.
+// With an exchange ex (ex->in_call >= 0, epoch ep): x is first replaced by
+// x + the sum over ranks of this rank's receive slots, and this CTA writes
+// its slice of that sum to ex->h_out.
 template <bool S16, int NC, class A>
-__device__ __forceinline__ void mt_quantise_x_rms(const A& a, int K, uint8_t* xq, int tid, float* scratch) {
+__device__ __forceinline__ void mt_quantise_x_rms(const A& a, int K, uint8_t* xq, int tid, float* scratch,
+                                                  const MvTp* ex = nullptr, unsigned ep = 0) {
     const int n4 = K / 4, nthr = NC * 32;
     const float4* x4 = reinterpret_cast<const float4*>(a.x);
     const float4* w4 = reinterpret_cast<const float4*>(a.nw);
@@ -264,6 +297,28 @@ __device__ __forceinline__ void mt_quantise_x_rms(const A& a, int K, uint8_t* xq
         if (t < n4) {
             v[j] = __ldcg(x4 + t);
             w[j] = __ldcg(w4 + t);
+        }
+    }
+    if (ex) {
+        const int world = ex->world;
+        const uint2* slots = static_cast<const uint2*>(ex->peers[ex->rank]) + (size_t)(ep & 1) * world * ex->H;
+        const int lo = (int)((long long)blockIdx.x * n4 / gridDim.x), hi = (int)((long long)(blockIdx.x + 1) * n4 / gridDim.x);
+        bool ok = true;
+#pragma unroll
+        for (int j = 0; j < MT_XU; j++) {
+            const int t = tid + j * nthr;
+            if (t >= n4) continue;
+            float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int q = 0; q < world; q++) {
+                float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (ok && !ll_wait4(slots + (size_t)q * ex->H + 4 * t, ep, f)) {
+                    ok = false;
+                    atomicExch(ex->err, (unsigned)(-GB_ETIMEOUT));
+                }
+                sum = make_float4(sum.x + f.x, sum.y + f.y, sum.z + f.z, sum.w + f.w);
+            }
+            v[j] = make_float4(v[j].x + sum.x, v[j].y + sum.y, v[j].z + sum.z, v[j].w + sum.w);
+            if (t >= lo && t < hi) reinterpret_cast<float4*>(ex->h_out)[t] = v[j];
         }
     }
     float ss = 0.f;

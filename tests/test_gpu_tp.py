@@ -36,7 +36,9 @@ def _decode(dm, vocab_rows):
     return toks, logits
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, fused):
+    if not fused:
+        os.environ["GB_TP_FUSED"] = "0"
     import torch
     import torch.distributed as dist
     import guanaco_b200 as gb
@@ -61,8 +63,11 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2])
-def test_tp_decode_matches_one_gpu(gb, cuda, world):
+@pytest.mark.parametrize("world,fused", [(2, True), (2, False)])
+def test_tp_decode_matches_one_gpu(gb, cuda, world, fused):
+    """fused: the hidden-state exchanges run inside the wo / ffn_down matvecs
+    (push) and the next RMSNorm matvec (sum); otherwise each exchange is its
+    own all-reduce launch."""
     if cuda.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     c = CFG
@@ -77,7 +82,7 @@ def test_tp_decode_matches_one_gpu(gb, cuda, world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, fused)) for r in range(world)]
     for p in procs:
         p.start()
     got = [q.get(timeout=300) for _ in range(world)]
