@@ -63,7 +63,7 @@ def _worker(rank, world, port, q, fused):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,fused", [(2, True), (2, False)])
+@pytest.mark.parametrize("world,fused", [(2, True), (2, False), (4, True)])
 def test_tp_decode_matches_one_gpu(gb, cuda, world, fused):
     """fused: the hidden-state exchanges run inside the wo / ffn_down matvecs
     (push) and the next RMSNorm matvec (sum); otherwise each exchange is its
