@@ -395,17 +395,29 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
     // warp per head), then every output is a weighted sum over the splits in
     // split order; the ring (free) holds the weights [GROUP][nsplit]
     float* wbuf = ring + C::TW * GROUP * WS;
-    if (warp < GROUP) {
+    if (warp < GROUP) {   // (m, l) of every split: one load per lane and 32 splits
         const int h = warp;
+        constexpr int MJ = (GB_NUM_SMS + 31) / 32;   // splits per lane at most
+        float2 ml[MJ];
+#pragma unroll
+        for (int i = 0; i < MJ; i++) {
+            const int j = lane + 32 * i;
+            ml[i] = j < nsplit ? __ldcg(reinterpret_cast<const float2*>(base + ((size_t)j * GROUP + h) * (HD + 2)))
+                               : make_float2(-INFINITY, 0.f);
+        }
         float M = -INFINITY;
-        for (int j = lane; j < nsplit; j += 32) M = fmaxf(M, __ldcg(base + ((size_t)j * GROUP + h) * (HD + 2)));
+#pragma unroll
+        for (int i = 0; i < MJ; i++) M = fmaxf(M, ml[i].x);
         M = warp_max(M);
         float L = 0.f;
-        for (int j = lane; j < nsplit; j += 32) {
-            const float* pj = base + ((size_t)j * GROUP + h) * (HD + 2);
-            const float w = expf(__ldcg(pj) - M);
-            wbuf[h * nsplit + j] = w;
-            L = fmaf(__ldcg(pj + 1), w, L);
+#pragma unroll
+        for (int i = 0; i < MJ; i++) {
+            const int j = lane + 32 * i;
+            if (j < nsplit) {
+                const float w = expf(ml[i].x - M);
+                wbuf[h * nsplit + j] = w;
+                L = fmaf(ml[i].y, w, L);
+            }
         }
         L = warp_sum(L);
         if (lane == 0) lm[h] = L;
@@ -417,8 +429,15 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
         const float* wj = wbuf + h * nsplit;
         const float* pj = base + (size_t)h * (HD + 2) + 2 + d;
         float O = 0.f;
-#pragma unroll 8
-        for (int j = 0; j < nsplit; j++) O = fmaf(__ldcg(pj + (size_t)j * GROUP * (HD + 2)), wj[j], O);
+        for (int j0 = 0; j0 < nsplit; j0 += 16) {   // 16 loads in flight, summed in split order
+            float pv[16];
+#pragma unroll
+            for (int i = 0; i < 16; i++)
+                pv[i] = j0 + i < nsplit ? __ldcg(pj + (size_t)(j0 + i) * GROUP * (HD + 2)) : 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; i++)
+                if (j0 + i < nsplit) O = fmaf(pv[i], wj[j0 + i], O);
+        }
         out[(size_t)(kvh * GROUP + h) * HD + d] = O / lm[h];
     }
     if (ctid == 0) tickets[kvh] = 0u;   // every split has arrived: safe to rearm

@@ -29,6 +29,8 @@ CASES = [
     (8, 8, 128, 64, 40), (16, 2, 128, 300, 257), (32, 4, 64, 300, 200), (8, 1, 64, 40, 0),
     (16, 2, 64, 130, 129), (4, 4, 64, 700, 650), (32, 8, 128, 2100, 2049),
     (8, 2, 64, 40, 9), (8, 2, 64, 40, 13), (16, 4, 64, 600, 333), (4, 2, 128, 100, 70),
+    # one KV head of 4 q heads over a long context (a rank's share at 8-way tensor parallelism)
+    (4, 1, 128, 4400, 4300),
 ]
 
 
