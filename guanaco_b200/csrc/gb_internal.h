@@ -36,12 +36,22 @@ size_t mv_ws_bytes(const MvPlan& p);
 // Optional transform of x inside the matvec (TMA path only): RMSNorm
 // x * r * w (r = 1 / sqrt(mean(x^2) + eps), the reference's rounding), or
 // silu(x) * x2 (the SwiGLU product).
-enum { MV_X_NONE = 0, MV_X_RMSNORM = 1, MV_X_SILU_MUL = 2 };
+// MV_X_PREQ: x arrives already quantised (xq, the layout the x quantiser
+// writes in shared memory, mt_xq_bytes(K, true) bytes).
+enum { MV_X_NONE = 0, MV_X_RMSNORM = 1, MV_X_SILU_MUL = 2, MV_X_PREQ = 3 };
 struct MvXform {
     int mode = MV_X_NONE;
     const float* w = nullptr;    // RMSNorm weight
     const float* x2 = nullptr;   // the up projection for MV_X_SILU_MUL
     float eps = 0.f;
+    const uint8_t* xq = nullptr;   // MV_X_PREQ input
+    // gate / up launch (two matrices of equal rows, one item per 32-row
+    // group): silu(y0) * y1 is also quantised into swq_out (mt_xq_bytes(rows,
+    // true) bytes, zero-initialised) for the ffn_down matvec; swq_tk holds one
+    // ticket per group (zero between launches)
+    uint8_t* swq_out = nullptr;
+    unsigned* swq_tk = nullptr;
+    int swq_K = 0;                 // columns of swq_out (the ffn_down K, >= rows, a multiple of 256)
 };
 // Tensor-parallel exchange attached to a TMA matvec launch (world > 1).
 // Every rank owns a receive buffer whose first part is slots[2][world][H]
@@ -145,6 +155,11 @@ struct LayerArgs {
     int H, n_heads, n_kv, hd, ff, max_seq;
     float eps;
     bool tp_fused = false;    // tensor parallel: exchanges inside the matvecs (tp_fusable for every layer)
+    // SwiGLU product quantised by the gate / up launch for ffn_down
+    // (5 K / 2 bytes for K = ffn_down's columns, zeroed once) and its pair
+    // tickets (K / 32, zero); null: ffn_down quantises it itself
+    uint8_t* swq = nullptr;
+    unsigned* swq_tk = nullptr;
 };
 int enqueue_layer(const LayerArgs& a, cudaStream_t st);
 bool tp_fusable(const MvPlan* const* mv, int H);

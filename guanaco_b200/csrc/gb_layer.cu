@@ -392,6 +392,8 @@ struct gb_model {
 
     float *kc = nullptr, *vc = nullptr, *rope = nullptr;
     float* hidden2 = nullptr;         // tensor parallel: second hidden-state buffer (exchanges ping-pong)
+    uint8_t* swq = nullptr;           // SwiGLU product quantised for ffn_down (zeroed)
+    unsigned* swq_tk = nullptr;       // its pair tickets (zero)
     void* attn_ws = nullptr;
     float *hidden = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr;
     float *gate = nullptr, *up = nullptr, *logits = nullptr;
@@ -479,6 +481,11 @@ extern "C" gb_model* gb_model_create_tp(const gb_model_config* cfg, int rank, in
     ok &= (m->attn = (float*)dalloc(m, (size_t)QD * 4)) != nullptr;
     ok &= (m->gate = (float*)dalloc(m, (size_t)FP * 4)) != nullptr;
     ok &= (m->up = (float*)dalloc(m, (size_t)FP * 4)) != nullptr;
+    const size_t swq_bytes = FP % 256 ? 0 : (size_t)FP * 5 / 2;   // x0, x1, per-64 scales and sums, 16-column sums
+    if (swq_bytes) {
+        ok &= (m->swq = (uint8_t*)dalloc(m, swq_bytes)) != nullptr;
+        ok &= (m->swq_tk = (unsigned*)dalloc(m, (size_t)FP / 32 * sizeof(unsigned))) != nullptr;
+    }
     ok &= (m->logits = (float*)dalloc(m, (size_t)m->vocab_l * 4)) != nullptr;
     ok &= (m->err = (unsigned*)dalloc(m, 16)) != nullptr;
     ok &= (m->d_tok = (int*)dalloc(m, 16)) != nullptr;
@@ -508,6 +515,8 @@ extern "C" gb_model* gb_model_create_tp(const gb_model_config* cfg, int rank, in
                   cudaMemsetAsync(m->d_step, 0, 16, m->stream) == cudaSuccess &&
                   cudaMemsetAsync(m->gate, 0, (size_t)FP * 4, m->stream) == cudaSuccess &&
                   cudaMemsetAsync(m->up, 0, (size_t)FP * 4, m->stream) == cudaSuccess;
+    if (ok && m->swq) ok &= cudaMemsetAsync(m->swq, 0, swq_bytes, m->stream) == cudaSuccess &&
+                            cudaMemsetAsync(m->swq_tk, 0, (size_t)FP / 32 * sizeof(unsigned), m->stream) == cudaSuccess;
     if (ok && m->comm) ok &= cudaMemsetAsync(m->comm, 0, m->comm_bytes, m->stream) == cudaSuccess;
     if (ok) ok &= gb_rope_table(m->rope, c.max_seq, c.head_dim, c.rope_theta, m->stream) == GB_OK;
     if (ok) ok &= cudaStreamSynchronize(m->stream) == cudaSuccess;
@@ -831,12 +840,26 @@ int enqueue_layer(const LayerArgs& a, cudaStream_t st) {
         return rc;
     }
     const MvTp* tgp = fx ? &tg : nullptr;
+    // the gate / up launch also writes ffn_down's x quantised (one launch,
+    // one format, one item per 32-row group, ffn_down on the TMA path)
+    const MvPlan* pg = a.mv[GB_WGATE];
+    const MvPlan* pu = a.mv[GB_WUP];
+    const MvPlan* pd = a.mv[GB_WDOWN];
+    const bool swq = a.swq && a.swq_tk && tma(GB_WGATE) && tma(GB_WUP) && tma(GB_WDOWN) && pg->dtype == pu->dtype &&
+                     pg->nch == 1 && pu->nch == 1 && pg->rows == pu->rows && pd->cols % 256 == 0 &&
+                     pd->cols >= pg->rows;
     if (tma(GB_WGATE) && tma(GB_WUP)) {
         const int gu[2] = {GB_WGATE, GB_WUP};
         float* ys[2] = {a.gate, a.up};
         const MvPlan* ps[2] = {a.mv[GB_WGATE], a.mv[GB_WUP]};
         if (mv_groupable(ps, 2)) {
-            if ((rc = group(gu, 2, hf, ys, &ffn, tgp))) return rc;
+            MvXform fq = ffn;
+            if (swq) {
+                fq.swq_out = a.swq;
+                fq.swq_tk = a.swq_tk;
+                fq.swq_K = pd->cols;
+            }
+            if ((rc = group(gu, 2, hf, ys, &fq, tgp))) return rc;
         } else {
             if ((rc = mv(GB_WGATE, hf, a.gate, nullptr, &ffn, tgp))) return rc;
             if ((rc = mv(GB_WUP, hf, a.up, nullptr, &ffn, tgp))) return rc;
@@ -848,7 +871,16 @@ int enqueue_layer(const LayerArgs& a, cudaStream_t st) {
     }
     float* dy = tp ? a.tp->part : a.hidden;
     const float* dres = tp ? nullptr : a.hidden;
-    if (tma(GB_WDOWN)) {
+    const bool gu_grouped = [&] {
+        const MvPlan* ps[2] = {pg, pu};
+        return tma(GB_WGATE) && tma(GB_WUP) && mv_groupable(ps, 2);
+    }();
+    if (swq && gu_grouped) {   // x arrives quantised from the gate / up launch
+        MvXform pq;
+        pq.mode = MV_X_PREQ;
+        pq.xq = a.swq;
+        rc = mv(GB_WDOWN, a.gate, dy, dres, &pq, fx ? &tdp : nullptr);
+    } else if (tma(GB_WDOWN)) {
         rc = mv(GB_WDOWN, a.gate, dy, dres, &swi, fx ? &tdp : nullptr);
     } else {
         if ((rc = gb_silu_mul(a.gate, a.up, F, st))) return rc;
@@ -932,6 +964,8 @@ static int enqueue_step(gb_model* m, const int* d_token, const int* d_pos, float
         LayerArgs a;
         a.tp = m->world > 1 ? &m->tp : nullptr;
         a.tp_fused = fx;
+        a.swq = m->swq;
+        a.swq_tk = m->swq_tk;
         a.layer = l;
         for (int i = 0; i < GB_NMAT; i++) a.mv[i] = &m->plan[(size_t)l * GB_NMAT + i];
         a.mv_ws = m->mv_ws;

@@ -610,6 +610,13 @@ struct MtArgs {
     const float* x2;
     float eps;
     MvTp tp;            // tensor-parallel exchange (push_call / in_call < 0: none)
+    const uint8_t* xpre;   // MV_X_PREQ: x already quantised
+    // gate / up: items interleaved (2 g = gate group g, 2 g + 1 = up group g),
+    // silu(gate) * up quantised into swq_out (swq_K columns); swq_tk: one
+    // ticket per group for pairs whose halves end in different CTAs
+    uint8_t* swq_out;
+    unsigned* swq_tk;
+    int swq_K;
 };
 
 // y row of matrix m: to y, or (tensor-parallel push) as {value, epoch} to
@@ -635,6 +642,12 @@ static_assert(MtQ4K::SI == 1 && MtQ6K::SI == 1, "one split item per stage");
 
 // matrix, group within it and item within the group of item t
 __device__ __forceinline__ void mt_locate(const MtArgs& a, int t, int& m, int& g, int& it) {
+    if (a.swq_out) {   // gate / up pairs interleaved, one item per group
+        m = t & 1;
+        g = t >> 1;
+        it = 0;
+        return;
+    }
     m = t >= a.ibase[1] ? (t >= a.ibase[2] ? 2 : 1) : 0;
     const int u = t - a.ibase[m];
     g = u / a.nchm[m];
@@ -661,6 +674,8 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
     unsigned* cnt = reinterpret_cast<unsigned*>(red + NSLOT * MT_NC * MT_GR);
     const uint32_t bar_full = (sptr(cnt + NSLOT) + 15) & ~7u;
     const uint32_t bar_empty = bar_full + 8 * S;
+    // gate values of the CTA's last two pairs, for the SwiGLU quantisation
+    float* stash = reinterpret_cast<float*>(smem + ((bar_empty + 8 * S - sbase + 15) & ~15u));
     const int c0 = blockIdx.x;
     const int TU = a.T / a.unit;
     const int t0 = mt_start(c0, TU, a.ncta) * a.unit, t1 = mt_start(c0 + 1, TU, a.ncta) * a.unit;
@@ -710,7 +725,24 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
     }
     // RMSNorm: one pass over x and the weight when every thread can hold its
     // share in registers (K <= 8192), else a scale pass and a quantise pass
-    if (a.xmode == MV_X_RMSNORM && K / 4 <= MT_XU * MT_NC * 32) {
+    if (a.xmode == MV_X_PREQ) {   // quantised by the producing matvec: copy it in
+        const int n16 = mt_xq_bytes(K, F::S16) / 16;
+        const uint4* src = reinterpret_cast<const uint4*>(a.xpre);
+        uint4* dst = reinterpret_cast<uint4*>(xq);
+        for (int base = threadIdx.x; base < n16; base += 8 * MT_NC * 32) {
+            uint4 v[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int t = base + j * MT_NC * 32;
+                v[j] = t < n16 ? __ldcg(src + t) : make_uint4(0u, 0u, 0u, 0u);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int t = base + j * MT_NC * 32;
+                if (t < n16) dst[t] = v[j];
+            }
+        }
+    } else if (a.xmode == MV_X_RMSNORM && K / 4 <= MT_XU * MT_NC * 32) {
         mt_quantise_x_rms<F::S16, MT_NC>(a, K, xq, threadIdx.x, red, a.tp.in_call >= 0 ? &a.tp : nullptr, ep_in);
     } else {
         const float rs = a.xmode == MV_X_RMSNORM ? mt_rms_scale<MT_NC>(a.x, K, a.eps, red, threadIdx.x) : 1.f;
@@ -780,11 +812,38 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
                 for (int w2 = 0; w2 < MT_NC; w2++) v += r0[w2 * MT_GR];
                 __syncwarp();
                 if (lane == 0) cnt[slot] = 0;
-                const int gs = a.ibase[m] + grp * nch;   // the group's first item
+                const int gs = a.swq_out ? 2 * grp + m : a.ibase[m] + grp * nch;   // the group's first item
                 const int row = grp * MT_GR + lane;
                 const float* const rm = a.residual[m];
                 if (gs >= t0 && gs + nch <= t1) {
                     if (row < a.rows[m]) mt_put(a, m, row, v + (rm ? rm[row] : 0.f), ep_push);
+                    if (a.swq_out) {   // SwiGLU product of pair grp, quantised for ffn_down
+                        const float val = row < a.rows[m] ? v : 0.f;
+                        float gate = 0.f, up = 0.f;
+                        bool have = false;
+                        if (m == 0 && gs + 1 < t1) {           // the up half follows in this CTA
+                            stash[(grp & 1) * MT_GR + lane] = val;
+                        } else if (m == 1 && gs - 1 >= t0) {   // the gate half was this CTA's
+                            gate = stash[(grp & 1) * MT_GR + lane];
+                            up = val;
+                            have = true;
+                        } else {   // halves in two CTAs: the second to finish pairs them
+                            __threadfence();
+                            __syncwarp();
+                            unsigned k = 0;
+                            if (lane == 0) k = atomicAdd(&a.swq_tk[grp], 1u);
+                            k = __shfl_sync(0xffffffffu, k, 0);
+                            if (k == 1u) {
+                                __threadfence();
+                                const float oth = row < a.rows[1 - m] ? __ldcg(a.y[1 - m] + row) : 0.f;
+                                gate = m == 0 ? val : oth;
+                                up = m == 0 ? oth : val;
+                                have = true;
+                                if (lane == 0) a.swq_tk[grp] = 0u;
+                            }
+                        }
+                        if (have) mt_quantise32(a.swq_out, a.swq_K, grp, lane, mt_silu_mul(gate, up));
+                    }
                 } else {
                     // split group: every owner publishes its partial rows and
                     // takes a ticket; the last one sums the partials in CTA
@@ -937,7 +996,7 @@ static size_t mt_smem_bytes(int S, int K) {
     const size_t xq = ((size_t)mt_xq_bytes(K, F::S16) + 15) & ~(size_t)15;
     const int nslot = S + 2;
     return (size_t)S * F::STG + xq + MT_ZERO + (size_t)nslot * F::NC * MT_GR * 4 + (size_t)nslot * 4 + 16 +
-           16 * (size_t)S;
+           16 * (size_t)S + 16 + 2 * MT_GR * 4;   // + the SwiGLU stash
 }
 
 // Encode the 3-D view {one box row of bytes as u64, rows, z} of W for format F.
@@ -1010,8 +1069,10 @@ static bool pdl_allowed() {
 
 static int mv_check_xform(const MvXform* xf, bool tma) {
     const int xmode = xf ? xf->mode : MV_X_NONE;
+    if (xf && (xf->swq_out || xf->swq_tk) && !tma) return GB_EINVAL;
     if (xmode == MV_X_NONE) return GB_OK;
     if (!tma) return GB_EINVAL;   // transforms run in the TMA kernels' x quantiser only
+    if (xmode == MV_X_PREQ) return xf->xq && !(reinterpret_cast<uintptr_t>(xf->xq) & 15) ? GB_OK : GB_EINVAL;
     const float* other = xmode == MV_X_RMSNORM ? xf->w : xf->x2;
     if (!other || (reinterpret_cast<uintptr_t>(other) & 15)) return GB_EINVAL;
     return GB_OK;
@@ -1122,6 +1183,16 @@ int mv_launch_group(const MvPlan* const* ps, int n, const float* x, float* const
     a.nw = a.xmode == MV_X_RMSNORM ? xf->w : nullptr;
     a.x2 = a.xmode == MV_X_SILU_MUL ? xf->x2 : nullptr;
     a.eps = xf ? xf->eps : 0.f;
+    a.xpre = a.xmode == MV_X_PREQ ? xf->xq : nullptr;
+    if (xf && xf->swq_out) {   // gate / up: two matrices of equal rows, one item per group
+        const int kq = xf->swq_K ? xf->swq_K : ps[0]->rows;
+        if (n != 2 || mixed || p.nch != 1 || ps[1]->nch != 1 || ps[0]->rows != ps[1]->rows || !xf->swq_tk ||
+            (res && (res[0] || res[1])) || kq % 256 || kq < ps[0]->rows || (tp && tp->push_call >= 0))
+            return GB_EINVAL;
+        a.swq_out = xf->swq_out;
+        a.swq_tk = xf->swq_tk;
+        a.swq_K = kq;
+    }
     if (tp) a.tp = *tp;
     if (!tp) a.tp.push_call = a.tp.in_call = -1;
     // with a workspace: stream-K over items; without: whole groups per CTA

@@ -215,6 +215,37 @@ __device__ __forceinline__ void mt_quantise4(const A& a, int K, uint8_t* xq, int
     }
 }
 
+// One 32-column sub-block sb of x held one value per lane (lane = column
+// 32 sb + lane), quantised by a warp into the x layout above at xq (K
+// columns, with the 16-column sums): the same scale, limbs and sums as
+// mt_quantise4 computes from float4s.  Used by a matvec that produces the
+// next matvec's x (the SwiGLU product of gate / up for ffn_down).
+__device__ __forceinline__ void mt_quantise32(uint8_t* xq, int K, int sb, int lane, float v) {
+    float mx = fabsf(v), sm = v;
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        sm += __shfl_xor_sync(0xffffffffu, sm, o);
+    }
+    float* f = reinterpret_cast<float*>(xq + 2 * K);
+    float* f16 = f + K / 16;
+    if ((lane & 15) == 0) {   // 16-column sum: column c0 = 32 sb + lane = 256 b + 128 n + 32 G + 16 h
+        const int c0 = 32 * sb + lane, b = c0 >> 8, n = (c0 >> 7) & 1, G = (c0 >> 5) & 3, h = (c0 >> 4) & 1;
+        f16[b * 16 + h * 8 + 4 * n + G] = sm;
+    }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+    sm += __shfl_xor_sync(0xffffffffu, sm, 16);
+    const float inv = mx > 0.f ? 127.f / mx : 0.f;
+    int x0, x1;
+    limbs(v * inv, x0, x1);
+    xq[32 * sb + lane] = (uint8_t)(x0 & 255);
+    xq[K + 32 * sb + lane] = (uint8_t)(x1 & 255);
+    if (lane == 0) {
+        f[(sb >> 1) * 4 + (sb & 1)] = mx / 127.f;
+        f[(sb >> 1) * 4 + 2 + (sb & 1)] = sm;
+    }
+}
+
 // Quantise x into shared memory.  The loads of MT_XU float4 per thread (and
 // of the transform's second operand) are issued before any is used, so the
 // L2 latency is paid once per MT_XU float4 rather than once per float4.  x
