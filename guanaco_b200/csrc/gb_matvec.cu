@@ -37,6 +37,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstdlib>
 #include <type_traits>
 #include <map>
@@ -617,6 +618,9 @@ struct MtArgs {
     uint8_t* swq_out;
     unsigned* swq_tk;
     int swq_K;
+    // c1 > 0: CTAs [0, c1) take one whole group of n1 items each (the
+    // leading matrices), the other CTAs split the rest (one item per group)
+    int c1, n1;
 };
 
 // y row of matrix m: to y, or (tensor-parallel push) as {value, epoch} to
@@ -678,7 +682,12 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
     float* stash = reinterpret_cast<float*>(smem + ((bar_empty + 8 * S - sbase + 15) & ~15u));
     const int c0 = blockIdx.x;
     const int TU = a.T / a.unit;
-    const int t0 = mt_start(c0, TU, a.ncta) * a.unit, t1 = mt_start(c0 + 1, TU, a.ncta) * a.unit;
+    auto range_start = [&](int c) {
+        if (a.c1)
+            return c <= a.c1 ? c * a.n1 : a.c1 * a.n1 + mt_start(c - a.c1, a.T - a.c1 * a.n1, a.ncta - a.c1);
+        return mt_start(c, TU, a.ncta) * a.unit;
+    };
+    const int t0 = range_start(c0), t1 = range_start(c0 + 1);
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
             mbs_init(bar_full + 8 * s, 1);
@@ -1142,6 +1151,24 @@ int mv_launch_group(const MvPlan* const* ps, int n, const float* x, float* const
     const MvPlan& p = *ps[0];
     bool mixed = false;
     for (int i = 1; i < n; i++) mixed |= ps[i]->dtype != p.dtype;
+    if (mixed) {   // matrices with more items per group first (their groups get whole CTAs)
+        int ord[MT_MAXM];
+        for (int i = 0; i < n; i++) ord[i] = i;
+        std::stable_sort(ord, ord + n, [&](int u, int v) { return ps[u]->nch > ps[v]->nch; });
+        bool moved = false;
+        for (int i = 0; i < n; i++) moved |= ord[i] != i;
+        if (moved) {
+            const MvPlan* ps2[MT_MAXM];
+            float* ys2[MT_MAXM];
+            const float* rs2[MT_MAXM];
+            for (int i = 0; i < n; i++) {
+                ps2[i] = ps[ord[i]];
+                ys2[i] = ys[ord[i]];
+                rs2[i] = res ? res[ord[i]] : nullptr;
+            }
+            return mv_launch_group(ps2, n, x, ys2, rs2, ws, st, pdl, xf, tp);
+        }
+    }
     if (mixed && !ws) {   // mixed formats split by items, which needs the workspace: one launch per matrix
         for (int i = 0; i < n; i++)
             if ((rc = mv_launch_group(&ps[i], 1, x, &ys[i], res ? &res[i] : nullptr, ws, st, pdl, xf, tp))) return rc;
@@ -1206,6 +1233,23 @@ int mv_launch_group(const MvPlan* const* ps, int n, const float* x, float* const
     a.unit = whole ? p.nch : 1;
     const int units = whole ? groups : a.T;
     a.ncta = units < GB_NUM_SMS ? units : GB_NUM_SMS;
+    if (mixed) {   // whole groups of the leading multi-item matrices, one per CTA, when no CTA gets more items
+        int g1 = 0, n1 = 0, i = 0;
+        for (; i < n && ps[i]->nch > 1; i++) {
+            if (n1 && ps[i]->nch != n1) break;
+            n1 = ps[i]->nch;
+            g1 += ps[i]->ngroups;
+        }
+        bool rest1 = i < n;
+        for (int j = i; j < n; j++) rest1 &= ps[j]->nch == 1;
+        const int t2 = a.T - g1 * n1, c2 = GB_NUM_SMS - g1;
+        if (rest1 && g1 > 0 && c2 > 0 && t2 > 0 &&
+            (t2 + c2 - 1) / c2 <= std::max(n1, (a.T + GB_NUM_SMS - 1) / GB_NUM_SMS)) {
+            a.c1 = g1;
+            a.n1 = n1;
+            a.ncta = g1 + std::min(c2, t2);
+        }
+    }
     a.S = mixed ? mix_stages(p.nb * 256) : p.S;
     if (a.S < 2) return GB_ELIMIT;
     cudaLaunchConfig_t cfg = {};
