@@ -1224,12 +1224,12 @@ int mv_launch_group(const MvPlan* const* ps, int n, const float* x, float* const
     if (!tp) a.tp.push_call = a.tp.in_call = -1;
     // with a workspace: stream-K over items; without: whole groups per CTA
     // (one format, so every group has the same item count).  Whole groups
-    // also when they give no CTA more items than stream-K would (e.g. 128
-    // groups of 7 items on 148 SMs): no group is then split, so no CTA ends
-    // with the cross-CTA fix-up.
+    // also when they give no CTA more than one item above what stream-K
+    // would (e.g. 128 groups of 7 items on 148 SMs): no group is then split,
+    // so no CTA ends with the cross-CTA fix-up, which costs more than an item.
     bool whole = !ws;
     if (ws && !mixed && p.nch > 1)
-        whole = (groups + GB_NUM_SMS - 1) / GB_NUM_SMS * p.nch <= (a.T + GB_NUM_SMS - 1) / GB_NUM_SMS;
+        whole = (groups + GB_NUM_SMS - 1) / GB_NUM_SMS * p.nch <= (a.T + GB_NUM_SMS - 1) / GB_NUM_SMS + 1;
     a.unit = whole ? p.nch : 1;
     const int units = whole ? groups : a.T;
     a.ncta = units < GB_NUM_SMS ? units : GB_NUM_SMS;
