@@ -388,7 +388,10 @@ extern "C" int cuda_transformer_layer_gpu(
     LayerKV* L = layer_kv(c, layer, n_kv_heads, head_dim, max_seq_len);
     if (!L) return GB_ENOMEM;
     int rc;
-    if (L->valid < pos) {   // positions computed elsewhere (CPU prefill, session load)
+    if (pos < L->valid) {   // a rewind (new conversation, restored session): the host cache is the truth
+        if (pos > 0 && (rc = upload_kv(c, L, h_k_cache, h_v_cache, head_stride, 0, pos))) return rc;
+        L->valid = pos;
+    } else if (L->valid < pos) {   // positions computed elsewhere (CPU prefill, session load)
         if ((rc = upload_kv(c, L, h_k_cache, h_v_cache, head_stride, L->valid, pos))) return rc;
         L->valid = pos;
     }
@@ -433,9 +436,12 @@ extern "C" void cuda_sync_kv_cache(int layer, int n_kv_heads, int head_dim, int 
     if (!c) return;
     LayerKV* L = layer_kv(c, layer, n_kv_heads, head_dim, max_seq);
     if (!L) return;
-    const int p0 = L->valid < pos ? L->valid : pos;
+    // a sync below the mirrored positions is a rewind (a restored session or
+    // prompt cache replaced the host K/V): upload the whole prefix again
+    const bool rewind = pos < L->valid;
+    const int p0 = rewind ? 0 : L->valid;
     const int p1 = pos + T < max_seq ? pos + T : max_seq;
-    if (upload_kv(c, L, h_k_cache, h_v_cache, stride0, p0, p1) == GB_OK && p1 > L->valid) L->valid = p1;
+    if (upload_kv(c, L, h_k_cache, h_v_cache, stride0, p0, p1) == GB_OK && (rewind || p1 > L->valid)) L->valid = p1;
 }
 
 // NVML read through dlopen (no link-time dependency); 0 when unavailable.

@@ -184,6 +184,42 @@ def test_model_argmax_split_first_maximum(gb, cuda, vocab):
         dm.close()
 
 
+def test_dropin_layer_rewind_uses_restored_host_kv(gb, oracle, cuda):
+    """After decoding positions 9..12 on the GPU, the engine restores another
+    session (new host K/V for positions 0..8, session.c kv_cache_load) and
+    decodes position 9 again: the layer must attend over the restored values,
+    not the device copy of the old conversation."""
+    H, nh, nkv, ff, ms, layer = 512, 8, 2, 1536, 40, 13
+    hd = H // nh
+    ws, dts, shapes, ra, rf = layer_weights(oracle, H, nh, nkv, hd, ff, 21, (4, 4, 4, 4, 4, 4, 4))
+    L = gb.lib()
+    dptr = [L.cuda_upload_weight(w.ctypes.data, w.nbytes) for w in ws]
+    args = []
+    for d, (r, c), dt in zip(dptr, shapes, dts):
+        args += [d, r, c, dt]
+    kc = np.zeros(nkv * ms * hd, np.float32)
+    vc = np.zeros(nkv * ms * hd, np.float32)
+    kc.reshape(nkv, ms, hd)[:, :9] = oracle.synth_normal(nkv * 9 * hd, 31, 1).reshape(nkv, 9, hd)
+    vc.reshape(nkv, ms, hd)[:, :9] = oracle.synth_normal(nkv * 9 * hd, 31, 2).reshape(nkv, 9, hd)
+    for pos in range(9, 13):   # the first conversation, decoded on the GPU
+        h = oracle.synth_normal(H, 40 + pos, 3)
+        assert L.cuda_transformer_layer_gpu(*args, ra.ctypes.data, rf.ctypes.data, h.ctypes.data, kc.ctypes.data,
+                                            vc.ctypes.data, ms * hd, H, nh, nkv, hd, pos, layer, ms) == 0
+        L.cuda_finish_layer()
+    # restore another session: new K/V for positions 0..8 in the host cache
+    kc[:] = 0.0
+    vc[:] = 0.0
+    kc.reshape(nkv, ms, hd)[:, :9] = oracle.synth_normal(nkv * 9 * hd, 32, 1).reshape(nkv, 9, hd)
+    vc.reshape(nkv, ms, hd)[:, :9] = oracle.synth_normal(nkv * 9 * hd, 32, 2).reshape(nkv, 9, hd)
+    h = oracle.synth_normal(H, 77, 3)
+    kc_ref, vc_ref = kc.copy(), vc.copy()
+    h_ref, _, _ = oracle.layer_decode(ws, dts, shapes, ra, rf, h.copy(), kc_ref, vc_ref, H, nh, nkv, hd, ff, ms, 9)
+    assert L.cuda_transformer_layer_gpu(*args, ra.ctypes.data, rf.ctypes.data, h.ctypes.data, kc.ctypes.data,
+                                        vc.ctypes.data, ms * hd, H, nh, nkv, hd, 9, layer, ms) == 0
+    L.cuda_finish_layer()
+    assert rel_l2(h, h_ref) <= REL_L2_TOL
+
+
 def test_dropin_norm_cache_follows_host_values(gb, oracle, cuda):
     """Norm weights are cached by host pointer: new values at the same address
     (a freed and reallocated host buffer) must be used, not the old copy."""
