@@ -44,8 +44,8 @@ def peaks():
 
 def ncu_traffic():
     """Per-launch DRAM bytes of the dominant kernel from the committed ncu
-    summary (profiles/q4k_matvec_14336x4096.md), or None."""
-    p = os.path.join(ROOT, "profiles", "q4k_matvec_14336x4096.md")
+    summary (profiles/q4k_gateup_grouped_2x14336x4096.md), or None."""
+    p = os.path.join(ROOT, "profiles", "q4k_gateup_grouped_2x14336x4096.md")
     if not os.path.exists(p):
         return None
     for line in open(p):
@@ -150,7 +150,28 @@ def kernel_benchmarks(gb, torch, dm, peak):
         torch.cuda.empty_cache()
         return gbs, alg, t
 
-    main = matvec_case("q4k_matvec_14336x4096", 4, 14336, 4096, 12, 200)
+    def gateup_case(tag, rows, cols, copies, n_iter):
+        """gate and up as the decode step launches them: one grouped launch
+        over two Q4_K matrices that share x."""
+        wbytes = gb.matrix_bytes(4, rows, cols)
+        bufs = [[torch.empty(wbytes + 16, dtype=torch.uint8, device="cuda") for _ in range(2)] for _ in range(copies)]
+        for j, pair in enumerate(bufs):
+            for i, b in enumerate(pair):
+                gb.synth_blocks(4, b, wbytes // gb.BLOCK_BYTES[4], SEED, 300 + 2 * j + i, stream=sp)
+        x = torch.empty(cols, dtype=torch.float32, device="cuda")
+        gb.synth_normal(x, cols, SEED, 5, stream=sp)
+        ys = [torch.empty(rows, dtype=torch.float32, device="cuda") for _ in range(2)]
+        st.synchronize()
+        t = timed(lambda i: gb.matvec_group([4, 4], bufs[i % copies], [rows, rows], cols, x, ys, stream=sp), n_iter)
+        alg = 2 * wbytes + 4 * cols + 2 * 4 * rows
+        gbs = alg / t / 1e9
+        res[tag] = {"us": round(t * 1e6, 2), "alg_bytes": alg, "GB/s": round(gbs, 1), "frac": round(gbs / peak, 3)}
+        del bufs
+        torch.cuda.empty_cache()
+        return gbs, alg, t
+
+    main = gateup_case("q4k_gateup_grouped_2x14336x4096", 14336, 4096, 6, 100)
+    matvec_case("q4k_matvec_14336x4096", 4, 14336, 4096, 12, 200)
     matvec_case("q4k_matvec_4096x4096 (config 0)", 4, 4096, 4096, 40, 400)
     matvec_case("q6k_matvec_4096x14336 (config 1)", 5, 4096, 14336, 10, 200)
     matvec_case("q6k_matvec_128256x4096 (config 1, output head)", 5, 128256, 4096, 2, 40)
@@ -362,7 +383,8 @@ def run_ours(args, rank, world, local_rank):
             "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4,
                     "api": "gb_model_decode_host (token, pos in; next token out)"},
             "gpu_launches": launches,
-            "roofline": {"bound": "hbm", "kernel": "q4k_matvec 14336x4096 (gate/up)", "achieved": round(gbs, 1),
+            "roofline": {"bound": "hbm", "kernel": "k_mvt Q4_K gate+up, one launch over 2 x 14336x4096 (the step's "
+                                                   "largest launch share)", "achieved": round(gbs, 1),
                          "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 3), "traffic": ncu_traffic(),
                          "alg_bytes_per_launch": alg, "peak_kind": peak_kind},
             "kernels": kernels,
@@ -403,6 +425,17 @@ def profile_kernel(name: str) -> None:
         out = torch.empty(nh * hd, dtype=torch.float32, device="cuda")
         launch = lambda i: gb.attention_decode(q, k, v, kc[i % copies], vc[i % copies], cs, d_pos, nh, nkv, hd,  # noqa
                                                ms, out, ws, stream=sp)
+    elif name == "q4k_gu":   # gate + up in one launch, as in the decode step
+        rows, cols, copies = 14336, 4096, 3
+        wb = gb.matrix_bytes(4, rows, cols)
+        bufs = [[torch.empty(wb + 16, dtype=torch.uint8, device="cuda") for _ in range(2)] for _ in range(copies)]
+        for j, pair in enumerate(bufs):
+            for i, b in enumerate(pair):
+                gb.synth_blocks(4, b, wb // gb.BLOCK_BYTES[4], SEED, 60 + 2 * j + i, stream=sp)
+        x = torch.empty(cols, dtype=torch.float32, device="cuda")
+        gb.synth_normal(x, cols, SEED, 5, stream=sp)
+        ys = [torch.empty(rows, dtype=torch.float32, device="cuda") for _ in range(2)]
+        launch = lambda i: gb.matvec_group([4, 4], bufs[i % copies], [rows, rows], cols, x, ys, stream=sp)  # noqa
     else:
         dt, rows, cols, copies = {"q4k": (4, 14336, 4096, 6), "q6k": (5, 4096, 14336, 4),
                                   "q6k_head": (5, 128256, 4096, 1), "q8_0": (2, 14336, 4096, 4)}[name]
@@ -464,7 +497,7 @@ def main():
     ap.add_argument("--decode-only", action="store_true",
                     help="run the warm-up and timed decode steps only (for ncu launch lists) and exit")
     ap.add_argument("--steps-ref", type=int, default=None, help="reference arm samples (default min(steps, 5))")
-    ap.add_argument("--kernel", choices=["q4k", "q6k", "q6k_head", "q8_0", "attn"], default=None,
+    ap.add_argument("--kernel", choices=["q4k", "q4k_gu", "q6k", "q6k_head", "q8_0", "attn"], default=None,
                     help="run only a few launches of one kernel (for ncu captures) and exit")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":

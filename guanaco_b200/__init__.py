@@ -95,6 +95,7 @@ SIGNATURES = {
     "gb_version": (C.c_char_p, []),
     "gb_device_sm_count": (_i, []),
     "gb_matvec": (_i, [_i, _vp, _i, _i, _vp, _vp, _vp, _vp]),
+    "gb_matvec_group": (_i, [_i, _vp, _vp, _vp, _i, _vp, _vp, _vp]),
     "gb_matvec_host": (_i, [_i, _vp, _i, _i, _vp, _vp]),
     "gb_device_error": (_i, [_i]),
     "gb_dequant": (_i, [_i, _vp, _sz, _vp, _vp]),
@@ -172,6 +173,17 @@ def check(fn: str, rc: int) -> None:
 def matvec(dtype, W, rows, cols, x, y, residual=None, stream=None) -> None:
     check("gb_matvec", lib().gb_matvec(dtype, _ptr(W), rows, cols, _ptr(x), _ptr(y), _ptr(residual),
                                         _stream(stream)))
+
+
+def matvec_group(dtypes, Ws, rows, cols, x, ys, stream=None) -> None:
+    """ys[i] = Ws[i] . x for up to three matrices sharing x (one launch when
+    their formats allow it)."""
+    n = len(Ws)
+    dt = (C.c_int * n)(*dtypes)
+    wp = (C.c_void_p * n)(*[_ptr(w) for w in Ws])
+    rw = (C.c_int * n)(*rows)
+    yp = (C.c_void_p * n)(*[_ptr(v) for v in ys])
+    check("gb_matvec_group", lib().gb_matvec_group(n, dt, wp, rw, cols, _ptr(x), yp, _stream(stream)))
 
 
 def dequant(dtype, blocks, nblocks, out, stream=None) -> None:

@@ -1333,6 +1333,31 @@ extern "C" int gb_matvec(int dtype, const void* W, int rows, int cols, const flo
     return mv_launch(p, x, y, residual, ws, st, false, nullptr);
 }
 
+extern "C" int gb_matvec_group(int n, const int* dtypes, const void* const* W, const int* rows, int cols,
+                               const float* x, float* const* y, void* stream) {
+    if (n < 1 || n > MT_MAXM || !dtypes || !W || !rows || !x || !y || cols <= 0) return GB_EINVAL;
+    if (reinterpret_cast<uintptr_t>(x) & 15) return GB_EINVAL;
+    MvPlan plans[MT_MAXM];
+    const MvPlan* ps[MT_MAXM];
+    for (int i = 0; i < n; i++) {
+        if (!W[i] || !y[i] || rows[i] <= 0 || (reinterpret_cast<uintptr_t>(W[i]) & 15)) return GB_EINVAL;
+        const int rc = mv_plan(&plans[i], dtypes[i], W[i], rows[i], cols);
+        if (rc) return rc;
+        ps[i] = &plans[i];
+    }
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (mv_groupable(ps, n)) {
+        void* ws = stream_workspace(st, mv_ws_bytes_group(ps, n));
+        return mv_launch_group(ps, n, x, y, nullptr, ws, st, false, nullptr);
+    }
+    for (int i = 0; i < n; i++) {
+        void* ws = plans[i].kind == MV_TMA ? stream_workspace(st, mv_ws_bytes(plans[i])) : nullptr;
+        const int rc = mv_launch(plans[i], x, y[i], nullptr, ws, st, false, nullptr);
+        if (rc) return rc;
+    }
+    return GB_OK;
+}
+
 extern "C" int gb_device_error(int clear) {
     unsigned v = 0;
     if (cudaMemcpyFromSymbol(&v, g_gb_device_err, sizeof(v)) != cudaSuccess) return GB_ECUDA;

@@ -102,6 +102,14 @@ int gb_device_sm_count(void);
 int gb_matvec(int dtype, const void* W, int rows, int cols, const float* x, float* y,
               const float* residual, void* stream);
 
+/* y_i = W_i . x for n <= 3 matrices that share x (all with cols columns):
+ * one launch with one work split when the formats allow it (the decode
+ * step's q/k/v and gate/up launches), else one launch per matrix.  The same
+ * alignment rules as gb_matvec.  No counterpart in the reference, which
+ * runs one matvec per weight (src/engine/engine.c:362-371, 533-543). */
+int gb_matvec_group(int n, const int* dtypes, const void* const* W, const int* rows, int cols, const float* x,
+                    float* const* y, void* stream);
+
 /* Sticky device error word set by the library's kernels (0 = none, -7 for a
  * bounded wait that ran out).  Synchronous; clear != 0 resets it. */
 int gb_device_error(int clear);

@@ -323,3 +323,31 @@ def test_vtable_host_cache_detects_reuse(gb, oracle, cuda):
         assert rel_l2(y, oracle.matvec(5, W, rows, cols, x)[1]) <= 1e-4
     finally:
         be.close()
+
+
+@pytest.mark.parametrize("dts,rows,cols", [
+    ((4, 4), (14336, 14336), 4096),        # gate / up
+    ((4, 4, 5), (4096, 1024, 1024), 4096),   # q / k / v: Q6_K v, mixed formats in one launch
+    ((4, 5), (96, 40), 2048),               # short, ragged rows
+    ((4, 2), (64, 64), 512),                # Q8_0 is off the grouped path: one launch per matrix
+])
+def test_matvec_group_matches_single(gb, oracle, cuda, dts, rows, cols):
+    """Matrices sharing x in one launch give each product within the
+    matvec tolerance of the oracle and of its own single launch."""
+    x_host = oracle.synth_normal(cols, 91, 1)
+    Ws, refs = [], []
+    for i, (dt, r) in enumerate(zip(dts, rows)):
+        W = oracle.synth_blocks(dt, r, cols, 91, 10 + i)
+        Ws.append(dev_blocks(cuda, W))
+        refs.append(oracle.matvec(dt, W, r, cols, x_host)[1])
+    x = to_dev(cuda, x_host)
+    ys = [cuda.empty(r, dtype=cuda.float32, device="cuda") for r in rows]
+    gb.matvec_group(list(dts), Ws, list(rows), cols, x, ys)
+    singles = [cuda.empty(r, dtype=cuda.float32, device="cuda") for r in rows]
+    for dt, W, r, y1 in zip(dts, Ws, rows, singles):
+        gb.matvec(dt, W, r, cols, x, y1)
+    cuda.cuda.synchronize()
+    assert gb.lib().gb_device_error(1) == 0
+    for y, y1, ref in zip(ys, singles, refs):
+        assert rel_l2(from_dev(y), ref) <= 1e-4
+        assert rel_l2(from_dev(y), from_dev(y1)) <= 1e-5
