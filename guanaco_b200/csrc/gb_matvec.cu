@@ -768,12 +768,14 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
     int gi = 0;
     bool ok = true;
     float acc_a[2] = {0.f, 0.f}, acc_b[2] = {0.f, 0.f};
-    for (int t = t0, i = 0; t < t1; i++) {
-        // stage i: item t, the same walk as the producer's
-        int m, grp, it;
-        mt_locate(a, t, m, grp, it);
-        const int s = i % S;
-        if (ok) ok = mbs_wait(bar_full + 8 * s, (i / S) & 1, &g_gb_device_err);
+    // item t's matrix, group and item within the group (the producer's walk),
+    // its ring slot and barrier parity: advanced per stage without divisions
+    int m, grp, it;
+    mt_locate(a, t0, m, grp, it);
+    int s = 0;
+    unsigned ph = 0;
+    for (int t = t0; t < t1;) {
+        if (ok) ok = mbs_wait(bar_full + 8 * s, ph, &g_gb_device_err);
         if (ok) {
             const bool q6 = MIXED ? a.fmt[m] != 0 : FQ6;
             if (q6)
@@ -785,6 +787,10 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
         }
         __syncwarp();
         if (lane == 0) mbs_arrive(bar_empty + 8 * s);
+        if (++s == S) {
+            s = 0;
+            ph ^= 1u;
+        }
         t++;
 
         const int nch = a.nchm[m];
@@ -880,6 +886,22 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
             }
             acc_a[0] = acc_a[1] = acc_b[0] = acc_b[1] = 0.f;
             gi++;
+        }
+        if (++it == nch) {   // the next item starts a group
+            it = 0;
+            if (a.swq_out) {   // gate g, up g, gate g + 1, ...
+                if (m) {
+                    m = 0;
+                    grp++;
+                } else {
+                    m = 1;
+                }
+            } else if (t == a.ibase[m + 1]) {
+                m++;
+                grp = 0;
+            } else {
+                grp++;
+            }
         }
     }
 }
