@@ -12,6 +12,7 @@
 #include "gb_common.cuh"
 #include "gb_internal.h"
 
+#include <algorithm>
 #include <cstring>
 
 #include <dlfcn.h>
@@ -47,6 +48,7 @@ struct Ctx {
     int rope_seq = 0, rope_hd = 0;
     void* ws = nullptr;
     size_t ws_bytes = 0;
+    int ws_shape[4] = {0, 0, 0, 0};   // (n_heads, n_kv, hd, max_seq) the ticket words were zeroed for
     std::vector<LayerKV> kv;
     struct CachedNorm {
         float* d = nullptr;
@@ -117,13 +119,23 @@ static bool ensure_rope(Ctx* c, int max_seq, int hd) {
 static bool ensure_ws(Ctx* c, int n_heads, int n_kv, int hd, int max_seq) {
     const size_t need = gb_attn_workspace_bytes(n_heads, n_kv, hd, max_seq);
     if (need == 0) return false;
-    if (c->ws && c->ws_bytes >= need) return true;
-    if (c->ws) { cudaStreamSynchronize(c->st); cudaFree(c->ws); }
-    c->ws = nullptr;
-    if (cudaMalloc(&c->ws, need) != cudaSuccess) { c->ws = nullptr; return false; }
+    const int shape[4] = {n_heads, n_kv, hd, max_seq};
+    const bool same = std::equal(shape, shape + 4, c->ws_shape);
+    if (c->ws && c->ws_bytes >= need) {
+        // the tickets sit after the partials, so another shape puts them on
+        // words that held partials: zero again (in stream order) on a change
+        if (same) return true;
+    } else {
+        if (c->ws) { cudaStreamSynchronize(c->st); cudaFree(c->ws); }
+        c->ws = nullptr;
+        c->ws_bytes = 0;
+        if (cudaMalloc(&c->ws, need) != cudaSuccess) { c->ws = nullptr; return false; }
+        c->ws_bytes = need;
+    }
     // zeroed in stream order: the split-K tickets must read 0 on first use
-    if (cudaMemsetAsync(c->ws, 0, need, c->st) != cudaSuccess) return false;
-    c->ws_bytes = need;
+    std::fill(c->ws_shape, c->ws_shape + 4, 0);
+    if (cudaMemsetAsync(c->ws, 0, c->ws_bytes, c->st) != cudaSuccess) return false;
+    std::copy(shape, shape + 4, c->ws_shape);
     return true;
 }
 

@@ -69,7 +69,7 @@ struct AttnCfg {
     static constexpr int CH = HD / 4;                 // float4 columns of a V row
     static constexpr int RPL = 32 / CH;               // rows a warp's P.V step covers
     // shared: q[GROUP][HD] | k_new[HD] | v_new[HD] | per-warp p[TP][2] |
-    // merge sums [8] | issued-item count [4] | ring[R][TILE] | full[R], empty[R]
+    // spare [8] | issued-item count [4] | ring[R][TILE] | full[R], empty[R]
     static constexpr int HEAD_FLOATS = GROUP * HD + 2 * HD + ATTN_CWARPS * TP * 2 + 8 + 4;
     static constexpr size_t RING_OFF = ((size_t)HEAD_FLOATS * sizeof(float) + 127) / 128 * 128;
     static constexpr int R0 = (int)((ATTN_SMEM_MAX - RING_OFF - 512) / (TILE * sizeof(float)));
@@ -136,11 +136,11 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
     float* kn = qs + GROUP * HD;          // [HD] rotated new k
     float* vn = kn + HD;                  // [HD] new v
     float* pw_all = vn + HD;              // [CWARPS][TP][2] each warp's scores, then probabilities
-    float* lm = pw_all + ATTN_CWARPS * C::TP * 2;   // [GROUP] merge: sum over the splits
+    float* spare = pw_all + ATTN_CWARPS * C::TP * 2;   // [8] unused
     // items the producer has issued: a consumer waits for its item to be
     // issued before it waits on the slot's barrier (a slot's barrier only
     // tells one generation from the next, and warps wait out of item order)
-    volatile int* issued = reinterpret_cast<volatile int*>(lm + 8);
+    volatile int* issued = reinterpret_cast<volatile int*>(spare + 8);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int kvh = blockIdx.x / grid_splits, split = blockIdx.x % grid_splits;
@@ -150,8 +150,9 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
         return;
     }
     const int seq = pos + 1;
-    int P = (seq + grid_splits - 1) / grid_splits;
-    P = (P + C::TP - 1) / C::TP * C::TP;
+    // positions per split: any count (a copy is whole 512-byte rows), so every
+    // split of the grid gets work
+    const int P = (seq + grid_splits - 1) / grid_splits;
     const int nsplit = (seq + P - 1) / P;
     if (split >= nsplit) return;
     const int s0 = split * P, n = min(seq, s0 + P) - s0;
@@ -162,39 +163,26 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
     unsigned char* smb = reinterpret_cast<unsigned char*>(sm);
     float* ring = reinterpret_cast<float*>(smb + C::RING_OFF);
     const uint32_t full = a_sptr(smb + C::BAR_OFF), empty = full + 8 * C::R;
-    if (tid == 0) {
-        for (int r = 0; r < C::R; r++) {
-            a_bar_init(full + 8 * r, 1);
-            a_bar_init(empty + 8 * r, C::NHG);   // the warps that own the tile release it
-        }
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        *issued = 0;
-    }
-    // ---- RoPE (reference rounding: a*c - b*s, a*s + b*c, no contraction)
-    const float* cs = rope_cs + (size_t)pos * HD;
-    for (int e = tid; e < (GROUP + 1) * (HD / 2); e += ATTN_THREADS) {
-        const int h = e / (HD / 2), i = e % (HD / 2);
-        const float* src = h < GROUP ? q + (size_t)(kvh * GROUP + h) * HD : knew + (size_t)kvh * HD;
-        float* dst = h < GROUP ? qs + h * HD : kn;
-        const float a = src[2 * i], b = src[2 * i + 1], c = cs[2 * i], s = cs[2 * i + 1];
-        dst[2 * i] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
-        dst[2 * i + 1] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
-    }
-    for (int i = tid; i < HD; i += ATTN_THREADS) vn[i] = vnew[(size_t)kvh * HD + i];
-    __syncthreads();
-    if (owner) {   // KV append at slot pos (the ring index pos % max_seq == pos here)
-        for (int i = tid; i < HD; i += ATTN_THREADS) {
-            kc[head_base + (size_t)pos * HD + i] = kn[i];
-            vc[head_base + (size_t)pos * HD + i] = vn[i];
-        }
-    }
 
     // ---- items: 2t = K tile t, 2t + 1 = V tile t, in slot item % R.  Tile t
     // belongs to the NHG consumer warps of tile lane t % TW (one per group of
     // HPW query heads), which release both of its slots.
     // The row of the new position is read from kn / vn, never from a tile
-    // (the copy may precede the append).
+    // (the copy may precede the append).  The producer starts the stream at
+    // once and only arrives on barrier 2, so RoPE runs on the consumer warps
+    // while the first tiles are in flight.
     if (warp == ATTN_CWARPS) {   // ---- producer
+        if (lane == 0) {
+            for (int r = 0; r < C::R; r++) {
+                a_bar_init(full + 8 * r, 1);
+                a_bar_init(empty + 8 * r, C::NHG);   // the warps that own the tile release it
+            }
+            asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+            *issued = 0;
+            __threadfence_block();
+        }
+        __syncwarp();
+        asm volatile("bar.arrive 2, %0;" ::"n"(ATTN_THREADS) : "memory");   // barriers and count ready
         if (lane == 0) {
             bool ok = true;
             int it = 0;
@@ -221,6 +209,27 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
                 }
         }
         return;
+    }
+
+    // ---- RoPE on the consumer warps (reference rounding: a*c - b*s,
+    // a*s + b*c, no contraction)
+    constexpr int CT = ATTN_CWARPS * 32;   // consumer threads
+    const float* cs = rope_cs + (size_t)pos * HD;
+    for (int e = tid; e < (GROUP + 1) * (HD / 2); e += CT) {
+        const int h = e / (HD / 2), i = e % (HD / 2);
+        const float* src = h < GROUP ? q + (size_t)(kvh * GROUP + h) * HD : knew + (size_t)kvh * HD;
+        float* dst = h < GROUP ? qs + h * HD : kn;
+        const float a = src[2 * i], b = src[2 * i + 1], c = cs[2 * i], s = cs[2 * i + 1];
+        dst[2 * i] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+        dst[2 * i + 1] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+    }
+    for (int i = tid; i < HD; i += CT) vn[i] = vnew[(size_t)kvh * HD + i];
+    asm volatile("bar.sync 2, %0;" ::"n"(ATTN_THREADS) : "memory");   // with the producer's arrival
+    if (owner) {   // KV append at slot pos (the ring index pos % max_seq == pos here)
+        for (int i = tid; i < HD; i += CT) {
+            kc[head_base + (size_t)pos * HD + i] = kn[i];
+            vc[head_base + (size_t)pos * HD + i] = vn[i];
+        }
     }
 
     // ---- consumer warps: each runs its own online softmax over its tiles
@@ -355,7 +364,7 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
     }
     __syncwarp();   // bar.sync is warp-aligned: reconverge the warp first
     asm volatile("bar.sync 1, %0;" ::"n"(ATTN_CWARPS * 32) : "memory");
-    const int ctid = tid;   // 0 .. 255
+    const int ctid = tid;   // 0 .. CT - 1
     const bool single = nsplit == 1;
     float* my = part + ((size_t)kvh * grid_splits + split) * GROUP * (HD + 2);
     for (int e = ctid; e < GROUP * HD; e += ATTN_CWARPS * 32) {
@@ -390,55 +399,52 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
     asm volatile("bar.sync 1, %0;" ::"n"(ATTN_CWARPS * 32) : "memory");
     if (!last) return;
     __threadfence();
+    // every output is a weighted sum over the splits in split order, in one
+    // pass with a running maximum: chunks of MC splits, the next chunk's
+    // loads in flight while the current one is summed
     const float* base = part + (size_t)kvh * grid_splits * GROUP * (HD + 2);
-    // split weights w_j = exp(m_j - M) and L = sum l_j w_j once per head (one
-    // warp per head), then every output is a weighted sum over the splits in
-    // split order; the ring (free) holds the weights [GROUP][nsplit]
-    float* wbuf = ring + C::TW * GROUP * WS;
-    if (warp < GROUP) {   // (m, l) of every split: one load per lane and 32 splits
-        const int h = warp;
-        constexpr int MJ = (GB_NUM_SMS + 31) / 32;   // splits per lane at most
-        float2 ml[MJ];
-#pragma unroll
-        for (int i = 0; i < MJ; i++) {
-            const int j = lane + 32 * i;
-            ml[i] = j < nsplit ? __ldcg(reinterpret_cast<const float2*>(base + ((size_t)j * GROUP + h) * (HD + 2)))
-                               : make_float2(-INFINITY, 0.f);
-        }
-        float M = -INFINITY;
-#pragma unroll
-        for (int i = 0; i < MJ; i++) M = fmaxf(M, ml[i].x);
-        M = warp_max(M);
-        float L = 0.f;
-#pragma unroll
-        for (int i = 0; i < MJ; i++) {
-            const int j = lane + 32 * i;
-            if (j < nsplit) {
-                const float w = expf(ml[i].x - M);
-                wbuf[h * nsplit + j] = w;
-                L = fmaf(ml[i].y, w, L);
-            }
-        }
-        L = warp_sum(L);
-        if (lane == 0) lm[h] = L;
-    }
-    __syncwarp();   // bar.sync is warp-aligned: reconverge the warp first
-    asm volatile("bar.sync 1, %0;" ::"n"(ATTN_CWARPS * 32) : "memory");
-    for (int e = ctid; e < GROUP * HD; e += ATTN_CWARPS * 32) {
+    constexpr int MC = 10;
+    constexpr size_t SS = (size_t)GROUP * (HD + 2);   // floats from one split to the next
+    for (int e = ctid; e < GROUP * HD; e += CT) {
         const int h = e / HD, d = e % HD;
-        const float* wj = wbuf + h * nsplit;
-        const float* pj = base + (size_t)h * (HD + 2) + 2 + d;
-        float O = 0.f;
-        for (int j0 = 0; j0 < nsplit; j0 += 16) {   // 16 loads in flight, summed in split order
-            float pv[16];
+        const float* hb = base + (size_t)h * (HD + 2);
+        float M = -INFINITY, L = 0.f, O = 0.f;
+        auto fetch = [&](float2 (&ml)[MC], float (&pv)[MC], int j0) {
 #pragma unroll
-            for (int i = 0; i < 16; i++)
-                pv[i] = j0 + i < nsplit ? __ldcg(pj + (size_t)(j0 + i) * GROUP * (HD + 2)) : 0.f;
+            for (int i = 0; i < MC; i++) {
+                const bool in = j0 + i < nsplit;
+                const float* pj = hb + (size_t)(j0 + i) * SS;
+                ml[i] = in ? __ldcg(reinterpret_cast<const float2*>(pj)) : make_float2(-INFINITY, 0.f);
+                pv[i] = in ? __ldcg(pj + 2 + d) : 0.f;
+            }
+        };
+        auto combine = [&](const float2 (&ml)[MC], const float (&pv)[MC], int j0) {
+            float Mc = M;
 #pragma unroll
-            for (int i = 0; i < 16; i++)
-                if (j0 + i < nsplit) O = fmaf(pv[i], wj[j0 + i], O);
+            for (int i = 0; i < MC; i++) Mc = fmaxf(Mc, ml[i].x);
+            const float a = M == -INFINITY ? 0.f : expf(M - Mc);   // L, O are 0 before the first chunk
+            L *= a;
+            O *= a;
+#pragma unroll
+            for (int i = 0; i < MC; i++)
+                if (j0 + i < nsplit) {
+                    const float w = expf(ml[i].x - Mc);
+                    L = fmaf(ml[i].y, w, L);
+                    O = fmaf(pv[i], w, O);
+                }
+            M = Mc;
+        };
+        float2 mla[MC], mlb[MC];
+        float pva[MC], pvb[MC];
+        fetch(mla, pva, 0);
+        for (int j0 = 0; j0 < nsplit; j0 += 2 * MC) {
+            if (j0 + MC < nsplit) fetch(mlb, pvb, j0 + MC);
+            combine(mla, pva, j0);
+            if (j0 + MC >= nsplit) break;
+            if (j0 + 2 * MC < nsplit) fetch(mla, pva, j0 + 2 * MC);
+            combine(mlb, pvb, j0 + MC);
         }
-        out[(size_t)(kvh * GROUP + h) * HD + d] = O / lm[h];
+        out[(size_t)(kvh * GROUP + h) * HD + d] = O / L;
     }
     if (ctid == 0) tickets[kvh] = 0u;   // every split has arrived: safe to rearm
 }

@@ -220,6 +220,33 @@ def test_dropin_layer_rewind_uses_restored_host_kv(gb, oracle, cuda):
     assert rel_l2(h, h_ref) <= REL_L2_TOL
 
 
+def test_dropin_layer_shape_change_rezeroes_attention_tickets(gb, oracle, cuda):
+    """The drop-in context keeps one attention workspace; a later call with a
+    smaller shape reuses it, and its split-merge tickets then fall on words
+    that held the earlier shape's partials.  Both calls must match the
+    reference layer."""
+    L = gb.lib()
+    for H, nh, nkv, ff, ms, pos, layer in ((512, 4, 2, 1024, 300, 200, 21), (512, 8, 2, 1536, 40, 9, 22)):
+        hd = H // nh
+        ws, dts, shapes, ra, rf = layer_weights(oracle, H, nh, nkv, hd, ff, 23, (4, 4, 4, 4, 4, 4, 4))
+        dptr = [L.cuda_upload_weight(w.ctypes.data, w.nbytes) for w in ws]
+        args = []
+        for d, (r, c), dt in zip(dptr, shapes, dts):
+            args += [d, r, c, dt]
+        kc = np.zeros(nkv * ms * hd, np.float32)
+        vc = np.zeros(nkv * ms * hd, np.float32)
+        kc.reshape(nkv, ms, hd)[:, :pos] = oracle.synth_normal(nkv * pos * hd, 41, 1).reshape(nkv, pos, hd)
+        vc.reshape(nkv, ms, hd)[:, :pos] = oracle.synth_normal(nkv * pos * hd, 41, 2).reshape(nkv, pos, hd)
+        h = oracle.synth_normal(H, 43, 3)
+        kc_ref, vc_ref = kc.copy(), vc.copy()
+        h_ref, _, _ = oracle.layer_decode(ws, dts, shapes, ra, rf, h.copy(), kc_ref, vc_ref, H, nh, nkv, hd, ff, ms,
+                                          pos)
+        assert L.cuda_transformer_layer_gpu(*args, ra.ctypes.data, rf.ctypes.data, h.ctypes.data, kc.ctypes.data,
+                                            vc.ctypes.data, ms * hd, H, nh, nkv, hd, pos, layer, ms) == 0
+        L.cuda_finish_layer()
+        assert rel_l2(h, h_ref) <= REL_L2_TOL, (ms, pos)
+
+
 def test_dropin_norm_cache_follows_host_values(gb, oracle, cuda):
     """Norm weights are cached by host pointer: new values at the same address
     (a freed and reallocated host buffer) must be used, not the old copy."""
