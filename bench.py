@@ -112,7 +112,11 @@ def kernel_benchmarks(gb, torch, dm, peak):
     def timed(launch, n_iter, warm=3, reps=3):
         """Seconds per launch: n_iter launches captured in one CUDA graph on
         the launching stream (as the decode step issues them, without host
-        overhead), replayed reps times between CUDA events on that stream."""
+        overhead), replayed reps times between CUDA events on that stream.
+        Matvec launches carry programmatic dependent launch, so each one
+        starts fetching weights during its predecessor's tail, as in the
+        decode step (GB_DISABLE_PDL=1 in the environment times them
+        unchained)."""
         for i in range(warm):
             launch(i)
         st.synchronize()

@@ -1088,6 +1088,14 @@ size_t mv_ws_bytes(const MvPlan& p) {
     return (size_t)GB_NUM_SMS * 2 * MT_GR * sizeof(float) + ((size_t)p.ngroups * sizeof(unsigned) + 255) / 256 * 256;
 }
 
+// Matvec launches carry the programmatic-dependent-launch attribute: after a
+// predecessor that has executed griddepcontrol.launch_dependents (the matvec
+// and attention kernels do so at their top) the CTAs start at once and stream
+// weight boxes; they read x, the residual and the workspace and write y only
+// after griddepcontrol.wait (the predecessor complete and its writes visible).
+// After any other predecessor the launch behaves as a plain one.  Weights must
+// therefore not be written by a kernel that triggers its dependents early (no
+// kernel of this library writes weights).
 // GB_DISABLE_PDL=1 in the environment turns programmatic dependent launch off
 // (every matvec then waits for the previous kernel to finish before starting).
 static bool pdl_allowed() {
@@ -1352,7 +1360,7 @@ extern "C" int gb_matvec(int dtype, const void* W, int rows, int cols, const flo
     if (rc) return rc;
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     void* ws = p.kind == MV_TMA ? stream_workspace(st, mv_ws_bytes(p)) : nullptr;
-    return mv_launch(p, x, y, residual, ws, st, false, nullptr);
+    return mv_launch(p, x, y, residual, ws, st, true, nullptr);
 }
 
 extern "C" int gb_matvec_group(int n, const int* dtypes, const void* const* W, const int* rows, int cols,
@@ -1370,11 +1378,11 @@ extern "C" int gb_matvec_group(int n, const int* dtypes, const void* const* W, c
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (mv_groupable(ps, n)) {
         void* ws = stream_workspace(st, mv_ws_bytes_group(ps, n));
-        return mv_launch_group(ps, n, x, y, nullptr, ws, st, false, nullptr);
+        return mv_launch_group(ps, n, x, y, nullptr, ws, st, true, nullptr);
     }
     for (int i = 0; i < n; i++) {
         void* ws = plans[i].kind == MV_TMA ? stream_workspace(st, mv_ws_bytes(plans[i])) : nullptr;
-        const int rc = mv_launch(plans[i], x, y[i], nullptr, ws, st, false, nullptr);
+        const int rc = mv_launch(plans[i], x, y[i], nullptr, ws, st, true, nullptr);
         if (rc) return rc;
     }
     return GB_OK;

@@ -98,7 +98,12 @@ int gb_device_sm_count(void);
 /* y[rows] = W[rows, cols] . x[cols] (+ residual[rows] when residual != NULL).
  * W: GGUF blocks, 16-byte aligned (row tiles are fetched with bulk copies);
  * x: 16-byte aligned.  y may alias residual.  The kernel's bounded waits
- * report through gb_device_error(). */
+ * report through gb_device_error().  Launched with programmatic dependent
+ * launch: right after another matvec of this library on the same stream it
+ * starts fetching W before that one has finished (x, residual and y are
+ * touched only after it), so W must not be written by the kernel just before
+ * it on the stream unless that kernel runs to completion first (any kernel
+ * that does not execute griddepcontrol.launch_dependents does). */
 int gb_matvec(int dtype, const void* W, int rows, int cols, const float* x, float* y,
               const float* residual, void* stream);
 
