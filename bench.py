@@ -384,7 +384,7 @@ def run_ours(args, rank, world, local_rank):
                        "positions": [pos_timed0, pos_timed0 + K - 1],
                        "step_alg_bytes": round(step_bytes),
                        "step_hbm_frac": round(step_bytes / world / (t_ms / K * 1e-3) / 1e9 / peak, 3)},
-            "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4,
+            "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8,
                     "api": "gb_model_decode_host (token, pos in; next token out)"},
             "gpu_launches": launches,
             "roofline": {"bound": "hbm", "kernel": "k_mvt Q4_K gate+up, one launch over 2 x 14336x4096 (the step's "

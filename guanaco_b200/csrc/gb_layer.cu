@@ -399,7 +399,8 @@ struct gb_model {
     float *gate = nullptr, *up = nullptr, *logits = nullptr;
     unsigned* err = nullptr;
     int *d_tok = nullptr, *d_pos = nullptr, *d_next = nullptr;
-    int* h_io = nullptr;              // pinned {token, pos, next}
+    int* io = nullptr;                // device {token, pos, next, error}: d_tok .. err point into it
+    int* h_io = nullptr;              // pinned {token, pos, next, error}
     cudaStream_t stream = nullptr;
 
     cudaGraphExec_t exec = nullptr;
@@ -487,10 +488,15 @@ extern "C" gb_model* gb_model_create_tp(const gb_model_config* cfg, int rank, in
         ok &= (m->swq_tk = (unsigned*)dalloc(m, (size_t)FP / 32 * sizeof(unsigned))) != nullptr;
     }
     ok &= (m->logits = (float*)dalloc(m, (size_t)m->vocab_l * 4)) != nullptr;
-    ok &= (m->err = (unsigned*)dalloc(m, 16)) != nullptr;
-    ok &= (m->d_tok = (int*)dalloc(m, 16)) != nullptr;
-    ok &= (m->d_pos = (int*)dalloc(m, 16)) != nullptr;
-    ok &= (m->d_next = (int*)dalloc(m, 16)) != nullptr;
+    // the host-facing words share one block: gb_model_decode_host sends
+    // {token, pos} in one copy and reads {next, error} back in one copy
+    ok &= (m->io = (int*)dalloc(m, 64)) != nullptr;
+    if (m->io) {
+        m->d_tok = m->io;
+        m->d_pos = m->io + 1;
+        m->d_next = m->io + 2;
+        m->err = reinterpret_cast<unsigned*>(m->io + 3);
+    }
     ok &= (m->d_count = (int*)dalloc(m, 16)) != nullptr;
     ok &= (m->am_ws = dalloc(m, AM_WS_BYTES)) != nullptr;
     ok &= (m->d_step = (unsigned long long*)dalloc(m, 16)) != nullptr;
@@ -510,7 +516,7 @@ extern "C" gb_model* gb_model_create_tp(const gb_model_config* cfg, int rank, in
     if (ok) ok &= cudaMemsetAsync(m->kc, 0, kv_elems * 4, m->stream) == cudaSuccess &&
                   cudaMemsetAsync(m->vc, 0, kv_elems * 4, m->stream) == cudaSuccess;
     if (ok) ok &= cudaMemsetAsync(m->attn_ws, 0, ws, m->stream) == cudaSuccess &&
-                  cudaMemsetAsync(m->err, 0, 16, m->stream) == cudaSuccess &&
+                  cudaMemsetAsync(m->io, 0, 64, m->stream) == cudaSuccess &&
                   cudaMemsetAsync(m->am_ws, 0, AM_WS_BYTES, m->stream) == cudaSuccess &&
                   cudaMemsetAsync(m->d_step, 0, 16, m->stream) == cudaSuccess &&
                   cudaMemsetAsync(m->gate, 0, (size_t)FP * 4, m->stream) == cudaSuccess &&
@@ -1294,16 +1300,14 @@ extern "C" int gb_model_decode_host(gb_model* m, int token, int pos, int* h_next
     cudaStream_t st = m->stream;
     m->h_io[0] = token;
     m->h_io[1] = pos;
-    GB_CUDA_TRY(cudaMemcpyAsync(m->d_tok, &m->h_io[0], sizeof(int), cudaMemcpyHostToDevice, st));
-    GB_CUDA_TRY(cudaMemcpyAsync(m->d_pos, &m->h_io[1], sizeof(int), cudaMemcpyHostToDevice, st));
+    GB_CUDA_TRY(cudaMemcpyAsync(m->d_tok, &m->h_io[0], 2 * sizeof(int), cudaMemcpyHostToDevice, st));   // token, pos
     int rc = gb_model_decode(m, m->d_tok, m->d_pos, m->logits, m->d_next, st);
     if (rc) return rc;
-    GB_CUDA_TRY(cudaMemcpyAsync(&m->h_io[2], m->d_next, sizeof(int), cudaMemcpyDeviceToHost, st));
+    GB_CUDA_TRY(cudaMemcpyAsync(&m->h_io[2], m->d_next, 2 * sizeof(int), cudaMemcpyDeviceToHost, st));   // next, error
     if (h_logits)
         GB_CUDA_TRY(cudaMemcpyAsync(h_logits, m->logits, (size_t)m->vocab_l * 4, cudaMemcpyDeviceToHost, st));
     GB_CUDA_TRY(cudaStreamSynchronize(st));
-    unsigned herr = 0;
-    GB_CUDA_TRY(cudaMemcpy(&herr, m->err, sizeof(unsigned), cudaMemcpyDeviceToHost));
+    const unsigned herr = static_cast<unsigned>(m->h_io[3]);
     if (herr) return -(int)herr;
     *h_next = m->h_io[2];
     return GB_OK;
