@@ -35,6 +35,7 @@
 // a pos outside [0, max_seq) sets the error word and touches nothing.
 #include "gb_common.cuh"
 #include "gb_internal.h"
+#include "gb_mt.cuh"
 
 #include <mutex>
 
@@ -128,7 +129,7 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
               float* __restrict__ kc, float* __restrict__ vc, const float* __restrict__ rope_cs,
               const int* __restrict__ d_pos, int n_kv, int max_seq, int grid_splits,
               float* __restrict__ out, float* __restrict__ part, unsigned* __restrict__ tickets,
-              unsigned* __restrict__ err) {
+              unsigned* __restrict__ err, uint8_t* __restrict__ xq_out) {
     using C = AttnCfg<HD, GROUP>;
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // wo may start its weight prefetch
     extern __shared__ __align__(16) float sm[];
@@ -382,6 +383,8 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
         }
         if (single) {
             out[(size_t)(kvh * GROUP + h) * HD + d] = O / L;
+            // a warp holds one 32-column group: e >> 5 is warp-uniform
+            if (xq_out) mt_quantise32(xq_out, n_kv * GROUP * HD, (kvh * GROUP * HD + e) >> 5, lane, O / L);
         } else {
             my[h * (HD + 2) + 2 + d] = O;
             if (d == 0) { my[h * (HD + 2)] = M; my[h * (HD + 2) + 1] = L; }
@@ -445,6 +448,7 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
             combine(mlb, pvb, j0 + MC);
         }
         out[(size_t)(kvh * GROUP + h) * HD + d] = O / L;
+        if (xq_out) mt_quantise32(xq_out, n_kv * GROUP * HD, (kvh * GROUP * HD + e) >> 5, lane, O / L);
     }
     if (ctid == 0) tickets[kvh] = 0u;   // every split has arrived: safe to rearm
 }
@@ -454,7 +458,7 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
 template <int HD, int GROUP>
 static cudaError_t launch_attn(const float* q, const float* k, const float* v, float* kc, float* vc,
                                const float* cs, const int* d_pos, int n_kv, int max_seq, float* out,
-                               float* part, unsigned* tickets, unsigned* err, cudaStream_t st) {
+                               float* part, unsigned* tickets, unsigned* err, uint8_t* xq_out, cudaStream_t st) {
     using C = AttnCfg<HD, GROUP>;
     static unsigned configured = 0;
     int dev = 0;
@@ -467,19 +471,19 @@ static cudaError_t launch_attn(const float* q, const float* k, const float* v, f
     }
     const int G = attn_grid_splits(n_kv, max_seq);
     k_attn_decode<HD, GROUP><<<n_kv * G, ATTN_THREADS, C::SMEM, st>>>(q, k, v, kc, vc, cs, d_pos, n_kv, max_seq, G,
-                                                                      out, part, tickets, err);
+                                                                      out, part, tickets, err, xq_out);
     return cudaGetLastError();
 }
 
 // Both entry points: pick the instantiation for (head_dim, group).
 static int attn_dispatch(const float* q, const float* k, const float* v, float* kc, float* vc, const float* cs,
                          const int* d_pos, int n_heads, int n_kv, int head_dim, int max_seq, float* out,
-                         float* part, unsigned* tickets, unsigned* err, cudaStream_t st) {
+                         float* part, unsigned* tickets, unsigned* err, cudaStream_t st, uint8_t* xq_out = nullptr) {
     const int group = n_heads / n_kv;
     cudaError_t e = cudaErrorInvalidValue;
 #define GB_ATTN_CASE(HDV, GV)                                                                                       \
     if (head_dim == HDV && group == GV)                                                                             \
-        e = launch_attn<HDV, GV>(q, k, v, kc, vc, cs, d_pos, n_kv, max_seq, out, part, tickets, err, st);
+        e = launch_attn<HDV, GV>(q, k, v, kc, vc, cs, d_pos, n_kv, max_seq, out, part, tickets, err, xq_out, st);
     GB_ATTN_CASE(128, 1) GB_ATTN_CASE(128, 2) GB_ATTN_CASE(128, 4) GB_ATTN_CASE(128, 8)
     GB_ATTN_CASE(64, 1) GB_ATTN_CASE(64, 2) GB_ATTN_CASE(64, 4) GB_ATTN_CASE(64, 8)
 #undef GB_ATTN_CASE
@@ -524,17 +528,25 @@ extern "C" size_t gb_attn_workspace_bytes(int n_heads, int n_kv, int head_dim, i
     return part + (size_t)(n_kv + 1) * sizeof(unsigned);
 }
 
-extern "C" int gb_attention_decode(const float* q, const float* k, const float* v, float* k_cache, float* v_cache,
-                                   const float* rope_cs, const int* d_pos, int n_heads, int n_kv, int head_dim,
-                                   int max_seq, float* out, void* ws, void* stream) {
+int gb::attention_decode_xq(const float* q, const float* k, const float* v, float* k_cache, float* v_cache,
+                            const float* rope_cs, const int* d_pos, int n_heads, int n_kv, int head_dim,
+                            int max_seq, float* out, void* ws, uint8_t* xq_out, cudaStream_t st) {
     if (!q || !k || !v || !k_cache || !v_cache || !rope_cs || !d_pos || !out || !ws) return GB_EINVAL;
     if (n_kv <= 0 || n_heads <= 0 || n_heads % n_kv || max_seq <= 0) return GB_EINVAL;
+    if (xq_out && (((n_heads * head_dim) % 256) || (reinterpret_cast<uintptr_t>(xq_out) & 15))) return GB_EINVAL;
     const int group = n_heads / n_kv;
     const int G = attn_grid_splits(n_kv, max_seq);
     float* part = static_cast<float*>(ws);
     unsigned* tickets = reinterpret_cast<unsigned*>(part + (size_t)n_kv * G * group * (head_dim + 2));
     return attn_dispatch(q, k, v, k_cache, v_cache, rope_cs, d_pos, n_heads, n_kv, head_dim, max_seq, out, part,
-                         tickets, tickets + n_kv, static_cast<cudaStream_t>(stream));
+                         tickets, tickets + n_kv, st, xq_out);
+}
+
+extern "C" int gb_attention_decode(const float* q, const float* k, const float* v, float* k_cache, float* v_cache,
+                                   const float* rope_cs, const int* d_pos, int n_heads, int n_kv, int head_dim,
+                                   int max_seq, float* out, void* ws, void* stream) {
+    return attention_decode_xq(q, k, v, k_cache, v_cache, rope_cs, d_pos, n_heads, n_kv, head_dim, max_seq, out, ws,
+                               nullptr, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int gb_attention_decode_static(const float* q, const float* k, const float* v, float* k_cache,

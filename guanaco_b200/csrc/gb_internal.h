@@ -11,6 +11,13 @@ namespace gb {
 // the grid has n_kv * grid_splits CTAs; each covers P consecutive positions,
 // P chosen in-kernel from pos so that the active splits fit the grid.
 int attn_grid_splits(int n_kv, int max_seq);
+// gb_attention_decode, and when xq_out != nullptr also the output quantised
+// for a matvec that reads it pre-quantised (MV_X_PREQ): the CTA that finishes
+// a KV head quantises each 32-column group of that head group's output
+// (mt_quantise32 layout, n_heads * head_dim columns, a multiple of 256).
+int attention_decode_xq(const float* q, const float* k, const float* v, float* k_cache, float* v_cache,
+                        const float* rope_cs, const int* d_pos, int n_heads, int n_kv, int head_dim, int max_seq,
+                        float* out, void* ws, uint8_t* xq_out, cudaStream_t st);
 
 // A prepared matvec: kernel choice, launch geometry and, for the TMA path,
 // the encoded tensor map of W.  Built once per weight matrix on the host
@@ -160,6 +167,7 @@ struct LayerArgs {
     // tickets (K / 32, zero); null: ffn_down quantises it itself
     uint8_t* swq = nullptr;
     unsigned* swq_tk = nullptr;
+    uint8_t* aq = nullptr;    // attention output quantised for wo (nullptr: wo quantises it)
 };
 int enqueue_layer(const LayerArgs& a, cudaStream_t st);
 bool tp_fusable(const MvPlan* const* mv, int H);

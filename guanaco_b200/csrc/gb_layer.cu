@@ -393,6 +393,7 @@ struct gb_model {
     float *kc = nullptr, *vc = nullptr, *rope = nullptr;
     float* hidden2 = nullptr;         // tensor parallel: second hidden-state buffer (exchanges ping-pong)
     uint8_t* swq = nullptr;           // SwiGLU product quantised for ffn_down (zeroed)
+    uint8_t* aq = nullptr;            // attention output quantised for wo
     unsigned* swq_tk = nullptr;       // its pair tickets (zero)
     void* attn_ws = nullptr;
     float *hidden = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr;
@@ -487,6 +488,8 @@ extern "C" gb_model* gb_model_create_tp(const gb_model_config* cfg, int rank, in
         ok &= (m->swq = (uint8_t*)dalloc(m, swq_bytes)) != nullptr;
         ok &= (m->swq_tk = (unsigned*)dalloc(m, (size_t)FP / 32 * sizeof(unsigned))) != nullptr;
     }
+    // wo's input quantised by the attention launch (same layout)
+    if (QD % 256 == 0) ok &= (m->aq = (uint8_t*)dalloc(m, (size_t)QD * 5 / 2)) != nullptr;
     ok &= (m->logits = (float*)dalloc(m, (size_t)m->vocab_l * 4)) != nullptr;
     // the host-facing words share one block: gb_model_decode_host sends
     // {token, pos} in one copy and reads {next, error} back in one copy
@@ -834,15 +837,22 @@ int enqueue_layer(const LayerArgs& a, cudaStream_t st) {
         if ((rc = mv(GB_WK, a.xn, a.k, nullptr, nullptr))) return rc;
         if ((rc = mv(GB_WV, a.xn, a.v, nullptr, nullptr))) return rc;
     }
-    if ((rc = gb_attention_decode(a.q, a.k, a.v, a.kc, a.vc, a.rope, a.d_pos, a.n_heads, a.n_kv, a.hd, a.max_seq,
-                                  a.attn, a.attn_ws, st)))
+    // wo's x arrives quantised from the attention launch: the CTA that
+    // finishes a KV head quantises its 32-column groups of the output
+    const bool aq = a.aq && tma(GB_WO) && a.mv[GB_WO]->cols == a.n_heads * a.hd;
+    if ((rc = attention_decode_xq(a.q, a.k, a.v, a.kc, a.vc, a.rope, a.d_pos, a.n_heads, a.n_kv, a.hd, a.max_seq,
+                                  a.attn, a.attn_ws, aq ? a.aq : nullptr, st)))
         return rc;
+    MvXform woq;
+    woq.mode = MV_X_PREQ;
+    woq.xq = a.aq;
+    const MvXform* wxf = aq ? &woq : nullptr;
     if (fx) {   // this rank's columns of wo, pushed to every rank
-        if ((rc = mv(GB_WO, a.attn, a.tp->part, nullptr, nullptr, &twp))) return rc;
+        if ((rc = mv(GB_WO, a.attn, a.tp->part, nullptr, wxf, &twp))) return rc;
     } else if (tp) {   // this rank's columns of wo, then the exchange as its own launch
-        if ((rc = mv(GB_WO, a.attn, a.tp->part, nullptr, nullptr))) return rc;
+        if ((rc = mv(GB_WO, a.attn, a.tp->part, nullptr, wxf))) return rc;
         if ((rc = tp_allreduce(*a.tp, a.tp->h[0], a.tp->h[1], H, c_wo, st))) return rc;
-    } else if ((rc = mv(GB_WO, a.attn, a.hidden, a.hidden, nullptr))) {
+    } else if ((rc = mv(GB_WO, a.attn, a.hidden, a.hidden, wxf))) {
         return rc;
     }
     const MvTp* tgp = fx ? &tg : nullptr;
@@ -972,6 +982,7 @@ static int enqueue_step(gb_model* m, const int* d_token, const int* d_pos, float
         a.tp_fused = fx;
         a.swq = m->swq;
         a.swq_tk = m->swq_tk;
+        a.aq = m->world == 1 ? m->aq : nullptr;   // one GPU only (the tensor-parallel wo keeps its own quantiser)
         a.layer = l;
         for (int i = 0; i < GB_NMAT; i++) a.mv[i] = &m->plan[(size_t)l * GB_NMAT + i];
         a.mv_ws = m->mv_ws;
