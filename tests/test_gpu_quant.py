@@ -351,3 +351,38 @@ def test_matvec_group_matches_single(gb, oracle, cuda, dts, rows, cols):
     for y, y1, ref in zip(ys, singles, refs):
         assert rel_l2(from_dev(y), ref) <= 1e-4
         assert rel_l2(from_dev(y), from_dev(y1)) <= 1e-5
+
+
+def test_matvec_chain_reads_predecessor_output(gb, oracle, cuda):
+    """Public matvec calls launch with programmatic dependent launch, so a
+    call starts fetching weights while the one before it on the stream is
+    still running.  A chain whose every x (and residual) is the previous
+    call's y, issued with no synchronisation in between and repeated with
+    new inputs, must give each product of the values its predecessor wrote."""
+    H, F = 4096, 14336
+    mats = [(4, H, H, 1), (4, H, H, 2), (5, F, H, 3), (5, H, F, 4)]
+    Wh = [oracle.synth_blocks(dt, r, c, 55, s) for dt, r, c, s in mats]
+    Wd = [dev_blocks(cuda, w) for w in Wh]
+    Gh = [oracle.synth_blocks(4, 1024, H, 55, 10 + i) for i in range(2)]
+    Gd = [dev_blocks(cuda, w) for w in Gh]
+    y = [cuda.empty(r, dtype=cuda.float32, device="cuda") for _, r, _, _ in mats]
+    g = [cuda.empty(1024, dtype=cuda.float32, device="cuda") for _ in range(2)]
+    for it in range(3):
+        x_host = oracle.synth_normal(H, 56, it)
+        x = to_dev(cuda, x_host)
+        cuda.cuda.synchronize()
+        gb.matvec(4, Wd[0], H, H, x, y[0])                        # y0 = W0 x
+        gb.matvec(4, Wd[1], H, H, y[0], y[1], residual=y[0])      # y1 = W1 y0 + y0
+        gb.matvec(5, Wd[2], F, H, y[1], y[2])                     # y2 = W2 y1
+        gb.matvec(5, Wd[3], H, F, y[2], y[3], residual=y[1])      # y3 = W3 y2 + y1
+        gb.matvec_group([4, 4], Gd, [1024, 1024], H, y[3], g)     # g = G y3
+        cuda.cuda.synchronize()
+        assert gb.lib().gb_device_error(1) == 0
+        got = [from_dev(t) for t in y] + [from_dev(t) for t in g]
+        # every product against the oracle applied to what the GPU wrote before it
+        assert rel_l2(got[0], oracle.matvec(4, Wh[0], H, H, x_host)[1]) <= REL_L2_TOL
+        assert rel_l2(got[1], oracle.matvec(4, Wh[1], H, H, got[0])[1] + got[0]) <= REL_L2_TOL
+        assert rel_l2(got[2], oracle.matvec(5, Wh[2], F, H, got[1])[1]) <= REL_L2_TOL
+        assert rel_l2(got[3], oracle.matvec(5, Wh[3], H, F, got[2])[1] + got[1]) <= REL_L2_TOL
+        for i in range(2):
+            assert rel_l2(got[4 + i], oracle.matvec(4, Gh[i], 1024, H, got[3])[1]) <= REL_L2_TOL, it
