@@ -722,6 +722,11 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
     }
 
     // ---- consumers
+    // the RMSNorm weight does not depend on the previous kernel: read it
+    // before the wait (the one-pass quantiser keeps it in registers)
+    const bool rms1 = a.xmode == MV_X_RMSNORM && K / 4 <= MT_XU * MT_NC * 32;
+    float4 nwr[MT_XU];
+    if (rms1) mt_load_norm_w<MT_NC>(a, K, threadIdx.x, nwr);
     griddep_wait();
     uint8_t* xq = smem + xq_off;
     // epochs of the tensor-parallel exchanges (the step counter is written
@@ -751,8 +756,8 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
                 if (t < n16) dst[t] = v[j];
             }
         }
-    } else if (a.xmode == MV_X_RMSNORM && K / 4 <= MT_XU * MT_NC * 32) {
-        mt_quantise_x_rms<F::S16, MT_NC>(a, K, xq, threadIdx.x, red, a.tp.in_call >= 0 ? &a.tp : nullptr, ep_in);
+    } else if (rms1) {
+        mt_quantise_x_rms<F::S16, MT_NC>(a, K, xq, threadIdx.x, red, nwr, a.tp.in_call >= 0 ? &a.tp : nullptr, ep_in);
     } else {
         const float rs = a.xmode == MV_X_RMSNORM ? mt_rms_scale<MT_NC>(a.x, K, a.eps, red, threadIdx.x) : 1.f;
         mt_quantise_x<F::S16>(a, K, xq, threadIdx.x, MT_NC * 32, rs);

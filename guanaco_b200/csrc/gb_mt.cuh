@@ -314,21 +314,32 @@ __device__ __forceinline__ bool ll_wait4(const uint2* p, unsigned ep, float4& ou
 // With an exchange ex (ex->in_call >= 0, epoch ep): x is first replaced by
 // x + the sum over ranks of this rank's receive slots, and this CTA writes
 // its slice of that sum to ex->h_out.
-template <bool S16, int NC, class A>
-__device__ __forceinline__ void mt_quantise_x_rms(const A& a, int K, uint8_t* xq, int tid, float* scratch,
-                                                  const MvTp* ex = nullptr, unsigned ep = 0) {
+// The thread's float4s of the RMSNorm weight for mt_quantise_x_rms.  The
+// weight is a model constant, so the consumers load it before
+// griddepcontrol.wait: otherwise its HBM reads queue behind this launch's own
+// weight stream on the critical path after the wait.
+template <int NC, class A>
+__device__ __forceinline__ void mt_load_norm_w(const A& a, int K, int tid, float4 (&w)[MT_XU]) {
     const int n4 = K / 4, nthr = NC * 32;
-    const float4* x4 = reinterpret_cast<const float4*>(a.x);
     const float4* w4 = reinterpret_cast<const float4*>(a.nw);
-    float4 v[MT_XU], w[MT_XU];
 #pragma unroll
     for (int j = 0; j < MT_XU; j++) {
         const int t = tid + j * nthr;
-        v[j] = w[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (t < n4) {
-            v[j] = __ldcg(x4 + t);
-            w[j] = __ldcg(w4 + t);
-        }
+        w[j] = t < n4 ? __ldg(w4 + t) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+}
+
+template <bool S16, int NC, class A>
+__device__ __forceinline__ void mt_quantise_x_rms(const A& a, int K, uint8_t* xq, int tid, float* scratch,
+                                                  const float4 (&w)[MT_XU], const MvTp* ex = nullptr,
+                                                  unsigned ep = 0) {
+    const int n4 = K / 4, nthr = NC * 32;
+    const float4* x4 = reinterpret_cast<const float4*>(a.x);
+    float4 v[MT_XU];
+#pragma unroll
+    for (int j = 0; j < MT_XU; j++) {
+        const int t = tid + j * nthr;
+        v[j] = t < n4 ? __ldcg(x4 + t) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     if (ex) {
         const int world = ex->world;
