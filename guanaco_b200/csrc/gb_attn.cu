@@ -392,16 +392,25 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
     }
     if (single) return;
 
-    // ---- merge in the last CTA of this KV head
+    // ---- merge in the last CTA of this KV head.  One release per CTA
+    // publishes its partials: after the CTA barrier thread 0 fences at GPU
+    // scope and takes a ticket with an acquire-release atomic, so the last
+    // arrival's thread 0 acquires every split's partials, and the barrier
+    // after it orders the whole CTA's reads behind that acquire.
     __shared__ unsigned last;
-    __threadfence();
     __syncwarp();   // bar.sync is warp-aligned: reconverge the warp first
     asm volatile("bar.sync 1, %0;" ::"n"(ATTN_CWARPS * 32) : "memory");
-    if (ctid == 0) last = (atomicAdd(&tickets[kvh], 1u) == (unsigned)(nsplit - 1));
+    if (ctid == 0) {
+        unsigned prev;
+        asm volatile("fence.acq_rel.gpu;\n\tatom.acq_rel.gpu.global.add.u32 %0, [%1], 1;"
+                     : "=r"(prev)
+                     : "l"(tickets + kvh)
+                     : "memory");
+        last = prev == (unsigned)(nsplit - 1);
+    }
     __syncwarp();   // bar.sync is warp-aligned: reconverge the warp first
     asm volatile("bar.sync 1, %0;" ::"n"(ATTN_CWARPS * 32) : "memory");
     if (!last) return;
-    __threadfence();
     // every output is a weighted sum over the splits in split order, in one
     // pass with a running maximum: chunks of MC splits, the next chunk's
     // loads in flight while the current one is summed
