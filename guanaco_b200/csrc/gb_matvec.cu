@@ -848,13 +848,20 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
                             up = val;
                             have = true;
                         } else {   // halves in two CTAs: the second to finish pairs them
-                            __threadfence();
+                            // one release for the warp's y rows (warp barrier, then
+                            // lane 0 fences at GPU scope and takes the pair's
+                            // ticket with an acquire-release atomic); the warp
+                            // barrier after it orders the lanes' reads behind the
+                            // acquire
                             __syncwarp();
                             unsigned k = 0;
-                            if (lane == 0) k = atomicAdd(&a.swq_tk[grp], 1u);
+                            if (lane == 0) {
+                                asm volatile("fence.acq_rel.gpu;" ::: "memory");
+                                k = atom_add_acq_rel(&a.swq_tk[grp], 1u);
+                            }
                             k = __shfl_sync(0xffffffffu, k, 0);
+                            __syncwarp();
                             if (k == 1u) {
-                                __threadfence();
                                 const float oth = row < a.rows[1 - m] ? __ldcg(a.y[1 - m] + row) : 0.f;
                                 gate = m == 0 ? val : oth;
                                 up = m == 0 ? oth : val;
