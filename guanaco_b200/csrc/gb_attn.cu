@@ -20,17 +20,20 @@
 // active splits fill the grid); it serves all GROUP = n_heads / n_kv query
 // heads of that KV head, so each K and V row is read from HBM exactly once.
 // One producer lane streams K and V tiles of 32 positions through a ring of
-// bulk copies (about 200 KB per SM in flight); each of 8 consumer warps owns
-// every 8th tile and runs its own online softmax, with no CTA-wide barrier
-// per tile:
+// bulk copies (about 200 KB per SM in flight), starting before RoPE; the 16
+// consumer warps form TW tile lanes of NHG warps (one per group of HPW query
+// heads): tile t belongs to tile lane t % TW, and each warp runs its own
+// online softmax, with no CTA-wide barrier per tile:
 //   scores:  LPP lanes share one K row (DPL dims each, 128-bit loads), dot
-//            products for all GROUP heads, shuffle-reduced;
+//            products for the warp's HPW heads, shuffle-reduced;
 //   softmax: per head, the tile's max updates the warp's running max m, and
 //            the running sum l and the output are rescaled by exp(m_old - m);
 //   P.V:     each lane accumulates one float4 column of every head;
 //   merge:   the warps' (m, l, o) combine in shared memory, each CTA
-//            publishes its (m, l, o[hd]) per head, and the last CTA of the KV
-//            head (atomic ticket) combines the splits and resets the ticket.
+//            publishes its (m, l, o[hd]) per head with one release (ticket),
+//            and the last CTA of the KV head combines the splits in split
+//            order, resets the ticket and, when asked, also writes the output
+//            quantised for the next matvec.
 // pos comes from device memory so the launch can live inside a CUDA graph;
 // a pos outside [0, max_seq) sets the error word and touches nothing.
 #include "gb_common.cuh"
