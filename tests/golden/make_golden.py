@@ -9,7 +9,7 @@ abi_layout.json -- sizeof / offsetof of the reference's Tensor,
                BackendConfig, KernelVTable and struct Backend, compiled from
                the reference headers.
 
-Usage: python tests/golden/make_golden.py [--ref /root/reference]
+Usage: python tests/golden/make_golden.py [--ref <reference checkout>]
 """
 from __future__ import annotations
 
