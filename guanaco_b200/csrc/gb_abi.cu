@@ -316,10 +316,20 @@ extern "C" int cuda_matvec_q4k_f32_impl(const void* W_data, const float* x, floa
 extern "C" __attribute__((visibility("hidden"))) int gb_vtable_matvec(int dtype, const void* host_data, const void* d_data, int resident,
                                 size_t byte_size, int rows, int cols, const float* x, float* y) {
     if (!x || !y || (!host_data && !(resident && d_data))) return GB_EINVAL;
-    int rc = check_dtype_shape(dtype, rows, cols);
-    if (rc) return rc;
+    // the reference kernels' order (quant_matvec_q4_k.c:150-158): columns not a
+    // multiple of the block width, then the byte size when it is known.  An
+    // empty matrix is no error there: no rows, nothing to do; no columns,
+    // every row's sum is 0.  Negative shapes are rejected here (the reference
+    // does not check them).
+    if (dtype != GB_DT_Q4_K && dtype != GB_DT_Q6_K && dtype != GB_DT_Q8_0) return GB_EINVAL;
+    if (rows < 0 || cols < 0) return GB_EINVAL;
+    if (cols % gb_block_width(dtype)) return GB_ESHAPE;
     const size_t need = gb_matrix_bytes(dtype, rows, cols);
     if (byte_size != 0 && need > byte_size) return GB_ESIZE;
+    if (rows == 0 || cols == 0) {
+        if (rows > 0) memset(y, 0, (size_t)rows * sizeof(float));
+        return GB_OK;
+    }
     std::lock_guard<std::mutex> lk(g_mu);
     Ctx* c = ctx();
     if (!c) return GB_ECUDA;
