@@ -1,7 +1,7 @@
 """ctypes bindings for the CPU checkers -- TEST INFRASTRUCTURE ONLY.
 
-Only tests/, __graft_entry__.smoke() and bench.py's CPU legs import this
-module.  It loads
+Only tests/, __graft_entry__.smoke(), bench.py's CPU legs and the GPU
+comparison script beside it (ref_cuda_compare.py) import this module.  It loads
 
 * ``oracle/liboracle.so`` -- the plain-C restatement of the reference hot path
   (gb_oracle.c), and
