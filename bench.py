@@ -179,6 +179,8 @@ def kernel_benchmarks(gb, torch, dm, peak):
     matvec_case("q4k_matvec_4096x4096 (config 0)", 4, 4096, 4096, 40, 400)
     matvec_case("q6k_matvec_4096x14336 (config 1)", 5, 4096, 14336, 10, 200)
     matvec_case("q6k_matvec_128256x4096 (config 1, output head)", 5, 128256, 4096, 2, 40)
+    matvec_case("q8_0_matvec_14336x4096", 2, 14336, 4096, 8, 200)
+    matvec_case("q6k_matvec_2048x5632 (config 3 ffn_down)", 5, 2048, 5632, 24, 400)
 
     # config 2: RoPE + append + GQA attention over 8193 positions (fp32 KV)
     nh, nkv, hd, ms, pos = 32, 8, 128, 8448, 8192
@@ -209,6 +211,71 @@ def kernel_benchmarks(gb, torch, dm, peak):
     del kcs, vcs
     torch.cuda.empty_cache()
     return res, main
+
+
+TINYLLAMA = dict(hidden_dim=2048, n_heads=32, n_kv_heads=4, n_layers=22, ff_dim=5632, vocab_size=32000)
+
+
+def tinyllama_decode(gb, torch, prompt_len=128, steps=256):
+    """TinyLlama-1.1B architecture, random-init Q4_K_M-style
+    weights, a 128-token prompt fed through the decode path, then 256 greedy
+    steps (device-timed, CUDA events on the launching stream)."""
+    import numpy as np
+    c = TINYLLAMA
+    dm = gb.DecodeModel(c["hidden_dim"], c["n_heads"], c["n_kv_heads"], c["n_layers"], c["ff_dim"],
+                        c["vocab_size"], prompt_len + steps + 8)
+    try:
+        dm.synthesize(SEED)
+        prompt = np.random.RandomState(SEED).randint(0, c["vocab_size"], prompt_len)
+        t0 = time.perf_counter()
+        nxt = 0
+        for pos, tok in enumerate(prompt):
+            nxt = dm.decode_host(int(tok), pos)
+        t_prompt = time.perf_counter() - t0
+        st = torch.cuda.Stream()
+        d_tok = torch.tensor([nxt], dtype=torch.int32, device="cuda")
+        d_pos = torch.tensor([prompt_len], dtype=torch.int32, device="cuda")
+        toks = torch.zeros(steps + 1, dtype=torch.int32, device="cuda")
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dm.generate(d_tok, d_pos, 3, toks, stream=st.cuda_stream)   # warm-up (graph capture)
+        st.synchronize()
+        d_tok.fill_(nxt)
+        d_pos.fill_(prompt_len)
+        st.synchronize()
+        e0.record(st)
+        dm.generate(d_tok, d_pos, steps, toks, stream=st.cuda_stream)
+        e1.record(st)
+        e1.synchronize()
+        if dm.error() != 0:
+            raise RuntimeError(f"decode error {dm.error()}")
+        ms = e0.elapsed_time(e1)
+        return {"workload": "tinyllama-1.1b-q4km (BASELINE config 3): 128-token prompt, 256 greedy steps",
+                "tokens_per_s": round(steps / (ms / 1e3), 1), "ms_per_token": round(ms / steps, 4),
+                "prompt_tokens_per_s_host_calls": round(prompt_len / t_prompt, 1),
+                "launches_per_step": dm.launches_per_step()}
+    finally:
+        dm.close()
+
+
+def one_gpu_tokens(gb, torch, max_seq, W, K):
+    """Greedy tokens of the timed steps from a one-GPU model of the same
+    seeded weights and KV fill (the tensor-parallel run must reproduce them)."""
+    c = LLAMA8B
+    dm = gb.DecodeModel(c["hidden_dim"], c["n_heads"], c["n_kv_heads"], c["n_layers"], c["ff_dim"],
+                        c["vocab_size"], max_seq)
+    try:
+        dm.synthesize(SEED)
+        dm.fill_kv(CTX, SEED)
+        st = torch.cuda.Stream()
+        d_tok = torch.tensor([1], dtype=torch.int32, device="cuda")
+        d_pos = torch.tensor([CTX], dtype=torch.int32, device="cuda")
+        toks = torch.zeros(max(W, K) + 1, dtype=torch.int32, device="cuda")
+        dm.generate(d_tok, d_pos, W, toks, stream=st.cuda_stream)
+        dm.generate(d_tok, d_pos, K, toks, stream=st.cuda_stream)
+        st.synchronize()
+        return toks[:K].cpu().tolist()
+    finally:
+        dm.close()
 
 
 def cpu_reference_token_time(threads: int, n_layers_sample: int = 1, reps: int = 2):
@@ -315,6 +382,7 @@ def run_ours(args, rank, world, local_rank):
         t_ms = float(tt.item())
     if dm.error() != 0:
         raise RuntimeError(f"decode error {dm.error()}")
+    timed_tokens = toks[:K].cpu().tolist()
     if args.decode_only:   # profiling runs: the timed decode steps only
         if dist:
             dist.barrier()
@@ -359,6 +427,14 @@ def run_ours(args, rank, world, local_rank):
     if dist:
         dist.barrier()   # every rank is done with the peers' exchange buffers
     dm.close()
+    tokens_check = None
+    tiny = None
+    if rank == 0 and world > 1:   # the tensor-parallel tokens against a one-GPU model
+        ref_toks = one_gpu_tokens(gb, torch, max_seq, W, K)
+        tokens_check = {"tokens_match": ref_toks == timed_tokens, "steps_compared": K,
+                        "against": "one-GPU model of the same seeded weights and KV fill"}
+    if rank == 0 and world == 1 and not args.no_extra:
+        tiny = tinyllama_decode(gb, torch)
 
     line = None
     if rank == 0:
@@ -376,7 +452,10 @@ def run_ours(args, rank, world, local_rank):
             "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world, "steps": K,
             "warmup": W, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
             "scaling": "strong" if world > 1 else "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init weights, ~N(0,1) KV fill)",
+            "vs_baseline": None,
+            "dtype": "f32 (weights Q4_K/Q6_K codes; matvec x as two int8 limbs per 32-column sub-block, "
+                     "~16 significant bits; fp32 scales, accumulation, KV cache and attention)",
+            "data": "synthetic (seeded random-init weights, ~N(0,1) KV fill)",
             "config": {"workload": "llama3.1-8b-q4km-decode (BASELINE config 4)", "global_batch": 1,
                        "seq_len": CTX, "parallelism": f"tp{world}" if world > 1 else "single",
                        "weights": "Q4_K + Q6_K(attn_v, ffn_down, output)", "kv": "fp32 head-major",
@@ -392,6 +471,8 @@ def run_ours(args, rank, world, local_rank):
                          "peak": peak, "unit": "GB/s", "frac": round(gbs / peak, 3), "traffic": ncu_traffic(),
                          "alg_bytes_per_launch": alg, "peak_kind": peak_kind},
             "kernels": kernels,
+            "tokens": tokens_check,
+            "config3": tiny,
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
         }
@@ -498,6 +579,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the config-3 (TinyLlama) line")
     ap.add_argument("--decode-only", action="store_true",
                     help="run the warm-up and timed decode steps only (for ncu launch lists) and exit")
     ap.add_argument("--steps-ref", type=int, default=None, help="reference arm samples (default min(steps, 5))")

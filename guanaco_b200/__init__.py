@@ -118,8 +118,6 @@ SIGNATURES = {
     "gb_model_destroy": (None, [_vp]),
     "gb_model_set_matrix": (_i, [_vp, _i, _i, _i, _vp]),
     "gb_model_set_norms": (_i, [_vp, _i, _vp, _vp]),
-    "gb_model_use_persistent": (_i, [_vp, _i]),
-    "gb_model_persistent": (_i, [_vp]),
     "gb_model_set_head": (_i, [_vp, _i, _vp, _vp, _i, _vp]),
     "gb_model_synthesize": (_i, [_vp, _u64]),
     "gb_model_k_cache": (_vp, [_vp, _i]),
@@ -321,14 +319,6 @@ class DecodeModel:
 
     def error(self) -> int:
         return lib().gb_model_error(self.h)
-
-    def use_persistent(self, on: bool) -> None:
-        """Persistent layer-boundary launches (True) or one launch per matrix group."""
-        check("gb_model_use_persistent", lib().gb_model_use_persistent(self.h, 1 if on else 0))
-
-    def persistent(self) -> bool:
-        """The last decode ran the persistent layer-boundary schedule."""
-        return bool(lib().gb_model_persistent(self.h))
 
     def launches_per_step(self) -> int:
         return lib().gb_model_launches_per_step(self.h)

@@ -52,7 +52,7 @@ constexpr int ATTN_SMEM_MAX = 227 * 1024;
 // its whole share of K/V requested nearly at once), at least one 32-position
 // tile per split.
 int attn_grid_splits(int n_kv, int max_seq) {
-    int s = GB_NUM_SMS / n_kv;
+    int s = sm_count() / n_kv;
     if (s < 1) s = 1;
     const int tiles = (max_seq + 31) / 32;
     return s < tiles ? s : tiles;
@@ -81,7 +81,7 @@ struct AttnCfg {
     static constexpr size_t BAR_OFF = RING_OFF + (size_t)R * TILE * sizeof(float);
     static constexpr size_t SMEM = BAR_OFF + 2 * R * sizeof(unsigned long long);
     // the warps' (m, l, o) merge reuses the ring
-    static_assert(TW * GROUP * (HD + 4) + GROUP * GB_NUM_SMS <= R * TILE, "merge buffers");
+    static_assert(TW * GROUP * (HD + 4) <= R * TILE, "merge buffers");
 };
 
 // ---- bulk-copy ring primitives (shared-memory addresses)
@@ -472,15 +472,8 @@ static cudaError_t launch_attn(const float* q, const float* k, const float* v, f
                                const float* cs, const int* d_pos, int n_kv, int max_seq, float* out,
                                float* part, unsigned* tickets, unsigned* err, uint8_t* xq_out, cudaStream_t st) {
     using C = AttnCfg<HD, GROUP>;
-    static unsigned configured = 0;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!(configured & (1u << (dev & 31)))) {
-        cudaError_t e = cudaFuncSetAttribute(k_attn_decode<HD, GROUP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)C::SMEM);
-        if (e != cudaSuccess) return e;
-        configured |= 1u << (dev & 31);
-    }
+    cudaError_t e = set_smem_once(reinterpret_cast<const void*>(k_attn_decode<HD, GROUP>), (int)C::SMEM);
+    if (e != cudaSuccess) return e;
     const int G = attn_grid_splits(n_kv, max_seq);
     k_attn_decode<HD, GROUP><<<n_kv * G, ATTN_THREADS, C::SMEM, st>>>(q, k, v, kc, vc, cs, d_pos, n_kv, max_seq, G,
                                                                       out, part, tickets, err, xq_out);

@@ -30,7 +30,9 @@
 #define GB_ETIMEOUT -7    // a bounded device-side wait ran out
 #define GB_ELIMIT -8      // size above a documented maximum
 
-#define GB_NUM_SMS 148
+// Upper bound on the SM count of a device (B200: 148); buffers sized per SM
+// use it, grids use the device's own count (gb::sm_count()).
+#define GB_MAX_SMS 192
 
 #define GB_CUDA_TRY(expr)                                   \
     do {                                                    \

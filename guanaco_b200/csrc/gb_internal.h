@@ -7,6 +7,12 @@
 
 namespace gb {
 
+// SM count of the current device (queried once per device).
+int sm_count();
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize, bytes) once per
+// (kernel, device); thread-safe.
+cudaError_t set_smem_once(const void* func, int bytes);
+
 // Attention split geometry shared by the launcher and the workspace sizing:
 // the grid has n_kv * grid_splits CTAs; each covers P consecutive positions,
 // P chosen in-kernel from pos so that the active splits fit the grid.
@@ -91,32 +97,6 @@ int mv_launch_group(const MvPlan* const* ps, int n, const float* x, float* const
 // Tensor map of a Q4_K / Q6_K weight view (gb_matvec.cu).
 bool mt_encode_view(void* map128, int dtype, const void* W, int rows, int nb, int boxz);
 bool mt_encode_rows(void* map128, const void* W, int rows, int nb, int box_u64);
-
-// Persistent multi-phase matvec (gb_chain.cu): one cooperative launch runs
-// several matvec phases in order, phase p + 1 reading what phase p wrote, with
-// the weight stream of every phase prefetched across the phase boundaries.
-constexpr int CH_MAXP = 6;   // phases per launch
-constexpr int CH_MAXM = 3;   // matrices per phase (one x, one column count)
-struct ChMatSpec {
-    int dtype = 0;
-    const void* W = nullptr;
-    int rows = 0, cols = 0;
-    float* y = nullptr;
-    const float* residual = nullptr;   // y = W x + residual (may alias y)
-};
-struct ChPhaseSpec {
-    ChMatSpec m[CH_MAXM];
-    int nm = 0;
-    const float* x = nullptr;
-    MvXform xf;
-};
-struct ChainSet;
-// Q4_K any width; Q6_K rows of a multiple of 8 blocks (16-byte row pitch).
-bool chain_compatible(int dtype, int cols);
-// Launch i runs phases [first[i], first[i + 1]).
-int chain_create(const ChPhaseSpec* phases, const int* first, int nlaunch, ChainSet** out);
-int chain_launch(const ChainSet* cs, int i, unsigned* err, cudaStream_t st);
-void chain_destroy(ChainSet* cs);
 
 // Tensor-parallel context of a layer (world > 1): the wo and ffn_down
 // matvecs write this rank's partial to `part`, then an all-reduce over peer

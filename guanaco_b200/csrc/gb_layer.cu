@@ -19,9 +19,42 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <atomic>
+#include <mutex>
+#include <set>
+#include <utility>
 #include <vector>
 
 namespace gb {
+
+static std::mutex g_dev_mu;
+
+int sm_count() {
+    static std::atomic<int> counts[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return 1;
+    if (dev < 64) {
+        const int c = counts[dev].load(std::memory_order_relaxed);
+        if (c > 0) return c;
+    }
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 1;
+    if (n > GB_MAX_SMS) n = GB_MAX_SMS;
+    if (dev < 64) counts[dev].store(n, std::memory_order_relaxed);
+    return n;
+}
+
+cudaError_t set_smem_once(const void* func, int bytes) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    static std::set<std::pair<const void*, int>> done;
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    if (done.count({func, dev})) return cudaSuccess;
+    e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) done.insert({func, dev});
+    return e;
+}
 
 // ---------------------------------------------------------------- glue kernels
 __device__ __forceinline__ float block_sum_1024(float v, float* sh) {
@@ -66,7 +99,7 @@ __global__ void k_silu_mul(float* __restrict__ g, const float* __restrict__ u, i
 // the last CTA to finish (ticket) merges the chunks in index order, so the
 // first maximum wins as in sample_greedy (tokenizer.c:175-185).
 struct ArgPart { float v; int i; };
-constexpr int AM_MAX_CTAS = GB_NUM_SMS;
+constexpr int AM_MAX_CTAS = 148;   // split-argmax CTAs at most (its workspace size)
 constexpr size_t AM_WS_BYTES = AM_MAX_CTAS * sizeof(ArgPart) + 16;
 __global__ void __launch_bounds__(1024) k_argmax_split(const float* __restrict__ x, int n, int* __restrict__ out,
                                                        ArgPart* __restrict__ part, unsigned* __restrict__ ticket,
@@ -410,14 +443,6 @@ struct gb_model {
     const void* gen_key[4] = {nullptr, nullptr, nullptr, nullptr};
     int* d_count = nullptr;
     void* am_ws = nullptr;            // argmax partials + ticket (zeroed)
-    // persistent layer-boundary launches (world == 1, every matrix on the
-    // TMA path): launch 0 = q/k/v of layer 0, launch l = wo, gate/up, down of
-    // layer l - 1 and q/k/v of layer l, launch L = the last layer's wo,
-    // gate/up, down and the output head
-    ChainSet* chain = nullptr;
-    std::vector<int> chain_seg;       // segment s (before attention s) = launches [seg[s], seg[s + 1])
-    bool chain_built = false;         // tried since the last weight change
-    int chain_mode = -1;              // 1 / 0: gb_model_use_persistent; -1: GB_CHAIN
 };
 
 static void* dalloc(gb_model* m, size_t bytes) {
@@ -589,7 +614,6 @@ extern "C" int gb_model_tp_info(const gb_model* m, int* rank, int* world, int* v
 
 extern "C" void gb_model_destroy(gb_model* m) {
     if (!m) return;
-    if (m->chain) chain_destroy(m->chain);
     if (m->exec) cudaGraphExecDestroy(m->exec);
     if (m->gen_exec) cudaGraphExecDestroy(m->gen_exec);
     if (m->stream) cudaStreamSynchronize(m->stream);
@@ -605,16 +629,6 @@ extern "C" void gb_model_destroy(gb_model* m) {
 static void invalidate_graph(gb_model* m) {
     if (m->exec) { cudaGraphExecDestroy(m->exec); m->exec = nullptr; }
     if (m->gen_exec) { cudaGraphExecDestroy(m->gen_exec); m->gen_exec = nullptr; }
-}
-// Weights, norms or the head changed: the persistent launches are rebuilt.
-static void drop_chain(gb_model* m) {
-    if (m->chain) {
-        if (m->stream) cudaStreamSynchronize(m->stream);
-        chain_destroy(m->chain);
-    }
-    m->chain = nullptr;
-    m->chain_seg.clear();
-    m->chain_built = false;
 }
 
 static void mat_shape(const gb_model* m, int which, int dtype, int* rows, int* cols);
@@ -632,15 +646,6 @@ extern "C" int gb_model_set_matrix(gb_model* m, int layer, int which, int dtype,
     m->dt[(size_t)layer * GB_NMAT + which] = dtype;
     m->plan[(size_t)layer * GB_NMAT + which] = p;
     invalidate_graph(m);
-    drop_chain(m);
-    return GB_OK;
-}
-extern "C" int gb_model_persistent(const gb_model* m) { return m && m->chain ? 1 : 0; }
-extern "C" int gb_model_use_persistent(gb_model* m, int on) {
-    if (!m) return GB_EINVAL;
-    m->chain_mode = on ? 1 : 0;
-    invalidate_graph(m);
-    drop_chain(m);
     return GB_OK;
 }
 extern "C" int gb_model_set_norms(gb_model* m, int layer, const float* a, const float* f) {
@@ -648,7 +653,6 @@ extern "C" int gb_model_set_norms(gb_model* m, int layer, const float* a, const 
     m->ra[layer] = a;
     m->rf[layer] = f;
     invalidate_graph(m);
-    drop_chain(m);
     return GB_OK;
 }
 extern "C" int gb_model_set_head(gb_model* m, int emb_dtype, const void* emb, const float* rms_final, int lm_dtype,
@@ -661,7 +665,6 @@ extern "C" int gb_model_set_head(gb_model* m, int emb_dtype, const void* emb, co
     m->emb = emb; m->emb_dt = emb_dtype; m->rms_final = rms_final; m->lm = lm; m->lm_dt = lm_dtype;
     m->lm_plan = p;
     invalidate_graph(m);
-    drop_chain(m);
     return GB_OK;
 }
 
@@ -955,26 +958,6 @@ static int enqueue_step(gb_model* m, const int* d_token, const int* d_pos, float
     const int H = c.hidden_dim;
     int rc;
     if ((rc = embed(m->emb, m->emb_dt, d_token, c.vocab_size, H, m->hidden, m->err, st, m->d_step))) return rc;
-    if (m->chain) {   // persistent launches between the attention kernels
-        auto segment = [&](int sgi) {
-            for (int i = m->chain_seg[sgi]; i < m->chain_seg[sgi + 1]; i++) {
-                const int r = chain_launch(m->chain, i, m->err, st);
-                if (r) return r;
-            }
-            return (int)GB_OK;
-        };
-        if ((rc = segment(0))) return rc;
-        for (int l = 0; l < c.n_layers; l++) {
-            if ((rc = gb_attention_decode(m->q, m->k, m->v, gb_model_k_cache(m, l), gb_model_v_cache(m, l), m->rope,
-                                          d_pos, m->nh, m->nkv, c.head_dim, c.max_seq, m->attn, m->attn_ws, st)))
-                return rc;
-            if ((rc = segment(l + 1))) return rc;
-        }
-        if (d_logits && d_logits != m->logits)
-            GB_CUDA_TRY(cudaMemcpyAsync(d_logits, m->logits, (size_t)m->vocab_l * sizeof(float),
-                                        cudaMemcpyDeviceToDevice, st));
-        return enqueue_argmax(m, m->logits, d_next, st);
-    }
     const bool fx = m->world > 1 && tp_fused(m);
     for (int l = 0; l < c.n_layers; l++) {
         LayerArgs a;
@@ -1035,126 +1018,6 @@ static int enqueue_argmax(gb_model* m, const float* lg, int* d_next, cudaStream_
 }
 
 // All weights set, and the shared matvec workspace sized for every plan.
-// GB_CHAIN=1 in the environment selects the persistent layer-boundary
-// launches (every matrix on the TMA path, one GPU); the default is one launch
-// per matrix (or matrix group), which measures at least as fast today.
-static bool chain_enabled() {
-    static const bool v = [] {
-        const char* e = getenv("GB_CHAIN");
-        return e && e[0] == '1';
-    }();
-    return v;
-}
-
-// Phases per persistent launch (GB_CHAIN_PHASES, 1 .. CH_MAXP; default 4,
-// one launch per layer boundary).
-static int chain_max_phases() {
-    static const int v = [] {
-        const char* e = getenv("GB_CHAIN_PHASES");
-        const int n = e ? atoi(e) : 4;
-        return n < 1 ? 1 : (n > CH_MAXP ? CH_MAXP : n);
-    }();
-    return v;
-}
-
-static void build_chain(gb_model* m) {
-    const gb_model_config& c = m->c;
-    const int L = c.n_layers;
-    const bool want = m->chain_mode >= 0 ? m->chain_mode == 1 : chain_enabled();
-    if (!want || m->world != 1 || L <= 0) return;
-    auto spec = [&](int l, int which, float* y, const float* res) {
-        ChMatSpec s;
-        s.dtype = m->dt[(size_t)l * GB_NMAT + which];
-        s.W = m->w[(size_t)l * GB_NMAT + which];
-        mat_shape(m, which, s.dtype, &s.rows, &s.cols);
-        s.y = y;
-        s.residual = res;
-        return s;
-    };
-    for (int l = 0; l < L; l++)
-        for (int i = 0; i < GB_NMAT; i++) {
-            const ChMatSpec s = spec(l, i, m->hidden, nullptr);
-            if (!chain_compatible(s.dtype, s.cols)) return;
-        }
-    if (!chain_compatible(m->lm_dt, c.hidden_dim)) return;
-    std::vector<ChPhaseSpec> ph;
-    std::vector<int> first;
-    auto qkv = [&](int l) {
-        ChPhaseSpec p;
-        p.m[0] = spec(l, GB_WQ, m->q, nullptr);
-        p.m[1] = spec(l, GB_WK, m->k, nullptr);
-        p.m[2] = spec(l, GB_WV, m->v, nullptr);
-        p.nm = 3;
-        p.x = m->hidden;
-        p.xf.mode = MV_X_RMSNORM;
-        p.xf.w = m->ra[l];
-        p.xf.eps = c.rms_eps;
-        ph.push_back(p);
-    };
-    auto tail = [&](int l) {   // wo, gate / up, down of layer l
-        ChPhaseSpec wo;
-        wo.m[0] = spec(l, GB_WO, m->hidden, m->hidden);
-        wo.nm = 1;
-        wo.x = m->attn;
-        ph.push_back(wo);
-        ChPhaseSpec gu;
-        gu.m[0] = spec(l, GB_WGATE, m->gate, nullptr);
-        gu.m[1] = spec(l, GB_WUP, m->up, nullptr);
-        gu.nm = 2;
-        gu.x = m->hidden;
-        gu.xf.mode = MV_X_RMSNORM;
-        gu.xf.w = m->rf[l];
-        gu.xf.eps = c.rms_eps;
-        ph.push_back(gu);
-        ChPhaseSpec dn;
-        dn.m[0] = spec(l, GB_WDOWN, m->hidden, m->hidden);
-        dn.nm = 1;
-        dn.x = m->gate;
-        dn.xf.mode = MV_X_SILU_MUL;
-        dn.xf.x2 = m->up;
-        ph.push_back(dn);
-    };
-    // segment s holds the phases between attention s - 1 and attention s; a
-    // segment is cut into launches of at most maxp phases
-    const int maxp = chain_max_phases();
-    std::vector<int> seg;
-    auto close_segment = [&](size_t p0) {
-        seg.push_back((int)first.size());
-        for (size_t p = p0; p < ph.size(); p += maxp) first.push_back((int)p);
-    };
-    size_t p0 = ph.size();
-    qkv(0);
-    close_segment(p0);
-    for (int l = 1; l < L; l++) {
-        p0 = ph.size();
-        tail(l - 1);
-        qkv(l);
-        close_segment(p0);
-    }
-    p0 = ph.size();
-    tail(L - 1);
-    ChPhaseSpec lm;
-    lm.m[0].dtype = m->lm_dt;
-    lm.m[0].W = m->lm;
-    lm.m[0].rows = m->vocab_l;
-    lm.m[0].cols = c.hidden_dim;
-    lm.m[0].y = m->logits;
-    lm.nm = 1;
-    lm.x = m->hidden;
-    lm.xf.mode = MV_X_RMSNORM;
-    lm.xf.w = m->rms_final;
-    lm.xf.eps = c.rms_eps;
-    ph.push_back(lm);
-    close_segment(p0);
-    seg.push_back((int)first.size());
-    first.push_back((int)ph.size());
-    ChainSet* cs = nullptr;
-    if (chain_create(ph.data(), first.data(), (int)first.size() - 1, &cs) == GB_OK) {
-        m->chain = cs;
-        m->chain_seg = seg;
-    }
-}
-
 static bool model_ready(gb_model* m) {
     if (m->world > 1 && !m->comm_ready) return false;   // gb_model_comm_open first
     for (size_t i = 0; i < m->w.size(); i++) if (!m->w[i]) return false;
@@ -1174,10 +1037,6 @@ static bool model_ready(gb_model* m) {
         m->mv_ws = p;
         m->mv_ws_size = need;
         invalidate_graph(m);
-    }
-    if (!m->chain_built) {
-        m->chain_built = true;
-        build_chain(m);   // on failure the per-matrix launches run instead
     }
     return true;
 }
@@ -1279,8 +1138,6 @@ extern "C" int gb_model_launches_per_step(const gb_model* m) {
     // kernels that are not fused into a TMA matvec) + output head (+ final
     // norm when not fused) + argmax
     if (!m) return 0;
-    if (m->chain)   // embed, persistent launches, attention per layer, argmax
-        return 1 + m->chain_seg.back() + m->c.n_layers + 1;
     int n = 1;
     for (int l = 0; l < m->c.n_layers; l++) {
         auto P = [&](int w) { return &m->plan[(size_t)l * GB_NMAT + w]; };

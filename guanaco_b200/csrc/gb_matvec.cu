@@ -963,16 +963,12 @@ static bool choose_geom(int dtype, int rows, int nb, MvGeom* g) {
 
 template <typename K>
 static cudaError_t launch_kernel(K kernel, const void* W, int rows, int nb, const float* x, float* y,
-                                 const float* residual, const MvGeom& g, cudaStream_t st, unsigned* configured) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!(*configured & (1u << (dev & 31)))) {
-        cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, MV_SMEM_MAX);
-        if (e != cudaSuccess) return e;
-        *configured |= 1u << (dev & 31);
-    }
+                                 const float* residual, const MvGeom& g, cudaStream_t st) {
+    cudaError_t e = set_smem_once(reinterpret_cast<const void*>(kernel), MV_SMEM_MAX);
+    if (e != cudaSuccess) return e;
     const size_t smem = (size_t)g.bar_off + 2 * g.S * sizeof(uint64_t) + (g.S + 3) * sizeof(int);
-    const int grid = g.ngroups < GB_NUM_SMS ? g.ngroups : GB_NUM_SMS;
+    const int nsm = sm_count();
+    const int grid = g.ngroups < nsm ? g.ngroups : nsm;
     kernel<<<grid, MV_THREADS, smem, st>>>(static_cast<const uint8_t*>(W), rows, nb, x, y, residual, g);
     return cudaGetLastError();
 }
@@ -1067,7 +1063,7 @@ static bool mt_encode(MvPlan* p, const void* W, int rows, int nb) {
     p->nch = (nb + F::IG - 1) / F::IG;   // split items per 32-row group
     p->ngroups = (rows + MT_GR - 1) / MT_GR;
     p->T = p->ngroups * p->nch;
-    p->ncta = p->T < GB_NUM_SMS ? p->T : GB_NUM_SMS;
+    p->ncta = std::min(p->T, sm_count());
     return true;
 }
 
@@ -1097,7 +1093,7 @@ int mv_plan(MvPlan* p, int dtype, const void* W, int rows, int cols) {
 
 size_t mv_ws_bytes(const MvPlan& p) {
     if (p.kind != MV_TMA) return 0;
-    return (size_t)GB_NUM_SMS * 2 * MT_GR * sizeof(float) + ((size_t)p.ngroups * sizeof(unsigned) + 255) / 256 * 256;
+    return (size_t)GB_MAX_SMS * 2 * MT_GR * sizeof(float) + ((size_t)p.ngroups * sizeof(unsigned) + 255) / 256 * 256;
 }
 
 // Matvec launches carry the programmatic-dependent-launch attribute: after a
@@ -1144,12 +1140,11 @@ int mv_launch(const MvPlan& p, const float* x, float* y, const float* residual, 
     if (rc) return rc;
     MvGeom g;
     if (!choose_geom(p.dtype, p.rows, p.nb, &g)) return GB_ELIMIT;
-    static unsigned conf[3] = {0, 0, 0};
     cudaError_t e;
     switch (p.dtype) {
-        case GB_DT_Q4_K: e = launch_kernel(k_mv_q4k, p.W, p.rows, p.nb, x, y, residual, g, st, &conf[0]); break;
-        case GB_DT_Q6_K: e = launch_kernel(k_mv_q6k, p.W, p.rows, p.nb, x, y, residual, g, st, &conf[1]); break;
-        default: e = launch_kernel(k_mv_q8_0, p.W, p.rows, p.nb, x, y, residual, g, st, &conf[2]); break;
+        case GB_DT_Q4_K: e = launch_kernel(k_mv_q4k, p.W, p.rows, p.nb, x, y, residual, g, st); break;
+        case GB_DT_Q6_K: e = launch_kernel(k_mv_q6k, p.W, p.rows, p.nb, x, y, residual, g, st); break;
+        default: e = launch_kernel(k_mv_q8_0, p.W, p.rows, p.nb, x, y, residual, g, st); break;
     }
     return e == cudaSuccess ? GB_OK : GB_ECUDA;
 }
@@ -1158,7 +1153,7 @@ size_t mv_ws_bytes_group(const MvPlan* const* ps, int n) {
     if (!mv_groupable(ps, n)) return 0;
     size_t groups = 0;
     for (int i = 0; i < n; i++) groups += (size_t)ps[i]->ngroups;
-    return (size_t)GB_NUM_SMS * 2 * MT_GR * sizeof(float) + (groups * sizeof(unsigned) + 255) / 256 * 256;
+    return (size_t)GB_MAX_SMS * 2 * MT_GR * sizeof(float) + (groups * sizeof(unsigned) + 255) / 256 * 256;
 }
 
 // Ring depth of a mixed-format launch with K columns (0 if none fits).
@@ -1170,18 +1165,7 @@ static int mix_stages(int K) {
 
 template <class F>
 static cudaError_t mvt_configure() {
-    static unsigned configured = 0;
-    static std::mutex mu;
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    std::lock_guard<std::mutex> lk(mu);
-    if (!(configured & (1u << (dev & 31)))) {
-        e = cudaFuncSetAttribute(k_mvt<F>, cudaFuncAttributeMaxDynamicSharedMemorySize, MV_SMEM_MAX);
-        if (e != cudaSuccess) return e;
-        configured |= 1u << (dev & 31);
-    }
-    return cudaSuccess;
+    return set_smem_once(reinterpret_cast<const void*>(k_mvt<F>), MV_SMEM_MAX);
 }
 
 int mv_launch_group(const MvPlan* const* ps, int n, const float* x, float* const* ys, const float* const* res,
@@ -1244,7 +1228,7 @@ int mv_launch_group(const MvPlan* const* ps, int n, const float* x, float* const
     }
     const int groups = a.gbase[MT_MAXM];
     a.part = static_cast<float*>(ws);
-    a.tickets = ws ? reinterpret_cast<unsigned*>(static_cast<char*>(ws) + (size_t)GB_NUM_SMS * 2 * MT_GR * sizeof(float))
+    a.tickets = ws ? reinterpret_cast<unsigned*>(static_cast<char*>(ws) + (size_t)GB_MAX_SMS * 2 * MT_GR * sizeof(float))
                    : nullptr;
     a.nb = p.nb;
     a.T = a.ibase[MT_MAXM];
@@ -1269,12 +1253,13 @@ int mv_launch_group(const MvPlan* const* ps, int n, const float* x, float* const
     // also when they give no CTA more than one item above what stream-K
     // would (e.g. 128 groups of 7 items on 148 SMs): no group is then split,
     // so no CTA ends with the cross-CTA fix-up, which costs more than an item.
+    const int nsm = sm_count();
     bool whole = !ws;
     if (ws && !mixed && p.nch > 1)
-        whole = (groups + GB_NUM_SMS - 1) / GB_NUM_SMS * p.nch <= (a.T + GB_NUM_SMS - 1) / GB_NUM_SMS + 1;
+        whole = (groups + nsm - 1) / nsm * p.nch <= (a.T + nsm - 1) / nsm + 1;
     a.unit = whole ? p.nch : 1;
     const int units = whole ? groups : a.T;
-    a.ncta = units < GB_NUM_SMS ? units : GB_NUM_SMS;
+    a.ncta = units < nsm ? units : nsm;
     if (mixed) {   // whole groups of the leading multi-item matrices, one per CTA, when no CTA gets more items
         int g1 = 0, n1 = 0, i = 0;
         for (; i < n && ps[i]->nch > 1; i++) {
@@ -1284,9 +1269,9 @@ int mv_launch_group(const MvPlan* const* ps, int n, const float* x, float* const
         }
         bool rest1 = i < n;
         for (int j = i; j < n; j++) rest1 &= ps[j]->nch == 1;
-        const int t2 = a.T - g1 * n1, c2 = GB_NUM_SMS - g1;
+        const int t2 = a.T - g1 * n1, c2 = nsm - g1;
         if (rest1 && g1 > 0 && c2 > 0 && t2 > 0 &&
-            (t2 + c2 - 1) / c2 <= std::max(n1, (a.T + GB_NUM_SMS - 1) / GB_NUM_SMS)) {
+            (t2 + c2 - 1) / c2 <= std::max(n1, (a.T + nsm - 1) / nsm)) {
             a.c1 = g1;
             a.n1 = n1;
             a.ncta = g1 + std::min(c2, t2);

@@ -265,17 +265,6 @@ int gb_model_error(gb_model* m);
 /* Kernel launches one decode step issues. */
 int gb_model_launches_per_step(const gb_model* m);
 
-/* Decode-step schedule (one GPU): on = 1 runs each layer boundary (wo, gate/up,
- * down, the next layer's q/k/v) as one persistent cooperative launch that
- * streams every phase's weights through one shared-memory ring; on = 0 issues
- * one launch per matrix group.  Default: GB_CHAIN=1 in the environment, else 0.
- * Needs every matrix on the TMA path (Q6_K rows of a multiple of 2048
- * columns); otherwise the per-matrix schedule runs. */
-int gb_model_use_persistent(gb_model* m, int on);
-/* 1 when the last decode step ran the persistent schedule (set up lazily by
- * the first decode after a weight change), else 0. */
-int gb_model_persistent(const gb_model* m);
-
 /* Byte count of one decode step's algorithmic HBM traffic at position pos
  * (weights + KV read + KV append + activations), for rooflines. */
 double gb_model_step_bytes(const gb_model* m, int pos);

@@ -10,6 +10,14 @@ if ROOT not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 (runs the CUDA library)")
+    # GB_REQUIRE_REF=1: the reference checker (oracle/_ref/libref.so, built
+    # from the reference sources) must be present, so the cases that compare
+    # against it fail loudly instead of skipping on a machine without it
+    if os.environ.get("GB_REQUIRE_REF") == "1":
+        from oracle import oracle as O
+        if not O.ref_available():
+            raise pytest.UsageError("GB_REQUIRE_REF=1 but oracle/_ref/libref.so is absent "
+                                    "(build it with make -C oracle REF=<reference checkout>)")
 
 
 @pytest.fixture(scope="session")

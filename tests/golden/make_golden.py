@@ -82,7 +82,8 @@ SHAPES = {O.DT_Q4_K: [(1, 256), (7, 512), (33, 1024), (64, 2048)],
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("GUANACO_REF", os.path.join(ROOT, "..", "reference")),
+                    help="reference checkout (default: $GUANACO_REF, else ../reference beside the repository)")
     a = ap.parse_args()
     O.build()
     if not O.ref_available():

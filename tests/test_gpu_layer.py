@@ -96,21 +96,18 @@ def upload(cuda, arr):
     return t
 
 
-@pytest.mark.parametrize("shape,persistent", [
+@pytest.mark.parametrize("shape", [
     # rows too short for the Q6_K tensor maps: one launch per matrix
-    (dict(H=256, nh=4, nkv=2, ff=512, vocab=1000), False),
-    # every matrix on the TMA path: per-matrix launches, then the persistent
-    # layer-boundary launches
-    (dict(H=2048, nh=16, nkv=4, ff=4096, vocab=1000), False),
-    (dict(H=2048, nh=16, nkv=4, ff=4096, vocab=1000), True),
+    dict(H=256, nh=4, nkv=2, ff=512, vocab=1000),
+    # every matrix on the TMA path, grouped launches
+    dict(H=2048, nh=16, nkv=4, ff=4096, vocab=1000),
 ])
-def test_model_decode_matches_reference_forward(gb, oracle, cuda, shape, persistent):
+def test_model_decode_matches_reference_forward(gb, oracle, cuda, shape):
     if not oracle.ref_available():
         pytest.skip("oracle/_ref not built")
     m = TinyModel(oracle, **shape)
     ref = oracle.RefModel(m)
     dm = gb.DecodeModel(m.H, m.n_heads, m.n_kv, m.n_layers, m.ff, m.vocab, m.max_seq)
-    dm.use_persistent(persistent)
     keep = []
     try:
         for l, lw in enumerate(m.layers):
@@ -138,7 +135,6 @@ def test_model_decode_matches_reference_forward(gb, oracle, cuda, shape, persist
                 agree += 1
             token = tok_ref   # teacher forcing on the reference's choice
         assert agree >= 8
-        assert dm.persistent() == persistent
     finally:
         dm.close()
         ref.close()
@@ -271,27 +267,3 @@ def test_dropin_norm_cache_follows_host_values(gb, oracle, cuda):
                                             vc.ctypes.data, ms * hd, H, nh, nkv, hd, 0, layer, ms) == 0
         L.cuda_finish_layer()
         assert rel_l2(h, h_ref) <= REL_L2_TOL, trial
-
-
-def test_model_persistent_decode_is_deterministic(gb, cuda):
-    """The persistent launches split groups across CTAs; partial rows are
-    summed in CTA order, so two runs give bit-identical logits."""
-    V = 3000
-    runs = []
-    for _ in range(2):
-        dm = gb.DecodeModel(2048, 16, 4, 2, 4096, V, 64)
-        try:
-            dm.synthesize(99)
-            dm.use_persistent(True)
-            out = []
-            t = 3
-            for pos in range(6):
-                lg = np.zeros(V, np.float32)
-                t = dm.decode_host(t, pos, lg)
-                out.append(lg)
-            assert dm.persistent()
-            runs.append(np.stack(out))
-        finally:
-            dm.close()
-    assert np.array_equal(runs[0], runs[1])
-    assert np.isfinite(runs[0]).all()

@@ -105,6 +105,34 @@ def test_matvec_parity(gb, oracle, cuda, name, rows, cols):
     assert gb.lib().gb_device_error(1) == 0
 
 
+@pytest.mark.parametrize("name", list(DTS))
+@pytest.mark.parametrize("rows,cols", [(100, 4096), (64, 14336), (4096, 4096)])
+@pytest.mark.parametrize("pattern", ["every_subblock", "one_subblock", "channel_1e3_and_tiny"])
+def test_matvec_outlier_activations(gb, oracle, cuda, name, rows, cols, pattern):
+    """Hidden states of real models carry outlier channels 100-1000x the
+    median.  The Q4_K / Q6_K matvecs carry x as two int8 limbs scaled per
+    32-column sub-block, so an outlier coarsens the other 31 values of its
+    sub-block; the result must stay inside the 1e-3 relative-L2 bound."""
+    dt = DTS[name]
+    W = oracle.synth_blocks(dt, rows, cols, 99, rows + cols)
+    x = oracle.synth_normal(cols, 99, 3).copy()
+    if pattern == "every_subblock":        # one channel at 1e3 in every 32-column sub-block
+        x[7::32] = 1e3
+    elif pattern == "one_subblock":        # a single outlier channel
+        x[cols // 2 + 5] = -1e3
+    else:                                  # outliers beside values of 1e-4 x the median
+        x[::32] = 1e3
+        x[1::32] *= 1e-4
+    rc, y_ref = oracle.matvec(dt, W, rows, cols, x)
+    assert rc == 0
+    y = run_matvec(gb, cuda, dt, W, rows, cols, x)
+    assert np.all(np.isfinite(y))
+    err = rel_l2(y, y_ref)
+    assert err <= REL_L2_TOL, err
+    assert err <= (1e-5 if dt == 2 else 2e-4), err
+    assert gb.lib().gb_device_error(1) == 0
+
+
 @pytest.mark.parametrize("rows,cols", [(3, 32), (9, 96), (31, 160), (300, 4128)])
 def test_matvec_q8_0_ragged_columns(gb, oracle, cuda, rows, cols):
     W = oracle.synth_blocks(2, rows, cols, 5, cols)

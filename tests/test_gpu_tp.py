@@ -15,6 +15,11 @@ pytestmark = pytest.mark.gpu
 # H 2048 keeps every matrix on the tensor-map path; ff 5120 gives each of two
 # ranks 2560 FFN columns, so the Q6_K ffn_down shard needs zero padding
 CFG = dict(hidden_dim=2048, n_heads=16, n_kv_heads=4, n_layers=2, ff_dim=5120, vocab_size=5000, max_seq=64)
+# eight ranks: one KV head (two q heads) and 768 FFN rows per rank, as the
+# Llama-3.1-8B shape gives at eight GPUs; 4096 positions of context so the
+# attention of each rank's single KV head splits over many CTAs
+CFG8 = dict(hidden_dim=2048, n_heads=16, n_kv_heads=8, n_layers=2, ff_dim=6144, vocab_size=5000, max_seq=4120)
+CTX8 = 4096
 SEED, CTX, STEPS = 4321, 20, 6
 
 
@@ -24,9 +29,9 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _decode(dm, vocab_rows):
+def _decode(dm, vocab_rows, ctx):
     toks, logits = [], []
-    tok, pos = 7, CTX
+    tok, pos = 7, ctx
     for _ in range(STEPS):
         lg = np.zeros(vocab_rows, np.float32)
         tok = dm.decode_host(tok, pos, logits=lg)
@@ -36,7 +41,7 @@ def _decode(dm, vocab_rows):
     return toks, logits
 
 
-def _worker(rank, world, port, q, fused):
+def _worker(rank, world, port, q, fused, c, ctx):
     if not fused:
         os.environ["GB_TP_FUSED"] = "0"
     import torch
@@ -47,14 +52,13 @@ def _worker(rank, world, port, q, fused):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        c = CFG
         dm = gb.DecodeModel(c["hidden_dim"], c["n_heads"], c["n_kv_heads"], c["n_layers"], c["ff_dim"],
                             c["vocab_size"], c["max_seq"], tp_rank=rank, tp_world=world)
         dm.exchange_handles(dist)
         dm.synthesize(SEED)
-        dm.fill_kv(CTX, SEED)
+        dm.fill_kv(ctx, SEED)
         _, _, off, n = dm.tp_info()
-        toks, logits = _decode(dm, n)
+        toks, logits = _decode(dm, n, ctx)
         assert dm.error() == 0
         q.put((rank, off, toks, logits))
         dist.barrier()
@@ -63,26 +67,27 @@ def _worker(rank, world, port, q, fused):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,fused", [(2, True), (2, False), (4, True)])
-def test_tp_decode_matches_one_gpu(gb, cuda, world, fused):
+@pytest.mark.parametrize("world,fused,big", [(2, True, False), (2, False, False), (4, True, False), (4, True, True),
+                                             (8, True, True), (8, False, True)])
+def test_tp_decode_matches_one_gpu(gb, cuda, world, fused, big):
     """fused: the hidden-state exchanges run inside the wo / ffn_down matvecs
     (push) and the next RMSNorm matvec (sum); otherwise each exchange is its
     own all-reduce launch."""
     if cuda.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
-    c = CFG
+    c, ctx = (CFG8, CTX8) if big else (CFG, CTX)
     ref = gb.DecodeModel(c["hidden_dim"], c["n_heads"], c["n_kv_heads"], c["n_layers"], c["ff_dim"],
                          c["vocab_size"], c["max_seq"])
     try:
         ref.synthesize(SEED)
-        ref.fill_kv(CTX, SEED)
-        toks_ref, logits_ref = _decode(ref, c["vocab_size"])
+        ref.fill_kv(ctx, SEED)
+        toks_ref, logits_ref = _decode(ref, c["vocab_size"], ctx)
     finally:
         ref.close()
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
+    mpc = mp.get_context("spawn")
+    q = mpc.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, fused)) for r in range(world)]
+    procs = [mpc.Process(target=_worker, args=(r, world, port, q, fused, c, ctx)) for r in range(world)]
     for p in procs:
         p.start()
     got = [q.get(timeout=300) for _ in range(world)]
