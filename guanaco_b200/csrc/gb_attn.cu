@@ -47,6 +47,13 @@ namespace gb {
 constexpr int ATTN_CWARPS = 16;                       // consumer warps
 constexpr int ATTN_THREADS = (ATTN_CWARPS + 1) * 32;   // + the producer warp
 constexpr int ATTN_SMEM_MAX = 227 * 1024;
+// A split's partial per query head: {m, l, 2 pad, o[head_dim]} (o 16-byte
+// aligned for the float4 merge).
+__host__ __device__ constexpr int attn_part_stride(int hd) { return hd + 4; }
+// Fewest positions a split takes (two 32-position tiles): with few KV heads
+// per GPU (tensor parallelism) the context is not cut into more splits than
+// the merge can combine quickly.
+constexpr int ATTN_MIN_SPLIT_POS = 64;
 
 // Splits per KV head: one CTA per SM over all heads (every split then has
 // its whole share of K/V requested nearly at once), at least one 32-position
@@ -156,7 +163,7 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
     const int seq = pos + 1;
     // positions per split: any count (a copy is whole 512-byte rows), so every
     // split of the grid gets work
-    const int P = (seq + grid_splits - 1) / grid_splits;
+    const int P = max((seq + grid_splits - 1) / grid_splits, ATTN_MIN_SPLIT_POS);
     const int nsplit = (seq + P - 1) / P;
     if (split >= nsplit) return;
     const int s0 = split * P, n = min(seq, s0 + P) - s0;
@@ -370,7 +377,8 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
     asm volatile("bar.sync 1, %0;" ::"n"(ATTN_CWARPS * 32) : "memory");
     const int ctid = tid;   // 0 .. CT - 1
     const bool single = nsplit == 1;
-    float* my = part + ((size_t)kvh * grid_splits + split) * GROUP * (HD + 2);
+    constexpr int PS = attn_part_stride(HD);
+    float* my = part + ((size_t)kvh * grid_splits + split) * GROUP * PS;
     for (int e = ctid; e < GROUP * HD; e += ATTN_CWARPS * 32) {
         const int h = e / HD, d = e % HD;
         float M = -INFINITY;
@@ -389,8 +397,8 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
             // a warp holds one 32-column group: e >> 5 is warp-uniform
             if (xq_out) mt_quantise32(xq_out, n_kv * GROUP * HD, (kvh * GROUP * HD + e) >> 5, lane, O / L);
         } else {
-            my[h * (HD + 2) + 2 + d] = O;
-            if (d == 0) { my[h * (HD + 2)] = M; my[h * (HD + 2) + 1] = L; }
+            my[h * PS + 4 + d] = O;
+            if (d == 0) { my[h * PS] = M; my[h * PS + 1] = L; }
         }
     }
     if (single) return;
@@ -414,53 +422,80 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
     __syncwarp();   // bar.sync is warp-aligned: reconverge the warp first
     asm volatile("bar.sync 1, %0;" ::"n"(ATTN_CWARPS * 32) : "memory");
     if (!last) return;
-    // every output is a weighted sum over the splits in split order, in one
-    // pass with a running maximum: chunks of MC splits, the next chunk's
-    // loads in flight while the current one is summed
-    const float* base = part + (size_t)kvh * grid_splits * GROUP * (HD + 2);
-    constexpr int MC = 10;
-    constexpr size_t SS = (size_t)GROUP * (HD + 2);   // floats from one split to the next
-    for (int e = ctid; e < GROUP * HD; e += CT) {
-        const int h = e / HD, d = e % HD;
-        const float* hb = base + (size_t)h * (HD + 2);
-        float M = -INFINITY, L = 0.f, O = 0.f;
-        auto fetch = [&](float2 (&ml)[MC], float (&pv)[MC], int j0) {
+    // Every output is a weighted sum over the splits.  The CTA's threads
+    // split the work both ways: NV threads each own a float4 of the output
+    // (head h, dims d4 .. d4 + 3), and NQ such groups take the splits
+    // q, q + NQ, ... with a running maximum (loads of MC splits in flight);
+    // the NQ partial (m, l, o) are then combined in q order (deterministic).
+    constexpr int NV = GROUP * HD / 4;            // float4 outputs
+    constexpr int NQ = CT / NV >= 1 ? CT / NV : 1;
+    static_assert(CT % NV == 0, "merge thread map");
+    const float* base = part + (size_t)kvh * grid_splits * GROUP * PS;
+    constexpr size_t SS = (size_t)GROUP * PS;     // floats from one split to the next
+    constexpr int MC = 8;
+    float* mq = ring;                              // [NQ][NV][6]: m, l, o.xyzw
+    static_assert((size_t)NQ * NV * 6 <= (size_t)C::R * C::TILE, "merge groups fit the ring");
+    for (int e = ctid; e < NQ * NV; e += CT) {
+        const int qg = e / NV, r = e % NV;
+        const int h = r / (HD / 4), d4 = (r % (HD / 4)) * 4;
+        const float* hb = base + (size_t)h * PS;
+        float M = -INFINITY, L = 0.f;
+        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j0 = qg; j0 < nsplit; j0 += MC * NQ) {
+            float2 ml[MC];
+            float4 pv[MC];
 #pragma unroll
             for (int i = 0; i < MC; i++) {
-                const bool in = j0 + i < nsplit;
-                const float* pj = hb + (size_t)(j0 + i) * SS;
-                ml[i] = in ? __ldcg(reinterpret_cast<const float2*>(pj)) : make_float2(-INFINITY, 0.f);
-                pv[i] = in ? __ldcg(pj + 2 + d) : 0.f;
+                const int j = j0 + i * NQ;
+                const float* pj = hb + (size_t)(j < nsplit ? j : 0) * SS;
+                ml[i] = j < nsplit ? __ldcg(reinterpret_cast<const float2*>(pj)) : make_float2(-INFINITY, 0.f);
+                pv[i] = j < nsplit ? __ldcg(reinterpret_cast<const float4*>(pj + 4 + d4))
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
             }
-        };
-        auto combine = [&](const float2 (&ml)[MC], const float (&pv)[MC], int j0) {
             float Mc = M;
 #pragma unroll
             for (int i = 0; i < MC; i++) Mc = fmaxf(Mc, ml[i].x);
-            const float a = M == -INFINITY ? 0.f : expf(M - Mc);   // L, O are 0 before the first chunk
+            if (Mc == -INFINITY) continue;
+            const float a = M == -INFINITY ? 0.f : expf(M - Mc);   // L, O are 0 before the first split
             L *= a;
-            O *= a;
+            O = make_float4(O.x * a, O.y * a, O.z * a, O.w * a);
 #pragma unroll
             for (int i = 0; i < MC; i++)
-                if (j0 + i < nsplit) {
+                if (ml[i].x != -INFINITY) {
                     const float w = expf(ml[i].x - Mc);
                     L = fmaf(ml[i].y, w, L);
-                    O = fmaf(pv[i], w, O);
+                    O = make_float4(fmaf(pv[i].x, w, O.x), fmaf(pv[i].y, w, O.y), fmaf(pv[i].z, w, O.z),
+                                    fmaf(pv[i].w, w, O.w));
                 }
             M = Mc;
-        };
-        float2 mla[MC], mlb[MC];
-        float pva[MC], pvb[MC];
-        fetch(mla, pva, 0);
-        for (int j0 = 0; j0 < nsplit; j0 += 2 * MC) {
-            if (j0 + MC < nsplit) fetch(mlb, pvb, j0 + MC);
-            combine(mla, pva, j0);
-            if (j0 + MC >= nsplit) break;
-            if (j0 + 2 * MC < nsplit) fetch(mla, pva, j0 + 2 * MC);
-            combine(mlb, pvb, j0 + MC);
         }
-        out[(size_t)(kvh * GROUP + h) * HD + d] = O / L;
-        if (xq_out) mt_quantise32(xq_out, n_kv * GROUP * HD, (kvh * GROUP * HD + e) >> 5, lane, O / L);
+        float* q6 = mq + (size_t)e * 6;
+        q6[0] = M;
+        q6[1] = L;
+        *reinterpret_cast<float2*>(q6 + 2) = make_float2(O.x, O.y);
+        *reinterpret_cast<float2*>(q6 + 4) = make_float2(O.z, O.w);
+    }
+    __syncwarp();   // bar.sync is warp-aligned: reconverge the warp first
+    asm volatile("bar.sync 1, %0;" ::"n"(ATTN_CWARPS * 32) : "memory");
+    // combine the NQ groups in q order, one output element per thread, in
+    // the mt_quantise32 lane layout (a warp holds 32 consecutive columns)
+    for (int e = ctid; e < GROUP * HD; e += CT) {
+        const int r = e / 4, comp = e % 4;
+        float M = -INFINITY;
+#pragma unroll
+        for (int qg = 0; qg < NQ; qg++) M = fmaxf(M, mq[((size_t)qg * NV + r) * 6]);
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int qg = 0; qg < NQ; qg++) {
+            const float* q6 = mq + ((size_t)qg * NV + r) * 6;
+            if (q6[0] == -INFINITY) continue;
+            const float w = expf(q6[0] - M);
+            L = fmaf(q6[1], w, L);
+            O = fmaf(q6[2 + comp], w, O);
+        }
+        const float val = O / L;
+        out[(size_t)kvh * GROUP * HD + e] = val;
+        if (xq_out) mt_quantise32(xq_out, n_kv * GROUP * HD, (kvh * GROUP * HD + e) >> 5, lane, val);
     }
     if (ctid == 0) tickets[kvh] = 0u;   // every split has arrived: safe to rearm
 }
@@ -529,7 +564,7 @@ extern "C" size_t gb_attn_workspace_bytes(int n_heads, int n_kv, int head_dim, i
     if (n_kv <= 0 || n_heads % n_kv) return 0;
     const int group = n_heads / n_kv;
     const int G = attn_grid_splits(n_kv, max_seq);
-    const size_t part = (size_t)n_kv * G * group * (head_dim + 2) * sizeof(float);
+    const size_t part = (size_t)n_kv * G * group * attn_part_stride(head_dim) * sizeof(float);
     return part + (size_t)(n_kv + 1) * sizeof(unsigned);
 }
 
@@ -542,7 +577,7 @@ int gb::attention_decode_xq(const float* q, const float* k, const float* v, floa
     const int group = n_heads / n_kv;
     const int G = attn_grid_splits(n_kv, max_seq);
     float* part = static_cast<float*>(ws);
-    unsigned* tickets = reinterpret_cast<unsigned*>(part + (size_t)n_kv * G * group * (head_dim + 2));
+    unsigned* tickets = reinterpret_cast<unsigned*>(part + (size_t)n_kv * G * group * attn_part_stride(head_dim));
     return attn_dispatch(q, k, v, k_cache, v_cache, rope_cs, d_pos, n_heads, n_kv, head_dim, max_seq, out, part,
                          tickets, tickets + n_kv, st, xq_out);
 }
@@ -562,7 +597,7 @@ extern "C" int gb_attention_decode_static(const float* q, const float* k, const 
     if (n_kv >= GB_ATTN_STATIC_ERR_WORD) return GB_ELIMIT;
     const int group = n_heads / n_kv;
     const int G = attn_grid_splits(n_kv, max_seq);
-    const size_t part_bytes = (size_t)n_kv * G * group * (head_dim + 2) * sizeof(float);
+    const size_t part_bytes = (size_t)n_kv * G * group * attn_part_stride(head_dim) * sizeof(float);
     if (part_bytes > GB_ATTN_STATIC_BYTES - GB_ATTN_STATIC_PART_OFFSET) return GB_ELIMIT;
     int rc;
     unsigned char* base = attn_static_scratch(&rc);

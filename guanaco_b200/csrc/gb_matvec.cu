@@ -374,7 +374,7 @@ k_mv_q4k(const uint8_t* __restrict__ W, int rows, int nb, const float* __restric
 // Staged x per block: xb[(b*8 + 4n + G)*8 + 2c + limb] (B-fragment pair of
 // columns 128n + 32G + 8c + 0..3, 4..7), xs[b*16 + 8n + 2G + (c>>1)] = x
 // scale of the 16-column sub-block, xs32[b*32 + (4n + G)*4 + c] = 32 * sum of
-// x over the lanes' 8 columns (the -32 offset of the codes).
+// the quantised x over the lanes' 8 columns (the -32 offset of the codes).
 __global__ void __launch_bounds__(MV_THREADS)
 k_mv_q6k(const uint8_t* __restrict__ W, int rows, int nb, const float* __restrict__ x, float* __restrict__ y,
          const float* __restrict__ residual, MvGeom g) {
@@ -397,11 +397,14 @@ k_mv_q6k(const uint8_t* __restrict__ W, int rows, int nb, const float* __restric
         float mx = fabsf(v);
 #pragma unroll
         for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        float s8 = v;
-#pragma unroll
-        for (int o = 4; o > 0; o >>= 1) s8 += __shfl_xor_sync(0xffffffffu, s8, o);
         int a0, a1;
         limbs(v * (mx > 0.f ? 127.f / mx : 0.f), a0, a1);
+        // 8-column sums of the quantised values: the -32 code offset then
+        // applies to the same x the codes multiply (see mt_quantise4)
+        float s8 = limb_value(a0, a1);
+#pragma unroll
+        for (int o = 4; o > 0; o >>= 1) s8 += __shfl_xor_sync(0xffffffffu, s8, o);
+        s8 *= mx / 127.f;
         const int c = lane >> 3;
         uint8_t* dst = reinterpret_cast<uint8_t*>(xb + (size_t)((b * 8 + 4 * n + G) * 8 + 2 * c));
         dst[lane & 7] = (uint8_t)a0;

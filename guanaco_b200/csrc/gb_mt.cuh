@@ -1,6 +1,6 @@
-// gb_mt.cuh -- device building blocks of the TMA-fed tensor-core matvec,
-// shared by the one-launch-per-matrix kernel (gb_matvec.cu) and the
-// persistent multi-phase kernel (gb_chain.cu).
+// gb_mt.cuh -- device building blocks of the TMA-fed tensor-core matvec
+// (gb_matvec.cu), also used by the attention kernel to quantise its output
+// for the next matvec.
 #pragma once
 #include "gb_common.cuh"
 #include "gb_internal.h"
@@ -34,6 +34,8 @@ __device__ __forceinline__ void limbs(float v, int& x0, int& x1) {
     const int r1 = (int)rintf((v - r0) * 256.f);
     x1 = r1 > 127 ? 127 : (r1 < -128 ? -128 : r1);
 }
+// The value a limb pair stands for, in units of the sub-block scale s.
+__device__ __forceinline__ float limb_value(int x0, int x1) { return fmaf((float)x1, 0.00390625f, (float)x0); }
 __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
     return (uint32_t)(a & 255) | ((uint32_t)(b & 255) << 8) | ((uint32_t)(c & 255) << 16) | ((uint32_t)(d & 255) << 24);
 }
@@ -190,16 +192,11 @@ __device__ __forceinline__ void mt_quantise4(const A& a, int K, uint8_t* xq, int
     }
     float mx = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
     float sm = (v.x + v.y) + (v.z + v.w);
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    sm += __shfl_xor_sync(0xffffffffu, sm, 1);
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    sm += __shfl_xor_sync(0xffffffffu, sm, 2);
-    if (S16 && (t & 3) == 0) {   // 16-column sum: column c0 = 4t = 256 b + 128 n + 32 G + 16 h
-        const int c0 = 4 * t, b = c0 >> 8, n = (c0 >> 7) & 1, G = (c0 >> 5) & 3, h = (c0 >> 4) & 1;
-        f16[b * 16 + h * 8 + 4 * n + G] = sm;
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        sm += __shfl_xor_sync(0xffffffffu, sm, o);
     }
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-    sm += __shfl_xor_sync(0xffffffffu, sm, 4);
     const float inv = mx > 0.f ? 127.f / mx : 0.f;
     int a0, a1, b0, b1, c0, c1, d0, d1;
     limbs(v.x * inv, a0, a1);
@@ -208,9 +205,24 @@ __device__ __forceinline__ void mt_quantise4(const A& a, int K, uint8_t* xq, int
     limbs(v.w * inv, d0, d1);
     p0[t] = pack4(a0, b0, c0, d0);
     p1[t] = pack4(a1, b1, c1, d1);
+    const float s = mx / 127.f;
+    if (S16) {
+        // 16-column sums of the QUANTISED values s (x0 + x1 / 256): the Q6_K
+        // consumer applies the -32 code offset with them, so the offset and
+        // the codes multiply the same x, and the quantisation error of x
+        // reaches the result only through (q - 32), not through the codes'
+        // mean (31.5), which would give every row a correlated error
+        float sq = (limb_value(a0, a1) + limb_value(b0, b1)) + (limb_value(c0, c1) + limb_value(d0, d1));
+        sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+        sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+        if ((t & 3) == 0) {   // 16-column sum: column c0 = 4t = 256 b + 128 n + 32 G + 16 h
+            const int cc = 4 * t, b = cc >> 8, n = (cc >> 7) & 1, G = (cc >> 5) & 3, h = (cc >> 4) & 1;
+            f16[b * 16 + h * 8 + 4 * n + G] = sq * s;
+        }
+    }
     const int sb = t >> 3;
     if ((t & 7) == 0) {
-        f[(sb >> 1) * 4 + (sb & 1)] = mx / 127.f;
+        f[(sb >> 1) * 4 + (sb & 1)] = s;
         f[(sb >> 1) * 4 + 2 + (sb & 1)] = sm;
     }
 }
@@ -223,25 +235,28 @@ __device__ __forceinline__ void mt_quantise4(const A& a, int K, uint8_t* xq, int
 __device__ __forceinline__ void mt_quantise32(uint8_t* xq, int K, int sb, int lane, float v) {
     float mx = fabsf(v), sm = v;
 #pragma unroll
-    for (int o = 1; o < 16; o <<= 1) {
+    for (int o = 1; o < 32; o <<= 1) {
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         sm += __shfl_xor_sync(0xffffffffu, sm, o);
     }
     float* f = reinterpret_cast<float*>(xq + 2 * K);
     float* f16 = f + K / 16;
-    if ((lane & 15) == 0) {   // 16-column sum: column c0 = 32 sb + lane = 256 b + 128 n + 32 G + 16 h
-        const int c0 = 32 * sb + lane, b = c0 >> 8, n = (c0 >> 7) & 1, G = (c0 >> 5) & 3, h = (c0 >> 4) & 1;
-        f16[b * 16 + h * 8 + 4 * n + G] = sm;
-    }
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-    sm += __shfl_xor_sync(0xffffffffu, sm, 16);
     const float inv = mx > 0.f ? 127.f / mx : 0.f;
     int x0, x1;
     limbs(v * inv, x0, x1);
     xq[32 * sb + lane] = (uint8_t)(x0 & 255);
     xq[K + 32 * sb + lane] = (uint8_t)(x1 & 255);
+    const float s = mx / 127.f;
+    // 16-column sums of the quantised values (see mt_quantise4)
+    float sq = limb_value(x0, x1);
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    if ((lane & 15) == 0) {   // 16-column sum: column c0 = 32 sb + lane = 256 b + 128 n + 32 G + 16 h
+        const int c0 = 32 * sb + lane, b = c0 >> 8, n = (c0 >> 7) & 1, G = (c0 >> 5) & 3, h = (c0 >> 4) & 1;
+        f16[b * 16 + h * 8 + 4 * n + G] = sq * s;
+    }
     if (lane == 0) {
-        f[(sb >> 1) * 4 + (sb & 1)] = mx / 127.f;
+        f[(sb >> 1) * 4 + (sb & 1)] = s;
         f[(sb >> 1) * 4 + 2 + (sb & 1)] = sm;
     }
 }

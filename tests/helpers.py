@@ -20,3 +20,20 @@ def to_dev(torch, arr):
 
 def from_dev(t):
     return t.detach().cpu().numpy()
+
+
+def two_limb(x):
+    """The x the Q4_K / Q6_K matvecs multiply: per 32-column sub-block,
+    s = max|x| / 127 and x ~ s (x0 + x1 / 256) with x0 = rint(x / s) and
+    x1 = rint((x / s - x0) * 256) clamped to int8 -- a model of the device
+    quantiser (guanaco_b200/csrc/gb_mt.cuh), used to check that the kernels
+    compute W . x~ up to fp32 rounding."""
+    x = np.asarray(x, np.float32).reshape(-1, 32)
+    mx = np.abs(x).max(axis=1, keepdims=True)
+    with np.errstate(divide="ignore"):
+        inv = np.where(mx > 0, np.float32(127) / mx, np.float32(0)).astype(np.float32)
+    v = (x * inv).astype(np.float32)
+    x0 = np.rint(v)
+    x1 = np.clip(np.rint((v - x0) * np.float32(256)), -128, 127)
+    s = (mx / np.float32(127)).astype(np.float32)
+    return ((x0 + x1 / 256.0) * s).astype(np.float32).ravel()

@@ -4,7 +4,7 @@ with the reference CPU kernels)."""
 import numpy as np
 import pytest
 
-from tests.helpers import REL_L2_TOL, from_dev, rel_l2, to_dev
+from tests.helpers import REL_L2_TOL, from_dev, rel_l2, to_dev, two_limb
 
 pytestmark = pytest.mark.gpu
 
@@ -131,6 +131,31 @@ def test_matvec_outlier_activations(gb, oracle, cuda, name, rows, cols, pattern)
     assert err <= REL_L2_TOL, err
     assert err <= (1e-5 if dt == 2 else 2e-4), err
     assert gb.lib().gb_device_error(1) == 0
+
+
+@pytest.mark.parametrize("name", ["q4k", "q6k"])
+@pytest.mark.parametrize("rows,cols", [(100, 4096), (64, 14336), (1024, 4096), (77, 2048), (40, 5632)])
+@pytest.mark.parametrize("xkind", ["normal", "positive"])
+def test_matvec_is_exact_on_the_quantised_x(gb, oracle, cuda, name, rows, cols, xkind):
+    """The only approximation of the Q4_K / Q6_K matvecs is x carried as two
+    int8 limbs per 32-column sub-block: given that x~, the result is W . x~ up
+    to fp32 rounding.  A consumer that mixes x and x~ (e.g. the Q6_K -32 code
+    offset applied with the sum of the exact x) shows up here as a larger
+    error that is correlated across rows, which a decoder stack amplifies."""
+    dt = DTS[name]
+    W = oracle.synth_blocks(dt, rows, cols, 7, rows * 3 + cols)
+    x = oracle.synth_normal(cols, 7, 11)
+    if xkind == "positive":   # a common-mode component, as hidden states of the synthetic models have
+        x = (np.abs(x) + 0.5).astype(np.float32)
+    _, y_exact = oracle.matvec(dt, W, rows, cols, x)
+    _, y_q = oracle.matvec(dt, W, rows, cols, two_limb(x))
+    y = run_matvec(gb, cuda, dt, W, rows, cols, x)
+    err_q, err_x = rel_l2(y, y_q), rel_l2(y, y_exact)
+    assert err_q <= 2e-6 or err_q <= 0.2 * err_x, (err_q, err_x)
+    e = y.astype(np.float64) - y_exact
+    eq = y_q.astype(np.float64) - y_exact
+    # the errors summed over the rows are no larger than the quantisation's own
+    assert abs(e.sum()) <= 2.0 * abs(eq.sum()) + 4.0 * np.sqrt(np.sum(eq * eq)) + 1e-6 * np.abs(y_exact).sum()
 
 
 @pytest.mark.parametrize("rows,cols", [(3, 32), (9, 96), (31, 160), (300, 4128)])
