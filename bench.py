@@ -453,8 +453,8 @@ def run_ours(args, rank, world, local_rank):
             "warmup": W, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
             "scaling": "strong" if world > 1 else "weak",
             "vs_baseline": None,
-            "dtype": "f32 (weights Q4_K/Q6_K codes; matvec x as two int8 limbs per 32-column sub-block, "
-                     "~16 significant bits; fp32 scales, accumulation, KV cache and attention)",
+            "dtype": "f32 (weights Q4_K/Q6_K codes; matvec x as three int8 limbs per 32-column sub-block, "
+                     "24 significant bits as fp32; fp32 scales, accumulation, KV cache and attention)",
             "data": "synthetic (seeded random-init weights, ~N(0,1) KV fill)",
             "config": {"workload": "llama3.1-8b-q4km-decode (BASELINE config 4)", "global_batch": 1,
                        "seq_len": CTX, "parallelism": f"tp{world}" if world > 1 else "single",

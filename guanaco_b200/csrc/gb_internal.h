@@ -75,13 +75,18 @@ struct MvXform {
 //   push_call >= 0: the launch's y rows (one matrix, no residual) go to slot
 //                   [rank] of every rank's buffer instead of y.
 //   in_call >= 0:   x (RMSNorm input) = x + sum over ranks, in rank order,
-//                   of this rank's slots of exchange in_call (bounded wait
-//                   for the tags); each CTA writes its slice of that sum to
-//                   h_out, the hidden state after the exchange.
+//                   of this rank's slots of exchange in_call.  CTA c of the
+//                   launch sums only its slice of x (bounded wait for the
+//                   tags), writes that slice of the new hidden state to
+//                   h_out and releases ready[c] = epoch; every CTA then waits
+//                   (bounded) for all ready flags and reads the whole new
+//                   hidden state from h_out.  The slots are read once per
+//                   rank, not once per CTA.
 struct MvTp {
     void* const* peers = nullptr;               // device array of the ranks' receive buffers
     const unsigned long long* step = nullptr;   // device step counter
     unsigned* err = nullptr;                    // device error word (GB_ETIMEOUT)
+    unsigned* ready = nullptr;                  // this rank's per-CTA slice flags (GB_MAX_SMS, zeroed once)
     int rank = 0, world = 1, calls = 0, H = 0;
     int push_call = -1, in_call = -1;
     float* h_out = nullptr;
@@ -107,6 +112,7 @@ struct TpCtx {
     const unsigned long long* d_step = nullptr;
     int calls = 0;                            // exchanges per step
     unsigned* err = nullptr;
+    unsigned* ready = nullptr;                // per-CTA slice flags of the in-matvec exchanges
     float* part = nullptr;                    // [H] local partial
     float* h[2] = {nullptr, nullptr};         // hidden state: exchange c reads h[c & 1], writes h[(c + 1) & 1]
     // an exchange attached to a matvec (push_call / in_call filled in by the caller)
@@ -115,6 +121,7 @@ struct TpCtx {
         t.peers = d_peers;
         t.step = d_step;
         t.err = err;
+        t.ready = ready;
         t.rank = rank;
         t.world = world;
         t.calls = calls;

@@ -407,6 +407,7 @@ struct gb_model {
     bool comm_ready = false;
     unsigned long long* d_step = nullptr;
     float* part = nullptr;            // local partial of wo / ffn_down
+    unsigned* tp_ready = nullptr;     // per-CTA slice flags of the in-matvec exchanges (zeroed)
     ArgPart* am_res = nullptr;        // local (max, index) of the output head
     TpCtx tp;
     std::vector<const void*> w;       // [n_layers * 7]
@@ -508,13 +509,13 @@ extern "C" gb_model* gb_model_create_tp(const gb_model_config* cfg, int rank, in
     ok &= (m->attn = (float*)dalloc(m, (size_t)QD * 4)) != nullptr;
     ok &= (m->gate = (float*)dalloc(m, (size_t)FP * 4)) != nullptr;
     ok &= (m->up = (float*)dalloc(m, (size_t)FP * 4)) != nullptr;
-    const size_t swq_bytes = FP % 256 ? 0 : (size_t)FP * 5 / 2;   // x0, x1, per-64 scales and sums, 16-column sums
+    const size_t swq_bytes = FP % 256 ? 0 : (size_t)FP * 7 / 2;   // x0, x1, x2, per-64 scales and sums, 16-column sums
     if (swq_bytes) {
         ok &= (m->swq = (uint8_t*)dalloc(m, swq_bytes)) != nullptr;
         ok &= (m->swq_tk = (unsigned*)dalloc(m, (size_t)FP / 32 * sizeof(unsigned))) != nullptr;
     }
     // wo's input quantised by the attention launch (same layout)
-    if (QD % 256 == 0) ok &= (m->aq = (uint8_t*)dalloc(m, (size_t)QD * 5 / 2)) != nullptr;
+    if (QD % 256 == 0) ok &= (m->aq = (uint8_t*)dalloc(m, (size_t)QD * 7 / 2)) != nullptr;
     ok &= (m->logits = (float*)dalloc(m, (size_t)m->vocab_l * 4)) != nullptr;
     // the host-facing words share one block: gb_model_decode_host sends
     // {token, pos} in one copy and reads {next, error} back in one copy
@@ -533,6 +534,7 @@ extern "C" gb_model* gb_model_create_tp(const gb_model_config* cfg, int rank, in
         m->comm_bytes = tp_comm_bytes(world, H);
         ok &= (m->part = (float*)dalloc(m, (size_t)H * 4)) != nullptr;
         ok &= (m->hidden2 = (float*)dalloc(m, (size_t)H * 4)) != nullptr;
+        ok &= (m->tp_ready = (unsigned*)dalloc(m, GB_MAX_SMS * sizeof(unsigned))) != nullptr;
         ok &= (m->d_peers = (void**)dalloc(m, 8 * sizeof(void*))) != nullptr;
         // the exchange buffer gets its own allocation: it is shared with the
         // peers through cudaIpcGetMemHandle
@@ -552,6 +554,7 @@ extern "C" gb_model* gb_model_create_tp(const gb_model_config* cfg, int rank, in
     if (ok && m->swq) ok &= cudaMemsetAsync(m->swq, 0, swq_bytes, m->stream) == cudaSuccess &&
                             cudaMemsetAsync(m->swq_tk, 0, (size_t)FP / 32 * sizeof(unsigned), m->stream) == cudaSuccess;
     if (ok && m->comm) ok &= cudaMemsetAsync(m->comm, 0, m->comm_bytes, m->stream) == cudaSuccess;
+    if (ok && m->tp_ready) ok &= cudaMemsetAsync(m->tp_ready, 0, GB_MAX_SMS * sizeof(unsigned), m->stream) == cudaSuccess;
     if (ok) ok &= gb_rope_table(m->rope, c.max_seq, c.head_dim, c.rope_theta, m->stream) == GB_OK;
     if (ok) ok &= cudaStreamSynchronize(m->stream) == cudaSuccess;
     if (!ok) {
@@ -564,6 +567,7 @@ extern "C" gb_model* gb_model_create_tp(const gb_model_config* cfg, int rank, in
     m->tp.d_step = m->d_step;
     m->tp.calls = 2 * c.n_layers + 1;
     m->tp.err = m->err;
+    m->tp.ready = m->tp_ready;
     m->tp.part = m->part;
     m->tp.h[0] = m->hidden;
     m->tp.h[1] = m->hidden2;

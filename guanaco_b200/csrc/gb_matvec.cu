@@ -19,12 +19,13 @@
 //    4-bit blocks (one mask per weight plus the fp32 FMA).  Q4_K and Q6_K
 //    therefore run their multiply-accumulates on the int8 tensor cores:
 //    mma.sync m16n8k32 u8 x s8 -> s32 with 16 weight rows per warp.  Weights
-//    enter as exact u8 codes (one LOP3 per 4 Q4_K weights); x enters as two
-//    int8 limbs x ~ s * (x0 + x1 / 256) with one scale s per sub-block, which
-//    keeps ~16 significant bits of every element; the 8 output columns are 4
-//    sub-blocks x 2 limbs, so each thread owns whole sub-blocks and applies
-//    their 6-bit / int8 block scales in fp32.  The result carries ~1e-5
-//    relative error, inside the 1e-3 relative-L2 parity bound.
+//    enter as exact u8 codes (one LOP3 per 4 Q4_K weights); x enters as three
+//    int8 limbs x ~ s (x0 + x1 / 256 + x2 / 65536) with one scale s per
+//    sub-block, which keeps fp32's 24 significant bits of every element; the
+//    8 output columns of the first MMA of a k-step are 4 sub-blocks x 2
+//    limbs, a second MMA on the same A fragment takes the third limb, so each
+//    thread owns whole sub-blocks and applies their 6-bit / int8 block scales
+//    in fp32.  The result matches an fp32 matvec to ~1e-6 relative.
 //  * Q8_0 keeps a CUDA-core fp32 consumer (field extraction into exact
 //    subnormal floats, FFMA2) on the same ring.
 //  * Every mbarrier wait is bounded (2 s of %globaltimer); a timeout records
@@ -253,6 +254,7 @@ k_mv_q4k(const uint8_t* __restrict__ W, int rows, int nb, const float* __restric
     uint2* xb = reinterpret_cast<uint2*>(smem);
     float* xs = reinterpret_cast<float*>(xb + (size_t)nb * 64);
     float* xsum = xs + (size_t)nb * 8;
+    uint2* xb2 = reinterpret_cast<uint2*>(xsum + (size_t)nb * 8);   // third limb [(b*8 + 2u + lohi)*4 + c]
     const MvShared sh = kernel_prologue(smem, g);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (warp == MV_CONSUMERS) {
@@ -265,11 +267,12 @@ k_mv_q4k(const uint8_t* __restrict__ W, int rows, int nb, const float* __restric
         const float v = x[b * 256 + 64 * cg + 32 * lohi + lane];
         const float mx = warp_max(fabsf(v));
         const float sum = warp_sum(v);
-        int a0, a1;
-        limbs(v * (mx > 0.f ? 127.f / mx : 0.f), a0, a1);
+        int a0, a1, a2;
+        limbs(v * (mx > 0.f ? 127.f / mx : 0.f), a0, a1, a2);
         uint8_t* dst = reinterpret_cast<uint8_t*>(xb + (size_t)((b * 8 + 2 * (lane >> 3) + lohi) * 8 + 2 * cg));
         dst[lane & 7] = (uint8_t)a0;
         dst[8 + (lane & 7)] = (uint8_t)a1;
+        reinterpret_cast<uint8_t*>(xb2 + (size_t)((b * 8 + 2 * (lane >> 3) + lohi) * 4 + cg))[lane & 7] = (uint8_t)a2;
         if (lane == 0) {
             xs[e] = (mx / 127.f) * (lohi ? 0.0625f : 1.f);
             xsum[e] = sum;
@@ -279,6 +282,7 @@ k_mv_q4k(const uint8_t* __restrict__ W, int rows, int nb, const float* __restric
 
     const int gq = lane >> 2, c = lane & 3;
     const bool bact = c == (gq >> 1);   // this lane carries a nonzero B fragment
+    const bool b2act = bact && !(gq & 1);   // ... and one of the third-limb MMA (column 2c)
     const int bsel = 2 * c + (gq & 1);
     const int sh8 = (c & 1) << 4;
     int it = 0, gi = 0;
@@ -308,22 +312,30 @@ k_mv_q4k(const uint8_t* __restrict__ W, int rows, int nb, const float* __restric
                 }
                 int4 cl[2] = {make_int4(0, 0, 0, 0), make_int4(0, 0, 0, 0)};
                 int4 ch[2] = {make_int4(0, 0, 0, 0), make_int4(0, 0, 0, 0)};
+                int4 cl3 = make_int4(0, 0, 0, 0), ch3 = make_int4(0, 0, 0, 0);
                 const uint2* xbb = xb + (size_t)b * 64;
+                const uint2* xbb2 = xb2 + (size_t)b * 32;
 #pragma unroll
                 for (int u = 0; u < 4; u++) {
                     const uint32_t wa0 = (u & 1) ? qa[u >> 1].z : qa[u >> 1].x;
                     const uint32_t wa1 = (u & 1) ? qa[u >> 1].w : qa[u >> 1].y;
                     const uint32_t wb0 = (u & 1) ? qb[u >> 1].z : qb[u >> 1].x;
                     const uint32_t wb1 = (u & 1) ? qb[u >> 1].w : qb[u >> 1].y;
-                    uint2 blo = make_uint2(0, 0), bhi = make_uint2(0, 0);
+                    uint2 blo = make_uint2(0, 0), bhi = make_uint2(0, 0), tlo = make_uint2(0, 0), thi = make_uint2(0, 0);
                     if (bact) {
                         blo = xbb[(2 * u) * 8 + bsel];
                         bhi = xbb[(2 * u + 1) * 8 + bsel];
+                    }
+                    if (b2act) {
+                        tlo = xbb2[(2 * u) * 4 + c];
+                        thi = xbb2[(2 * u + 1) * 4 + c];
                     }
                     mma_u8s8(cl[u & 1], wa0 & 0x0F0F0F0Fu, wb0 & 0x0F0F0F0Fu, wa1 & 0x0F0F0F0Fu, wb1 & 0x0F0F0F0Fu,
                              blo.x, blo.y);
                     mma_u8s8(ch[u & 1], wa0 & 0xF0F0F0F0u, wb0 & 0xF0F0F0F0u, wa1 & 0xF0F0F0F0u, wb1 & 0xF0F0F0F0u,
                              bhi.x, bhi.y);
+                    mma_u8s8(cl3, wa0 & 0x0F0F0F0Fu, wb0 & 0x0F0F0F0Fu, wa1 & 0x0F0F0F0Fu, wb1 & 0x0F0F0F0Fu, tlo.x, tlo.y);
+                    mma_u8s8(ch3, wa0 & 0xF0F0F0F0u, wb0 & 0xF0F0F0F0u, wa1 & 0xF0F0F0F0u, wb1 & 0xF0F0F0F0u, thi.x, thi.y);
                 }
                 const int4 clo = make_int4(cl[0].x + cl[1].x, cl[0].y + cl[1].y, cl[0].z + cl[1].z, cl[0].w + cl[1].w);
                 const int4 chi = make_int4(ch[0].x + ch[1].x, ch[0].y + ch[1].y, ch[0].z + ch[1].z, ch[0].w + ch[1].w);
@@ -341,8 +353,9 @@ k_mv_q4k(const uint8_t* __restrict__ W, int rows, int nb, const float* __restric
                     const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
                     const int c0 = w ? clo.z : clo.x, c1 = w ? clo.w : clo.y;
                     const int e0 = w ? chi.z : chi.x, e1 = w ? chi.w : chi.y;
-                    const float dlo = fmaf((float)c1, 0.00390625f, (float)c0);
-                    const float dhi = fmaf((float)e1, 0.00390625f, (float)e0);
+                    const int c2 = w ? cl3.z : cl3.x, e2 = w ? ch3.z : ch3.x;
+                    const float dlo = fmaf((float)c2, 1.0f / 65536.0f, fmaf((float)c1, 0.00390625f, (float)c0));
+                    const float dhi = fmaf((float)e2, 1.0f / 65536.0f, fmaf((float)e1, 0.00390625f, (float)e0));
                     const float part = dm.x * (sc_lo * sxs.x * dlo + sc_hi * sxs.y * dhi) -
                                        dm.y * (m_lo * sxm.x + m_hi * sxm.y);
                     if (w) acc_b += part; else acc_a += part;
@@ -382,6 +395,7 @@ k_mv_q6k(const uint8_t* __restrict__ W, int rows, int nb, const float* __restric
     uint2* xb = reinterpret_cast<uint2*>(smem);
     float* xs = reinterpret_cast<float*>(xb + (size_t)nb * 64);
     float* xs32 = xs + (size_t)nb * 16;
+    uint2* xb2 = reinterpret_cast<uint2*>(xs32 + (size_t)nb * 32);   // third limb [(b*8 + 4n + G)*4 + c]
     const MvShared sh = kernel_prologue(smem, g);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const size_t rb = (size_t)nb * GB_Q6K_BYTES;
@@ -397,11 +411,11 @@ k_mv_q6k(const uint8_t* __restrict__ W, int rows, int nb, const float* __restric
         float mx = fabsf(v);
 #pragma unroll
         for (int o = 8; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        int a0, a1;
-        limbs(v * (mx > 0.f ? 127.f / mx : 0.f), a0, a1);
+        int a0, a1, a2;
+        limbs(v * (mx > 0.f ? 127.f / mx : 0.f), a0, a1, a2);
         // 8-column sums of the quantised values: the -32 code offset then
         // applies to the same x the codes multiply (see mt_quantise4)
-        float s8 = limb_value(a0, a1);
+        float s8 = limb_value(a0, a1, a2);
 #pragma unroll
         for (int o = 4; o > 0; o >>= 1) s8 += __shfl_xor_sync(0xffffffffu, s8, o);
         s8 *= mx / 127.f;
@@ -409,6 +423,7 @@ k_mv_q6k(const uint8_t* __restrict__ W, int rows, int nb, const float* __restric
         uint8_t* dst = reinterpret_cast<uint8_t*>(xb + (size_t)((b * 8 + 4 * n + G) * 8 + 2 * c));
         dst[lane & 7] = (uint8_t)a0;
         dst[8 + (lane & 7)] = (uint8_t)a1;
+        reinterpret_cast<uint8_t*>(xb2 + (size_t)((b * 8 + 4 * n + G) * 4 + c))[lane & 7] = (uint8_t)a2;
         if ((lane & 15) == 0) xs[b * 16 + 8 * n + 2 * G + (lane >> 4)] = mx / 127.f;
         if ((lane & 7) == 0) xs32[b * 32 + (4 * n + G) * 4 + c] = 32.f * s8;
     }
@@ -416,6 +431,7 @@ k_mv_q6k(const uint8_t* __restrict__ W, int rows, int nb, const float* __restric
 
     const int gq = lane >> 2, c = lane & 3;
     const bool bact = c == (gq >> 1);
+    const bool b2act = bact && !(gq & 1);
     const int bsel = 2 * c + (gq & 1);
     int it = 0, gi = 0;
     for (int grp = blockIdx.x; grp < g.ngroups; grp += gridDim.x) {
@@ -438,6 +454,7 @@ k_mv_q6k(const uint8_t* __restrict__ W, int rows, int nb, const float* __restric
                 const float da = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(ba + 208)));
                 const float db = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(bb + 208)));
                 const uint2* xbb = xb + (size_t)b * 64;
+                const uint2* xbb2 = xb2 + (size_t)b * 32;
 #pragma unroll
                 for (int n = 0; n < 2; n++) {
                     Pair32 qa0 = {0, 0}, qa1 = {0, 0}, ha = {0, 0}, qb0 = {0, 0}, qb1 = {0, 0}, hb = {0, 0};
@@ -465,17 +482,19 @@ k_mv_q6k(const uint8_t* __restrict__ W, int rows, int nb, const float* __restric
                             const uint32_t hi2 = G == 0 ? (hw << 4) : G == 1 ? (hw << 2) : G == 2 ? hw : (hw >> 2);
                             A[t] = nib | (hi2 & 0x30303030u);
                         }
-                        uint2 bf = make_uint2(0, 0);
+                        uint2 bf = make_uint2(0, 0), bf2 = make_uint2(0, 0);
                         if (bact) bf = xbb[(4 * n + G) * 8 + bsel];
-                        int4 cc = make_int4(0, 0, 0, 0);
+                        if (b2act) bf2 = xbb2[(4 * n + G) * 4 + c];
+                        int4 cc = make_int4(0, 0, 0, 0), cc2 = make_int4(0, 0, 0, 0);
                         mma_u8s8(cc, A[0], A[1], A[2], A[3], bf.x, bf.y);
+                        mma_u8s8(cc2, A[0], A[1], A[2], A[3], bf2.x, bf2.y);
                         const int sb = 8 * n + 2 * G + (c >> 1);
                         const float xsc = xs[b * 16 + sb];
                         const float x32 = xs32[b * 32 + (4 * n + G) * 4 + c];
                         const float sca = (float)(int)(int8_t)ba[192 + sb];
                         const float scb = (float)(int)(int8_t)bb[192 + sb];
-                        const float dla = fmaf((float)cc.y, 0.00390625f, (float)cc.x);
-                        const float dlb = fmaf((float)cc.w, 0.00390625f, (float)cc.z);
+                        const float dla = fmaf((float)cc2.x, 1.0f / 65536.0f, fmaf((float)cc.y, 0.00390625f, (float)cc.x));
+                        const float dlb = fmaf((float)cc2.z, 1.0f / 65536.0f, fmaf((float)cc.w, 0.00390625f, (float)cc.z));
                         acc_a = fmaf(da * sca, fmaf(xsc, dla, -x32), acc_a);
                         acc_b = fmaf(db * scb, fmaf(xsc, dlb, -x32), acc_b);
                     }
@@ -770,9 +789,13 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
     L4.gq = L6.gq = lane >> 2;
     L4.c = L6.c = lane & 3;
     const bool bact = L4.c == (L4.gq >> 1);   // this lane carries a nonzero B fragment
+    const bool b2act = bact && !(L4.gq & 1);   // column 2c of the third-limb MMA
     L4.xlb = bact ? xq + (L4.gq & 1) * K + MtQ4K::XB_LANE * L4.c : smem + zero_off;
     L6.xlb = bact ? xq + (L6.gq & 1) * K + MtQ6K::XB_LANE * L6.c : smem + zero_off;
     L4.xstr = L6.xstr = bact ? 256 : 0;
+    L4.x2b = b2act ? xq + 2 * K + MtQ4K::XB_LANE * L4.c : smem + zero_off;
+    L6.x2b = b2act ? xq + 2 * K + MtQ6K::XB_LANE * L6.c : smem + zero_off;
+    L4.x2str = L6.x2str = b2act ? 256 : 0;
     int gi = 0;
     bool ok = true;
     float acc_a[2] = {0.f, 0.f}, acc_b[2] = {0.f, 0.f};
@@ -926,8 +949,8 @@ __host__ __device__ constexpr int round_up(int v, int a) { return (v + a - 1) / 
 
 static int staged_bytes(int dtype, int nb) {
     switch (dtype) {
-        case GB_DT_Q4_K: return nb * (64 * 8 + 16 * 4);
-        case GB_DT_Q6_K: return nb * (64 * 8 + 48 * 4);
+        case GB_DT_Q4_K: return nb * (64 * 8 + 16 * 4 + 32 * 8);
+        case GB_DT_Q6_K: return nb * (64 * 8 + 48 * 4 + 32 * 8);
         default: return ((nb + 7) / 8) * 32 * (2 * 16 + 4);
     }
 }
@@ -1206,7 +1229,7 @@ int mv_launch_group(const MvPlan* const* ps, int n, const float* x, float* const
     if (tp && (tp->push_call >= 0 || tp->in_call >= 0)) {   // tensor-parallel exchange: check its shape
         if (!tp->peers || !tp->step || !tp->err || tp->world < 2 || tp->H <= 0) return GB_EINVAL;
         if (tp->push_call >= 0 && (n != 1 || (res && res[0]) || ps[0]->rows > tp->H)) return GB_EINVAL;
-        if (tp->in_call >= 0 && (!xf || xf->mode != MV_X_RMSNORM || p.nb * 256 != tp->H ||
+        if (tp->in_call >= 0 && (!xf || xf->mode != MV_X_RMSNORM || p.nb * 256 != tp->H || !tp->ready ||
                                  p.nb * 64 > MT_XU * MtMix::NC * 32 || !tp->h_out ||
                                  (reinterpret_cast<uintptr_t>(tp->h_out) & 15)))
             return GB_EINVAL;

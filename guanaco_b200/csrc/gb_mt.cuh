@@ -26,16 +26,30 @@ __device__ __forceinline__ void mma_u8s8(int4& d, uint32_t a0, uint32_t a1, uint
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Two int8 limbs of x: x ~ s * (x0 + x1/256), |x0| <= 127, s = max|x| / 127
-// over the sub-block; v is x / s.
-__device__ __forceinline__ void limbs(float v, int& x0, int& x1) {
+// Three int8 limbs of x: x ~ s (x0 + x1 / 256 + x2 / 65536), |x0| <= 127,
+// s = max|x| / 127 over the 32-column sub-block; v is x / s.  Every step is
+// exact in fp32 (v - x0, the scalings by 256, t - rint(t)), so the limbs
+// carry v to 2^-17 (24 significant bits at the sub-block's maximum): x enters
+// the int8 tensor cores at fp32 precision.  A middle limb that rounds to 128
+// moves one unit into x0 (x0 <= 126 then), so it stays in int8.
+__device__ __forceinline__ void limbs(float v, int& x0, int& x1, int& x2) {
     const float r0 = rintf(v);
+    const float t1 = (v - r0) * 256.f;
+    const float r1 = rintf(t1);
+    const int r2 = (int)rintf((t1 - r1) * 256.f);
     x0 = (int)r0;
-    const int r1 = (int)rintf((v - r0) * 256.f);
-    x1 = r1 > 127 ? 127 : (r1 < -128 ? -128 : r1);
+    x1 = (int)r1;
+    if (x1 > 127) {   // 128 / 256 = 1 - 128 / 256
+        x1 -= 256;
+        x0 += 1;
+    }
+    x2 = r2 > 127 ? 127 : (r2 < -128 ? -128 : r2);
 }
-// The value a limb pair stands for, in units of the sub-block scale s.
-__device__ __forceinline__ float limb_value(int x0, int x1) { return fmaf((float)x1, 0.00390625f, (float)x0); }
+// The value a limb triple stands for, in units of the sub-block scale s
+// (exact: 24 bits).
+__device__ __forceinline__ float limb_value(int x0, int x1, int x2) {
+    return fmaf((float)x2, 1.0f / 65536.0f, fmaf((float)x1, 0.00390625f, (float)x0));
+}
 __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
     return (uint32_t)(a & 255) | ((uint32_t)(b & 255) << 8) | ((uint32_t)(c & 255) << 16) | ((uint32_t)(d & 255) << 24);
 }
@@ -128,12 +142,12 @@ __device__ __forceinline__ int mt_start(int c, int T, int n) { return (int)((lon
 __device__ __forceinline__ int mt_owner(int t, int T, int n) { return (int)(((long long)(t + 1) * n - 1) / T); }
 
 // x in shared memory (K = 256 nb columns):
-//   x0[K], x1[K]                int8 limbs, x ~ s * (x0 + x1 / 256)
+//   x0[K], x1[K], x2[K]         int8 limbs, x ~ s (x0 + x1 / 256 + x2 / 65536)
 //   f[K/64][4]                  per 64 columns {s lo, s hi, sum lo, sum hi} of
 //                               its two 32-column sub-blocks (s = max|x| / 127)
 //   s16[K/256][2][8]  (Q6_K)    sums of the 16-column sub-blocks 8n + 2G + h,
 //                               stored at [b][h][4n + G]
-__host__ __device__ constexpr int mt_xq_bytes(int K, bool s16) { return 2 * K + K / 4 + (s16 ? K / 4 : 0); }
+__host__ __device__ constexpr int mt_xq_bytes(int K, bool s16) { return 3 * K + K / 4 + (s16 ? K / 4 : 0); }
 constexpr int MT_ZERO = 256;   // zero line read by lanes without a B fragment
 
 // RMSNorm scale 1 / sqrt(mean(x^2) + eps) over the K columns, summed by the
@@ -175,14 +189,15 @@ __device__ __forceinline__ float mt_silu_mul(float g, float u) {
     return __fdividef(g, 1.0f + __expf(-fmaxf(g, -80.f))) * u;
 }
 
-// One float4 of x (columns 4t .. 4t + 3): transform, quantise to two int8
+// One float4 of x (columns 4t .. 4t + 3): transform, quantise to three int8
 // limbs per value against the 32-column sub-block's max |x|, and record the
 // sub-block scale and sum.  Lanes 8k .. 8k + 7 of a warp hold one sub-block.
 template <bool S16, class A>
 __device__ __forceinline__ void mt_quantise4(const A& a, int K, uint8_t* xq, int t, float4 v, float4 w, float rs) {
     uint32_t* p0 = reinterpret_cast<uint32_t*>(xq);
     uint32_t* p1 = reinterpret_cast<uint32_t*>(xq + K);
-    float* f = reinterpret_cast<float*>(xq + 2 * K);
+    uint32_t* p2 = reinterpret_cast<uint32_t*>(xq + 2 * K);
+    float* f = reinterpret_cast<float*>(xq + 3 * K);
     float* f16 = f + K / 16;
     if (a.xmode == MV_X_RMSNORM) {   // w * (x * r), the reference's rounding
         v = make_float4(__fmul_rn(w.x, __fmul_rn(v.x, rs)), __fmul_rn(w.y, __fmul_rn(v.y, rs)),
@@ -198,13 +213,14 @@ __device__ __forceinline__ void mt_quantise4(const A& a, int K, uint8_t* xq, int
         sm += __shfl_xor_sync(0xffffffffu, sm, o);
     }
     const float inv = mx > 0.f ? 127.f / mx : 0.f;
-    int a0, a1, b0, b1, c0, c1, d0, d1;
-    limbs(v.x * inv, a0, a1);
-    limbs(v.y * inv, b0, b1);
-    limbs(v.z * inv, c0, c1);
-    limbs(v.w * inv, d0, d1);
+    int a0, a1, a2, b0, b1, b2, c0, c1, c2, d0, d1, d2;
+    limbs(v.x * inv, a0, a1, a2);
+    limbs(v.y * inv, b0, b1, b2);
+    limbs(v.z * inv, c0, c1, c2);
+    limbs(v.w * inv, d0, d1, d2);
     p0[t] = pack4(a0, b0, c0, d0);
     p1[t] = pack4(a1, b1, c1, d1);
+    p2[t] = pack4(a2, b2, c2, d2);
     const float s = mx / 127.f;
     if (S16) {
         // 16-column sums of the QUANTISED values s (x0 + x1 / 256): the Q6_K
@@ -212,7 +228,7 @@ __device__ __forceinline__ void mt_quantise4(const A& a, int K, uint8_t* xq, int
         // the codes multiply the same x, and the quantisation error of x
         // reaches the result only through (q - 32), not through the codes'
         // mean (31.5), which would give every row a correlated error
-        float sq = (limb_value(a0, a1) + limb_value(b0, b1)) + (limb_value(c0, c1) + limb_value(d0, d1));
+        float sq = (limb_value(a0, a1, a2) + limb_value(b0, b1, b2)) + (limb_value(c0, c1, c2) + limb_value(d0, d1, d2));
         sq += __shfl_xor_sync(0xffffffffu, sq, 1);
         sq += __shfl_xor_sync(0xffffffffu, sq, 2);
         if ((t & 3) == 0) {   // 16-column sum: column c0 = 4t = 256 b + 128 n + 32 G + 16 h
@@ -239,16 +255,17 @@ __device__ __forceinline__ void mt_quantise32(uint8_t* xq, int K, int sb, int la
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         sm += __shfl_xor_sync(0xffffffffu, sm, o);
     }
-    float* f = reinterpret_cast<float*>(xq + 2 * K);
+    float* f = reinterpret_cast<float*>(xq + 3 * K);
     float* f16 = f + K / 16;
     const float inv = mx > 0.f ? 127.f / mx : 0.f;
-    int x0, x1;
-    limbs(v * inv, x0, x1);
+    int x0, x1, x2;
+    limbs(v * inv, x0, x1, x2);
     xq[32 * sb + lane] = (uint8_t)(x0 & 255);
     xq[K + 32 * sb + lane] = (uint8_t)(x1 & 255);
+    xq[2 * K + 32 * sb + lane] = (uint8_t)(x2 & 255);
     const float s = mx / 127.f;
     // 16-column sums of the quantised values (see mt_quantise4)
-    float sq = limb_value(x0, x1);
+    float sq = limb_value(x0, x1, x2);
 #pragma unroll
     for (int o = 1; o < 16; o <<= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
     if ((lane & 15) == 0) {   // 16-column sum: column c0 = 32 sb + lane = 256 b + 128 n + 32 G + 16 h
@@ -322,13 +339,6 @@ __device__ __forceinline__ bool ll_wait4(const uint2* p, unsigned ep, float4& ou
     return true;
 }
 
-// RMSNorm and quantisation in one pass (K / 4 <= MT_XU * NC * 32): every
-// float4 of x and of the weight is loaded once, the sum of squares reduced
-// (same order as mt_rms_scale, so the same scale), then the registers are
-// quantised.  One round trip to L2 instead of two.  scratch: NC floats.
-// With an exchange ex (ex->in_call >= 0, epoch ep): x is first replaced by
-// x + the sum over ranks of this rank's receive slots, and this CTA writes
-// its slice of that sum to ex->h_out.
 // The thread's float4s of the RMSNorm weight for mt_quantise_x_rms.  The
 // weight is a model constant, so the consumers load it before
 // griddepcontrol.wait: otherwise its HBM reads queue behind this launch's own
@@ -344,39 +354,69 @@ __device__ __forceinline__ void mt_load_norm_w(const A& a, int K, int tid, float
     }
 }
 
+// Tensor-parallel exchange on the way in (ex->in_call >= 0, epoch ep): this
+// CTA's slice of x plus the sum over ranks, in rank order, of this rank's
+// receive slots goes to ex->h_out; one release flag per CTA publishes it, and
+// once every CTA's flag carries ep the whole new hidden state is in h_out.
+// Each slot is read by one CTA only.  Returns the array to read x from.
+template <int NC>
+__device__ __forceinline__ const float4* mt_exchange_in(const float4* x4, int n4, int tid, const MvTp* ex,
+                                                        unsigned ep) {
+    const int world = ex->world;
+    const uint2* slots = static_cast<const uint2*>(ex->peers[ex->rank]) + (size_t)(ep & 1) * world * ex->H;
+    const int lo = (int)((long long)blockIdx.x * n4 / gridDim.x), hi = (int)((long long)(blockIdx.x + 1) * n4 / gridDim.x);
+    bool ok = true;
+    for (int t = lo + tid; t < hi; t += NC * 32) {
+        float4 v = __ldcg(x4 + t);
+        for (int q = 0; q < world; q++) {
+            float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (ok && !ll_wait4(slots + (size_t)q * ex->H + 4 * t, ep, f)) {
+                ok = false;
+                atomicExch(ex->err, (unsigned)(-GB_ETIMEOUT));
+            }
+            v = make_float4(v.x + f.x, v.y + f.y, v.z + f.z, v.w + f.w);
+        }
+        __stcg(reinterpret_cast<float4*>(ex->h_out) + t, v);
+    }
+    mt_consumer_sync<NC>();   // the CTA's slice is written
+    if (tid == 0)   // one release for the slice: fence at GPU scope, then the flag
+        asm volatile("fence.acq_rel.gpu;\n\tst.relaxed.gpu.global.u32 [%0], %1;" ::"l"(ex->ready + blockIdx.x), "r"(ep)
+                     : "memory");
+    if (tid < 32) {   // wait (bounded) until every CTA's flag has reached ep
+        for (int c = tid; c < (int)gridDim.x; c += 32) {
+            const unsigned* f = ex->ready + c;
+            if ((int)(ld_acquire(f) - ep) < 0) {
+                const uint64_t t0 = gtimer();
+                while ((int)(ld_acquire(f) - ep) < 0)
+                    if (gtimer() - t0 > MT_WAIT_NS) {
+                        atomicExch(ex->err, (unsigned)(-GB_ETIMEOUT));
+                        break;
+                    }
+            }
+        }
+    }
+    mt_consumer_sync<NC>();   // warp 0's acquires order every thread's reads below
+    return reinterpret_cast<const float4*>(ex->h_out);
+}
+
+// RMSNorm and quantisation in one pass (K / 4 <= MT_XU * NC * 32): every
+// float4 of x and of the weight is loaded once, the sum of squares reduced
+// (same order as mt_rms_scale, so the same scale), then the registers are
+// quantised.  One round trip to L2 instead of two.  scratch: NC floats.
+// With an exchange ex (ex->in_call >= 0, epoch ep), x is the hidden state
+// after the exchange (mt_exchange_in).
 template <bool S16, int NC, class A>
 __device__ __forceinline__ void mt_quantise_x_rms(const A& a, int K, uint8_t* xq, int tid, float* scratch,
                                                   const float4 (&w)[MT_XU], const MvTp* ex = nullptr,
                                                   unsigned ep = 0) {
     const int n4 = K / 4, nthr = NC * 32;
     const float4* x4 = reinterpret_cast<const float4*>(a.x);
+    if (ex) x4 = mt_exchange_in<NC>(x4, n4, tid, ex, ep);
     float4 v[MT_XU];
 #pragma unroll
     for (int j = 0; j < MT_XU; j++) {
         const int t = tid + j * nthr;
         v[j] = t < n4 ? __ldcg(x4 + t) : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-    if (ex) {
-        const int world = ex->world;
-        const uint2* slots = static_cast<const uint2*>(ex->peers[ex->rank]) + (size_t)(ep & 1) * world * ex->H;
-        const int lo = (int)((long long)blockIdx.x * n4 / gridDim.x), hi = (int)((long long)(blockIdx.x + 1) * n4 / gridDim.x);
-        bool ok = true;
-#pragma unroll
-        for (int j = 0; j < MT_XU; j++) {
-            const int t = tid + j * nthr;
-            if (t >= n4) continue;
-            float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int q = 0; q < world; q++) {
-                float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (ok && !ll_wait4(slots + (size_t)q * ex->H + 4 * t, ep, f)) {
-                    ok = false;
-                    atomicExch(ex->err, (unsigned)(-GB_ETIMEOUT));
-                }
-                sum = make_float4(sum.x + f.x, sum.y + f.y, sum.z + f.z, sum.w + f.w);
-            }
-            v[j] = make_float4(v[j].x + sum.x, v[j].y + sum.y, v[j].z + sum.z, v[j].w + sum.w);
-            if (t >= lo && t < hi) reinterpret_cast<float4*>(ex->h_out)[t] = v[j];
-        }
     }
     float ss = 0.f;
 #pragma unroll
@@ -404,11 +444,15 @@ __device__ __forceinline__ void mt_quantise_x_rms(const A& a, int K, uint8_t* xq
 // Per-lane constants of the tensor-core fragment map (g = lane / 4 is the
 // row within an 8-row half tile and the B column; c = lane % 4 the column
 // group).  Only lanes with c == g / 2 carry nonzero B fragments; the others
-// read a zero line, with a zero stride, so no lane branches.
+// read a zero line, with a zero stride, so no lane branches.  The first MMA of
+// a k-step takes limbs x0, x1 (columns 2c, 2c + 1), a second one the third
+// limb x2 (column 2c; column 2c + 1 zero) with the same A fragment.
 struct MtLane {
     int gq, c;
-    const uint8_t* xlb;   // B fragment base
+    const uint8_t* xlb;   // B fragment base (limb gq & 1 of column group c)
     int xstr;             // bytes per 256-column block (0 for zero lanes)
+    const uint8_t* x2b;   // B fragment base of the third limb (column 2c of the second MMA)
+    int x2str;            // its bytes per block (0: a zero column)
 };
 
 // ---------------------------------------------------------------- Q4_K stage
@@ -445,11 +489,12 @@ struct MtQ4KT {
         const int mfirst = TPW == 2 ? 0 : warp / KC;
         const int b = b0 + bl;
         if (b >= bend) return;
-        const float4* xfb = reinterpret_cast<const float4*>(xq + 2 * K) + c;
+        const float4* xfb = reinterpret_cast<const float4*>(xq + 3 * K) + c;
         const int sh8 = (c & 1) << 4;
         const uint32_t MW = c >= 2 ? 0x0F0Fu : 0u, MY = c >= 2 ? 0x3030u : 0x3F3Fu, SY = c >= 2 ? 2u : 0u;
         const uint4* xb = reinterpret_cast<const uint4*>(L.xlb + b * L.xstr);
         const uint4 bl0 = xb[0], bl1 = xb[1], bh0 = xb[2], bh1 = xb[3];
+        const uint8_t* x2 = L.x2b + b * L.x2str;   // third limb: lo sub-block at 8u, hi at 32 + 8u
         const float4 xf = xfb[b * 4];
         const float xlo = xf.x * 0.00390625f, xhi = xf.y * (0.00390625f * 0.0625f);
 #pragma unroll
@@ -465,6 +510,7 @@ struct MtQ4KT {
             const uint4 qb0 = *reinterpret_cast<const uint4*>(rb + 16 + 32 * c);
             const uint4 qb1 = *reinterpret_cast<const uint4*>(rb + 32 + 32 * c);
             int4 cl = make_int4(0, 0, 0, 0), chh = make_int4(0, 0, 0, 0);
+            int4 cl2 = make_int4(0, 0, 0, 0), ch2 = make_int4(0, 0, 0, 0);
 #pragma unroll
             for (int u = 0; u < 4; u++) {
                 const uint4& qa = (u >> 1) ? qa1 : qa0;
@@ -475,8 +521,17 @@ struct MtQ4KT {
                 const uint4& bhx = (u >> 1) ? bh1 : bh0;
                 const uint32_t l0 = (u & 1) ? blx.z : blx.x, l1 = (u & 1) ? blx.w : blx.y;
                 const uint32_t h0 = (u & 1) ? bhx.z : bhx.x, h1 = (u & 1) ? bhx.w : bhx.y;
-                mma_u8s8(cl, wa0 & 0x0F0F0F0Fu, wb0 & 0x0F0F0F0Fu, wa1 & 0x0F0F0F0Fu, wb1 & 0x0F0F0F0Fu, l0, l1);
-                mma_u8s8(chh, wa0 & 0xF0F0F0F0u, wb0 & 0xF0F0F0F0u, wa1 & 0xF0F0F0F0u, wb1 & 0xF0F0F0F0u, h0, h1);
+                const uint2 tl = *reinterpret_cast<const uint2*>(x2 + 8 * u);
+                const uint2 th = *reinterpret_cast<const uint2*>(x2 + 32 + 8 * u);
+                const uint32_t m0 = tl.x, m1 = tl.y, n0 = th.x, n1 = th.y;
+                const uint32_t la0 = wa0 & 0x0F0F0F0Fu, lb0 = wb0 & 0x0F0F0F0Fu, la1 = wa1 & 0x0F0F0F0Fu,
+                               lb1 = wb1 & 0x0F0F0F0Fu;
+                const uint32_t ha0 = wa0 & 0xF0F0F0F0u, hb0 = wb0 & 0xF0F0F0F0u, ha1 = wa1 & 0xF0F0F0F0u,
+                               hb1 = wb1 & 0xF0F0F0F0u;
+                mma_u8s8(cl, la0, lb0, la1, lb1, l0, l1);
+                mma_u8s8(chh, ha0, hb0, ha1, hb1, h0, h1);
+                mma_u8s8(cl2, la0, lb0, la1, lb1, m0, m1);
+                mma_u8s8(ch2, ha0, hb0, ha1, hb1, n0, n1);
             }
             // sub-blocks 2c (low nibbles) and 2c + 1 (high nibbles) of rows a, b
             float pab[2];
@@ -491,7 +546,9 @@ struct MtQ4KT {
                 const float2 dm = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
                 const int dl = (w ? cl.z : cl.x) * 256 + (w ? cl.w : cl.y);
                 const int dh = (w ? chh.z : chh.x) * 256 + (w ? chh.w : chh.y);
-                const float tt = (sc_lo * xlo) * (float)dl + (sc_hi * xhi) * (float)dh;
+                const float fl = fmaf((float)(w ? cl2.z : cl2.x), 0.00390625f, (float)dl);
+                const float fh = fmaf((float)(w ? ch2.z : ch2.x), 0.00390625f, (float)dh);
+                const float tt = (sc_lo * xlo) * fl + (sc_hi * xhi) * fh;
                 const float mm = m_lo * xf.z + m_hi * xf.w;
                 pab[w] = fmaf(dm.x, tt, -dm.y * mm);
             }
@@ -557,7 +614,8 @@ struct MtQ6K {
     static constexpr int ZUNIT = 8;      // blocks per tensor-map z unit
     static constexpr int BOXZ = 1;
     template <int MIS>
-    __device__ static __forceinline__ void tile(const uint8_t* blk_a, int c, const uint8_t* xb, const float* xf,
+    __device__ static __forceinline__ void tile(const uint8_t* blk_a, int c, const uint8_t* xb, const uint8_t* x2b,
+                                                const float* xf,
                                                 const float4 s16lo, const float4 s16hi, float fc, int selsc0,
                                                 int selsc1, float& acc_a, float& acc_b) {
         const uint8_t* blk_b = blk_a + 8 * RB;
@@ -591,8 +649,10 @@ struct MtQ6K {
                     default: A0 = q6_code<3>(la.x, ha.x); A1 = q6_code<3>(lb.x, hb.x); A2 = q6_code<3>(la.y, ha.y); A3 = q6_code<3>(lb.y, hb.y); break;
                 }
                 const uint2 bf = *reinterpret_cast<const uint2*>(xb + 128 * n + 32 * G);
-                int4 cc = make_int4(0, 0, 0, 0);
+                const uint2 bf2 = *reinterpret_cast<const uint2*>(x2b + 128 * n + 32 * G);
+                int4 cc = make_int4(0, 0, 0, 0), cc2 = make_int4(0, 0, 0, 0);
                 mma_u8s8(cc, A0, A1, A2, A3, bf.x, bf.y);
+                mma_u8s8(cc2, A0, A1, A2, A3, bf2.x, bf2.y);
                 const float xsg = ((G >> 1) ? ((G & 1) ? xs2.y : xs2.x) : ((G & 1) ? xs.y : xs.x)) * 0.00390625f;
                 const float s16 = n ? ((G == 0) ? s16hi.x : (G == 1) ? s16hi.y : (G == 2) ? s16hi.z : s16hi.w)
                                     : ((G == 0) ? s16lo.x : (G == 1) ? s16lo.y : (G == 2) ? s16lo.z : s16lo.w);
@@ -600,8 +660,8 @@ struct MtQ6K {
                 const int sel = (G & 1) ? selsc1 : selsc0;
                 const float sca = (float)prmt_sext(sa[2 * n + (G >> 1)], sel);
                 const float scb = (float)prmt_sext(sb[2 * n + (G >> 1)], sel);
-                const float ta = fmaf(xsg, (float)(cc.x * 256 + cc.y), fc * s16);
-                const float tb = fmaf(xsg, (float)(cc.z * 256 + cc.w), fc * s16);
+                const float ta = fmaf(xsg, fmaf((float)cc2.x, 0.00390625f, (float)(cc.x * 256 + cc.y)), fc * s16);
+                const float tb = fmaf(xsg, fmaf((float)cc2.z, 0.00390625f, (float)(cc.z * 256 + cc.w)), fc * s16);
                 ba = fmaf(sca, ta, ba);
                 bb = fmaf(scb, tb, bb);
             }
@@ -616,10 +676,11 @@ struct MtQ6K {
                                                int K, float acc_a[2], float acc_b[2]) {
         const int c = L.c;
         const uint8_t* xb = L.xlb + b * L.xstr;
-        const float* xf = reinterpret_cast<const float*>(xq + 2 * K) + b * 16;   // {s, s, sum, sum} x 4
+        const uint8_t* x2b = L.x2b + b * L.x2str;
+        const float* xf = reinterpret_cast<const float*>(xq + 3 * K) + b * 16;   // {s, s, sum, sum} x 4
         // xf holds per 64-column chunk {s lo, s hi, sum lo, sum hi}: the scale
         // of 32-column sub-block 4n + G is xf[8n + 4 (G >> 1) + (G & 1)]
-        const float* f16 = reinterpret_cast<const float*>(xq + 2 * K + K / 4) + b * 16 + (c >> 1) * 8;
+        const float* f16 = reinterpret_cast<const float*>(xq + 3 * K + K / 4) + b * 16 + (c >> 1) * 8;
         const float4 s16lo = *reinterpret_cast<const float4*>(f16);
         const float4 s16hi = *reinterpret_cast<const float4*>(f16 + 4);
         const float fc = (c & 1) ? 0.f : -32.f;   // the -32 offset of the codes, once per 16 columns
@@ -630,7 +691,7 @@ struct MtQ6K {
         const int selsc1 = b1 | ((b1 | 8) << 4) | ((b1 | 8) << 8) | ((b1 | 8) << 12);
         const int m = warp >> 3;
         const uint8_t* blk = stg + (m * 16 + L.gq) * RB + (warp & 7) * GB_Q6K_BYTES;
-        tile<MIS>(blk, c, xb, xf, s16lo, s16hi, fc, selsc0, selsc1, acc_a[m], acc_b[m]);
+        tile<MIS>(blk, c, xb, x2b, xf, s16lo, s16hi, fc, selsc0, selsc1, acc_a[m], acc_b[m]);
     }
     __device__ static __forceinline__ void consume(const uint8_t* stg, int b0, int bend, int warp, const MtLane& L,
                                                    const uint8_t* xq, int K, float acc_a[2], float acc_b[2]) {

@@ -22,18 +22,21 @@ def from_dev(t):
     return t.detach().cpu().numpy()
 
 
-def two_limb(x):
-    """The x the Q4_K / Q6_K matvecs multiply: per 32-column sub-block,
-    s = max|x| / 127 and x ~ s (x0 + x1 / 256) with x0 = rint(x / s) and
-    x1 = rint((x / s - x0) * 256) clamped to int8 -- a model of the device
-    quantiser (guanaco_b200/csrc/gb_mt.cuh), used to check that the kernels
+def device_x(x, group=32):
+    """The x the Q4_K / Q6_K matvecs multiply: per sub-block of `group`
+    columns, s = max|x| / 127 and x ~ s (x0 + x1 / 256 + x2 / 65536), the
+    three int8 limbs of v = x / s taken by rounding to nearest (a middle limb
+    of 128 carries into x0) -- a model of the device quantiser
+    (guanaco_b200/csrc/gb_mt.cuh: limbs), used to check that the kernels
     compute W . x~ up to fp32 rounding."""
-    x = np.asarray(x, np.float32).reshape(-1, 32)
+    x = np.asarray(x, np.float32).reshape(-1, group)
     mx = np.abs(x).max(axis=1, keepdims=True)
     with np.errstate(divide="ignore"):
         inv = np.where(mx > 0, np.float32(127) / mx, np.float32(0)).astype(np.float32)
     v = (x * inv).astype(np.float32)
     x0 = np.rint(v)
-    x1 = np.clip(np.rint((v - x0) * np.float32(256)), -128, 127)
+    t1 = ((v - x0) * np.float32(256)).astype(np.float32)
+    x1 = np.rint(t1)
+    x2 = np.clip(np.rint((t1 - x1) * np.float32(256)), -128, 127)
     s = (mx / np.float32(127)).astype(np.float32)
-    return ((x0 + x1 / 256.0) * s).astype(np.float32).ravel()
+    return ((x0 + x1 / 256.0 + x2 / 65536.0) * s).astype(np.float32).ravel()

@@ -4,7 +4,7 @@ with the reference CPU kernels)."""
 import numpy as np
 import pytest
 
-from tests.helpers import REL_L2_TOL, from_dev, rel_l2, to_dev, two_limb
+from tests.helpers import REL_L2_TOL, device_x, from_dev, rel_l2, to_dev
 
 pytestmark = pytest.mark.gpu
 
@@ -100,8 +100,8 @@ def test_matvec_parity(gb, oracle, cuda, name, rows, cols):
     assert np.all(np.isfinite(y))
     assert rel_l2(y, y_ref) <= REL_L2_TOL
     # far inside the tolerance: Q8_0 accumulates in fp32; Q4_K / Q6_K carry x
-    # as two int8 limbs per sub-block (~16 significant bits) into the tensor cores
-    assert rel_l2(y, y_ref) <= (1e-5 if dt == 2 else 1e-4)
+    # as three int8 limbs per sub-block (fp32's 24 bits) into the tensor cores
+    assert rel_l2(y, y_ref) <= 1e-5
     assert gb.lib().gb_device_error(1) == 0
 
 
@@ -110,9 +110,10 @@ def test_matvec_parity(gb, oracle, cuda, name, rows, cols):
 @pytest.mark.parametrize("pattern", ["every_subblock", "one_subblock", "channel_1e3_and_tiny"])
 def test_matvec_outlier_activations(gb, oracle, cuda, name, rows, cols, pattern):
     """Hidden states of real models carry outlier channels 100-1000x the
-    median.  The Q4_K / Q6_K matvecs carry x as two int8 limbs scaled per
-    32-column sub-block, so an outlier coarsens the other 31 values of its
-    sub-block; the result must stay inside the 1e-3 relative-L2 bound."""
+    median.  The Q4_K / Q6_K matvecs carry x as three int8 limbs scaled per
+    32-column sub-block, so an outlier sets the scale of its 31 neighbours;
+    with 24 bits they keep fp32-like precision (well inside the 1e-3
+    relative-L2 bound)."""
     dt = DTS[name]
     W = oracle.synth_blocks(dt, rows, cols, 99, rows + cols)
     x = oracle.synth_normal(cols, 99, 3).copy()
@@ -129,33 +130,39 @@ def test_matvec_outlier_activations(gb, oracle, cuda, name, rows, cols, pattern)
     assert np.all(np.isfinite(y))
     err = rel_l2(y, y_ref)
     assert err <= REL_L2_TOL, err
-    assert err <= (1e-5 if dt == 2 else 2e-4), err
+    assert err <= 1e-5, err
     assert gb.lib().gb_device_error(1) == 0
 
 
 @pytest.mark.parametrize("name", ["q4k", "q6k"])
 @pytest.mark.parametrize("rows,cols", [(100, 4096), (64, 14336), (1024, 4096), (77, 2048), (40, 5632)])
-@pytest.mark.parametrize("xkind", ["normal", "positive"])
-def test_matvec_is_exact_on_the_quantised_x(gb, oracle, cuda, name, rows, cols, xkind):
-    """The only approximation of the Q4_K / Q6_K matvecs is x carried as two
-    int8 limbs per 32-column sub-block: given that x~, the result is W . x~ up
-    to fp32 rounding.  A consumer that mixes x and x~ (e.g. the Q6_K -32 code
-    offset applied with the sum of the exact x) shows up here as a larger
-    error that is correlated across rows, which a decoder stack amplifies."""
+@pytest.mark.parametrize("xkind", ["normal", "positive", "outlier"])
+def test_matvec_is_exact_on_the_device_x(gb, oracle, cuda, name, rows, cols, xkind):
+    """The only approximation of the Q4_K / Q6_K matvecs is x carried as three
+    int8 limbs per sub-block (24 significant bits, as fp32): given that x~,
+    the result is W . x~ up to fp32 rounding, and it is as close to the
+    reference's fp32 result as fp32 arithmetic in another summation order
+    is.  A consumer that mixed x and x~ (e.g. the Q6_K -32 code offset
+    applied with the sum of the exact x) shows up here as an error
+    correlated across rows, which a decoder stack amplifies."""
     dt = DTS[name]
     W = oracle.synth_blocks(dt, rows, cols, 7, rows * 3 + cols)
     x = oracle.synth_normal(cols, 7, 11)
     if xkind == "positive":   # a common-mode component, as hidden states of the synthetic models have
         x = (np.abs(x) + 0.5).astype(np.float32)
+    elif xkind == "outlier":
+        x[5::32] *= 1e3
+    # the ring kernel (Q6_K rows that are not a multiple of 8 blocks) scales x per 16 columns
+    group = 16 if dt == 5 and (cols // 256) % 8 else 32
     _, y_exact = oracle.matvec(dt, W, rows, cols, x)
-    _, y_q = oracle.matvec(dt, W, rows, cols, two_limb(x))
+    _, y_q = oracle.matvec(dt, W, rows, cols, device_x(x, group))
     y = run_matvec(gb, cuda, dt, W, rows, cols, x)
-    err_q, err_x = rel_l2(y, y_q), rel_l2(y, y_exact)
-    assert err_q <= 2e-6 or err_q <= 0.2 * err_x, (err_q, err_x)
+    grow = max(1.0, np.sqrt(cols / 4096))   # fp32 rounding of the sums grows with sqrt(K)
+    assert rel_l2(y, y_q) <= 2e-6 * grow, rel_l2(y, y_q)
+    assert rel_l2(y, y_exact) <= 3e-6 * grow, rel_l2(y, y_exact)
+    # the errors summed over the rows are no larger than fp32 rounding gives
     e = y.astype(np.float64) - y_exact
-    eq = y_q.astype(np.float64) - y_exact
-    # the errors summed over the rows are no larger than the quantisation's own
-    assert abs(e.sum()) <= 2.0 * abs(eq.sum()) + 4.0 * np.sqrt(np.sum(eq * eq)) + 1e-6 * np.abs(y_exact).sum()
+    assert abs(e.sum()) <= 4.0 * np.sqrt(np.sum(e * e)) * max(1.0, np.sqrt(rows) / 8) + 1e-7 * np.abs(y_exact).sum()
 
 
 @pytest.mark.parametrize("rows,cols", [(3, 32), (9, 96), (31, 160), (300, 4128)])
