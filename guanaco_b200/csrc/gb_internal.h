@@ -75,18 +75,20 @@ struct MvXform {
 //   push_call >= 0: the launch's y rows (one matrix, no residual) go to slot
 //                   [rank] of every rank's buffer instead of y.
 //   in_call >= 0:   x (RMSNorm input) = x + sum over ranks, in rank order,
-//                   of this rank's slots of exchange in_call.  CTA c of the
-//                   launch sums only its slice of x (bounded wait for the
-//                   tags), writes that slice of the new hidden state to
-//                   h_out and releases ready[c] = epoch; every CTA then waits
-//                   (bounded) for all ready flags and reads the whole new
-//                   hidden state from h_out.  The slots are read once per
-//                   rank, not once per CTA.
+//                   of this rank's slots of exchange in_call (bounded waits
+//                   for the tags); h_out receives the new hidden state.
+//                   Slice form (ready != null): CTA c sums only its slice of
+//                   x, writes it to h_out and releases ready[c] = epoch;
+//                   every CTA then waits (bounded) for all ready flags and
+//                   reads the whole new hidden state from h_out, so the slots
+//                   are read once per rank.  Direct form (ready == null):
+//                   every CTA sums all slots itself and writes its slice of
+//                   h_out -- no grid-wide wait, world x H slot reads per CTA.
 struct MvTp {
     void* const* peers = nullptr;               // device array of the ranks' receive buffers
     const unsigned long long* step = nullptr;   // device step counter
     unsigned* err = nullptr;                    // device error word (GB_ETIMEOUT)
-    unsigned* ready = nullptr;                  // this rank's per-CTA slice flags (GB_MAX_SMS, zeroed once)
+    unsigned* ready = nullptr;                  // slice form: this rank's per-CTA flags (GB_MAX_SMS, zeroed once)
     int rank = 0, world = 1, calls = 0, H = 0;
     int push_call = -1, in_call = -1;
     float* h_out = nullptr;

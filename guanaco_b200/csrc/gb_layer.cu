@@ -461,6 +461,18 @@ static size_t tp_comm_bytes(int world, int H) {
     return (size_t)2 * world * H * sizeof(uint2) + 2 * world * sizeof(ArgPart) + 2 * world * sizeof(unsigned);
 }
 
+// Form of the hidden-state exchanges inside the matvecs: with few ranks every
+// CTA reads all ranks' slots itself (direct; world x H x 8 bytes of L2 reads
+// per CTA, no grid-wide wait); with more, each CTA reduces one slice and the
+// CTAs meet on per-CTA flags (slice; the slots are read once).
+// GB_TP_EXCHANGE=direct|slice in the environment overrides the choice.
+static bool tp_slice_exchange(int world) {
+    const char* e = getenv("GB_TP_EXCHANGE");
+    if (e && !strcmp(e, "direct")) return false;
+    if (e && !strcmp(e, "slice")) return true;
+    return world > 2;
+}
+
 extern "C" gb_model* gb_model_create_tp(const gb_model_config* cfg, int rank, int world) {
     if (!cfg) return nullptr;
     const gb_model_config& c = *cfg;
@@ -567,7 +579,7 @@ extern "C" gb_model* gb_model_create_tp(const gb_model_config* cfg, int rank, in
     m->tp.d_step = m->d_step;
     m->tp.calls = 2 * c.n_layers + 1;
     m->tp.err = m->err;
-    m->tp.ready = m->tp_ready;
+    m->tp.ready = tp_slice_exchange(world) ? m->tp_ready : nullptr;
     m->tp.part = m->part;
     m->tp.h[0] = m->hidden;
     m->tp.h[1] = m->hidden2;

@@ -1229,7 +1229,7 @@ int mv_launch_group(const MvPlan* const* ps, int n, const float* x, float* const
     if (tp && (tp->push_call >= 0 || tp->in_call >= 0)) {   // tensor-parallel exchange: check its shape
         if (!tp->peers || !tp->step || !tp->err || tp->world < 2 || tp->H <= 0) return GB_EINVAL;
         if (tp->push_call >= 0 && (n != 1 || (res && res[0]) || ps[0]->rows > tp->H)) return GB_EINVAL;
-        if (tp->in_call >= 0 && (!xf || xf->mode != MV_X_RMSNORM || p.nb * 256 != tp->H || !tp->ready ||
+        if (tp->in_call >= 0 && (!xf || xf->mode != MV_X_RMSNORM || p.nb * 256 != tp->H ||
                                  p.nb * 64 > MT_XU * MtMix::NC * 32 || !tp->h_out ||
                                  (reinterpret_cast<uintptr_t>(tp->h_out) & 15)))
             return GB_EINVAL;

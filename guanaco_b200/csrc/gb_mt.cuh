@@ -411,12 +411,36 @@ __device__ __forceinline__ void mt_quantise_x_rms(const A& a, int K, uint8_t* xq
                                                   unsigned ep = 0) {
     const int n4 = K / 4, nthr = NC * 32;
     const float4* x4 = reinterpret_cast<const float4*>(a.x);
-    if (ex) x4 = mt_exchange_in<NC>(x4, n4, tid, ex, ep);
     float4 v[MT_XU];
+    if (ex && !ex->ready) {
+        // direct form (few ranks): every CTA adds all ranks' slots to x
+        // itself, in rank order, and writes its slice of the sum to h_out
+        const int world = ex->world;
+        const uint2* slots = static_cast<const uint2*>(ex->peers[ex->rank]) + (size_t)(ep & 1) * world * ex->H;
+        const int lo = (int)((long long)blockIdx.x * n4 / gridDim.x), hi = (int)((long long)(blockIdx.x + 1) * n4 / gridDim.x);
+        bool ok = true;
 #pragma unroll
-    for (int j = 0; j < MT_XU; j++) {
-        const int t = tid + j * nthr;
-        v[j] = t < n4 ? __ldcg(x4 + t) : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int j = 0; j < MT_XU; j++) {
+            const int t = tid + j * nthr;
+            v[j] = t < n4 ? __ldcg(x4 + t) : make_float4(0.f, 0.f, 0.f, 0.f);
+            if (t >= n4) continue;
+            for (int q = 0; q < world; q++) {
+                float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (ok && !ll_wait4(slots + (size_t)q * ex->H + 4 * t, ep, f)) {
+                    ok = false;
+                    atomicExch(ex->err, (unsigned)(-GB_ETIMEOUT));
+                }
+                v[j] = make_float4(v[j].x + f.x, v[j].y + f.y, v[j].z + f.z, v[j].w + f.w);
+            }
+            if (t >= lo && t < hi) reinterpret_cast<float4*>(ex->h_out)[t] = v[j];
+        }
+    } else {
+        if (ex) x4 = mt_exchange_in<NC>(x4, n4, tid, ex, ep);   // slice form
+#pragma unroll
+        for (int j = 0; j < MT_XU; j++) {
+            const int t = tid + j * nthr;
+            v[j] = t < n4 ? __ldcg(x4 + t) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
     }
     float ss = 0.f;
 #pragma unroll

@@ -41,9 +41,11 @@ def _decode(dm, vocab_rows, ctx):
     return toks, logits
 
 
-def _worker(rank, world, port, q, fused, c, ctx):
+def _worker(rank, world, port, q, fused, c, ctx, exchange):
     if not fused:
         os.environ["GB_TP_FUSED"] = "0"
+    if exchange:
+        os.environ["GB_TP_EXCHANGE"] = exchange
     import torch
     import torch.distributed as dist
     import guanaco_b200 as gb
@@ -67,12 +69,16 @@ def _worker(rank, world, port, q, fused, c, ctx):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,fused,big", [(2, True, False), (2, False, False), (4, True, False), (4, True, True),
-                                             (8, True, True), (8, False, True)])
-def test_tp_decode_matches_one_gpu(gb, cuda, world, fused, big):
+@pytest.mark.parametrize("world,fused,big,exchange", [
+    (2, True, False, "direct"), (2, True, False, "slice"), (2, False, False, None), (2, True, True, None),
+    (4, True, False, None), (4, True, True, "slice"), (4, True, True, "direct"),
+    (8, True, True, None), (8, False, True, None)])
+def test_tp_decode_matches_one_gpu(gb, cuda, world, fused, big, exchange):
     """fused: the hidden-state exchanges run inside the wo / ffn_down matvecs
-    (push) and the next RMSNorm matvec (sum); otherwise each exchange is its
-    own all-reduce launch."""
+    (push) and the next RMSNorm matvec (sum), in the direct form (every CTA
+    sums all ranks' slots) or the slice form (each CTA sums one slice, the
+    CTAs meet on per-CTA flags); otherwise each exchange is its own
+    all-reduce launch."""
     if cuda.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     c, ctx = (CFG8, CTX8) if big else (CFG, CTX)
@@ -87,7 +93,7 @@ def test_tp_decode_matches_one_gpu(gb, cuda, world, fused, big):
     mpc = mp.get_context("spawn")
     q = mpc.Queue()
     port = _free_port()
-    procs = [mpc.Process(target=_worker, args=(r, world, port, q, fused, c, ctx)) for r in range(world)]
+    procs = [mpc.Process(target=_worker, args=(r, world, port, q, fused, c, ctx, exchange)) for r in range(world)]
     for p in procs:
         p.start()
     got = [q.get(timeout=300) for _ in range(world)]
