@@ -58,8 +58,18 @@ constexpr int ATTN_MIN_SPLIT_POS = 64;
 // Splits per KV head: one CTA per SM over all heads (every split then has
 // its whole share of K/V requested nearly at once), at least one 32-position
 // tile per split.
+// GB_ATTN_SPLITS=n in the environment caps the splits per KV head.
+static int attn_split_cap() {
+    static const int v = [] {
+        const char* e = getenv("GB_ATTN_SPLITS");
+        return e ? atoi(e) : 0;
+    }();
+    return v;
+}
+
 int attn_grid_splits(int n_kv, int max_seq) {
     int s = sm_count() / n_kv;
+    if (attn_split_cap() > 0 && s > attn_split_cap()) s = attn_split_cap();
     if (s < 1) s = 1;
     const int tiles = (max_seq + 31) / 32;
     return s < tiles ? s : tiles;
@@ -222,6 +232,10 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
         return;
     }
 
+    // q, k, v come from the previous kernel: with programmatic dependent
+    // launch the producer above already streams the cached K / V (written by
+    // earlier steps), the consumers wait here for the projections
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     // ---- RoPE on the consumer warps (reference rounding: a*c - b*s,
     // a*s + b*c, no contraction)
     constexpr int CT = ATTN_CWARPS * 32;   // consumer threads
@@ -502,28 +516,53 @@ k_attn_decode(const float* __restrict__ q, const float* __restrict__ knew, const
 
 // part: split partials; tickets: n_kv per-KV-head counters (zero between
 // calls); err: the error word (GB_EPOS when pos is outside [0, max_seq)).
+// pdl: launch with programmatic stream serialization, so the CTAs start (and
+// stream the cached K / V) while the previous kernel finishes.  Only for a
+// predecessor that writes neither the caches nor the position (the decode
+// step's q/k/v matvec): the producer reads both before griddepcontrol.wait.
 template <int HD, int GROUP>
 static cudaError_t launch_attn(const float* q, const float* k, const float* v, float* kc, float* vc,
                                const float* cs, const int* d_pos, int n_kv, int max_seq, float* out,
-                               float* part, unsigned* tickets, unsigned* err, uint8_t* xq_out, cudaStream_t st) {
+                               float* part, unsigned* tickets, unsigned* err, uint8_t* xq_out, cudaStream_t st,
+                               bool pdl) {
     using C = AttnCfg<HD, GROUP>;
     cudaError_t e = set_smem_once(reinterpret_cast<const void*>(k_attn_decode<HD, GROUP>), (int)C::SMEM);
     if (e != cudaSuccess) return e;
     const int G = attn_grid_splits(n_kv, max_seq);
-    k_attn_decode<HD, GROUP><<<n_kv * G, ATTN_THREADS, C::SMEM, st>>>(q, k, v, kc, vc, cs, d_pos, n_kv, max_seq, G,
-                                                                      out, part, tickets, err, xq_out);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(n_kv * G);
+    cfg.blockDim = dim3(ATTN_THREADS);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_attn_decode<HD, GROUP>, q, k, v, kc, vc, cs, d_pos, n_kv, max_seq, G, out,
+                              part, tickets, err, xq_out);
+}
+
+// GB_ATTN_PDL=1 in the environment launches the decode step's attention with
+// programmatic dependent launch.
+static bool attn_pdl() {
+    static const bool v = [] {
+        const char* e = getenv("GB_ATTN_PDL");
+        return e && e[0] == '1';
+    }();
+    return v;
 }
 
 // Both entry points: pick the instantiation for (head_dim, group).
 static int attn_dispatch(const float* q, const float* k, const float* v, float* kc, float* vc, const float* cs,
                          const int* d_pos, int n_heads, int n_kv, int head_dim, int max_seq, float* out,
-                         float* part, unsigned* tickets, unsigned* err, cudaStream_t st, uint8_t* xq_out = nullptr) {
+                         float* part, unsigned* tickets, unsigned* err, cudaStream_t st, uint8_t* xq_out = nullptr,
+                         bool pdl = false) {
     const int group = n_heads / n_kv;
     cudaError_t e = cudaErrorInvalidValue;
 #define GB_ATTN_CASE(HDV, GV)                                                                                       \
     if (head_dim == HDV && group == GV)                                                                             \
-        e = launch_attn<HDV, GV>(q, k, v, kc, vc, cs, d_pos, n_kv, max_seq, out, part, tickets, err, xq_out, st);
+        e = launch_attn<HDV, GV>(q, k, v, kc, vc, cs, d_pos, n_kv, max_seq, out, part, tickets, err, xq_out, st, pdl);
     GB_ATTN_CASE(128, 1) GB_ATTN_CASE(128, 2) GB_ATTN_CASE(128, 4) GB_ATTN_CASE(128, 8)
     GB_ATTN_CASE(64, 1) GB_ATTN_CASE(64, 2) GB_ATTN_CASE(64, 4) GB_ATTN_CASE(64, 8)
 #undef GB_ATTN_CASE
@@ -570,7 +609,7 @@ extern "C" size_t gb_attn_workspace_bytes(int n_heads, int n_kv, int head_dim, i
 
 int gb::attention_decode_xq(const float* q, const float* k, const float* v, float* k_cache, float* v_cache,
                             const float* rope_cs, const int* d_pos, int n_heads, int n_kv, int head_dim,
-                            int max_seq, float* out, void* ws, uint8_t* xq_out, cudaStream_t st) {
+                            int max_seq, float* out, void* ws, uint8_t* xq_out, cudaStream_t st, bool pdl) {
     if (!q || !k || !v || !k_cache || !v_cache || !rope_cs || !d_pos || !out || !ws) return GB_EINVAL;
     if (n_kv <= 0 || n_heads <= 0 || n_heads % n_kv || max_seq <= 0) return GB_EINVAL;
     if (xq_out && (((n_heads * head_dim) % 256) || (reinterpret_cast<uintptr_t>(xq_out) & 15))) return GB_EINVAL;
@@ -579,14 +618,14 @@ int gb::attention_decode_xq(const float* q, const float* k, const float* v, floa
     float* part = static_cast<float*>(ws);
     unsigned* tickets = reinterpret_cast<unsigned*>(part + (size_t)n_kv * G * group * attn_part_stride(head_dim));
     return attn_dispatch(q, k, v, k_cache, v_cache, rope_cs, d_pos, n_heads, n_kv, head_dim, max_seq, out, part,
-                         tickets, tickets + n_kv, st, xq_out);
+                         tickets, tickets + n_kv, st, xq_out, pdl && attn_pdl());
 }
 
 extern "C" int gb_attention_decode(const float* q, const float* k, const float* v, float* k_cache, float* v_cache,
                                    const float* rope_cs, const int* d_pos, int n_heads, int n_kv, int head_dim,
                                    int max_seq, float* out, void* ws, void* stream) {
     return attention_decode_xq(q, k, v, k_cache, v_cache, rope_cs, d_pos, n_heads, n_kv, head_dim, max_seq, out, ws,
-                               nullptr, static_cast<cudaStream_t>(stream));
+                               nullptr, static_cast<cudaStream_t>(stream), false);
 }
 
 extern "C" int gb_attention_decode_static(const float* q, const float* k, const float* v, float* k_cache,

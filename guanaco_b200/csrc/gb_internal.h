@@ -21,9 +21,11 @@ int attn_grid_splits(int n_kv, int max_seq);
 // for a matvec that reads it pre-quantised (MV_X_PREQ): the CTA that finishes
 // a KV head quantises each 32-column group of that head group's output
 // (mt_quantise32 layout, n_heads * head_dim columns, a multiple of 256).
+// pdl: the decode step's launch after its q/k/v matvec (which writes neither
+// the caches nor the position) may start early and stream the cached K / V.
 int attention_decode_xq(const float* q, const float* k, const float* v, float* k_cache, float* v_cache,
                         const float* rope_cs, const int* d_pos, int n_heads, int n_kv, int head_dim, int max_seq,
-                        float* out, void* ws, uint8_t* xq_out, cudaStream_t st);
+                        float* out, void* ws, uint8_t* xq_out, cudaStream_t st, bool pdl = false);
 
 // A prepared matvec: kernel choice, launch geometry and, for the TMA path,
 // the encoded tensor map of W.  Built once per weight matrix on the host

@@ -860,7 +860,7 @@ int enqueue_layer(const LayerArgs& a, cudaStream_t st) {
     // finishes a KV head quantises its 32-column groups of the output
     const bool aq = a.aq && tma(GB_WO) && a.mv[GB_WO]->cols == a.n_heads * a.hd;
     if ((rc = attention_decode_xq(a.q, a.k, a.v, a.kc, a.vc, a.rope, a.d_pos, a.n_heads, a.n_kv, a.hd, a.max_seq,
-                                  a.attn, a.attn_ws, aq ? a.aq : nullptr, st)))
+                                  a.attn, a.attn_ws, aq ? a.aq : nullptr, st, true)))
         return rc;
     MvXform woq;
     woq.mode = MV_X_PREQ;

@@ -643,6 +643,7 @@ struct MtArgs {
     // c1 > 0: CTAs [0, c1) take one whole group of n1 items each (the
     // leading matrices), the other CTAs split the rest (one item per group)
     int c1, n1;
+    int l2pf;           // boxes past the ring prefetched into L2 at the start
 };
 
 // y row of matrix m: to y, or (tensor-parallel push) as {value, epoch} to
@@ -736,6 +737,18 @@ __global__ void __launch_bounds__((F::NC + 1) * 32, 1) k_mvt(const __grid_consta
                 // z: 16-block units of blocks (Q4_K), 8-block runs (Q6_K)
                 mbs_expect(bar_full + 8 * s, q6 ? MtQ6K::ITEM : MtQ4K::ITEM);
                 tma_load_3d(sbase + s * F::STG, tm, 0, g * MT_GR, q6 ? it : it * MtQ4K::IG, bar_full + 8 * s);
+                if (i == S - 1 && a.l2pf > 0) {
+                    // the ring is full and the consumers are still waiting
+                    // for x: pull this CTA's next boxes into L2 so HBM keeps
+                    // streaming through the wait
+                    for (int k = 1; k <= a.l2pf && t + k < t1; k++) {
+                        int m2, g2, it2;
+                        mt_locate(a, t + k, m2, g2, it2);
+                        const CUtensorMap* tm2p = m2 == 0 ? &tm0 : (m2 == 1 ? &tm1 : &tm2);
+                        const bool q62 = MIXED ? a.fmt[m2] != 0 : FQ6;
+                        tma_prefetch_3d(tm2p, 0, g2 * MT_GR, q62 ? it2 : it2 * MtQ4K::IG);
+                    }
+                }
             }
             // do not retire while a box is still landing in this CTA's ring
             for (int k = i > S ? i - S : 0; ok && k < i; k++) ok = mbs_wait(bar_empty + 8 * (k % S), (k / S) & 1, &g_gb_device_err);
@@ -1140,6 +1153,16 @@ static bool pdl_allowed() {
     return ok;
 }
 
+// GB_MV_L2PF=k in the environment: at its start, once its ring is full,
+// each CTA also prefetches its next k boxes into L2.
+static int mv_l2_prefetch() {
+    static const int v = [] {
+        const char* e = getenv("GB_MV_L2PF");
+        return e ? atoi(e) : 0;
+    }();
+    return v;
+}
+
 static int mv_check_xform(const MvXform* xf, bool tma) {
     const int xmode = xf ? xf->mode : MV_X_NONE;
     if (xf && (xf->swq_out || xf->swq_tk) && !tma) return GB_EINVAL;
@@ -1304,6 +1327,7 @@ int mv_launch_group(const MvPlan* const* ps, int n, const float* x, float* const
         }
     }
     a.S = mixed ? mix_stages(p.nb * 256) : p.S;
+    a.l2pf = mv_l2_prefetch();
     if (a.S < 2) return GB_ELIMIT;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.ncta);

@@ -116,6 +116,11 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* map, int x
         ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(z), "r"(bar)
         : "memory");
 }
+// L2 prefetch of one tensor-map box (no shared memory, no completion).
+__device__ __forceinline__ void tma_prefetch_3d(const void* map, int x, int y, int z) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(map), "r"(x), "r"(y), "r"(z)
+                 : "memory");
+}
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ unsigned atom_add_acq_rel(unsigned* p, unsigned v) {

@@ -76,6 +76,52 @@ def ref_available() -> bool:
     return os.path.exists(os.path.join(HERE, "_ref", "libref.so"))
 
 
+def _bind_harness(R) -> None:
+    vp, i, sz = C.c_void_p, C.c_int, C.c_size_t
+    R.ref_set_threads.argtypes = [i]
+    R.ref_matvec.argtypes = [i, vp, i, i, sz, vp, vp]
+    R.ref_matvec.restype = i
+    R.ref_dequant.argtypes = [i, vp, i, vp]
+    R.ref_dequant.restype = i
+    R.ref_attention_step.argtypes = [vp, vp, vp, vp, vp, i, i, i, i, i, vp]
+    R.ref_attention_step.restype = i
+    R.ref_model_create.argtypes = [vp]
+    R.ref_model_create.restype = vp
+    R.ref_model_kv.argtypes = [vp, i, i]
+    R.ref_model_kv.restype = C.POINTER(C.c_float)
+    R.ref_model_forward.argtypes = [vp, i, i, vp]
+    R.ref_model_forward.restype = i
+    R.ref_model_forward_n.argtypes = [vp, vp, i, i, vp]
+    R.ref_model_forward_n.restype = i
+    R.ref_model_destroy.argtypes = [vp]
+
+
+_dropin = None
+
+
+def dropin_available() -> bool:
+    return os.path.exists(os.path.join(HERE, "_ref", "libref_dropin.so"))
+
+
+def dropin() -> C.CDLL:
+    """The reference engine compiled with -DUSE_CUDA=1 against
+    libguanaco_b200.so (oracle/_ref/libref_dropin.so): its forward() runs the
+    drop-in cuda_transformer_layer_gpu once ref_model_to_gpu has moved a
+    model's layers to the device.  Loaded privately (RTLD_LOCAL), so its copy
+    of the reference symbols never mixes with libref.so's."""
+    global _dropin
+    if _dropin is None:
+        path = os.path.join(HERE, "_ref", "libref_dropin.so")
+        if not os.path.exists(path):
+            raise FileNotFoundError("oracle/_ref/libref_dropin.so not built (reference tree absent)")
+        R = C.CDLL(path, mode=os.RTLD_LOCAL)
+        _bind_harness(R)
+        R.ref_model_to_gpu.argtypes = [C.c_void_p, C.c_int]
+        R.ref_model_to_gpu.restype = C.c_int
+        _dropin = R
+    return _dropin
+
+
 def ref() -> C.CDLL:
     """The reference's own CPU kernels (oracle/_ref/libref.so)."""
     global _ref
@@ -83,7 +129,7 @@ def ref() -> C.CDLL:
         path = os.path.join(HERE, "_ref", "libref.so")
         if not os.path.exists(path):
             raise FileNotFoundError("oracle/_ref/libref.so not built (reference tree absent)")
-        R = C.CDLL(path)
+        R = C.CDLL(path, mode=os.RTLD_LOCAL)
         vp, i, sz = C.c_void_p, C.c_int, C.c_size_t
         R.ref_set_threads.argtypes = [i]
         R.ref_matvec.argtypes = [i, vp, i, i, sz, vp, vp]
@@ -99,6 +145,8 @@ def ref() -> C.CDLL:
         R.ref_model_forward.argtypes = [vp, i, i, vp]
         R.ref_model_forward.restype = i
         R.ref_model_destroy.argtypes = [vp]
+        R.ref_model_forward_n.argtypes = [vp, vp, i, i, vp]
+        R.ref_model_forward_n.restype = i
         _ref = R
     return _ref
 
@@ -232,9 +280,12 @@ class _ModelDesc(C.Structure):
 
 
 class RefModel:
-    """The reference forward() (engine.c:559-594) over caller-owned weights."""
+    """The reference forward() (engine.c:559-594) over caller-owned weights.
+    lib: the harness to run it in (ref() by default; dropin() for the engine
+    built with -DUSE_CUDA=1, see to_gpu)."""
 
-    def __init__(self, model):
+    def __init__(self, model, lib=None):
+        self._L = lib or ref()
         m = model
         n = m.n_layers
         self._keep = m
@@ -248,24 +299,40 @@ class RefModel:
                        m.embedding.ctypes.data, m.emb_dtype, m.rms_final.ctypes.data,
                        m.lm_head.ctypes.data, m.lm_dtype)
         self._d = d
-        self.h = ref().ref_model_create(C.byref(d))
+        self.h = self._L.ref_model_create(C.byref(d))
         if not self.h:
             raise MemoryError("ref_model_create failed")
 
     def kv(self, layer: int, which_v: int, count: int) -> np.ndarray:
-        p = ref().ref_model_kv(self.h, layer, which_v)
+        p = self._L.ref_model_kv(self.h, layer, which_v)
         return np.ctypeslib.as_array(p, shape=(count,))
 
     def forward(self, token: int, pos: int) -> np.ndarray:
         logits = np.empty(self._keep.vocab, dtype=np.float32)
-        rc = ref().ref_model_forward(self.h, token, pos, _p(logits))
+        rc = self._L.ref_model_forward(self.h, token, pos, _p(logits))
         if rc != 0:
             raise RuntimeError("ref forward failed")
         return logits
 
+    def forward_tokens(self, tokens, pos: int) -> np.ndarray:
+        """forward() over a prompt (T = len(tokens) <= 16): logits of the last."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        logits = np.empty(self._keep.vocab, dtype=np.float32)
+        rc = self._L.ref_model_forward_n(self.h, _p(t), t.size, pos, _p(logits))
+        if rc != 0:
+            raise RuntimeError("ref forward failed")
+        return logits
+
+    def to_gpu(self, threads: int) -> None:
+        """Engine CUDA set-up (dropin() harness only): device copies of the
+        layer matrices and the kernel table of backend_create(AUTO)."""
+        rc = self._L.ref_model_to_gpu(self.h, threads)
+        if rc != 0:
+            raise RuntimeError(f"ref_model_to_gpu rc={rc}")
+
     def close(self):
         if self.h:
-            ref().ref_model_destroy(self.h)
+            self._L.ref_model_destroy(self.h)
             self.h = None
 
     def __del__(self):

@@ -17,7 +17,8 @@ import sys
 import time
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-sys.path.insert(0, ROOT)
+# run as a script, this file's directory would shadow the oracle package
+sys.path = [ROOT] + [p for p in sys.path if os.path.abspath(p or ".") != os.path.join(ROOT, "oracle")]
 
 LLAMA8B = dict(hidden_dim=4096, n_heads=32, n_kv_heads=8, n_layers=32, ff_dim=14336, vocab_size=128256)
 SEED = 1234

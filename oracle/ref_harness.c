@@ -184,6 +184,7 @@ typedef struct {
     KVCache* kv;
     Scratch* scr;
     KernelVTable kt;
+    void* backend;   /* the engine's Backend (USE_CUDA build, after ref_model_to_gpu) */
 } ref_model;
 
 static size_t q_bytes(int dtype, int rows, int cols) {
@@ -244,10 +245,13 @@ void* ref_model_create(const ref_model_desc* d) {
     m->arena = arena_create(kv_bytes + (4u << 20));
     m->kv = m->arena ? kv_cache_create(m->arena, c, d->max_seq) : NULL;
     /* forward() resets the scratch once per call, so it must hold every
-     * layer's temporaries (engine.c:354-546) plus the final norm and logits. */
-    const size_t per_layer = (size_t)(10 * d->H + 2 * kv_dim + 2 * d->ff + d->max_seq + 2 * d->hd) * sizeof(float)
-                             + 32 * (sizeof(Tensor) + 128);
-    size_t scr = (size_t)d->n_layers * per_layer + (size_t)(4 * d->H + 2 * d->vocab) * sizeof(float) + (1u << 20);
+     * layer's temporaries (engine.c:354-546) plus the final norm and logits,
+     * for prompts of up to REF_MAX_T tokens (ref_model_forward_n). */
+    enum { REF_MAX_T = 16 };
+    const size_t per_layer = (size_t)REF_MAX_T * (10 * d->H + 2 * kv_dim + 2 * d->ff + d->max_seq + 2 * d->hd) *
+                                 sizeof(float) + 32 * (sizeof(Tensor) + 128);
+    size_t scr = (size_t)d->n_layers * per_layer + (size_t)REF_MAX_T * (4 * d->H + 2 * d->vocab) * sizeof(float) +
+                 (1u << 20);
     m->scr = scratch_create(scr);
     m->kt = ref_vtable();
     if (!m->kv || !m->scr) return NULL;
@@ -270,9 +274,81 @@ int ref_model_forward(void* h, int token, int pos, float* logits) {
     return 0;
 }
 
+#ifdef USE_CUDA
+/* The engine's CUDA set-up (src/engine/loader.c:701-716 and
+ * src/engine/generate.c:55-70), applied to the harness model: every layer
+ * matrix gets a device copy through cuda_upload_weight and
+ * device_residency = 1, and the kernel table comes from backend_create with
+ * BACKEND_AUTO, as the engine makes it.  forward() then takes the
+ * cuda_transformer_layer_gpu branch of transformer_layer (engine.c:314-350)
+ * for every layer, back to back, and the output head goes through the
+ * backend's matvec slot (engine.c:590).  Returns 0 when the CUDA backend was
+ * selected and every layer matrix is on the device. */
+extern void* cuda_upload_weight(const void* host, size_t bytes);
+extern void cuda_finish_layer(void);
+#include "backend_internal.h"
+int ref_model_to_gpu(void* h, int threads) {
+    ref_model* m = (ref_model*)h;
+    int resident = 0;
+    for (int l = 0; l < m->mw.config.n_layers; l++) {
+        LayerWeights* L = &m->mw.layers[l];
+        Tensor* ts[7] = {L->wq, L->wk, L->wv, L->wo, L->w_gate, L->w_up, L->w_down};
+        for (int i = 0; i < 7; i++) {
+            void* d = cuda_upload_weight(ts[i]->data, ts[i]->byte_size);
+            if (d) {
+                ts[i]->d_data = d;
+                ts[i]->device_residency = 1;
+                resident++;
+            }
+        }
+    }
+    BackendConfig cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.kind = BACKEND_AUTO;
+    cfg.threads = threads;
+    cfg.device_id = 0;
+    cfg.n_gpu_layers = m->mw.config.n_layers;
+    Backend* b = backend_create(&cfg);
+    if (!b) return -1;
+    m->backend = b;
+    m->kt = *backend_kernels(b);
+    /* glue slots the library could not bind (it was loaded before these
+     * kernels were): the engine's own CPU kernels, as the CUDA backend binds
+     * them when linked into the engine */
+    KernelVTable cpu = ref_vtable();
+    if (!m->kt.gemm_f32) m->kt.gemm_f32 = cpu.gemm_f32;
+    if (!m->kt.gemm_f32_nn) m->kt.gemm_f32_nn = cpu.gemm_f32_nn;
+    if (!m->kt.rmsnorm) m->kt.rmsnorm = cpu.rmsnorm;
+    if (!m->kt.softmax_inplace) m->kt.softmax_inplace = cpu.softmax_inplace;
+    if (!m->kt.silu_inplace) m->kt.silu_inplace = cpu.silu_inplace;
+    if (!m->kt.rope) m->kt.rope = cpu.rope;
+    if (!m->kt.residual_add) m->kt.residual_add = cpu.residual_add;
+    if (!m->kt.elemwise_mul) m->kt.elemwise_mul = cpu.elemwise_mul;
+    return (backend_kind(b) == BACKEND_CUDA && resident == 7 * m->mw.config.n_layers) ? 0 : -2;
+}
+#endif
+
+/* forward() over n prompt tokens at positions pos .. pos + n - 1 (T = n:
+ * the engine's prefill, engine.c:559-594 and 353-554); logits of the last. */
+int ref_model_forward_n(void* h, const int* tokens, int n, int pos, float* logits) {
+    ref_model* m = (ref_model*)h;
+    int* t = (int*)malloc((size_t)n * sizeof(int));
+    if (!t) return -1;
+    memcpy(t, tokens, (size_t)n * sizeof(int));
+    Tensor* lg = forward(&m->mw, m->kv, m->scr, t, n, pos, &m->kt);
+    free(t);
+    if (!lg) return -1;
+    memcpy(logits, lg->data, (size_t)m->mw.config.vocab_size * sizeof(float));
+    return 0;
+}
+
 void ref_model_destroy(void* h) {
     ref_model* m = (ref_model*)h;
     if (!m) return;
+#ifdef USE_CUDA
+    cuda_finish_layer();
+    if (m->backend) backend_destroy((Backend*)m->backend);
+#endif
     if (m->kv) kv_cache_destroy(m->kv);
     if (m->arena) arena_destroy(m->arena);
     if (m->scr) scratch_destroy(m->scr);
