@@ -97,6 +97,7 @@ SIGNATURES = {
     "gb_matvec": (_i, [_i, _vp, _i, _i, _vp, _vp, _vp, _vp]),
     "gb_matvec_group": (_i, [_i, _vp, _vp, _vp, _i, _vp, _vp, _vp]),
     "gb_matvec_host": (_i, [_i, _vp, _i, _i, _vp, _vp]),
+    "gb_vtable_cache_clear": (_i, []),
     "gb_device_error": (_i, [_i]),
     "gb_dequant": (_i, [_i, _vp, _sz, _vp, _vp]),
     "gb_synth_blocks": (_i, [_i, _vp, _sz, _u64, _u64, _vp]),

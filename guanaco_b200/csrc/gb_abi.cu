@@ -58,9 +58,12 @@ struct Ctx {
     struct CachedWeight {
         void* d = nullptr;
         size_t bytes = 0;
-        uint64_t sig = 0;   // checksum of sampled bytes (detects a reused host address)
+        uint64_t sig = 0;        // checksum of sampled bytes (detects a reused host address)
+        uint64_t last_use = 0;   // use clock at the last call (least recently used goes first)
     };
     std::unordered_map<const void*, CachedWeight> weight_cache;
+    size_t weight_cache_bytes = 0;
+    uint64_t use_clock = 0;
     // prepared matvecs keyed by device weight pointer, and their workspace
     std::unordered_map<const void*, MvPlan> plans;
     void* mv_ws = nullptr;
@@ -264,6 +267,17 @@ static int ensure_mv_ws(Ctx* c, size_t need) {
 }
 
 // FNV-1a over 64 words spread evenly through the buffer (and its last word).
+// Byte cap of the vtable slots' cache of uploaded weights:
+// GB_VTABLE_CACHE_MB in the environment, default 16384 (16 GiB).
+static size_t vtable_cache_cap() {
+    static const size_t v = [] {
+        const char* e = getenv("GB_VTABLE_CACHE_MB");
+        const long mb = e ? atol(e) : 16384;
+        return (size_t)(mb > 0 ? mb : 16384) << 20;
+    }();
+    return v;
+}
+
 static uint64_t sample_signature(const void* p, size_t n) {
     const unsigned char* b = static_cast<const unsigned char*>(p);
     uint64_t h = 1469598103934665603ull ^ n;
@@ -337,27 +351,57 @@ extern "C" __attribute__((visibility("hidden"))) int gb_vtable_matvec(int dtype,
     if (!dW) {
         // A cached copy is reused only for the same size and sampled content:
         // a host buffer freed and reallocated at the same address must not
-        // pick up (or over-read) the old device copy.
+        // pick up (or over-read) the old device copy.  An edit in place that
+        // misses the sampled bytes is not seen: such callers clear the cache
+        // (gb_vtable_cache_clear).  The cache holds at most
+        // vtable_cache_cap() bytes; the least recently used copies go first.
         const uint64_t sig = sample_signature(host_data, need);
         Ctx::CachedWeight& e = c->weight_cache[host_data];
         if (!e.d || e.bytes != need || e.sig != sig) {
+            cudaStreamSynchronize(c->st);   // no launch still reads a copy freed below
             if (e.d) {
-                cudaStreamSynchronize(c->st);
                 cudaFree(e.d);
+                c->weight_cache_bytes -= e.bytes;
                 e = Ctx::CachedWeight{};
             }
+            while (c->weight_cache_bytes + need > vtable_cache_cap() && c->weight_cache_bytes > 0) {
+                auto lru = c->weight_cache.end();
+                for (auto it = c->weight_cache.begin(); it != c->weight_cache.end(); ++it)
+                    if (it->second.d && (lru == c->weight_cache.end() || it->second.last_use < lru->second.last_use))
+                        lru = it;
+                if (lru == c->weight_cache.end()) break;
+                cudaFree(lru->second.d);
+                c->weight_cache_bytes -= lru->second.bytes;
+                c->weight_cache.erase(lru);
+            }
+            Ctx::CachedWeight& f = c->weight_cache[host_data];   // the erase above may have moved it
             void* d = upload_bytes(host_data, need, c->st);
             if (!d) {
                 c->weight_cache.erase(host_data);
                 return GB_ENOMEM;
             }
-            e.d = d;
-            e.bytes = need;
-            e.sig = sig;
+            f.d = d;
+            f.bytes = need;
+            f.sig = sig;
+            c->weight_cache_bytes += need;
         }
-        dW = e.d;
+        Ctx::CachedWeight& g = c->weight_cache[host_data];
+        g.last_use = ++c->use_clock;
+        dW = g.d;
     }
     return matvec_hostio(c, dtype, dW, rows, cols, x, y);
+}
+
+extern "C" int gb_vtable_cache_clear(void) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    Ctx* c = ctx();
+    if (!c) return GB_ECUDA;
+    cudaStreamSynchronize(c->st);
+    for (auto& kv : c->weight_cache)
+        if (kv.second.d) cudaFree(kv.second.d);
+    c->weight_cache.clear();
+    c->weight_cache_bytes = 0;
+    return GB_OK;
 }
 
 // Native host-buffer entry (same path as the vtable slots, device W).

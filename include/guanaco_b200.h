@@ -158,16 +158,28 @@ int gb_attention_decode(const float* q, const float* k, const float* v,
                         const int* d_pos, int n_heads, int n_kv, int head_dim, int max_seq,
                         float* out, void* ws, void* stream);
 
+/* Frees every device copy the vtable matvec slots made of weights that were
+ * never uploaded (the engine's lm_head).  Those copies are keyed by host
+ * pointer and checked against the byte size and a checksum of sampled
+ * bytes; a caller that edits a weight in place after its first use calls
+ * this before the next matvec.  The cache also drops its least recently used
+ * copies above GB_VTABLE_CACHE_MB (environment, default 16384 MiB).
+ * Synchronises the library's stream.  No counterpart in the reference, whose
+ * CUDA backend fell back to the CPU for such tensors. */
+int gb_vtable_cache_clear(void);
+
 /* gb_attention_decode without a caller workspace and without allocating:
  * the split-K scratch is a file-scope device array of GB_ATTN_STATIC_BYTES
  * (4 MiB), resolved with cudaGetSymbolAddress once per device.  Returns
  * GB_ELIMIT when the configuration needs more (partials of n_kv * splits *
- * (n_heads / n_kv) * (head_dim + 2) floats above 4 MiB - 4 KiB, or n_kv >= 1023).
+ * (n_heads / n_kv) * (head_dim + 4) floats above 4 MiB - 4 KiB, or n_kv >= 1023).
  * The scratch is shared by every call on the device: calls that overlap in
  * time (other streams, other threads) race and must not be issued.  The first
  * call on a device does the symbol lookup, so make it before any stream
- * capture.  A position outside [0, max_seq) is reported through
- * gb_attention_static_error (after synchronising the stream). */
+ * capture.  The looked-up address belongs to the device's primary context: a
+ * process that calls cudaDeviceReset on a device must not call this entry
+ * point on that device afterwards.  A position outside [0, max_seq) is
+ * reported through gb_attention_static_error (after synchronising the stream). */
 #define GB_ATTN_STATIC_BYTES (4u << 20)
 int gb_attention_decode_static(const float* q, const float* k, const float* v,
                                float* k_cache, float* v_cache, const float* rope_cs,

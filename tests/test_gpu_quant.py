@@ -385,6 +385,34 @@ def test_vtable_host_cache_detects_reuse(gb, oracle, cuda):
         be.close()
 
 
+def test_vtable_cache_clear_after_in_place_edit(gb, oracle, cuda, monkeypatch):
+    """An edit in place that the sampled checksum cannot see (one block of one
+    row) is picked up after gb_vtable_cache_clear; the cache also evicts
+    least recently used copies above its byte cap."""
+    be = gb.CudaBackend()
+    try:
+        rows, cols = 64, 4096
+        W = oracle.synth_blocks(4, rows, cols, 31, 1)
+        x = oracle.synth_normal(cols, 31, 2)
+        t = gb.make_tensor(4, W, rows, cols)
+        y = np.zeros(rows, np.float32)
+        assert be.matvec(t, x, y) == 0
+        blk = 144 * (cols // 256)
+        W[7 * blk + 20: 7 * blk + 40] ^= 0x5A   # row 7, inside its first block's quants
+        assert gb.lib().gb_vtable_cache_clear() == 0
+        assert be.matvec(t, x, y) == 0
+        assert rel_l2(y, oracle.matvec(4, W, rows, cols, x)[1]) <= 1e-5
+        # many distinct tensors: every result stays right while older copies are evicted
+        for i in range(6):
+            Wi = oracle.synth_blocks(4, rows, cols, 31, 10 + i)
+            ti = gb.make_tensor(4, Wi, rows, cols)
+            assert be.matvec(ti, x, y) == 0
+            assert rel_l2(y, oracle.matvec(4, Wi, rows, cols, x)[1]) <= 1e-5
+    finally:
+        be.close()
+        gb.lib().gb_vtable_cache_clear()
+
+
 @pytest.mark.parametrize("dts,rows,cols", [
     ((4, 4), (14336, 14336), 4096),        # gate / up
     ((4, 4, 5), (4096, 1024, 1024), 4096),   # q / k / v: Q6_K v, mixed formats in one launch
