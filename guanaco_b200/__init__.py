@@ -99,6 +99,8 @@ SIGNATURES = {
     "gb_matvec_host": (_i, [_i, _vp, _i, _i, _vp, _vp]),
     "gb_vtable_cache_clear": (_i, []),
     "gb_device_error": (_i, [_i]),
+    "gb_gemm": (_i, [_i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
+    "gb_gemm_error": (_i, [_i]),
     "gb_dequant": (_i, [_i, _vp, _sz, _vp, _vp]),
     "gb_synth_blocks": (_i, [_i, _vp, _sz, _u64, _u64, _vp]),
     "gb_synth_normal": (_i, [_vp, _sz, _u64, _u64, _vp]),
@@ -183,6 +185,11 @@ def matvec_group(dtypes, Ws, rows, cols, x, ys, stream=None) -> None:
     rw = (C.c_int * n)(*rows)
     yp = (C.c_void_p * n)(*[_ptr(v) for v in ys])
     check("gb_matvec_group", lib().gb_matvec_group(n, dt, wp, rw, cols, _ptr(x), yp, _stream(stream)))
+
+
+def gemm(dtype, W, X, Y, N, K, T, R=None, stream=None) -> None:
+    """Y[t][n] = sum_k X[t][k] W[n][k] (+ R[t][n]) on the tensor cores (prefill)."""
+    check("gb_gemm", lib().gb_gemm(dtype, _ptr(W), _ptr(X), _ptr(Y), _ptr(R), N, K, T, _stream(stream)))
 
 
 def dequant(dtype, blocks, nblocks, out, stream=None) -> None:

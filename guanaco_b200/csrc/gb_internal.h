@@ -107,6 +107,12 @@ int mv_launch_group(const MvPlan* const* ps, int n, const float* x, float* const
 bool mt_encode_view(void* map128, int dtype, const void* W, int rows, int nb, int boxz);
 bool mt_encode_rows(void* map128, const void* W, int rows, int nb, int box_u64);
 
+// Prefill GEMM on the tensor cores (gb_gemm.cu): Y[t][n] = sum_k X[t][k]
+// W[n][k] (+ R[t][n]) for T tokens, W fp32 (dtype GB_DT_F32) or GGUF blocks;
+// fp32-equivalent (3xTF32).  R may alias Y.
+int gemm_launch(int dtype, const void* W, const float* X, float* Y, const float* R, int N, int K, int T,
+                cudaStream_t st);
+
 // Tensor-parallel context of a layer (world > 1): the wo and ffn_down
 // matvecs write this rank's partial to `part`, then an all-reduce over peer
 // memory adds every rank's partial to the hidden state.

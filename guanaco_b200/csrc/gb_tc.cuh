@@ -1,0 +1,111 @@
+// gb_tc.cuh -- 5th-generation tensor core (tcgen05) building blocks for the
+// prefill GEMMs on sm_100a: tensor-memory allocation, shared-memory matrix
+// descriptors, the MMA instruction descriptor, MMA issue and completion
+// tracking, and tensor-memory loads.
+//
+// Operand layout used here: K-major, no swizzle.  A tile of R rows x 32
+// fp32 / tf32 elements is stored as "core matrices" of 8 rows x 4 elements
+// (16 bytes per row, 128 bytes each): element (r, k) lives at
+//     (r / 8) * 128 + (k / 4) * (R / 8 * 128) + (r % 8) * 16 + (k % 4) * 4
+// bytes from the tile base, so consecutive 8-row groups are 128 bytes apart
+// (the descriptor's stride byte offset) and consecutive 4-element column
+// groups R * 16 bytes apart (its leading byte offset).  One tf32 MMA covers
+// K = 8, i.e. two column groups.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gb {
+namespace tc {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// Byte offset of element (r, k) in a K-major tile of R rows x 32 elements.
+__host__ __device__ __forceinline__ uint32_t tile_off(int r, int k, int R) {
+    return (uint32_t)((r >> 3) * 128 + (k >> 2) * (R / 8 * 128) + (r & 7) * 16 + (k & 3) * 4);
+}
+
+// Shared-memory matrix descriptor (sm_100): start address, leading byte
+// offset (between core matrices along K) and stride byte offset (between
+// 8-row groups), each in 16-byte units; descriptor version 1; no swizzle.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;   // version
+    return d;                 // base offset 0, layout type 0 (no swizzle)
+}
+
+// Instruction descriptor of kind::tf32 with fp32 accumulation, both operands
+// K-major, M x N (M = 128, N a multiple of 16 up to 256).
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
+    return (1u << 4)                        // D format: f32
+         | (2u << 7)                        // A format: tf32
+         | (2u << 10)                       // B format: tf32
+         | ((uint32_t)(N >> 3) << 17)       // N / 8
+         | ((uint32_t)(M >> 4) << 24);      // M / 16
+}
+
+// Tensor memory: a warp allocates ncols columns (a power of two >= 32) and
+// writes the base address to *slot (shared memory).
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void fence_before_sync() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// Generic-proxy shared-memory writes made visible to the tensor cores (async proxy).
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem] . B[smem]^T, issued by one thread.
+__device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate)
+        : "memory");
+}
+// Arrive once on an mbarrier when every MMA this thread issued so far has completed.
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+// 16 consecutive fp32 columns of this thread's tensor-memory lane (warp w of
+// a warpgroup reads lanes 32 (w % 4) .. + 31; taddr carries the lane in bits
+// 31:16 and the column in 15:0).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// x = hi + lo with hi representable in tf32 (round to nearest on the top 19
+// bits) and lo = x - hi exact in fp32; the tensor core reads lo as tf32 too,
+// so hi.hi + hi.lo + lo.hi carries ~22 bits of each operand.
+__device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
+    uint32_t h;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
+    hi = __uint_as_float(h);
+    lo = x - hi;
+}
+
+}  // namespace tc
+}  // namespace gb

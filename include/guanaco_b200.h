@@ -158,6 +158,19 @@ int gb_attention_decode(const float* q, const float* k, const float* v,
                         const int* d_pos, int n_heads, int n_kv, int head_dim, int max_seq,
                         float* out, void* ws, void* stream);
 
+/* Prefill GEMM for T tokens at once on the tcgen05 tensor cores:
+ * Y[t][n] = sum_k X[t][k] W[n][k] (+ R[t][n] when R is not NULL; R may be Y),
+ * all device pointers, X / Y / R row-major fp32 (T x K, T x N).  W is N rows of
+ * GGUF blocks (dtype 4 Q4_K, 5 Q6_K, 2 Q8_0) or fp32 (dtype 0).  fp32-
+ * equivalent: weights and activations are split into tf32 + fp32 remainders
+ * (hi.hi + hi.lo + lo.hi).  Replaces the per-token loop of linear_dispatch
+ * (src/engine/engine.c:119-153) for T > 1; the reference's GPU prefill hook is
+ * a stub (src/engine/gpu_prefill.c:3-20).  Asynchronous on `stream`. */
+int gb_gemm(int dtype, const void* W, const float* X, float* Y, const float* R, int N, int K, int T, void* stream);
+/* Device error word of the GEMM's bounded waits (GB_ETIMEOUT); clear != 0
+ * resets it. */
+int gb_gemm_error(int clear);
+
 /* Frees every device copy the vtable matvec slots made of weights that were
  * never uploaded (the engine's lm_head).  Those copies are keyed by host
  * pointer and checked against the byte size and a checksum of sampled

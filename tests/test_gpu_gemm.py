@@ -1,0 +1,65 @@
+"""Prefill GEMM on the tcgen05 tensor cores (gb_gemm): Y = X . W^T (+ R) for T
+tokens at once, W fp32 or GGUF Q4_K / Q6_K / Q8_0 blocks dequantised on the
+fly.  fp32-equivalent arithmetic (3xTF32; the tensor cores' accumulator is
+restarted every 256 columns of K and the partial sums added in fp32
+registers), so the result must match an fp64 product of the oracle's
+dequantised weights (the reference's formulas) to a few 1e-6 relative L2
+(bound 1e-5 at every K tested, up to 2048), far inside the 1e-3 bound."""
+import numpy as np
+import pytest
+
+from tests.helpers import rel_l2, to_dev, from_dev
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(gb, cuda, dt, Wdev, X, N, K, T, R=None):
+    Xd = to_dev(cuda, X)
+    Y = cuda.full((T, N), float("nan"), dtype=cuda.float32, device="cuda")
+    Rd = to_dev(cuda, R) if R is not None else None
+    gb.gemm(dt, Wdev, Xd, Y, N, K, T, R=Rd)
+    cuda.cuda.synchronize()
+    assert gb.lib().gb_gemm_error(1) == 0
+    return from_dev(Y)
+
+
+@pytest.mark.parametrize("N,K,T", [(128, 32, 16), (128, 256, 128), (200, 512, 130), (37, 96, 3), (300, 64, 257)])
+def test_gemm_fp32_matches_fp64(gb, oracle, cuda, N, K, T):
+    W = oracle.synth_normal(N * K, 3, N).reshape(N, K)
+    X = oracle.synth_normal(T * K, 3, K + T).reshape(T, K)
+    Y = _run(gb, cuda, 0, to_dev(cuda, W), X, N, K, T)
+    ref = X.astype(np.float64) @ W.astype(np.float64).T
+    assert np.all(np.isfinite(Y))
+    assert rel_l2(Y, ref) <= 1e-5, rel_l2(Y, ref)
+
+
+@pytest.mark.parametrize("dt", [4, 5, 2])
+@pytest.mark.parametrize("N,K,T", [(128, 256, 1), (256, 1024, 128), (100, 512, 37), (260, 2048, 200)])
+def test_gemm_quantised_matches_dequantised_product(gb, oracle, cuda, dt, N, K, T):
+    W = oracle.synth_blocks(dt, N, K, 5, N + K)
+    Wd = cuda.zeros(W.size + 16, dtype=cuda.uint8, device="cuda")
+    Wd[: W.size] = to_dev(cuda, W)
+    X = oracle.synth_normal(T * K, 5, T).reshape(T, K)
+    R = oracle.synth_normal(T * N, 5, 7).reshape(T, N)
+    Y = _run(gb, cuda, dt, Wd, X, N, K, T, R=R)
+    Wf = oracle.dequant(dt, W).reshape(N, K).astype(np.float64)
+    ref = X.astype(np.float64) @ Wf.T + R
+    assert rel_l2(Y, ref) <= 1e-5, rel_l2(Y, ref)
+    # each row agrees with the reference's own matvec on that token
+    for t in (0, T - 1):
+        _, y = oracle.matvec(dt, W, N, K, X[t])
+        assert rel_l2(Y[t] - R[t], y) <= 1e-5
+
+
+def test_gemm_residual_in_place(gb, oracle, cuda):
+    N, K, T = 256, 512, 40
+    W = oracle.synth_blocks(4, N, K, 9, 1)
+    Wd = cuda.zeros(W.size + 16, dtype=cuda.uint8, device="cuda")
+    Wd[: W.size] = to_dev(cuda, W)
+    X = oracle.synth_normal(T * K, 9, 2).reshape(T, K)
+    H = oracle.synth_normal(T * N, 9, 3).reshape(T, N)
+    Hd = to_dev(cuda, H)
+    gb.gemm(4, Wd, to_dev(cuda, X), Hd, N, K, T, R=Hd)
+    cuda.cuda.synchronize()
+    ref = X.astype(np.float64) @ oracle.dequant(4, W).reshape(N, K).astype(np.float64).T + H
+    assert rel_l2(from_dev(Hd), ref) <= 1e-5
