@@ -101,6 +101,7 @@ SIGNATURES = {
     "gb_device_error": (_i, [_i]),
     "gb_gemm": (_i, [_i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "gb_gemm_error": (_i, [_i]),
+    "gb_prefill_attention": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "gb_dequant": (_i, [_i, _vp, _sz, _vp, _vp]),
     "gb_synth_blocks": (_i, [_i, _vp, _sz, _u64, _u64, _vp]),
     "gb_synth_normal": (_i, [_vp, _sz, _u64, _u64, _vp]),
@@ -127,6 +128,8 @@ SIGNATURES = {
     "gb_model_v_cache": (_vp, [_vp, _i]),
     "gb_model_decode": (_i, [_vp, _vp, _vp, _vp, _vp, _vp]),
     "gb_model_decode_host": (_i, [_vp, _i, _i, _vp, _vp]),
+    "gb_model_prefill": (_i, [_vp, _vp, _i, _i, _vp, _vp, _vp]),
+    "gb_model_prefill_host": (_i, [_vp, _vp, _i, _i, _vp, _vp]),
     "gb_model_step_bytes": (C.c_double, [_vp, _i]),
     "gb_model_generate": (_i, [_vp, _vp, _vp, _i, _vp, _vp]),
     "gb_model_fill_kv": (_i, [_vp, _i, _u64]),
@@ -190,6 +193,14 @@ def matvec_group(dtypes, Ws, rows, cols, x, ys, stream=None) -> None:
 def gemm(dtype, W, X, Y, N, K, T, R=None, stream=None) -> None:
     """Y[t][n] = sum_k X[t][k] W[n][k] (+ R[t][n]) on the tensor cores (prefill)."""
     check("gb_gemm", lib().gb_gemm(dtype, _ptr(W), _ptr(X), _ptr(Y), _ptr(R), N, K, T, _stream(stream)))
+
+
+def prefill_attention(q, k_cache, v_cache, out, n_tokens, pos, n_heads, n_kv, head_dim, max_seq,
+                      stream=None) -> None:
+    """Causal attention of n_tokens prompt rows (positions pos ..) over a layer's cache."""
+    check("gb_prefill_attention", lib().gb_prefill_attention(_ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(out),
+                                                             n_tokens, pos, n_heads, n_kv, head_dim, max_seq,
+                                                             _stream(stream)))
 
 
 def dequant(dtype, blocks, nblocks, out, stream=None) -> None:
@@ -316,6 +327,24 @@ class DecodeModel:
         if logits is not None:
             ptr = logits.ctypes.data if hasattr(logits, "ctypes") else _ptr(logits)
         check("gb_model_decode_host", lib().gb_model_decode_host(self.h, token, pos, C.byref(nxt), ptr))
+        return nxt.value
+
+    def prefill(self, d_tokens, n_tokens: int, pos: int, d_logits, d_next, stream=None) -> None:
+        """A prompt of n_tokens device tokens at positions pos ..: K / V cache
+        rows written, last row's logits / argmax out (asynchronous)."""
+        check("gb_model_prefill", lib().gb_model_prefill(self.h, _ptr(d_tokens), n_tokens, pos, _ptr(d_logits),
+                                                         _ptr(d_next), _stream(stream)))
+
+    def prefill_host(self, tokens, pos: int, logits=None) -> int:
+        """Host prompt in, next token (and optionally the logits) out."""
+        import numpy as np
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        nxt = C.c_int(0)
+        ptr = None
+        if logits is not None:
+            ptr = logits.ctypes.data if hasattr(logits, "ctypes") else _ptr(logits)
+        check("gb_model_prefill_host", lib().gb_model_prefill_host(self.h, t.ctypes.data, t.size, pos,
+                                                                   C.byref(nxt), ptr))
         return nxt.value
 
     def generate(self, d_token, d_pos, n_steps, d_out=None, stream=None) -> None:

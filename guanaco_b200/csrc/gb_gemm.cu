@@ -25,7 +25,8 @@
 // a fresh accumulator (two in tensor memory, alternating), and warps 5-12
 // read each finished one back and add it into fp32 registers (lane r = weight
 // row, 64 of the 128 token columns per warp), then write Y after the last.
-// Every wait is bounded (2 s of %globaltimer) and records GB_ETIMEOUT.
+// Every wait is bounded (2 s of %globaltimer) and records GB_ETIMEOUT in the
+// caller's error word (gb_gemm: a module-wide word read by gb_gemm_error).
 #include "gb_common.cuh"
 #include "gb_internal.h"
 #include "gb_mt.cuh"
@@ -97,12 +98,12 @@ __device__ __forceinline__ void dequant32(const uint8_t* __restrict__ W, int n, 
     }
 }
 
-__device__ __forceinline__ bool gm_wait(uint32_t bar, uint32_t parity) {
+__device__ __forceinline__ bool gm_wait(uint32_t bar, uint32_t parity, unsigned* err) {
     if (mbs_test(bar, parity)) return true;
     const uint64_t t0 = gtimer();
     while (!mbs_test(bar, parity))
         if (gtimer() - t0 > MT_WAIT_NS) {
-            atomicExch(&g_gemm_err, (unsigned)(-GB_ETIMEOUT));
+            atomicExch(err ? err : &g_gemm_err, (unsigned)(-GB_ETIMEOUT));
             return false;
         }
     return true;
@@ -125,7 +126,8 @@ __device__ __forceinline__ void store_split(uint8_t* hi, uint8_t* lo, int r, con
 
 template <int DT>
 __global__ void __launch_bounds__(GM_THREADS, 1)
-k_gemm(const uint8_t* __restrict__ W, const float* __restrict__ X, float* Y, const float* R, int N, int K, int T) {
+k_gemm(const uint8_t* __restrict__ W, const float* __restrict__ X, float* Y, const float* R, int N, int K, int T,
+       unsigned* err) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte aligned stage ring; barriers and the tensor-memory address
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -161,14 +163,14 @@ k_gemm(const uint8_t* __restrict__ W, const float* __restrict__ X, float* Y, con
             bool ok = true;
             for (int g = 0; g < ng && ok; g++) {
                 const int a = g & 1;
-                if (g >= 2) ok = gm_wait(accfree + 8 * a, ((g >> 1) - 1) & 1);
+                if (g >= 2) ok = gm_wait(accfree + 8 * a, ((g >> 1) - 1) & 1, err);
                 if (!ok) break;
                 tc::fence_after_sync();
                 const uint32_t acc = tmem + (uint32_t)(a * GM_BT);
                 const int k1 = min(nk, (g + 1) * GM_KG);
                 for (int kc = g * GM_KG; kc < k1; kc++) {
                     const int s = kc % GM_S;
-                    ok = gm_wait(full + 8 * s, (kc / GM_S) & 1);
+                    ok = gm_wait(full + 8 * s, (kc / GM_S) & 1, err);
                     if (!ok) break;
                     tc::fence_after_sync();
                     const uint32_t base = tc::smem_u32(smem + (size_t)s * GM_STAGE);
@@ -196,7 +198,7 @@ k_gemm(const uint8_t* __restrict__ W, const float* __restrict__ X, float* Y, con
         bool ok = true;
         for (int kc = 0; kc < nk; kc++) {
             const int s = kc % GM_S;
-            if (kc >= GM_S && ok) ok = gm_wait(empty + 8 * s, ((kc / GM_S) - 1) & 1);
+            if (kc >= GM_S && ok) ok = gm_wait(empty + 8 * s, ((kc / GM_S) - 1) & 1, err);
             uint8_t* st = smem + (size_t)s * GM_STAGE;
             float v[32];
             if (n < N) {
@@ -232,7 +234,7 @@ k_gemm(const uint8_t* __restrict__ W, const float* __restrict__ X, float* Y, con
         bool ok = true;
         for (int g = 0; g < ng && ok; g++) {
             const int a = g & 1;
-            ok = gm_wait(accfull + 8 * a, (g >> 1) & 1);
+            ok = gm_wait(accfull + 8 * a, (g >> 1) & 1, err);
             if (!ok) break;
             tc::fence_after_sync();
             const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * GM_BT + c0);
@@ -267,23 +269,24 @@ k_gemm(const uint8_t* __restrict__ W, const float* __restrict__ X, float* Y, con
 }
 
 template <int DT>
-static int launch_gemm(const void* W, const float* X, float* Y, const float* R, int N, int K, int T, cudaStream_t st) {
+static int launch_gemm(const void* W, const float* X, float* Y, const float* R, int N, int K, int T, cudaStream_t st,
+                       unsigned* err) {
     GB_CUDA_TRY(set_smem_once(reinterpret_cast<const void*>(k_gemm<DT>), GM_SMEM));
     dim3 grid((N + GM_ROWS - 1) / GM_ROWS, (T + GM_BT - 1) / GM_BT);
-    k_gemm<DT><<<grid, GM_THREADS, GM_SMEM, st>>>(static_cast<const uint8_t*>(W), X, Y, R, N, K, T);
+    k_gemm<DT><<<grid, GM_THREADS, GM_SMEM, st>>>(static_cast<const uint8_t*>(W), X, Y, R, N, K, T, err);
     return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
 }
 
 int gemm_launch(int dtype, const void* W, const float* X, float* Y, const float* R, int N, int K, int T,
-                cudaStream_t st) {
+                cudaStream_t st, unsigned* err) {
     if (!W || !X || !Y || N <= 0 || K <= 0 || T <= 0) return GB_EINVAL;
     if ((reinterpret_cast<uintptr_t>(X) & 15) || (dtype == GB_DT_F32 && (reinterpret_cast<uintptr_t>(W) & 15)))
         return GB_EINVAL;
     switch (dtype) {
-        case GB_DT_F32: return K % GM_BK ? GB_ESHAPE : launch_gemm<GB_DT_F32>(W, X, Y, R, N, K, T, st);
-        case GB_DT_Q8_0: return K % 32 ? GB_ESHAPE : launch_gemm<GB_DT_Q8_0>(W, X, Y, R, N, K, T, st);
-        case GB_DT_Q4_K: return K % 256 ? GB_ESHAPE : launch_gemm<GB_DT_Q4_K>(W, X, Y, R, N, K, T, st);
-        case GB_DT_Q6_K: return K % 256 ? GB_ESHAPE : launch_gemm<GB_DT_Q6_K>(W, X, Y, R, N, K, T, st);
+        case GB_DT_F32: return K % GM_BK ? GB_ESHAPE : launch_gemm<GB_DT_F32>(W, X, Y, R, N, K, T, st, err);
+        case GB_DT_Q8_0: return K % 32 ? GB_ESHAPE : launch_gemm<GB_DT_Q8_0>(W, X, Y, R, N, K, T, st, err);
+        case GB_DT_Q4_K: return K % 256 ? GB_ESHAPE : launch_gemm<GB_DT_Q4_K>(W, X, Y, R, N, K, T, st, err);
+        case GB_DT_Q6_K: return K % 256 ? GB_ESHAPE : launch_gemm<GB_DT_Q6_K>(W, X, Y, R, N, K, T, st, err);
         default: return GB_EINVAL;
     }
 }
@@ -292,7 +295,7 @@ int gemm_launch(int dtype, const void* W, const float* X, float* Y, const float*
 
 extern "C" int gb_gemm(int dtype, const void* W, const float* X, float* Y, const float* R, int N, int K, int T,
                        void* stream) {
-    return gb::gemm_launch(dtype, W, X, Y, R, N, K, T, static_cast<cudaStream_t>(stream));
+    return gb::gemm_launch(dtype, W, X, Y, R, N, K, T, static_cast<cudaStream_t>(stream), nullptr);
 }
 
 extern "C" int gb_gemm_error(int clear) {

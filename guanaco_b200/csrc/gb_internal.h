@@ -109,9 +109,10 @@ bool mt_encode_rows(void* map128, const void* W, int rows, int nb, int box_u64);
 
 // Prefill GEMM on the tensor cores (gb_gemm.cu): Y[t][n] = sum_k X[t][k]
 // W[n][k] (+ R[t][n]) for T tokens, W fp32 (dtype GB_DT_F32) or GGUF blocks;
-// fp32-equivalent (3xTF32).  R may alias Y.
+// fp32-equivalent (3xTF32).  R may alias Y.  A wait that gives up records
+// GB_ETIMEOUT in *err (null: the module-wide word of gb_gemm_error).
 int gemm_launch(int dtype, const void* W, const float* X, float* Y, const float* R, int N, int K, int T,
-                cudaStream_t st);
+                cudaStream_t st, unsigned* err = nullptr);
 
 // Tensor-parallel context of a layer (world > 1): the wo and ffn_down
 // matvecs write this rank's partial to `part`, then an all-reduce over peer
@@ -170,9 +171,30 @@ int enqueue_layer(const LayerArgs& a, cudaStream_t st);
 bool tp_fusable(const MvPlan* const* mv, int H);
 // Matvec workspace one layer's launches need (grouped launches included).
 size_t layer_ws_bytes(const MvPlan* const* mv);
+// Embedding rows of d_token[0 .. rows) into out[rows][H].
 int embed(const void* emb, int dtype, const int* d_token, int vocab, int H, float* out, unsigned* err,
-          cudaStream_t st, unsigned long long* step = nullptr);
+          cudaStream_t st, unsigned long long* step = nullptr, int rows = 1);
+// out[r] = RMSNorm(x[r]) * w for rows r < rows of n elements.
+int rmsnorm_rows(const float* x, const float* w, float* out, int n, int rows, float eps, cudaStream_t st);
 int set_device_int(int* p, int v, cudaStream_t st);
+
+// Everything one prefill layer needs (gb_prefill.cu): T prompt tokens at
+// positions pos0 .. pos0 + T - 1, activations row-major [T][width].
+struct PrefillArgs {
+    const void* w[GB_NMAT];   // whole matrices (one GPU)
+    int dt[GB_NMAT];
+    const float *ra, *rf;     // RMSNorm weights
+    float *kc, *vc;           // this layer's caches [n_kv][max_seq][hd]
+    const float* rope;        // RoPE table [max_seq][hd]
+    float *hidden, *xn, *q, *k, *v, *attn, *gate, *up;
+    unsigned* err;            // the model's error word
+    int T, pos0, H, n_heads, n_kv, hd, ff, max_seq;
+    float eps;
+};
+int enqueue_prefill_layer(const PrefillArgs& a, cudaStream_t st);
+// Causal attention of T query rows (positions pos0 ..) over the cache.
+int prefill_attention(const float* q, const float* kc, const float* vc, float* out, int T, int pos0, int n_heads,
+                      int n_kv, int head_dim, int max_seq, cudaStream_t st);
 // Synthetic blocks of a slice of a larger matrix: local block r * sn + j
 // (r < rows, j < sn) is global block (row0 + r) * nbg + c0 + j of stream
 // stream_id, written at out block r * ldo + j (ldo >= sn; blocks j >= sn of a

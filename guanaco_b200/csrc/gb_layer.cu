@@ -71,10 +71,13 @@ __device__ __forceinline__ float block_sum_1024(float v, float* sh) {
     return r;
 }
 
-// out = w * (x * r), r = 1/sqrt(sum(x^2)/n + eps)  (kernels_cpu.c:242-263)
+// out = w * (x * r), r = 1/sqrt(sum(x^2)/n + eps)  (kernels_cpu.c:242-263),
+// row blockIdx.x of n-element rows
 __global__ void __launch_bounds__(1024) k_rmsnorm(const float* __restrict__ x, const float* __restrict__ w,
                                                   float* __restrict__ out, int n, float eps) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // successors may start their weight prefetch
+    x += (size_t)blockIdx.x * n;
+    out += (size_t)blockIdx.x * n;
     __shared__ float sh[33];
     float ss = 0.f;
     for (int i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(x[i], x[i], ss);
@@ -185,13 +188,15 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ x, in
     }
 }
 
-// Embedding row of *d_token (engine.c:214-283): F32 copy, Q8_0 q*scale,
-// Q4_K d1*q - m1 -- bit-exact with the reference dequantiser.
+// Embedding rows of d_token[0 .. gridDim.y) (engine.c:214-283): F32 copy,
+// Q8_0 q*scale, Q4_K d1*q - m1 -- bit-exact with the reference dequantiser.
+// Row y of out is token y's (a decode step has one row).
 __global__ void k_embed(const void* __restrict__ emb, int dtype, const int* __restrict__ d_token, int vocab, int H,
                         float* __restrict__ out, unsigned* __restrict__ err, unsigned long long* __restrict__ step) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");   // successors may start their weight prefetch
-    if (step && blockIdx.x == 0 && threadIdx.x == 0) *step += 1;   // epochs of this step's exchanges
-    const int tok = *d_token;
+    if (step && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) *step += 1;   // epochs of this step's exchanges
+    const int tok = d_token[blockIdx.y];
+    out += (size_t)blockIdx.y * H;
     if (tok < 0 || tok >= vocab) {
         if (threadIdx.x == 0 && blockIdx.x == 0 && err) atomicExch(err, (unsigned)(-GB_EINVAL));
         return;
@@ -444,6 +449,12 @@ struct gb_model {
     const void* gen_key[4] = {nullptr, nullptr, nullptr, nullptr};
     int* d_count = nullptr;
     void* am_ws = nullptr;            // argmax partials + ticket (zeroed)
+    // prefill activations for up to pf_cap tokens (allocated by the first
+    // prefill, grown when a longer chunk arrives, freed with the model)
+    void* pf = nullptr;
+    int pf_cap = 0;
+    int* pf_tok = nullptr;            // device copy of a host prompt
+    int pf_tok_cap = 0;
 };
 
 static void* dalloc(gb_model* m, size_t bytes) {
@@ -637,6 +648,8 @@ extern "C" void gb_model_destroy(gb_model* m) {
         if (p) cudaIpcCloseMemHandle(p);
     if (m->comm) cudaFree(m->comm);
     for (void* p : m->owned) cudaFree(p);
+    if (m->pf) cudaFree(m->pf);
+    if (m->pf_tok) cudaFree(m->pf_tok);
     if (m->h_io) cudaFreeHost(m->h_io);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
@@ -937,8 +950,12 @@ size_t layer_ws_bytes(const MvPlan* const* mv) {
 }
 
 int embed(const void* emb, int dtype, const int* d_token, int vocab, int H, float* out, unsigned* err, cudaStream_t st,
-          unsigned long long* step) {
-    k_embed<<<(H + 255) / 256, 256, 0, st>>>(emb, dtype, d_token, vocab, H, out, err, step);
+          unsigned long long* step, int rows) {
+    k_embed<<<dim3((H + 255) / 256, rows), 256, 0, st>>>(emb, dtype, d_token, vocab, H, out, err, step);
+    return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
+}
+int rmsnorm_rows(const float* x, const float* w, float* out, int n, int rows, float eps, cudaStream_t st) {
+    k_rmsnorm<<<rows, 1024, 0, st>>>(x, w, out, n, eps);
     return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
 }
 int tp_allreduce(const TpCtx& tp, const float* h_in, float* h_out, int H, int call, cudaStream_t st) {
@@ -968,6 +985,7 @@ static bool tp_fused(const gb_model* m) {
 
 // Enqueue one decode step on stream st.
 static int enqueue_argmax(gb_model* m, const float* lg, int* d_next, cudaStream_t st);
+static int enqueue_head(gb_model* m, const float* hx, float* lg, bool fx, cudaStream_t st);
 static int enqueue_step(gb_model* m, const int* d_token, const int* d_pos, float* d_logits, int* d_next,
                         cudaStream_t st) {
     const gb_model_config& c = m->c;
@@ -995,6 +1013,15 @@ static int enqueue_step(gb_model* m, const int* d_token, const int* d_pos, float
         if ((rc = enqueue_layer(a, st))) return rc;
     }
     float* lg = d_logits ? d_logits : m->logits;
+    if ((rc = enqueue_head(m, fx ? m->tp.h[1] : m->hidden, lg, fx, st))) return rc;
+    return enqueue_argmax(m, lg, d_next, st);
+}
+
+// Final RMSNorm and the output head of hidden row hx (engine.c:580-592).
+static int enqueue_head(gb_model* m, const float* hx, float* lg, bool fx, cudaStream_t st) {
+    const gb_model_config& c = m->c;
+    const int H = c.hidden_dim;
+    int rc;
     if (m->lm_plan.kind == MV_TMA) {   // final RMSNorm inside the output-head matvec
         MvXform fin;
         fin.mode = MV_X_RMSNORM;
@@ -1007,13 +1034,10 @@ static int enqueue_step(gb_model* m, const int* d_token, const int* d_pos, float
             th.in_call = 2 * c.n_layers - 1;
             th.h_out = m->tp.h[0];
         }
-        const float* hx = fx ? m->tp.h[1] : m->hidden;
-        if ((rc = mv_launch(m->lm_plan, hx, lg, nullptr, m->mv_ws, st, true, &fin, fx ? &th : nullptr))) return rc;
-    } else {
-        if ((rc = gb_rmsnorm(m->hidden, m->rms_final, m->xn, H, c.rms_eps, st))) return rc;
-        if ((rc = mv_launch(m->lm_plan, m->xn, lg, nullptr, m->mv_ws, st, true))) return rc;
+        return mv_launch(m->lm_plan, hx, lg, nullptr, m->mv_ws, st, true, &fin, fx ? &th : nullptr);
     }
-    return enqueue_argmax(m, lg, d_next, st);
+    if ((rc = gb_rmsnorm(hx, m->rms_final, m->xn, H, c.rms_eps, st))) return rc;
+    return mv_launch(m->lm_plan, m->xn, lg, nullptr, m->mv_ws, st, true);
 }
 
 // Next token = first index of the largest logit (over the ranks' slices).
@@ -1186,6 +1210,113 @@ extern "C" int gb_model_decode_host(gb_model* m, int token, int pos, int* h_next
     m->h_io[1] = pos;
     GB_CUDA_TRY(cudaMemcpyAsync(m->d_tok, &m->h_io[0], 2 * sizeof(int), cudaMemcpyHostToDevice, st));   // token, pos
     int rc = gb_model_decode(m, m->d_tok, m->d_pos, m->logits, m->d_next, st);
+    if (rc) return rc;
+    GB_CUDA_TRY(cudaMemcpyAsync(&m->h_io[2], m->d_next, 2 * sizeof(int), cudaMemcpyDeviceToHost, st));   // next, error
+    if (h_logits)
+        GB_CUDA_TRY(cudaMemcpyAsync(h_logits, m->logits, (size_t)m->vocab_l * 4, cudaMemcpyDeviceToHost, st));
+    GB_CUDA_TRY(cudaStreamSynchronize(st));
+    const unsigned herr = static_cast<unsigned>(m->h_io[3]);
+    if (herr) return -(int)herr;
+    *h_next = m->h_io[2];
+    return GB_OK;
+}
+
+// ---------------------------------------------------------------- prefill
+// Prompt tokens per pass through the layers (GB_PREFILL_CHUNK overrides): a
+// longer prompt runs as consecutive chunks, each attending to the cache the
+// earlier ones filled.
+static int prefill_chunk() {
+    const char* e = getenv("GB_PREFILL_CHUNK");
+    const int v = e ? atoi(e) : 0;
+    return v > 0 ? v : 4096;
+}
+
+// Activation floats per prompt token: hidden, xn, q, k, v, attn, gate, up.
+static size_t pf_floats_per_token(const gb_model* m) {
+    const int H = m->c.hidden_dim, QD = m->nh * m->c.head_dim;
+    return 2 * (size_t)H + 2 * (size_t)QD + 2 * (size_t)m->kv_dim + 2 * (size_t)m->ff;
+}
+
+static int pf_reserve(gb_model* m, int T) {
+    if (T <= m->pf_cap) return GB_OK;
+    if (m->pf) {   // earlier prefills on this stream may still read it
+        GB_CUDA_TRY(cudaStreamSynchronize(m->stream));
+        GB_CUDA_TRY(cudaDeviceSynchronize());
+        cudaFree(m->pf);
+        m->pf = nullptr;
+        m->pf_cap = 0;
+    }
+    if (cudaMalloc(&m->pf, (size_t)T * pf_floats_per_token(m) * sizeof(float)) != cudaSuccess) {
+        m->pf = nullptr;
+        return GB_ENOMEM;
+    }
+    m->pf_cap = T;
+    return GB_OK;
+}
+
+extern "C" int gb_model_prefill(gb_model* m, const int* d_tokens, int n_tokens, int pos, float* d_logits, int* d_next,
+                                void* stream) {
+    if (!m || !d_tokens || !d_next || n_tokens <= 0) return GB_EINVAL;
+    const gb_model_config& c = m->c;
+    if (pos < 0 || (long long)pos + n_tokens > c.max_seq) return GB_EPOS;
+    if (m->world != 1) return GB_EINVAL;   // one GPU: the matrices are whole
+    if (!model_ready(m)) return GB_EINVAL;
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : m->stream;
+    const int chunk = std::min(n_tokens, prefill_chunk());
+    int rc;
+    if ((rc = pf_reserve(m, chunk))) return rc;
+    const int H = c.hidden_dim, QD = m->nh * c.head_dim, KVD = m->kv_dim, F = m->ff;
+    float* base = static_cast<float*>(m->pf);
+    const size_t cap = (size_t)m->pf_cap;
+    PrefillArgs a;
+    a.hidden = base;
+    a.xn = a.hidden + cap * H;
+    a.q = a.xn + cap * H;
+    a.attn = a.q + cap * QD;
+    a.k = a.attn + cap * QD;
+    a.v = a.k + cap * KVD;
+    a.gate = a.v + cap * KVD;
+    a.up = a.gate + cap * F;
+    a.err = m->err;
+    a.rope = m->rope;
+    a.H = H; a.n_heads = m->nh; a.n_kv = m->nkv; a.hd = c.head_dim; a.ff = F; a.max_seq = c.max_seq;
+    a.eps = c.rms_eps;
+    int T = 0;
+    for (int c0 = 0; c0 < n_tokens; c0 += chunk) {
+        T = std::min(chunk, n_tokens - c0);
+        if ((rc = embed(m->emb, m->emb_dt, d_tokens + c0, c.vocab_size, H, a.hidden, m->err, st, nullptr, T)))
+            return rc;
+        a.T = T;
+        a.pos0 = pos + c0;
+        for (int l = 0; l < c.n_layers; l++) {
+            for (int i = 0; i < GB_NMAT; i++) {
+                a.w[i] = m->w[(size_t)l * GB_NMAT + i];
+                a.dt[i] = m->dt[(size_t)l * GB_NMAT + i];
+            }
+            a.ra = m->ra[l]; a.rf = m->rf[l];
+            a.kc = gb_model_k_cache(m, l); a.vc = gb_model_v_cache(m, l);
+            if ((rc = enqueue_prefill_layer(a, st))) return rc;
+        }
+    }
+    float* lg = d_logits ? d_logits : m->logits;
+    if ((rc = enqueue_head(m, a.hidden + (size_t)(T - 1) * H, lg, false, st))) return rc;
+    return enqueue_argmax(m, lg, d_next, st);
+}
+
+extern "C" int gb_model_prefill_host(gb_model* m, const int* h_tokens, int n_tokens, int pos, int* h_next,
+                                     float* h_logits) {
+    if (!m || !h_tokens || !h_next || n_tokens <= 0) return GB_EINVAL;
+    cudaStream_t st = m->stream;
+    if (n_tokens > m->pf_tok_cap) {
+        GB_CUDA_TRY(cudaStreamSynchronize(st));
+        if (m->pf_tok) cudaFree(m->pf_tok);
+        m->pf_tok = nullptr;
+        m->pf_tok_cap = 0;
+        GB_CUDA_TRY(cudaMalloc(&m->pf_tok, (size_t)n_tokens * sizeof(int)));
+        m->pf_tok_cap = n_tokens;
+    }
+    GB_CUDA_TRY(cudaMemcpyAsync(m->pf_tok, h_tokens, (size_t)n_tokens * sizeof(int), cudaMemcpyHostToDevice, st));
+    int rc = gb_model_prefill(m, m->pf_tok, n_tokens, pos, m->logits, m->d_next, st);
     if (rc) return rc;
     GB_CUDA_TRY(cudaMemcpyAsync(&m->h_io[2], m->d_next, 2 * sizeof(int), cudaMemcpyDeviceToHost, st));   // next, error
     if (h_logits)

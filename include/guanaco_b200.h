@@ -171,6 +171,16 @@ int gb_gemm(int dtype, const void* W, const float* X, float* Y, const float* R, 
  * resets it. */
 int gb_gemm_error(int clear);
 
+/* Causal attention of a prompt's n_tokens query rows (positions pos ..
+ * pos + n_tokens - 1) over the device KV cache of one layer, whose rows
+ * [0, pos + n_tokens) are filled: out[t][h*hd..] = softmax over keys
+ * s <= pos + t of (q_t . k_s) / sqrt(hd), times v_s.  q / out row-major
+ * [n_tokens][n_heads * head_dim]; caches [n_kv][max_seq][hd].  The T > 1
+ * attention of transformer_layer (src/engine/engine.c:431-500).  head_dim 64
+ * or 128; n_heads / n_kv_heads in {1, 2, 4, 8}.  Asynchronous on `stream`. */
+int gb_prefill_attention(const float* q, const float* k_cache, const float* v_cache, float* out, int n_tokens,
+                         int pos, int n_heads, int n_kv_heads, int head_dim, int max_seq, void* stream);
+
 /* Frees every device copy the vtable matvec slots made of weights that were
  * never uploaded (the engine's lm_head).  Those copies are keyed by host
  * pointer and checked against the byte size and a checksum of sampled
@@ -272,6 +282,23 @@ int gb_model_decode(gb_model* m, const int* d_token, const int* d_pos, float* d_
  * host logits) out: the end-to-end entry point. */
 int gb_model_decode_host(gb_model* m, int token, int pos, int* h_next, float* h_logits);
 /* (h_logits / d_logits receive this rank's vocabulary rows; all of them on one GPU.) */
+
+/* Prefill: forward() of engine.c:559-594 for a prompt of n_tokens tokens at
+ * positions pos .. pos + n_tokens - 1 -- what the reference's GPU prefill
+ * hook gpu_prefill(backend, model, kv, scr, token_ids, n_tokens, pos)
+ * (src/engine/gpu_prefill.c:3-20, a stub there) is for.  Every layer runs
+ * over all the prompt's rows at once (tensor-core GEMMs, causal attention),
+ * the K / V cache rows pos .. pos + n_tokens - 1 are written, and the last
+ * row's logits (d_logits, may be NULL) and argmax (d_next) come out, so
+ * decode continues at pos + n_tokens.  Long prompts run in chunks of 4096
+ * rows (GB_PREFILL_CHUNK).  One GPU (world 1).  Asynchronous on `stream`;
+ * returns GB_EPOS when pos + n_tokens > max_seq.  Activation buffers are
+ * allocated by the first call and kept with the model. */
+int gb_model_prefill(gb_model* m, const int* d_tokens, int n_tokens, int pos, float* d_logits, int* d_next,
+                     void* stream);
+/* Same with the prompt on the host and the next token (and optionally the
+ * logits) returned to the host; synchronous. */
+int gb_model_prefill_host(gb_model* m, const int* h_tokens, int n_tokens, int pos, int* h_next, float* h_logits);
 
 /* Greedy generation entirely on the device: n_steps replays of a graph that
  * runs one decode step and then feeds the argmax back (*d_token = next,

@@ -315,7 +315,8 @@ class RefModel:
         return logits
 
     def forward_tokens(self, tokens, pos: int) -> np.ndarray:
-        """forward() over a prompt (T = len(tokens) <= 16): logits of the last."""
+        """forward() over a prompt of T = len(tokens) tokens at positions pos ..
+        pos + T - 1 (the reference's CPU prefill): logits of the last."""
         t = np.ascontiguousarray(tokens, dtype=np.int32)
         logits = np.empty(self._keep.vocab, dtype=np.float32)
         rc = self._L.ref_model_forward_n(self.h, _p(t), t.size, pos, _p(logits))

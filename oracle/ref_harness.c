@@ -185,7 +185,18 @@ typedef struct {
     Scratch* scr;
     KernelVTable kt;
     void* backend;   /* the engine's Backend (USE_CUDA build, after ref_model_to_gpu) */
+    int H, kv_dim, ff, hd, vocab, n_layers, max_seq;
+    int max_t;       /* prompt length the scratch holds (grown by ref_model_forward_n) */
 } ref_model;
+
+/* forward() resets the scratch once per call, so it must hold every layer's
+ * temporaries (engine.c:354-546) plus the final norm and logits for a
+ * prompt of T tokens; the attention scores are T x seq_len per layer. */
+static size_t ref_scratch_bytes(const ref_model* m, int T) {
+    const size_t per_layer = (size_t)T * (10 * m->H + 2 * m->kv_dim + 2 * m->ff + m->max_seq + 2 * m->hd) *
+                                 sizeof(float) + 32 * (sizeof(Tensor) + 128);
+    return (size_t)m->n_layers * per_layer + (size_t)T * (4 * m->H + 2 * m->vocab) * sizeof(float) + (1u << 20);
+}
 
 static size_t q_bytes(int dtype, int rows, int cols) {
     switch (dtype) {
@@ -244,15 +255,10 @@ void* ref_model_create(const ref_model_desc* d) {
     const size_t kv_bytes = 2 * (size_t)d->n_layers * kv_dim * d->max_seq * sizeof(float);
     m->arena = arena_create(kv_bytes + (4u << 20));
     m->kv = m->arena ? kv_cache_create(m->arena, c, d->max_seq) : NULL;
-    /* forward() resets the scratch once per call, so it must hold every
-     * layer's temporaries (engine.c:354-546) plus the final norm and logits,
-     * for prompts of up to REF_MAX_T tokens (ref_model_forward_n). */
-    enum { REF_MAX_T = 16 };
-    const size_t per_layer = (size_t)REF_MAX_T * (10 * d->H + 2 * kv_dim + 2 * d->ff + d->max_seq + 2 * d->hd) *
-                                 sizeof(float) + 32 * (sizeof(Tensor) + 128);
-    size_t scr = (size_t)d->n_layers * per_layer + (size_t)REF_MAX_T * (4 * d->H + 2 * d->vocab) * sizeof(float) +
-                 (1u << 20);
-    m->scr = scratch_create(scr);
+    m->H = d->H; m->kv_dim = kv_dim; m->ff = d->ff; m->hd = d->hd; m->vocab = d->vocab;
+    m->n_layers = d->n_layers; m->max_seq = d->max_seq;
+    m->max_t = 16;
+    m->scr = scratch_create(ref_scratch_bytes(m, m->max_t));
     m->kt = ref_vtable();
     if (!m->kv || !m->scr) return NULL;
     return m;
@@ -332,6 +338,14 @@ int ref_model_to_gpu(void* h, int threads) {
  * the engine's prefill, engine.c:559-594 and 353-554); logits of the last. */
 int ref_model_forward_n(void* h, const int* tokens, int n, int pos, float* logits) {
     ref_model* m = (ref_model*)h;
+    if (n <= 0) return -1;
+    if (n > m->max_t) {   /* a longer prompt than any before: a larger scratch */
+        Scratch* s2 = scratch_create(ref_scratch_bytes(m, n));
+        if (!s2) return -1;
+        scratch_destroy(m->scr);
+        m->scr = s2;
+        m->max_t = n;
+    }
     int* t = (int*)malloc((size_t)n * sizeof(int));
     if (!t) return -1;
     memcpy(t, tokens, (size_t)n * sizeof(int));

@@ -40,3 +40,14 @@ def device_x(x, group=32):
     x2 = np.clip(np.rint((t1 - x1) * np.float32(256)), -128, 127)
     s = (mx / np.float32(127)).astype(np.float32)
     return ((x0 + x1 / 256.0 + x2 / 65536.0) * s).astype(np.float32).ravel()
+
+
+def read_device(ptr: int, count: int, dtype=np.float32) -> np.ndarray:
+    """count elements at a raw device address (e.g. a model's KV cache) as a
+    host array, through the CUDA runtime's cudaMemcpy."""
+    from cuda.bindings import runtime as rt
+
+    out = np.empty(count, dtype=dtype)
+    (err,) = rt.cudaMemcpy(out.ctypes.data, ptr, out.nbytes, rt.cudaMemcpyKind.cudaMemcpyDeviceToHost)
+    assert err == rt.cudaError_t.cudaSuccess, err
+    return out
