@@ -14,17 +14,21 @@
 // fp32 arithmetic as closely as the decode matvecs do.
 //
 // CTA tile: 128 weight rows (the MMA's M) x BT = 128 tokens (its N), K in
-// chunks of 32.  Warps 0-3 convert: thread r dequantises row r's 32 weights
-// of the chunk and splits token r's 32 activations, storing both into a
-// 3-stage shared-memory ring in the tensor cores' K-major layout (gb_tc.cuh).
+// chunks of 32.  Warps 0-3 convert weights: thread r dequantises row r's 32
+// weights of the chunk (Q4_K: 16-byte loads of a chunk pair's nibbles, the
+// next pair loaded before this one is converted).  Warps 9-12 convert
+// activations: each reads 32 token rows with coalesced 16-byte loads (one
+// chunk ahead) and splits them.  Both store into a 3-stage shared-memory ring
+// in the tensor cores' K-major layout (gb_tc.cuh).
 // Warp 4 allocates the tensor memory and one of its lanes issues the 12 MMAs
 // of a chunk (4 k-steps x 3 products), then commits them to the stage's
 // "empty" barrier so the converters may refill it.  The tensor cores' fp32
 // accumulation is not round-to-nearest, so its error grows with the number
 // of MMAs summed into one accumulator: every 256 columns of K the MMAs start
-// a fresh accumulator (two in tensor memory, alternating), and warps 5-12
-// read each finished one back and add it into fp32 registers (lane r = weight
-// row, 64 of the 128 token columns per warp), then write Y after the last.
+// a fresh accumulator (two in tensor memory, alternating), and warps 5-8
+// read each finished one back and add it to a running fp32 sum kept in a
+// third tensor-memory region (lane r = weight row), then write Y after the
+// last.
 // Every wait is bounded (2 s of %globaltimer) and records GB_ETIMEOUT in the
 // caller's error word (gb_gemm: a module-wide word read by gb_gemm_error).
 #include "gb_common.cuh"
@@ -42,10 +46,11 @@ constexpr int GM_KG = 8;                 // stages summed into one accumulator (
 constexpr int GM_TILE_A = GM_ROWS * GM_BK * 4;   // 16 KB (one of hi / lo)
 constexpr int GM_TILE_B = GM_BT * GM_BK * 4;     // 16 KB
 constexpr int GM_STAGE = 2 * GM_TILE_A + 2 * GM_TILE_B;
-constexpr int GM_READERS = 8;            // accumulator-reader warps (5 .. 12)
-constexpr int GM_THREADS = (5 + GM_READERS) * 32;
+constexpr int GM_READERS = 4;            // accumulator-reader warps (5 .. 8)
+constexpr int GM_XWARPS = 4;             // activation converter warps (9 .. 12)
+constexpr int GM_THREADS = (5 + GM_READERS + GM_XWARPS) * 32;
 constexpr int GM_SMEM = GM_S * GM_STAGE + 1024;
-constexpr uint32_t GM_TMEM_COLS = 2 * GM_BT;   // two accumulators
+constexpr uint32_t GM_TMEM_COLS = 4 * GM_BT;   // two accumulators and the running sum (power of two)
 
 __device__ unsigned g_gemm_err;
 
@@ -141,7 +146,7 @@ k_gemm(const uint8_t* __restrict__ W, const float* __restrict__ X, float* Y, con
     const int ng = (nk + GM_KG - 1) / GM_KG;   // accumulator groups
     if (threadIdx.x == 0) {
         for (int s = 0; s < GM_S; s++) {
-            mbs_init(full + 8 * s, 4);   // one arrival per converter warp
+            mbs_init(full + 8 * s, 4 + GM_XWARPS);   // one arrival per converter warp
             mbs_init(empty + 8 * s, 1);  // the MMA commit
         }
         for (int a = 0; a < 2; a++) {
@@ -192,72 +197,153 @@ k_gemm(const uint8_t* __restrict__ W, const float* __restrict__ X, float* Y, con
             }
         }
         __syncwarp();
-    } else if (warp < 4) {   // ---- warps 0-3: convert
-        const int r = threadIdx.x;   // weight row n0 + r and token t0 + r of every chunk
-        const int n = n0 + r, t = t0 + r;
+    } else if (warp < 4) {   // ---- warps 0-3: weight rows n0 + threadIdx.x
+        const int r = threadIdx.x, n = n0 + r;
         bool ok = true;
-        for (int kc = 0; kc < nk; kc++) {
+        auto put = [&](int kc, const float (&v)[32]) {   // one chunk into its stage
             const int s = kc % GM_S;
             if (kc >= GM_S && ok) ok = gm_wait(empty + 8 * s, ((kc / GM_S) - 1) & 1, err);
             uint8_t* st = smem + (size_t)s * GM_STAGE;
-            float v[32];
-            if (n < N) {
-                dequant32<DT>(W, n, K, kc * GM_BK, v);
-            } else {
-#pragma unroll
-                for (int i = 0; i < 32; i++) v[i] = 0.f;
-            }
             store_split<GM_ROWS>(st, st + GM_TILE_A, r, v);
-            if (t < T) {
-                const float4* p = reinterpret_cast<const float4*>(X + (size_t)t * K + kc * GM_BK);
-#pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    const float4 u = __ldg(p + i);
-                    v[4 * i] = u.x; v[4 * i + 1] = u.y; v[4 * i + 2] = u.z; v[4 * i + 3] = u.w;
-                }
-            } else {
-#pragma unroll
-                for (int i = 0; i < 32; i++) v[i] = 0.f;
-            }
-            store_split<GM_BT>(st + 2 * GM_TILE_A, st + 2 * GM_TILE_A + GM_TILE_B, r, v);
             tc::fence_async_smem();   // generic-proxy stores -> tensor-core reads
             __syncwarp();
             if (lane == 0) mbs_arrive(full + 8 * s);
-        }
-    } else {   // ---- warps 5-12: sum the accumulators in fp32, then write Y
-        const int q = warp & 3;                       // tensor-memory lane quarter this warp may read
-        const int c0 = (warp - 5) >= 4 ? GM_BT / 2 : 0;   // the warp's half of the token columns
-        const int r = q * 32 + lane, n = n0 + r;
-        float sum[GM_BT / 2];
+        };
+        if constexpr (DT == GB_DT_Q4_K) {
+            // chunks 2p and 2p + 1 share 32 bytes of nibbles (low / high); the
+            // next pair's bytes are loaded before this pair is converted
+            const int nb = K / 256;
+            const uint8_t* row = W + (size_t)(n < N ? n : 0) * nb * GB_Q4K_BYTES;
+            auto load = [&](int p, uint4& qa, uint4& qb, uint4& hd) {
+                const uint8_t* blk = row + (size_t)(p >> 2) * GB_Q4K_BYTES;
+                hd = __ldg(reinterpret_cast<const uint4*>(blk));   // d, dmin, 12 scale bytes
+                qa = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 32 * (p & 3)));
+                qb = __ldg(reinterpret_cast<const uint4*>(blk + 32 + 32 * (p & 3)));
+            };
+            uint4 qa, qb, hd;
+            load(0, qa, qb, hd);
+            for (int p = 0; p < nk / 2; p++) {
+                uint4 na = qa, nbq = qb, nh = hd;
+                if (p + 1 < nk / 2) load(p + 1, na, nbq, nh);
+                const float d = f16_bits_to_f32(hd.x & 0xFFFF), dmin = f16_bits_to_f32(hd.x >> 16);
+                const uint32_t sw[3] = {hd.y, hd.z, hd.w};
+                const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
-        for (int i = 0; i < GM_BT / 2; i++) sum[i] = 0.f;
+                for (int h = 0; h < 2; h++) {
+                    const int j = 2 * (p & 3) + h;   // sub-block of the 256-column block
+                    auto sbyte = [&](int i) { return (sw[i >> 2] >> (8 * (i & 3))) & 0xFFu; };
+                    uint32_t sc, mn;
+                    if (j < 4) { sc = sbyte(j) & 63; mn = sbyte(j + 4) & 63; }
+                    else { sc = (sbyte(j + 4) & 0xF) | ((sbyte(j - 4) >> 6) << 4); mn = (sbyte(j + 4) >> 4) | ((sbyte(j) >> 6) << 4); }
+                    const float d1 = d * (float)sc, m1 = dmin * (float)mn;
+                    float v[32];
+#pragma unroll
+                    for (int i = 0; i < 32; i++) {
+                        const uint32_t q = (qw[i >> 2] >> (8 * (i & 3) + 4 * h)) & 0xFu;
+                        v[i] = n < N ? fmaf(d1, (float)q, -m1) : 0.f;
+                    }
+                    put(2 * p + h, v);
+                }
+                qa = na; qb = nbq; hd = nh;
+            }
+        } else {
+            for (int kc = 0; kc < nk; kc++) {
+                float v[32];
+                if (n < N) {
+                    dequant32<DT>(W, n, K, kc * GM_BK, v);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; i++) v[i] = 0.f;
+                }
+                put(kc, v);
+            }
+        }
+    } else if (warp >= 5 + GM_READERS) {   // ---- activations: 32 token rows per warp
+        // lane (rs, q): rows 8 i + rs of the warp, column groups q and q + 4;
+        // an instruction reads 8 rows x 64 contiguous bytes and the stores of
+        // a quarter-warp fill 8 consecutive 16-byte slots of the tile
+        const int xw = warp - (5 + GM_READERS), rs = lane & 7, q = lane >> 3;
+        bool ok = true;
+        float4 cur[8], nxt[8];
+        auto load = [&](int kc, float4 (&u)[8]) {
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int t = t0 + xw * 32 + 8 * i + rs;
+#pragma unroll
+                for (int hh = 0; hh < 2; hh++) {
+                    const int g = q + 4 * hh;
+                    u[2 * i + hh] = t < T ? __ldg(reinterpret_cast<const float4*>(X + (size_t)t * K + kc * GM_BK + 4 * g))
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+        };
+        load(0, cur);
+        for (int kc = 0; kc < nk; kc++) {
+            if (kc + 1 < nk) load(kc + 1, nxt);
+            const int s = kc % GM_S;
+            if (kc >= GM_S && ok) ok = gm_wait(empty + 8 * s, ((kc / GM_S) - 1) & 1, err);
+            uint8_t* st = smem + (size_t)s * GM_STAGE + 2 * GM_TILE_A;
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int hh = 0; hh < 2; hh++) {
+                    const float4 u = cur[2 * i + hh];
+                    float h[4], l[4];
+                    tc::split_tf32(u.x, h[0], l[0]);
+                    tc::split_tf32(u.y, h[1], l[1]);
+                    tc::split_tf32(u.z, h[2], l[2]);
+                    tc::split_tf32(u.w, h[3], l[3]);
+                    const uint32_t off = tc::tile_off(xw * 32 + 8 * i + rs, 4 * (q + 4 * hh), GM_BT);
+                    *reinterpret_cast<float4*>(st + off) = make_float4(h[0], h[1], h[2], h[3]);
+                    *reinterpret_cast<float4*>(st + GM_TILE_B + off) = make_float4(l[0], l[1], l[2], l[3]);
+                }
+            tc::fence_async_smem();
+            __syncwarp();
+            if (lane == 0) mbs_arrive(full + 8 * s);
+#pragma unroll
+            for (int i = 0; i < 8; i++) cur[i] = nxt[i];
+        }
+    } else {   // ---- warps 5-8: sum the accumulators in fp32, then write Y
+        // lane r of warp w reads tensor-memory lane 32 (w % 4) + r = weight
+        // row; the running sum lives in a third tensor-memory region
+        const int q = warp & 3;
+        const int r = q * 32 + lane, n = n0 + r;
+        const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+        const uint32_t sum = lane_base + (uint32_t)(2 * GM_BT);
         bool ok = true;
         for (int g = 0; g < ng && ok; g++) {
             const int a = g & 1;
             ok = gm_wait(accfull + 8 * a, (g >> 1) & 1, err);
             if (!ok) break;
             tc::fence_after_sync();
-            const uint32_t base = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * GM_BT + c0);
-#pragma unroll
-            for (int c = 0; c < GM_BT / 2; c += 16) {
+            const uint32_t acc = lane_base + (uint32_t)(a * GM_BT);
+            const bool last = g == ng - 1;
+#pragma unroll 1
+            for (int c = 0; c < GM_BT; c += 16) {
                 float v[16];
-                tc::tmem_ld16(base + c, v);
+                tc::tmem_ld16(acc + c, v);
+                if (g > 0) {
+                    float u[16];
+                    tc::tmem_ld16(sum + c, u);
 #pragma unroll
-                for (int i = 0; i < 16; i++) sum[c + i] += v[i];
+                    for (int i = 0; i < 16; i++) v[i] += u[i];
+                }
+                if (!last) {
+                    tc::tmem_st16(sum + c, v);
+                } else if (n < N) {
+#pragma unroll
+                    for (int i = 0; i < 16; i++) {
+                        const int tt = t0 + c + i;
+                        if (tt < T) {
+                            const size_t o = (size_t)tt * N + n;
+                            Y[o] = v[i] + (R ? R[o] : 0.f);
+                        }
+                    }
+                }
             }
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) mbs_arrive(accfree + 8 * a);
-        }
-        if (ok && n < N) {
-#pragma unroll
-            for (int i = 0; i < GM_BT / 2; i++) {
-                const int tt = t0 + c0 + i;
-                if (tt < T) {
-                    const size_t o = (size_t)tt * N + n;
-                    Y[o] = sum[i] + (R ? R[o] : 0.f);
-                }
-            }
         }
     }
     tc::fence_before_sync();
@@ -280,7 +366,8 @@ static int launch_gemm(const void* W, const float* X, float* Y, const float* R, 
 int gemm_launch(int dtype, const void* W, const float* X, float* Y, const float* R, int N, int K, int T,
                 cudaStream_t st, unsigned* err) {
     if (!W || !X || !Y || N <= 0 || K <= 0 || T <= 0) return GB_EINVAL;
-    if ((reinterpret_cast<uintptr_t>(X) & 15) || (dtype == GB_DT_F32 && (reinterpret_cast<uintptr_t>(W) & 15)))
+    if ((reinterpret_cast<uintptr_t>(X) & 15) ||
+        ((dtype == GB_DT_F32 || dtype == GB_DT_Q4_K) && (reinterpret_cast<uintptr_t>(W) & 15)))
         return GB_EINVAL;
     switch (dtype) {
         case GB_DT_F32: return K % GM_BK ? GB_ESHAPE : launch_gemm<GB_DT_F32>(W, X, Y, R, N, K, T, st, err);

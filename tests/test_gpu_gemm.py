@@ -34,7 +34,8 @@ def test_gemm_fp32_matches_fp64(gb, oracle, cuda, N, K, T):
 
 
 @pytest.mark.parametrize("dt", [4, 5, 2])
-@pytest.mark.parametrize("N,K,T", [(128, 256, 1), (256, 1024, 128), (100, 512, 37), (260, 2048, 200)])
+@pytest.mark.parametrize("N,K,T", [(128, 256, 1), (256, 1024, 128), (100, 512, 37), (260, 2048, 200),
+                                   (256, 1024, 4096), (140, 4096, 1000)])
 def test_gemm_quantised_matches_dequantised_product(gb, oracle, cuda, dt, N, K, T):
     W = oracle.synth_blocks(dt, N, K, 5, N + K)
     Wd = cuda.zeros(W.size + 16, dtype=cuda.uint8, device="cuda")
