@@ -32,6 +32,7 @@ LLAMA8B = dict(hidden_dim=4096, n_heads=32, n_kv_heads=8, n_layers=32, ff_dim=14
 CTX = 4096
 SEED = 1234
 METRIC = "decode tokens/s (Llama-3.1-8B arch, Q4_K_M, ctx 4096, batch 1)"
+PREFILL_T = 4096
 
 
 def peaks():
@@ -40,6 +41,14 @@ def peaks():
         d = json.load(open(p))
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def tf32_peak():
+    """Dense tf32 tensor peak: half the measured bf16 dense sustained rate."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return float(json.load(open(p))["bf16_tflops_sustained"]) / 2
+    return 1400.0 / 2
 
 
 def ncu_traffic():
@@ -278,25 +287,17 @@ def one_gpu_tokens(gb, torch, max_seq, W, K):
         dm.close()
 
 
-def cpu_reference_token_time(threads: int, n_layers_sample: int = 1, reps: int = 2):
-    """Seconds per Llama-8B decode token on the host cores through the
-    reference's own forward() (oracle/_ref, compiled unchanged), measured on a
-    bounded sample: forward() of a model with n_layers_sample layers plus the
-    full output head, and the output-head matvec alone; the token time is
-    head + 32 * (sample - head) / n_layers_sample."""
+def _ref_llama_sample(O, n_layers_sample: int, max_seq: int):
+    """The reference harness model (oracle/_ref) at the Llama-8B width with
+    n_layers_sample seeded layers and the full output head."""
     import numpy as np
-    from oracle import oracle as O
-    if not O.ref_available():
-        return None
-    R = O.ref()
-    R.ref_set_threads(threads)
 
     class M:
         pass
     m = M()
     c = LLAMA8B
     m.H, m.n_heads, m.n_kv, m.hd, m.ff = c["hidden_dim"], c["n_heads"], c["n_kv_heads"], 128, c["ff_dim"]
-    m.vocab, m.n_layers, m.max_seq = c["vocab_size"], n_layers_sample, CTX + 8
+    m.vocab, m.n_layers, m.max_seq = c["vocab_size"], n_layers_sample, max_seq
     m.layers = []
     kv = m.n_kv * m.hd
     shapes = [(m.H, m.H), (kv, m.H), (kv, m.H), (m.H, m.H), (m.ff, m.H), (m.ff, m.H), (m.H, m.ff)]
@@ -312,7 +313,21 @@ def cpu_reference_token_time(threads: int, n_layers_sample: int = 1, reps: int =
     m.embedding = O.synth_blocks(4, m.vocab, m.H, SEED, 1000001)
     m.lm_head = O.synth_blocks(5, m.vocab, m.H, SEED, 1000002)
     m.rms_final = np.ones(m.H, np.float32)
-    ref = O.RefModel(m)
+    return m, O.RefModel(m)
+
+
+def cpu_reference_token_time(threads: int, n_layers_sample: int = 1, reps: int = 2):
+    """Seconds per Llama-8B decode token on the host cores through the
+    reference's own forward() (oracle/_ref, compiled unchanged), measured on a
+    bounded sample: forward() of a model with n_layers_sample layers plus the
+    full output head, and the output-head matvec alone; the token time is
+    head + 32 * (sample - head) / n_layers_sample."""
+    from oracle import oracle as O
+    if not O.ref_available():
+        return None
+    R = O.ref()
+    R.ref_set_threads(threads)
+    m, ref = _ref_llama_sample(O, n_layers_sample, CTX + 8)
     for li in range(n_layers_sample):
         for which in (0, 1):
             buf = ref.kv(li, which, m.n_kv * m.max_seq * m.hd).reshape(m.n_kv, m.max_seq, m.hd)
@@ -330,6 +345,112 @@ def cpu_reference_token_time(threads: int, n_layers_sample: int = 1, reps: int =
     R.ref_set_threads(1)
     fw, head = min(t_fw), min(t_head)
     return head + LLAMA8B["n_layers"] * max(fw - head, 0.0) / n_layers_sample
+
+
+def cpu_reference_prefill_rate(threads: int, T: int = 32):
+    """Prompt tokens/s of the reference's CPU prefill (forward() with
+    n_tokens = T, oracle/_ref compiled unchanged) at the Llama-8B shape, on a
+    bounded sample: one layer plus the output head over a T-token prompt, and
+    the head alone; rate = T / (32 x (sample - head)).  The reference's
+    linear_dispatch runs its matvec once per prompt row (engine.c:119-153), so
+    the per-row cost hardly depends on T."""
+    import numpy as np
+    from oracle import oracle as O
+    if not O.ref_available():
+        return None
+    R = O.ref()
+    R.ref_set_threads(threads)
+    m, ref = _ref_llama_sample(O, 1, T + 8)
+    prompt = np.random.RandomState(SEED).randint(0, m.vocab, T).astype(np.int32)
+    x = O.synth_normal(m.H, SEED, 3)
+    t0 = time.perf_counter()
+    ref.forward_tokens(prompt, 0)
+    t_fw = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    O.ref_matvec(5, m.lm_head, m.vocab, m.H, x)
+    t_head = time.perf_counter() - t0
+    ref.close()
+    R.ref_set_threads(1)
+    layer = max(t_fw - t_head, 1e-9)
+    return T / (LLAMA8B["n_layers"] * layer)
+
+
+def prefill_bench(gb, torch, peak_tf32, T=PREFILL_T, reps=2):
+    """Prompt tokens/s of gb_model_prefill on the Llama-3.1-8B shape (32 layers,
+    seeded Q4_K_M-style weights): one T-token prompt per step, device-timed
+    with CUDA events on the launching stream after one warm-up prefill; e2e
+    through gb_model_prefill_host (prompt H2D, next token D2H, synchronous).
+    The dominant kernel, the Q4_K gate / up GEMM (14336 x 4096 x T), is timed
+    alone for the roofline: tensor rate = 3 tf32 products x 2 N K T / time."""
+    import numpy as np
+    c = LLAMA8B
+    dm = gb.DecodeModel(c["hidden_dim"], c["n_heads"], c["n_kv_heads"], c["n_layers"], c["ff_dim"],
+                        c["vocab_size"], T + 8)
+    try:
+        dm.synthesize(SEED)
+        prompt = np.random.RandomState(SEED).randint(0, c["vocab_size"], T).astype(np.int32)
+        st = torch.cuda.Stream()
+        d_tok = torch.from_numpy(prompt).to("cuda")
+        lg = torch.empty(c["vocab_size"], device="cuda")
+        nx = torch.empty(1, dtype=torch.int32, device="cuda")
+        torch.cuda.synchronize()
+        dm.prefill(d_tok, T, 0, lg, nx, stream=st.cuda_stream)   # warm-up (buffers, smem attributes)
+        st.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(reps):
+            dm.prefill(d_tok, T, 0, lg, nx, stream=st.cuda_stream)
+        e1.record(st)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        if dm.error() != 0:
+            raise RuntimeError(f"prefill error {dm.error()}")
+        t0 = time.perf_counter()
+        nxt = dm.prefill_host(prompt, 0)
+        e2e_s = time.perf_counter() - t0
+        # dominant kernel alone
+        N, K = c["ff_dim"], c["hidden_dim"]
+        nb = gb.matrix_bytes(4, N, K)
+        W = torch.empty(nb + 16, dtype=torch.uint8, device="cuda")
+        gb.synth_blocks(4, W, nb // gb.BLOCK_BYTES[4], SEED, 5)
+        X = torch.randn(T * K, device="cuda")
+        Y = torch.empty(T * N, device="cuda")
+        for _ in range(3):
+            gb.gemm(4, W, X, Y, N, K, T, stream=st.cuda_stream)
+        e0.record(st)
+        for _ in range(5):
+            gb.gemm(4, W, X, Y, N, K, T, stream=st.cuda_stream)
+        e1.record(st)
+        e1.synchronize()
+        g_ms = e0.elapsed_time(e1) / 5
+        if gb.lib().gb_gemm_error(1) != 0:
+            raise RuntimeError("gemm timeout")
+        tf = 3 * 2.0 * N * K * T / (g_ms * 1e-3) / 1e12
+        del W, X, Y
+        flops = 2.0 * T * sum(r * cc for r, cc in _llama_layer_shapes()) * c["n_layers"]
+        return {"metric": "prompt tokens/s (Llama-3.1-8B arch, Q4_K_M, 4096-token prompt, batch 1)",
+                "value": round(T / (ms * 1e-3), 1), "unit": "tokens/s", "ms_per_prompt": round(ms, 2),
+                "config": {"workload": f"llama3.1-8b-q4km-prefill, {T}-token prompt at position 0, 32 layers",
+                           "chunk": min(T, 4096), "reps": reps, "warmup": 1,
+                           "l2": "weights 4.9 GB and activations > 126 MB L2 per prompt"},
+                "dtype": "fp32-equivalent (weights dequantised to fp32, 3xTF32 tensor-core GEMMs, fp32 attention)",
+                "layer_gemm_tflops_fp32_equiv": round(flops / (ms * 1e-3) / 1e12, 1),
+                "e2e": {"value": round(T / e2e_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": 4 * T,
+                        "d2h_bytes_per_step": 8, "api": "gb_model_prefill_host (prompt in, next token out)"},
+                "next_token": int(nxt),
+                "roofline": {"bound": "tensor", "kernel": f"k_gemm<Q4_K> gate/up 14336x4096 at T={T}",
+                             "achieved": round(tf, 1), "peak": round(peak_tf32, 1), "unit": "TFLOP/s",
+                             "frac": round(tf / peak_tf32, 3), "traffic": None,
+                             "fp32_equiv_tflops": round(tf / 3, 1), "ms": round(g_ms, 3),
+                             "peak_kind": "tf32 dense = half the measured bf16 dense sustained rate"}}
+    finally:
+        dm.close()
+
+
+def _llama_layer_shapes():
+    c = LLAMA8B
+    H, kv, F = c["hidden_dim"], c["n_kv_heads"] * 128, c["ff_dim"]
+    return [(H, H), (kv, H), (kv, H), (H, H), (F, H), (F, H), (H, F)]
 
 
 def run_ours(args, rank, world, local_rank):
@@ -433,8 +554,18 @@ def run_ours(args, rank, world, local_rank):
         ref_toks = one_gpu_tokens(gb, torch, max_seq, W, K)
         tokens_check = {"tokens_match": ref_toks == timed_tokens, "steps_compared": K,
                         "against": "one-GPU model of the same seeded weights and KV fill"}
+    prefill = None
     if rank == 0 and world == 1 and not args.no_extra:
         tiny = tinyllama_decode(gb, torch)
+        prefill = prefill_bench(gb, torch, tf32_peak())
+        if not args.no_cpu_baseline:
+            cores = os.cpu_count() or 1
+            rate = cpu_reference_prefill_rate(cores)
+            if rate:
+                prefill["cpu_baseline"] = {
+                    "value": round(rate, 3), "unit": "tokens/s", "cores": cores, "kind": "reference",
+                    "sample": "reference forward() over a 32-token prompt (oracle/_ref) on one Llama-8B-width "
+                              "layer plus the output head, head timed alone; rate = 32 / (32 x layer time)"}
 
     line = None
     if rank == 0:
@@ -473,6 +604,7 @@ def run_ours(args, rank, world, local_rank):
             "kernels": kernels,
             "tokens": tokens_check,
             "config3": tiny,
+            "prefill": prefill,
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
         }
@@ -579,7 +711,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-extra", action="store_true", help="skip the config-3 (TinyLlama) line")
+    ap.add_argument("--no-extra", action="store_true", help="skip the config-3 (TinyLlama) and prefill lines")
     ap.add_argument("--decode-only", action="store_true",
                     help="run the warm-up and timed decode steps only (for ncu launch lists) and exit")
     ap.add_argument("--steps-ref", type=int, default=None, help="reference arm samples (default min(steps, 5))")

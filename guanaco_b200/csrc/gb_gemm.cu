@@ -15,11 +15,12 @@
 //
 // CTA tile: 128 weight rows (the MMA's M) x BT = 128 tokens (its N), K in
 // chunks of 32.  Warps 0-3 convert weights: thread r dequantises row r's 32
-// weights of the chunk (Q4_K: 16-byte loads of a chunk pair's nibbles, the
-// next pair loaded before this one is converted).  Warps 9-12 convert
-// activations: each reads 32 token rows with coalesced 16-byte loads (one
-// chunk ahead) and splits them.  Both store into a 3-stage shared-memory ring
-// in the tensor cores' K-major layout (gb_tc.cuh).
+// weights of the chunk (Q4_K: 16-byte loads of a chunk pair's nibbles; Q6_K:
+// 4-byte words of a 128-column half-block; the next pair / half-block loaded
+// before this one is converted).  Warp 13 loads each chunk's raw activation
+// tile [128 tokens][32] fp32 by TMA into the stage, and warps 9-12 split it
+// in place.  Both land in a 3-stage shared-memory ring in the tensor cores'
+// K-major layout (gb_tc.cuh).
 // Warp 4 allocates the tensor memory and one of its lanes issues the 12 MMAs
 // of a chunk (4 k-steps x 3 products), then commits them to the stage's
 // "empty" barrier so the converters may refill it.  The tensor cores' fp32
@@ -48,7 +49,8 @@ constexpr int GM_TILE_B = GM_BT * GM_BK * 4;     // 16 KB
 constexpr int GM_STAGE = 2 * GM_TILE_A + 2 * GM_TILE_B;
 constexpr int GM_READERS = 4;            // accumulator-reader warps (5 .. 8)
 constexpr int GM_XWARPS = 4;             // activation converter warps (9 .. 12)
-constexpr int GM_THREADS = (5 + GM_READERS + GM_XWARPS) * 32;
+constexpr int GM_XPROD = 5 + GM_READERS + GM_XWARPS;   // warp 13: activation tile loads (TMA)
+constexpr int GM_THREADS = (GM_XPROD + 1) * 32;
 constexpr int GM_SMEM = GM_S * GM_STAGE + 1024;
 constexpr uint32_t GM_TMEM_COLS = 4 * GM_BT;   // two accumulators and the running sum (power of two)
 
@@ -131,23 +133,24 @@ __device__ __forceinline__ void store_split(uint8_t* hi, uint8_t* lo, int r, con
 
 template <int DT>
 __global__ void __launch_bounds__(GM_THREADS, 1)
-k_gemm(const uint8_t* __restrict__ W, const float* __restrict__ X, float* Y, const float* R, int N, int K, int T,
-       unsigned* err) {
+k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, float* Y, const float* R, int N, int K,
+       int T, unsigned* err) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte aligned stage ring; barriers and the tensor-memory address
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ __align__(8) uint64_t bars[2 * GM_S + 4];
+    __shared__ __align__(8) uint64_t bars[3 * GM_S + 4];
     __shared__ uint32_t tmem_slot;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * GM_ROWS, t0 = blockIdx.y * GM_BT;
-    const uint32_t full = tc::smem_u32(&bars[0]), empty = full + 8 * GM_S;
-    const uint32_t accfull = full + 16 * GM_S, accfree = accfull + 16;   // [2] each
+    const uint32_t full = tc::smem_u32(&bars[0]), empty = full + 8 * GM_S, xfull = full + 16 * GM_S;
+    const uint32_t accfull = full + 24 * GM_S, accfree = accfull + 16;   // [2] each
     const int nk = K / GM_BK;
     const int ng = (nk + GM_KG - 1) / GM_KG;   // accumulator groups
     if (threadIdx.x == 0) {
         for (int s = 0; s < GM_S; s++) {
             mbs_init(full + 8 * s, 4 + GM_XWARPS);   // one arrival per converter warp
             mbs_init(empty + 8 * s, 1);  // the MMA commit
+            mbs_init(xfull + 8 * s, 1);  // the activation tile's TMA load
         }
         for (int a = 0; a < 2; a++) {
             mbs_init(accfull + 8 * a, 1);            // the MMA commit of a group
@@ -246,6 +249,66 @@ k_gemm(const uint8_t* __restrict__ W, const float* __restrict__ X, float* Y, con
                 }
                 qa = na; qb = nbq; hd = nh;
             }
+        } else if constexpr (DT == GB_DT_Q6_K) {
+            // one 128-column half-block (4 chunks) per step: its ql (64 B),
+            // qh (32 B), scales (8 B) and d as 4-byte words from the 2-byte
+            // aligned block (realigned by funnel shifts); the next half-block
+            // is loaded before this one is converted
+            const int nb = K / 256;
+            const uint8_t* row = W + (size_t)(n < N ? n : 0) * nb * GB_Q6K_BYTES;
+            struct Raw { uint32_t ql[17], qh[9], sc[3]; uint32_t d, sh; };
+            auto load = [&](int hb, Raw& w) {
+                const uint8_t* blk = row + (size_t)(hb >> 1) * GB_Q6K_BYTES;
+                const int h = hb & 1;
+                const uint32_t* pl = reinterpret_cast<const uint32_t*>(reinterpret_cast<uintptr_t>(blk + 64 * h) & ~uintptr_t(3));
+                const uint32_t* ph = reinterpret_cast<const uint32_t*>(reinterpret_cast<uintptr_t>(blk + 128 + 32 * h) & ~uintptr_t(3));
+                const uint32_t* ps = reinterpret_cast<const uint32_t*>(reinterpret_cast<uintptr_t>(blk + 192 + 8 * h) & ~uintptr_t(3));
+#pragma unroll
+                for (int i = 0; i < 17; i++) w.ql[i] = __ldg(pl + i);   // within the block: ends by byte 132
+#pragma unroll
+                for (int i = 0; i < 9; i++) w.qh[i] = __ldg(ph + i);    // ends by byte 196
+                w.sc[0] = __ldg(ps);
+                w.sc[1] = __ldg(ps + 1);
+                // a third word only when the scales start 2 bytes into a word (it then ends at byte 210)
+                w.sc[2] = (reinterpret_cast<uintptr_t>(blk) & 3) ? __ldg(ps + 2) : 0u;
+                w.d = *reinterpret_cast<const uint16_t*>(blk + 208);
+                w.sh = (uint32_t)((reinterpret_cast<uintptr_t>(blk) & 3) * 8);   // 0 or 16 (blocks are 2-byte aligned)
+            };
+            Raw cur, nxt;
+            load(0, cur);
+            for (int hb = 0; hb < nk / 4; hb++) {
+                if (hb + 1 < nk / 4) load(hb + 1, nxt);
+                uint32_t ql[16], qh[8], scw[2];
+                const uint32_t sh = cur.sh;
+#pragma unroll
+                for (int i = 0; i < 16; i++) ql[i] = __funnelshift_r(cur.ql[i], cur.ql[i + 1], sh);
+#pragma unroll
+                for (int i = 0; i < 8; i++) qh[i] = __funnelshift_r(cur.qh[i], cur.qh[i + 1], sh);
+                scw[0] = __funnelshift_r(cur.sc[0], cur.sc[1], sh);
+                scw[1] = __funnelshift_r(cur.sc[1], cur.sc[2], sh);
+                const float d = f16_bits_to_f32(cur.d);
+#pragma unroll
+                for (int G = 0; G < 4; G++) {
+                    const int s0 = (int)(int8_t)((scw[G >> 1] >> (16 * (G & 1))) & 0xFF);
+                    const int s1 = (int)(int8_t)((scw[G >> 1] >> (16 * (G & 1) + 8)) & 0xFF);
+                    const float ds0 = d * (float)s0, ds1 = d * (float)s1;
+                    float v[32];
+#pragma unroll
+                    for (int wi = 0; wi < 8; wi++) {
+                        const uint32_t lo4 = (ql[8 * (G & 1) + wi] >> (4 * (G >> 1))) & 0x0F0F0F0Fu;
+                        const uint32_t hi2 = ((qh[wi] >> (2 * G)) & 0x03030303u) << 4;
+                        const uint32_t qw = lo4 | hi2;
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            const int i = 4 * wi + e;
+                            const int q = (int)((qw >> (8 * e)) & 0xFF);
+                            v[i] = n < N ? (i < 16 ? ds0 : ds1) * (float)(q - 32) : 0.f;
+                        }
+                    }
+                    put(4 * hb + G, v);
+                }
+                cur = nxt;
+            }
         } else {
             for (int kc = 0; kc < nk; kc++) {
                 float v[32];
@@ -258,50 +321,50 @@ k_gemm(const uint8_t* __restrict__ W, const float* __restrict__ X, float* Y, con
                 put(kc, v);
             }
         }
-    } else if (warp >= 5 + GM_READERS) {   // ---- activations: 32 token rows per warp
-        // lane (rs, q): rows 8 i + rs of the warp, column groups q and q + 4;
-        // an instruction reads 8 rows x 64 contiguous bytes and the stores of
-        // a quarter-warp fill 8 consecutive 16-byte slots of the tile
-        const int xw = warp - (5 + GM_READERS), rs = lane & 7, q = lane >> 3;
-        bool ok = true;
-        float4 cur[8], nxt[8];
-        auto load = [&](int kc, float4 (&u)[8]) {
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const int t = t0 + xw * 32 + 8 * i + rs;
-#pragma unroll
-                for (int hh = 0; hh < 2; hh++) {
-                    const int g = q + 4 * hh;
-                    u[2 * i + hh] = t < T ? __ldg(reinterpret_cast<const float4*>(X + (size_t)t * K + kc * GM_BK + 4 * g))
-                                          : make_float4(0.f, 0.f, 0.f, 0.f);
-                }
+    } else if (warp == GM_XPROD) {   // ---- activation tiles: raw fp32 [128 tokens][32] by TMA
+        if (lane == 0) {
+            bool ok = true;
+            for (int kc = 0; kc < nk && ok; kc++) {
+                const int s = kc % GM_S;
+                if (kc >= GM_S) ok = gm_wait(empty + 8 * s, ((kc / GM_S) - 1) & 1, err);
+                if (!ok) break;
+                mbs_expect(xfull + 8 * s, GM_TILE_B);
+                // into the stage's hi tile; rows past T read as zeros
+                tma_load_3d(tc::smem_u32(smem + (size_t)s * GM_STAGE + 2 * GM_TILE_A), &xmap, kc * GM_BK, t0, 0,
+                            xfull + 8 * s);
             }
-        };
-        load(0, cur);
+        }
+        __syncwarp();
+    } else if (warp >= 5 + GM_READERS) {   // ---- activations: split the raw tile in place
+        // lane (qq, j) converts row xw * 32 + 8 qq + j; step c takes its
+        // column group (j + c) mod 8, so a quarter-warp's 16-byte reads (one
+        // raw row each) and writes (one core matrix) hit 8 different bank groups
+        const int xw = warp - (5 + GM_READERS), j = lane & 7;
+        const int rr = xw * 32 + 8 * (lane >> 3) + j;
+        bool ok = true;
         for (int kc = 0; kc < nk; kc++) {
-            if (kc + 1 < nk) load(kc + 1, nxt);
             const int s = kc % GM_S;
-            if (kc >= GM_S && ok) ok = gm_wait(empty + 8 * s, ((kc / GM_S) - 1) & 1, err);
-            uint8_t* st = smem + (size_t)s * GM_STAGE + 2 * GM_TILE_A;
+            if (ok) ok = gm_wait(xfull + 8 * s, (kc / GM_S) & 1, err);
+            uint8_t* hi = smem + (size_t)s * GM_STAGE + 2 * GM_TILE_A;
+            float4 u[8];
 #pragma unroll
-            for (int i = 0; i < 4; i++)
+            for (int c = 0; c < 8; c++) u[c] = *reinterpret_cast<const float4*>(hi + rr * 128 + ((j + c) & 7) * 16);
+            // every raw row is read before any core matrix overwrites it
+            asm volatile("bar.sync 1, %0;" ::"n"(GM_XWARPS * 32) : "memory");
 #pragma unroll
-                for (int hh = 0; hh < 2; hh++) {
-                    const float4 u = cur[2 * i + hh];
-                    float h[4], l[4];
-                    tc::split_tf32(u.x, h[0], l[0]);
-                    tc::split_tf32(u.y, h[1], l[1]);
-                    tc::split_tf32(u.z, h[2], l[2]);
-                    tc::split_tf32(u.w, h[3], l[3]);
-                    const uint32_t off = tc::tile_off(xw * 32 + 8 * i + rs, 4 * (q + 4 * hh), GM_BT);
-                    *reinterpret_cast<float4*>(st + off) = make_float4(h[0], h[1], h[2], h[3]);
-                    *reinterpret_cast<float4*>(st + GM_TILE_B + off) = make_float4(l[0], l[1], l[2], l[3]);
-                }
+            for (int c = 0; c < 8; c++) {
+                float h[4], l[4];
+                tc::split_tf32(u[c].x, h[0], l[0]);
+                tc::split_tf32(u[c].y, h[1], l[1]);
+                tc::split_tf32(u[c].z, h[2], l[2]);
+                tc::split_tf32(u[c].w, h[3], l[3]);
+                const uint32_t off = tc::tile_off(rr, 4 * ((j + c) & 7), GM_BT);
+                *reinterpret_cast<float4*>(hi + off) = make_float4(h[0], h[1], h[2], h[3]);
+                *reinterpret_cast<float4*>(hi + GM_TILE_B + off) = make_float4(l[0], l[1], l[2], l[3]);
+            }
             tc::fence_async_smem();
             __syncwarp();
             if (lane == 0) mbs_arrive(full + 8 * s);
-#pragma unroll
-            for (int i = 0; i < 8; i++) cur[i] = nxt[i];
         }
     } else {   // ---- warps 5-8: sum the accumulators in fp32, then write Y
         // lane r of warp w reads tensor-memory lane 32 (w % 4) + r = weight
@@ -358,8 +421,10 @@ template <int DT>
 static int launch_gemm(const void* W, const float* X, float* Y, const float* R, int N, int K, int T, cudaStream_t st,
                        unsigned* err) {
     GB_CUDA_TRY(set_smem_once(reinterpret_cast<const void*>(k_gemm<DT>), GM_SMEM));
+    CUtensorMap xmap;
+    if (!gemm_encode_x(&xmap, X, T, K, GM_BK, GM_BT)) return GB_ECUDA;
     dim3 grid((N + GM_ROWS - 1) / GM_ROWS, (T + GM_BT - 1) / GM_BT);
-    k_gemm<DT><<<grid, GM_THREADS, GM_SMEM, st>>>(static_cast<const uint8_t*>(W), X, Y, R, N, K, T, err);
+    k_gemm<DT><<<grid, GM_THREADS, GM_SMEM, st>>>(xmap, static_cast<const uint8_t*>(W), Y, R, N, K, T, err);
     return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
 }
 

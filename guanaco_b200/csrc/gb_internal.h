@@ -106,6 +106,9 @@ int mv_launch_group(const MvPlan* const* ps, int n, const float* x, float* const
 // Tensor map of a Q4_K / Q6_K weight view (gb_matvec.cu).
 bool mt_encode_view(void* map128, int dtype, const void* W, int rows, int nb, int boxz);
 bool mt_encode_rows(void* map128, const void* W, int rows, int nb, int box_u64);
+// Tensor map of a row-major fp32 matrix X[T][K] with boxes {box_k columns,
+// box_t rows, 1}; rows past T read as zeros.  X and the row pitch 16-byte aligned.
+bool gemm_encode_x(void* map128, const float* X, int T, int K, int box_k, int box_t);
 
 // Prefill GEMM on the tensor cores (gb_gemm.cu): Y[t][n] = sum_k X[t][k]
 // W[n][k] (+ R[t][n]) for T tokens, W fp32 (dtype GB_DT_F32) or GGUF blocks;

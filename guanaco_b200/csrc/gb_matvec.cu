@@ -1069,6 +1069,18 @@ bool mt_encode_rows(void* map128, const void* W, int rows, int nb, int box_u64) 
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool gemm_encode_x(void* map128, const float* X, int T, int K, int box_k, int box_t) {
+    auto enc = tensor_map_encoder();
+    if (!enc || (reinterpret_cast<uintptr_t>(X) & 15) || K % 4 || box_k * 4 % 16) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)T, 1};
+    cuuint64_t strides[2] = {(cuuint64_t)K * 4, (cuuint64_t)K * 4 * (cuuint64_t)T};
+    cuuint32_t box[3] = {(cuuint32_t)box_k, (cuuint32_t)box_t, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    return enc(reinterpret_cast<CUtensorMap*>(map128), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(X), dims,
+               strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <class F>
 static size_t mt_smem_bytes(int S, int K) {
     const size_t xq = ((size_t)mt_xq_bytes(K, F::S16) + 15) & ~(size_t)15;
