@@ -642,6 +642,27 @@ def profile_kernel(name: str) -> None:
         out = torch.empty(nh * hd, dtype=torch.float32, device="cuda")
         launch = lambda i: gb.attention_decode(q, k, v, kc[i % copies], vc[i % copies], cs, d_pos, nh, nkv, hd,  # noqa
                                                ms, out, ws, stream=sp)
+    elif name == "pf_attn":   # prefill causal attention, 4096-token prompt at position 0
+        nh, nkv, hd, T = 32, 8, 128, PREFILL_T
+        n = nkv * T * hd
+        kc = torch.empty(n, dtype=torch.float32, device="cuda")
+        vc = torch.empty(n, dtype=torch.float32, device="cuda")
+        q = torch.empty(T * nh * hd, dtype=torch.float32, device="cuda")
+        gb.synth_normal(kc, n, SEED, 10, stream=sp)
+        gb.synth_normal(vc, n, SEED, 20, stream=sp)
+        gb.synth_normal(q, T * nh * hd, SEED, 30, stream=sp)
+        out = torch.empty_like(q)
+        launch = lambda i: gb.prefill_attention(q, kc, vc, out, T, 0, nh, nkv, hd, T, stream=sp)  # noqa: E731
+    elif name in ("gemm_q4k", "gemm_q6k"):   # prefill GEMM at the 4096-token prompt
+        dt, rows, cols = (4, 14336, 4096) if name == "gemm_q4k" else (5, 4096, 14336)
+        T = PREFILL_T
+        wb = gb.matrix_bytes(dt, rows, cols)
+        W = torch.empty(wb + 16, dtype=torch.uint8, device="cuda")
+        gb.synth_blocks(dt, W, wb // gb.BLOCK_BYTES[dt], SEED, 40, stream=sp)
+        X = torch.empty(T * cols, dtype=torch.float32, device="cuda")
+        gb.synth_normal(X, T * cols, SEED, 5, stream=sp)
+        Y = torch.empty(T * rows, dtype=torch.float32, device="cuda")
+        launch = lambda i: gb.gemm(dt, W, X, Y, rows, cols, T, stream=sp)  # noqa: E731
     elif name == "q4k_gu":   # gate + up in one launch, as in the decode step
         rows, cols, copies = 14336, 4096, 3
         wb = gb.matrix_bytes(4, rows, cols)
@@ -715,7 +736,8 @@ def main():
     ap.add_argument("--decode-only", action="store_true",
                     help="run the warm-up and timed decode steps only (for ncu launch lists) and exit")
     ap.add_argument("--steps-ref", type=int, default=None, help="reference arm samples (default min(steps, 5))")
-    ap.add_argument("--kernel", choices=["q4k", "q4k_gu", "q6k", "q6k_head", "q8_0", "attn"], default=None,
+    ap.add_argument("--kernel", choices=["q4k", "q4k_gu", "q6k", "q6k_head", "q8_0", "attn", "pf_attn", "gemm_q4k",
+                                         "gemm_q6k"], default=None,
                     help="run only a few launches of one kernel (for ncu captures) and exit")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":

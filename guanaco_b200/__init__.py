@@ -19,8 +19,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "lib", "libguanaco_b200.so")
 
 DT_F32, DT_Q8_0, DT_Q4_K, DT_Q6_K = 0, 2, 4, 5
-BLOCK_BYTES = {DT_Q4_K: 144, DT_Q6_K: 210, DT_Q8_0: 34}
-BLOCK_WIDTH = {DT_Q4_K: 256, DT_Q6_K: 256, DT_Q8_0: 32}
+DT_F16, DT_Q5_K = 1, 13   # Q5_K: GGML's type number (no reference DataType)
+BLOCK_BYTES = {DT_Q4_K: 144, DT_Q6_K: 210, DT_Q8_0: 34, DT_Q5_K: 176, DT_F16: 64}   # F16: blocks of 32 halves
+BLOCK_WIDTH = {DT_Q4_K: 256, DT_Q6_K: 256, DT_Q8_0: 32, DT_Q5_K: 256, DT_F16: 32}
 WQ, WK, WV, WO, WGATE, WUP, WDOWN = range(7)
 
 GB_OK, GB_EINVAL, GB_ESHAPE, GB_ESIZE, GB_EPOS, GB_ECUDA, GB_ENOMEM, GB_ETIMEOUT, GB_ELIMIT = \

@@ -297,7 +297,9 @@ static uint64_t sample_signature(const void* p, size_t n) {
 
 static int check_dtype_shape(int dtype, int rows, int cols) {
     if (rows <= 0 || cols <= 0) return GB_EINVAL;
-    if (dtype != GB_DT_Q4_K && dtype != GB_DT_Q6_K && dtype != GB_DT_Q8_0) return GB_EINVAL;
+    if (dtype != GB_DT_Q4_K && dtype != GB_DT_Q6_K && dtype != GB_DT_Q8_0 && dtype != GB_DT_Q5_K &&
+        dtype != GB_DT_F16)
+        return GB_EINVAL;
     if (cols % gb_block_width(dtype)) return GB_ESHAPE;
     return GB_OK;
 }

@@ -12,11 +12,18 @@
 #define GB_DT_Q8_0 2
 #define GB_DT_Q4_K 4
 #define GB_DT_Q6_K 5
+// Q5_K has no code in the reference's DataType (its loader sizes the GGUF
+// type, src/engine/loader.c:98,117, and rejects it, :586-651); 13 is its
+// GGML type number.
+#define GB_DT_Q5_K 13
 
 // GGUF block sizes (src/engine/loader.c:113-119).
 #define GB_Q4K_BYTES 144
 #define GB_Q6K_BYTES 210
 #define GB_Q80_BYTES 34
+#define GB_Q5K_BYTES 176
+// F16 rows are handled in "blocks" of 32 halves (64 bytes).
+#define GB_F16_BYTES 64
 
 // Error codes shared by every entry point.  0..-3 follow the reference vtable
 // convention (src/kernels/cpu/quant_matvec_q4_k.c:143-158); the rest are new.
@@ -43,9 +50,11 @@
 static inline size_t gb_block_bytes(int dtype) {
     return dtype == GB_DT_Q4_K ? GB_Q4K_BYTES
          : dtype == GB_DT_Q6_K ? GB_Q6K_BYTES
-         : dtype == GB_DT_Q8_0 ? GB_Q80_BYTES : 0;
+         : dtype == GB_DT_Q8_0 ? GB_Q80_BYTES
+         : dtype == GB_DT_Q5_K ? GB_Q5K_BYTES
+         : dtype == GB_DT_F16 ? GB_F16_BYTES : 0;
 }
-static inline int gb_block_width(int dtype) { return dtype == GB_DT_Q8_0 ? 32 : 256; }
+static inline int gb_block_width(int dtype) { return dtype == GB_DT_Q8_0 || dtype == GB_DT_F16 ? 32 : 256; }
 static inline size_t gb_matrix_bytes(int dtype, int rows, int cols) {
     return (size_t)rows * (size_t)(cols / gb_block_width(dtype)) * gb_block_bytes(dtype);
 }

@@ -1,7 +1,7 @@
 // gb_gemm.cu -- prefill GEMM on the sm_100a tensor cores (tcgen05):
 //     Y[t][n] = sum_k X[t][k] W[n][k]  (+ R[t][n])
-// for T prompt tokens at once, with W in GGUF Q4_K / Q6_K / Q8_0 blocks
-// (dequantised on the fly) or plain fp32.  This is the T > 1 half of the
+// for T prompt tokens at once, with W in GGUF Q4_K / Q6_K / Q8_0 / Q5_K blocks
+// (dequantised on the fly) or plain fp32 / fp16 rows.  This is the T > 1 half of the
 // reference's linear_dispatch (src/engine/engine.c:87-154), which loops the
 // matvec once per token; the reference's GPU prefill hook is a stub
 // (src/engine/gpu_prefill.c:3-20).
@@ -65,6 +65,19 @@ __device__ __forceinline__ void dequant32(const uint8_t* __restrict__ W, int n, 
         for (int i = 0; i < 8; i++) {
             const float4 v = __ldg(p + i);
             w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
+        }
+    } else if constexpr (DT == GB_DT_F16) {   // exact half -> float
+        const uint4* p = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(W) + (size_t)n * K + k0);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint4 v = __ldg(p + i);
+            const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[e]));
+                w[8 * i + 2 * e] = f.x;
+                w[8 * i + 2 * e + 1] = f.y;
+            }
         }
     } else if constexpr (DT == GB_DT_Q8_0) {
         // quant_matvec_q8_0.c:41-78: w = q * d (block of 32)
@@ -212,25 +225,38 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
             __syncwarp();
             if (lane == 0) mbs_arrive(full + 8 * s);
         };
-        if constexpr (DT == GB_DT_Q4_K) {
-            // chunks 2p and 2p + 1 share 32 bytes of nibbles (low / high); the
-            // next pair's bytes are loaded before this pair is converted
+        if constexpr (DT == GB_DT_Q4_K || DT == GB_DT_Q5_K) {
+            // chunks 2p and 2p + 1 share 32 bytes of nibbles (low / high) and,
+            // for Q5_K, the 32 bytes of fifth bits (bit j of byte i for
+            // sub-block j); the next pair's bytes are loaded before this pair
+            // is converted
+            constexpr bool Q5 = DT == GB_DT_Q5_K;
+            constexpr int BB = Q5 ? GB_Q5K_BYTES : GB_Q4K_BYTES, QS = Q5 ? 48 : 16;
             const int nb = K / 256;
-            const uint8_t* row = W + (size_t)(n < N ? n : 0) * nb * GB_Q4K_BYTES;
-            auto load = [&](int p, uint4& qa, uint4& qb, uint4& hd) {
-                const uint8_t* blk = row + (size_t)(p >> 2) * GB_Q4K_BYTES;
-                hd = __ldg(reinterpret_cast<const uint4*>(blk));   // d, dmin, 12 scale bytes
-                qa = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 32 * (p & 3)));
-                qb = __ldg(reinterpret_cast<const uint4*>(blk + 32 + 32 * (p & 3)));
+            const uint8_t* row = W + (size_t)(n < N ? n : 0) * nb * BB;
+            struct Raw { uint4 hd, qa, qb, ha, hb; };
+            auto load = [&](int p, Raw& w) {
+                const uint8_t* blk = row + (size_t)(p >> 2) * BB;
+                w.hd = __ldg(reinterpret_cast<const uint4*>(blk));   // d, dmin, 12 scale bytes
+                w.qa = __ldg(reinterpret_cast<const uint4*>(blk + QS + 32 * (p & 3)));
+                w.qb = __ldg(reinterpret_cast<const uint4*>(blk + QS + 16 + 32 * (p & 3)));
+                if (Q5) {
+                    w.ha = __ldg(reinterpret_cast<const uint4*>(blk + 16));
+                    w.hb = __ldg(reinterpret_cast<const uint4*>(blk + 32));
+                } else {
+                    w.ha = w.hb = make_uint4(0u, 0u, 0u, 0u);
+                }
             };
-            uint4 qa, qb, hd;
-            load(0, qa, qb, hd);
+            Raw cur, nxt;
+            load(0, cur);
             for (int p = 0; p < nk / 2; p++) {
-                uint4 na = qa, nbq = qb, nh = hd;
-                if (p + 1 < nk / 2) load(p + 1, na, nbq, nh);
+                nxt = cur;
+                if (p + 1 < nk / 2) load(p + 1, nxt);
+                const uint4 hd = cur.hd;
                 const float d = f16_bits_to_f32(hd.x & 0xFFFF), dmin = f16_bits_to_f32(hd.x >> 16);
                 const uint32_t sw[3] = {hd.y, hd.z, hd.w};
-                const uint32_t qw[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+                const uint32_t qw[8] = {cur.qa.x, cur.qa.y, cur.qa.z, cur.qa.w, cur.qb.x, cur.qb.y, cur.qb.z, cur.qb.w};
+                const uint32_t hw[8] = {cur.ha.x, cur.ha.y, cur.ha.z, cur.ha.w, cur.hb.x, cur.hb.y, cur.hb.z, cur.hb.w};
 #pragma unroll
                 for (int h = 0; h < 2; h++) {
                     const int j = 2 * (p & 3) + h;   // sub-block of the 256-column block
@@ -241,13 +267,21 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
                     const float d1 = d * (float)sc, m1 = dmin * (float)mn;
                     float v[32];
 #pragma unroll
-                    for (int i = 0; i < 32; i++) {
-                        const uint32_t q = (qw[i >> 2] >> (8 * (i & 3) + 4 * h)) & 0xFu;
-                        v[i] = n < N ? fmaf(d1, (float)q, -m1) : 0.f;
+                    for (int wi = 0; wi < 8; wi++) {
+                        uint32_t code = (qw[wi] >> (4 * h)) & 0x0F0F0F0Fu;   // 4 codes, one per byte
+                        if (Q5) code |= ((hw[wi] >> j) & 0x01010101u) << 4;
+                        v[4 * wi + 0] = fmaf(d1, tc::byte_as_float<0>(code, 0.f), -m1);
+                        v[4 * wi + 1] = fmaf(d1, tc::byte_as_float<1>(code, 0.f), -m1);
+                        v[4 * wi + 2] = fmaf(d1, tc::byte_as_float<2>(code, 0.f), -m1);
+                        v[4 * wi + 3] = fmaf(d1, tc::byte_as_float<3>(code, 0.f), -m1);
+                    }
+                    if (n >= N) {
+#pragma unroll
+                        for (int i = 0; i < 32; i++) v[i] = 0.f;
                     }
                     put(2 * p + h, v);
                 }
-                qa = na; qb = nbq; hd = nh;
+                cur = nxt;
             }
         } else if constexpr (DT == GB_DT_Q6_K) {
             // one 128-column half-block (4 chunks) per step: its ql (64 B),
@@ -297,13 +331,16 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
                     for (int wi = 0; wi < 8; wi++) {
                         const uint32_t lo4 = (ql[8 * (G & 1) + wi] >> (4 * (G >> 1))) & 0x0F0F0F0Fu;
                         const uint32_t hi2 = ((qh[wi] >> (2 * G)) & 0x03030303u) << 4;
-                        const uint32_t qw = lo4 | hi2;
+                        const uint32_t qw = lo4 | hi2;   // 4 six-bit codes, one per byte
+                        const float dsw = wi < 4 ? ds0 : ds1;
+                        v[4 * wi + 0] = dsw * tc::byte_as_float<0>(qw, 32.f);
+                        v[4 * wi + 1] = dsw * tc::byte_as_float<1>(qw, 32.f);
+                        v[4 * wi + 2] = dsw * tc::byte_as_float<2>(qw, 32.f);
+                        v[4 * wi + 3] = dsw * tc::byte_as_float<3>(qw, 32.f);
+                    }
+                    if (n >= N) {
 #pragma unroll
-                        for (int e = 0; e < 4; e++) {
-                            const int i = 4 * wi + e;
-                            const int q = (int)((qw >> (8 * e)) & 0xFF);
-                            v[i] = n < N ? (i < 16 ? ds0 : ds1) * (float)(q - 32) : 0.f;
-                        }
+                        for (int i = 0; i < 32; i++) v[i] = 0.f;
                     }
                     put(4 * hb + G, v);
                 }
@@ -432,13 +469,16 @@ int gemm_launch(int dtype, const void* W, const float* X, float* Y, const float*
                 cudaStream_t st, unsigned* err) {
     if (!W || !X || !Y || N <= 0 || K <= 0 || T <= 0) return GB_EINVAL;
     if ((reinterpret_cast<uintptr_t>(X) & 15) ||
-        ((dtype == GB_DT_F32 || dtype == GB_DT_Q4_K) && (reinterpret_cast<uintptr_t>(W) & 15)))
+        ((dtype == GB_DT_F32 || dtype == GB_DT_Q4_K || dtype == GB_DT_Q5_K || dtype == GB_DT_F16) &&
+         (reinterpret_cast<uintptr_t>(W) & 15)))
         return GB_EINVAL;
     switch (dtype) {
         case GB_DT_F32: return K % GM_BK ? GB_ESHAPE : launch_gemm<GB_DT_F32>(W, X, Y, R, N, K, T, st, err);
         case GB_DT_Q8_0: return K % 32 ? GB_ESHAPE : launch_gemm<GB_DT_Q8_0>(W, X, Y, R, N, K, T, st, err);
         case GB_DT_Q4_K: return K % 256 ? GB_ESHAPE : launch_gemm<GB_DT_Q4_K>(W, X, Y, R, N, K, T, st, err);
         case GB_DT_Q6_K: return K % 256 ? GB_ESHAPE : launch_gemm<GB_DT_Q6_K>(W, X, Y, R, N, K, T, st, err);
+        case GB_DT_Q5_K: return K % 256 ? GB_ESHAPE : launch_gemm<GB_DT_Q5_K>(W, X, Y, R, N, K, T, st, err);
+        case GB_DT_F16: return K % GM_BK ? GB_ESHAPE : launch_gemm<GB_DT_F16>(W, X, Y, R, N, K, T, st, err);
         default: return GB_EINVAL;
     }
 }

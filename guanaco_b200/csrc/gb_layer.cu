@@ -665,7 +665,9 @@ static void invalidate_graph(gb_model* m);
 
 extern "C" int gb_model_set_matrix(gb_model* m, int layer, int which, int dtype, const void* d_w) {
     if (!m || layer < 0 || layer >= m->c.n_layers || which < 0 || which >= GB_NMAT || !d_w) return GB_EINVAL;
-    if (dtype != GB_DT_Q4_K && dtype != GB_DT_Q6_K && dtype != GB_DT_Q8_0) return GB_EINVAL;
+    if (dtype != GB_DT_Q4_K && dtype != GB_DT_Q6_K && dtype != GB_DT_Q8_0 && dtype != GB_DT_Q5_K &&
+        dtype != GB_DT_F16)
+        return GB_EINVAL;
     int rows, cols;
     mat_shape(m, which, dtype, &rows, &cols);
     MvPlan p;

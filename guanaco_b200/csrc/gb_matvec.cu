@@ -34,6 +34,7 @@
 #include "gb_common.cuh"
 #include "gb_internal.h"
 #include "gb_mt.cuh"
+#include "gb_tc.cuh"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -608,6 +609,120 @@ k_mv_q8_0(const uint8_t* __restrict__ W, int rows, int nb, const float* __restri
     }
 }
 
+// ================================================================== Q5_K / F16 (CUDA cores)
+// Formats the reference does not compute (its loader rejects them): GGML's
+// Q5_K (block of 256: d, dmin, 12 packed 6-bit scales / mins as Q4_K, qh[32]
+// fifth bits, qs[128] low nibbles; w = d sc q - dmin m, q = nibble + 16 x bit
+// j of qh for sub-block j) and plain fp16 rows.  x is staged in shared memory
+// as fp32 (Q5_K also with per-8-column sums); each consumer warp owns one row
+// of the 16-row group.  Q5_K: lane (j = lane / 4, c = lane % 4) takes columns
+// 32 j + 8 c .. + 7 of every block, sum = d sc (q . x) - dmin m (sum x).  F16:
+// lane l takes 8 consecutive halves of every 256-column chunk.
+template <int DT>
+__global__ void __launch_bounds__(MV_THREADS)
+k_mv_plain(const uint8_t* __restrict__ W, int rows, int nb, const float* __restrict__ x, float* __restrict__ y,
+           const float* __restrict__ residual, MvGeom g) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    constexpr bool Q5 = DT == GB_DT_Q5_K;
+    constexpr int WIDTH = Q5 ? 256 : 32, BYTES = Q5 ? GB_Q5K_BYTES : GB_F16_BYTES;
+    const int K = nb * WIDTH;
+    float* xs = reinterpret_cast<float*>(smem);   // [K] fp32, then (Q5_K) [K / 8] sums
+    float* x8 = xs + K;
+    const MvShared sh = kernel_prologue(smem, g);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const size_t rb = (size_t)nb * BYTES;
+    if (warp == MV_CONSUMERS) {
+        ring_producer(W, rows, nb, BYTES, g, sh.ring, sh.full, sh.empty, sh.abort_flag);
+        return;
+    }
+    for (int e = tid; e < K / 4; e += MV_CONSUMERS * 32) {
+        const float4 v = reinterpret_cast<const float4*>(x)[e];
+        reinterpret_cast<float4*>(xs)[e] = v;
+        if (Q5) {   // sums of 8 columns: two float4 per sum, added by the even thread
+            const float h = (v.x + v.y) + (v.z + v.w);
+            const float o = __shfl_down_sync(0xffffffffu, h, 1);
+            if ((e & 1) == 0) x8[e >> 1] = h + o;
+        }
+    }
+    consumer_sync();
+    int it = 0, gi = 0;
+    const int lr = warp;   // 16-row groups, one row per consumer warp
+    for (int grp = blockIdx.x; grp < g.ngroups; grp += gridDim.x) {
+        const int row0 = grp * g.T;
+        const int nrows = rows - row0 < g.T ? rows - row0 : g.T;
+        float acc = 0.f;
+        for (int kc = 0; kc < g.nk; kc++, it++) {
+            const int s = it % g.S;
+            mbar_wait(&sh.full[s], (it / g.S) & 1, sh.abort_flag);
+            const int b0 = kc * g.KC, nblk = nb - b0 < g.KC ? nb - b0 : g.KC;
+            if (lr < nrows) {
+                // rows of 176 / 64-byte blocks start 16-byte aligned in the stage
+                const uint8_t* prow = sh.ring + (size_t)s * g.SB + (size_t)lr * g.RS + seg_lead(row0 + lr, b0, rb, BYTES);
+                if constexpr (Q5) {
+                    const int j = lane >> 2, c8 = 8 * (lane & 3);
+                    for (int bl = 0; bl < nblk; bl++) {
+                        const uint8_t* blk = prow + (size_t)bl * BYTES;
+                        const uint4 hd = *reinterpret_cast<const uint4*>(blk);
+                        const uint2 qh = *reinterpret_cast<const uint2*>(blk + 16 + c8);
+                        const uint2 qs = *reinterpret_cast<const uint2*>(blk + 48 + 32 * (j >> 1) + c8);
+                        const float d = f16_bits_to_f32(hd.x & 0xFFFFu), dmin = f16_bits_to_f32(hd.x >> 16);
+                        auto sbyte = [&](int i) {
+                            const uint32_t w = i < 4 ? hd.y : (i < 8 ? hd.z : hd.w);
+                            return (w >> (8 * (i & 3))) & 0xFFu;
+                        };
+                        uint32_t sc, mn;
+                        if (j < 4) { sc = sbyte(j) & 63; mn = sbyte(j + 4) & 63; }
+                        else { sc = (sbyte(j + 4) & 0xF) | ((sbyte(j - 4) >> 6) << 4); mn = (sbyte(j + 4) >> 4) | ((sbyte(j) >> 6) << 4); }
+                        const int col = (b0 + bl) * 256 + 32 * j + c8;
+                        const float4 xa = *reinterpret_cast<const float4*>(xs + col);
+                        const float4 xb = *reinterpret_cast<const float4*>(xs + col + 4);
+                        const uint32_t q0 = ((qs.x >> (4 * (j & 1))) & 0x0F0F0F0Fu) | (((qh.x >> j) & 0x01010101u) << 4);
+                        const uint32_t q1 = ((qs.y >> (4 * (j & 1))) & 0x0F0F0F0Fu) | (((qh.y >> j) & 0x01010101u) << 4);
+                        float dot = tc::byte_as_float<0>(q0, 0.f) * xa.x;
+                        dot = fmaf(tc::byte_as_float<1>(q0, 0.f), xa.y, dot);
+                        dot = fmaf(tc::byte_as_float<2>(q0, 0.f), xa.z, dot);
+                        dot = fmaf(tc::byte_as_float<3>(q0, 0.f), xa.w, dot);
+                        dot = fmaf(tc::byte_as_float<0>(q1, 0.f), xb.x, dot);
+                        dot = fmaf(tc::byte_as_float<1>(q1, 0.f), xb.y, dot);
+                        dot = fmaf(tc::byte_as_float<2>(q1, 0.f), xb.z, dot);
+                        dot = fmaf(tc::byte_as_float<3>(q1, 0.f), xb.w, dot);
+                        acc = fmaf(d * (float)sc, dot, acc);
+                        acc = fmaf(-(dmin * (float)mn), x8[col >> 3], acc);
+                    }
+                } else {
+                    for (int c = 0; c * 8 < nblk; c++) {
+                        if (c * 8 + (lane >> 2) >= nblk) continue;
+                        const uint4 h = *reinterpret_cast<const uint4*>(prow + (size_t)c * 512 + 16 * lane);
+                        const int col = (b0 + 8 * c) * 32 + 8 * lane;
+                        const float4 xa = *reinterpret_cast<const float4*>(xs + col);
+                        const float4 xb = *reinterpret_cast<const float4*>(xs + col + 4);
+                        const float2 w0 = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+                        const float2 w1 = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
+                        const float2 w2 = __half22float2(*reinterpret_cast<const __half2*>(&h.z));
+                        const float2 w3 = __half22float2(*reinterpret_cast<const __half2*>(&h.w));
+                        acc = fmaf(w0.x, xa.x, acc);
+                        acc = fmaf(w0.y, xa.y, acc);
+                        acc = fmaf(w1.x, xa.z, acc);
+                        acc = fmaf(w1.y, xa.w, acc);
+                        acc = fmaf(w2.x, xb.x, acc);
+                        acc = fmaf(w2.y, xb.y, acc);
+                        acc = fmaf(w3.x, xb.z, acc);
+                        acc = fmaf(w3.y, xb.w, acc);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh.empty[s]);
+        }
+        const int slot = gi++ % (g.S + 2);
+        const float v = warp_sum(acc);
+        if (lane == 0 && lr < nrows)   // whole rows per warp: the owner's sum in slot 0, zeros elsewhere
+            for (int k = 0; k < MV_CONSUMERS; k++)
+                sh.red[(size_t)slot * MV_CONSUMERS * g.T + k * g.T + lr] = k == 0 ? v : 0.f;
+        group_epilogue(sh, g, slot, row0, nrows, y, residual);
+    }
+}
+
 // Up to MT_MAXM matrices of one format and one column count that share x run
 // as one launch: their (group, item) sequences are concatenated, matrix m
 // owning the global 32-row groups [gbase[m], gbase[m + 1]).
@@ -964,6 +1079,8 @@ static int staged_bytes(int dtype, int nb) {
     switch (dtype) {
         case GB_DT_Q4_K: return nb * (64 * 8 + 16 * 4 + 32 * 8);
         case GB_DT_Q6_K: return nb * (64 * 8 + 48 * 4 + 32 * 8);
+        case GB_DT_Q5_K: return nb * 256 * 4 + nb * 32 * 4;   // x fp32 + sums of 8 columns
+        case GB_DT_F16: return nb * 32 * 4;
         default: return ((nb + 7) / 8) * 32 * (2 * 16 + 4);
     }
 }
@@ -1121,7 +1238,9 @@ static bool mt_encode(MvPlan* p, const void* W, int rows, int nb) {
 int mv_plan(MvPlan* p, int dtype, const void* W, int rows, int cols) {
     if (!p || !W || rows <= 0 || cols <= 0) return GB_EINVAL;
     if (reinterpret_cast<uintptr_t>(W) & 15) return GB_EINVAL;
-    if (dtype != GB_DT_Q4_K && dtype != GB_DT_Q6_K && dtype != GB_DT_Q8_0) return GB_EINVAL;
+    if (dtype != GB_DT_Q4_K && dtype != GB_DT_Q6_K && dtype != GB_DT_Q8_0 && dtype != GB_DT_Q5_K &&
+        dtype != GB_DT_F16)
+        return GB_EINVAL;
     const int width = gb_block_width(dtype);
     if (cols % width) return GB_ESHAPE;
     *p = MvPlan{};
@@ -1205,6 +1324,8 @@ int mv_launch(const MvPlan& p, const float* x, float* y, const float* residual, 
     switch (p.dtype) {
         case GB_DT_Q4_K: e = launch_kernel(k_mv_q4k, p.W, p.rows, p.nb, x, y, residual, g, st); break;
         case GB_DT_Q6_K: e = launch_kernel(k_mv_q6k, p.W, p.rows, p.nb, x, y, residual, g, st); break;
+        case GB_DT_Q5_K: e = launch_kernel(k_mv_plain<GB_DT_Q5_K>, p.W, p.rows, p.nb, x, y, residual, g, st); break;
+        case GB_DT_F16: e = launch_kernel(k_mv_plain<GB_DT_F16>, p.W, p.rows, p.nb, x, y, residual, g, st); break;
         default: e = launch_kernel(k_mv_q8_0, p.W, p.rows, p.nb, x, y, residual, g, st); break;
     }
     return e == cudaSuccess ? GB_OK : GB_ECUDA;

@@ -1,4 +1,4 @@
-// gb_quant.cu -- bit-exact GGUF dequantisers (Q4_K / Q6_K / Q8_0) and the
+// gb_quant.cu -- bit-exact GGUF dequantisers (Q4_K / Q6_K / Q8_0 / Q5_K / F16) and the
 // seeded synthetic block / activation generators used by the tests and the
 // benchmark.  The fused dequant + matvec kernels live in gb_matvec.cu.
 //
@@ -6,6 +6,9 @@
 //   Q4_K  src/engine/engine.c:257-275   w = (d*sc)*q - dmin*m, two roundings
 //   Q6_K  src/kernels/cpu/quant_matvec_q6_k.c:84-87   w = (d*sc)*(q-32)
 //   Q8_0  src/engine/engine.c:238       w = q*scale
+//   Q5_K  (GGML k-quant; no reference kernel) w = (d*sc)*q - dmin*m, q = nibble
+//         + 16 x bit j of qh for sub-block j, two roundings like Q4_K
+//   F16   exact half -> float (engine.c:183-212's mapping)
 #include "gb_common.cuh"
 #include "gb_internal.h"
 
@@ -67,6 +70,36 @@ __global__ void k_dequant_q8_0(const uint8_t* __restrict__ B, size_t nblocks, fl
     const uint8_t* blk = B + (i >> 5) * GB_Q80_BYTES;
     const float scale = f16_bits_to_f32(blk[0] | (blk[1] << 8));
     out[i] = __fmul_rn((float)(int8_t)blk[2 + (i & 31)], scale);   // engine.c:238
+}
+
+__global__ void k_dequant_q5k(const uint8_t* __restrict__ B, size_t nblocks, float* __restrict__ out) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;   // one qs byte
+    if (i >= nblocks * 128) return;
+    const size_t b = i >> 7;
+    const int l = (int)(i & 127), g = l >> 5, ll = l & 31;
+    const uint8_t* blk = B + b * GB_Q5K_BYTES;
+    const float d_all = f16_bits_to_f32(blk[0] | (blk[1] << 8));
+    const float min_all = f16_bits_to_f32(blk[2] | (blk[3] << 8));
+    const uint8_t* s = blk + 4;
+    const uint8_t qh = blk[16 + ll], q = blk[48 + l];
+    float* o = out + b * 256 + 64 * g;
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const int j = 2 * g + h;
+        uint32_t sc, mn;
+        if (j < 4) { sc = s[j] & 63; mn = s[j + 4] & 63; }
+        else {
+            sc = (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4);
+            mn = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+        }
+        const uint32_t code = ((q >> (4 * h)) & 0xF) | (((qh >> j) & 1) << 4);
+        o[32 * h + ll] = __fsub_rn(__fmul_rn(__fmul_rn(d_all, (float)sc), (float)code), __fmul_rn(min_all, (float)mn));
+    }
+}
+
+__global__ void k_dequant_f16(const uint16_t* __restrict__ B, size_t n, float* __restrict__ out) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = f16_bits_to_f32(B[i]);
 }
 
 // ------------------------------------------------------------------ synthesis
@@ -139,6 +172,37 @@ __device__ void synth_q8_0_block(uint8_t* blk, uint64_t g, uint64_t seed, uint64
     }
 }
 
+// Q5_K: the Q4_K header and nibbles (same words), then 32 bytes of fifth bits.
+__device__ void synth_q5k_block(uint8_t* blk, uint64_t g, uint64_t seed, uint64_t stream) {
+    alignas(16) uint8_t tmp[GB_Q4K_BYTES];   // synth_q4k_block stores 16-byte words
+    synth_q4k_block(tmp, g, seed, stream);   // header words 0-2, nibbles 3-18
+    uint4* dst = reinterpret_cast<uint4*>(blk);   // 176-byte blocks: 16-byte aligned
+    const uint4* src = reinterpret_cast<const uint4*>(tmp);
+    dst[0] = src[0];
+    const uint64_t i0 = g * 32;
+    for (int w = 0; w < 2; w++) {
+        const uint64_t a = rand64(seed, stream, i0 + 19 + 2 * w), c = rand64(seed, stream, i0 + 20 + 2 * w);
+        dst[1 + w] = make_uint4((uint32_t)a, (uint32_t)(a >> 32), (uint32_t)c, (uint32_t)(c >> 32));
+    }
+    for (int w = 0; w < 8; w++) dst[3 + w] = src[1 + w];
+}
+
+// F16 "block" g: 32 halves, each the Irwin-Hall value of k_synth_normal at
+// index 32 g + e times 2^-5, rounded to nearest even.
+__device__ void synth_f16_block(uint8_t* blk, uint64_t g, uint64_t seed, uint64_t stream) {
+    uint16_t* h = reinterpret_cast<uint16_t*>(blk);
+    for (int e = 0; e < 32; e++) {
+        const uint64_t i = g * 32 + e;
+        int32_t acc = 0;
+        for (int w = 0; w < 3; w++) {
+            const uint64_t r = rand64(seed, stream, 3 * i + w);
+            acc += (int32_t)(r & 0xffff) + (int32_t)((r >> 16) & 0xffff) + (int32_t)((r >> 32) & 0xffff) +
+                   (int32_t)((r >> 48) & 0xffff);
+        }
+        h[e] = __half_as_ushort(__float2half_rn((float)(acc + 6 - 393216) * (1.0f / 2097152.0f)));
+    }
+}
+
 // Local block b = r * sn + j (r < rows, j < sn) is global block
 // (row0 + r) * nbg + c0 + j, written at output block r * ldo + j: a row or
 // column slice of a larger synthetic matrix (tensor-parallel shards) gets
@@ -153,10 +217,13 @@ __global__ void k_synth_map(uint8_t* B, uint64_t n_local, uint64_t seed, uint64_
     if (b >= n_local) return;
     const uint64_t r = b / m.sn, j = b - r * m.sn;
     const uint64_t g = (m.row0 + r) * m.nbg + m.c0 + j;
-    constexpr int BYTES = DT == GB_DT_Q4_K ? GB_Q4K_BYTES : DT == GB_DT_Q6_K ? GB_Q6K_BYTES : GB_Q80_BYTES;
+    constexpr int BYTES = DT == GB_DT_Q4_K ? GB_Q4K_BYTES : DT == GB_DT_Q6_K ? GB_Q6K_BYTES
+                        : DT == GB_DT_Q5_K ? GB_Q5K_BYTES : DT == GB_DT_F16 ? GB_F16_BYTES : GB_Q80_BYTES;
     uint8_t* blk = B + (r * m.ldo + j) * BYTES;
     if (DT == GB_DT_Q4_K) synth_q4k_block(blk, g, seed, stream);
     else if (DT == GB_DT_Q6_K) synth_q6k_block(blk, g, seed, stream);
+    else if (DT == GB_DT_Q5_K) synth_q5k_block(blk, g, seed, stream);
+    else if (DT == GB_DT_F16) synth_f16_block(blk, g, seed, stream);
     else synth_q8_0_block(blk, g, seed, stream);
 }
 
@@ -191,6 +258,12 @@ extern "C" int gb_dequant(int dtype, const void* blocks, size_t nblocks, float* 
         case GB_DT_Q4_K: k_dequant_q4k<<<(unsigned)((nblocks * 128 + 255) / 256), 256, 0, st>>>(B, nblocks, out); break;
         case GB_DT_Q6_K: k_dequant_q6k<<<(unsigned)((nblocks * 64 + 255) / 256), 256, 0, st>>>(B, nblocks, out); break;
         case GB_DT_Q8_0: k_dequant_q8_0<<<(unsigned)((nblocks * 32 + 255) / 256), 256, 0, st>>>(B, nblocks, out); break;
+        case GB_DT_Q5_K: k_dequant_q5k<<<(unsigned)((nblocks * 128 + 255) / 256), 256, 0, st>>>(B, nblocks, out); break;
+        case GB_DT_F16:
+            if (reinterpret_cast<uintptr_t>(blocks) & 1) return GB_EINVAL;
+            k_dequant_f16<<<(unsigned)((nblocks * 32 + 255) / 256), 256, 0, st>>>(
+                reinterpret_cast<const uint16_t*>(B), nblocks * 32, out);
+            break;
         default: return GB_EINVAL;
     }
     return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
@@ -215,6 +288,12 @@ int synth_blocks_shard(int dtype, void* out, size_t rows, size_t sn, size_t ldo,
         case GB_DT_Q8_0:
             if (reinterpret_cast<uintptr_t>(out) & 1) return GB_EINVAL;
             k_synth_map<GB_DT_Q8_0><<<grid, 256, 0, st>>>(B, n, seed, stream_id, m); break;
+        case GB_DT_Q5_K:
+            if (reinterpret_cast<uintptr_t>(out) & 15) return GB_EINVAL;
+            k_synth_map<GB_DT_Q5_K><<<grid, 256, 0, st>>>(B, n, seed, stream_id, m); break;
+        case GB_DT_F16:
+            if (reinterpret_cast<uintptr_t>(out) & 1) return GB_EINVAL;
+            k_synth_map<GB_DT_F16><<<grid, 256, 0, st>>>(B, n, seed, stream_id, m); break;
         default: return GB_EINVAL;
     }
     return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;

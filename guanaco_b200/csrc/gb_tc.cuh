@@ -112,14 +112,24 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
     asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-// x = hi + lo with hi representable in tf32 (round to nearest on the top 19
-// bits) and lo = x - hi exact in fp32; the tensor core reads lo as tf32 too,
-// so hi.hi + hi.lo + lo.hi carries ~22 bits of each operand.
+// x = hi + lo with hi representable in tf32 (the top 19 bits, rounded to
+// nearest with ties away from zero: half a tf32 unit added to the magnitude
+// bits, then the low 13 bits cleared -- two integer operations instead of a
+// conversion) and lo = x - hi exact in fp32; the tensor core reads lo as
+// tf32 too, so hi.hi + hi.lo + lo.hi carries ~22 bits of each operand.
+// Finite inputs only (a magnitude within half a unit of FLT_MAX rounds to inf).
 __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
-    uint32_t h;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(h) : "f"(x));
-    hi = __uint_as_float(h);
+    hi = __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
     lo = x - hi;
+}
+
+// Byte e (0..3) of w as an exact float minus `bias`: the byte is placed in
+// the low mantissa bits of 2^23 by one byte permute, and 2^23 + bias is
+// subtracted (exact for bytes and small integer biases).
+template <int E>
+__device__ __forceinline__ float byte_as_float(uint32_t w, float bias) {
+    const uint32_t f = __byte_perm(w, 0x4B000000u, (uint32_t)E | 0x7540u);   // bytes {w.E, 0, 0, 0x4B}
+    return __uint_as_float(f) - (8388608.0f + bias);
 }
 
 }  // namespace tc

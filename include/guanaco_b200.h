@@ -24,7 +24,12 @@
  * device wait ran out; -8 size above a documented maximum.
  *
  * dtype codes follow the reference DataType enum (src/include/types.h:16-24):
- * F32 = 0, Q8_0 = 2, Q4_K = 4, Q6_K = 5.
+ * F32 = 0, F16 = 1, Q8_0 = 2, Q4_K = 4, Q6_K = 5; Q5_K, which that enum lacks
+ * (the reference loader sizes it, src/engine/loader.c:98,117, and rejects
+ * it, :586-651), is 13, GGML's type number.  F16 rows are handled in
+ * "blocks" of 32 halves (64 bytes).  gb_matvec / gb_matvec_host / gb_gemm /
+ * gb_dequant / gb_model_set_matrix / the output head take Q5_K and F16 too;
+ * the reference-facing vtable slots and layer ABI keep the reference's set.
  */
 #ifndef GUANACO_B200_H
 #define GUANACO_B200_H
@@ -124,7 +129,7 @@ int gb_device_error(int clear);
 int gb_matvec_host(int dtype, const void* W, int rows, int cols, const float* h_x, float* h_y);
 
 /* Bit-exact dequantisation of nblocks GGUF blocks into fp32 (256 values per
- * Q4_K / Q6_K block, 32 per Q8_0 block). */
+ * Q4_K / Q6_K / Q5_K block, 32 per Q8_0 block or F16 block of 32 halves). */
 int gb_dequant(int dtype, const void* blocks, size_t nblocks, float* out, void* stream);
 
 /* Seeded synthetic inputs, byte-identical to the CPU generators in the test
@@ -161,7 +166,8 @@ int gb_attention_decode(const float* q, const float* k, const float* v,
 /* Prefill GEMM for T tokens at once on the tcgen05 tensor cores:
  * Y[t][n] = sum_k X[t][k] W[n][k] (+ R[t][n] when R is not NULL; R may be Y),
  * all device pointers, X / Y / R row-major fp32 (T x K, T x N).  W is N rows of
- * GGUF blocks (dtype 4 Q4_K, 5 Q6_K, 2 Q8_0) or fp32 (dtype 0).  fp32-
+ * GGUF blocks (dtype 4 Q4_K, 5 Q6_K, 2 Q8_0, 13 Q5_K) or fp32 / fp16 rows
+ * (dtype 0 / 1).  fp32-
  * equivalent: weights and activations are split into tf32 + fp32 remainders
  * (hi.hi + hi.lo + lo.hi).  Replaces the per-token loop of linear_dispatch
  * (src/engine/engine.c:119-153) for T > 1; the reference's GPU prefill hook is

@@ -157,6 +157,44 @@ void gbo_dequant_q8_0(const void* blocks, size_t nblocks, float* out) {
     }
 }
 
+/* Q5_K: the reference has no Q5_K kernel (its loader sizes the GGUF type,
+ * src/engine/loader.c:98,117, and rejects it, :586-651).  Restated from GGML's
+ * published k-quant layout (llama.cpp ggml-quants, block_q5_K {d, dmin,
+ * scales[12], qh[32], qs[128]}, dequantize_row_q5_K): per 64 columns two
+ * sub-blocks j = 2g, 2g + 1 with get_scale_min_k4 scales; q = low / high
+ * nibble of qs[32 g + l] + 16 * bit j of qh[l]; w = (d sc) q - dmin m with two
+ * roundings, as the reference's Q4_K dequantiser (engine.c:257-275). */
+void gbo_dequant_q5k(const void* blocks, size_t nblocks, float* out) {
+    const uint8_t* base = (const uint8_t*)blocks;
+    for (size_t b = 0; b < nblocks; b++) {
+        const uint8_t* blk = base + b * GBO_Q5K_BYTES;
+        const float d_all = gbo_f16_to_f32(rd16(blk));
+        const float min_all = gbo_f16_to_f32(rd16(blk + 2));
+        const uint8_t* sc = blk + 4;
+        const uint8_t* qh = blk + 16;
+        const uint8_t* q = blk + 48;
+        float* px = out + b * 256;
+        for (int g = 0; g < 4; g++) {
+            uint8_t s, m;
+            gbo_q4k_scale_min(2 * g, sc, &s, &m);
+            const float d1 = d_all * s, m1 = min_all * m;
+            gbo_q4k_scale_min(2 * g + 1, sc, &s, &m);
+            const float d2 = d_all * s, m2 = min_all * m;
+            for (int l = 0; l < 32; l++) px[l] = d1 * ((q[l] & 0xF) + ((qh[l] >> (2 * g)) & 1 ? 16 : 0)) - m1;
+            for (int l = 0; l < 32; l++) px[32 + l] = d2 * ((q[l] >> 4) + ((qh[l] >> (2 * g + 1)) & 1 ? 16 : 0)) - m2;
+            q += 32;
+            px += 64;
+        }
+    }
+}
+
+/* F16 rows: each half converted exactly by the reference's own mapping
+ * (extract_f16_to_f32, src/engine/engine.c:183-212); "blocks" of 32. */
+void gbo_dequant_f16(const void* blocks, size_t nblocks, float* out) {
+    const uint8_t* base = (const uint8_t*)blocks;
+    for (size_t i = 0; i < nblocks * 32; i++) out[i] = gbo_f16_to_f32(rd16(base + 2 * i));
+}
+
 /* ------------------------------------------------------------------------ */
 /* Matvec                                                                    */
 /* ------------------------------------------------------------------------ */
@@ -269,6 +307,34 @@ int gbo_matvec_q8_0(const void* W, int rows, int cols, size_t byte_size, const f
         y[r] = sum;
     }
     return 0;
+}
+
+/* Q5_K / F16 (formats the reference does not compute): each row dequantised
+ * by the definitions above, then dotted with x in 8 FMA lanes summed in the
+ * order of the reference's gemm_f32 row dot (kernels_cpu.c:44-69).  Errors as
+ * the reference kernels: -2 for columns not a multiple of the block width,
+ * -3 when byte_size (if non-zero) is too small. */
+static float dot_lanes(const float* a, const float* b, int K);
+static int matvec_rows(int width, int bbytes, void (*deq)(const void*, size_t, float*), const void* W, int rows,
+                       int cols, size_t byte_size, const float* x, float* y) {
+    if (!W || !x || !y) return -1;
+    if (cols % width) return -2;
+    const size_t rb = (size_t)(cols / width) * bbytes;
+    if (byte_size && rb * (size_t)rows > byte_size) return -3;
+    float* w = (float*)malloc((size_t)cols * sizeof(float));
+    if (!w) return -1;
+    for (int r = 0; r < rows; r++) {
+        deq((const uint8_t*)W + (size_t)r * rb, (size_t)(cols / width), w);
+        y[r] = dot_lanes(w, x, cols);
+    }
+    free(w);
+    return 0;
+}
+int gbo_matvec_q5k(const void* W, int rows, int cols, size_t byte_size, const float* x, float* y) {
+    return matvec_rows(256, GBO_Q5K_BYTES, gbo_dequant_q5k, W, rows, cols, byte_size, x, y);
+}
+int gbo_matvec_f16(const void* W, int rows, int cols, size_t byte_size, const float* x, float* y) {
+    return matvec_rows(32, 64, gbo_dequant_f16, W, rows, cols, byte_size, x, y);
 }
 
 /* ------------------------------------------------------------------------ */
@@ -425,6 +491,8 @@ static int matvec_any(int dtype, const void* W, int rows, int cols, const float*
         case 2: return gbo_matvec_q8_0(W, rows, cols, 0, x, y);
         case 4: return gbo_matvec_q4k(W, rows, cols, 0, x, y);
         case 5: return gbo_matvec_q6k(W, rows, cols, 0, x, y);
+        case GBO_DT_Q5_K: return gbo_matvec_q5k(W, rows, cols, 0, x, y);
+        case 1: return gbo_matvec_f16(W, rows, cols, 0, x, y);
         default: return -1;
     }
 }
@@ -493,32 +561,33 @@ static inline void wr16(uint8_t* p, uint16_t v) { p[0] = (uint8_t)v; p[1] = (uin
 
 /* Q4_K block: d, dmin ~ fp16 U[1e-4,1e-3]; 8 scales and 8 mins U{0..63}
  * packed as get_scale_min_k4 unpacks them; qs uniform bytes (two U{0..15}). */
+void gbo_synth_q4k_at(uint8_t* blk, uint64_t b, uint64_t seed, uint64_t stream) {
+    const uint64_t i0 = b * 32;
+    const uint64_t r0 = gbo_rand64(seed, stream, i0);
+    wr16(blk, synth_scale(r0));
+    wr16(blk + 2, synth_scale(r0 >> 24));
+    const uint64_t r1 = gbo_rand64(seed, stream, i0 + 1);
+    const uint64_t r2 = gbo_rand64(seed, stream, i0 + 2);
+    uint8_t sc[8], mn[8];
+    for (int j = 0; j < 8; j++) {
+        sc[j] = (uint8_t)((r1 >> (6 * j)) & 63);
+        mn[j] = (uint8_t)((r2 >> (6 * j)) & 63);
+    }
+    uint8_t* s = blk + 4;
+    for (int j = 0; j < 4; j++) {
+        s[j] = (uint8_t)(sc[j] | ((sc[j + 4] >> 4) << 6));
+        s[j + 4] = (uint8_t)(mn[j] | ((mn[j + 4] >> 4) << 6));
+        s[j + 8] = (uint8_t)((sc[j + 4] & 0xF) | ((mn[j + 4] & 0xF) << 4));
+    }
+    for (int w = 0; w < 16; w++) {
+        const uint64_t r = gbo_rand64(seed, stream, i0 + 3 + w);
+        memcpy(blk + 16 + 8 * w, &r, 8);
+    }
+}
+
 void gbo_synth_q4k(void* blocks, size_t nblocks, uint64_t seed, uint64_t stream) {
     uint8_t* base = (uint8_t*)blocks;
-    for (size_t b = 0; b < nblocks; b++) {
-        uint8_t* blk = base + b * GBO_Q4K_BYTES;
-        const uint64_t i0 = (uint64_t)b * 32;
-        const uint64_t r0 = gbo_rand64(seed, stream, i0);
-        wr16(blk, synth_scale(r0));
-        wr16(blk + 2, synth_scale(r0 >> 24));
-        const uint64_t r1 = gbo_rand64(seed, stream, i0 + 1);
-        const uint64_t r2 = gbo_rand64(seed, stream, i0 + 2);
-        uint8_t sc[8], mn[8];
-        for (int j = 0; j < 8; j++) {
-            sc[j] = (uint8_t)((r1 >> (6 * j)) & 63);
-            mn[j] = (uint8_t)((r2 >> (6 * j)) & 63);
-        }
-        uint8_t* s = blk + 4;
-        for (int j = 0; j < 4; j++) {
-            s[j] = (uint8_t)(sc[j] | ((sc[j + 4] >> 4) << 6));
-            s[j + 4] = (uint8_t)(mn[j] | ((mn[j + 4] >> 4) << 6));
-            s[j + 8] = (uint8_t)((sc[j + 4] & 0xF) | ((mn[j + 4] & 0xF) << 4));
-        }
-        for (int w = 0; w < 16; w++) {
-            const uint64_t r = gbo_rand64(seed, stream, i0 + 3 + w);
-            memcpy(blk + 16 + 8 * w, &r, 8);
-        }
-    }
+    for (size_t b = 0; b < nblocks; b++) gbo_synth_q4k_at(base + b * GBO_Q4K_BYTES, (uint64_t)b, seed, stream);
 }
 
 /* Q6_K block: ql, qh uniform bytes; scales int8 U{-32..31}; d fp16 U[1e-4,1e-3]. */
@@ -552,6 +621,40 @@ void gbo_synth_q8_0(void* blocks, size_t nblocks, uint64_t seed, uint64_t stream
             const uint64_t r = gbo_rand64(seed, stream, i0 + 1 + w);
             memcpy(blk + 2 + 8 * w, &r, 8);
         }
+    }
+}
+
+/* Q5_K block: the Q4_K block's header and nibbles (same random words), then
+ * 32 bytes of fifth bits from words 19-22. */
+void gbo_synth_q5k(void* blocks, size_t nblocks, uint64_t seed, uint64_t stream) {
+    uint8_t* base = (uint8_t*)blocks;
+    uint8_t tmp[GBO_Q4K_BYTES];
+    for (size_t b = 0; b < nblocks; b++) {
+        uint8_t* blk = base + b * GBO_Q5K_BYTES;
+        /* the Q4_K generator for global block b of this stream */
+        const uint64_t i0 = (uint64_t)b * 32;
+        gbo_synth_q4k_at(tmp, (uint64_t)b, seed, stream);
+        memcpy(blk, tmp, 16);
+        for (int w = 0; w < 4; w++) {
+            const uint64_t r = gbo_rand64(seed, stream, i0 + 19 + w);
+            memcpy(blk + 16 + 8 * w, &r, 8);
+        }
+        memcpy(blk + 48, tmp + 16, 128);
+    }
+}
+
+/* F16 "blocks" of 32 halves: the Irwin-Hall value of gbo_synth_normal at
+ * index i, times 2^-5, rounded to the nearest half (ties to even). */
+void gbo_synth_f16(void* blocks, size_t nblocks, uint64_t seed, uint64_t stream) {
+    uint8_t* base = (uint8_t*)blocks;
+    for (size_t i = 0; i < nblocks * 32; i++) {
+        int32_t acc = 0;
+        for (int w = 0; w < 3; w++) {
+            const uint64_t r = gbo_rand64(seed, stream, 3 * (uint64_t)i + w);
+            acc += (int32_t)(r & 0xffff) + (int32_t)((r >> 16) & 0xffff) +
+                   (int32_t)((r >> 32) & 0xffff) + (int32_t)((r >> 48) & 0xffff);
+        }
+        wr16(base + 2 * i, gbo_f32_to_f16((float)(acc + 6 - 393216) * (1.0f / 2097152.0f)));
     }
 }
 

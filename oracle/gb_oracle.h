@@ -31,6 +31,8 @@ extern "C" {
 #define GBO_Q4K_BYTES 144
 #define GBO_Q6K_BYTES 210
 #define GBO_Q80_BYTES 34
+#define GBO_Q5K_BYTES 176   /* loader.c:117 */
+#define GBO_DT_Q5_K 13      /* GGML's type number; the reference's DataType has none */
 
 /* ---- scalar helpers ---- */
 float    gbo_f16_to_f32(uint16_t h);            /* quant_matvec_q4_k.c:18-45 */
@@ -41,11 +43,15 @@ void     gbo_q4k_scale_min(int j, const uint8_t* q, uint8_t* d, uint8_t* m); /* 
 void gbo_dequant_q4k(const void* blocks, size_t nblocks, float* out);  /* engine.c:248-276 */
 void gbo_dequant_q6k(const void* blocks, size_t nblocks, float* out);  /* quant_matvec_q6_k.c:75-92 */
 void gbo_dequant_q8_0(const void* blocks, size_t nblocks, float* out); /* engine.c:235-240 */
+void gbo_dequant_q5k(const void* blocks, size_t nblocks, float* out);  /* GGML block_q5_K (no reference kernel) */
+void gbo_dequant_f16(const void* blocks, size_t nblocks, float* out);  /* engine.c:183-212, blocks of 32 */
 
 /* ---- matvec y[rows] = W[rows, cols] . x[cols]; return codes as the reference ---- */
 int gbo_matvec_q4k(const void* W, int rows, int cols, size_t byte_size, const float* x, float* y);
 int gbo_matvec_q6k(const void* W, int rows, int cols, size_t byte_size, const float* x, float* y);
 int gbo_matvec_q8_0(const void* W, int rows, int cols, size_t byte_size, const float* x, float* y);
+int gbo_matvec_q5k(const void* W, int rows, int cols, size_t byte_size, const float* x, float* y);
+int gbo_matvec_f16(const void* W, int rows, int cols, size_t byte_size, const float* x, float* y);
 
 /* ---- decode-layer pieces (T = 1) ---- */
 void gbo_rope(float* q, float* k, int n_heads, int n_kv_heads, int head_dim, int pos, float theta);
@@ -78,6 +84,9 @@ uint64_t gbo_rand64(uint64_t seed, uint64_t stream, uint64_t i);
 void gbo_synth_q4k(void* blocks, size_t nblocks, uint64_t seed, uint64_t stream);
 void gbo_synth_q6k(void* blocks, size_t nblocks, uint64_t seed, uint64_t stream);
 void gbo_synth_q8_0(void* blocks, size_t nblocks, uint64_t seed, uint64_t stream);
+void gbo_synth_q4k_at(uint8_t* blk, uint64_t b, uint64_t seed, uint64_t stream);
+void gbo_synth_q5k(void* blocks, size_t nblocks, uint64_t seed, uint64_t stream);
+void gbo_synth_f16(void* blocks, size_t nblocks, uint64_t seed, uint64_t stream);
 void gbo_synth_normal(float* out, size_t n, uint64_t seed, uint64_t stream);
 
 #ifdef __cplusplus

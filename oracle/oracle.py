@@ -20,7 +20,9 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 Q4K_BYTES, Q6K_BYTES, Q80_BYTES = 144, 210, 34
+Q5K_BYTES, F16_BYTES = 176, 64   # F16 in "blocks" of 32 halves
 DT_Q8_0, DT_Q4_K, DT_Q6_K, DT_F32 = 2, 4, 5, 0
+DT_F16, DT_Q5_K = 1, 13   # Q5_K: GGML's type number (the reference's DataType has no Q5_K)
 
 _lib = None
 _ref = None
@@ -43,13 +45,13 @@ def lib() -> C.CDLL:
             build()
         L = C.CDLL(path)
         vp, i, sz, u64 = C.c_void_p, C.c_int, C.c_size_t, C.c_uint64
-        for name in ("gbo_matvec_q4k", "gbo_matvec_q6k", "gbo_matvec_q8_0"):
+        for name in ("gbo_matvec_q4k", "gbo_matvec_q6k", "gbo_matvec_q8_0", "gbo_matvec_q5k", "gbo_matvec_f16"):
             getattr(L, name).argtypes = [vp, i, i, sz, vp, vp]
             getattr(L, name).restype = i
-        for name in ("gbo_dequant_q4k", "gbo_dequant_q6k", "gbo_dequant_q8_0"):
+        for name in ("gbo_dequant_q4k", "gbo_dequant_q6k", "gbo_dequant_q8_0", "gbo_dequant_q5k", "gbo_dequant_f16"):
             getattr(L, name).argtypes = [vp, sz, vp]
             getattr(L, name).restype = None
-        for name in ("gbo_synth_q4k", "gbo_synth_q6k", "gbo_synth_q8_0"):
+        for name in ("gbo_synth_q4k", "gbo_synth_q6k", "gbo_synth_q8_0", "gbo_synth_q5k", "gbo_synth_f16"):
             getattr(L, name).argtypes = [vp, sz, u64, u64]
             getattr(L, name).restype = None
         L.gbo_synth_normal.argtypes = [vp, sz, u64, u64]
@@ -153,17 +155,18 @@ def ref() -> C.CDLL:
 
 # ---------------------------------------------------------------- synthesis
 def block_bytes(dtype: int) -> int:
-    return {DT_Q4_K: Q4K_BYTES, DT_Q6_K: Q6K_BYTES, DT_Q8_0: Q80_BYTES}[dtype]
+    return {DT_Q4_K: Q4K_BYTES, DT_Q6_K: Q6K_BYTES, DT_Q8_0: Q80_BYTES, DT_Q5_K: Q5K_BYTES, DT_F16: F16_BYTES}[dtype]
 
 
 def weights_per_block(dtype: int) -> int:
-    return 32 if dtype == DT_Q8_0 else 256
+    return 32 if dtype in (DT_Q8_0, DT_F16) else 256
 
 
 def synth_blocks(dtype: int, rows: int, cols: int, seed: int, stream: int) -> np.ndarray:
     nb = rows * (cols // weights_per_block(dtype))
     out = np.empty(nb * block_bytes(dtype), dtype=np.uint8)
-    fn = {DT_Q4_K: "gbo_synth_q4k", DT_Q6_K: "gbo_synth_q6k", DT_Q8_0: "gbo_synth_q8_0"}[dtype]
+    fn = {DT_Q4_K: "gbo_synth_q4k", DT_Q6_K: "gbo_synth_q6k", DT_Q8_0: "gbo_synth_q8_0", DT_Q5_K: "gbo_synth_q5k",
+          DT_F16: "gbo_synth_f16"}[dtype]
     getattr(lib(), fn)(_p(out), nb, seed, stream)
     return out
 
@@ -177,7 +180,8 @@ def synth_normal(n: int, seed: int, stream: int) -> np.ndarray:
 # ---------------------------------------------------------------- compute
 def matvec(dtype: int, W: np.ndarray, rows: int, cols: int, x: np.ndarray, byte_size: int = 0):
     y = np.zeros(rows, dtype=np.float32)
-    fn = {DT_Q4_K: "gbo_matvec_q4k", DT_Q6_K: "gbo_matvec_q6k", DT_Q8_0: "gbo_matvec_q8_0"}[dtype]
+    fn = {DT_Q4_K: "gbo_matvec_q4k", DT_Q6_K: "gbo_matvec_q6k", DT_Q8_0: "gbo_matvec_q8_0", DT_Q5_K: "gbo_matvec_q5k",
+          DT_F16: "gbo_matvec_f16"}[dtype]
     rc = getattr(lib(), fn)(_p(W), rows, cols, byte_size, _p(x), _p(y))
     return rc, y
 
@@ -185,7 +189,8 @@ def matvec(dtype: int, W: np.ndarray, rows: int, cols: int, x: np.ndarray, byte_
 def dequant(dtype: int, blocks: np.ndarray) -> np.ndarray:
     nb = blocks.size // block_bytes(dtype)
     out = np.empty(nb * weights_per_block(dtype), dtype=np.float32)
-    fn = {DT_Q4_K: "gbo_dequant_q4k", DT_Q6_K: "gbo_dequant_q6k", DT_Q8_0: "gbo_dequant_q8_0"}[dtype]
+    fn = {DT_Q4_K: "gbo_dequant_q4k", DT_Q6_K: "gbo_dequant_q6k", DT_Q8_0: "gbo_dequant_q8_0", DT_Q5_K: "gbo_dequant_q5k",
+          DT_F16: "gbo_dequant_f16"}[dtype]
     getattr(lib(), fn)(_p(blocks), nb, _p(out))
     return out
 
