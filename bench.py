@@ -642,6 +642,27 @@ def profile_kernel(name: str) -> None:
         out = torch.empty(nh * hd, dtype=torch.float32, device="cuda")
         launch = lambda i: gb.attention_decode(q, k, v, kc[i % copies], vc[i % copies], cs, d_pos, nh, nkv, hd,  # noqa
                                                ms, out, ws, stream=sp)
+    elif name == "prefill":   # whole prefills (launch lists): 1 warm-up + 2 timed
+        c = LLAMA8B
+        dm = gb.DecodeModel(c["hidden_dim"], c["n_heads"], c["n_kv_heads"], c["n_layers"], c["ff_dim"],
+                            c["vocab_size"], PREFILL_T + 8)
+        dm.synthesize(SEED)
+        toks = torch.randint(0, c["vocab_size"], (PREFILL_T,), dtype=torch.int32,
+                             generator=torch.Generator().manual_seed(SEED)).to("cuda")
+        lg = torch.empty(c["vocab_size"], device="cuda")
+        nx = torch.empty(1, dtype=torch.int32, device="cuda")
+        dm.prefill(toks, PREFILL_T, 0, lg, nx, stream=sp)
+        st.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(2):
+            dm.prefill(toks, PREFILL_T, 0, lg, nx, stream=sp)
+        e1.record(st)
+        e1.synchronize()
+        err = dm.error()
+        dm.close()
+        print(json.dumps({"kernel": name, "ms_per_prefill": round(e0.elapsed_time(e1) / 2, 2), "error": err}))
+        return
     elif name == "pf_attn":   # prefill causal attention, 4096-token prompt at position 0
         nh, nkv, hd, T = 32, 8, 128, PREFILL_T
         n = nkv * T * hd
@@ -737,7 +758,7 @@ def main():
                     help="run the warm-up and timed decode steps only (for ncu launch lists) and exit")
     ap.add_argument("--steps-ref", type=int, default=None, help="reference arm samples (default min(steps, 5))")
     ap.add_argument("--kernel", choices=["q4k", "q4k_gu", "q6k", "q6k_head", "q8_0", "attn", "pf_attn", "gemm_q4k",
-                                         "gemm_q6k"], default=None,
+                                         "gemm_q6k", "prefill"], default=None,
                     help="run only a few launches of one kernel (for ncu captures) and exit")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":

@@ -54,8 +54,8 @@ __global__ void __launch_bounds__(256) k_pf_rope_kv(float* __restrict__ q, const
 // the cache serves all the heads that share it.  Keys stream in tiles of 64
 // through a two-stage cp.async ring; scores, the online softmax (running max
 // and sum per row, as flash attention does) and P.V run on the fp32 CUDA
-// cores.  Thread (tr, tc) owns rows tr + 16 i and keys tc + 16 j of a tile
-// (i, j < 4) and output columns 4 tc + 64 c .. + 3.  The reference's order
+// cores (packed two-wide FMAs).  Thread (tr, tc) owns rows tr + 16 i and keys
+// tc + 16 j of a tile (i, j < 4) and output columns 4 tc + 64 c .. + 3.  The reference's order
 // (engine.c:431-500: scores * scale, -inf above the diagonal, softmax,
 // scores . V) is kept; only the summation order differs.
 constexpr int PA_R = 64;        // (head, query) rows per CTA
@@ -138,11 +138,13 @@ __global__ void __launch_bounds__(PA_THREADS) k_pf_attn(const float* __restrict_
         const float* Kb = Ks + b * PA_BK * LD;
         const float* Vb = Vs + b * PA_BK * LD;
         // ---- scores
-        float s[4][4];
+        // two partial sums per score (even / odd columns), two FMAs per
+        // packed instruction
+        float2 s2[4][4];
 #pragma unroll
         for (int i = 0; i < 4; i++)
 #pragma unroll
-            for (int j = 0; j < 4; j++) s[i][j] = 0.f;
+            for (int j = 0; j < 4; j++) s2[i][j] = make_float2(0.f, 0.f);
 #pragma unroll 4
         for (int d = 0; d < HD; d += 4) {
             float4 qv[4], kv[4];
@@ -154,12 +156,15 @@ __global__ void __launch_bounds__(PA_THREADS) k_pf_attn(const float* __restrict_
             for (int i = 0; i < 4; i++)
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
-                    s[i][j] = fmaf(qv[i].x, kv[j].x, s[i][j]);
-                    s[i][j] = fmaf(qv[i].y, kv[j].y, s[i][j]);
-                    s[i][j] = fmaf(qv[i].z, kv[j].z, s[i][j]);
-                    s[i][j] = fmaf(qv[i].w, kv[j].w, s[i][j]);
+                    s2[i][j] = __ffma2_rn(make_float2(qv[i].x, qv[i].y), make_float2(kv[j].x, kv[j].y), s2[i][j]);
+                    s2[i][j] = __ffma2_rn(make_float2(qv[i].z, qv[i].w), make_float2(kv[j].z, kv[j].w), s2[i][j]);
                 }
         }
+        float s[4][4];
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) s[i][j] = s2[i][j].x + s2[i][j].y;
         // ---- scale, causal mask, online softmax
         float p[4][4];
 #pragma unroll
@@ -202,10 +207,13 @@ __global__ void __launch_bounds__(PA_THREADS) k_pf_attn(const float* __restrict_
                 const float4 vv = *reinterpret_cast<const float4*>(Vb + kk * LD + 64 * c + 4 * tc);
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
-                    o[i][4 * c] = fmaf(pr[i], vv.x, o[i][4 * c]);
-                    o[i][4 * c + 1] = fmaf(pr[i], vv.y, o[i][4 * c + 1]);
-                    o[i][4 * c + 2] = fmaf(pr[i], vv.z, o[i][4 * c + 2]);
-                    o[i][4 * c + 3] = fmaf(pr[i], vv.w, o[i][4 * c + 3]);
+                    const float2 pp = make_float2(pr[i], pr[i]);
+                    float2 lo = __ffma2_rn(pp, make_float2(vv.x, vv.y), make_float2(o[i][4 * c], o[i][4 * c + 1]));
+                    float2 hi = __ffma2_rn(pp, make_float2(vv.z, vv.w), make_float2(o[i][4 * c + 2], o[i][4 * c + 3]));
+                    o[i][4 * c] = lo.x;
+                    o[i][4 * c + 1] = lo.y;
+                    o[i][4 * c + 2] = hi.x;
+                    o[i][4 * c + 3] = hi.y;
                 }
             }
         }
