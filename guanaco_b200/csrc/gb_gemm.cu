@@ -15,9 +15,9 @@
 //
 // CTA tile: 128 weight rows (the MMA's M) x BT = 128 tokens (its N), K in
 // chunks of 32.  Warps 0-3 convert weights: thread r dequantises row r's 32
-// weights of the chunk (Q4_K: 16-byte loads of a chunk pair's nibbles; Q6_K:
-// 4-byte words of a 128-column half-block; the next pair / half-block loaded
-// before this one is converted).  Warp 13 loads each chunk's raw activation
+// weights of the chunk (Q4_K / Q5_K: 16-byte loads of a chunk pair's bytes,
+// three / two pairs in flight; Q6_K: 4-byte words of a 128-column
+// half-block, the next one loaded before this one is converted).  Warp 13 loads each chunk's raw activation
 // tile [128 tokens][32] fp32 by TMA into the stage, and warps 9-12 split it
 // in place.  Both land in a 3-stage shared-memory ring in the tensor cores'
 // K-major layout (gb_tc.cuh).
@@ -247,11 +247,19 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
                     w.ha = w.hb = make_uint4(0u, 0u, 0u, 0u);
                 }
             };
-            Raw cur, nxt;
+            // D pairs in flight (3 for Q4_K, 2 for Q5_K's larger pairs): the
+            // loads of pair p + D are issued before pair p is converted
+            constexpr int D = Q5 ? 2 : 3;
+            const int np = nk / 2;
+            Raw cur, n1, n2;
             load(0, cur);
-            for (int p = 0; p < nk / 2; p++) {
-                nxt = cur;
-                if (p + 1 < nk / 2) load(p + 1, nxt);
+            n1 = cur;
+            n2 = cur;
+            if (np > 1) load(1, n1);
+            if (D == 3 && np > 2) load(2, n2);
+            for (int p = 0; p < np; p++) {
+                Raw n3 = D == 3 ? n2 : n1;
+                if (p + D < np) load(p + D, n3);
                 const uint4 hd = cur.hd;
                 const float d = f16_bits_to_f32(hd.x & 0xFFFF), dmin = f16_bits_to_f32(hd.x >> 16);
                 const uint32_t sw[3] = {hd.y, hd.z, hd.w};
@@ -281,7 +289,14 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
                     }
                     put(2 * p + h, v);
                 }
-                cur = nxt;
+                if (D == 3) {
+                    cur = n1;
+                    n1 = n2;
+                    n2 = n3;
+                } else {
+                    cur = n1;
+                    n1 = n3;
+                }
             }
         } else if constexpr (DT == GB_DT_Q6_K) {
             // one 128-column half-block (4 chunks) per step: its ql (64 B),
