@@ -103,6 +103,7 @@ SIGNATURES = {
     "gb_gemm": (_i, [_i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "gb_gemm_error": (_i, [_i]),
     "gb_prefill_attention": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
+    "gb_prefill_attention_error": (_i, [_i]),
     "gb_dequant": (_i, [_i, _vp, _sz, _vp, _vp]),
     "gb_synth_blocks": (_i, [_i, _vp, _sz, _u64, _u64, _vp]),
     "gb_synth_normal": (_i, [_vp, _sz, _u64, _u64, _vp]),

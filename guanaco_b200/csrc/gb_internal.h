@@ -196,8 +196,10 @@ struct PrefillArgs {
 };
 int enqueue_prefill_layer(const PrefillArgs& a, cudaStream_t st);
 // Causal attention of T query rows (positions pos0 ..) over the cache.
+// Timeouts of its bounded waits go to *err (null: the module word read by
+// gb_prefill_attention_error).
 int prefill_attention(const float* q, const float* kc, const float* vc, float* out, int T, int pos0, int n_heads,
-                      int n_kv, int head_dim, int max_seq, cudaStream_t st);
+                      int n_kv, int head_dim, int max_seq, cudaStream_t st, unsigned* err);
 // Synthetic blocks of a slice of a larger matrix: local block r * sn + j
 // (r < rows, j < sn) is global block (row0 + r) * nbg + c0 + j of stream
 // stream_id, written at out block r * ldo + j (ldo >= sn; blocks j >= sn of a

@@ -16,8 +16,15 @@
 // decode layout [n_kv][max_seq][hd], so decode continues from pos0 + T.
 #include "gb_common.cuh"
 #include "gb_internal.h"
+#include "gb_mt.cuh"
+#include "gb_tc.cuh"
+
+#include <stdlib.h>
+#include <string.h>
 
 namespace gb {
+
+__device__ unsigned g_pf_err;   // bounded-wait timeouts of gb_prefill_attention (no model error word)
 
 // ---------------------------------------------------------------- RoPE + KV append
 // Row t (position pos0 + t): q heads rotated in place, k heads rotated into
@@ -244,14 +251,350 @@ static cudaError_t launch_pf_attn(const float* q, const float* kc, const float* 
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------- causal attention on the tensor cores
+// One CTA: KV head g and TA_R = 128 (head, query) rows (GROUP heads x 128 /
+// GROUP queries), keys in tiles of TA_NK = 32.  3xTF32 as the GEMM (gb_gemm.cu):
+// every operand is split into a tf32 part and an fp32 remainder and the
+// tensor cores sum hi.hi + hi.lo + lo.hi.
+//   S = Q K^T   A = Q (resident in shared memory as hi / lo, M 128 x K hd),
+//               B = the K tile (N 32 keys x K hd), S in tensor memory,
+//               double-buffered so S(t + 1) is computed during softmax(t)
+//   softmax     warps 0-3, thread = row = tensor-memory lane: the scores
+//               scaled and masked as the reference does (engine.c:431-500),
+//               running max and sum (online softmax); P = exp(s - m) split
+//               into shared memory; O (tensor memory) rescaled by
+//               exp(m_old - m_new) before the next P.V accumulates into it
+//   O += P V    A = P (M 128 x K 32), B = V^T (N hd x K 32: the converters
+//               transpose the V tile)
+// Warps 4-7 convert the K / V tiles (read from the cache, L2-resident,
+// loaded one tile ahead); warp 8 owns the tensor memory and one lane issues
+// the MMAs.  Every wait is bounded and records GB_ETIMEOUT.
+constexpr int TA_R = 128;
+constexpr int TA_NK = 32;
+constexpr int TA_THREADS = 9 * 32;
+
+template <int HD>
+struct TaLayout {
+    static constexpr int QSUB = TA_R * 32 * 4;            // one [128 x 32] sub-tile (16 KB)
+    static constexpr int KSUB = TA_NK * 32 * 4;           // one [32 x 32] sub-tile (4 KB)
+    static constexpr int NS = HD / 32;                    // sub-tiles along head_dim
+    static constexpr int Q_HI = 0, Q_LO = NS * QSUB;
+    static constexpr int K_HI = 2 * NS * QSUB, K_LO = K_HI + NS * KSUB;
+    static constexpr int V_HI = K_HI + 2 * NS * KSUB;     // V^T [HD x 32 keys]
+    static constexpr int V_LO = V_HI + HD * TA_NK * 4;
+    static constexpr int P_HI = V_LO + HD * TA_NK * 4;    // P [128 x 32 keys]
+    static constexpr int P_LO = P_HI + QSUB;
+    static constexpr int BYTES = P_LO + QSUB;
+    static constexpr int SMEM = BYTES + 1024;             // + alignment slack
+    static constexpr uint32_t TMEM_COLS = 256;            // S[2] at 0 / 32, O at 128
+};
+static_assert(TaLayout<128>::SMEM <= 227 * 1024, "shared memory");
+
+__device__ __forceinline__ bool ta_wait(uint32_t bar, uint32_t parity, unsigned* err) {
+    if (mbs_test(bar, parity)) return true;
+    const uint64_t t0 = gtimer();
+    while (!mbs_test(bar, parity))
+        if (gtimer() - t0 > MT_WAIT_NS) {
+            atomicExch(err, (unsigned)(-GB_ETIMEOUT));
+            return false;
+        }
+    return true;
+}
+
+// 4 consecutive fp32 values split into the hi / lo tiles at byte offset off.
+__device__ __forceinline__ void ta_store4(uint8_t* hi, uint8_t* lo, uint32_t off, float4 v) {
+    float4 h, l;
+    tc::split_tf32(v.x, h.x, l.x);
+    tc::split_tf32(v.y, h.y, l.y);
+    tc::split_tf32(v.z, h.z, l.z);
+    tc::split_tf32(v.w, h.w, l.w);
+    *reinterpret_cast<float4*>(hi + off) = h;
+    *reinterpret_cast<float4*>(lo + off) = l;
+}
+
+template <int HD, int GROUP>
+__global__ void __launch_bounds__(TA_THREADS, 1)
+k_pf_attn_tc(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+             float* __restrict__ out, int T, int pos0, int nh, int max_seq, unsigned* err) {
+    using L = TaLayout<HD>;
+    constexpr int BQ = TA_R / GROUP, NS = L::NS;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    __shared__ __align__(8) uint64_t bars[9];
+    __shared__ uint32_t tmem_slot;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = blockIdx.y;
+    const int qb = gridDim.x - 1 - blockIdx.x;   // longest blocks first
+    const int q0 = qb * BQ, QD = nh * HD;
+    const float* kh = kc + (size_t)g * max_seq * HD;
+    const float* vh = vc + (size_t)g * max_seq * HD;
+    const int kend = pos0 + min(q0 + BQ, T);     // keys 0 .. kend - 1
+    const int nt = (kend + TA_NK - 1) / TA_NK;
+    const uint32_t b0 = tc::smem_u32(&bars[0]);
+    const uint32_t kfull = b0, kempty = b0 + 8, vfull = b0 + 16, pfull = b0 + 24, pvdone = b0 + 32;
+    const uint32_t sfull = b0 + 40, sfree = b0 + 56;   // [2] each
+    if (tid == 0) {
+        mbs_init(kfull, 4);    // the converter warps
+        mbs_init(kempty, 1);   // MMA commit: the scores of the K tile are done
+        mbs_init(vfull, 4);
+        mbs_init(pfull, 4);    // the softmax warps: P written, O rescaled
+        mbs_init(pvdone, 1);   // MMA commit: O += P V done
+        for (int b = 0; b < 2; b++) {
+            mbs_init(sfull + 8 * b, 1);
+            mbs_init(sfree + 8 * b, 4);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 8) tc::tmem_alloc(&tmem_slot, L::TMEM_COLS);
+    // Q rows (row r = head g GROUP + r / BQ, query q0 + r % BQ; zero past T),
+    // split into [128 x 32] sub-tiles along head_dim
+    for (int e = tid; e < TA_R * HD / 4; e += TA_THREADS) {
+        const int r = e / (HD / 4), d = 4 * (e % (HD / 4));
+        const int t = q0 + r % BQ, h = g * GROUP + r / BQ;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (t < T) v = *reinterpret_cast<const float4*>(q + (size_t)t * QD + (size_t)h * HD + d);
+        ta_store4(sm + L::Q_HI, sm + L::Q_LO, (d >> 5) * L::QSUB + tc::tile_off(r, d & 31, TA_R), v);
+    }
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = tmem_slot;
+    bool ok = true;
+
+    if (warp == 8) {   // ---- MMA issue (one lane)
+        if (lane == 0) {
+            constexpr uint32_t idS = tc::idesc_tf32(TA_R, TA_NK), idO = tc::idesc_tf32(TA_R, HD);
+            constexpr uint32_t LQ = TA_R / 8 * 128, LK = TA_NK / 8 * 128, LV = HD / 8 * 128;
+            const uint32_t base = tc::smem_u32(sm);
+            auto scores = [&](int t) {   // S[t & 1] = Q K^T over head_dim: NS sub-tiles x 4 k-steps x 3 products
+                const uint32_t S = tmem + (uint32_t)(32 * (t & 1));
+#pragma unroll
+                for (int c = 0; c < NS; c++)
+#pragma unroll
+                    for (int ks = 0; ks < 4; ks++) {
+                        const uint64_t qh = tc::smem_desc(base + L::Q_HI + c * L::QSUB + ks * 2 * LQ, LQ, 128);
+                        const uint64_t ql = tc::smem_desc(base + L::Q_LO + c * L::QSUB + ks * 2 * LQ, LQ, 128);
+                        const uint64_t kh2 = tc::smem_desc(base + L::K_HI + c * L::KSUB + ks * 2 * LK, LK, 128);
+                        const uint64_t kl2 = tc::smem_desc(base + L::K_LO + c * L::KSUB + ks * 2 * LK, LK, 128);
+                        tc::mma_tf32(S, qh, kh2, idS, c > 0 || ks > 0);
+                        tc::mma_tf32(S, qh, kl2, idS, true);
+                        tc::mma_tf32(S, ql, kh2, idS, true);
+                    }
+                tc::mma_commit(sfull + 8 * (t & 1));
+                tc::mma_commit(kempty);
+            };
+            if (ok) ok = ta_wait(kfull, 0, err);
+            if (ok) {
+                tc::fence_after_sync();
+                scores(0);
+            }
+            for (int t = 0; t < nt && ok; t++) {
+                if (t + 1 < nt) {   // the next tile's scores run during this tile's softmax
+                    ok = ta_wait(kfull, (t + 1) & 1, err);
+                    if (ok && t + 1 >= 2) ok = ta_wait(sfree + 8 * ((t + 1) & 1), (((t + 1) >> 1) - 1) & 1, err);
+                    if (!ok) break;
+                    tc::fence_after_sync();
+                    scores(t + 1);
+                }
+                ok = ta_wait(pfull, t & 1, err) && ta_wait(vfull, t & 1, err);
+                if (!ok) break;
+                tc::fence_after_sync();
+                const uint32_t O = tmem + 128u;
+#pragma unroll
+                for (int ks = 0; ks < 4; ks++) {   // O (+)= P V over the tile's 32 keys
+                    const uint64_t ph = tc::smem_desc(base + L::P_HI + ks * 2 * LQ, LQ, 128);
+                    const uint64_t pl = tc::smem_desc(base + L::P_LO + ks * 2 * LQ, LQ, 128);
+                    const uint64_t vh2 = tc::smem_desc(base + L::V_HI + ks * 2 * LV, LV, 128);
+                    const uint64_t vl2 = tc::smem_desc(base + L::V_LO + ks * 2 * LV, LV, 128);
+                    tc::mma_tf32(O, ph, vh2, idO, t > 0 || ks > 0);
+                    tc::mma_tf32(O, ph, vl2, idO, true);
+                    tc::mma_tf32(O, pl, vh2, idO, true);
+                }
+                tc::mma_commit(pvdone);
+            }
+        }
+        __syncwarp();
+    } else if (warp >= 4) {   // ---- warps 4-7: K and V tiles (the next tile's loads issued once this one is stored)
+        const int cw = warp - 4, ct = tid - 128;
+        // K: lane (j = lane % 8, e = lane / 8) takes key 8 cw + j and the
+        // float4 columns 4 it + e of it: a quarter-warp writes one core
+        // matrix (8 keys, conflict-free) and reads 8 rows x 16 bytes
+        constexpr int KIT = HD / 16;
+        const int kj = 8 * cw + (lane & 7), ke = lane >> 3;
+        // V^T: thread ct takes head_dim column d = ct % HD and keys
+        // kv0 .. kv0 + VK - 1 (kv0 = VK (ct / HD)); a warp reads 32
+        // consecutive floats of one key row
+        constexpr int VK = TA_NK * HD / 128;   // keys per thread (32 for hd 128, 16 for 64)
+        const int vd = ct % HD, kv0 = VK * (ct / HD);
+        float4 kr[KIT];
+        float vr[VK];
+        auto load_k = [&](int t) {
+            const int key = t * TA_NK + kj;
+#pragma unroll
+            for (int i = 0; i < KIT; i++)
+                kr[i] = key < kend ? __ldg(reinterpret_cast<const float4*>(kh + (size_t)key * HD + 4 * (4 * i + ke)))
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+        };
+        auto load_v = [&](int t) {
+#pragma unroll
+            for (int i = 0; i < VK; i++) {
+                const int kv = t * TA_NK + kv0 + i;
+                vr[i] = kv < kend ? __ldg(vh + (size_t)kv * HD + vd) : 0.f;   // rows past the range: zero
+            }
+        };
+        load_k(0);
+        load_v(0);
+        for (int t = 0; t < nt; t++) {
+            // K(t) once the scores of tile t - 1 are done; then tile t + 1's K loads
+            if (t > 0 && ok) ok = ta_wait(kempty, (t - 1) & 1, err);
+#pragma unroll
+            for (int i = 0; i < KIT; i++) {
+                const int d = 4 * (4 * i + ke);
+                ta_store4(sm + L::K_HI, sm + L::K_LO, (d >> 5) * L::KSUB + tc::tile_off(kj, d & 31, TA_NK), kr[i]);
+            }
+            tc::fence_async_smem();
+            __syncwarp();
+            if (lane == 0) mbs_arrive(kfull);
+            if (t + 1 < nt) load_k(t + 1);
+            // V(t) once O += P V of tile t - 1 is done; then tile t + 1's V loads
+            if (t > 0 && ok) ok = ta_wait(pvdone, (t - 1) & 1, err);
+#pragma unroll
+            for (int i = 0; i < VK; i += 4)
+                ta_store4(sm + L::V_HI, sm + L::V_LO, tc::tile_off(vd, kv0 + i, HD),
+                          make_float4(vr[i], vr[i + 1], vr[i + 2], vr[i + 3]));
+            tc::fence_async_smem();
+            __syncwarp();
+            if (lane == 0) mbs_arrive(vfull);
+            if (t + 1 < nt) load_v(t + 1);
+        }
+    } else {   // ---- warps 0-3: softmax, O rescale, output; thread = row r = tensor-memory lane
+        const int r = tid;
+        const int tq = q0 + r % BQ, h = g * GROUP + r / BQ;
+        const int qpos = pos0 + tq;
+        const uint32_t lb = tmem + ((uint32_t)(warp * 32) << 16);
+        const uint32_t O = lb + 128u;
+        const float scale = 1.0f / sqrtf((float)HD);
+        float m = -INFINITY, l = 0.f;
+        for (int t = 0; t < nt; t++) {
+            const int b = t & 1;
+            if (ok) ok = ta_wait(sfull + 8 * b, (t >> 1) & 1, err);
+            tc::fence_after_sync();
+            float sc[TA_NK];
+            {
+                float a16[16];
+                tc::tmem_ld16(lb + (uint32_t)(32 * b), a16);
+#pragma unroll
+                for (int i = 0; i < 16; i++) sc[i] = a16[i];
+                tc::tmem_ld16(lb + (uint32_t)(32 * b + 16), a16);
+#pragma unroll
+                for (int i = 0; i < 16; i++) sc[16 + i] = a16[i];
+            }
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbs_arrive(sfree + 8 * b);   // S[b] may be overwritten
+            // scale, causal mask (key > query position: -inf), online softmax
+            float mx = -INFINITY;
+#pragma unroll
+            for (int i = 0; i < TA_NK; i++) {
+                const int key = t * TA_NK + i;
+                sc[i] = key > qpos ? -INFINITY : sc[i] * scale;
+                mx = fmaxf(mx, sc[i]);
+            }
+            const float mn = fmaxf(m, mx);   // finite: key 0 is in every row's range
+            const float alpha = expf(m - mn);
+            float sum = 0.f;
+#pragma unroll
+            for (int i = 0; i < TA_NK; i++) {
+                sc[i] = expf(sc[i] - mn);
+                sum += sc[i];
+            }
+            l = fmaf(l, alpha, sum);
+            m = mn;
+            if (t > 0) {   // P and V of tile t - 1 consumed, O holds its sum: rescale O
+                if (ok) ok = ta_wait(pvdone, (t - 1) & 1, err);
+                tc::fence_after_sync();
+                if (!__all_sync(0xffffffffu, alpha == 1.0f)) {
+#pragma unroll 1
+                    for (int c = 0; c < HD; c += 16) {
+                        float o16[16];
+                        tc::tmem_ld16(O + (uint32_t)c, o16);
+#pragma unroll
+                        for (int i = 0; i < 16; i++) o16[i] *= alpha;
+                        tc::tmem_st16(O + (uint32_t)c, o16);
+                    }
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < TA_NK / 4; j++)
+                ta_store4(sm + L::P_HI, sm + L::P_LO, tc::tile_off(r, 4 * j, TA_R),
+                          make_float4(sc[4 * j], sc[4 * j + 1], sc[4 * j + 2], sc[4 * j + 3]));
+            tc::fence_async_smem();   // P (generic stores) -> tensor-core reads
+            tc::fence_before_sync();  // O (tensor-memory stores) -> the next MMA
+            __syncwarp();
+            if (lane == 0) mbs_arrive(pfull);
+        }
+        if (ok) ok = ta_wait(pvdone, (nt - 1) & 1, err);
+        tc::fence_after_sync();
+        const float inv = 1.0f / l;
+        float* dst = out + (size_t)tq * QD + (size_t)h * HD;
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 16) {
+            float o16[16];
+            tc::tmem_ld16(O + (uint32_t)c, o16);
+            if (tq < T && ok)
+#pragma unroll
+                for (int i = 0; i < 16; i += 4)
+                    *reinterpret_cast<float4*>(dst + c + i) =
+                        make_float4(o16[i] * inv, o16[i + 1] * inv, o16[i + 2] * inv, o16[i + 3] * inv);
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 8) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, L::TMEM_COLS);
+    }
+}
+
+template <int HD, int GROUP>
+static cudaError_t launch_pf_attn_tc(const float* q, const float* kc, const float* vc, float* out, int T, int pos0,
+                                     int n_kv, int max_seq, unsigned* err, cudaStream_t st) {
+    constexpr int smem = TaLayout<HD>::SMEM;
+    cudaError_t e = set_smem_once(reinterpret_cast<const void*>(k_pf_attn_tc<HD, GROUP>), smem);
+    if (e != cudaSuccess) return e;
+    constexpr int BQ = TA_R / GROUP;
+    dim3 grid((T + BQ - 1) / BQ, n_kv);
+    k_pf_attn_tc<HD, GROUP><<<grid, TA_THREADS, smem, st>>>(q, kc, vc, out, T, pos0, n_kv * GROUP, max_seq, err);
+    return cudaGetLastError();
+}
+
+// GB_PF_ATTN=cuda selects the CUDA-core kernel (for comparison); the default
+// is the tensor-core kernel.
+static bool pf_attn_tensor_cores() {
+    static const bool tc = [] {
+        const char* e = getenv("GB_PF_ATTN");
+        return !(e && !strcmp(e, "cuda"));
+    }();
+    return tc;
+}
+
 int prefill_attention(const float* q, const float* kc, const float* vc, float* out, int T, int pos0, int n_heads,
-                      int n_kv, int head_dim, int max_seq, cudaStream_t st) {
+                      int n_kv, int head_dim, int max_seq, cudaStream_t st, unsigned* err) {
     if (!q || !kc || !vc || !out || T <= 0 || pos0 < 0 || n_kv <= 0 || n_heads % n_kv || pos0 + T > max_seq)
         return GB_EINVAL;
+    if (!err) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_pf_err) != cudaSuccess) return GB_ECUDA;
+        err = static_cast<unsigned*>(p);
+    }
     const int group = n_heads / n_kv;
+    const bool tcore = pf_attn_tensor_cores();
     cudaError_t e = cudaErrorInvalidValue;
-#define GB_PA_CASE(HDV, GV) \
-    if (head_dim == HDV && group == GV) e = launch_pf_attn<HDV, GV>(q, kc, vc, out, T, pos0, n_kv, max_seq, st);
+#define GB_PA_CASE(HDV, GV)                                                                            \
+    if (head_dim == HDV && group == GV)                                                                \
+        e = tcore ? launch_pf_attn_tc<HDV, GV>(q, kc, vc, out, T, pos0, n_kv, max_seq, err, st)        \
+                  : launch_pf_attn<HDV, GV>(q, kc, vc, out, T, pos0, n_kv, max_seq, st);
     GB_PA_CASE(128, 1) GB_PA_CASE(128, 2) GB_PA_CASE(128, 4) GB_PA_CASE(128, 8)
     GB_PA_CASE(64, 1) GB_PA_CASE(64, 2) GB_PA_CASE(64, 4) GB_PA_CASE(64, 8)
 #undef GB_PA_CASE
@@ -272,7 +615,7 @@ int enqueue_prefill_layer(const PrefillArgs& a, cudaStream_t st) {
     if ((rc = gemm(GB_WV, a.xn, a.v, nullptr, KVD, H))) return rc;
     k_pf_rope_kv<<<T, 256, 0, st>>>(a.q, a.k, a.v, a.kc, a.vc, a.rope, a.pos0, a.n_heads, a.n_kv, a.hd, a.max_seq);
     if (cudaGetLastError() != cudaSuccess) return GB_ECUDA;
-    if ((rc = prefill_attention(a.q, a.kc, a.vc, a.attn, T, a.pos0, a.n_heads, a.n_kv, a.hd, a.max_seq, st)))
+    if ((rc = prefill_attention(a.q, a.kc, a.vc, a.attn, T, a.pos0, a.n_heads, a.n_kv, a.hd, a.max_seq, st, a.err)))
         return rc;
     if ((rc = gemm(GB_WO, a.attn, a.hidden, a.hidden, H, QD))) return rc;
     if ((rc = rmsnorm_rows(a.hidden, a.rf, a.xn, H, T, a.eps, st))) return rc;
@@ -288,5 +631,15 @@ extern "C" int gb_prefill_attention(const float* q, const float* k_cache, const 
                                     int n_tokens, int pos, int n_heads, int n_kv_heads, int head_dim, int max_seq,
                                     void* stream) {
     return gb::prefill_attention(q, k_cache, v_cache, out, n_tokens, pos, n_heads, n_kv_heads, head_dim, max_seq,
-                                 static_cast<cudaStream_t>(stream));
+                                 static_cast<cudaStream_t>(stream), nullptr);
+}
+
+extern "C" int gb_prefill_attention_error(int clear) {
+    unsigned v = 0;
+    if (cudaMemcpyFromSymbol(&v, gb::g_pf_err, sizeof(v)) != cudaSuccess) return GB_ECUDA;
+    if (clear && v) {
+        const unsigned z = 0;
+        if (cudaMemcpyToSymbol(gb::g_pf_err, &z, sizeof(z)) != cudaSuccess) return GB_ECUDA;
+    }
+    return -(int)v;
 }

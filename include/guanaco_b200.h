@@ -182,10 +182,14 @@ int gb_gemm_error(int clear);
  * [0, pos + n_tokens) are filled: out[t][h*hd..] = softmax over keys
  * s <= pos + t of (q_t . k_s) / sqrt(hd), times v_s.  q / out row-major
  * [n_tokens][n_heads * head_dim]; caches [n_kv][max_seq][hd].  The T > 1
- * attention of transformer_layer (src/engine/engine.c:431-500).  head_dim 64
+ * attention of transformer_layer (src/engine/engine.c:431-500), on the tensor
+ * cores (fp32-equivalent 3xTF32 scores and P.V, fp32 softmax).  head_dim 64
  * or 128; n_heads / n_kv_heads in {1, 2, 4, 8}.  Asynchronous on `stream`. */
 int gb_prefill_attention(const float* q, const float* k_cache, const float* v_cache, float* out, int n_tokens,
                          int pos, int n_heads, int n_kv_heads, int head_dim, int max_seq, void* stream);
+/* Device error word of gb_prefill_attention's bounded waits (GB_ETIMEOUT);
+ * clear != 0 resets it. */
+int gb_prefill_attention_error(int clear);
 
 /* Frees every device copy the vtable matvec slots made of weights that were
  * never uploaded (the engine's lm_head).  Those copies are keyed by host
