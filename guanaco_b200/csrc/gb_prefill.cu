@@ -253,42 +253,46 @@ static cudaError_t launch_pf_attn(const float* q, const float* kc, const float* 
 
 // ---------------------------------------------------------------- causal attention on the tensor cores
 // One CTA: KV head g and TA_R = 128 (head, query) rows (GROUP heads x 128 /
-// GROUP queries), keys in tiles of TA_NK = 32.  3xTF32 as the GEMM (gb_gemm.cu):
+// GROUP queries), keys in tiles of TA_NK = 64.  3xTF32 as the GEMM (gb_gemm.cu):
 // every operand is split into a tf32 part and an fp32 remainder and the
 // tensor cores sum hi.hi + hi.lo + lo.hi.
-//   S = Q K^T   A = Q (resident in shared memory as hi / lo, M 128 x K hd),
-//               B = the K tile (N 32 keys x K hd), S in tensor memory,
-//               double-buffered so S(t + 1) is computed during softmax(t)
+//   S = Q K^T   A = Q, resident in tensor memory as hi / lo (lane = row,
+//               head_dim columns each), B = the K tile in shared memory
+//               (N 64 keys x K head_dim); S in tensor memory, double-buffered
+//               so S(t + 1) is computed during softmax(t)
 //   softmax     warps 0-3, thread = row = tensor-memory lane: the scores
 //               scaled and masked as the reference does (engine.c:431-500),
-//               running max and sum (online softmax); P = exp(s - m) split
-//               into shared memory; O (tensor memory) rescaled by
-//               exp(m_old - m_new) before the next P.V accumulates into it
-//   O += P V    A = P (M 128 x K 32), B = V^T (N hd x K 32: the converters
+//               running max and sum (online softmax, the max moved only when
+//               exceeded by more than TA_TAU); P = exp(s - m) split into
+//               shared memory; O (tensor memory) rescaled by exp(m_old -
+//               m_new) before the next P.V accumulates into it, when m moved
+//   O += P V    A = P (M 128 x K 64), B = V^T (N hd x K 64: the converters
 //               transpose the V tile)
-// Warps 4-7 convert the K / V tiles (read from the cache, L2-resident,
-// loaded one tile ahead); warp 8 owns the tensor memory and one lane issues
-// the MMAs.  Every wait is bounded and records GB_ETIMEOUT.
+// Tensor memory: Q hi [0, hd), Q lo [hd, 2 hd), S[2] at 2 hd + 0 / 64, O at
+// 2 hd + 128 (512 columns at hd 128).  Warps 4-7 convert the K / V tiles
+// (read from the cache, L2-resident); warp 8 owns the tensor memory and one
+// lane issues the MMAs.  Every wait is bounded and records GB_ETIMEOUT.
 constexpr int TA_R = 128;
-constexpr int TA_NK = 32;
+constexpr int TA_NK = 64;
 constexpr int TA_THREADS = 9 * 32;
+constexpr float TA_TAU = 8.0f;   // a row's max moves (O, l rescaled) only when exceeded by this much
 
 template <int HD>
 struct TaLayout {
-    static constexpr int QSUB = TA_R * 32 * 4;            // one [128 x 32] sub-tile (16 KB)
-    static constexpr int KSUB = TA_NK * 32 * 4;           // one [32 x 32] sub-tile (4 KB)
-    static constexpr int NS = HD / 32;                    // sub-tiles along head_dim
-    static constexpr int Q_HI = 0, Q_LO = NS * QSUB;
-    static constexpr int K_HI = 2 * NS * QSUB, K_LO = K_HI + NS * KSUB;
-    static constexpr int V_HI = K_HI + 2 * NS * KSUB;     // V^T [HD x 32 keys]
-    static constexpr int V_LO = V_HI + HD * TA_NK * 4;
-    static constexpr int P_HI = V_LO + HD * TA_NK * 4;    // P [128 x 32 keys]
-    static constexpr int P_LO = P_HI + QSUB;
-    static constexpr int BYTES = P_LO + QSUB;
+    static constexpr int NS = HD / 32;                    // 32-column sub-tiles along head_dim
+    static constexpr int KSUB = TA_NK * 32 * 4;           // K: [64 keys x 32] sub-tile (8 KB)
+    static constexpr int VSUB = HD * 32 * 4;              // V^T: [hd x 32 keys] sub-tile
+    static constexpr int PSUB = TA_R * 32 * 4;            // P: [128 x 32 keys] sub-tile (16 KB)
+    static constexpr int K_HI = 0, K_LO = NS * KSUB;
+    static constexpr int V_HI = 2 * NS * KSUB, V_LO = V_HI + 2 * VSUB;
+    static constexpr int P_HI = V_LO + 2 * VSUB, P_LO = P_HI + 2 * PSUB;
+    static constexpr int BYTES = P_LO + 2 * PSUB;
     static constexpr int SMEM = BYTES + 1024;             // + alignment slack
-    static constexpr uint32_t TMEM_COLS = 256;            // S[2] at 0 / 32, O at 128
+    static constexpr uint32_t QHI = 0, QLO = HD, S0 = 2 * HD, OC = 2 * HD + 128;   // tensor-memory columns
+    static constexpr uint32_t TMEM_COLS = 512;
 };
 static_assert(TaLayout<128>::SMEM <= 227 * 1024, "shared memory");
+static_assert(TaLayout<128>::OC + 128 <= TaLayout<128>::TMEM_COLS, "tensor memory");
 
 __device__ __forceinline__ bool ta_wait(uint32_t bar, uint32_t parity, unsigned* err) {
     if (mbs_test(bar, parity)) return true;
@@ -346,41 +350,52 @@ k_pf_attn_tc(const float* __restrict__ q, const float* __restrict__ kc, const fl
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 8) tc::tmem_alloc(&tmem_slot, L::TMEM_COLS);
-    // Q rows (row r = head g GROUP + r / BQ, query q0 + r % BQ; zero past T),
-    // split into [128 x 32] sub-tiles along head_dim
-    for (int e = tid; e < TA_R * HD / 4; e += TA_THREADS) {
-        const int r = e / (HD / 4), d = 4 * (e % (HD / 4));
-        const int t = q0 + r % BQ, h = g * GROUP + r / BQ;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (t < T) v = *reinterpret_cast<const float4*>(q + (size_t)t * QD + (size_t)h * HD + d);
-        ta_store4(sm + L::Q_HI, sm + L::Q_LO, (d >> 5) * L::QSUB + tc::tile_off(r, d & 31, TA_R), v);
-    }
-    tc::fence_async_smem();
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tmem = tmem_slot;
+    if (warp < 4) {   // Q row r (head g GROUP + r / BQ, query q0 + r % BQ; zero past T) into tensor-memory lane r
+        const int r = tid, t = q0 + r % BQ, h = g * GROUP + r / BQ;
+        const float* src = q + (size_t)t * QD + (size_t)h * HD;
+        const uint32_t lb = tmem + ((uint32_t)(warp * 32) << 16);
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 16) {
+            float hv[16], lv[16];
+#pragma unroll
+            for (int i = 0; i < 16; i += 4) {
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (t < T) v = __ldg(reinterpret_cast<const float4*>(src + c + i));
+                tc::split_tf32(v.x, hv[i], lv[i]);
+                tc::split_tf32(v.y, hv[i + 1], lv[i + 1]);
+                tc::split_tf32(v.z, hv[i + 2], lv[i + 2]);
+                tc::split_tf32(v.w, hv[i + 3], lv[i + 3]);
+            }
+            tc::tmem_st16(lb + L::QHI + (uint32_t)c, hv);
+            tc::tmem_st16(lb + L::QLO + (uint32_t)c, lv);
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
     bool ok = true;
 
     if (warp == 8) {   // ---- MMA issue (one lane)
         if (lane == 0) {
             constexpr uint32_t idS = tc::idesc_tf32(TA_R, TA_NK), idO = tc::idesc_tf32(TA_R, HD);
-            constexpr uint32_t LQ = TA_R / 8 * 128, LK = TA_NK / 8 * 128, LV = HD / 8 * 128;
+            constexpr uint32_t LK = TA_NK / 8 * 128, LP = TA_R / 8 * 128, LV = HD / 8 * 128;
             const uint32_t base = tc::smem_u32(sm);
-            auto scores = [&](int t) {   // S[t & 1] = Q K^T over head_dim: NS sub-tiles x 4 k-steps x 3 products
-                const uint32_t S = tmem + (uint32_t)(32 * (t & 1));
+            auto scores = [&](int t) {   // S[t & 1] = Q K^T: hd / 8 k-steps x 3 products, A from tensor memory
+                const uint32_t S = tmem + L::S0 + (uint32_t)(TA_NK * (t & 1));
 #pragma unroll
-                for (int c = 0; c < NS; c++)
-#pragma unroll
-                    for (int ks = 0; ks < 4; ks++) {
-                        const uint64_t qh = tc::smem_desc(base + L::Q_HI + c * L::QSUB + ks * 2 * LQ, LQ, 128);
-                        const uint64_t ql = tc::smem_desc(base + L::Q_LO + c * L::QSUB + ks * 2 * LQ, LQ, 128);
-                        const uint64_t kh2 = tc::smem_desc(base + L::K_HI + c * L::KSUB + ks * 2 * LK, LK, 128);
-                        const uint64_t kl2 = tc::smem_desc(base + L::K_LO + c * L::KSUB + ks * 2 * LK, LK, 128);
-                        tc::mma_tf32(S, qh, kh2, idS, c > 0 || ks > 0);
-                        tc::mma_tf32(S, qh, kl2, idS, true);
-                        tc::mma_tf32(S, ql, kh2, idS, true);
-                    }
+                for (int ks = 0; ks < HD / 8; ks++) {
+                    const uint32_t koff = (ks >> 2) * L::KSUB + (ks & 3) * 2 * LK;
+                    const uint64_t khd = tc::smem_desc(base + L::K_HI + koff, LK, 128);
+                    const uint64_t kld = tc::smem_desc(base + L::K_LO + koff, LK, 128);
+                    const uint32_t qh = tmem + L::QHI + (uint32_t)(8 * ks), ql = tmem + L::QLO + (uint32_t)(8 * ks);
+                    tc::mma_tf32_ta(S, qh, khd, idS, ks > 0);
+                    tc::mma_tf32_ta(S, qh, kld, idS, true);
+                    tc::mma_tf32_ta(S, ql, khd, idS, true);
+                }
                 tc::mma_commit(sfull + 8 * (t & 1));
                 tc::mma_commit(kempty);
             };
@@ -400,16 +415,18 @@ k_pf_attn_tc(const float* __restrict__ q, const float* __restrict__ kc, const fl
                 ok = ta_wait(pfull, t & 1, err) && ta_wait(vfull, t & 1, err);
                 if (!ok) break;
                 tc::fence_after_sync();
-                const uint32_t O = tmem + 128u;
+                const uint32_t O = tmem + L::OC;
 #pragma unroll
-                for (int ks = 0; ks < 4; ks++) {   // O (+)= P V over the tile's 32 keys
-                    const uint64_t ph = tc::smem_desc(base + L::P_HI + ks * 2 * LQ, LQ, 128);
-                    const uint64_t pl = tc::smem_desc(base + L::P_LO + ks * 2 * LQ, LQ, 128);
-                    const uint64_t vh2 = tc::smem_desc(base + L::V_HI + ks * 2 * LV, LV, 128);
-                    const uint64_t vl2 = tc::smem_desc(base + L::V_LO + ks * 2 * LV, LV, 128);
-                    tc::mma_tf32(O, ph, vh2, idO, t > 0 || ks > 0);
-                    tc::mma_tf32(O, ph, vl2, idO, true);
-                    tc::mma_tf32(O, pl, vh2, idO, true);
+                for (int ks = 0; ks < TA_NK / 8; ks++) {   // O (+)= P V over the tile's 64 keys
+                    const uint32_t poff = (ks >> 2) * L::PSUB + (ks & 3) * 2 * LP;
+                    const uint32_t voff = (ks >> 2) * L::VSUB + (ks & 3) * 2 * LV;
+                    const uint64_t ph = tc::smem_desc(base + L::P_HI + poff, LP, 128);
+                    const uint64_t pl = tc::smem_desc(base + L::P_LO + poff, LP, 128);
+                    const uint64_t vhd = tc::smem_desc(base + L::V_HI + voff, LV, 128);
+                    const uint64_t vld = tc::smem_desc(base + L::V_LO + voff, LV, 128);
+                    tc::mma_tf32(O, ph, vhd, idO, t > 0 || ks > 0);
+                    tc::mma_tf32(O, ph, vld, idO, true);
+                    tc::mma_tf32(O, pl, vhd, idO, true);
                 }
                 tc::mma_commit(pvdone);
             }
@@ -417,24 +434,28 @@ k_pf_attn_tc(const float* __restrict__ q, const float* __restrict__ kc, const fl
         __syncwarp();
     } else if (warp >= 4) {   // ---- warps 4-7: K and V tiles (the next tile's loads issued once this one is stored)
         const int cw = warp - 4, ct = tid - 128;
-        // K: lane (j = lane % 8, e = lane / 8) takes key 8 cw + j and the
-        // float4 columns 4 it + e of it: a quarter-warp writes one core
-        // matrix (8 keys, conflict-free) and reads 8 rows x 16 bytes
+        // K: lane (j = lane % 8, e = lane / 8) takes keys 8 cw + j and
+        // 32 + 8 cw + j, float4 columns 4 it + e of each: a quarter-warp
+        // writes one core matrix (8 keys, conflict-free) and reads 8 rows x
+        // 16 bytes
         constexpr int KIT = HD / 16;
         const int kj = 8 * cw + (lane & 7), ke = lane >> 3;
-        // V^T: thread ct takes head_dim column d = ct % HD and keys
-        // kv0 .. kv0 + VK - 1 (kv0 = VK (ct / HD)); a warp reads 32
-        // consecutive floats of one key row
-        constexpr int VK = TA_NK * HD / 128;   // keys per thread (32 for hd 128, 16 for 64)
+        // V^T: thread ct takes head_dim column d = ct % HD and keys kv0 ..
+        // kv0 + VK - 1; a warp reads 32 consecutive floats of one key row
+        constexpr int VK = TA_NK * HD / 128;   // keys per thread (64 at hd 128, 32 at 64)
         const int vd = ct % HD, kv0 = VK * (ct / HD);
-        float4 kr[KIT];
+        float4 kr[2][KIT];
         float vr[VK];
         auto load_k = [&](int t) {
-            const int key = t * TA_NK + kj;
 #pragma unroll
-            for (int i = 0; i < KIT; i++)
-                kr[i] = key < kend ? __ldg(reinterpret_cast<const float4*>(kh + (size_t)key * HD + 4 * (4 * i + ke)))
-                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int hh = 0; hh < 2; hh++) {
+                const int key = t * TA_NK + 32 * hh + kj;
+#pragma unroll
+                for (int i = 0; i < KIT; i++)
+                    kr[hh][i] = key < kend
+                                    ? __ldg(reinterpret_cast<const float4*>(kh + (size_t)key * HD + 4 * (4 * i + ke)))
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
         };
         auto load_v = [&](int t) {
 #pragma unroll
@@ -449,10 +470,13 @@ k_pf_attn_tc(const float* __restrict__ q, const float* __restrict__ kc, const fl
             // K(t) once the scores of tile t - 1 are done; then tile t + 1's K loads
             if (t > 0 && ok) ok = ta_wait(kempty, (t - 1) & 1, err);
 #pragma unroll
-            for (int i = 0; i < KIT; i++) {
-                const int d = 4 * (4 * i + ke);
-                ta_store4(sm + L::K_HI, sm + L::K_LO, (d >> 5) * L::KSUB + tc::tile_off(kj, d & 31, TA_NK), kr[i]);
-            }
+            for (int hh = 0; hh < 2; hh++)
+#pragma unroll
+                for (int i = 0; i < KIT; i++) {
+                    const int d = 4 * (4 * i + ke);
+                    ta_store4(sm + L::K_HI, sm + L::K_LO,
+                              (d >> 5) * L::KSUB + tc::tile_off(32 * hh + kj, d & 31, TA_NK), kr[hh][i]);
+                }
             tc::fence_async_smem();
             __syncwarp();
             if (lane == 0) mbs_arrive(kfull);
@@ -460,9 +484,11 @@ k_pf_attn_tc(const float* __restrict__ q, const float* __restrict__ kc, const fl
             // V(t) once O += P V of tile t - 1 is done; then tile t + 1's V loads
             if (t > 0 && ok) ok = ta_wait(pvdone, (t - 1) & 1, err);
 #pragma unroll
-            for (int i = 0; i < VK; i += 4)
-                ta_store4(sm + L::V_HI, sm + L::V_LO, tc::tile_off(vd, kv0 + i, HD),
+            for (int i = 0; i < VK; i += 4) {
+                const int key = kv0 + i;
+                ta_store4(sm + L::V_HI, sm + L::V_LO, (key >> 5) * L::VSUB + tc::tile_off(vd, key & 31, HD),
                           make_float4(vr[i], vr[i + 1], vr[i + 2], vr[i + 3]));
+            }
             tc::fence_async_smem();
             __syncwarp();
             if (lane == 0) mbs_arrive(vfull);
@@ -473,7 +499,7 @@ k_pf_attn_tc(const float* __restrict__ q, const float* __restrict__ kc, const fl
         const int tq = q0 + r % BQ, h = g * GROUP + r / BQ;
         const int qpos = pos0 + tq;
         const uint32_t lb = tmem + ((uint32_t)(warp * 32) << 16);
-        const uint32_t O = lb + 128u;
+        const uint32_t O = lb + L::OC;
         const float scale = 1.0f / sqrtf((float)HD);
         float m = -INFINITY, l = 0.f;
         for (int t = 0; t < nt; t++) {
@@ -481,19 +507,22 @@ k_pf_attn_tc(const float* __restrict__ q, const float* __restrict__ kc, const fl
             if (ok) ok = ta_wait(sfull + 8 * b, (t >> 1) & 1, err);
             tc::fence_after_sync();
             float sc[TA_NK];
-            {
+#pragma unroll
+            for (int c = 0; c < TA_NK; c += 16) {
                 float a16[16];
-                tc::tmem_ld16(lb + (uint32_t)(32 * b), a16);
+                tc::tmem_ld16(lb + L::S0 + (uint32_t)(TA_NK * b + c), a16);
 #pragma unroll
-                for (int i = 0; i < 16; i++) sc[i] = a16[i];
-                tc::tmem_ld16(lb + (uint32_t)(32 * b + 16), a16);
-#pragma unroll
-                for (int i = 0; i < 16; i++) sc[16 + i] = a16[i];
+                for (int i = 0; i < 16; i++) sc[c + i] = a16[i];
             }
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) mbs_arrive(sfree + 8 * b);   // S[b] may be overwritten
             // scale, causal mask (key > query position: -inf), online softmax
+            // with a lazily updated max: p = exp(s - m) for the row's max m as
+            // of its last rescale, which moves (and O, l are rescaled) only
+            // when a score exceeds it by more than TA_TAU -- so p <= e^TA_TAU
+            // and the rescale of O in tensor memory is rare; O / l is the
+            // same softmax for any common m
             float mx = -INFINITY;
 #pragma unroll
             for (int i = 0; i < TA_NK; i++) {
@@ -501,8 +530,9 @@ k_pf_attn_tc(const float* __restrict__ q, const float* __restrict__ kc, const fl
                 sc[i] = key > qpos ? -INFINITY : sc[i] * scale;
                 mx = fmaxf(mx, sc[i]);
             }
-            const float mn = fmaxf(m, mx);   // finite: key 0 is in every row's range
-            const float alpha = expf(m - mn);
+            const bool move = mx > m + TA_TAU;   // always on the first tile (m = -inf; key 0 is in range)
+            const float mn = move ? mx : m;
+            const float alpha = expf(m - mn);    // 1 when the max stays, 0 on the first tile
             float sum = 0.f;
 #pragma unroll
             for (int i = 0; i < TA_NK; i++) {
@@ -511,10 +541,10 @@ k_pf_attn_tc(const float* __restrict__ q, const float* __restrict__ kc, const fl
             }
             l = fmaf(l, alpha, sum);
             m = mn;
-            if (t > 0) {   // P and V of tile t - 1 consumed, O holds its sum: rescale O
+            if (t > 0) {   // P and V of tile t - 1 consumed, O holds its sum: rescale O if a row's max moved
                 if (ok) ok = ta_wait(pvdone, (t - 1) & 1, err);
                 tc::fence_after_sync();
-                if (!__all_sync(0xffffffffu, alpha == 1.0f)) {
+                if (__any_sync(0xffffffffu, move)) {
 #pragma unroll 1
                     for (int c = 0; c < HD; c += 16) {
                         float o16[16];
@@ -527,7 +557,7 @@ k_pf_attn_tc(const float* __restrict__ q, const float* __restrict__ kc, const fl
             }
 #pragma unroll
             for (int j = 0; j < TA_NK / 4; j++)
-                ta_store4(sm + L::P_HI, sm + L::P_LO, tc::tile_off(r, 4 * j, TA_R),
+                ta_store4(sm + L::P_HI, sm + L::P_LO, (j >> 3) * L::PSUB + tc::tile_off(r, 4 * (j & 7), TA_R),
                           make_float4(sc[4 * j], sc[4 * j + 1], sc[4 * j + 2], sc[4 * j + 3]));
             tc::fence_async_smem();   // P (generic stores) -> tensor-core reads
             tc::fence_before_sync();  // O (tensor-memory stores) -> the next MMA
