@@ -13,23 +13,24 @@
 // about 22 bits of each operand, so a prompt pass agrees with the reference's
 // fp32 arithmetic as closely as the decode matvecs do.
 //
-// CTA tile: 128 weight rows (the MMA's M) x BT = 128 tokens (its N), K in
-// chunks of 32.  Warps 0-3 convert weights: thread r dequantises row r's 32
-// weights of the chunk (Q4_K / Q5_K: 16-byte loads of a chunk pair's bytes,
-// three / two pairs in flight; Q6_K: 4-byte words of a 128-column
-// half-block, the next one loaded before this one is converted).  Warp 13 loads each chunk's raw activation
-// tile [128 tokens][32] fp32 by TMA into the stage, and warps 9-12 split it
-// in place.  Both land in a 3-stage shared-memory ring in the tensor cores'
-// K-major layout (gb_tc.cuh).
-// Warp 4 allocates the tensor memory and one of its lanes issues the 12 MMAs
-// of a chunk (4 k-steps x 3 products), then commits them to the stage's
-// "empty" barrier so the converters may refill it.  The tensor cores' fp32
-// accumulation is not round-to-nearest, so its error grows with the number
-// of MMAs summed into one accumulator: every 256 columns of K the MMAs start
-// a fresh accumulator (two in tensor memory, alternating), and warps 5-8
-// read each finished one back and add it to a running fp32 sum kept in a
-// third tensor-memory region (lane r = weight row), then write Y after the
-// last.
+// CTA tile: 128 weight rows (the MMA's M) x BT = 128 or 256 tokens (its N;
+// 256 when that grid still fills every SM), K in chunks of 32 through a
+// 3-stage (2 at BT 256) shared-memory ring in the tensor cores' K-major
+// layout (gb_tc.cuh).  Warps 0-3 convert weights: thread r dequantises row
+// r's 32 weights of the chunk (Q4_K / Q5_K: 16-byte loads of a chunk pair's
+// bytes, three / two pairs in flight; Q6_K: 4-byte words of a 128-column
+// half-block, the next one loaded before this one is converted).  Warp 13
+// loads each chunk's raw activation tile [BT tokens][32] fp32 by TMA into the
+// stage, and warps 9-12 split it in place.  Warp 4 allocates the tensor
+// memory and one of its lanes issues the 12 MMAs of a chunk (4 k-steps x 3
+// products), then commits them to the stage's "empty" barrier so the
+// converters may refill it.  The tensor cores' fp32 accumulation is not
+// round-to-nearest, so its error grows with the number of MMAs summed into
+// one accumulator: every 256 columns of K the MMAs start a fresh accumulator
+// (two in tensor memory, alternating; one at BT 256, refilled once read), and
+// warps 5-8 read each finished one back and add it to a running fp32 sum kept
+// in a further tensor-memory region (lane r = weight row), then write Y after
+// the last.
 // Every wait is bounded (2 s of %globaltimer) and records GB_ETIMEOUT in the
 // caller's error word (gb_gemm: a module-wide word read by gb_gemm_error).
 #include "gb_common.cuh"
@@ -40,19 +41,27 @@
 namespace gb {
 
 constexpr int GM_ROWS = 128;             // weight rows per CTA (MMA M)
-constexpr int GM_BT = 128;               // tokens per CTA (MMA N)
 constexpr int GM_BK = 32;                // K per stage
-constexpr int GM_S = 3;                  // ring stages
 constexpr int GM_KG = 8;                 // stages summed into one accumulator (256 columns of K)
 constexpr int GM_TILE_A = GM_ROWS * GM_BK * 4;   // 16 KB (one of hi / lo)
-constexpr int GM_TILE_B = GM_BT * GM_BK * 4;     // 16 KB
-constexpr int GM_STAGE = 2 * GM_TILE_A + 2 * GM_TILE_B;
 constexpr int GM_READERS = 4;            // accumulator-reader warps (5 .. 8)
 constexpr int GM_XWARPS = 4;             // activation converter warps (9 .. 12)
 constexpr int GM_XPROD = 5 + GM_READERS + GM_XWARPS;   // warp 13: activation tile loads (TMA)
 constexpr int GM_THREADS = (GM_XPROD + 1) * 32;
-constexpr int GM_SMEM = GM_S * GM_STAGE + 1024;
-constexpr uint32_t GM_TMEM_COLS = 4 * GM_BT;   // two accumulators and the running sum (power of two)
+
+// Token-tile size BT (the MMA's N): 128 (3 stages, two accumulators
+// alternating) or 256 (2 stages: 96 KB each; one accumulator, refilled once
+// the readers have taken it).
+template <int BT>
+struct GmCfg {
+    static constexpr int TILE_B = BT * GM_BK * 4;              // 16 / 32 KB (one of hi / lo)
+    static constexpr int STAGE = 2 * GM_TILE_A + 2 * TILE_B;
+    static constexpr int S = BT == 256 ? 2 : 3;                 // ring stages
+    static constexpr int NACC = BT == 256 ? 1 : 2;              // accumulators in tensor memory
+    static constexpr int SMEM = S * STAGE + 1024;
+    static constexpr uint32_t TMEM_COLS = 512;                  // NACC x BT accumulator + BT running sum
+};
+static_assert(GmCfg<256>::SMEM <= 227 * 1024 && GmCfg<128>::SMEM <= 227 * 1024, "shared memory");
 
 __device__ unsigned g_gemm_err;
 
@@ -144,23 +153,24 @@ __device__ __forceinline__ void store_split(uint8_t* hi, uint8_t* lo, int r, con
     }
 }
 
-template <int DT>
+template <int DT, int BT>
 __global__ void __launch_bounds__(GM_THREADS, 1)
 k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, float* Y, const float* R, int N, int K,
        int T, unsigned* err) {
+    using C = GmCfg<BT>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte aligned stage ring; barriers and the tensor-memory address
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    __shared__ __align__(8) uint64_t bars[3 * GM_S + 4];
+    __shared__ __align__(8) uint64_t bars[3 * C::S + 4];
     __shared__ uint32_t tmem_slot;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * GM_ROWS, t0 = blockIdx.y * GM_BT;
-    const uint32_t full = tc::smem_u32(&bars[0]), empty = full + 8 * GM_S, xfull = full + 16 * GM_S;
-    const uint32_t accfull = full + 24 * GM_S, accfree = accfull + 16;   // [2] each
+    const int n0 = blockIdx.x * GM_ROWS, t0 = blockIdx.y * BT;
+    const uint32_t full = tc::smem_u32(&bars[0]), empty = full + 8 * C::S, xfull = full + 16 * C::S;
+    const uint32_t accfull = full + 24 * C::S, accfree = accfull + 16;   // [2] each
     const int nk = K / GM_BK;
     const int ng = (nk + GM_KG - 1) / GM_KG;   // accumulator groups
     if (threadIdx.x == 0) {
-        for (int s = 0; s < GM_S; s++) {
+        for (int s = 0; s < C::S; s++) {
             mbs_init(full + 8 * s, 4 + GM_XWARPS);   // one arrival per converter warp
             mbs_init(empty + 8 * s, 1);  // the MMA commit
             mbs_init(xfull + 8 * s, 1);  // the activation tile's TMA load
@@ -171,7 +181,7 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 4) tc::tmem_alloc(&tmem_slot, GM_TMEM_COLS);
+    if (warp == 4) tc::tmem_alloc(&tmem_slot, C::TMEM_COLS);
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
@@ -179,24 +189,24 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
 
     if (warp == 4) {   // ---- MMA issue (one lane)
         if (lane == 0) {
-            constexpr uint32_t idesc = tc::idesc_tf32(GM_ROWS, GM_BT);
-            constexpr uint32_t LBO_A = GM_ROWS / 8 * 128, LBO_B = GM_BT / 8 * 128;
+            constexpr uint32_t idesc = tc::idesc_tf32(GM_ROWS, BT);
+            constexpr uint32_t LBO_A = GM_ROWS / 8 * 128, LBO_B = BT / 8 * 128;
             bool ok = true;
             for (int g = 0; g < ng && ok; g++) {
-                const int a = g & 1;
-                if (g >= 2) ok = gm_wait(accfree + 8 * a, ((g >> 1) - 1) & 1, err);
+                const int a = g % C::NACC;   // accumulator of group g; reused once the readers took group g - NACC
+                if (g >= C::NACC) ok = gm_wait(accfree + 8 * a, ((g / C::NACC) - 1) & 1, err);
                 if (!ok) break;
                 tc::fence_after_sync();
-                const uint32_t acc = tmem + (uint32_t)(a * GM_BT);
+                const uint32_t acc = tmem + (uint32_t)(a * BT);
                 const int k1 = min(nk, (g + 1) * GM_KG);
                 for (int kc = g * GM_KG; kc < k1; kc++) {
-                    const int s = kc % GM_S;
-                    ok = gm_wait(full + 8 * s, (kc / GM_S) & 1, err);
+                    const int s = kc % C::S;
+                    ok = gm_wait(full + 8 * s, (kc / C::S) & 1, err);
                     if (!ok) break;
                     tc::fence_after_sync();
-                    const uint32_t base = tc::smem_u32(smem + (size_t)s * GM_STAGE);
+                    const uint32_t base = tc::smem_u32(smem + (size_t)s * C::STAGE);
                     const uint32_t ahi = base, alo = base + GM_TILE_A, bhi = base + 2 * GM_TILE_A,
-                                   blo = bhi + GM_TILE_B;
+                                   blo = bhi + C::TILE_B;
 #pragma unroll
                     for (int ks = 0; ks < GM_BK / 8; ks++) {
                         const uint64_t dah = tc::smem_desc(ahi + ks * 2 * LBO_A, LBO_A, 128);
@@ -217,9 +227,9 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
         const int r = threadIdx.x, n = n0 + r;
         bool ok = true;
         auto put = [&](int kc, const float (&v)[32]) {   // one chunk into its stage
-            const int s = kc % GM_S;
-            if (kc >= GM_S && ok) ok = gm_wait(empty + 8 * s, ((kc / GM_S) - 1) & 1, err);
-            uint8_t* st = smem + (size_t)s * GM_STAGE;
+            const int s = kc % C::S;
+            if (kc >= C::S && ok) ok = gm_wait(empty + 8 * s, ((kc / C::S) - 1) & 1, err);
+            uint8_t* st = smem + (size_t)s * C::STAGE;
             store_split<GM_ROWS>(st, st + GM_TILE_A, r, v);
             tc::fence_async_smem();   // generic-proxy stores -> tensor-core reads
             __syncwarp();
@@ -377,12 +387,12 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
         if (lane == 0) {
             bool ok = true;
             for (int kc = 0; kc < nk && ok; kc++) {
-                const int s = kc % GM_S;
-                if (kc >= GM_S) ok = gm_wait(empty + 8 * s, ((kc / GM_S) - 1) & 1, err);
+                const int s = kc % C::S;
+                if (kc >= C::S) ok = gm_wait(empty + 8 * s, ((kc / C::S) - 1) & 1, err);
                 if (!ok) break;
-                mbs_expect(xfull + 8 * s, GM_TILE_B);
+                mbs_expect(xfull + 8 * s, C::TILE_B);
                 // into the stage's hi tile; rows past T read as zeros
-                tma_load_3d(tc::smem_u32(smem + (size_t)s * GM_STAGE + 2 * GM_TILE_A), &xmap, kc * GM_BK, t0, 0,
+                tma_load_3d(tc::smem_u32(smem + (size_t)s * C::STAGE + 2 * GM_TILE_A), &xmap, kc * GM_BK, t0, 0,
                             xfull + 8 * s);
             }
         }
@@ -395,25 +405,31 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
         const int rr = xw * 32 + 8 * (lane >> 3) + j;
         bool ok = true;
         for (int kc = 0; kc < nk; kc++) {
-            const int s = kc % GM_S;
-            if (ok) ok = gm_wait(xfull + 8 * s, (kc / GM_S) & 1, err);
-            uint8_t* hi = smem + (size_t)s * GM_STAGE + 2 * GM_TILE_A;
-            float4 u[8];
+            const int s = kc % C::S;
+            if (ok) ok = gm_wait(xfull + 8 * s, (kc / C::S) & 1, err);
+            uint8_t* hi = smem + (size_t)s * C::STAGE + 2 * GM_TILE_A;
+            constexpr int NP = BT / 128;   // 128-row passes (the warp's rows rr + 128 pass)
+            float4 u[NP][8];
 #pragma unroll
-            for (int c = 0; c < 8; c++) u[c] = *reinterpret_cast<const float4*>(hi + rr * 128 + ((j + c) & 7) * 16);
+            for (int pp = 0; pp < NP; pp++)
+#pragma unroll
+                for (int c = 0; c < 8; c++)
+                    u[pp][c] = *reinterpret_cast<const float4*>(hi + (rr + 128 * pp) * 128 + ((j + c) & 7) * 16);
             // every raw row is read before any core matrix overwrites it
             asm volatile("bar.sync 1, %0;" ::"n"(GM_XWARPS * 32) : "memory");
 #pragma unroll
-            for (int c = 0; c < 8; c++) {
-                float h[4], l[4];
-                tc::split_tf32(u[c].x, h[0], l[0]);
-                tc::split_tf32(u[c].y, h[1], l[1]);
-                tc::split_tf32(u[c].z, h[2], l[2]);
-                tc::split_tf32(u[c].w, h[3], l[3]);
-                const uint32_t off = tc::tile_off(rr, 4 * ((j + c) & 7), GM_BT);
-                *reinterpret_cast<float4*>(hi + off) = make_float4(h[0], h[1], h[2], h[3]);
-                *reinterpret_cast<float4*>(hi + GM_TILE_B + off) = make_float4(l[0], l[1], l[2], l[3]);
-            }
+            for (int pp = 0; pp < NP; pp++)
+#pragma unroll
+                for (int c = 0; c < 8; c++) {
+                    float h[4], l[4];
+                    tc::split_tf32(u[pp][c].x, h[0], l[0]);
+                    tc::split_tf32(u[pp][c].y, h[1], l[1]);
+                    tc::split_tf32(u[pp][c].z, h[2], l[2]);
+                    tc::split_tf32(u[pp][c].w, h[3], l[3]);
+                    const uint32_t off = tc::tile_off(rr + 128 * pp, 4 * ((j + c) & 7), BT);
+                    *reinterpret_cast<float4*>(hi + off) = make_float4(h[0], h[1], h[2], h[3]);
+                    *reinterpret_cast<float4*>(hi + C::TILE_B + off) = make_float4(l[0], l[1], l[2], l[3]);
+                }
             tc::fence_async_smem();
             __syncwarp();
             if (lane == 0) mbs_arrive(full + 8 * s);
@@ -424,17 +440,17 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
         const int q = warp & 3;
         const int r = q * 32 + lane, n = n0 + r;
         const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
-        const uint32_t sum = lane_base + (uint32_t)(2 * GM_BT);
+        const uint32_t sum = lane_base + (uint32_t)(C::NACC * BT);
         bool ok = true;
         for (int g = 0; g < ng && ok; g++) {
-            const int a = g & 1;
-            ok = gm_wait(accfull + 8 * a, (g >> 1) & 1, err);
+            const int a = g % C::NACC;
+            ok = gm_wait(accfull + 8 * a, (g / C::NACC) & 1, err);
             if (!ok) break;
             tc::fence_after_sync();
-            const uint32_t acc = lane_base + (uint32_t)(a * GM_BT);
+            const uint32_t acc = lane_base + (uint32_t)(a * BT);
             const bool last = g == ng - 1;
 #pragma unroll 1
-            for (int c = 0; c < GM_BT; c += 16) {
+            for (int c = 0; c < BT; c += 16) {
                 float v[16];
                 tc::tmem_ld16(acc + c, v);
                 if (g > 0) {
@@ -465,19 +481,36 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
     __syncthreads();
     if (warp == 4) {
         tc::fence_after_sync();
-        tc::tmem_dealloc(tmem, GM_TMEM_COLS);
+        tc::tmem_dealloc(tmem, C::TMEM_COLS);
     }
 }
 
+template <int DT, int BT>
+static int launch_gemm_bt(const void* W, const float* X, float* Y, const float* R, int N, int K, int T, cudaStream_t st,
+                          unsigned* err) {
+    using C = GmCfg<BT>;
+    GB_CUDA_TRY(set_smem_once(reinterpret_cast<const void*>(k_gemm<DT, BT>), C::SMEM));
+    CUtensorMap xmap;
+    if (!gemm_encode_x(&xmap, X, T, K, GM_BK, BT)) return GB_ECUDA;
+    dim3 grid((N + GM_ROWS - 1) / GM_ROWS, (T + BT - 1) / BT);
+    k_gemm<DT, BT><<<grid, GM_THREADS, C::SMEM, st>>>(xmap, static_cast<const uint8_t*>(W), Y, R, N, K, T, err);
+    return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
+}
+
+// 256-token tiles (half the MMA instructions and weight conversions per
+// FLOP) when their grid still gives every SM a CTA, else 128-token tiles
+// (GB_GEMM_BT=128 / 256 forces one size).
 template <int DT>
 static int launch_gemm(const void* W, const float* X, float* Y, const float* R, int N, int K, int T, cudaStream_t st,
                        unsigned* err) {
-    GB_CUDA_TRY(set_smem_once(reinterpret_cast<const void*>(k_gemm<DT>), GM_SMEM));
-    CUtensorMap xmap;
-    if (!gemm_encode_x(&xmap, X, T, K, GM_BK, GM_BT)) return GB_ECUDA;
-    dim3 grid((N + GM_ROWS - 1) / GM_ROWS, (T + GM_BT - 1) / GM_BT);
-    k_gemm<DT><<<grid, GM_THREADS, GM_SMEM, st>>>(xmap, static_cast<const uint8_t*>(W), Y, R, N, K, T, err);
-    return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
+    static const int force = [] {
+        const char* e = getenv("GB_GEMM_BT");
+        return e ? atoi(e) : 0;
+    }();
+    const long ctas256 = (long)((N + GM_ROWS - 1) / GM_ROWS) * ((T + 255) / 256);
+    const bool wide = force ? force == 256 : ctas256 >= sm_count();
+    return wide ? launch_gemm_bt<DT, 256>(W, X, Y, R, N, K, T, st, err)
+                : launch_gemm_bt<DT, 128>(W, X, Y, R, N, K, T, st, err);
 }
 
 int gemm_launch(int dtype, const void* W, const float* X, float* Y, const float* R, int N, int K, int T,
