@@ -26,8 +26,9 @@
 // products), then commits them to the stage's "empty" barrier so the
 // converters may refill it.  The tensor cores' fp32 accumulation is not
 // round-to-nearest, so its error grows with the number of MMAs summed into
-// one accumulator: every 256 columns of K the MMAs start a fresh accumulator
-// (two in tensor memory, alternating; one at BT 256, refilled once read), and
+// one accumulator: every 256 columns of K (512 at BT 256) the MMAs start a
+// fresh accumulator (two in tensor memory, alternating; one at BT 256,
+// refilled once read), and
 // warps 5-8 read each finished one back and add it to a running fp32 sum kept
 // in a further tensor-memory region (lane r = weight row), then write Y after
 // the last.
@@ -42,7 +43,6 @@ namespace gb {
 
 constexpr int GM_ROWS = 128;             // weight rows per CTA (MMA M)
 constexpr int GM_BK = 32;                // K per stage
-constexpr int GM_KG = 8;                 // stages summed into one accumulator (256 columns of K)
 constexpr int GM_TILE_A = GM_ROWS * GM_BK * 4;   // 16 KB (one of hi / lo)
 constexpr int GM_READERS = 4;            // accumulator-reader warps (5 .. 8)
 constexpr int GM_XWARPS = 4;             // activation converter warps (9 .. 12)
@@ -58,6 +58,7 @@ struct GmCfg {
     static constexpr int STAGE = 2 * GM_TILE_A + 2 * TILE_B;
     static constexpr int S = BT == 256 ? 2 : 3;                 // ring stages
     static constexpr int NACC = BT == 256 ? 1 : 2;              // accumulators in tensor memory
+    static constexpr int KG = BT == 256 ? 16 : 8;               // chunks per accumulator group (512 / 256 columns of K)
     static constexpr int SMEM = S * STAGE + 1024;
     static constexpr uint32_t TMEM_COLS = 512;                  // NACC x BT accumulator + BT running sum
 };
@@ -168,7 +169,7 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
     const uint32_t full = tc::smem_u32(&bars[0]), empty = full + 8 * C::S, xfull = full + 16 * C::S;
     const uint32_t accfull = full + 24 * C::S, accfree = accfull + 16;   // [2] each
     const int nk = K / GM_BK;
-    const int ng = (nk + GM_KG - 1) / GM_KG;   // accumulator groups
+    const int ng = (nk + C::KG - 1) / C::KG;   // accumulator groups
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::S; s++) {
             mbs_init(full + 8 * s, 4 + GM_XWARPS);   // one arrival per converter warp
@@ -198,8 +199,8 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
                 if (!ok) break;
                 tc::fence_after_sync();
                 const uint32_t acc = tmem + (uint32_t)(a * BT);
-                const int k1 = min(nk, (g + 1) * GM_KG);
-                for (int kc = g * GM_KG; kc < k1; kc++) {
+                const int k1 = min(nk, (g + 1) * C::KG);
+                for (int kc = g * C::KG; kc < k1; kc++) {
                     const int s = kc % C::S;
                     ok = gm_wait(full + 8 * s, (kc / C::S) & 1, err);
                     if (!ok) break;
@@ -213,7 +214,7 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
                         const uint64_t dal = tc::smem_desc(alo + ks * 2 * LBO_A, LBO_A, 128);
                         const uint64_t dbh = tc::smem_desc(bhi + ks * 2 * LBO_B, LBO_B, 128);
                         const uint64_t dbl = tc::smem_desc(blo + ks * 2 * LBO_B, LBO_B, 128);
-                        tc::mma_tf32(acc, dah, dbh, idesc, kc > g * GM_KG || ks > 0);
+                        tc::mma_tf32(acc, dah, dbh, idesc, kc > g * C::KG || ks > 0);
                         tc::mma_tf32(acc, dah, dbl, idesc, true);
                         tc::mma_tf32(acc, dal, dbh, idesc, true);
                     }
