@@ -64,3 +64,25 @@ def test_gemm_residual_in_place(gb, oracle, cuda):
     cuda.cuda.synchronize()
     ref = X.astype(np.float64) @ oracle.dequant(4, W).reshape(N, K).astype(np.float64).T + H
     assert rel_l2(from_dev(Hd), ref) <= 1e-5
+
+
+@pytest.mark.parametrize("dt", [4, 5])
+def test_gemm_long_k_wide_tiles(gb, oracle, cuda, dt):
+    """ffn_down's K = 14336 on the 256-token tiles (1280 rows x 4096 tokens: a
+    grid of 10 x 16 CTAs, more than one per SM): 28 accumulator groups of 512
+    columns; 64 sampled token rows against fp64."""
+    N, K, T = 1280, 14336, 4096
+    W = oracle.synth_blocks(dt, N, K, 21, 3)
+    Wd = cuda.zeros(W.size + 16, dtype=cuda.uint8, device="cuda")
+    Wd[: W.size] = to_dev(cuda, W)
+    X = oracle.synth_normal(T * K, 21, 4).reshape(T, K)
+    Y = cuda.full((T, N), float("nan"), dtype=cuda.float32, device="cuda")
+    gb.gemm(dt, Wd, to_dev(cuda, X), Y, N, K, T)
+    cuda.cuda.synchronize()
+    assert gb.lib().gb_gemm_error(1) == 0
+    rows = np.random.RandomState(5).choice(T, 64, replace=False)
+    Wf = oracle.dequant(dt, W).reshape(N, K).astype(np.float64)
+    ref = X[rows].astype(np.float64) @ Wf.T
+    got = from_dev(Y)[rows]
+    assert np.all(np.isfinite(from_dev(Y)))
+    assert rel_l2(got, ref) <= 1e-5, rel_l2(got, ref)
