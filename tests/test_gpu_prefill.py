@@ -11,7 +11,9 @@ compiled unchanged into oracle/_ref/libref.so) on the same seeded weights.
   1e-3 relative, every layer's K / V cache rows within 1e-4 of the
   reference's, and decode continuing from the prefilled cache.
 * A prompt split into two prefills (pos > 0), and chunked prefill
-  (GB_PREFILL_CHUNK), against one reference prefill."""
+  (GB_PREFILL_CHUNK), against one reference prefill.
+* The Llama-3.1-8B width (two layers, the full output head, a 300-token
+  prompt) against the reference forward()."""
 import os
 
 import numpy as np
@@ -187,3 +189,31 @@ def test_prefill_device_entry_and_errors(gb, oracle, cuda):
             dm.prefill_host(bad, 0)
     finally:
         dm.close()
+
+
+def test_prefill_llama8b_width_matches_reference_forward(gb, oracle, cuda):
+    """The benchmarked shapes: hidden 4096, 32 / 8 heads of 128, FFN 14336, the
+    full 128256-row Q6_K output head, two layers, a 300-token prompt (gate /
+    up on 256-token tiles, ffn_down at K = 14336), against the reference
+    forward() over the same prompt; then two decode steps from the prefilled
+    cache."""
+    m, ref, dm = _models(gb, oracle, cuda, 4096, 32, 8, 2, 14336, 128256, 320)
+    try:
+        prompt = np.random.RandomState(SEED + 2).randint(0, m.vocab, 300).astype(np.int32)
+        lr = ref.forward_tokens(prompt, 0)
+        lg = np.zeros(m.vocab, np.float32)
+        nxt = dm.prefill_host(prompt, 0, lg)
+        _check_logits(oracle, lg, lr, nxt)
+        _check_kv(m, ref, dm, len(prompt))
+        token = oracle.argmax(lr)
+        for pos in range(len(prompt), len(prompt) + 2):
+            lr = ref.forward(int(token), pos)
+            lg = np.zeros(m.vocab, np.float32)
+            nxt = dm.decode_host(int(token), pos, lg)
+            _check_logits(oracle, lg, lr, nxt)
+            token = oracle.argmax(lr)
+        assert dm.error() == 0
+    finally:
+        dm.close()
+        ref.close()
+        oracle.ref().ref_set_threads(1)
