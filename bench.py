@@ -51,10 +51,11 @@ def tf32_peak():
     return 1400.0 / 2
 
 
-def ncu_traffic():
-    """Per-launch DRAM bytes of the dominant kernel from the committed ncu
-    summary (profiles/q4k_gateup_grouped_2x14336x4096.md), or None."""
-    p = os.path.join(ROOT, "profiles", "q4k_gateup_grouped_2x14336x4096.md")
+def ncu_traffic(summary: str = "q4k_gateup_grouped_2x14336x4096.md"):
+    """Per-launch DRAM bytes of a dominant kernel from its committed ncu
+    summary under profiles/ (the decode step's gate + up launch by default),
+    or None."""
+    p = os.path.join(ROOT, "profiles", summary)
     if not os.path.exists(p):
         return None
     for line in open(p):
@@ -440,7 +441,8 @@ def prefill_bench(gb, torch, peak_tf32, T=PREFILL_T, reps=2):
                 "next_token": int(nxt),
                 "roofline": {"bound": "tensor", "kernel": f"k_gemm<Q4_K> gate/up 14336x4096 at T={T}",
                              "achieved": round(tf, 1), "peak": round(peak_tf32, 1), "unit": "TFLOP/s",
-                             "frac": round(tf / peak_tf32, 3), "traffic": None,
+                             "frac": round(tf / peak_tf32, 3),
+                             "traffic": ncu_traffic("gemm_q4k_14336x4096_T4096.md"),
                              "fp32_equiv_tflops": round(tf / 3, 1), "ms": round(g_ms, 3),
                              "peak_kind": "tf32 dense = half the measured bf16 dense sustained rate"}}
     finally:
