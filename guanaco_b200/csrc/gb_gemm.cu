@@ -154,10 +154,14 @@ __device__ __forceinline__ void store_split(uint8_t* hi, uint8_t* lo, int r, con
     }
 }
 
-template <int DT, int BT>
+// SW (SwiGLU): W holds the gate rows and W2 the up rows of an FFN; a CTA
+// takes 64 gate rows and the same 64 up rows (its 128 weight rows), and the
+// readers write Y[t][f] = silu(gate) * up (k_silu_mul's rounding) for its 64
+// columns instead of the two products.
+template <int DT, int BT, bool SW>
 __global__ void __launch_bounds__(GM_THREADS, 1)
-k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, float* Y, const float* R, int N, int K,
-       int T, unsigned* err) {
+k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, const uint8_t* __restrict__ W2, float* Y,
+       const float* R, int N, int K, int T, unsigned* err) {
     using C = GmCfg<BT>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte aligned stage ring; barriers and the tensor-memory address
@@ -165,7 +169,7 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
     __shared__ __align__(8) uint64_t bars[3 * C::S + 4];
     __shared__ uint32_t tmem_slot;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * GM_ROWS, t0 = blockIdx.y * BT;
+    const int n0 = blockIdx.x * (SW ? GM_ROWS / 2 : GM_ROWS), t0 = blockIdx.y * BT;
     const uint32_t full = tc::smem_u32(&bars[0]), empty = full + 8 * C::S, xfull = full + 16 * C::S;
     const uint32_t accfull = full + 24 * C::S, accfree = accfull + 16;   // [2] each
     const int nk = K / GM_BK;
@@ -225,7 +229,10 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
         }
         __syncwarp();
     } else if (warp < 4) {   // ---- warps 0-3: weight rows n0 + threadIdx.x
-        const int r = threadIdx.x, n = n0 + r;
+        const int r = threadIdx.x;
+        // SW: rows 0-63 are gate rows n0 .., rows 64-127 the same up rows (W2)
+        const int n = SW ? n0 + (r & 63) : n0 + r;
+        const uint8_t* Wm = (SW && r >= 64) ? W2 : W;
         bool ok = true;
         auto put = [&](int kc, const float (&v)[32]) {   // one chunk into its stage
             const int s = kc % C::S;
@@ -244,7 +251,7 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
             constexpr bool Q5 = DT == GB_DT_Q5_K;
             constexpr int BB = Q5 ? GB_Q5K_BYTES : GB_Q4K_BYTES, QS = Q5 ? 48 : 16;
             const int nb = K / 256;
-            const uint8_t* row = W + (size_t)(n < N ? n : 0) * nb * BB;
+            const uint8_t* row = Wm + (size_t)(n < N ? n : 0) * nb * BB;
             struct Raw { uint4 hd, qa, qb, ha, hb; };
             auto load = [&](int p, Raw& w) {
                 const uint8_t* blk = row + (size_t)(p >> 2) * BB;
@@ -315,7 +322,7 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
             // aligned block (realigned by funnel shifts); the next half-block
             // is loaded before this one is converted
             const int nb = K / 256;
-            const uint8_t* row = W + (size_t)(n < N ? n : 0) * nb * GB_Q6K_BYTES;
+            const uint8_t* row = Wm + (size_t)(n < N ? n : 0) * nb * GB_Q6K_BYTES;
             struct Raw { uint32_t ql[17], qh[9], sc[3]; uint32_t d, sh; };
             auto load = [&](int hb, Raw& w) {
                 const uint8_t* blk = row + (size_t)(hb >> 1) * GB_Q6K_BYTES;
@@ -376,7 +383,7 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
             for (int kc = 0; kc < nk; kc++) {
                 float v[32];
                 if (n < N) {
-                    dequant32<DT>(W, n, K, kc * GM_BK, v);
+                    dequant32<DT>(Wm, n, K, kc * GM_BK, v);
                 } else {
 #pragma unroll
                     for (int i = 0; i < 32; i++) v[i] = 0.f;
@@ -439,8 +446,10 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
         // lane r of warp w reads tensor-memory lane 32 (w % 4) + r = weight
         // row; the running sum lives in a third tensor-memory region
         const int q = warp & 3;
-        const int r = q * 32 + lane, n = n0 + r;
+        const int r = q * 32 + lane, n = SW ? n0 + (r & 63) : n0 + r;
         const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+        constexpr int XLD = BT + 1;   // SW: final sums [128 rows][BT] in the (then idle) stage memory
+        float* xch = reinterpret_cast<float*>(smem);
         const uint32_t sum = lane_base + (uint32_t)(C::NACC * BT);
         bool ok = true;
         for (int g = 0; g < ng && ok; g++) {
@@ -462,6 +471,9 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
                 }
                 if (!last) {
                     tc::tmem_st16(sum + c, v);
+                } else if constexpr (SW) {
+#pragma unroll
+                    for (int i = 0; i < 16; i++) xch[r * XLD + c + i] = v[i];
                 } else if (n < N) {
 #pragma unroll
                     for (int i = 0; i < 16; i++) {
@@ -477,6 +489,20 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
             __syncwarp();
             if (lane == 0) mbs_arrive(accfree + 8 * a);
         }
+        if constexpr (SW) {
+            // every MMA has completed (the last group's commit), so the stages
+            // are idle; gate row i pairs with up row 64 + i
+            asm volatile("bar.sync 2, %0;" ::"n"(GM_READERS * 32) : "memory");
+            const int rt = (warp - 5) * 32 + lane;
+            for (int idx = rt; idx < 64 * BT && ok; idx += GM_READERS * 32) {
+                const int fi = idx & 63, tl = idx >> 6, f = n0 + fi, tt = t0 + tl;
+                if (f < N && tt < T) {
+                    const float x = xch[fi * XLD + tl], u = xch[(64 + fi) * XLD + tl];
+                    const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));   // k_silu_mul (kernels_cpu.c:323-336)
+                    Y[(size_t)tt * N + f] = __fmul_rn(__fmul_rn(x, sig), u);
+                }
+            }
+        }
     }
     tc::fence_before_sync();
     __syncthreads();
@@ -486,50 +512,65 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
     }
 }
 
-template <int DT, int BT>
-static int launch_gemm_bt(const void* W, const float* X, float* Y, const float* R, int N, int K, int T, cudaStream_t st,
-                          unsigned* err) {
+template <int DT, int BT, bool SW>
+static int launch_gemm_bt(const void* W, const void* W2, const float* X, float* Y, const float* R, int N, int K, int T,
+                          cudaStream_t st, unsigned* err) {
     using C = GmCfg<BT>;
-    GB_CUDA_TRY(set_smem_once(reinterpret_cast<const void*>(k_gemm<DT, BT>), C::SMEM));
+    static_assert(!SW || 128 * (BT + 1) * 4 <= C::S * C::STAGE, "SwiGLU exchange fits the stages");
+    GB_CUDA_TRY(set_smem_once(reinterpret_cast<const void*>(k_gemm<DT, BT, SW>), C::SMEM));
     CUtensorMap xmap;
     if (!gemm_encode_x(&xmap, X, T, K, GM_BK, BT)) return GB_ECUDA;
-    dim3 grid((N + GM_ROWS - 1) / GM_ROWS, (T + BT - 1) / BT);
-    k_gemm<DT, BT><<<grid, GM_THREADS, C::SMEM, st>>>(xmap, static_cast<const uint8_t*>(W), Y, R, N, K, T, err);
+    const int rows = SW ? GM_ROWS / 2 : GM_ROWS;
+    dim3 grid((N + rows - 1) / rows, (T + BT - 1) / BT);
+    k_gemm<DT, BT, SW><<<grid, GM_THREADS, C::SMEM, st>>>(xmap, static_cast<const uint8_t*>(W),
+                                                           static_cast<const uint8_t*>(W2), Y, R, N, K, T, err);
     return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
 }
 
 // 256-token tiles (half the MMA instructions and weight conversions per
 // FLOP) when their grid still gives every SM a CTA, else 128-token tiles
 // (GB_GEMM_BT=128 / 256 forces one size).
-template <int DT>
-static int launch_gemm(const void* W, const float* X, float* Y, const float* R, int N, int K, int T, cudaStream_t st,
-                       unsigned* err) {
+template <int DT, bool SW>
+static int launch_gemm(const void* W, const void* W2, const float* X, float* Y, const float* R, int N, int K, int T,
+                       cudaStream_t st, unsigned* err) {
     static const int force = [] {
         const char* e = getenv("GB_GEMM_BT");
         return e ? atoi(e) : 0;
     }();
-    const long ctas256 = (long)((N + GM_ROWS - 1) / GM_ROWS) * ((T + 255) / 256);
+    const int rows = SW ? GM_ROWS / 2 : GM_ROWS;
+    const long ctas256 = (long)((N + rows - 1) / rows) * ((T + 255) / 256);
     const bool wide = force ? force == 256 : ctas256 >= sm_count();
-    return wide ? launch_gemm_bt<DT, 256>(W, X, Y, R, N, K, T, st, err)
-                : launch_gemm_bt<DT, 128>(W, X, Y, R, N, K, T, st, err);
+    return wide ? launch_gemm_bt<DT, 256, SW>(W, W2, X, Y, R, N, K, T, st, err)
+                : launch_gemm_bt<DT, 128, SW>(W, W2, X, Y, R, N, K, T, st, err);
+}
+
+template <bool SW>
+static int gemm_dispatch(int dtype, const void* W, const void* W2, const float* X, float* Y, const float* R, int N,
+                         int K, int T, cudaStream_t st, unsigned* err) {
+    if (!W || !X || !Y || N <= 0 || K <= 0 || T <= 0 || (SW && !W2)) return GB_EINVAL;
+    const bool a16 = dtype == GB_DT_F32 || dtype == GB_DT_Q4_K || dtype == GB_DT_Q5_K || dtype == GB_DT_F16;
+    if ((reinterpret_cast<uintptr_t>(X) & 15) ||
+        (a16 && ((reinterpret_cast<uintptr_t>(W) & 15) || (SW && (reinterpret_cast<uintptr_t>(W2) & 15)))))
+        return GB_EINVAL;
+    switch (dtype) {
+        case GB_DT_F32: return K % GM_BK ? GB_ESHAPE : launch_gemm<GB_DT_F32, SW>(W, W2, X, Y, R, N, K, T, st, err);
+        case GB_DT_Q8_0: return K % 32 ? GB_ESHAPE : launch_gemm<GB_DT_Q8_0, SW>(W, W2, X, Y, R, N, K, T, st, err);
+        case GB_DT_Q4_K: return K % 256 ? GB_ESHAPE : launch_gemm<GB_DT_Q4_K, SW>(W, W2, X, Y, R, N, K, T, st, err);
+        case GB_DT_Q6_K: return K % 256 ? GB_ESHAPE : launch_gemm<GB_DT_Q6_K, SW>(W, W2, X, Y, R, N, K, T, st, err);
+        case GB_DT_Q5_K: return K % 256 ? GB_ESHAPE : launch_gemm<GB_DT_Q5_K, SW>(W, W2, X, Y, R, N, K, T, st, err);
+        case GB_DT_F16: return K % GM_BK ? GB_ESHAPE : launch_gemm<GB_DT_F16, SW>(W, W2, X, Y, R, N, K, T, st, err);
+        default: return GB_EINVAL;
+    }
 }
 
 int gemm_launch(int dtype, const void* W, const float* X, float* Y, const float* R, int N, int K, int T,
                 cudaStream_t st, unsigned* err) {
-    if (!W || !X || !Y || N <= 0 || K <= 0 || T <= 0) return GB_EINVAL;
-    if ((reinterpret_cast<uintptr_t>(X) & 15) ||
-        ((dtype == GB_DT_F32 || dtype == GB_DT_Q4_K || dtype == GB_DT_Q5_K || dtype == GB_DT_F16) &&
-         (reinterpret_cast<uintptr_t>(W) & 15)))
-        return GB_EINVAL;
-    switch (dtype) {
-        case GB_DT_F32: return K % GM_BK ? GB_ESHAPE : launch_gemm<GB_DT_F32>(W, X, Y, R, N, K, T, st, err);
-        case GB_DT_Q8_0: return K % 32 ? GB_ESHAPE : launch_gemm<GB_DT_Q8_0>(W, X, Y, R, N, K, T, st, err);
-        case GB_DT_Q4_K: return K % 256 ? GB_ESHAPE : launch_gemm<GB_DT_Q4_K>(W, X, Y, R, N, K, T, st, err);
-        case GB_DT_Q6_K: return K % 256 ? GB_ESHAPE : launch_gemm<GB_DT_Q6_K>(W, X, Y, R, N, K, T, st, err);
-        case GB_DT_Q5_K: return K % 256 ? GB_ESHAPE : launch_gemm<GB_DT_Q5_K>(W, X, Y, R, N, K, T, st, err);
-        case GB_DT_F16: return K % GM_BK ? GB_ESHAPE : launch_gemm<GB_DT_F16>(W, X, Y, R, N, K, T, st, err);
-        default: return GB_EINVAL;
-    }
+    return gemm_dispatch<false>(dtype, W, nullptr, X, Y, R, N, K, T, st, err);
+}
+
+int gemm_swiglu_launch(int dtype, const void* Wg, const void* Wu, const float* X, float* Y, int F, int K, int T,
+                       cudaStream_t st, unsigned* err) {
+    return gemm_dispatch<true>(dtype, Wg, Wu, X, Y, nullptr, F, K, T, st, err);
 }
 
 }  // namespace gb

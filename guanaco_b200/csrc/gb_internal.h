@@ -116,6 +116,11 @@ bool gemm_encode_x(void* map128, const float* X, int T, int K, int box_k, int bo
 // GB_ETIMEOUT in *err (null: the module-wide word of gb_gemm_error).
 int gemm_launch(int dtype, const void* W, const float* X, float* Y, const float* R, int N, int K, int T,
                 cudaStream_t st, unsigned* err = nullptr);
+// Y[t][f] = silu(X Wg^T)[t][f] * (X Wu^T)[t][f] (k_silu_mul's rounding) for
+// f < F, in one GEMM launch: gate and up (same dtype, F rows each) share the
+// activation tiles, and the two products never reach HBM.
+int gemm_swiglu_launch(int dtype, const void* Wg, const void* Wu, const float* X, float* Y, int F, int K, int T,
+                       cudaStream_t st, unsigned* err = nullptr);
 
 // Tensor-parallel context of a layer (world > 1): the wo and ffn_down
 // matvecs write this rank's partial to `part`, then an all-reduce over peer

@@ -8,8 +8,8 @@
 //   RoPE(q), RoPE(k), KV append     k_pf_rope_kv (rows pos0 .. pos0 + T - 1)
 //   attn = causal softmax(q k^T / sqrt(hd)) v    k_pf_attn
 //   h += attn . Wo^T                gb_gemm with the residual
-//   xn = RMSNorm(h); gate, up       k_rmsnorm, gb_gemm x 2
-//   gate = silu(gate) * up          k_silu_mul
+//   xn = RMSNorm(h)                 k_rmsnorm
+//   gate = silu(xn Wg^T) * (xn Wu^T)  one GEMM launch (gate and up rows per CTA)
 //   h += gate . Wdown^T             gb_gemm with the residual
 //
 // Activations are row-major [T][width] fp32 in HBM; the K / V caches keep the
@@ -649,9 +649,14 @@ int enqueue_prefill_layer(const PrefillArgs& a, cudaStream_t st) {
         return rc;
     if ((rc = gemm(GB_WO, a.attn, a.hidden, a.hidden, H, QD))) return rc;
     if ((rc = rmsnorm_rows(a.hidden, a.rf, a.xn, H, T, a.eps, st))) return rc;
-    if ((rc = gemm(GB_WGATE, a.xn, a.gate, nullptr, F, H))) return rc;
-    if ((rc = gemm(GB_WUP, a.xn, a.up, nullptr, F, H))) return rc;
-    if ((rc = gb_silu_mul(a.gate, a.up, T * F, st))) return rc;
+    if (a.dt[GB_WGATE] == a.dt[GB_WUP]) {   // silu(gate) * up straight from one GEMM
+        if ((rc = gemm_swiglu_launch(a.dt[GB_WGATE], a.w[GB_WGATE], a.w[GB_WUP], a.xn, a.gate, F, H, T, st, a.err)))
+            return rc;
+    } else {
+        if ((rc = gemm(GB_WGATE, a.xn, a.gate, nullptr, F, H))) return rc;
+        if ((rc = gemm(GB_WUP, a.xn, a.up, nullptr, F, H))) return rc;
+        if ((rc = gb_silu_mul(a.gate, a.up, T * F, st))) return rc;
+    }
     return gemm(GB_WDOWN, a.gate, a.hidden, a.hidden, H, F);
 }
 
