@@ -146,7 +146,9 @@ def kernel_benchmarks(gb, torch, dm, peak):
         del g
         return e0.elapsed_time(e1) / (n_iter * reps) * 1e-3
 
-    def matvec_case(tag, dt, rows, cols, copies, n_iter):
+    def matvec_case(tag, dt, rows, cols, copies, n_iter, alg_cols=None):
+        # alg_cols: the matrix's real columns when its rows are laid out padded
+        # to `cols` (the algorithmic bytes count the real ones)
         wbytes = gb.matrix_bytes(dt, rows, cols)
         bufs = [torch.empty(wbytes + 16, dtype=torch.uint8, device="cuda") for _ in range(copies)]
         nblk = wbytes // gb.BLOCK_BYTES[dt]
@@ -157,7 +159,8 @@ def kernel_benchmarks(gb, torch, dm, peak):
         y = torch.empty(rows, dtype=torch.float32, device="cuda")
         st.synchronize()
         t = timed(lambda i: gb.matvec(dt, bufs[i % copies], rows, cols, x, y, stream=sp), n_iter)
-        alg = wbytes + 4 * cols + 4 * rows
+        ac = alg_cols or cols
+        alg = gb.matrix_bytes(dt, rows, ac) + 4 * ac + 4 * rows
         gbs = alg / t / 1e9
         res[tag] = {"us": round(t * 1e6, 2), "alg_bytes": alg, "GB/s": round(gbs, 1), "frac": round(gbs / peak, 3)}
         del bufs
@@ -190,7 +193,8 @@ def kernel_benchmarks(gb, torch, dm, peak):
     matvec_case("q6k_matvec_4096x14336 (config 1)", 5, 4096, 14336, 10, 200)
     matvec_case("q6k_matvec_128256x4096 (config 1, output head)", 5, 128256, 4096, 2, 40)
     matvec_case("q8_0_matvec_14336x4096", 2, 14336, 4096, 8, 200)
-    matvec_case("q6k_matvec_2048x5632 (config 3 ffn_down)", 5, 2048, 5632, 24, 400)
+    matvec_case("q6k_matvec_2048x5632 (config 3 ffn_down, rows padded to 24 blocks as the model lays them out)", 5,
+                2048, 6144, 24, 400, alg_cols=5632)
 
     # config 2: RoPE + append + GQA attention over 8193 positions (fp32 KV)
     nh, nkv, hd, ms, pos = 32, 8, 128, 8448, 8192

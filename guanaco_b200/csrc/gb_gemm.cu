@@ -161,7 +161,7 @@ __device__ __forceinline__ void store_split(uint8_t* hi, uint8_t* lo, int r, con
 template <int DT, int BT, bool SW>
 __global__ void __launch_bounds__(GM_THREADS, 1)
 k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, const uint8_t* __restrict__ W2, float* Y,
-       const float* R, int N, int K, int T, unsigned* err) {
+       const float* R, int N, int ldy, int K, int T, unsigned* err) {
     using C = GmCfg<BT>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte aligned stage ring; barriers and the tensor-memory address
@@ -479,7 +479,7 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
                     for (int i = 0; i < 16; i++) {
                         const int tt = t0 + c + i;
                         if (tt < T) {
-                            const size_t o = (size_t)tt * N + n;
+                            const size_t o = (size_t)tt * ldy + n;
                             Y[o] = v[i] + (R ? R[o] : 0.f);
                         }
                     }
@@ -499,7 +499,7 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
                 if (f < N && tt < T) {
                     const float x = xch[fi * XLD + tl], u = xch[(64 + fi) * XLD + tl];
                     const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));   // k_silu_mul (kernels_cpu.c:323-336)
-                    Y[(size_t)tt * N + f] = __fmul_rn(__fmul_rn(x, sig), u);
+                    Y[(size_t)tt * ldy + f] = __fmul_rn(__fmul_rn(x, sig), u);
                 }
             }
         }
@@ -513,8 +513,8 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
 }
 
 template <int DT, int BT, bool SW>
-static int launch_gemm_bt(const void* W, const void* W2, const float* X, float* Y, const float* R, int N, int K, int T,
-                          cudaStream_t st, unsigned* err) {
+static int launch_gemm_bt(const void* W, const void* W2, const float* X, float* Y, const float* R, int N, int ldy, int K,
+                          int T, cudaStream_t st, unsigned* err) {
     using C = GmCfg<BT>;
     static_assert(!SW || 128 * (BT + 1) * 4 <= C::S * C::STAGE, "SwiGLU exchange fits the stages");
     GB_CUDA_TRY(set_smem_once(reinterpret_cast<const void*>(k_gemm<DT, BT, SW>), C::SMEM));
@@ -523,7 +523,7 @@ static int launch_gemm_bt(const void* W, const void* W2, const float* X, float* 
     const int rows = SW ? GM_ROWS / 2 : GM_ROWS;
     dim3 grid((N + rows - 1) / rows, (T + BT - 1) / BT);
     k_gemm<DT, BT, SW><<<grid, GM_THREADS, C::SMEM, st>>>(xmap, static_cast<const uint8_t*>(W),
-                                                           static_cast<const uint8_t*>(W2), Y, R, N, K, T, err);
+                                                           static_cast<const uint8_t*>(W2), Y, R, N, ldy, K, T, err);
     return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
 }
 
@@ -531,8 +531,8 @@ static int launch_gemm_bt(const void* W, const void* W2, const float* X, float* 
 // FLOP) when their grid still gives every SM a CTA, else 128-token tiles
 // (GB_GEMM_BT=128 / 256 forces one size).
 template <int DT, bool SW>
-static int launch_gemm(const void* W, const void* W2, const float* X, float* Y, const float* R, int N, int K, int T,
-                       cudaStream_t st, unsigned* err) {
+static int launch_gemm(const void* W, const void* W2, const float* X, float* Y, const float* R, int N, int ldy, int K,
+                       int T, cudaStream_t st, unsigned* err) {
     static const int force = [] {
         const char* e = getenv("GB_GEMM_BT");
         return e ? atoi(e) : 0;
@@ -540,37 +540,37 @@ static int launch_gemm(const void* W, const void* W2, const float* X, float* Y, 
     const int rows = SW ? GM_ROWS / 2 : GM_ROWS;
     const long ctas256 = (long)((N + rows - 1) / rows) * ((T + 255) / 256);
     const bool wide = force ? force == 256 : ctas256 >= sm_count();
-    return wide ? launch_gemm_bt<DT, 256, SW>(W, W2, X, Y, R, N, K, T, st, err)
-                : launch_gemm_bt<DT, 128, SW>(W, W2, X, Y, R, N, K, T, st, err);
+    return wide ? launch_gemm_bt<DT, 256, SW>(W, W2, X, Y, R, N, ldy, K, T, st, err)
+                : launch_gemm_bt<DT, 128, SW>(W, W2, X, Y, R, N, ldy, K, T, st, err);
 }
 
 template <bool SW>
 static int gemm_dispatch(int dtype, const void* W, const void* W2, const float* X, float* Y, const float* R, int N,
-                         int K, int T, cudaStream_t st, unsigned* err) {
-    if (!W || !X || !Y || N <= 0 || K <= 0 || T <= 0 || (SW && !W2)) return GB_EINVAL;
+                         int ldy, int K, int T, cudaStream_t st, unsigned* err) {
+    if (!W || !X || !Y || N <= 0 || K <= 0 || T <= 0 || ldy < N || (SW && !W2)) return GB_EINVAL;
     const bool a16 = dtype == GB_DT_F32 || dtype == GB_DT_Q4_K || dtype == GB_DT_Q5_K || dtype == GB_DT_F16;
     if ((reinterpret_cast<uintptr_t>(X) & 15) ||
         (a16 && ((reinterpret_cast<uintptr_t>(W) & 15) || (SW && (reinterpret_cast<uintptr_t>(W2) & 15)))))
         return GB_EINVAL;
     switch (dtype) {
-        case GB_DT_F32: return K % GM_BK ? GB_ESHAPE : launch_gemm<GB_DT_F32, SW>(W, W2, X, Y, R, N, K, T, st, err);
-        case GB_DT_Q8_0: return K % 32 ? GB_ESHAPE : launch_gemm<GB_DT_Q8_0, SW>(W, W2, X, Y, R, N, K, T, st, err);
-        case GB_DT_Q4_K: return K % 256 ? GB_ESHAPE : launch_gemm<GB_DT_Q4_K, SW>(W, W2, X, Y, R, N, K, T, st, err);
-        case GB_DT_Q6_K: return K % 256 ? GB_ESHAPE : launch_gemm<GB_DT_Q6_K, SW>(W, W2, X, Y, R, N, K, T, st, err);
-        case GB_DT_Q5_K: return K % 256 ? GB_ESHAPE : launch_gemm<GB_DT_Q5_K, SW>(W, W2, X, Y, R, N, K, T, st, err);
-        case GB_DT_F16: return K % GM_BK ? GB_ESHAPE : launch_gemm<GB_DT_F16, SW>(W, W2, X, Y, R, N, K, T, st, err);
+        case GB_DT_F32: return K % GM_BK ? GB_ESHAPE : launch_gemm<GB_DT_F32, SW>(W, W2, X, Y, R, N, ldy, K, T, st, err);
+        case GB_DT_Q8_0: return K % 32 ? GB_ESHAPE : launch_gemm<GB_DT_Q8_0, SW>(W, W2, X, Y, R, N, ldy, K, T, st, err);
+        case GB_DT_Q4_K: return K % 256 ? GB_ESHAPE : launch_gemm<GB_DT_Q4_K, SW>(W, W2, X, Y, R, N, ldy, K, T, st, err);
+        case GB_DT_Q6_K: return K % 256 ? GB_ESHAPE : launch_gemm<GB_DT_Q6_K, SW>(W, W2, X, Y, R, N, ldy, K, T, st, err);
+        case GB_DT_Q5_K: return K % 256 ? GB_ESHAPE : launch_gemm<GB_DT_Q5_K, SW>(W, W2, X, Y, R, N, ldy, K, T, st, err);
+        case GB_DT_F16: return K % GM_BK ? GB_ESHAPE : launch_gemm<GB_DT_F16, SW>(W, W2, X, Y, R, N, ldy, K, T, st, err);
         default: return GB_EINVAL;
     }
 }
 
 int gemm_launch(int dtype, const void* W, const float* X, float* Y, const float* R, int N, int K, int T,
-                cudaStream_t st, unsigned* err) {
-    return gemm_dispatch<false>(dtype, W, nullptr, X, Y, R, N, K, T, st, err);
+                cudaStream_t st, unsigned* err, int ldy) {
+    return gemm_dispatch<false>(dtype, W, nullptr, X, Y, R, N, ldy ? ldy : N, K, T, st, err);
 }
 
 int gemm_swiglu_launch(int dtype, const void* Wg, const void* Wu, const float* X, float* Y, int F, int K, int T,
-                       cudaStream_t st, unsigned* err) {
-    return gemm_dispatch<true>(dtype, Wg, Wu, X, Y, nullptr, F, K, T, st, err);
+                       cudaStream_t st, unsigned* err, int ldy) {
+    return gemm_dispatch<true>(dtype, Wg, Wu, X, Y, nullptr, F, ldy ? ldy : F, K, T, st, err);
 }
 
 }  // namespace gb

@@ -113,14 +113,15 @@ bool gemm_encode_x(void* map128, const float* X, int T, int K, int box_k, int bo
 // Prefill GEMM on the tensor cores (gb_gemm.cu): Y[t][n] = sum_k X[t][k]
 // W[n][k] (+ R[t][n]) for T tokens, W fp32 (dtype GB_DT_F32) or GGUF blocks;
 // fp32-equivalent (3xTF32).  R may alias Y.  A wait that gives up records
-// GB_ETIMEOUT in *err (null: the module-wide word of gb_gemm_error).
+// GB_ETIMEOUT in *err (null: the module-wide word of gb_gemm_error).  Rows of
+// Y and R are ldy floats apart (0: N).
 int gemm_launch(int dtype, const void* W, const float* X, float* Y, const float* R, int N, int K, int T,
-                cudaStream_t st, unsigned* err = nullptr);
+                cudaStream_t st, unsigned* err = nullptr, int ldy = 0);
 // Y[t][f] = silu(X Wg^T)[t][f] * (X Wu^T)[t][f] (k_silu_mul's rounding) for
 // f < F, in one GEMM launch: gate and up (same dtype, F rows each) share the
 // activation tiles, and the two products never reach HBM.
 int gemm_swiglu_launch(int dtype, const void* Wg, const void* Wu, const float* X, float* Y, int F, int K, int T,
-                       cudaStream_t st, unsigned* err = nullptr);
+                       cudaStream_t st, unsigned* err = nullptr, int ldy = 0);
 
 // Tensor-parallel context of a layer (world > 1): the wo and ffn_down
 // matvecs write this rank's partial to `part`, then an all-reduce over peer
@@ -197,6 +198,7 @@ struct PrefillArgs {
     float *hidden, *xn, *q, *k, *v, *attn, *gate, *up;
     unsigned* err;            // the model's error word
     int T, pos0, H, n_heads, n_kv, hd, ff, max_seq;
+    int fk;                   // ffn_down's columns (ff, or ff rounded up with zero padding): gate / up row width
     float eps;
 };
 int enqueue_prefill_layer(const PrefillArgs& a, cudaStream_t st);

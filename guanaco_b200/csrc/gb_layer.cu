@@ -404,6 +404,7 @@ struct gb_model {
     int rank = 0, world = 1;
     int nh = 0, nkv = 0;              // local q / kv heads
     int ff = 0, ff_pad = 0;           // local FFN rows; padded width of the gate / up buffers
+    bool pad_down = false;            // gb_model_synthesize: Q6_K ffn_down rows padded to ff_pad columns
     int vocab_l = 0, vocab_off = 0;   // output-head rows of this rank
     void* comm = nullptr;             // exchange buffer (world > 1)
     size_t comm_bytes = 0;
@@ -504,10 +505,11 @@ extern "C" gb_model* gb_model_create_tp(const gb_model_config* cfg, int rank, in
     m->nh = c.n_heads / world;
     m->nkv = c.n_kv_heads / world;
     m->ff = c.ff_dim / world;
-    // a Q6_K ffn_down shard keeps its rows at 8-block multiples (zero blocks
-    // after the shard's columns) so its tensor map has a 16-byte stride; the
-    // gate / up buffers carry the matching zero tail
-    m->ff_pad = world > 1 ? (m->ff + 2047) / 2048 * 2048 : m->ff;
+    // a Q6_K ffn_down shard (and a synthesised one-GPU ffn_down) keeps its
+    // rows at 8-block multiples (zero blocks after the FFN columns) so its
+    // tensor map has a 16-byte stride; the gate / up buffers carry the
+    // matching zero tail
+    m->ff_pad = (m->ff + 2047) / 2048 * 2048;
     m->vocab_off = (int)((long long)rank * c.vocab_size / world);
     m->vocab_l = (int)((long long)(rank + 1) * c.vocab_size / world) - m->vocab_off;
     m->kv_dim = m->nkv * c.head_dim;
@@ -716,7 +718,7 @@ static void mat_shape(const gb_model* m, int which, int dtype, int* rows, int* c
         case GB_WK: case GB_WV: *rows = m->kv_dim; *cols = H; break;
         case GB_WO: *rows = H; *cols = QD; break;
         case GB_WGATE: case GB_WUP: *rows = m->ff; *cols = H; break;
-        default: *rows = H; *cols = (dtype == GB_DT_Q6_K && m->world > 1) ? m->ff_pad : m->ff; break;
+        default: *rows = H; *cols = (dtype == GB_DT_Q6_K && (m->world > 1 || m->pad_down)) ? m->ff_pad : m->ff; break;
     }
 }
 
@@ -759,6 +761,13 @@ extern "C" int gb_model_synthesize(gb_model* m, uint64_t seed) {
     if (!ones) return GB_ENOMEM;
     int rc = gb_fill_f32(ones, H, 1.0f, m->stream);
     if (rc) return rc;
+    // the synthesised Q6_K ffn_down rows are padded to 8-block multiples (the
+    // tensor-map path); gb_model_set_matrix afterwards takes unpadded rows
+    struct PadScope {
+        gb_model* m;
+        ~PadScope() { m->pad_down = false; }
+    } pad_scope{m};
+    m->pad_down = true;
     for (int l = 0; l < c.n_layers; l++) {
         for (int wi = 0; wi < GB_NMAT; wi++) {
             const int dtype = (wi == GB_WV || wi == GB_WDOWN) ? GB_DT_Q6_K : GB_DT_Q4_K;
@@ -1233,10 +1242,11 @@ static int prefill_chunk() {
     return v > 0 ? v : 4096;
 }
 
-// Activation floats per prompt token: hidden, xn, q, k, v, attn, gate, up.
+// Activation floats per prompt token: hidden, xn, q, k, v, attn, gate, up
+// (gate / up rows ff_pad wide: ffn_down's columns, zero past the FFN).
 static size_t pf_floats_per_token(const gb_model* m) {
     const int H = m->c.hidden_dim, QD = m->nh * m->c.head_dim;
-    return 2 * (size_t)H + 2 * (size_t)QD + 2 * (size_t)m->kv_dim + 2 * (size_t)m->ff;
+    return 2 * (size_t)H + 2 * (size_t)QD + 2 * (size_t)m->kv_dim + 2 * (size_t)m->ff_pad;
 }
 
 static int pf_reserve(gb_model* m, int T) {
@@ -1248,10 +1258,14 @@ static int pf_reserve(gb_model* m, int T) {
         m->pf = nullptr;
         m->pf_cap = 0;
     }
-    if (cudaMalloc(&m->pf, (size_t)T * pf_floats_per_token(m) * sizeof(float)) != cudaSuccess) {
+    const size_t bytes = (size_t)T * pf_floats_per_token(m) * sizeof(float);
+    if (cudaMalloc(&m->pf, bytes) != cudaSuccess) {
         m->pf = nullptr;
         return GB_ENOMEM;
     }
+    // zero once: the gate / up columns past the FFN stay zero (never written)
+    if (cudaMemsetAsync(m->pf, 0, bytes, m->stream) != cudaSuccess || cudaStreamSynchronize(m->stream) != cudaSuccess)
+        return GB_ECUDA;
     m->pf_cap = T;
     return GB_OK;
 }
@@ -1278,7 +1292,7 @@ extern "C" int gb_model_prefill(gb_model* m, const int* d_tokens, int n_tokens, 
     a.k = a.attn + cap * QD;
     a.v = a.k + cap * KVD;
     a.gate = a.v + cap * KVD;
-    a.up = a.gate + cap * F;
+    a.up = a.gate + cap * (size_t)m->ff_pad;
     a.err = m->err;
     a.rope = m->rope;
     a.H = H; a.n_heads = m->nh; a.n_kv = m->nkv; a.hd = c.head_dim; a.ff = F; a.max_seq = c.max_seq;
@@ -1297,6 +1311,7 @@ extern "C" int gb_model_prefill(gb_model* m, const int* d_tokens, int n_tokens, 
             }
             a.ra = m->ra[l]; a.rf = m->rf[l];
             a.kc = gb_model_k_cache(m, l); a.vc = gb_model_v_cache(m, l);
+            a.fk = m->plan[(size_t)l * GB_NMAT + GB_WDOWN].cols;   // ff, or ff_pad for padded rows
             if ((rc = enqueue_prefill_layer(a, st))) return rc;
         }
     }

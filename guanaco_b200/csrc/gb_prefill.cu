@@ -649,15 +649,18 @@ int enqueue_prefill_layer(const PrefillArgs& a, cudaStream_t st) {
         return rc;
     if ((rc = gemm(GB_WO, a.attn, a.hidden, a.hidden, H, QD))) return rc;
     if ((rc = rmsnorm_rows(a.hidden, a.rf, a.xn, H, T, a.eps, st))) return rc;
+    // gate / up rows are fk wide (ffn_down's columns); columns F .. fk - 1
+    // stay zero (the prefill buffer is zeroed once and never written there)
+    const int FK = a.fk;
     if (a.dt[GB_WGATE] == a.dt[GB_WUP]) {   // silu(gate) * up straight from one GEMM
-        if ((rc = gemm_swiglu_launch(a.dt[GB_WGATE], a.w[GB_WGATE], a.w[GB_WUP], a.xn, a.gate, F, H, T, st, a.err)))
+        if ((rc = gemm_swiglu_launch(a.dt[GB_WGATE], a.w[GB_WGATE], a.w[GB_WUP], a.xn, a.gate, F, H, T, st, a.err, FK)))
             return rc;
     } else {
-        if ((rc = gemm(GB_WGATE, a.xn, a.gate, nullptr, F, H))) return rc;
-        if ((rc = gemm(GB_WUP, a.xn, a.up, nullptr, F, H))) return rc;
-        if ((rc = gb_silu_mul(a.gate, a.up, T * F, st))) return rc;
+        if ((rc = gemm_launch(a.dt[GB_WGATE], a.w[GB_WGATE], a.xn, a.gate, nullptr, F, H, T, st, a.err, FK))) return rc;
+        if ((rc = gemm_launch(a.dt[GB_WUP], a.w[GB_WUP], a.xn, a.up, nullptr, F, H, T, st, a.err, FK))) return rc;
+        if ((rc = gb_silu_mul(a.gate, a.up, T * FK, st))) return rc;   // silu(0) * 0 = 0 in the padding
     }
-    return gemm(GB_WDOWN, a.gate, a.hidden, a.hidden, H, F);
+    return gemm(GB_WDOWN, a.gate, a.hidden, a.hidden, H, FK);
 }
 
 }  // namespace gb
