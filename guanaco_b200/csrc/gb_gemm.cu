@@ -6,24 +6,31 @@
 // matvec once per token; the reference's GPU prefill hook is a stub
 // (src/engine/gpu_prefill.c:3-20).
 //
-// Precision: fp32-equivalent ("3xTF32").  Every weight is dequantised to its
-// fp32 value (the reference's per-weight formula), every activation is fp32;
-// both are split into a tf32 part and an fp32 remainder (x = hi + lo), and
+// Precision: fp32-equivalent.  Every weight is dequantised to its fp32 value
+// (the reference's per-weight formula), every activation is fp32; both are
+// split into an 11-significant-bit part and the remainder (x = hi + lo), and
 // the tensor cores accumulate hi.hi + hi.lo + lo.hi in fp32 tensor memory --
 // about 22 bits of each operand, so a prompt pass agrees with the reference's
-// fp32 arithmetic as closely as the decode matvecs do.
+// fp32 arithmetic as closely as the decode matvecs do.  The operands are fp16
+// pairs by default ("3xF16", kind::f16: twice the tensor rate of tf32 and
+// half the shared-memory bytes); fp16's narrow exponent range is handled by
+// powers of two -- each weight row by 2^e_n chosen from its blocks' scale
+// fields (an upper bound of |w|), each token row of X by 2^e_t chosen from
+// its largest |x| (gemm_row_absmax), both to below 2^15 -- taken back out
+// exactly when Y is written.  GB_GEMM_KIND=tf32 selects tf32 pairs ("3xTF32",
+// no scaling) instead.
 //
 // CTA tile: 128 weight rows (the MMA's M) x BT = 128 or 256 tokens (its N;
 // 256 when that grid still fills every SM), K in chunks of 32 through a
-// 3-stage (2 at BT 256) shared-memory ring in the tensor cores' K-major
-// layout (gb_tc.cuh).  Warps 0-3 convert weights: thread r dequantises row
+// shared-memory ring in the tensor cores' K-major layout (gb_tc.cuh): 6 / 4
+// stages of fp16 pairs at BT 128 / 256 (3 / 2 of tf32 pairs).  Warps 0-3 convert weights: thread r dequantises row
 // r's 32 weights of the chunk (Q4_K / Q5_K: 16-byte loads of a chunk pair's
 // bytes, three / two pairs in flight; Q6_K: 4-byte words of a 128-column
 // half-block, the next one loaded before this one is converted).  Warp 13
 // loads each chunk's raw activation tile [BT tokens][32] fp32 by TMA into the
 // stage, and warps 9-12 split it in place.  Warp 4 allocates the tensor
-// memory and one of its lanes issues the 12 MMAs of a chunk (4 k-steps x 3
-// products), then commits them to the stage's "empty" barrier so the
+// memory and one of its lanes issues the MMAs of a chunk (2 k-steps of 16
+// for fp16, 4 of 8 for tf32, x 3 products), then commits them to the stage's "empty" barrier so the
 // converters may refill it.  The tensor cores' fp32 accumulation is not
 // round-to-nearest, so its error grows with the number of MMAs summed into
 // one accumulator: every 256 columns of K (512 at BT 256) the MMAs start a
@@ -39,30 +46,38 @@
 #include "gb_mt.cuh"
 #include "gb_tc.cuh"
 
+#include <string.h>
+
 namespace gb {
 
 constexpr int GM_ROWS = 128;             // weight rows per CTA (MMA M)
 constexpr int GM_BK = 32;                // K per stage
-constexpr int GM_TILE_A = GM_ROWS * GM_BK * 4;   // 16 KB (one of hi / lo)
 constexpr int GM_READERS = 4;            // accumulator-reader warps (5 .. 8)
 constexpr int GM_XWARPS = 4;             // activation converter warps (9 .. 12)
 constexpr int GM_XPROD = 5 + GM_READERS + GM_XWARPS;   // warp 13: activation tile loads (TMA)
 constexpr int GM_THREADS = (GM_XPROD + 1) * 32;
 
-// Token-tile size BT (the MMA's N): 128 (3 stages, two accumulators
-// alternating) or 256 (2 stages: 96 KB each; one accumulator, refilled once
-// the readers have taken it).
-template <int BT>
+// Token-tile size BT (the MMA's N): 128 (two accumulators alternating) or
+// 256 (one accumulator, refilled once the readers have taken it); operands
+// as fp16 (H16) or tf32 pairs.  A stage holds the hi and lo tiles of A (the
+// weights) and B (the activations); the raw fp32 activation tile lands in
+// B's hi (and, for fp16, lo) tile and is split in place.
+template <int BT, bool H16>
 struct GmCfg {
-    static constexpr int TILE_B = BT * GM_BK * 4;              // 16 / 32 KB (one of hi / lo)
-    static constexpr int STAGE = 2 * GM_TILE_A + 2 * TILE_B;
-    static constexpr int S = BT == 256 ? 2 : 3;                 // ring stages
+    static constexpr int EB = H16 ? 2 : 4;                     // operand element bytes
+    static constexpr int TILE_A = GM_ROWS * GM_BK * EB;        // one of hi / lo: 8 / 16 KB
+    static constexpr int TILE_B = BT * GM_BK * EB;
+    static constexpr int XRAW = BT * GM_BK * 4;                // the raw fp32 activation tile
+    static constexpr int STAGE = 2 * TILE_A + 2 * TILE_B;
+    static constexpr int S = H16 ? (BT == 256 ? 4 : 6) : (BT == 256 ? 2 : 3);   // ring stages
     static constexpr int NACC = BT == 256 ? 1 : 2;              // accumulators in tensor memory
     static constexpr int KG = BT == 256 ? 16 : 8;               // chunks per accumulator group (512 / 256 columns of K)
     static constexpr int SMEM = S * STAGE + 1024;
     static constexpr uint32_t TMEM_COLS = 512;                  // NACC x BT accumulator + BT running sum
+    static_assert(XRAW <= 2 * TILE_B, "the raw activation tile fits B's tiles");
 };
-static_assert(GmCfg<256>::SMEM <= 227 * 1024 && GmCfg<128>::SMEM <= 227 * 1024, "shared memory");
+static_assert(GmCfg<256, false>::SMEM <= 227 * 1024 && GmCfg<128, false>::SMEM <= 227 * 1024, "shared memory");
+static_assert(GmCfg<256, true>::SMEM <= 227 * 1024 && GmCfg<128, true>::SMEM <= 227 * 1024, "shared memory");
 
 __device__ unsigned g_gemm_err;
 
@@ -154,15 +169,75 @@ __device__ __forceinline__ void store_split(uint8_t* hi, uint8_t* lo, int r, con
     }
 }
 
+// The same for fp16 pairs (values already scaled below 2^15).
+template <int R>
+__device__ __forceinline__ void store_split16(uint8_t* hi, uint8_t* lo, int r, const float (&v)[32]) {
+#pragma unroll
+    for (int g = 0; g < 4; g++) {
+        uint32_t h[4], l[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) tc::split_f16x2(v[8 * g + 2 * e], v[8 * g + 2 * e + 1], h[e], l[e]);
+        const uint32_t off = tc::tile_off16(r, 8 * g, R);
+        *reinterpret_cast<uint4*>(hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<uint4*>(lo + off) = make_uint4(l[0], l[1], l[2], l[3]);
+    }
+}
+
+// Scale exponent of weight row n for fp16 operands, from an upper bound of
+// its |w|: per block |d| * max|sc * q| + |dmin| * max(m) (Q4_K 15 * 63 and
+// 63, Q5_K 31 * 63 and 63), |d| * 128 * 32 (Q6_K), |d| * 128 (Q8_0), the
+// row's largest |w| (F32); fp16 rows are exact as they are (0).
+template <int DT>
+__device__ int row_scale_exp(const uint8_t* __restrict__ W, int n, int K) {
+    float b = 0.f;
+    if constexpr (DT == GB_DT_F16) {
+        return 0;
+    } else if constexpr (DT == GB_DT_F32) {
+        const float4* p = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(W) + (size_t)n * K);
+#pragma unroll 8
+        for (int i = 0; i < K / 4; i++) {
+            const float4 v = __ldg(p + i);
+            b = fmaxf(b, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+    } else if constexpr (DT == GB_DT_Q4_K || DT == GB_DT_Q5_K) {
+        constexpr int BB = DT == GB_DT_Q5_K ? GB_Q5K_BYTES : GB_Q4K_BYTES;
+        constexpr float QM = DT == GB_DT_Q5_K ? 31.f * 63.f : 15.f * 63.f;
+        const int nb = K / 256;
+        const uint8_t* row = W + (size_t)n * nb * BB;
+#pragma unroll 8
+        for (int i = 0; i < nb; i++) {
+            const uint32_t h = __ldg(reinterpret_cast<const uint32_t*>(row + (size_t)i * BB));
+            b = fmaxf(b, fabsf(f16_bits_to_f32(h & 0xFFFF)) * QM + fabsf(f16_bits_to_f32(h >> 16)) * 63.f);
+        }
+    } else if constexpr (DT == GB_DT_Q6_K) {
+        const int nb = K / 256;
+        const uint8_t* row = W + (size_t)n * nb * GB_Q6K_BYTES;
+#pragma unroll 8
+        for (int i = 0; i < nb; i++)
+            b = fmaxf(b, fabsf(f16_bits_to_f32(__ldg(reinterpret_cast<const uint16_t*>(row + (size_t)i * GB_Q6K_BYTES + 208)))) *
+                             4096.f);
+    } else {   // Q8_0
+        const int nb = K / 32;
+        const uint8_t* row = W + (size_t)n * nb * GB_Q80_BYTES;
+#pragma unroll 8
+        for (int i = 0; i < nb; i++)
+            b = fmaxf(b, fabsf(f16_bits_to_f32(__ldg(reinterpret_cast<const uint16_t*>(row + (size_t)i * GB_Q80_BYTES)))) *
+                             128.f);
+    }
+    return tc::f16_scale_exp(__float_as_uint(b));
+}
+
 // SW (SwiGLU): W holds the gate rows and W2 the up rows of an FFN; a CTA
 // takes 64 gate rows and the same 64 up rows (its 128 weight rows), and the
 // readers write Y[t][f] = silu(gate) * up (k_silu_mul's rounding) for its 64
 // columns instead of the two products.
-template <int DT, int BT, bool SW>
+// H16: fp16 operand pairs, X token rows scaled by the exponents that
+// xmax[t] (the bits of max |X[t][.]|) gives; else tf32 pairs (xmax unused).
+template <int DT, int BT, bool SW, bool H16>
 __global__ void __launch_bounds__(GM_THREADS, 1)
 k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, const uint8_t* __restrict__ W2, float* Y,
-       const float* R, int N, int ldy, int K, int T, unsigned* err) {
-    using C = GmCfg<BT>;
+       const float* R, const uint32_t* __restrict__ xmax, int N, int ldy, int K, int T, unsigned* err) {
+    using C = GmCfg<BT, H16>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte aligned stage ring; barriers and the tensor-memory address
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -194,7 +269,8 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
 
     if (warp == 4) {   // ---- MMA issue (one lane)
         if (lane == 0) {
-            constexpr uint32_t idesc = tc::idesc_tf32(GM_ROWS, BT);
+            constexpr uint32_t idesc = H16 ? tc::idesc_f16(GM_ROWS, BT) : tc::idesc_tf32(GM_ROWS, BT);
+            constexpr int KS = H16 ? 16 : 8;   // K per MMA
             constexpr uint32_t LBO_A = GM_ROWS / 8 * 128, LBO_B = BT / 8 * 128;
             bool ok = true;
             for (int g = 0; g < ng && ok; g++) {
@@ -210,17 +286,23 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
                     if (!ok) break;
                     tc::fence_after_sync();
                     const uint32_t base = tc::smem_u32(smem + (size_t)s * C::STAGE);
-                    const uint32_t ahi = base, alo = base + GM_TILE_A, bhi = base + 2 * GM_TILE_A,
+                    const uint32_t ahi = base, alo = base + C::TILE_A, bhi = base + 2 * C::TILE_A,
                                    blo = bhi + C::TILE_B;
 #pragma unroll
-                    for (int ks = 0; ks < GM_BK / 8; ks++) {
+                    for (int ks = 0; ks < GM_BK / KS; ks++) {   // each k-step spans two core-matrix column groups
                         const uint64_t dah = tc::smem_desc(ahi + ks * 2 * LBO_A, LBO_A, 128);
                         const uint64_t dal = tc::smem_desc(alo + ks * 2 * LBO_A, LBO_A, 128);
                         const uint64_t dbh = tc::smem_desc(bhi + ks * 2 * LBO_B, LBO_B, 128);
                         const uint64_t dbl = tc::smem_desc(blo + ks * 2 * LBO_B, LBO_B, 128);
-                        tc::mma_tf32(acc, dah, dbh, idesc, kc > g * C::KG || ks > 0);
-                        tc::mma_tf32(acc, dah, dbl, idesc, true);
-                        tc::mma_tf32(acc, dal, dbh, idesc, true);
+                        if constexpr (H16) {
+                            tc::mma_f16(acc, dah, dbh, idesc, kc > g * C::KG || ks > 0);
+                            tc::mma_f16(acc, dah, dbl, idesc, true);
+                            tc::mma_f16(acc, dal, dbh, idesc, true);
+                        } else {
+                            tc::mma_tf32(acc, dah, dbh, idesc, kc > g * C::KG || ks > 0);
+                            tc::mma_tf32(acc, dah, dbl, idesc, true);
+                            tc::mma_tf32(acc, dal, dbh, idesc, true);
+                        }
                     }
                     tc::mma_commit(empty + 8 * s);   // the stage may be refilled once these MMAs are done
                 }
@@ -233,12 +315,15 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
         // SW: rows 0-63 are gate rows n0 .., rows 64-127 the same up rows (W2)
         const int n = SW ? n0 + (r & 63) : n0 + r;
         const uint8_t* Wm = (SW && r >= 64) ? W2 : W;
+        // fp16 operands: the row scaled by 2^e (folded into the block scales)
+        const float rs = H16 && n < N ? tc::pow2f(row_scale_exp<DT>(Wm, n, K)) : 1.f;
         bool ok = true;
         auto put = [&](int kc, const float (&v)[32]) {   // one chunk into its stage
             const int s = kc % C::S;
             if (kc >= C::S && ok) ok = gm_wait(empty + 8 * s, ((kc / C::S) - 1) & 1, err);
             uint8_t* st = smem + (size_t)s * C::STAGE;
-            store_split<GM_ROWS>(st, st + GM_TILE_A, r, v);
+            if constexpr (H16) store_split16<GM_ROWS>(st, st + C::TILE_A, r, v);
+            else store_split<GM_ROWS>(st, st + C::TILE_A, r, v);
             tc::fence_async_smem();   // generic-proxy stores -> tensor-core reads
             __syncwarp();
             if (lane == 0) mbs_arrive(full + 8 * s);
@@ -290,7 +375,7 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
                     uint32_t sc, mn;
                     if (j < 4) { sc = sbyte(j) & 63; mn = sbyte(j + 4) & 63; }
                     else { sc = (sbyte(j + 4) & 0xF) | ((sbyte(j - 4) >> 6) << 4); mn = (sbyte(j + 4) >> 4) | ((sbyte(j) >> 6) << 4); }
-                    const float d1 = d * (float)sc, m1 = dmin * (float)mn;
+                    const float d1 = d * (float)sc * rs, m1 = dmin * (float)mn * rs;   // exact: rs is 2^e
                     float v[32];
 #pragma unroll
                     for (int wi = 0; wi < 8; wi++) {
@@ -358,7 +443,7 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
                 for (int G = 0; G < 4; G++) {
                     const int s0 = (int)(int8_t)((scw[G >> 1] >> (16 * (G & 1))) & 0xFF);
                     const int s1 = (int)(int8_t)((scw[G >> 1] >> (16 * (G & 1) + 8)) & 0xFF);
-                    const float ds0 = d * (float)s0, ds1 = d * (float)s1;
+                    const float ds0 = d * (float)s0 * rs, ds1 = d * (float)s1 * rs;
                     float v[32];
 #pragma unroll
                     for (int wi = 0; wi < 8; wi++) {
@@ -384,6 +469,10 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
                 float v[32];
                 if (n < N) {
                     dequant32<DT>(Wm, n, K, kc * GM_BK, v);
+                    if constexpr (H16) {
+#pragma unroll
+                        for (int i = 0; i < 32; i++) v[i] *= rs;
+                    }
                 } else {
 #pragma unroll
                     for (int i = 0; i < 32; i++) v[i] = 0.f;
@@ -398,9 +487,9 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
                 const int s = kc % C::S;
                 if (kc >= C::S) ok = gm_wait(empty + 8 * s, ((kc / C::S) - 1) & 1, err);
                 if (!ok) break;
-                mbs_expect(xfull + 8 * s, C::TILE_B);
-                // into the stage's hi tile; rows past T read as zeros
-                tma_load_3d(tc::smem_u32(smem + (size_t)s * C::STAGE + 2 * GM_TILE_A), &xmap, kc * GM_BK, t0, 0,
+                mbs_expect(xfull + 8 * s, C::XRAW);
+                // into the stage's B tiles; rows past T read as zeros
+                tma_load_3d(tc::smem_u32(smem + (size_t)s * C::STAGE + 2 * C::TILE_A), &xmap, kc * GM_BK, t0, 0,
                             xfull + 8 * s);
             }
         }
@@ -411,12 +500,18 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
         // raw row each) and writes (one core matrix) hit 8 different bank groups
         const int xw = warp - (5 + GM_READERS), j = lane & 7;
         const int rr = xw * 32 + 8 * (lane >> 3) + j;
+        constexpr int NP = BT / 128;   // 128-row passes (the warp's rows rr + 128 pass)
+        float xs[NP];                  // fp16 operands: token row scales 2^e_t
+#pragma unroll
+        for (int pp = 0; pp < NP; pp++) {
+            const int t = t0 + rr + 128 * pp;
+            xs[pp] = H16 && t < T ? tc::pow2f(tc::f16_scale_exp(xmax[t])) : 1.f;
+        }
         bool ok = true;
         for (int kc = 0; kc < nk; kc++) {
             const int s = kc % C::S;
             if (ok) ok = gm_wait(xfull + 8 * s, (kc / C::S) & 1, err);
-            uint8_t* hi = smem + (size_t)s * C::STAGE + 2 * GM_TILE_A;
-            constexpr int NP = BT / 128;   // 128-row passes (the warp's rows rr + 128 pass)
+            uint8_t* hi = smem + (size_t)s * C::STAGE + 2 * C::TILE_A;
             float4 u[NP][8];
 #pragma unroll
             for (int pp = 0; pp < NP; pp++)
@@ -429,6 +524,16 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
             for (int pp = 0; pp < NP; pp++)
 #pragma unroll
                 for (int c = 0; c < 8; c++) {
+                    if constexpr (H16) {   // 4 columns: 8 bytes of hi, 8 of lo
+                        const float4 x = u[pp][c];
+                        uint32_t h01, l01, h23, l23;
+                        tc::split_f16x2(x.x * xs[pp], x.y * xs[pp], h01, l01);
+                        tc::split_f16x2(x.z * xs[pp], x.w * xs[pp], h23, l23);
+                        const uint32_t off = tc::tile_off16(rr + 128 * pp, 4 * ((j + c) & 7), BT);
+                        *reinterpret_cast<uint2*>(hi + off) = make_uint2(h01, h23);
+                        *reinterpret_cast<uint2*>(hi + C::TILE_B + off) = make_uint2(l01, l23);
+                        continue;
+                    }
                     float h[4], l[4];
                     tc::split_tf32(u[pp][c].x, h[0], l[0]);
                     tc::split_tf32(u[pp][c].y, h[1], l[1]);
@@ -451,6 +556,8 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
         constexpr int XLD = BT + 1;   // SW: final sums [128 rows][BT] in the (then idle) stage memory
         float* xch = reinterpret_cast<float*>(smem);
         const uint32_t sum = lane_base + (uint32_t)(C::NACC * BT);
+        // fp16 operands: 2^-e_n of this weight row (times 2^-e_t per token below)
+        const float inv_r = H16 && n < N ? tc::pow2f(-row_scale_exp<DT>((SW && r >= 64) ? W2 : W, n, K)) : 1.f;
         bool ok = true;
         for (int g = 0; g < ng && ok; g++) {
             const int a = g % C::NACC;
@@ -471,7 +578,16 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
                 }
                 if (!last) {
                     tc::tmem_st16(sum + c, v);
-                } else if constexpr (SW) {
+                    continue;
+                }
+                if constexpr (H16) {
+#pragma unroll
+                    for (int i = 0; i < 16; i++) {
+                        const int tt = t0 + c + i;
+                        v[i] = v[i] * inv_r * (tt < T ? tc::pow2f(-tc::f16_scale_exp(xmax[tt])) : 1.f);
+                    }
+                }
+                if constexpr (SW) {
 #pragma unroll
                     for (int i = 0; i < 16; i++) xch[r * XLD + c + i] = v[i];
                 } else if (n < N) {
@@ -512,18 +628,53 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
     }
 }
 
-template <int DT, int BT, bool SW>
-static int launch_gemm_bt(const void* W, const void* W2, const float* X, float* Y, const float* R, int N, int ldy, int K,
-                          int T, cudaStream_t st, unsigned* err) {
-    using C = GmCfg<BT>;
+// Bits of max |X[t][.]| for every token row t (one CTA per row; K a
+// multiple of 4): the fp16 operands' token exponents.  Non-negative floats
+// order as their bit patterns.
+__global__ void __launch_bounds__(256) k_row_absmax(const float* __restrict__ X, int K, uint32_t* __restrict__ xmax) {
+    const float4* row = reinterpret_cast<const float4*>(X + (size_t)blockIdx.x * K);
+    uint32_t m = 0;
+    for (int i = threadIdx.x; i < K / 4; i += blockDim.x) {
+        const float4 v = __ldg(row + i);
+        m = max(m, max(max(__float_as_uint(fabsf(v.x)), __float_as_uint(fabsf(v.y))),
+                       max(__float_as_uint(fabsf(v.z)), __float_as_uint(fabsf(v.w)))));
+    }
+    m = __reduce_max_sync(0xFFFFFFFFu, m);
+    __shared__ uint32_t part[8];
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++) m = max(m, part[w]);
+        xmax[blockIdx.x] = m;
+    }
+}
+
+bool gemm_f16_operands() {
+    static const bool f16 = [] {
+        const char* e = getenv("GB_GEMM_KIND");
+        return !(e && strcmp(e, "tf32") == 0);
+    }();
+    return f16;
+}
+
+int gemm_row_absmax(const float* X, int T, int K, uint32_t* xmax, cudaStream_t st) {
+    if (!X || !xmax || T <= 0 || K <= 0 || (K & 3) || (reinterpret_cast<uintptr_t>(X) & 15)) return GB_EINVAL;
+    k_row_absmax<<<T, 256, 0, st>>>(X, K, xmax);
+    return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
+}
+
+template <int DT, int BT, bool SW, bool H16>
+static int launch_gemm_bt(const void* W, const void* W2, const float* X, float* Y, const float* R, const uint32_t* xmax,
+                          int N, int ldy, int K, int T, cudaStream_t st, unsigned* err) {
+    using C = GmCfg<BT, H16>;
     static_assert(!SW || 128 * (BT + 1) * 4 <= C::S * C::STAGE, "SwiGLU exchange fits the stages");
-    GB_CUDA_TRY(set_smem_once(reinterpret_cast<const void*>(k_gemm<DT, BT, SW>), C::SMEM));
+    GB_CUDA_TRY(set_smem_once(reinterpret_cast<const void*>(k_gemm<DT, BT, SW, H16>), C::SMEM));
     CUtensorMap xmap;
     if (!gemm_encode_x(&xmap, X, T, K, GM_BK, BT)) return GB_ECUDA;
     const int rows = SW ? GM_ROWS / 2 : GM_ROWS;
     dim3 grid((N + rows - 1) / rows, (T + BT - 1) / BT);
-    k_gemm<DT, BT, SW><<<grid, GM_THREADS, C::SMEM, st>>>(xmap, static_cast<const uint8_t*>(W),
-                                                           static_cast<const uint8_t*>(W2), Y, R, N, ldy, K, T, err);
+    k_gemm<DT, BT, SW, H16><<<grid, GM_THREADS, C::SMEM, st>>>(
+        xmap, static_cast<const uint8_t*>(W), static_cast<const uint8_t*>(W2), Y, R, xmax, N, ldy, K, T, err);
     return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
 }
 
@@ -531,8 +682,8 @@ static int launch_gemm_bt(const void* W, const void* W2, const float* X, float* 
 // FLOP) when their grid still gives every SM a CTA, else 128-token tiles
 // (GB_GEMM_BT=128 / 256 forces one size).
 template <int DT, bool SW>
-static int launch_gemm(const void* W, const void* W2, const float* X, float* Y, const float* R, int N, int ldy, int K,
-                       int T, cudaStream_t st, unsigned* err) {
+static int launch_gemm(const void* W, const void* W2, const float* X, float* Y, const float* R, const uint32_t* xmax,
+                       int N, int ldy, int K, int T, cudaStream_t st, unsigned* err) {
     static const int force = [] {
         const char* e = getenv("GB_GEMM_BT");
         return e ? atoi(e) : 0;
@@ -540,37 +691,60 @@ static int launch_gemm(const void* W, const void* W2, const float* X, float* Y, 
     const int rows = SW ? GM_ROWS / 2 : GM_ROWS;
     const long ctas256 = (long)((N + rows - 1) / rows) * ((T + 255) / 256);
     const bool wide = force ? force == 256 : ctas256 >= sm_count();
-    return wide ? launch_gemm_bt<DT, 256, SW>(W, W2, X, Y, R, N, ldy, K, T, st, err)
-                : launch_gemm_bt<DT, 128, SW>(W, W2, X, Y, R, N, ldy, K, T, st, err);
+    if (gemm_f16_operands())
+        return wide ? launch_gemm_bt<DT, 256, SW, true>(W, W2, X, Y, R, xmax, N, ldy, K, T, st, err)
+                    : launch_gemm_bt<DT, 128, SW, true>(W, W2, X, Y, R, xmax, N, ldy, K, T, st, err);
+    return wide ? launch_gemm_bt<DT, 256, SW, false>(W, W2, X, Y, R, xmax, N, ldy, K, T, st, err)
+                : launch_gemm_bt<DT, 128, SW, false>(W, W2, X, Y, R, xmax, N, ldy, K, T, st, err);
 }
 
 template <bool SW>
 static int gemm_dispatch(int dtype, const void* W, const void* W2, const float* X, float* Y, const float* R, int N,
-                         int ldy, int K, int T, cudaStream_t st, unsigned* err) {
+                         int ldy, int K, int T, cudaStream_t st, unsigned* err, const uint32_t* xmax) {
     if (!W || !X || !Y || N <= 0 || K <= 0 || T <= 0 || ldy < N || (SW && !W2)) return GB_EINVAL;
     const bool a16 = dtype == GB_DT_F32 || dtype == GB_DT_Q4_K || dtype == GB_DT_Q5_K || dtype == GB_DT_F16;
     if ((reinterpret_cast<uintptr_t>(X) & 15) ||
         (a16 && ((reinterpret_cast<uintptr_t>(W) & 15) || (SW && (reinterpret_cast<uintptr_t>(W2) & 15)))))
         return GB_EINVAL;
-    switch (dtype) {
-        case GB_DT_F32: return K % GM_BK ? GB_ESHAPE : launch_gemm<GB_DT_F32, SW>(W, W2, X, Y, R, N, ldy, K, T, st, err);
-        case GB_DT_Q8_0: return K % 32 ? GB_ESHAPE : launch_gemm<GB_DT_Q8_0, SW>(W, W2, X, Y, R, N, ldy, K, T, st, err);
-        case GB_DT_Q4_K: return K % 256 ? GB_ESHAPE : launch_gemm<GB_DT_Q4_K, SW>(W, W2, X, Y, R, N, ldy, K, T, st, err);
-        case GB_DT_Q6_K: return K % 256 ? GB_ESHAPE : launch_gemm<GB_DT_Q6_K, SW>(W, W2, X, Y, R, N, ldy, K, T, st, err);
-        case GB_DT_Q5_K: return K % 256 ? GB_ESHAPE : launch_gemm<GB_DT_Q5_K, SW>(W, W2, X, Y, R, N, ldy, K, T, st, err);
-        case GB_DT_F16: return K % GM_BK ? GB_ESHAPE : launch_gemm<GB_DT_F16, SW>(W, W2, X, Y, R, N, ldy, K, T, st, err);
-        default: return GB_EINVAL;
+    if (dtype != GB_DT_F32 && dtype != GB_DT_Q8_0 && dtype != GB_DT_Q4_K && dtype != GB_DT_Q6_K &&
+        dtype != GB_DT_Q5_K && dtype != GB_DT_F16)
+        return GB_EINVAL;
+    const int kmul = (dtype == GB_DT_Q4_K || dtype == GB_DT_Q6_K || dtype == GB_DT_Q5_K) ? 256 : 32;
+    if (K % kmul) return GB_ESHAPE;
+    // fp16 operands without the caller's row maxima: computed here into
+    // stream-ordered scratch
+    uint32_t* tmp = nullptr;
+    if (gemm_f16_operands() && !xmax) {
+        if (cudaMallocAsync(reinterpret_cast<void**>(&tmp), (size_t)T * sizeof(uint32_t), st) != cudaSuccess)
+            return GB_ENOMEM;
+        const int rc = gemm_row_absmax(X, T, K, tmp, st);
+        if (rc) {
+            cudaFreeAsync(tmp, st);
+            return rc;
+        }
+        xmax = tmp;
     }
+    int rc;
+    switch (dtype) {
+        case GB_DT_F32: rc = launch_gemm<GB_DT_F32, SW>(W, W2, X, Y, R, xmax, N, ldy, K, T, st, err); break;
+        case GB_DT_Q8_0: rc = launch_gemm<GB_DT_Q8_0, SW>(W, W2, X, Y, R, xmax, N, ldy, K, T, st, err); break;
+        case GB_DT_Q4_K: rc = launch_gemm<GB_DT_Q4_K, SW>(W, W2, X, Y, R, xmax, N, ldy, K, T, st, err); break;
+        case GB_DT_Q6_K: rc = launch_gemm<GB_DT_Q6_K, SW>(W, W2, X, Y, R, xmax, N, ldy, K, T, st, err); break;
+        case GB_DT_Q5_K: rc = launch_gemm<GB_DT_Q5_K, SW>(W, W2, X, Y, R, xmax, N, ldy, K, T, st, err); break;
+        default: rc = launch_gemm<GB_DT_F16, SW>(W, W2, X, Y, R, xmax, N, ldy, K, T, st, err); break;
+    }
+    if (tmp && cudaFreeAsync(tmp, st) != cudaSuccess && rc == GB_OK) rc = GB_ECUDA;
+    return rc;
 }
 
 int gemm_launch(int dtype, const void* W, const float* X, float* Y, const float* R, int N, int K, int T,
-                cudaStream_t st, unsigned* err, int ldy) {
-    return gemm_dispatch<false>(dtype, W, nullptr, X, Y, R, N, ldy ? ldy : N, K, T, st, err);
+                cudaStream_t st, unsigned* err, int ldy, const uint32_t* xmax) {
+    return gemm_dispatch<false>(dtype, W, nullptr, X, Y, R, N, ldy ? ldy : N, K, T, st, err, xmax);
 }
 
 int gemm_swiglu_launch(int dtype, const void* Wg, const void* Wu, const float* X, float* Y, int F, int K, int T,
-                       cudaStream_t st, unsigned* err, int ldy) {
-    return gemm_dispatch<true>(dtype, Wg, Wu, X, Y, nullptr, F, ldy ? ldy : F, K, T, st, err);
+                       cudaStream_t st, unsigned* err, int ldy, const uint32_t* xmax) {
+    return gemm_dispatch<true>(dtype, Wg, Wu, X, Y, nullptr, F, ldy ? ldy : F, K, T, st, err, xmax);
 }
 
 }  // namespace gb

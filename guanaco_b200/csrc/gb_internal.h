@@ -112,16 +112,22 @@ bool gemm_encode_x(void* map128, const float* X, int T, int K, int box_k, int bo
 
 // Prefill GEMM on the tensor cores (gb_gemm.cu): Y[t][n] = sum_k X[t][k]
 // W[n][k] (+ R[t][n]) for T tokens, W fp32 (dtype GB_DT_F32) or GGUF blocks;
-// fp32-equivalent (3xTF32).  R may alias Y.  A wait that gives up records
-// GB_ETIMEOUT in *err (null: the module-wide word of gb_gemm_error).  Rows of
-// Y and R are ldy floats apart (0: N).
+// fp32-equivalent (3xF16, or 3xTF32 with GB_GEMM_KIND=tf32).  R may alias Y.
+// A wait that gives up records GB_ETIMEOUT in *err (null: the module-wide
+// word of gb_gemm_error).  Rows of Y and R are ldy floats apart (0: N).
+// xmax: the bits of max |X[t][.]| per token (gemm_row_absmax), shared by
+// GEMMs of one X; null computes them into stream-ordered scratch.
 int gemm_launch(int dtype, const void* W, const float* X, float* Y, const float* R, int N, int K, int T,
-                cudaStream_t st, unsigned* err = nullptr, int ldy = 0);
+                cudaStream_t st, unsigned* err = nullptr, int ldy = 0, const uint32_t* xmax = nullptr);
 // Y[t][f] = silu(X Wg^T)[t][f] * (X Wu^T)[t][f] (k_silu_mul's rounding) for
 // f < F, in one GEMM launch: gate and up (same dtype, F rows each) share the
 // activation tiles, and the two products never reach HBM.
 int gemm_swiglu_launch(int dtype, const void* Wg, const void* Wu, const float* X, float* Y, int F, int K, int T,
-                       cudaStream_t st, unsigned* err = nullptr, int ldy = 0);
+                       cudaStream_t st, unsigned* err = nullptr, int ldy = 0, const uint32_t* xmax = nullptr);
+// True unless GB_GEMM_KIND=tf32: the GEMMs read xmax.
+bool gemm_f16_operands();
+// xmax[t] = bits of max |X[t][k]| over k < K (X rows K floats apart).
+int gemm_row_absmax(const float* X, int T, int K, uint32_t* xmax, cudaStream_t st);
 
 // Tensor-parallel context of a layer (world > 1): the wo and ffn_down
 // matvecs write this rank's partial to `part`, then an all-reduce over peer
@@ -196,6 +202,7 @@ struct PrefillArgs {
     float *kc, *vc;           // this layer's caches [n_kv][max_seq][hd]
     const float* rope;        // RoPE table [max_seq][hd]
     float *hidden, *xn, *q, *k, *v, *attn, *gate, *up;
+    uint32_t* xmax;           // [T] row maxima of the GEMMs' X (fp16 operands)
     unsigned* err;            // the model's error word
     int T, pos0, H, n_heads, n_kv, hd, ff, max_seq;
     int fk;                   // ffn_down's columns (ff, or ff rounded up with zero padding): gate / up row width

@@ -1243,10 +1243,11 @@ static int prefill_chunk() {
 }
 
 // Activation floats per prompt token: hidden, xn, q, k, v, attn, gate, up
-// (gate / up rows ff_pad wide: ffn_down's columns, zero past the FFN).
+// (gate / up rows ff_pad wide: ffn_down's columns, zero past the FFN), and
+// the GEMM inputs' row maximum.
 static size_t pf_floats_per_token(const gb_model* m) {
     const int H = m->c.hidden_dim, QD = m->nh * m->c.head_dim;
-    return 2 * (size_t)H + 2 * (size_t)QD + 2 * (size_t)m->kv_dim + 2 * (size_t)m->ff_pad;
+    return 2 * (size_t)H + 2 * (size_t)QD + 2 * (size_t)m->kv_dim + 2 * (size_t)m->ff_pad + 1;   // + xmax
 }
 
 static int pf_reserve(gb_model* m, int T) {
@@ -1293,6 +1294,7 @@ extern "C" int gb_model_prefill(gb_model* m, const int* d_tokens, int n_tokens, 
     a.v = a.k + cap * KVD;
     a.gate = a.v + cap * KVD;
     a.up = a.gate + cap * (size_t)m->ff_pad;
+    a.xmax = reinterpret_cast<uint32_t*>(a.up + cap * (size_t)m->ff_pad);
     a.err = m->err;
     a.rope = m->rope;
     a.H = H; a.n_heads = m->nh; a.n_kv = m->nkv; a.hd = c.head_dim; a.ff = F; a.max_seq = c.max_seq;

@@ -12,6 +12,7 @@
 // groups R * 16 bytes apart (its leading byte offset).  One tf32 MMA covers
 // K = 8, i.e. two column groups.
 #pragma once
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -23,6 +24,13 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)_
 // Byte offset of element (r, k) in a K-major tile of R rows x 32 elements.
 __host__ __device__ __forceinline__ uint32_t tile_off(int r, int k, int R) {
     return (uint32_t)((r >> 3) * 128 + (k >> 2) * (R / 8 * 128) + (r & 7) * 16 + (k & 3) * 4);
+}
+
+// The same layout for 16-bit elements: core matrices of 8 rows x 8 elements
+// (still 16 bytes per row), so one f16 MMA (K = 16) also covers two column
+// groups and the descriptors are unchanged.
+__host__ __device__ __forceinline__ uint32_t tile_off16(int r, int k, int R) {
+    return (uint32_t)((r >> 3) * 128 + (k >> 3) * (R / 8 * 128) + (r & 7) * 16 + (k & 7) * 2);
 }
 
 // Shared-memory matrix descriptor (sm_100): start address, leading byte
@@ -45,6 +53,16 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
          | (2u << 10)                       // B format: tf32
          | ((uint32_t)(N >> 3) << 17)       // N / 8
          | ((uint32_t)(M >> 4) << 24);      // M / 16
+}
+
+// Instruction descriptor of kind::f16 with fp16 A and B (the same type, as
+// the instruction requires) and fp32 accumulation, both K-major.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+    return (1u << 4)                        // D format: f32
+         | (0u << 7)                        // A format: f16
+         | (0u << 10)                       // B format: f16
+         | ((uint32_t)(N >> 3) << 17)
+         | ((uint32_t)(M >> 4) << 24);
 }
 
 // Tensor memory: a warp allocates ncols columns (a power of two >= 32) and
@@ -71,6 +89,15 @@ __device__ __forceinline__ void mma_tf32(uint32_t tmem_d, uint64_t adesc, uint64
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate)
+        : "memory");
+}
+// D[tmem] (+)= A[smem] . B[smem]^T with fp16 operands (K = 16 per instruction).
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate)
         : "memory");
 }
@@ -131,6 +158,35 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) 
 __device__ __forceinline__ void split_tf32(float x, float& hi, float& lo) {
     hi = __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
     lo = x - hi;
+}
+
+// Two values split for fp16 operands: the 11-bit hi of split_tf32 is exact in
+// fp16 (for magnitudes in its normal range; callers scale by powers of two
+// so that |x| < 2^15), and the fp32 remainder is rounded to fp16.  Returns
+// the packed hi pair (first value in the low half) and the lo pair.
+__device__ __forceinline__ void split_f16x2(float a, float b, uint32_t& hi, uint32_t& lo) {
+    float ha, la, hb, lb;
+    split_tf32(a, ha, la);
+    split_tf32(b, hb, lb);
+    const __half2 h = __floats2half2_rn(ha, hb), l = __floats2half2_rn(la, lb);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+// Power-of-two exponent e for which 2^e * m lies in [2^14, 2^15), from the
+// bits of a magnitude m >= 0: 0 for inf / NaN, the largest (126) for zero and
+// fp32 subnormals; clamped to [-126, 126] so that 2^e and 2^-e are both
+// normal floats.
+__host__ __device__ __forceinline__ int f16_scale_exp(uint32_t mbits) {
+    const int E = (int)((mbits >> 23) & 0xFFu);
+    if (E == 255) return 0;
+    if (E == 0) return 126;
+    const int e = 141 - E;
+    return e < -126 ? -126 : (e > 126 ? 126 : e);
+}
+// 2^e for |e| <= 126, built from its exponent bits.
+__device__ __forceinline__ float pow2f(int e) {
+    return __uint_as_float((uint32_t)(127 + e) << 23);
 }
 
 // Byte e (0..3) of w as an exact float minus `bias`: the byte is placed in
