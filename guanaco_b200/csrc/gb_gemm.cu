@@ -231,12 +231,15 @@ __device__ int row_scale_exp(const uint8_t* __restrict__ W, int n, int K) {
 // takes 64 gate rows and the same 64 up rows (its 128 weight rows), and the
 // readers write Y[t][f] = silu(gate) * up (k_silu_mul's rounding) for its 64
 // columns instead of the two products.
-// H16: fp16 operand pairs, X token rows scaled by the exponents that
-// xmax[t] (the bits of max |X[t][.]|) gives; else tf32 pairs (xmax unused).
+// H16: fp16 operand pairs; the activations come split (gemm_split_x): xmap
+// and xlmap view their hi and lo halves, and xinv holds the token scales'
+// inverses.  Else tf32 pairs: xmap views the fp32 X, which warps 9-12 split
+// in shared memory (xlmap and xinv unused).
 template <int DT, int BT, bool SW, bool H16>
 __global__ void __launch_bounds__(GM_THREADS, 1)
 k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, const uint8_t* __restrict__ W2, float* Y,
-       const float* R, const uint32_t* __restrict__ xmax, int N, int ldy, int K, int T, unsigned* err) {
+       const float* R, const __grid_constant__ CUtensorMap xlmap, const float* __restrict__ xinv, int N, int ldy, int K,
+       int T, unsigned* err) {
     using C = GmCfg<BT, H16>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte aligned stage ring; barriers and the tensor-memory address
@@ -251,7 +254,9 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
     const int ng = (nk + C::KG - 1) / C::KG;   // accumulator groups
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::S; s++) {
-            mbs_init(full + 8 * s, 4 + GM_XWARPS);   // one arrival per converter warp
+            // one arrival per converter warp (W, and for tf32 X), or for
+            // fp16 the W converters and the activation loads' expect_tx
+            mbs_init(full + 8 * s, H16 ? 4 + 1 : 4 + GM_XWARPS);
             mbs_init(empty + 8 * s, 1);  // the MMA commit
             mbs_init(xfull + 8 * s, 1);  // the activation tile's TMA load
         }
@@ -480,13 +485,23 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
                 put(kc, v);
             }
         }
-    } else if (warp == GM_XPROD) {   // ---- activation tiles: raw fp32 [128 tokens][32] by TMA
+    } else if (warp == GM_XPROD) {   // ---- activation tiles by TMA
         if (lane == 0) {
             bool ok = true;
             for (int kc = 0; kc < nk && ok; kc++) {
                 const int s = kc % C::S;
                 if (kc >= C::S) ok = gm_wait(empty + 8 * s, ((kc / C::S) - 1) & 1, err);
                 if (!ok) break;
+                if constexpr (H16) {
+                    // the hi and lo tiles [BT tokens][32] in the K-major
+                    // layout, completing on the stage's "full" barrier
+                    const uint32_t b = tc::smem_u32(smem + (size_t)s * C::STAGE + 2 * C::TILE_A);
+                    mbs_expect(full + 8 * s, 2 * C::TILE_B);
+                    tma_load_3d(b, &xmap, 0, t0 / 128, kc * (GM_BK / 8), full + 8 * s);
+                    tma_load_3d(b + C::TILE_B, &xlmap, 0, t0 / 128, kc * (GM_BK / 8), full + 8 * s);
+                    continue;
+                }
+                // raw fp32 [BT tokens][32]
                 mbs_expect(xfull + 8 * s, C::XRAW);
                 // into the stage's B tiles; rows past T read as zeros
                 tma_load_3d(tc::smem_u32(smem + (size_t)s * C::STAGE + 2 * C::TILE_A), &xmap, kc * GM_BK, t0, 0,
@@ -494,19 +509,14 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
             }
         }
         __syncwarp();
-    } else if (warp >= 5 + GM_READERS) {   // ---- activations: split the raw tile in place
+    } else if (warp >= 5 + GM_READERS) {   // ---- tf32: split the raw activation tile in place
+      if constexpr (!H16) {
         // lane (qq, j) converts row xw * 32 + 8 qq + j; step c takes its
         // column group (j + c) mod 8, so a quarter-warp's 16-byte reads (one
         // raw row each) and writes (one core matrix) hit 8 different bank groups
         const int xw = warp - (5 + GM_READERS), j = lane & 7;
         const int rr = xw * 32 + 8 * (lane >> 3) + j;
         constexpr int NP = BT / 128;   // 128-row passes (the warp's rows rr + 128 pass)
-        float xs[NP];                  // fp16 operands: token row scales 2^e_t
-#pragma unroll
-        for (int pp = 0; pp < NP; pp++) {
-            const int t = t0 + rr + 128 * pp;
-            xs[pp] = H16 && t < T ? tc::pow2f(tc::f16_scale_exp(xmax[t])) : 1.f;
-        }
         bool ok = true;
         for (int kc = 0; kc < nk; kc++) {
             const int s = kc % C::S;
@@ -524,16 +534,6 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
             for (int pp = 0; pp < NP; pp++)
 #pragma unroll
                 for (int c = 0; c < 8; c++) {
-                    if constexpr (H16) {   // 4 columns: 8 bytes of hi, 8 of lo
-                        const float4 x = u[pp][c];
-                        uint32_t h01, l01, h23, l23;
-                        tc::split_f16x2(x.x * xs[pp], x.y * xs[pp], h01, l01);
-                        tc::split_f16x2(x.z * xs[pp], x.w * xs[pp], h23, l23);
-                        const uint32_t off = tc::tile_off16(rr + 128 * pp, 4 * ((j + c) & 7), BT);
-                        *reinterpret_cast<uint2*>(hi + off) = make_uint2(h01, h23);
-                        *reinterpret_cast<uint2*>(hi + C::TILE_B + off) = make_uint2(l01, l23);
-                        continue;
-                    }
                     float h[4], l[4];
                     tc::split_tf32(u[pp][c].x, h[0], l[0]);
                     tc::split_tf32(u[pp][c].y, h[1], l[1]);
@@ -547,6 +547,7 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
             __syncwarp();
             if (lane == 0) mbs_arrive(full + 8 * s);
         }
+      }
     } else {   // ---- warps 5-8: sum the accumulators in fp32, then write Y
         // lane r of warp w reads tensor-memory lane 32 (w % 4) + r = weight
         // row; the running sum lives in a third tensor-memory region
@@ -584,7 +585,7 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
 #pragma unroll
                     for (int i = 0; i < 16; i++) {
                         const int tt = t0 + c + i;
-                        v[i] = v[i] * inv_r * (tt < T ? tc::pow2f(-tc::f16_scale_exp(xmax[tt])) : 1.f);
+                        v[i] = v[i] * inv_r * (tt < T ? xinv[tt] : 1.f);
                     }
                 }
                 if constexpr (SW) {
@@ -628,24 +629,52 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
     }
 }
 
-// Bits of max |X[t][.]| for every token row t (one CTA per row; K a
-// multiple of 4): the fp16 operands' token exponents.  Non-negative floats
-// order as their bit patterns.
-__global__ void __launch_bounds__(256) k_row_absmax(const float* __restrict__ X, int K, uint32_t* __restrict__ xmax) {
-    const float4* row = reinterpret_cast<const float4*>(X + (size_t)blockIdx.x * K);
-    uint32_t m = 0;
-    for (int i = threadIdx.x; i < K / 4; i += blockDim.x) {
-        const float4 v = __ldg(row + i);
-        m = max(m, max(max(__float_as_uint(fabsf(v.x)), __float_as_uint(fabsf(v.y))),
-                       max(__float_as_uint(fabsf(v.z)), __float_as_uint(fabsf(v.w)))));
+// Split 16 token rows of X per CTA (K a multiple of 32) for fp16 operands:
+// e from each row's largest |x| (so that |x| 2^e < 2^15), then x 2^e = hi +
+// lo as fp16 halves (tc::split_f16x2) written column-group-major (16 rows x
+// 16 bytes contiguous per group), inv = 2^-e; rows T .. tp - 1 are zero.
+// Non-negative floats order as their bit patterns.
+constexpr int XS_ROWS = 16;
+__global__ void __launch_bounds__(256) k_x_split16(const float* __restrict__ X, int K, int T, int tp,
+                                                    uint4* __restrict__ hi, uint4* __restrict__ lo,
+                                                    float* __restrict__ inv) {
+    __shared__ float scale[XS_ROWS];
+    const int t0 = blockIdx.x * XS_ROWS, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int rr = warp; rr < XS_ROWS; rr += 8) {   // each warp: two rows' maxima
+        const int t = t0 + rr;
+        uint32_t m = 0;
+        if (t < T) {
+            const float4* row = reinterpret_cast<const float4*>(X + (size_t)t * K);
+            for (int i = lane; i < K / 4; i += 32) {
+                const float4 v = __ldg(row + i);
+                m = max(m, max(max(__float_as_uint(fabsf(v.x)), __float_as_uint(fabsf(v.y))),
+                               max(__float_as_uint(fabsf(v.z)), __float_as_uint(fabsf(v.w)))));
+            }
+        }
+        m = __reduce_max_sync(0xFFFFFFFFu, m);
+        if (lane == 0) {
+            const int e = tc::f16_scale_exp(m);
+            scale[rr] = tc::pow2f(e);
+            if (t < T) inv[t] = tc::pow2f(-e);
+        }
     }
-    m = __reduce_max_sync(0xFFFFFFFFu, m);
-    __shared__ uint32_t part[8];
-    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = m;
     __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int w = 1; w < (int)(blockDim.x >> 5); w++) m = max(m, part[w]);
-        xmax[blockIdx.x] = m;
+    const int ng = K / 8;
+    for (int idx = threadIdx.x; idx < ng * XS_ROWS; idx += blockDim.x) {
+        const int rr = idx % XS_ROWS, g = idx / XS_ROWS, t = t0 + rr;
+        uint4 h = make_uint4(0u, 0u, 0u, 0u), l = h;
+        if (t < T) {
+            const float4* p = reinterpret_cast<const float4*>(X + (size_t)t * K + 8 * g);
+            const float4 a = __ldg(p), b = __ldg(p + 1);
+            const float sc = scale[rr];
+            tc::split_f16x2(a.x * sc, a.y * sc, h.x, l.x);
+            tc::split_f16x2(a.z * sc, a.w * sc, h.y, l.y);
+            tc::split_f16x2(b.x * sc, b.y * sc, h.z, l.z);
+            tc::split_f16x2(b.z * sc, b.w * sc, h.w, l.w);
+        }
+        const size_t o = (size_t)g * tp + t;
+        hi[o] = h;
+        lo[o] = l;
     }
 }
 
@@ -657,24 +686,36 @@ bool gemm_f16_operands() {
     return f16;
 }
 
-int gemm_row_absmax(const float* X, int T, int K, uint32_t* xmax, cudaStream_t st) {
-    if (!X || !xmax || T <= 0 || K <= 0 || (K & 3) || (reinterpret_cast<uintptr_t>(X) & 15)) return GB_EINVAL;
-    k_row_absmax<<<T, 256, 0, st>>>(X, K, xmax);
+int gemm_split_x(const float* X, int T, int K, void* hi, void* lo, float* inv, cudaStream_t st) {
+    if (!X || !hi || !lo || !inv || T <= 0 || K <= 0 || K % 32 || (reinterpret_cast<uintptr_t>(X) & 15) ||
+        (reinterpret_cast<uintptr_t>(hi) & 15) || (reinterpret_cast<uintptr_t>(lo) & 15))
+        return GB_EINVAL;
+    const int tp = gemm_split_rows(T);
+    k_x_split16<<<tp / XS_ROWS, 256, 0, st>>>(X, K, T, tp, static_cast<uint4*>(hi), static_cast<uint4*>(lo), inv);
     return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
 }
 
 template <int DT, int BT, bool SW, bool H16>
-static int launch_gemm_bt(const void* W, const void* W2, const float* X, float* Y, const float* R, const uint32_t* xmax,
+static int launch_gemm_bt(const void* W, const void* W2, const float* X, float* Y, const float* R, const GemmX16* x16,
                           int N, int ldy, int K, int T, cudaStream_t st, unsigned* err) {
     using C = GmCfg<BT, H16>;
     static_assert(!SW || 128 * (BT + 1) * 4 <= C::S * C::STAGE, "SwiGLU exchange fits the stages");
     GB_CUDA_TRY(set_smem_once(reinterpret_cast<const void*>(k_gemm<DT, BT, SW, H16>), C::SMEM));
-    CUtensorMap xmap;
-    if (!gemm_encode_x(&xmap, X, T, K, GM_BK, BT)) return GB_ECUDA;
+    CUtensorMap xmap, xlmap;
+    const float* xinv = nullptr;
+    if constexpr (H16) {
+        if (x16->tp < gemm_split_rows(T) || !gemm_encode_x16(&xmap, x16->hi, x16->tp, K, BT) ||
+            !gemm_encode_x16(&xlmap, x16->lo, x16->tp, K, BT))
+            return GB_ECUDA;
+        xinv = x16->inv;
+    } else {
+        if (!gemm_encode_x(&xmap, X, T, K, GM_BK, BT)) return GB_ECUDA;
+        xlmap = xmap;
+    }
     const int rows = SW ? GM_ROWS / 2 : GM_ROWS;
     dim3 grid((N + rows - 1) / rows, (T + BT - 1) / BT);
     k_gemm<DT, BT, SW, H16><<<grid, GM_THREADS, C::SMEM, st>>>(
-        xmap, static_cast<const uint8_t*>(W), static_cast<const uint8_t*>(W2), Y, R, xmax, N, ldy, K, T, err);
+        xmap, static_cast<const uint8_t*>(W), static_cast<const uint8_t*>(W2), Y, R, xlmap, xinv, N, ldy, K, T, err);
     return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
 }
 
@@ -682,7 +723,7 @@ static int launch_gemm_bt(const void* W, const void* W2, const float* X, float* 
 // FLOP) when their grid still gives every SM a CTA, else 128-token tiles
 // (GB_GEMM_BT=128 / 256 forces one size).
 template <int DT, bool SW>
-static int launch_gemm(const void* W, const void* W2, const float* X, float* Y, const float* R, const uint32_t* xmax,
+static int launch_gemm(const void* W, const void* W2, const float* X, float* Y, const float* R, const GemmX16* x16,
                        int N, int ldy, int K, int T, cudaStream_t st, unsigned* err) {
     static const int force = [] {
         const char* e = getenv("GB_GEMM_BT");
@@ -691,16 +732,16 @@ static int launch_gemm(const void* W, const void* W2, const float* X, float* Y, 
     const int rows = SW ? GM_ROWS / 2 : GM_ROWS;
     const long ctas256 = (long)((N + rows - 1) / rows) * ((T + 255) / 256);
     const bool wide = force ? force == 256 : ctas256 >= sm_count();
-    if (gemm_f16_operands())
-        return wide ? launch_gemm_bt<DT, 256, SW, true>(W, W2, X, Y, R, xmax, N, ldy, K, T, st, err)
-                    : launch_gemm_bt<DT, 128, SW, true>(W, W2, X, Y, R, xmax, N, ldy, K, T, st, err);
-    return wide ? launch_gemm_bt<DT, 256, SW, false>(W, W2, X, Y, R, xmax, N, ldy, K, T, st, err)
-                : launch_gemm_bt<DT, 128, SW, false>(W, W2, X, Y, R, xmax, N, ldy, K, T, st, err);
+    if (x16)
+        return wide ? launch_gemm_bt<DT, 256, SW, true>(W, W2, X, Y, R, x16, N, ldy, K, T, st, err)
+                    : launch_gemm_bt<DT, 128, SW, true>(W, W2, X, Y, R, x16, N, ldy, K, T, st, err);
+    return wide ? launch_gemm_bt<DT, 256, SW, false>(W, W2, X, Y, R, nullptr, N, ldy, K, T, st, err)
+                : launch_gemm_bt<DT, 128, SW, false>(W, W2, X, Y, R, nullptr, N, ldy, K, T, st, err);
 }
 
 template <bool SW>
 static int gemm_dispatch(int dtype, const void* W, const void* W2, const float* X, float* Y, const float* R, int N,
-                         int ldy, int K, int T, cudaStream_t st, unsigned* err, const uint32_t* xmax) {
+                         int ldy, int K, int T, cudaStream_t st, unsigned* err, const GemmX16* x16) {
     if (!W || !X || !Y || N <= 0 || K <= 0 || T <= 0 || ldy < N || (SW && !W2)) return GB_EINVAL;
     const bool a16 = dtype == GB_DT_F32 || dtype == GB_DT_Q4_K || dtype == GB_DT_Q5_K || dtype == GB_DT_F16;
     if ((reinterpret_cast<uintptr_t>(X) & 15) ||
@@ -711,40 +752,47 @@ static int gemm_dispatch(int dtype, const void* W, const void* W2, const float* 
         return GB_EINVAL;
     const int kmul = (dtype == GB_DT_Q4_K || dtype == GB_DT_Q6_K || dtype == GB_DT_Q5_K) ? 256 : 32;
     if (K % kmul) return GB_ESHAPE;
-    // fp16 operands without the caller's row maxima: computed here into
-    // stream-ordered scratch
-    uint32_t* tmp = nullptr;
-    if (gemm_f16_operands() && !xmax) {
-        if (cudaMallocAsync(reinterpret_cast<void**>(&tmp), (size_t)T * sizeof(uint32_t), st) != cudaSuccess)
-            return GB_ENOMEM;
-        const int rc = gemm_row_absmax(X, T, K, tmp, st);
+    if (!gemm_f16_operands()) x16 = nullptr;
+    // fp16 operands without the caller's split: X split here into
+    // stream-ordered scratch (hi, lo, inv)
+    void* tmp = nullptr;
+    GemmX16 own;
+    if (gemm_f16_operands() && !x16) {
+        const size_t half = (size_t)gemm_split_rows(T) * K * 2;
+        if (cudaMallocAsync(&tmp, 2 * half + (size_t)T * sizeof(float), st) != cudaSuccess) return GB_ENOMEM;
+        uint8_t* b = static_cast<uint8_t*>(tmp);
+        own.hi = b;
+        own.lo = b + half;
+        own.inv = reinterpret_cast<const float*>(b + 2 * half);
+        own.tp = gemm_split_rows(T);
+        const int rc = gemm_split_x(X, T, K, b, b + half, reinterpret_cast<float*>(b + 2 * half), st);
         if (rc) {
             cudaFreeAsync(tmp, st);
             return rc;
         }
-        xmax = tmp;
+        x16 = &own;
     }
     int rc;
     switch (dtype) {
-        case GB_DT_F32: rc = launch_gemm<GB_DT_F32, SW>(W, W2, X, Y, R, xmax, N, ldy, K, T, st, err); break;
-        case GB_DT_Q8_0: rc = launch_gemm<GB_DT_Q8_0, SW>(W, W2, X, Y, R, xmax, N, ldy, K, T, st, err); break;
-        case GB_DT_Q4_K: rc = launch_gemm<GB_DT_Q4_K, SW>(W, W2, X, Y, R, xmax, N, ldy, K, T, st, err); break;
-        case GB_DT_Q6_K: rc = launch_gemm<GB_DT_Q6_K, SW>(W, W2, X, Y, R, xmax, N, ldy, K, T, st, err); break;
-        case GB_DT_Q5_K: rc = launch_gemm<GB_DT_Q5_K, SW>(W, W2, X, Y, R, xmax, N, ldy, K, T, st, err); break;
-        default: rc = launch_gemm<GB_DT_F16, SW>(W, W2, X, Y, R, xmax, N, ldy, K, T, st, err); break;
+        case GB_DT_F32: rc = launch_gemm<GB_DT_F32, SW>(W, W2, X, Y, R, x16, N, ldy, K, T, st, err); break;
+        case GB_DT_Q8_0: rc = launch_gemm<GB_DT_Q8_0, SW>(W, W2, X, Y, R, x16, N, ldy, K, T, st, err); break;
+        case GB_DT_Q4_K: rc = launch_gemm<GB_DT_Q4_K, SW>(W, W2, X, Y, R, x16, N, ldy, K, T, st, err); break;
+        case GB_DT_Q6_K: rc = launch_gemm<GB_DT_Q6_K, SW>(W, W2, X, Y, R, x16, N, ldy, K, T, st, err); break;
+        case GB_DT_Q5_K: rc = launch_gemm<GB_DT_Q5_K, SW>(W, W2, X, Y, R, x16, N, ldy, K, T, st, err); break;
+        default: rc = launch_gemm<GB_DT_F16, SW>(W, W2, X, Y, R, x16, N, ldy, K, T, st, err); break;
     }
     if (tmp && cudaFreeAsync(tmp, st) != cudaSuccess && rc == GB_OK) rc = GB_ECUDA;
     return rc;
 }
 
 int gemm_launch(int dtype, const void* W, const float* X, float* Y, const float* R, int N, int K, int T,
-                cudaStream_t st, unsigned* err, int ldy, const uint32_t* xmax) {
-    return gemm_dispatch<false>(dtype, W, nullptr, X, Y, R, N, ldy ? ldy : N, K, T, st, err, xmax);
+                cudaStream_t st, unsigned* err, int ldy, const GemmX16* x16) {
+    return gemm_dispatch<false>(dtype, W, nullptr, X, Y, R, N, ldy ? ldy : N, K, T, st, err, x16);
 }
 
 int gemm_swiglu_launch(int dtype, const void* Wg, const void* Wu, const float* X, float* Y, int F, int K, int T,
-                       cudaStream_t st, unsigned* err, int ldy, const uint32_t* xmax) {
-    return gemm_dispatch<true>(dtype, Wg, Wu, X, Y, nullptr, F, ldy ? ldy : F, K, T, st, err, xmax);
+                       cudaStream_t st, unsigned* err, int ldy, const GemmX16* x16) {
+    return gemm_dispatch<true>(dtype, Wg, Wu, X, Y, nullptr, F, ldy ? ldy : F, K, T, st, err, x16);
 }
 
 }  // namespace gb

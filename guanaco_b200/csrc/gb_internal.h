@@ -109,25 +109,38 @@ bool mt_encode_rows(void* map128, const void* W, int rows, int nb, int box_u64);
 // Tensor map of a row-major fp32 matrix X[T][K] with boxes {box_k columns,
 // box_t rows, 1}; rows past T read as zeros.  X and the row pitch 16-byte aligned.
 bool gemm_encode_x(void* map128, const float* X, int T, int K, int box_k, int box_t);
+bool gemm_encode_x16(void* map128, const void* X16, int Tp, int K, int box_t);
 
+// A GEMM's activations split for fp16 operands (gemm_split_x): X * 2^e_t =
+// hi + lo, rows scaled so that max |x| < 2^15, hi and lo each laid out
+// [K / 8][tp][8] halves (column group, token, column; tp = T rounded up to a
+// multiple of 256, rows past T zero), and inv[t] = 2^-e_t.
+struct GemmX16 {
+    const void* hi;
+    const void* lo;
+    const float* inv;
+    int tp;
+};
+inline int gemm_split_rows(int T) { return (T + 255) / 256 * 256; }
 // Prefill GEMM on the tensor cores (gb_gemm.cu): Y[t][n] = sum_k X[t][k]
 // W[n][k] (+ R[t][n]) for T tokens, W fp32 (dtype GB_DT_F32) or GGUF blocks;
 // fp32-equivalent (3xF16, or 3xTF32 with GB_GEMM_KIND=tf32).  R may alias Y.
 // A wait that gives up records GB_ETIMEOUT in *err (null: the module-wide
 // word of gb_gemm_error).  Rows of Y and R are ldy floats apart (0: N).
-// xmax: the bits of max |X[t][.]| per token (gemm_row_absmax), shared by
-// GEMMs of one X; null computes them into stream-ordered scratch.
+// x16: X already split (shared by GEMMs of one X); null splits X into
+// stream-ordered scratch first.
 int gemm_launch(int dtype, const void* W, const float* X, float* Y, const float* R, int N, int K, int T,
-                cudaStream_t st, unsigned* err = nullptr, int ldy = 0, const uint32_t* xmax = nullptr);
+                cudaStream_t st, unsigned* err = nullptr, int ldy = 0, const GemmX16* x16 = nullptr);
 // Y[t][f] = silu(X Wg^T)[t][f] * (X Wu^T)[t][f] (k_silu_mul's rounding) for
 // f < F, in one GEMM launch: gate and up (same dtype, F rows each) share the
 // activation tiles, and the two products never reach HBM.
 int gemm_swiglu_launch(int dtype, const void* Wg, const void* Wu, const float* X, float* Y, int F, int K, int T,
-                       cudaStream_t st, unsigned* err = nullptr, int ldy = 0, const uint32_t* xmax = nullptr);
-// True unless GB_GEMM_KIND=tf32: the GEMMs read xmax.
+                       cudaStream_t st, unsigned* err = nullptr, int ldy = 0, const GemmX16* x16 = nullptr);
+// True unless GB_GEMM_KIND=tf32: the GEMMs take split activations.
 bool gemm_f16_operands();
-// xmax[t] = bits of max |X[t][k]| over k < K (X rows K floats apart).
-int gemm_row_absmax(const float* X, int T, int K, uint32_t* xmax, cudaStream_t st);
+// Split X [T][K] (rows K floats apart, K a multiple of 32) for fp16 operands
+// into hi / lo (gemm_split_rows(T) x K halves each) and inv (T floats).
+int gemm_split_x(const float* X, int T, int K, void* hi, void* lo, float* inv, cudaStream_t st);
 
 // Tensor-parallel context of a layer (world > 1): the wo and ffn_down
 // matvecs write this rank's partial to `part`, then an all-reduce over peer
@@ -202,7 +215,8 @@ struct PrefillArgs {
     float *kc, *vc;           // this layer's caches [n_kv][max_seq][hd]
     const float* rope;        // RoPE table [max_seq][hd]
     float *hidden, *xn, *q, *k, *v, *attn, *gate, *up;
-    uint32_t* xmax;           // [T] row maxima of the GEMMs' X (fp16 operands)
+    void *xh, *xl;            // [T][K] fp16 halves of the current GEMM input (fp16 operands)
+    float* xinv;              // [T] its token scales' inverses
     unsigned* err;            // the model's error word
     int T, pos0, H, n_heads, n_kv, hd, ff, max_seq;
     int fk;                   // ffn_down's columns (ff, or ff rounded up with zero padding): gate / up row width

@@ -1244,10 +1244,22 @@ static int prefill_chunk() {
 
 // Activation floats per prompt token: hidden, xn, q, k, v, attn, gate, up
 // (gate / up rows ff_pad wide: ffn_down's columns, zero past the FFN), and
-// the GEMM inputs' row maximum.
+// the current GEMM input's token scales; its split (pf_split_floats) follows.
+static size_t pf_split_k(const gb_model* m) {
+    return std::max({(size_t)m->c.hidden_dim, (size_t)m->nh * m->c.head_dim, (size_t)m->ff_pad});
+}
 static size_t pf_floats_per_token(const gb_model* m) {
     const int H = m->c.hidden_dim, QD = m->nh * m->c.head_dim;
-    return 2 * (size_t)H + 2 * (size_t)QD + 2 * (size_t)m->kv_dim + 2 * (size_t)m->ff_pad + 1;   // + xmax
+    return 2 * (size_t)H + 2 * (size_t)QD + 2 * (size_t)m->kv_dim + 2 * (size_t)m->ff_pad + 1;
+}
+// The split of the current GEMM input for cap prompt rows, in floats: hi and
+// lo halves of up to pf_split_k columns over the padded rows.
+static size_t pf_split_floats(const gb_model* m, int cap) {
+    return (size_t)gemm_split_rows(cap) * pf_split_k(m);
+}
+// Where the split starts: after the per-token floats, 256-byte aligned.
+static size_t pf_split_offset(const gb_model* m, int cap) {
+    return ((size_t)cap * pf_floats_per_token(m) + 63) / 64 * 64;
 }
 
 static int pf_reserve(gb_model* m, int T) {
@@ -1259,7 +1271,7 @@ static int pf_reserve(gb_model* m, int T) {
         m->pf = nullptr;
         m->pf_cap = 0;
     }
-    const size_t bytes = (size_t)T * pf_floats_per_token(m) * sizeof(float);
+    const size_t bytes = (pf_split_offset(m, T) + pf_split_floats(m, T)) * sizeof(float);
     if (cudaMalloc(&m->pf, bytes) != cudaSuccess) {
         m->pf = nullptr;
         return GB_ENOMEM;
@@ -1294,7 +1306,9 @@ extern "C" int gb_model_prefill(gb_model* m, const int* d_tokens, int n_tokens, 
     a.v = a.k + cap * KVD;
     a.gate = a.v + cap * KVD;
     a.up = a.gate + cap * (size_t)m->ff_pad;
-    a.xmax = reinterpret_cast<uint32_t*>(a.up + cap * (size_t)m->ff_pad);
+    a.xinv = a.up + cap * (size_t)m->ff_pad;
+    a.xh = base + pf_split_offset(m, (int)cap);
+    a.xl = static_cast<float*>(a.xh) + pf_split_floats(m, (int)cap) / 2;
     a.err = m->err;
     a.rope = m->rope;
     a.H = H; a.n_heads = m->nh; a.n_kv = m->nkv; a.hd = c.head_dim; a.ff = F; a.max_seq = c.max_seq;

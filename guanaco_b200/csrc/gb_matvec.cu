@@ -1198,6 +1198,23 @@ bool gemm_encode_x(void* map128, const float* X, int T, int K, int box_k, int bo
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Split fp16 activations laid out column-group-major, [K / 8][Tp][8 halves]
+// (Tp a multiple of 256), viewed as {256 x u64 = 128 rows of one group, Tp /
+// 128, K / 8}: a box {256, box_t / 128, 4} copies 2 KB runs and lands as the
+// tensor cores' K-major tile of box_t rows x 32 columns (core matrices of 8
+// rows x 16 bytes, column groups box_t x 16 bytes apart).
+bool gemm_encode_x16(void* map128, const void* X16, int Tp, int K, int box_t) {
+    auto enc = tensor_map_encoder();
+    if (!enc || (reinterpret_cast<uintptr_t>(X16) & 15) || K % 32 || Tp % 256 || box_t % 128) return false;
+    cuuint64_t dims[3] = {256, (cuuint64_t)Tp / 128, (cuuint64_t)K / 8};
+    cuuint64_t strides[2] = {2048, (cuuint64_t)Tp * 16};
+    cuuint32_t box[3] = {256, (cuuint32_t)box_t / 128, 4};
+    cuuint32_t es[3] = {1, 1, 1};
+    return enc(reinterpret_cast<CUtensorMap*>(map128), CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<void*>(X16), dims,
+               strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 template <class F>
 static size_t mt_smem_bytes(int S, int K) {
     const size_t xq = ((size_t)mt_xq_bytes(K, F::S16) + 15) & ~(size_t)15;

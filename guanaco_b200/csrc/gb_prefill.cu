@@ -636,15 +636,17 @@ int prefill_attention(const float* q, const float* kc, const float* vc, float* o
 int enqueue_prefill_layer(const PrefillArgs& a, cudaStream_t st) {
     const int T = a.T, H = a.H, QD = a.n_heads * a.hd, KVD = a.n_kv * a.hd, F = a.ff;
     int rc;
-    // row maxima of each GEMM input, once per X (fp16 operands only)
+    // fp16 operands: each GEMM input split once (shared by q / k / v and
+    // by gate / up)
     const bool f16 = gemm_f16_operands();
-    auto absmax = [&](const float* x, int K) { return f16 ? gemm_row_absmax(x, T, K, a.xmax, st) : GB_OK; };
-    const uint32_t* xm = f16 ? a.xmax : nullptr;
+    const GemmX16 x16{a.xh, a.xl, a.xinv, gemm_split_rows(T)};
+    auto split = [&](const float* x, int K) { return f16 ? gemm_split_x(x, T, K, a.xh, a.xl, a.xinv, st) : GB_OK; };
+    const GemmX16* xm = f16 ? &x16 : nullptr;
     auto gemm = [&](int which, const float* x, float* y, const float* res, int N, int K) {
         return gemm_launch(a.dt[which], a.w[which], x, y, res, N, K, T, st, a.err, 0, xm);
     };
     if ((rc = rmsnorm_rows(a.hidden, a.ra, a.xn, H, T, a.eps, st))) return rc;
-    if ((rc = absmax(a.xn, H))) return rc;
+    if ((rc = split(a.xn, H))) return rc;
     if ((rc = gemm(GB_WQ, a.xn, a.q, nullptr, QD, H))) return rc;
     if ((rc = gemm(GB_WK, a.xn, a.k, nullptr, KVD, H))) return rc;
     if ((rc = gemm(GB_WV, a.xn, a.v, nullptr, KVD, H))) return rc;
@@ -652,10 +654,10 @@ int enqueue_prefill_layer(const PrefillArgs& a, cudaStream_t st) {
     if (cudaGetLastError() != cudaSuccess) return GB_ECUDA;
     if ((rc = prefill_attention(a.q, a.kc, a.vc, a.attn, T, a.pos0, a.n_heads, a.n_kv, a.hd, a.max_seq, st, a.err)))
         return rc;
-    if ((rc = absmax(a.attn, QD))) return rc;
+    if ((rc = split(a.attn, QD))) return rc;
     if ((rc = gemm(GB_WO, a.attn, a.hidden, a.hidden, H, QD))) return rc;
     if ((rc = rmsnorm_rows(a.hidden, a.rf, a.xn, H, T, a.eps, st))) return rc;
-    if ((rc = absmax(a.xn, H))) return rc;
+    if ((rc = split(a.xn, H))) return rc;
     // gate / up rows are fk wide (ffn_down's columns); columns F .. fk - 1
     // stay zero (the prefill buffer is zeroed once and never written there)
     const int FK = a.fk;
@@ -669,7 +671,7 @@ int enqueue_prefill_layer(const PrefillArgs& a, cudaStream_t st) {
         if ((rc = gemm_launch(a.dt[GB_WUP], a.w[GB_WUP], a.xn, a.up, nullptr, F, H, T, st, a.err, FK, xm))) return rc;
         if ((rc = gb_silu_mul(a.gate, a.up, T * FK, st))) return rc;   // silu(0) * 0 = 0 in the padding
     }
-    if ((rc = absmax(a.gate, FK))) return rc;
+    if ((rc = split(a.gate, FK))) return rc;
     return gemm(GB_WDOWN, a.gate, a.hidden, a.hidden, H, FK);
 }
 
