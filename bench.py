@@ -43,6 +43,14 @@ def peaks():
     return 6650.0, "fallback"
 
 
+def bf16_peak():
+    """Dense fp16 / bf16 tensor peak: the measured bf16 dense sustained rate."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return float(json.load(open(p))["bf16_tflops_sustained"])
+    return 1400.0
+
+
 def tf32_peak():
     """Dense tf32 tensor peak: half the measured bf16 dense sustained rate."""
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -385,8 +393,10 @@ def prefill_bench(gb, torch, peak_tf32, T=PREFILL_T, reps=2):
     seeded Q4_K_M-style weights): one T-token prompt per step, device-timed
     with CUDA events on the launching stream after one warm-up prefill; e2e
     through gb_model_prefill_host (prompt H2D, next token D2H, synchronous).
-    The dominant kernel, the Q4_K gate / up GEMM (14336 x 4096 x T), is timed
-    alone for the roofline: tensor rate = 3 tf32 products x 2 N K T / time."""
+    The dominant kernel, the Q4_K GEMM 14336 x 4096 x T (gate or up), is timed
+    alone on an X split beforehand (fp16 operands; the split is its own
+    launch) for the roofline: tensor rate = 3 products x 2 N K T / time,
+    against the fp16 (or, with GB_GEMM_KIND=tf32, the tf32) dense peak."""
     import numpy as np
     c = LLAMA8B
     dm = gb.DecodeModel(c["hidden_dim"], c["n_heads"], c["n_kv_heads"], c["n_layers"], c["ff_dim"],
@@ -420,11 +430,22 @@ def prefill_bench(gb, torch, peak_tf32, T=PREFILL_T, reps=2):
         gb.synth_blocks(4, W, nb // gb.BLOCK_BYTES[4], SEED, 5)
         X = torch.randn(T * K, device="cuda")
         Y = torch.empty(T * N, device="cuda")
+        f16 = os.environ.get("GB_GEMM_KIND", "") != "tf32"
+        if f16:
+            sb = gb.gemm_split_bytes(T, K)
+            xh = torch.empty(sb, dtype=torch.uint8, device="cuda")
+            xl = torch.empty(sb, dtype=torch.uint8, device="cuda")
+            xi = torch.empty(T, device="cuda")
+            gb.gemm_split(X, T, K, xh, xl, xi, stream=st.cuda_stream)
+            run = lambda: gb.gemm_presplit(4, W, xh, xl, xi, Y, N, K, T, stream=st.cuda_stream)  # noqa: E731
+        else:
+            run = lambda: gb.gemm(4, W, X, Y, N, K, T, stream=st.cuda_stream)  # noqa: E731
+        peak = bf16_peak() if f16 else peak_tf32
         for _ in range(3):
-            gb.gemm(4, W, X, Y, N, K, T, stream=st.cuda_stream)
+            run()
         e0.record(st)
         for _ in range(5):
-            gb.gemm(4, W, X, Y, N, K, T, stream=st.cuda_stream)
+            run()
         e1.record(st)
         e1.synchronize()
         g_ms = e0.elapsed_time(e1) / 5
@@ -438,17 +459,20 @@ def prefill_bench(gb, torch, peak_tf32, T=PREFILL_T, reps=2):
                 "config": {"workload": f"llama3.1-8b-q4km-prefill, {T}-token prompt at position 0, 32 layers",
                            "chunk": min(T, 4096), "reps": reps, "warmup": 1,
                            "l2": "weights 4.9 GB and activations > 126 MB L2 per prompt"},
-                "dtype": "fp32-equivalent (weights dequantised to fp32, 3xTF32 tensor-core GEMMs, fp32 attention)",
+                "dtype": ("fp32-equivalent (weights dequantised to fp32, " +
+                          ("3xF16 with power-of-two row scales" if f16 else "3xTF32") +
+                          " tensor-core GEMMs, 3xTF32 attention)"),
                 "layer_gemm_tflops_fp32_equiv": round(flops / (ms * 1e-3) / 1e12, 1),
                 "e2e": {"value": round(T / e2e_s, 1), "unit": "tokens/s", "h2d_bytes_per_step": 4 * T,
                         "d2h_bytes_per_step": 8, "api": "gb_model_prefill_host (prompt in, next token out)"},
                 "next_token": int(nxt),
                 "roofline": {"bound": "tensor", "kernel": f"k_gemm<Q4_K> gate/up 14336x4096 at T={T}",
-                             "achieved": round(tf, 1), "peak": round(peak_tf32, 1), "unit": "TFLOP/s",
-                             "frac": round(tf / peak_tf32, 3),
+                             "achieved": round(tf, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
+                             "frac": round(tf / peak, 3),
                              "traffic": ncu_traffic("gemm_q4k_14336x4096_T4096.md"),
                              "fp32_equiv_tflops": round(tf / 3, 1), "ms": round(g_ms, 3),
-                             "peak_kind": "tf32 dense = half the measured bf16 dense sustained rate"}}
+                             "peak_kind": ("fp16 dense = the measured bf16 dense sustained rate" if f16 else
+                                           "tf32 dense = half the measured bf16 dense sustained rate")}}
     finally:
         dm.close()
 
@@ -689,7 +713,15 @@ def profile_kernel(name: str) -> None:
         X = torch.empty(T * cols, dtype=torch.float32, device="cuda")
         gb.synth_normal(X, T * cols, SEED, 5, stream=sp)
         Y = torch.empty(T * rows, dtype=torch.float32, device="cuda")
-        launch = lambda i: gb.gemm(dt, W, X, Y, rows, cols, T, stream=sp)  # noqa: E731
+        if os.environ.get("GB_GEMM_KIND", "") != "tf32":   # the GEMM launch alone on a split X
+            sb = gb.gemm_split_bytes(T, cols)
+            xh = torch.empty(sb, dtype=torch.uint8, device="cuda")
+            xl = torch.empty(sb, dtype=torch.uint8, device="cuda")
+            xi = torch.empty(T, dtype=torch.float32, device="cuda")
+            gb.gemm_split(X, T, cols, xh, xl, xi, stream=sp)
+            launch = lambda i: gb.gemm_presplit(dt, W, xh, xl, xi, Y, rows, cols, T, stream=sp)  # noqa: E731
+        else:
+            launch = lambda i: gb.gemm(dt, W, X, Y, rows, cols, T, stream=sp)  # noqa: E731
     elif name == "q4k_gu":   # gate + up in one launch, as in the decode step
         rows, cols, copies = 14336, 4096, 3
         wb = gb.matrix_bytes(4, rows, cols)

@@ -102,6 +102,9 @@ SIGNATURES = {
     "gb_device_error": (_i, [_i]),
     "gb_gemm": (_i, [_i, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "gb_gemm_error": (_i, [_i]),
+    "gb_gemm_split_bytes": (_sz, [_i, _i]),
+    "gb_gemm_split": (_i, [_vp, _i, _i, _vp, _vp, _vp, _vp]),
+    "gb_gemm_presplit": (_i, [_i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "gb_prefill_attention": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp]),
     "gb_prefill_attention_error": (_i, [_i]),
     "gb_dequant": (_i, [_i, _vp, _sz, _vp, _vp]),
@@ -195,6 +198,21 @@ def matvec_group(dtypes, Ws, rows, cols, x, ys, stream=None) -> None:
 def gemm(dtype, W, X, Y, N, K, T, R=None, stream=None) -> None:
     """Y[t][n] = sum_k X[t][k] W[n][k] (+ R[t][n]) on the tensor cores (prefill)."""
     check("gb_gemm", lib().gb_gemm(dtype, _ptr(W), _ptr(X), _ptr(Y), _ptr(R), N, K, T, _stream(stream)))
+
+
+def gemm_split(X, T, K, hi, lo, inv, stream=None) -> None:
+    """Split X [T][K] once for fp16-operand GEMMs (hi / lo: gemm_split_bytes each)."""
+    check("gb_gemm_split", lib().gb_gemm_split(_ptr(X), T, K, _ptr(hi), _ptr(lo), _ptr(inv), _stream(stream)))
+
+
+def gemm_split_bytes(T, K) -> int:
+    return int(lib().gb_gemm_split_bytes(T, K))
+
+
+def gemm_presplit(dtype, W, hi, lo, inv, Y, N, K, T, R=None, stream=None) -> None:
+    """gemm() on an X split by gemm_split()."""
+    check("gb_gemm_presplit", lib().gb_gemm_presplit(dtype, _ptr(W), _ptr(hi), _ptr(lo), _ptr(inv), _ptr(Y), _ptr(R),
+                                                     N, K, T, _stream(stream)))
 
 
 def prefill_attention(q, k_cache, v_cache, out, n_tokens, pos, n_heads, n_kv, head_dim, max_seq,

@@ -742,7 +742,8 @@ static int launch_gemm(const void* W, const void* W2, const float* X, float* Y, 
 template <bool SW>
 static int gemm_dispatch(int dtype, const void* W, const void* W2, const float* X, float* Y, const float* R, int N,
                          int ldy, int K, int T, cudaStream_t st, unsigned* err, const GemmX16* x16) {
-    if (!W || !X || !Y || N <= 0 || K <= 0 || T <= 0 || ldy < N || (SW && !W2)) return GB_EINVAL;
+    if (!W || (!X && !x16) || !Y || N <= 0 || K <= 0 || T <= 0 || ldy < N || (SW && !W2)) return GB_EINVAL;
+    if (x16 && (!x16->hi || !x16->lo || !x16->inv)) return GB_EINVAL;
     const bool a16 = dtype == GB_DT_F32 || dtype == GB_DT_Q4_K || dtype == GB_DT_Q5_K || dtype == GB_DT_F16;
     if ((reinterpret_cast<uintptr_t>(X) & 15) ||
         (a16 && ((reinterpret_cast<uintptr_t>(W) & 15) || (SW && (reinterpret_cast<uintptr_t>(W2) & 15)))))
@@ -752,7 +753,10 @@ static int gemm_dispatch(int dtype, const void* W, const void* W2, const float* 
         return GB_EINVAL;
     const int kmul = (dtype == GB_DT_Q4_K || dtype == GB_DT_Q6_K || dtype == GB_DT_Q5_K) ? 256 : 32;
     if (K % kmul) return GB_ESHAPE;
-    if (!gemm_f16_operands()) x16 = nullptr;
+    if (!gemm_f16_operands()) {
+        if (!X) return GB_EINVAL;   // a split X needs the fp16 form
+        x16 = nullptr;
+    }
     // fp16 operands without the caller's split: X split here into
     // stream-ordered scratch (hi, lo, inv)
     void* tmp = nullptr;
@@ -800,6 +804,22 @@ int gemm_swiglu_launch(int dtype, const void* Wg, const void* Wu, const float* X
 extern "C" int gb_gemm(int dtype, const void* W, const float* X, float* Y, const float* R, int N, int K, int T,
                        void* stream) {
     return gb::gemm_launch(dtype, W, X, Y, R, N, K, T, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+extern "C" size_t gb_gemm_split_bytes(int T, int K) {
+    return T > 0 && K > 0 ? (size_t)gb::gemm_split_rows(T) * K * 2 : 0;
+}
+
+extern "C" int gb_gemm_split(const float* X, int T, int K, void* hi, void* lo, float* inv, void* stream) {
+    if (!gb::gemm_f16_operands()) return GB_EINVAL;
+    return gb::gemm_split_x(X, T, K, hi, lo, inv, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int gb_gemm_presplit(int dtype, const void* W, const void* hi, const void* lo, const float* inv, float* Y,
+                                const float* R, int N, int K, int T, void* stream) {
+    if (!gb::gemm_f16_operands() || T <= 0) return GB_EINVAL;
+    const gb::GemmX16 x16{hi, lo, inv, gb::gemm_split_rows(T)};
+    return gb::gemm_launch(dtype, W, nullptr, Y, R, N, K, T, static_cast<cudaStream_t>(stream), nullptr, 0, &x16);
 }
 
 extern "C" int gb_gemm_error(int clear) {

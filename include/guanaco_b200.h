@@ -167,12 +167,24 @@ int gb_attention_decode(const float* q, const float* k, const float* v,
  * Y[t][n] = sum_k X[t][k] W[n][k] (+ R[t][n] when R is not NULL; R may be Y),
  * all device pointers, X / Y / R row-major fp32 (T x K, T x N).  W is N rows of
  * GGUF blocks (dtype 4 Q4_K, 5 Q6_K, 2 Q8_0, 13 Q5_K) or fp32 / fp16 rows
- * (dtype 0 / 1).  fp32-
- * equivalent: weights and activations are split into tf32 + fp32 remainders
- * (hi.hi + hi.lo + lo.hi).  Replaces the per-token loop of linear_dispatch
- * (src/engine/engine.c:119-153) for T > 1; the reference's GPU prefill hook is
- * a stub (src/engine/gpu_prefill.c:3-20).  Asynchronous on `stream`. */
+ * (dtype 0 / 1).  fp32-equivalent: weights and activations are split into
+ * an 11-bit part and a remainder (hi.hi + hi.lo + lo.hi), as fp16 pairs with
+ * power-of-two row scales (default) or tf32 pairs (GB_GEMM_KIND=tf32).  In
+ * the fp16 form X is first split into stream-ordered scratch
+ * (cudaMallocAsync, gb_gemm_split_bytes x 2 + 4 T bytes).  Replaces the
+ * per-token loop of linear_dispatch (src/engine/engine.c:119-153) for T > 1;
+ * the reference's GPU prefill hook is a stub (src/engine/gpu_prefill.c:3-20).
+ * Asynchronous on `stream`. */
 int gb_gemm(int dtype, const void* W, const float* X, float* Y, const float* R, int N, int K, int T, void* stream);
+/* The fp16 form in two steps, so that one split X serves several GEMMs (no
+ * reference counterpart; the reference has no batched GEMM): gb_gemm_split
+ * writes hi and lo (gb_gemm_split_bytes(T, K) bytes each, 16-byte aligned)
+ * and inv (T floats); gb_gemm_presplit then computes Y as gb_gemm does.
+ * K a multiple of 32.  GB_EINVAL when GB_GEMM_KIND=tf32. */
+size_t gb_gemm_split_bytes(int T, int K);
+int gb_gemm_split(const float* X, int T, int K, void* hi, void* lo, float* inv, void* stream);
+int gb_gemm_presplit(int dtype, const void* W, const void* hi, const void* lo, const float* inv, float* Y,
+                     const float* R, int N, int K, int T, void* stream);
 /* Device error word of the GEMM's bounded waits (GB_ETIMEOUT); clear != 0
  * resets it. */
 int gb_gemm_error(int clear);

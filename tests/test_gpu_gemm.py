@@ -86,3 +86,38 @@ def test_gemm_long_k_wide_tiles(gb, oracle, cuda, dt):
     got = from_dev(Y)[rows]
     assert np.all(np.isfinite(from_dev(Y)))
     assert rel_l2(got, ref) <= 1e-5, rel_l2(got, ref)
+
+
+@pytest.mark.parametrize("N,K,T", [(256, 1024, 300), (128, 4096, 40)])
+def test_gemm_presplit_equals_gemm(gb, oracle, cuda, N, K, T):
+    """gb_gemm_split + gb_gemm_presplit (one split X for several GEMMs) give
+    gb_gemm's result bit for bit, also for T not a multiple of the 256-row
+    split pitch; the split X is reused by a second GEMM with a residual.
+    Activations with a wide dynamic range (rows scaled by 2^-20 .. 2^12) keep
+    the fp64 bound, since each token row has its own power-of-two scale."""
+    W = oracle.synth_blocks(4, N, K, 9, N + K)
+    X = oracle.synth_normal(T * K, 9, T).reshape(T, K)
+    X *= np.exp2(np.linspace(-20, 12, T)).astype(np.float32)[:, None]
+    Wd = cuda.zeros(W.size + 16, dtype=cuda.uint8, device="cuda")
+    Wd[: W.size] = cuda.from_numpy(W).cuda()
+    ref_y = _run(gb, cuda, 4, Wd, X, N, K, T)
+    sb = gb.gemm_split_bytes(T, K)
+    assert sb == ((T + 255) // 256 * 256) * K * 2
+    xh = cuda.empty(sb, dtype=cuda.uint8, device="cuda")
+    xl = cuda.empty(sb, dtype=cuda.uint8, device="cuda")
+    xi = cuda.empty(T, dtype=cuda.float32, device="cuda")
+    gb.gemm_split(to_dev(cuda, X), T, K, xh, xl, xi)
+    Y = cuda.full((T, N), float("nan"), dtype=cuda.float32, device="cuda")
+    gb.gemm_presplit(4, Wd, xh, xl, xi, Y, N, K, T)
+    R = oracle.synth_normal(T * N, 9, 7).reshape(T, N)
+    Y2 = to_dev(cuda, R)
+    gb.gemm_presplit(4, Wd, xh, xl, xi, Y2, N, K, T, R=Y2)
+    cuda.cuda.synchronize()
+    assert gb.lib().gb_gemm_error(1) == 0
+    assert np.array_equal(from_dev(Y).view(np.uint32), ref_y.view(np.uint32))
+    Wf = oracle.dequant(4, W).reshape(N, K).astype(np.float64)
+    ref = X.astype(np.float64) @ Wf.T
+    # relative to each token row's own magnitude
+    err = np.linalg.norm(from_dev(Y) - ref, axis=1) / np.maximum(np.linalg.norm(ref, axis=1), 1e-300)
+    assert err.max() <= 1e-5, err.max()
+    assert rel_l2(from_dev(Y2), ref + R) <= 1e-5
