@@ -1,8 +1,9 @@
 """Prefill GEMM on the tcgen05 tensor cores (gb_gemm): Y = X . W^T (+ R) for T
 tokens at once, W fp32 or GGUF Q4_K / Q6_K / Q8_0 blocks dequantised on the
-fly.  fp32-equivalent arithmetic (3xTF32; the tensor cores' accumulator is
-restarted every 256 columns of K and the partial sums added in fp32
-registers), so the result must match an fp64 product of the oracle's
+fly.  fp32-equivalent arithmetic (3xF16 with power-of-two row scales by
+default, 3xTF32 with GB_GEMM_KIND=tf32; the tensor cores' accumulator is
+restarted every 256 / 512 columns of K and the partial sums added in fp32),
+so the result must match an fp64 product of the oracle's
 dequantised weights (the reference's formulas) to a few 1e-6 relative L2
 (bound 1e-5 at every K tested, up to 2048), far inside the 1e-3 bound."""
 import numpy as np
