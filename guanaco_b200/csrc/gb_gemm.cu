@@ -71,7 +71,9 @@ struct GmCfg {
     static constexpr int STAGE = 2 * TILE_A + 2 * TILE_B;
     static constexpr int S = H16 ? (BT == 256 ? 4 : 6) : (BT == 256 ? 2 : 3);   // ring stages
     static constexpr int NACC = BT == 256 ? 1 : 2;              // accumulators in tensor memory
-    static constexpr int KG = BT == 256 ? 16 : 8;               // chunks per accumulator group (512 / 256 columns of K)
+    // chunks per accumulator group: 512 / 256 columns of K for tf32, twice
+    // that for fp16 (the same 192 / 96 MMAs per accumulator)
+    static constexpr int KG = (BT == 256 ? 16 : 8) * (H16 ? 2 : 1);
     static constexpr int SMEM = S * STAGE + 1024;
     static constexpr uint32_t TMEM_COLS = 512;                  // NACC x BT accumulator + BT running sum
     static_assert(XRAW <= 2 * TILE_B, "the raw activation tile fits B's tiles");
@@ -568,32 +570,33 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
             const uint32_t acc = lane_base + (uint32_t)(a * BT);
             const bool last = g == ng - 1;
 #pragma unroll 1
-            for (int c = 0; c < BT; c += 16) {
-                float v[16];
-                tc::tmem_ld16(acc + c, v);
+            for (int c = 0; c < BT; c += 32) {
+                float v[32];
                 if (g > 0) {
-                    float u[16];
-                    tc::tmem_ld16(sum + c, u);
+                    float u[32];
+                    tc::tmem_ld32x2(acc + c, sum + c, v, u);
 #pragma unroll
-                    for (int i = 0; i < 16; i++) v[i] += u[i];
+                    for (int i = 0; i < 32; i++) v[i] += u[i];
+                } else {
+                    tc::tmem_ld32(acc + c, v);
                 }
                 if (!last) {
-                    tc::tmem_st16(sum + c, v);
+                    tc::tmem_st32_nowait(sum + c, v);
                     continue;
                 }
                 if constexpr (H16) {
 #pragma unroll
-                    for (int i = 0; i < 16; i++) {
+                    for (int i = 0; i < 32; i++) {
                         const int tt = t0 + c + i;
                         v[i] = v[i] * inv_r * (tt < T ? xinv[tt] : 1.f);
                     }
                 }
                 if constexpr (SW) {
 #pragma unroll
-                    for (int i = 0; i < 16; i++) xch[r * XLD + c + i] = v[i];
+                    for (int i = 0; i < 32; i++) xch[r * XLD + c + i] = v[i];
                 } else if (n < N) {
 #pragma unroll
-                    for (int i = 0; i < 16; i++) {
+                    for (int i = 0; i < 32; i++) {
                         const int tt = t0 + c + i;
                         if (tt < T) {
                             const size_t o = (size_t)tt * ldy + n;
@@ -602,6 +605,7 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
                     }
                 }
             }
+            if (!last) tc::tmem_wait_st();   // the running sum is read back by the next group
             tc::fence_before_sync();
             __syncwarp();
             if (lane == 0) mbs_arrive(accfree + 8 * a);
