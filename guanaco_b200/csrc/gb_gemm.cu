@@ -633,18 +633,19 @@ k_gemm(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ W, 
     }
 }
 
-// Split 16 token rows of X per CTA (K a multiple of 32) for fp16 operands:
-// e from each row's largest |x| (so that |x| 2^e < 2^15), then x 2^e = hi +
-// lo as fp16 halves (tc::split_f16x2) written column-group-major (16 rows x
-// 16 bytes contiguous per group), inv = 2^-e; rows T .. tp - 1 are zero.
-// Non-negative floats order as their bit patterns.
-constexpr int XS_ROWS = 16;
+// Split 8 token rows of X per CTA (K a multiple of 32) for fp16 operands:
+// e from each row's largest |x| (so that |x| 2^e < 2^15; one warp per row),
+// then x 2^e = hi + lo as fp16 halves (tc::split_f16x2) written
+// column-group-major (8 rows x 16 bytes: one 128-byte line per group), inv =
+// 2^-e; rows T .. tp - 1 are zero.  Non-negative floats order as their bit
+// patterns.
+constexpr int XS_ROWS = 8;
 __global__ void __launch_bounds__(256) k_x_split16(const float* __restrict__ X, int K, int T, int tp,
                                                     uint4* __restrict__ hi, uint4* __restrict__ lo,
                                                     float* __restrict__ inv) {
     __shared__ float scale[XS_ROWS];
     const int t0 = blockIdx.x * XS_ROWS, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int rr = warp; rr < XS_ROWS; rr += 8) {   // each warp: two rows' maxima
+    for (int rr = warp; rr < XS_ROWS; rr += 8) {   // a row per warp
         const int t = t0 + rr;
         uint32_t m = 0;
         if (t < T) {
