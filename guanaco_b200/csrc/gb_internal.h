@@ -217,6 +217,8 @@ struct PrefillArgs {
     float *hidden, *xn, *q, *k, *v, *attn, *gate, *up;
     void *xh, *xl;            // [T][K] fp16 halves of the current GEMM input (fp16 operands)
     float* xinv;              // [T] its token scales' inverses
+    cudaStream_t side;        // wk / wv run here beside wq (null: all on the layer's stream)
+    cudaEvent_t fork, join;
     unsigned* err;            // the model's error word
     int T, pos0, H, n_heads, n_kv, hd, ff, max_seq;
     int fk;                   // ffn_down's columns (ff, or ff rounded up with zero padding): gate / up row width

@@ -456,6 +456,10 @@ struct gb_model {
     int pf_cap = 0;
     int* pf_tok = nullptr;            // device copy of a host prompt
     int pf_tok_cap = 0;
+    // prefill: a second stream for the wk / wv GEMMs, which run beside wq
+    // (fork / join events recorded on the caller's stream)
+    cudaStream_t pf_side = nullptr;
+    cudaEvent_t pf_fork = nullptr, pf_join = nullptr;
 };
 
 static void* dalloc(gb_model* m, size_t bytes) {
@@ -650,8 +654,12 @@ extern "C" void gb_model_destroy(gb_model* m) {
         if (p) cudaIpcCloseMemHandle(p);
     if (m->comm) cudaFree(m->comm);
     for (void* p : m->owned) cudaFree(p);
+    if (m->pf_side) cudaStreamSynchronize(m->pf_side);
     if (m->pf) cudaFree(m->pf);
     if (m->pf_tok) cudaFree(m->pf_tok);
+    if (m->pf_fork) cudaEventDestroy(m->pf_fork);
+    if (m->pf_join) cudaEventDestroy(m->pf_join);
+    if (m->pf_side) cudaStreamDestroy(m->pf_side);
     if (m->h_io) cudaFreeHost(m->h_io);
     if (m->stream) cudaStreamDestroy(m->stream);
     delete m;
@@ -1263,6 +1271,12 @@ static size_t pf_split_offset(const gb_model* m, int cap) {
 }
 
 static int pf_reserve(gb_model* m, int T) {
+    if (!m->pf_side) {   // the side stream and its events (created once)
+        if (cudaStreamCreateWithFlags(&m->pf_side, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&m->pf_fork, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&m->pf_join, cudaEventDisableTiming) != cudaSuccess)
+            return GB_ECUDA;
+    }
     if (T <= m->pf_cap) return GB_OK;
     if (m->pf) {   // earlier prefills on this stream may still read it
         GB_CUDA_TRY(cudaStreamSynchronize(m->stream));
@@ -1310,6 +1324,9 @@ extern "C" int gb_model_prefill(gb_model* m, const int* d_tokens, int n_tokens, 
     a.xh = base + pf_split_offset(m, (int)cap);
     a.xl = static_cast<float*>(a.xh) + pf_split_floats(m, (int)cap) / 2;
     a.err = m->err;
+    a.side = m->pf_side;
+    a.fork = m->pf_fork;
+    a.join = m->pf_join;
     a.rope = m->rope;
     a.H = H; a.n_heads = m->nh; a.n_kv = m->nkv; a.hd = c.head_dim; a.ff = F; a.max_seq = c.max_seq;
     a.eps = c.rms_eps;

@@ -642,14 +642,28 @@ int enqueue_prefill_layer(const PrefillArgs& a, cudaStream_t st) {
     const GemmX16 x16{a.xh, a.xl, a.xinv, gemm_split_rows(T)};
     auto split = [&](const float* x, int K) { return f16 ? gemm_split_x(x, T, K, a.xh, a.xl, a.xinv, st) : GB_OK; };
     const GemmX16* xm = f16 ? &x16 : nullptr;
+    auto gemm_on = [&](cudaStream_t s, int which, const float* x, float* y, const float* res, int N, int K) {
+        return gemm_launch(a.dt[which], a.w[which], x, y, res, N, K, T, s, a.err, 0, xm);
+    };
     auto gemm = [&](int which, const float* x, float* y, const float* res, int N, int K) {
-        return gemm_launch(a.dt[which], a.w[which], x, y, res, N, K, T, st, a.err, 0, xm);
+        return gemm_on(st, which, x, y, res, N, K);
     };
     if ((rc = rmsnorm_rows(a.hidden, a.ra, a.xn, H, T, a.eps, st))) return rc;
     if ((rc = split(a.xn, H))) return rc;
+    // wk and wv (few CTAs each) on the side stream beside wq, whose last wave
+    // leaves most SMs idle; all three only read the split of xn
+    cudaStream_t kv = a.side ? a.side : st;
+    if (a.side) {
+        if (cudaEventRecord(a.fork, st) != cudaSuccess || cudaStreamWaitEvent(a.side, a.fork, 0) != cudaSuccess)
+            return GB_ECUDA;
+    }
     if ((rc = gemm(GB_WQ, a.xn, a.q, nullptr, QD, H))) return rc;
-    if ((rc = gemm(GB_WK, a.xn, a.k, nullptr, KVD, H))) return rc;
-    if ((rc = gemm(GB_WV, a.xn, a.v, nullptr, KVD, H))) return rc;
+    if ((rc = gemm_on(kv, GB_WK, a.xn, a.k, nullptr, KVD, H))) return rc;
+    if ((rc = gemm_on(kv, GB_WV, a.xn, a.v, nullptr, KVD, H))) return rc;
+    if (a.side) {
+        if (cudaEventRecord(a.join, a.side) != cudaSuccess || cudaStreamWaitEvent(st, a.join, 0) != cudaSuccess)
+            return GB_ECUDA;
+    }
     k_pf_rope_kv<<<T, 256, 0, st>>>(a.q, a.k, a.v, a.kc, a.vc, a.rope, a.pos0, a.n_heads, a.n_kv, a.hd, a.max_seq);
     if (cudaGetLastError() != cudaSuccess) return GB_ECUDA;
     if ((rc = prefill_attention(a.q, a.kc, a.vc, a.attn, T, a.pos0, a.n_heads, a.n_kv, a.hd, a.max_seq, st, a.err)))
