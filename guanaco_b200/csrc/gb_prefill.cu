@@ -327,8 +327,10 @@ k_pf_attn_tc(const float* __restrict__ q, const float* __restrict__ kc, const fl
     __shared__ __align__(8) uint64_t bars[9];
     __shared__ uint32_t tmem_slot;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int g = blockIdx.y;
-    const int qb = gridDim.x - 1 - blockIdx.x;   // longest blocks first
+    // grid (KV heads, query blocks), heads fastest: CTAs start in order of
+    // decreasing length (the longest query blocks of every head first)
+    const int g = blockIdx.x;
+    const int qb = gridDim.y - 1 - blockIdx.y;
     const int q0 = qb * BQ, QD = nh * HD;
     const float* kh = kc + (size_t)g * max_seq * HD;
     const float* vh = vc + (size_t)g * max_seq * HD;
@@ -594,7 +596,8 @@ static cudaError_t launch_pf_attn_tc(const float* q, const float* kc, const floa
     cudaError_t e = set_smem_once(reinterpret_cast<const void*>(k_pf_attn_tc<HD, GROUP>), smem);
     if (e != cudaSuccess) return e;
     constexpr int BQ = TA_R / GROUP;
-    dim3 grid((T + BQ - 1) / BQ, n_kv);
+    if ((T + BQ - 1) / BQ > 65535) return cudaErrorInvalidValue;   // grid.y limit: 2M prompt rows at GROUP 4
+    dim3 grid(n_kv, (T + BQ - 1) / BQ);
     k_pf_attn_tc<HD, GROUP><<<grid, TA_THREADS, smem, st>>>(q, kc, vc, out, T, pos0, n_kv * GROUP, max_seq, err);
     return cudaGetLastError();
 }
