@@ -122,3 +122,23 @@ def test_gemm_presplit_equals_gemm(gb, oracle, cuda, N, K, T):
     err = np.linalg.norm(from_dev(Y) - ref, axis=1) / np.maximum(np.linalg.norm(ref, axis=1), 1e-300)
     assert err.max() <= 1e-5, err.max()
     assert rel_l2(from_dev(Y2), ref + R) <= 1e-5
+
+
+def test_gemm_tf32_operands_in_a_subprocess():
+    """The 3xTF32 form (GB_GEMM_KIND=tf32, read once per process) against the
+    same fp64 bounds: the quantised GEMM cases, the long-K case and the
+    model-level prefill parity of tests/test_gpu_prefill.py, run by pytest in
+    a child process with the variable set."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, GB_GEMM_KIND="tf32")
+    cmd = [sys.executable, "-m", "pytest", "-q", "-x", "-p", "no:cacheprovider",
+           "tests/test_gpu_gemm.py::test_gemm_quantised_matches_dequantised_product",
+           "tests/test_gpu_gemm.py::test_gemm_long_k_wide_tiles",
+           "tests/test_gpu_gemm.py::test_gemm_fp32_matches_fp64",
+           "tests/test_gpu_prefill.py::test_prefill_matches_reference_forward"]
+    r = subprocess.run(cmd, cwd=root, env=env, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+    assert " passed" in r.stdout and "failed" not in r.stdout, r.stdout[-2000:]
