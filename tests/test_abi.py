@@ -89,3 +89,13 @@ def test_product_does_not_touch_the_oracle():
             if f.endswith((".py", ".cu", ".c", ".h", ".cuh")):
                 txt = open(os.path.join(dirpath, f)).read()
                 assert "gbo_" not in txt and "oracle" not in txt.lower().replace("oracle.", ""), f
+
+
+def test_gemm_split_bytes_without_a_gpu(gb):
+    """gb_gemm_split_bytes is host arithmetic: token rows rounded up to the
+    256-row pitch of the column-group-major split, 2 bytes per element."""
+    assert gb.gemm_split_bytes(300, 1024) == 512 * 1024 * 2
+    assert gb.gemm_split_bytes(256, 4096) == 256 * 4096 * 2
+    assert gb.gemm_split_bytes(1, 32) == 256 * 32 * 2
+    assert gb.gemm_split_bytes(0, 4096) == 0
+    assert gb.gemm_split_bytes(16, -1) == 0
