@@ -683,6 +683,85 @@ __global__ void __launch_bounds__(256) k_x_split16(const float* __restrict__ X, 
     }
 }
 
+// RMSNorm of 8 token rows per CTA fused with their split: xn = w * (x * r),
+// r = 1 / sqrt(sum(x^2) / K + eps) (kernels_cpu.c:242-263, k_rmsnorm's
+// roundings; the sum of squares in another order), then split as
+// k_x_split16 does.  xn itself is not written.
+__global__ void __launch_bounds__(256) k_rmsnorm_split16(const float* __restrict__ X, const float* __restrict__ w,
+                                                          int K, float eps, int T, int tp, uint4* __restrict__ hi,
+                                                          uint4* __restrict__ lo, float* __restrict__ inv) {
+    __shared__ float scale[XS_ROWS], rsq[XS_ROWS];
+    const int t0 = blockIdx.x * XS_ROWS, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+    for (int rr = warp; rr < XS_ROWS; rr += 8) {   // a row per warp
+        const int t = t0 + rr;
+        float r = 0.f;
+        uint32_t m = 0;
+        if (t < T) {
+            const float4* row = reinterpret_cast<const float4*>(X + (size_t)t * K);
+            float ss = 0.f;
+            for (int i = lane; i < K / 4; i += 32) {
+                const float4 v = __ldg(row + i);
+                ss = fmaf(v.x, v.x, ss);
+                ss = fmaf(v.y, v.y, ss);
+                ss = fmaf(v.z, v.z, ss);
+                ss = fmaf(v.w, v.w, ss);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+            r = __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)K), eps)));
+            for (int i = lane; i < K / 4; i += 32) {
+                const float4 v = __ldg(row + i);
+                const float4 g = w ? __ldg(w4 + i) : make_float4(1.f, 1.f, 1.f, 1.f);
+                m = max(m, max(max(__float_as_uint(fabsf(__fmul_rn(g.x, __fmul_rn(v.x, r)))),
+                                   __float_as_uint(fabsf(__fmul_rn(g.y, __fmul_rn(v.y, r))))),
+                               max(__float_as_uint(fabsf(__fmul_rn(g.z, __fmul_rn(v.z, r)))),
+                                   __float_as_uint(fabsf(__fmul_rn(g.w, __fmul_rn(v.w, r)))))));
+            }
+        }
+        m = __reduce_max_sync(0xFFFFFFFFu, m);
+        if (lane == 0) {
+            const int e = tc::f16_scale_exp(m);
+            scale[rr] = tc::pow2f(e);
+            rsq[rr] = r;
+            if (t < T) inv[t] = tc::pow2f(-e);
+        }
+    }
+    __syncthreads();
+    const int ng = K / 8;
+    for (int idx = threadIdx.x; idx < ng * XS_ROWS; idx += blockDim.x) {
+        const int rr = idx % XS_ROWS, g = idx / XS_ROWS, t = t0 + rr;
+        uint4 h = make_uint4(0u, 0u, 0u, 0u), l = h;
+        if (t < T) {
+            const float4* p = reinterpret_cast<const float4*>(X + (size_t)t * K + 8 * g);
+            const float4 a = __ldg(p), b = __ldg(p + 1);
+            const float4 ga = w ? __ldg(w4 + 2 * g) : make_float4(1.f, 1.f, 1.f, 1.f);
+            const float4 gb = w ? __ldg(w4 + 2 * g + 1) : make_float4(1.f, 1.f, 1.f, 1.f);
+            const float r = rsq[rr], sc = scale[rr];
+            auto nv = [&](float x, float gg) { return __fmul_rn(gg, __fmul_rn(x, r)) * sc; };
+            tc::split_f16x2(nv(a.x, ga.x), nv(a.y, ga.y), h.x, l.x);
+            tc::split_f16x2(nv(a.z, ga.z), nv(a.w, ga.w), h.y, l.y);
+            tc::split_f16x2(nv(b.x, gb.x), nv(b.y, gb.y), h.z, l.z);
+            tc::split_f16x2(nv(b.z, gb.z), nv(b.w, gb.w), h.w, l.w);
+        }
+        const size_t o = (size_t)g * tp + t;
+        hi[o] = h;
+        lo[o] = l;
+    }
+}
+
+int gemm_rmsnorm_split_x(const float* X, const float* w, int T, int K, float eps, void* hi, void* lo, float* inv,
+                         cudaStream_t st) {
+    if (!X || !hi || !lo || !inv || T <= 0 || K <= 0 || K % 32 || (reinterpret_cast<uintptr_t>(X) & 15) ||
+        (w && (reinterpret_cast<uintptr_t>(w) & 15)) || (reinterpret_cast<uintptr_t>(hi) & 15) ||
+        (reinterpret_cast<uintptr_t>(lo) & 15))
+        return GB_EINVAL;
+    const int tp = gemm_split_rows(T);
+    k_rmsnorm_split16<<<tp / XS_ROWS, 256, 0, st>>>(X, w, K, eps, T, tp, static_cast<uint4*>(hi),
+                                                    static_cast<uint4*>(lo), inv);
+    return cudaGetLastError() == cudaSuccess ? GB_OK : GB_ECUDA;
+}
+
 bool gemm_f16_operands() {
     static const bool f16 = [] {
         const char* e = getenv("GB_GEMM_KIND");

@@ -141,6 +141,10 @@ bool gemm_f16_operands();
 // Split X [T][K] (rows K floats apart, K a multiple of 32) for fp16 operands
 // into hi / lo (gemm_split_rows(T) x K halves each) and inv (T floats).
 int gemm_split_x(const float* X, int T, int K, void* hi, void* lo, float* inv, cudaStream_t st);
+// The split of RMSNorm(X) rows (weight w, may be null) without writing them:
+// rmsnorm_rows followed by gemm_split_x in one pass.
+int gemm_rmsnorm_split_x(const float* X, const float* w, int T, int K, float eps, void* hi, void* lo, float* inv,
+                         cudaStream_t st);
 
 // Tensor-parallel context of a layer (world > 1): the wo and ffn_down
 // matvecs write this rank's partial to `part`, then an all-reduce over peer

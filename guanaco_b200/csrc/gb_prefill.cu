@@ -321,7 +321,7 @@ __global__ void __launch_bounds__(TA_THREADS, 1)
 k_pf_attn_tc(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
              float* __restrict__ out, int T, int pos0, int nh, int max_seq, unsigned* err) {
     using L = TaLayout<HD>;
-    constexpr int BQ = TA_R / GROUP, NS = L::NS;
+    constexpr int BQ = TA_R / GROUP;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     __shared__ __align__(8) uint64_t bars[9];
@@ -651,8 +651,12 @@ int enqueue_prefill_layer(const PrefillArgs& a, cudaStream_t st) {
     auto gemm = [&](int which, const float* x, float* y, const float* res, int N, int K) {
         return gemm_on(st, which, x, y, res, N, K);
     };
-    if ((rc = rmsnorm_rows(a.hidden, a.ra, a.xn, H, T, a.eps, st))) return rc;
-    if ((rc = split(a.xn, H))) return rc;
+    // RMSNorm: with fp16 operands straight into the split (xn not written)
+    auto norm = [&](const float* w) {
+        return f16 ? gemm_rmsnorm_split_x(a.hidden, w, T, H, a.eps, a.xh, a.xl, a.xinv, st)
+                   : rmsnorm_rows(a.hidden, w, a.xn, H, T, a.eps, st);
+    };
+    if ((rc = norm(a.ra))) return rc;
     // wk and wv (few CTAs each) on the side stream beside wq, whose last wave
     // leaves most SMs idle; all three only read the split of xn
     cudaStream_t kv = a.side ? a.side : st;
@@ -673,8 +677,7 @@ int enqueue_prefill_layer(const PrefillArgs& a, cudaStream_t st) {
         return rc;
     if ((rc = split(a.attn, QD))) return rc;
     if ((rc = gemm(GB_WO, a.attn, a.hidden, a.hidden, H, QD))) return rc;
-    if ((rc = rmsnorm_rows(a.hidden, a.rf, a.xn, H, T, a.eps, st))) return rc;
-    if ((rc = split(a.xn, H))) return rc;
+    if ((rc = norm(a.rf))) return rc;
     // gate / up rows are fk wide (ffn_down's columns); columns F .. fk - 1
     // stay zero (the prefill buffer is zeroed once and never written there)
     const int FK = a.fk;
