@@ -179,8 +179,9 @@ int gb_gemm(int dtype, const void* W, const float* X, float* Y, const float* R, 
 /* The fp16 form in two steps, so that one split X serves several GEMMs (no
  * reference counterpart; the reference has no batched GEMM): gb_gemm_split
  * writes hi and lo (gb_gemm_split_bytes(T, K) bytes each, 16-byte aligned)
- * and inv (T floats); gb_gemm_presplit then computes Y as gb_gemm does.
- * K a multiple of 32.  GB_EINVAL when GB_GEMM_KIND=tf32. */
+ * and inv (T floats); gb_gemm_presplit then computes Y as gb_gemm does from
+ * a split made with the same T and K (the layout's row pitch is T rounded up
+ * to 256).  K a multiple of 32.  GB_EINVAL when GB_GEMM_KIND=tf32. */
 size_t gb_gemm_split_bytes(int T, int K);
 int gb_gemm_split(const float* X, int T, int K, void* hi, void* lo, float* inv, void* stream);
 int gb_gemm_presplit(int dtype, const void* W, const void* hi, const void* lo, const float* inv, float* Y,
